@@ -1,0 +1,174 @@
+/*
+ * llamamps_b200.h -- C ABI of the B200 (sm_100a) LlamaMPS decode kernels.
+ *
+ * Conventions (mirroring the reference's Metal binding, runners/engine.py:49-58,
+ * where every kernel takes positional device buffers and never allocates):
+ *   - every pointer is a device pointer owned by the caller; fp16 tensors are
+ *     passed as uint16_t* holding IEEE binary16 bits;
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream);
+ *   - a call enqueues work and returns LMPS_OK (0), a negative LMPS_ERR_* for
+ *     rejected arguments (nothing is launched), or a positive cudaError_t from
+ *     the launch; lmps_status_string() names any of them;
+ *   - no entry point allocates device memory: scratch is passed in, with a
+ *     *_workspace_size() query beside the call that needs it.
+ *
+ * Weight format (utils/pack_weights.py:42-60): a [rows, k] matrix is packed
+ * row-major as uint8[rows*k/2] (element 2b in the low nibble of byte b, 2b+1
+ * in the high nibble, code+8) plus fp16 scales[rows*k/32] (one per 32
+ * consecutive elements, code = round(w / scale), scale = max|w| / 7).
+ */
+#ifndef LLAMAMPS_B200_H_
+#define LLAMAMPS_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  LMPS_OK = 0,
+  LMPS_ERR_INVALID_ARGUMENT = -1, /* shape/pointer/alignment rejected */
+  LMPS_ERR_UNSUPPORTED = -2,      /* shape outside the compiled variants */
+  LMPS_ERR_WORKSPACE = -3,        /* workspace too small */
+  LMPS_ERR_DEVICE_TIMEOUT = -4    /* a bounded device-side wait gave up */
+};
+
+enum { LMPS_ROPE_INTERLEAVED = 0, LMPS_ROPE_NEOX = 1 };
+
+/* Library version (major*10000 + minor*100 + patch). */
+int lmps_version(void);
+/* Human-readable name of a status code returned by any entry point. */
+const char* lmps_status_string(int status);
+
+/* ---- Q4 GEMV family ------------------------------------------------------
+ * y[b, r] = sum_k W[r, k] * x[b, k] with W in the Q4 format above, fp32
+ * accumulation, y rounded to fp16.  x is [batch, k] with row stride ldx
+ * elements, y is [batch, rows] with row stride ldy.  k % 32 == 0,
+ * 1 <= batch <= 8, packed 16-byte aligned.
+ */
+
+/* Replaces kernels/quant_matmul.metal:15-22 `gemv_q4_0` (dispatched at
+ * runners/engine.py:192-195, :215-217, :228-231, :237-239, :171-175). */
+int lmps_gemv_q4_0(const uint8_t* packed, const uint16_t* scales, const uint16_t* x, int ldx,
+                   uint16_t* y, int ldy, int rows, int k, int batch, void* stream);
+
+/* gemv_q4_0 + bias epilogue: y = fp16(acc + bias[r]).  Qwen2 q/k/v biases
+ * (absent from the reference, runners/engine.py:124-141). */
+int lmps_gemv_q4_bias(const uint8_t* packed, const uint16_t* scales, const uint16_t* bias,
+                      const uint16_t* x, int ldx, uint16_t* y, int ldy, int rows, int k,
+                      int batch, void* stream);
+
+/* gemv_q4_0 + residual_add: y = residual + fp16(acc) in fp16.  Replaces the
+ * o_proj/down_proj GEMV + kernels/residual.metal:13-20 pair
+ * (runners/engine.py:215-221, :237-243).  y may alias residual. */
+int lmps_gemv_q4_residual(const uint8_t* packed, const uint16_t* scales, const uint16_t* x,
+                          int ldx, const uint16_t* residual, uint16_t* y, int ldy, int rows,
+                          int k, int batch, void* stream);
+
+/* gate/up GEMVs + kernels/swiglu.metal:13-23: y = fp16(silu(g) * u) with
+ * g = fp16(acc_gate), u = fp16(acc_up) (runners/engine.py:228-235). */
+int lmps_gemv_q4_swiglu(const uint8_t* gate_packed, const uint16_t* gate_scales,
+                        const uint8_t* up_packed, const uint16_t* up_scales, const uint16_t* x,
+                        int ldx, uint16_t* y, int ldy, int rows, int k, int batch, void* stream);
+
+/* LM head GEMV + argmax.  Replaces runners/engine.py:171-181 (Q4 tied head
+ * GEMV, logits read-back, host argmax over fp32(logits) with first-index
+ * ties).  logits (may be NULL) receives fp16[batch, rows].  keys is a
+ * caller-owned uint64[batch] workspace that must be zero on entry and is left
+ * zero on return; token_ids receives int32[batch]. */
+int lmps_lm_head_argmax(const uint8_t* packed, const uint16_t* scales, const uint16_t* x,
+                        int ldx, uint16_t* logits, unsigned long long* keys,
+                        int32_t* token_ids, int rows, int k, int batch, void* stream);
+
+/* ---- normalisation / elementwise ---------------------------------------- */
+
+/* Replaces kernels/rms_norm.metal:14-19 `rms_norm_q4` (runners/engine.py:188-190,
+ * :224-226, :165-169): out = fp16(fp16(x * rsqrt(mean(x^2) + eps)) * gamma),
+ * reduced over the full vector.  x/out are [batch, dim]. */
+int lmps_rms_norm(const uint16_t* x, const uint16_t* gamma, uint16_t* out, int dim, int batch,
+                  float eps, void* stream);
+
+/* Replaces kernels/rope.metal:13-16 `apply_rope_q4` (runners/engine.py:198-200),
+ * in place on vec [batch, n_heads*head_dim] at position pos[b].  inv_freq is
+ * fp32[head_dim/2] (base^-(2i/head_dim)); style LMPS_ROPE_*. */
+int lmps_rope(uint16_t* vec, const int32_t* pos, const float* inv_freq, int n_heads,
+              int head_dim, int batch, int style, void* stream);
+
+/* Replaces kernels/residual.metal:13-20 `residual_add`: out = x + y (fp16). */
+int lmps_residual_add(const uint16_t* x, const uint16_t* y, uint16_t* out, int n, void* stream);
+
+/* Replaces kernels/swiglu.metal:13-23 `swiglu`. */
+int lmps_swiglu(const uint16_t* gate, const uint16_t* up, uint16_t* out, int n, void* stream);
+
+/* Replaces the embedding-row lookup of utils/tokenizer.py:22-26 on the device:
+ * out[b, :] = table[ids[b], :] for an fp16 [vocab, dim] table.  Ids outside
+ * [0, vocab) produce a zero row and set *bad_ids (may be NULL) to 1. */
+int lmps_embed_gather(const uint16_t* table, const int32_t* ids, uint16_t* out, int dim,
+                      int vocab, int batch, int32_t* bad_ids, void* stream);
+
+/* ---- attention ------------------------------------------------------------
+ * The reference's three-stage attention over a contiguous cache
+ * k_cache/v_cache [seq_len, n_kv_heads*head_dim] (kernels/attention.metal:33,
+ * kernels/attn_sum.metal:30), scores fp32 [n_q_heads, seq_len]. */
+
+/* Replaces kernels/attention.metal:13-18 `attention_scores` (engine.py:202-204). */
+int lmps_attention_scores(const uint16_t* q, const uint16_t* k_cache, float* scores,
+                          int seq_len, int n_q_heads, int n_kv_heads, int head_dim,
+                          void* stream);
+/* Replaces kernels/softmax.metal:14-18 `softmax` (engine.py:206-208), in place. */
+int lmps_softmax(float* scores, int seq_len, int n_heads, void* stream);
+/* Replaces kernels/attn_sum.metal:14-19 `attn_weighted_sum` (engine.py:210-212). */
+int lmps_attn_weighted_sum(const float* scores, const uint16_t* v_cache, uint16_t* out,
+                           int seq_len, int n_q_heads, int n_kv_heads, int head_dim,
+                           void* stream);
+
+/* Paged KV cache: one layer's K (and V) pool is fp16
+ * [n_pages, n_kv_heads, page_size, head_dim]; block_table is int32
+ * [batch, max_pages] mapping page j of sequence b to a pool page. */
+
+/* RoPE + KV append, the q/k half of runners/engine.py:198-200 plus the cache
+ * write the reference lacks (engine.py:90-91 hold one token).  qkv is the
+ * fused q|k|v GEMV output [batch, (n_q+2*n_kv)*head_dim]; q_out receives the
+ * rotated q [batch, n_q*head_dim]; rotated k and raw v go to position pos[b]. */
+int lmps_rope_kv_append(const uint16_t* qkv, const int32_t* pos, const float* inv_freq,
+                        uint16_t* q_out, uint16_t* k_pool, uint16_t* v_pool,
+                        const int32_t* block_table, int max_pages, int page_size,
+                        int n_q_heads, int n_kv_heads, int head_dim, int batch, int style,
+                        void* stream);
+
+/* Fused GQA decode attention (scores + softmax + weighted sum of
+ * kernels/attention.metal, softmax.metal, attn_sum.metal) over the paged
+ * cache for seq_lens[b] positions, split over the sequence with a
+ * log-sum-exp combine.  out is fp16 [batch, n_q_heads*head_dim].  workspace
+ * must hold lmps_gqa_attention_workspace_size(...) bytes. */
+int lmps_gqa_attention_splits(int batch, int n_kv_heads, int max_seq_len, int page_size);
+size_t lmps_gqa_attention_workspace_size(int batch, int n_q_heads, int head_dim, int n_splits);
+int lmps_gqa_decode_attention(const uint16_t* q, const uint16_t* k_pool, const uint16_t* v_pool,
+                              const int32_t* block_table, const int32_t* seq_lens, uint16_t* out,
+                              void* workspace, size_t workspace_bytes, int max_pages,
+                              int page_size, int n_q_heads, int n_kv_heads, int head_dim,
+                              int batch, int max_seq_len, int n_splits, void* stream);
+
+/* ---- weight format ---------------------------------------------------- */
+
+/* Device Q4 packer, bit-exact with utils/pack_weights.py:42-60
+ * `pack_tensor_4bit`: w is fp32[n]; packed receives ceil(n/32)*16 bytes and
+ * scales ceil(n/32) fp16 values (the tail group is zero-padded). */
+int lmps_q4_pack(const float* w, long long n, uint8_t* packed, uint16_t* scales, void* stream);
+
+/* ---- decode loop bookkeeping ------------------------------------------- */
+
+/* After an argmax: tokens[b] = next[b]; pos[b] += 1; seq_lens[b] += 1 and,
+ * when history != NULL, history[step[0]*batch + b] = next[b], step[0] += 1
+ * (history has room for max_steps rows; later steps are dropped). */
+int lmps_decode_advance(const int32_t* next, int32_t* tokens, int32_t* pos, int32_t* seq_lens,
+                        int32_t* history, int32_t* step, int max_steps, int batch,
+                        void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LLAMAMPS_B200_H_ */

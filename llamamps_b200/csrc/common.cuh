@@ -1,0 +1,98 @@
+// Shared helpers for the LlamaMPS B200 kernels (sm_100a).
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "../../include/llamamps_b200.h"
+
+#define LMPS_CHECK_ARG(cond)                      \
+  do {                                            \
+    if (!(cond)) return LMPS_ERR_INVALID_ARGUMENT; \
+  } while (0)
+
+// Status after a launch: 0, or the CUDA error code (always > 0).
+static inline int lmps_launch_status() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LMPS_OK : static_cast<int>(e);
+}
+
+static inline cudaStream_t lmps_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+static inline bool lmps_aligned(const void* p, uintptr_t a) {
+  return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
+}
+
+namespace lmps {
+
+constexpr int kWarp = 32;
+constexpr int kQ4Group = 32;        // elements per scale (utils/pack_weights.py:9)
+constexpr int kQ4GroupBytes = 16;   // 32 nibbles
+constexpr float kAttnScale = 0.088388f;  // kernels/attention.metal:40
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Sum over aligned segments of SEG lanes (SEG a power of two <= 32).
+template <int SEG>
+__device__ __forceinline__ float segment_sum(float v) {
+#pragma unroll
+  for (int o = SEG / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// 128-bit streaming load that bypasses L1 allocation (weights are read once).
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// Nibble k (k = 0..7) of a 32-bit word as the signed code (n - 8) in fp32.
+// 0x4B000000 is 2^23 as a float: OR-ing a 4-bit value into its mantissa gives
+// exactly 2^23 + n, and subtracting 2^23 + 8 leaves n - 8 with no rounding.
+__device__ __forceinline__ float nib_code(uint32_t w, int k) {
+  return __uint_as_float(0x4B000000u | ((w >> (4 * k)) & 0xFu)) - 8388616.0f;
+}
+
+// Order-preserving map of a float onto uint32 (larger float -> larger key).
+__device__ __forceinline__ uint32_t float_order_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// 64-bit argmax key: value in the high word, (0xffffffff - index) in the low
+// word, so that atomicMax keeps the largest value and, among equal values,
+// the smallest index -- numpy.argmax's first-index rule (runners/engine.py:181).
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
+  return (static_cast<unsigned long long>(float_order_key(v)) << 32) |
+         static_cast<unsigned long long>(0xFFFFFFFFu - idx);
+}
+
+__device__ __forceinline__ unsigned long long u64_max(unsigned long long a, unsigned long long b) {
+  return a > b ? a : b;
+}
+
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = u64_max(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  return (g / (1.0f + expf(-g))) * u;
+}
+
+}  // namespace lmps

@@ -1,0 +1,376 @@
+// Normalisation, RoPE + KV append, elementwise kernels, the reference's
+// three-stage attention drop-ins, the device Q4 packer and decode bookkeeping.
+#include <cmath>
+
+#include "common.cuh"
+
+namespace lmps {
+
+// ---------------------------------------------------------------------------
+// RMSNorm -- kernels/rms_norm.metal:20-39, reduced over the full vector (the
+// Metal launch at runners/engine.py:190 splits it over two threadgroups and
+// reads past its 32-entry partial-sum array; the intended math is used).
+// One CTA per row; scale = 1 / sqrt(sum(x^2)/dim + eps) with IEEE sqrt and
+// division; out = fp16(fp16(x*scale) * gamma).
+// ---------------------------------------------------------------------------
+constexpr int kNormThreads = 256;
+
+__device__ __forceinline__ float block_sum_256(float v, float* red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = (lane < kNormThreads / kWarp) ? red[lane] : 0.0f;
+  t = warp_sum(t);
+  __syncthreads();
+  return t;
+}
+
+__global__ void __launch_bounds__(kNormThreads)
+rms_norm_kernel(const __half* __restrict__ x, const __half* __restrict__ gamma,
+                __half* __restrict__ out, int dim, float eps) {
+  __shared__ float red[kNormThreads / kWarp];
+  const __half* xr = x + static_cast<size_t>(blockIdx.x) * dim;
+  __half* orow = out + static_cast<size_t>(blockIdx.x) * dim;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < dim; i += kNormThreads) {
+    const float v = __half2float(xr[i]);
+    ss = fmaf(v, v, ss);
+  }
+  ss = block_sum_256(ss, red);
+  const float scale = 1.0f / sqrtf(ss / static_cast<float>(dim) + eps);
+  for (int i = threadIdx.x; i < dim; i += kNormThreads) {
+    const __half nrm = __float2half_rn(__half2float(xr[i]) * scale);
+    orow[i] = __float2half_rn(__half2float(nrm) * __half2float(gamma[i]));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// RoPE -- kernels/rope.metal:19-40 with the position and frequency table as
+// inputs: angle = float(pos) * inv_freq[i]; (x1, x2) -> (x1 c - x2 s, x1 s + x2 c).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void rope_pair_index(int pair, int head_dim, int style, int& i1, int& i2,
+                                                int& fi) {
+  const int half_d = head_dim / 2;
+  const int h = pair / half_d;
+  const int j = pair - h * half_d;
+  if (style == LMPS_ROPE_INTERLEAVED) {
+    i1 = h * head_dim + 2 * j;
+    i2 = i1 + 1;
+  } else {
+    i1 = h * head_dim + j;
+    i2 = i1 + half_d;
+  }
+  fi = j;
+}
+
+__device__ __forceinline__ void rope_rotate(__half& a, __half& b, float ang) {
+  float s, c;
+  sincosf(ang, &s, &c);
+  const float x1 = __half2float(a), x2 = __half2float(b);
+  a = __float2half_rn(x1 * c - x2 * s);
+  b = __float2half_rn(x1 * s + x2 * c);
+}
+
+__global__ void rope_kernel(__half* vec, const int32_t* pos, const float* inv_freq, int n_heads,
+                            int head_dim, int style) {
+  const int b = blockIdx.y;
+  const int npairs = n_heads * head_dim / 2;
+  const float m = static_cast<float>(pos[b]);
+  __half* v = vec + static_cast<size_t>(b) * n_heads * head_dim;
+  for (int pr = blockIdx.x * blockDim.x + threadIdx.x; pr < npairs; pr += gridDim.x * blockDim.x) {
+    int i1, i2, fi;
+    rope_pair_index(pr, head_dim, style, i1, i2, fi);
+    __half a = v[i1], c = v[i2];
+    rope_rotate(a, c, m * inv_freq[fi]);
+    v[i1] = a;
+    v[i2] = c;
+  }
+}
+
+// RoPE on q and k of the fused q|k|v row, then the paged KV-cache append.
+__global__ void rope_kv_append_kernel(const __half* __restrict__ qkv, const int32_t* __restrict__ pos,
+                                      const float* __restrict__ inv_freq, __half* __restrict__ q_out,
+                                      __half* __restrict__ k_pool, __half* __restrict__ v_pool,
+                                      const int32_t* __restrict__ block_table, int max_pages,
+                                      int page_size, int n_q_heads, int n_kv_heads, int head_dim,
+                                      int style) {
+  const int b = blockIdx.x;
+  const int q_dim = n_q_heads * head_dim, kv_dim = n_kv_heads * head_dim;
+  const __half* row = qkv + static_cast<size_t>(b) * (q_dim + 2 * kv_dim);
+  const int p = pos[b];
+  const float m = static_cast<float>(p);
+  const int page = block_table[static_cast<size_t>(b) * max_pages + p / page_size];
+  const int off = p % page_size;
+  const int q_pairs = q_dim / 2, k_pairs = kv_dim / 2;
+  for (int t = threadIdx.x; t < q_pairs + k_pairs; t += blockDim.x) {
+    const bool is_q = t < q_pairs;
+    const int pr = is_q ? t : t - q_pairs;
+    int i1, i2, fi;
+    rope_pair_index(pr, head_dim, style, i1, i2, fi);
+    const __half* src = is_q ? row : row + q_dim;
+    __half a = src[i1], c = src[i2];
+    rope_rotate(a, c, m * inv_freq[fi]);
+    if (is_q) {
+      q_out[static_cast<size_t>(b) * q_dim + i1] = a;
+      q_out[static_cast<size_t>(b) * q_dim + i2] = c;
+    } else {
+      const int h1 = i1 / head_dim, h2 = i2 / head_dim;
+      k_pool[((static_cast<size_t>(page) * n_kv_heads + h1) * page_size + off) * head_dim + (i1 - h1 * head_dim)] = a;
+      k_pool[((static_cast<size_t>(page) * n_kv_heads + h2) * page_size + off) * head_dim + (i2 - h2 * head_dim)] = c;
+    }
+  }
+  const __half* vsrc = row + q_dim + kv_dim;
+  for (int i = threadIdx.x; i < kv_dim; i += blockDim.x) {
+    const int h = i / head_dim;
+    v_pool[((static_cast<size_t>(page) * n_kv_heads + h) * page_size + off) * head_dim + (i - h * head_dim)] = vsrc[i];
+  }
+}
+
+// residual.metal:19 and swiglu.metal:19-22.
+__global__ void residual_add_kernel(const __half* x, const __half* y, __half* out, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    out[i] = __hadd(x[i], y[i]);
+}
+
+__global__ void swiglu_kernel(const __half* g, const __half* u, __half* out, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    out[i] = __float2half_rn(silu_mul(__half2float(g[i]), __half2float(u[i])));
+}
+
+// utils/tokenizer.py:22-26 -- one fp16 row per sequence.
+__global__ void embed_gather_kernel(const __half* table, const int32_t* ids, __half* out, int dim,
+                                    int vocab, int32_t* bad) {
+  const int b = blockIdx.x;
+  const int id = ids[b];
+  const bool ok = id >= 0 && id < vocab;
+  if (!ok && threadIdx.x == 0 && bad) *bad = 1;
+  const __half* src = table + static_cast<size_t>(ok ? id : 0) * dim;
+  __half* dst = out + static_cast<size_t>(b) * dim;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) dst[i] = ok ? src[i] : __float2half_rn(0.0f);
+}
+
+// ---------------------------------------------------------------------------
+// The reference's three attention stages over a contiguous [seq, kv_dim]
+// cache, one thread per (head, position) / head / output element as in
+// attention.metal:22-40, softmax.metal:19-36, attn_sum.metal:21-33.
+// ---------------------------------------------------------------------------
+__global__ void attention_scores_kernel(const __half* q, const __half* k_cache, float* scores,
+                                        int seq_len, int n_q_heads, int n_kv_heads, int head_dim) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n_q_heads * seq_len) return;
+  const int h = idx / seq_len, i = idx - h * seq_len;
+  const int kvh = h / (n_q_heads / n_kv_heads);
+  const __half* qp = q + static_cast<size_t>(h) * head_dim;
+  const __half* kp = k_cache + static_cast<size_t>(i) * n_kv_heads * head_dim + kvh * head_dim;
+  float dot = 0.0f;
+  for (int d = 0; d < head_dim; ++d) dot = fmaf(__half2float(qp[d]), __half2float(kp[d]), dot);
+  scores[static_cast<size_t>(h) * seq_len + i] = dot * kAttnScale;
+}
+
+__global__ void softmax_kernel(float* scores, int seq_len) {
+  __shared__ float red[kNormThreads / kWarp];
+  float* s = scores + static_cast<size_t>(blockIdx.x) * seq_len;
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < seq_len; i += blockDim.x) m = fmaxf(m, s[i]);
+  m = warp_max(m);
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  m = (lane < kNormThreads / kWarp) ? red[lane] : -INFINITY;
+  m = warp_max(m);
+  __syncthreads();
+  float sum = 0.0f;
+  for (int i = threadIdx.x; i < seq_len; i += blockDim.x) {
+    const float e = expf(s[i] - m);
+    s[i] = e;
+    sum += e;
+  }
+  sum = block_sum_256(sum, red);
+  for (int i = threadIdx.x; i < seq_len; i += blockDim.x) s[i] = s[i] / sum;
+}
+
+__global__ void attn_weighted_sum_kernel(const float* scores, const __half* v_cache, __half* out,
+                                         int seq_len, int n_q_heads, int n_kv_heads, int head_dim) {
+  const int tid = blockIdx.x * blockDim.x + threadIdx.x;
+  if (tid >= n_q_heads * head_dim) return;
+  const int h = tid / head_dim, d = tid - h * head_dim;
+  const int kvh = h / (n_q_heads / n_kv_heads);
+  float acc = 0.0f;
+  for (int i = 0; i < seq_len; ++i)
+    acc = fmaf(scores[static_cast<size_t>(h) * seq_len + i],
+               __half2float(v_cache[static_cast<size_t>(i) * n_kv_heads * head_dim + kvh * head_dim + d]), acc);
+  out[tid] = __float2half_rn(acc);
+}
+
+// ---------------------------------------------------------------------------
+// Device Q4 packer -- utils/pack_weights.py:42-60: one thread per group of 32.
+// scale = max|w| / 7 (IEEE division), 0 -> 1; code = rint(w / scale) (ties to
+// even, like torch.round) clamped to [-8, 7]; nibble = code + 8; byte b =
+// nib[2b] | nib[2b+1] << 4; scale stored fp16 (round to nearest even).
+// ---------------------------------------------------------------------------
+__global__ void q4_pack_kernel(const float* __restrict__ w, long long n, uint8_t* __restrict__ packed,
+                               __half* __restrict__ scales, long long n_groups) {
+  for (long long g = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; g < n_groups;
+       g += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float v[32];
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const long long i = g * 32 + j;
+      v[j] = i < n ? w[i] : 0.0f;
+      amax = fmaxf(amax, fabsf(v[j]));
+    }
+    float scale = __fdiv_rn(amax, 7.0f);
+    if (scale == 0.0f) scale = 1.0f;
+    uint32_t words[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      float q = rintf(__fdiv_rn(v[j], scale));
+      q = fminf(fmaxf(q, -8.0f), 7.0f);
+      const uint32_t nib = static_cast<uint32_t>(static_cast<int>(q) + 8) & 0xFu;
+      words[j / 8] |= nib << (4 * (j % 8));
+    }
+    reinterpret_cast<uint4*>(packed)[g] = make_uint4(words[0], words[1], words[2], words[3]);
+    scales[g] = __float2half_rn(scale);
+  }
+}
+
+__global__ void decode_advance_kernel(const int32_t* next, int32_t* tokens, int32_t* pos,
+                                      int32_t* seq_lens, int32_t* history, int32_t* step,
+                                      int max_steps, int batch) {
+  const int s = (history && step) ? step[0] : 0;
+  for (int b = threadIdx.x; b < batch; b += blockDim.x) {
+    const int32_t t = next[b];
+    tokens[b] = t;
+    if (pos) pos[b] += 1;
+    if (seq_lens) seq_lens[b] += 1;
+    if (history && step && s < max_steps) history[static_cast<size_t>(s) * batch + b] = t;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && history && step) step[0] = s + 1;
+}
+
+}  // namespace lmps
+
+using namespace lmps;
+
+#define H(p) reinterpret_cast<__half*>(p)
+#define CH(p) reinterpret_cast<const __half*>(p)
+
+extern "C" int lmps_version(void) { return 100; }
+
+extern "C" const char* lmps_status_string(int status) {
+  switch (status) {
+    case LMPS_OK: return "ok";
+    case LMPS_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case LMPS_ERR_UNSUPPORTED: return "unsupported shape";
+    case LMPS_ERR_WORKSPACE: return "workspace too small";
+    case LMPS_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    default: break;
+  }
+  if (status > 0) return cudaGetErrorString(static_cast<cudaError_t>(status));
+  return "unknown status";
+}
+
+extern "C" int lmps_rms_norm(const uint16_t* x, const uint16_t* gamma, uint16_t* out, int dim,
+                             int batch, float eps, void* stream) {
+  LMPS_CHECK_ARG(x && gamma && out && dim > 0 && batch > 0 && eps >= 0.0f);
+  rms_norm_kernel<<<batch, kNormThreads, 0, lmps_stream(stream)>>>(CH(x), CH(gamma), H(out), dim, eps);
+  return lmps_launch_status();
+}
+
+extern "C" int lmps_rope(uint16_t* vec, const int32_t* pos, const float* inv_freq, int n_heads,
+                         int head_dim, int batch, int style, void* stream) {
+  LMPS_CHECK_ARG(vec && pos && inv_freq && n_heads > 0 && batch > 0);
+  LMPS_CHECK_ARG(head_dim > 0 && head_dim % 2 == 0);
+  LMPS_CHECK_ARG(style == LMPS_ROPE_INTERLEAVED || style == LMPS_ROPE_NEOX);
+  const int npairs = n_heads * head_dim / 2;
+  dim3 grid((npairs + 255) / 256, batch);
+  rope_kernel<<<grid, 256, 0, lmps_stream(stream)>>>(H(vec), pos, inv_freq, n_heads, head_dim, style);
+  return lmps_launch_status();
+}
+
+extern "C" int lmps_rope_kv_append(const uint16_t* qkv, const int32_t* pos, const float* inv_freq,
+                                   uint16_t* q_out, uint16_t* k_pool, uint16_t* v_pool,
+                                   const int32_t* block_table, int max_pages, int page_size,
+                                   int n_q_heads, int n_kv_heads, int head_dim, int batch,
+                                   int style, void* stream) {
+  LMPS_CHECK_ARG(qkv && pos && inv_freq && q_out && k_pool && v_pool && block_table);
+  LMPS_CHECK_ARG(max_pages > 0 && page_size > 0 && batch > 0 && head_dim > 0 && head_dim % 2 == 0);
+  LMPS_CHECK_ARG(n_kv_heads > 0 && n_q_heads > 0 && n_q_heads % n_kv_heads == 0);
+  LMPS_CHECK_ARG(style == LMPS_ROPE_INTERLEAVED || style == LMPS_ROPE_NEOX);
+  rope_kv_append_kernel<<<batch, 256, 0, lmps_stream(stream)>>>(
+      CH(qkv), pos, inv_freq, H(q_out), H(k_pool), H(v_pool), block_table, max_pages, page_size,
+      n_q_heads, n_kv_heads, head_dim, style);
+  return lmps_launch_status();
+}
+
+extern "C" int lmps_residual_add(const uint16_t* x, const uint16_t* y, uint16_t* out, int n,
+                                 void* stream) {
+  LMPS_CHECK_ARG(x && y && out && n > 0);
+  residual_add_kernel<<<(n + 255) / 256, 256, 0, lmps_stream(stream)>>>(CH(x), CH(y), H(out), n);
+  return lmps_launch_status();
+}
+
+extern "C" int lmps_swiglu(const uint16_t* gate, const uint16_t* up, uint16_t* out, int n,
+                           void* stream) {
+  LMPS_CHECK_ARG(gate && up && out && n > 0);
+  swiglu_kernel<<<(n + 255) / 256, 256, 0, lmps_stream(stream)>>>(CH(gate), CH(up), H(out), n);
+  return lmps_launch_status();
+}
+
+extern "C" int lmps_embed_gather(const uint16_t* table, const int32_t* ids, uint16_t* out, int dim,
+                                 int vocab, int batch, int32_t* bad_ids, void* stream) {
+  LMPS_CHECK_ARG(table && ids && out && dim > 0 && vocab > 0 && batch > 0);
+  embed_gather_kernel<<<batch, 256, 0, lmps_stream(stream)>>>(CH(table), ids, H(out), dim, vocab, bad_ids);
+  return lmps_launch_status();
+}
+
+extern "C" int lmps_attention_scores(const uint16_t* q, const uint16_t* k_cache, float* scores,
+                                     int seq_len, int n_q_heads, int n_kv_heads, int head_dim,
+                                     void* stream) {
+  LMPS_CHECK_ARG(q && k_cache && scores && seq_len > 0 && head_dim > 0);
+  LMPS_CHECK_ARG(n_kv_heads > 0 && n_q_heads > 0 && n_q_heads % n_kv_heads == 0);
+  const int n = n_q_heads * seq_len;
+  attention_scores_kernel<<<(n + 127) / 128, 128, 0, lmps_stream(stream)>>>(
+      CH(q), CH(k_cache), scores, seq_len, n_q_heads, n_kv_heads, head_dim);
+  return lmps_launch_status();
+}
+
+extern "C" int lmps_softmax(float* scores, int seq_len, int n_heads, void* stream) {
+  LMPS_CHECK_ARG(scores && seq_len > 0 && n_heads > 0);
+  softmax_kernel<<<n_heads, kNormThreads, 0, lmps_stream(stream)>>>(scores, seq_len);
+  return lmps_launch_status();
+}
+
+extern "C" int lmps_attn_weighted_sum(const float* scores, const uint16_t* v_cache, uint16_t* out,
+                                      int seq_len, int n_q_heads, int n_kv_heads, int head_dim,
+                                      void* stream) {
+  LMPS_CHECK_ARG(scores && v_cache && out && seq_len > 0 && head_dim > 0);
+  LMPS_CHECK_ARG(n_kv_heads > 0 && n_q_heads > 0 && n_q_heads % n_kv_heads == 0);
+  const int n = n_q_heads * head_dim;
+  attn_weighted_sum_kernel<<<(n + 127) / 128, 128, 0, lmps_stream(stream)>>>(
+      scores, CH(v_cache), H(out), seq_len, n_q_heads, n_kv_heads, head_dim);
+  return lmps_launch_status();
+}
+
+extern "C" int lmps_q4_pack(const float* w, long long n, uint8_t* packed, uint16_t* scales,
+                            void* stream) {
+  LMPS_CHECK_ARG(w && packed && scales && n > 0 && lmps_aligned(packed, 16));
+  const long long groups = (n + 31) / 32;
+  long long blocks = (groups + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  q4_pack_kernel<<<static_cast<unsigned>(blocks), 256, 0, lmps_stream(stream)>>>(w, n, packed, H(scales), groups);
+  return lmps_launch_status();
+}
+
+extern "C" int lmps_decode_advance(const int32_t* next, int32_t* tokens, int32_t* pos,
+                                   int32_t* seq_lens, int32_t* history, int32_t* step,
+                                   int max_steps, int batch, void* stream) {
+  LMPS_CHECK_ARG(next && tokens && batch > 0 && batch <= 4096);
+  LMPS_CHECK_ARG(!history || (step && max_steps > 0));
+  decode_advance_kernel<<<1, 256, 0, lmps_stream(stream)>>>(next, tokens, pos, seq_lens, history,
+                                                            step, max_steps, batch);
+  return lmps_launch_status();
+}

@@ -1,0 +1,294 @@
+"""QwenEngine on B200: the reference's engine API over the sm_100a kernels.
+
+Mirrors runners/engine.py:25-245:
+
+* ``QwenEngine(weights_dir, device=None)`` loads the reference's flat-.bin
+  layout (or takes ``weights=`` already on the device) -- but once, into HBM,
+  where the reference re-uploads 26 MB per layer per token (engine.py:145-155);
+* ``run_inference(input_vector) -> np.float16[V]`` runs one token through all
+  layers, the final norm and the LM head (engine.py:157-178); unlike the
+  reference it keeps a KV cache, so consecutive calls are consecutive
+  positions of one sequence (the first call is exactly the reference's
+  seq_len=1, position-0 forward);
+* ``predict_next_token(logits) -> int`` is the host argmax (engine.py:180-181).
+
+Added for the decode loop the reference does not have: ``generate`` (greedy,
+batch 1), ``generate_batch`` and ``decode_step`` (B independent sequences),
+a paged KV cache, the LM-head argmax on the device, and CUDA-graph replay of
+a whole decode step (one graph launch per token instead of 29
+command-buffer round trips, engine.py:176,244-245).
+
+A decode step per layer (kernel names from csrc/):
+    rms_norm -> gemv_q4_bias(q|k|v) -> rope_kv_append -> gqa_decode_attention
+    -> gemv_q4_residual(o) -> rms_norm -> gemv_q4_swiglu(gate, up)
+    -> gemv_q4_residual(down)
+then rms_norm(final) -> lm_head_argmax -> decode_advance.
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import kernels as K
+from ._lib import lib
+from .config import QWEN2_5_1_5B, ModelConfig
+from .kv_cache import PagedKVCache
+from .weights import ModelWeights, load_reference_layout
+
+
+def rope_inv_freq(head_dim: int, theta: float) -> np.ndarray:
+    """base^-(2i/head_dim) in fp32 (kernels/rope.metal:28-30 with idx % 128 = 2i)."""
+    i2 = np.arange(0, head_dim, 2, dtype=np.float32)
+    return np.power(np.float32(theta), -(i2 / np.float32(head_dim))).astype(np.float32)
+
+
+class QwenEngine:
+    def __init__(self, weights_dir: Optional[str] = None, device=None, *,
+                 weights: Optional[ModelWeights] = None, config: ModelConfig = QWEN2_5_1_5B,
+                 max_batch: int = 1, max_seq_len: int = 2048, page_size: int = 64,
+                 use_graphs: bool = True, page_order: Optional[List[int]] = None):
+        if not torch.cuda.is_available():
+            raise RuntimeError("QwenEngine needs a CUDA device (B200); there is no CPU path.")
+        self.device = torch.device(device if device is not None else "cuda")
+        lib()  # fail loudly now if the native library is missing
+        if weights is None:
+            if weights_dir is None:
+                raise ValueError("pass weights_dir (reference .bin layout) or weights=")
+            weights = load_reference_layout(weights_dir, config, self.device)
+        self.weights = weights
+        self.cfg = weights.cfg
+        self.weights_dir = weights_dir
+        self.layers = len(weights.layers)
+        self.hidden_dim = self.cfg.hidden
+        self.mlp_intermediate = self.cfg.intermediate
+        self.max_batch = max_batch
+        self.use_graphs = use_graphs
+        self.cache = PagedKVCache(self.cfg, self.layers, max_batch, max_seq_len, page_size,
+                                  self.device, page_order=page_order)
+        self.max_seq_len = self.cache.max_seq_len
+        self.n_splits = K.attention_splits(max_batch, self.cfg.n_kv_heads, self.max_seq_len, page_size)
+        self._create_buffer_pool()
+        self._graphs = {}
+        self.batch = 1
+        self.reset(1)
+
+    # -- buffers (runners/engine.py:84-118, plus decode state) ---------------
+    def _create_buffer_pool(self) -> None:
+        c, B, dev = self.cfg, self.max_batch, self.device
+        h = torch.float16
+        self.buf_residual = torch.zeros(B, c.hidden, dtype=h, device=dev)
+        self.buf_normed = torch.zeros(B, c.hidden, dtype=h, device=dev)
+        self.buf_qkv = torch.zeros(B, c.qkv_rows, dtype=h, device=dev)
+        self.buf_q = torch.zeros(B, c.q_dim, dtype=h, device=dev)
+        self.buf_attn = torch.zeros(B, c.q_dim, dtype=h, device=dev)
+        self.buf_mlp = torch.zeros(B, c.intermediate, dtype=h, device=dev)
+        self.buf_logits = torch.zeros(B, c.vocab, dtype=h, device=dev)
+        ws = K.attention_workspace_size(B, c.n_q_heads, c.head_dim, self.n_splits)
+        self.attn_ws = torch.zeros(max(ws, 16), dtype=torch.uint8, device=dev)
+        self.inv_freq = torch.from_numpy(rope_inv_freq(c.head_dim, c.rope_theta)).to(dev)
+        i32 = torch.int32
+        self.tokens = torch.zeros(B, dtype=i32, device=dev)
+        self.pos = torch.zeros(B, dtype=i32, device=dev)
+        self.seq_lens = torch.ones(B, dtype=i32, device=dev)
+        self.next_ids = torch.zeros(B, dtype=i32, device=dev)
+        self.argmax_keys = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.bad_ids = torch.zeros(1, dtype=i32, device=dev)
+        self.history = torch.zeros(1, B, dtype=i32, device=dev)
+        self.step_counter = torch.zeros(1, dtype=i32, device=dev)
+        self._pin_vec = torch.zeros(c.hidden, dtype=h).pin_memory()
+        self._pin_logits = torch.zeros(c.vocab, dtype=h).pin_memory()
+        self._pin_ids = torch.zeros(B, dtype=i32).pin_memory()
+        self._pin_next = torch.zeros(B, dtype=i32).pin_memory()
+
+    def reset(self, batch: Optional[int] = None, start_pos: int = 0) -> None:
+        """Start ``batch`` fresh sequences (slots 0..batch-1) at ``start_pos``."""
+        b = self.batch if batch is None else batch
+        if not 1 <= b <= self.max_batch:
+            raise ValueError(f"batch {b} outside [1, {self.max_batch}]")
+        self.batch = b
+        self.cache.release_all()
+        for s in range(b):
+            self.cache.reserve(s, self.max_seq_len)
+        self.pos.fill_(start_pos)
+        self.seq_lens.fill_(start_pos + 1)
+        self.step_counter.zero_()
+        self.host_pos = start_pos
+
+    # -- one forward over the current tokens/pos ----------------------------
+    def _layers(self, B: int) -> None:
+        c, w = self.cfg, self.weights
+        x = self.buf_residual[:B]
+        xn = self.buf_normed[:B]
+        for li, lw in enumerate(w.layers):
+            kp, vp = self.cache.layer(li)
+            K.rms_norm(x, lw.in_norm, c.eps, out=xn)
+            K.gemv_q4_bias(lw.qkv_packed, lw.qkv_scales, lw.qkv_bias, xn, c.qkv_rows, c.hidden,
+                           out=self.buf_qkv[:B])
+            K.rope_kv_append(self.buf_qkv[:B], self.pos, self.inv_freq, self.buf_q[:B], kp, vp,
+                             self.cache.block_table, self.cache.page_size, c.n_q_heads,
+                             c.n_kv_heads, c.head_dim, c.rope_style_code)
+            K.gqa_decode_attention(self.buf_q[:B], kp, vp, self.cache.block_table, self.seq_lens,
+                                   self.buf_attn[:B], self.attn_ws, self.cache.page_size,
+                                   c.n_q_heads, c.n_kv_heads, c.head_dim, self.max_seq_len,
+                                   self.n_splits)
+            K.gemv_q4_residual(lw.o_packed, lw.o_scales, self.buf_attn[:B], x, c.hidden, c.q_dim, out=x)
+            K.rms_norm(x, lw.post_norm, c.eps, out=xn)
+            K.gemv_q4_swiglu(lw.gate_packed, lw.gate_scales, lw.up_packed, lw.up_scales, xn,
+                             c.intermediate, c.hidden, out=self.buf_mlp[:B])
+            K.gemv_q4_residual(lw.down_packed, lw.down_scales, self.buf_mlp[:B], x, c.hidden,
+                               c.intermediate, out=x)
+
+    def _head(self, B: int, want_logits: bool) -> None:
+        c, w = self.cfg, self.weights
+        K.rms_norm(self.buf_residual[:B], w.final_norm, c.eps, out=self.buf_normed[:B])
+        K.lm_head_argmax(w.lm_packed, w.lm_scales, self.buf_normed[:B], c.vocab, c.hidden,
+                         self.argmax_keys[:B], self.next_ids[:B],
+                         logits=self.buf_logits[:B] if want_logits else None)
+
+    def _device_step(self, B: int, want_logits: bool = False, record: bool = True) -> None:
+        """Embed -> layers -> head -> advance; device-only, graph-capturable."""
+        K.embed_gather(self.weights.embed, self.tokens[:B], self.buf_residual[:B], self.bad_ids)
+        self._layers(B)
+        self._head(B, want_logits)
+        K.decode_advance(self.next_ids[:B], self.tokens[:B], self.pos[:B], self.seq_lens[:B],
+                         self.history if record else None, self.step_counter if record else None)
+
+    # -- reference API -------------------------------------------------------
+    def _vector_step(self) -> None:
+        """Layers + head + advance from buf_residual[0] (run_inference's body)."""
+        self._layers(1)
+        self._head(1, want_logits=True)
+        K.decode_advance(self.next_ids[:1], self.tokens[:1], self.pos[:1], self.seq_lens[:1])
+
+    def run_inference(self, input_vector: np.ndarray) -> np.ndarray:
+        """engine.py:157-178 for sequence 0: one embedding vector in, fp16 logits out.
+
+        The vector goes through pinned host memory; the whole forward is one
+        CUDA-graph replay; the fp16 logits come back through pinned memory."""
+        if self.batch != 1:
+            self.reset(1)
+        if self.host_pos >= self.max_seq_len:
+            raise RuntimeError("KV cache full")
+        vec = np.ascontiguousarray(input_vector, dtype=np.float16).reshape(-1)
+        if vec.size != self.cfg.hidden:
+            raise ValueError(f"input vector has {vec.size} elements, expected {self.cfg.hidden}")
+        self._pin_vec.numpy()[:] = vec
+        self.buf_residual[0].copy_(self._pin_vec, non_blocking=True)
+        if self.use_graphs:
+            self._graph_for(1, record=False, vector=True).replay()
+        else:
+            self._vector_step()
+        self._pin_logits.copy_(self.buf_logits[0], non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        self.host_pos += 1
+        return self._pin_logits.numpy().copy()
+
+    def predict_next_token(self, logits: np.ndarray) -> int:
+        """engine.py:180-181: argmax over fp32(logits), first index on ties."""
+        return int(np.argmax(np.asarray(logits).astype(np.float32)))
+
+    # -- decode loop ---------------------------------------------------------
+    def _graph_for(self, B: int, record: bool, vector: bool = False):
+        key = (B, record, vector)
+        g = self._graphs.get(key)
+        if g is None:
+            def body():
+                if vector:
+                    self._vector_step()
+                else:
+                    self._device_step(B, record=record)
+            # Warm every launch path once outside capture (kernel attributes,
+            # lazy module loading), then restore the state the warm-up touched.
+            state = (self.tokens, self.pos, self.seq_lens, self.step_counter, self.buf_residual)
+            saved = [t.clone() for t in state]
+            body()
+            torch.cuda.synchronize(self.device)
+            for t, sv in zip(state, saved):
+                t.copy_(sv)
+            g = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream(self.device)
+            s.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(g, stream=s):
+                    body()
+            torch.cuda.current_stream(self.device).wait_stream(s)
+            for t, sv in zip(state, saved):
+                t.copy_(sv)
+            torch.cuda.synchronize(self.device)
+            self._graphs[key] = g
+        return g
+
+    def launches_per_step(self) -> int:
+        """Kernels one decode step launches (what a graph replay runs)."""
+        per_layer = 8 + (1 if self.n_splits > 1 else 0)
+        return 1 + self.layers * per_layer + 1 + 2 + 1
+
+    def step_tokens(self, token_ids) -> np.ndarray:
+        """Public streaming step: host ids [batch] in (pinned H2D), one graph
+        replay, the next ids [batch] out (pinned D2H)."""
+        B = self.batch
+        ids = np.ascontiguousarray(token_ids, dtype=np.int32).reshape(-1)
+        if ids.size != B:
+            raise ValueError(f"expected {B} token ids")
+        self._pin_ids.numpy()[:B] = ids
+        self.tokens[:B].copy_(self._pin_ids[:B], non_blocking=True)
+        self.decode_step(record=False)
+        self._pin_next.copy_(self.tokens, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return self._pin_next.numpy()[:B].copy()
+
+    def decode_step(self, record: bool = True) -> None:
+        """Advance every active sequence by one token (device-resident state)."""
+        B = self.batch
+        if self.host_pos >= self.max_seq_len:
+            raise RuntimeError("KV cache full")
+        if self.use_graphs:
+            self._graph_for(B, record).replay()
+        else:
+            self._device_step(B, record=record)
+        self.host_pos += 1
+
+    def _ensure_history(self, steps: int) -> None:
+        if self.history.shape[0] < steps or self.history.shape[1] != self.max_batch:
+            self.history = torch.zeros(steps, self.max_batch, dtype=torch.int32, device=self.device)
+            self._graphs.clear()  # graphs captured the old history pointer
+
+    def prefill(self, prompts: torch.Tensor) -> None:
+        """Feed prompt tokens [B, P] position by position (causal); afterwards
+        ``tokens`` holds each sequence's first generated token."""
+        B, P = prompts.shape
+        if P + 1 > self.max_seq_len:
+            raise ValueError("prompt longer than the KV cache")
+        prompts = prompts.to(self.device, torch.int32)
+        for t in range(P):
+            self.tokens[:B].copy_(prompts[:, t])
+            if t == P - 1:
+                self.step_counter.zero_()
+            self.decode_step(record=True)
+
+    def generate_batch(self, prompts, max_new_tokens: int) -> np.ndarray:
+        """Greedy decode of B equal-length prompts; returns int32 [B, max_new_tokens]."""
+        p = torch.as_tensor(np.asarray(prompts), dtype=torch.int32)
+        if p.dim() == 1:
+            p = p[None]
+        B, P = p.shape
+        if P + max_new_tokens > self.max_seq_len:
+            raise ValueError("prompt + generation exceed the KV cache")
+        self._ensure_history(max_new_tokens)
+        self.reset(B)
+        self.prefill(p)
+        for _ in range(max_new_tokens - 1):
+            self.decode_step(record=True)
+        torch.cuda.synchronize(self.device)
+        if int(self.bad_ids.item()) != 0:
+            self.bad_ids.zero_()
+            raise ValueError("token id outside the vocabulary")
+        # decode_advance writes row-major [step, B] with the active batch as stride
+        hist = self.history.reshape(-1)[: max_new_tokens * B].reshape(max_new_tokens, B)
+        return hist.t().cpu().numpy()
+
+    def generate(self, token_ids: Sequence[int], max_new_tokens: int) -> List[int]:
+        """Greedy continuation of one prompt (the demo.py flow with a real prompt)."""
+        return [int(t) for t in self.generate_batch(np.asarray(token_ids)[None], max_new_tokens)[0]]

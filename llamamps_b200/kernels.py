@@ -1,0 +1,196 @@
+"""Torch-tensor front end of the C ABI: shape/dtype checks, then one call.
+
+Each function mirrors one reference kernel (named in its docstring) and
+launches on torch's current CUDA stream, so the calls compose with torch
+streams and can be captured into CUDA graphs.  Outputs may be passed in
+(``out=``) so that a decode step allocates nothing.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from ._lib import call, lib
+
+FP16 = torch.float16
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _dev(t: torch.Tensor, name: str, dtype=None):
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor (the decode path has no CPU fallback)")
+    if dtype is not None and t.dtype != dtype:
+        raise TypeError(f"{name}: expected {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t.data_ptr()
+
+
+def _x2d(x: torch.Tensor):
+    x2 = x if x.dim() == 2 else x.reshape(1, -1)
+    return x2, x2.shape[0]
+
+
+def gemv_q4(packed, scales, x, rows: int, k: int, out: Optional[torch.Tensor] = None):
+    """kernels/quant_matmul.metal `gemv_q4_0`: y[b] = W x[b] (fp32 accumulate)."""
+    x2, B = _x2d(x)
+    y = out if out is not None else torch.empty(B, rows, dtype=FP16, device=x.device)
+    call("lmps_gemv_q4_0", _dev(packed, "packed", torch.uint8), _dev(scales, "scales", FP16),
+         _dev(x2, "x", FP16), k, _dev(y, "y", FP16), rows, rows, k, B, _stream())
+    return y if x.dim() == 2 else y.reshape(-1)
+
+
+def gemv_q4_bias(packed, scales, bias, x, rows: int, k: int, out=None):
+    x2, B = _x2d(x)
+    y = out if out is not None else torch.empty(B, rows, dtype=FP16, device=x.device)
+    call("lmps_gemv_q4_bias", _dev(packed, "packed", torch.uint8), _dev(scales, "scales", FP16),
+         _dev(bias, "bias", FP16), _dev(x2, "x", FP16), k, _dev(y, "y", FP16), rows, rows, k, B,
+         _stream())
+    return y if x.dim() == 2 else y.reshape(-1)
+
+
+def gemv_q4_residual(packed, scales, x, residual, rows: int, k: int, out=None):
+    """GEMV + kernels/residual.metal: out = residual + fp16(W x).  out may be residual."""
+    x2, B = _x2d(x)
+    r2 = residual if residual.dim() == 2 else residual.reshape(1, -1)
+    y = out if out is not None else torch.empty(B, rows, dtype=FP16, device=x.device)
+    call("lmps_gemv_q4_residual", _dev(packed, "packed", torch.uint8), _dev(scales, "scales", FP16),
+         _dev(x2, "x", FP16), k, _dev(r2, "residual", FP16), _dev(y, "y", FP16), rows, rows, k, B,
+         _stream())
+    return y if x.dim() == 2 else y.reshape(-1)
+
+
+def gemv_q4_swiglu(gate_packed, gate_scales, up_packed, up_scales, x, rows: int, k: int, out=None):
+    """gate/up GEMVs + kernels/swiglu.metal in one pass."""
+    x2, B = _x2d(x)
+    y = out if out is not None else torch.empty(B, rows, dtype=FP16, device=x.device)
+    call("lmps_gemv_q4_swiglu", _dev(gate_packed, "gate_packed", torch.uint8),
+         _dev(gate_scales, "gate_scales", FP16), _dev(up_packed, "up_packed", torch.uint8),
+         _dev(up_scales, "up_scales", FP16), _dev(x2, "x", FP16), k, _dev(y, "y", FP16), rows,
+         rows, k, B, _stream())
+    return y if x.dim() == 2 else y.reshape(-1)
+
+
+def lm_head_argmax(packed, scales, x, rows: int, k: int, keys: torch.Tensor, ids: torch.Tensor,
+                   logits: Optional[torch.Tensor] = None):
+    """runners/engine.py:171-181 on the device: Q4 LM head + first-index argmax."""
+    x2, B = _x2d(x)
+    call("lmps_lm_head_argmax", _dev(packed, "packed", torch.uint8), _dev(scales, "scales", FP16),
+         _dev(x2, "x", FP16), k, _dev(logits, "logits", FP16) if logits is not None else None,
+         _dev(keys, "keys", torch.int64), _dev(ids, "ids", torch.int32), rows, k, B, _stream())
+    return ids
+
+
+def rms_norm(x, gamma, eps: float = 1e-6, out=None):
+    """kernels/rms_norm.metal `rms_norm_q4` (full-vector reduction)."""
+    x2, B = _x2d(x)
+    y = out if out is not None else torch.empty_like(x2)
+    call("lmps_rms_norm", _dev(x2, "x", FP16), _dev(gamma, "gamma", FP16), _dev(y, "out", FP16),
+         x2.shape[1], B, float(eps), _stream())
+    return y if x.dim() == 2 else y.reshape(-1)
+
+
+def rope_(vec, pos, inv_freq, n_heads: int, head_dim: int, style: int = 0):
+    """kernels/rope.metal `apply_rope_q4`, in place, per-row position."""
+    v2, B = _x2d(vec)
+    call("lmps_rope", _dev(v2, "vec", FP16), _dev(pos, "pos", torch.int32),
+         _dev(inv_freq, "inv_freq", torch.float32), n_heads, head_dim, B, style, _stream())
+    return vec
+
+
+def residual_add(x, y, out=None):
+    o = out if out is not None else torch.empty_like(x)
+    call("lmps_residual_add", _dev(x, "x", FP16), _dev(y, "y", FP16), _dev(o, "out", FP16),
+         x.numel(), _stream())
+    return o
+
+
+def swiglu(gate, up, out=None):
+    o = out if out is not None else torch.empty_like(gate)
+    call("lmps_swiglu", _dev(gate, "gate", FP16), _dev(up, "up", FP16), _dev(o, "out", FP16),
+         gate.numel(), _stream())
+    return o
+
+
+def embed_gather(table, ids, out, bad: Optional[torch.Tensor] = None):
+    V, D = table.shape
+    call("lmps_embed_gather", _dev(table, "table", FP16), _dev(ids, "ids", torch.int32),
+         _dev(out, "out", FP16), D, V, ids.numel(),
+         _dev(bad, "bad", torch.int32) if bad is not None else None, _stream())
+    return out
+
+
+def attention_scores(q, k_cache, seq_len: int, n_q_heads: int, n_kv_heads: int, head_dim: int, out=None):
+    s = out if out is not None else torch.empty(n_q_heads, seq_len, dtype=torch.float32, device=q.device)
+    call("lmps_attention_scores", _dev(q, "q", FP16), _dev(k_cache, "k_cache", FP16),
+         _dev(s, "scores", torch.float32), seq_len, n_q_heads, n_kv_heads, head_dim, _stream())
+    return s
+
+
+def softmax_(scores, seq_len: int, n_heads: int):
+    call("lmps_softmax", _dev(scores, "scores", torch.float32), seq_len, n_heads, _stream())
+    return scores
+
+
+def attn_weighted_sum(scores, v_cache, seq_len: int, n_q_heads: int, n_kv_heads: int, head_dim: int, out=None):
+    o = out if out is not None else torch.empty(n_q_heads * head_dim, dtype=FP16, device=scores.device)
+    call("lmps_attn_weighted_sum", _dev(scores, "scores", torch.float32), _dev(v_cache, "v_cache", FP16),
+         _dev(o, "out", FP16), seq_len, n_q_heads, n_kv_heads, head_dim, _stream())
+    return o
+
+
+def rope_kv_append(qkv, pos, inv_freq, q_out, k_pool, v_pool, block_table, page_size: int,
+                   n_q_heads: int, n_kv_heads: int, head_dim: int, style: int = 0):
+    B = qkv.shape[0]
+    call("lmps_rope_kv_append", _dev(qkv, "qkv", FP16), _dev(pos, "pos", torch.int32),
+         _dev(inv_freq, "inv_freq", torch.float32), _dev(q_out, "q_out", FP16),
+         _dev(k_pool, "k_pool", FP16), _dev(v_pool, "v_pool", FP16),
+         _dev(block_table, "block_table", torch.int32), block_table.shape[1], page_size,
+         n_q_heads, n_kv_heads, head_dim, B, style, _stream())
+    return q_out
+
+
+def attention_splits(batch: int, n_kv_heads: int, max_seq_len: int, page_size: int) -> int:
+    return int(lib().lmps_gqa_attention_splits(batch, n_kv_heads, max_seq_len, page_size))
+
+
+def attention_workspace_size(batch: int, n_q_heads: int, head_dim: int, n_splits: int) -> int:
+    return int(lib().lmps_gqa_attention_workspace_size(batch, n_q_heads, head_dim, n_splits))
+
+
+def gqa_decode_attention(q, k_pool, v_pool, block_table, seq_lens, out, workspace,
+                         page_size: int, n_q_heads: int, n_kv_heads: int, head_dim: int,
+                         max_seq_len: int, n_splits: int):
+    """Fused attention.metal + softmax.metal + attn_sum.metal over the paged cache."""
+    B = q.shape[0]
+    ws_ptr = workspace.data_ptr() if workspace is not None and workspace.numel() else None
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    call("lmps_gqa_decode_attention", _dev(q, "q", FP16), _dev(k_pool, "k_pool", FP16),
+         _dev(v_pool, "v_pool", FP16), _dev(block_table, "block_table", torch.int32),
+         _dev(seq_lens, "seq_lens", torch.int32), _dev(out, "out", FP16), ws_ptr, ws_bytes,
+         block_table.shape[1], page_size, n_q_heads, n_kv_heads, head_dim, B, max_seq_len,
+         n_splits, _stream())
+    return out
+
+
+def q4_pack_device(w: torch.Tensor):
+    """utils/pack_weights.py `pack_tensor_4bit` on the device (bit-exact)."""
+    n = w.numel()
+    groups = (n + 31) // 32
+    packed = torch.empty(groups * 16, dtype=torch.uint8, device=w.device)
+    scales = torch.empty(groups, dtype=FP16, device=w.device)
+    call("lmps_q4_pack", _dev(w, "w", torch.float32), n, packed.data_ptr(), scales.data_ptr(), _stream())
+    return packed, scales
+
+
+def decode_advance(next_ids, tokens, pos, seq_lens, history=None, step=None):
+    B = tokens.numel()
+    max_steps = history.shape[0] if history is not None else 0
+    call("lmps_decode_advance", _dev(next_ids, "next", torch.int32), _dev(tokens, "tokens", torch.int32),
+         _dev(pos, "pos", torch.int32), _dev(seq_lens, "seq_lens", torch.int32),
+         _dev(history, "history", torch.int32) if history is not None else None,
+         _dev(step, "step", torch.int32) if step is not None else None, max_steps, B, _stream())

@@ -1,0 +1,63 @@
+"""The C-ABI library loads and exports every symbol include/llamamps_b200.h
+declares; argument validation rejects bad calls before any device work.
+No kernel runs here (no GPU)."""
+import ctypes
+import subprocess
+
+import pytest
+
+from llamamps_b200 import _lib
+from llamamps_b200.build import LIB_PATH
+
+
+def test_library_exports_every_header_symbol():
+    L = _lib.lib()
+    syms = _lib.header_symbols()
+    assert len(syms) >= 20
+    missing = [s for s in syms if not hasattr(L, s)]
+    assert not missing, f"not exported: {missing}"
+    out = subprocess.run(["nm", "-D", "--defined-only", LIB_PATH], capture_output=True, text=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    assert set(syms) <= exported
+
+
+def test_every_header_symbol_has_a_python_signature():
+    assert set(_lib.header_symbols()) == set(_lib._SIGS)
+
+
+def test_status_strings():
+    assert _lib.status_string(0) == "ok"
+    assert "argument" in _lib.status_string(-1)
+    assert "workspace" in _lib.status_string(-3)
+    assert "timed out" in _lib.status_string(-4)
+    assert _lib.lib().lmps_version() >= 100
+
+
+@pytest.mark.parametrize("call", [
+    lambda L: L.lmps_gemv_q4_0(None, None, None, 1536, None, 1536, 1536, 1536, 1, None),
+    lambda L: L.lmps_gemv_q4_0(16, 16, 16, 1536, 16, 1536, 1536, 1500, 1, None),   # k % 32
+    lambda L: L.lmps_gemv_q4_0(16, 16, 16, 1536, 16, 1536, 1536, 1536, 9, None),   # batch > 8
+    lambda L: L.lmps_gemv_q4_0(17, 16, 16, 1536, 16, 1536, 1536, 1536, 1, None),   # misaligned
+    lambda L: L.lmps_rms_norm(16, 16, 16, 0, 1, 1e-6, None),
+    lambda L: L.lmps_rope(16, 16, 16, 12, 127, 1, 0, None),                        # odd head_dim
+    lambda L: L.lmps_rope(16, 16, 16, 12, 128, 1, 7, None),                        # bad style
+    lambda L: L.lmps_gqa_decode_attention(16, 16, 16, 16, 16, 16, None, 0, 1, 64, 12, 5, 128, 1, 64, 1, None),
+    lambda L: L.lmps_q4_pack(16, 0, 16, 16, None),
+])
+def test_invalid_arguments_rejected(call):
+    assert call(_lib.lib()) == -1
+
+
+def test_attention_unsupported_head_dim_and_workspace():
+    L = _lib.lib()
+    assert L.lmps_gqa_decode_attention(16, 16, 16, 16, 16, 16, None, 0, 1, 64, 12, 2, 64, 1, 64, 1, None) == -2
+    need = L.lmps_gqa_attention_workspace_size(1, 12, 128, 4)
+    assert need == 12 * 4 * (128 * 4 + 8)
+    assert L.lmps_gqa_decode_attention(16, 16, 16, 16, 16, 16, 16, need - 1, 1, 64, 12, 2, 128, 1, 64, 4, None) == -3
+
+
+def test_split_heuristic():
+    L = _lib.lib()
+    assert L.lmps_gqa_attention_splits(1, 2, 160, 64) == 3        # bounded by 64-position tiles
+    assert L.lmps_gqa_attention_splits(4, 2, 32768 + 128, 64) == 37
+    assert L.lmps_gqa_attention_splits(64, 2, 384, 64) == 3

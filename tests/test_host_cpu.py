@@ -1,0 +1,83 @@
+"""Host-side logic on CPU tensors: weight layout round trip, KV paging, sizes."""
+import numpy as np
+import pytest
+import torch
+
+from llamamps_b200.config import QWEN2_5_1_5B, ModelConfig
+from llamamps_b200.kv_cache import PagedKVCache
+from llamamps_b200 import weights as W
+
+SMALL = ModelConfig(hidden=128, intermediate=256, vocab=512, n_layers=2, n_q_heads=4, n_kv_heads=2,
+                    head_dim=32)
+
+
+def test_algorithmic_bytes():
+    c = QWEN2_5_1_5B
+    assert c.layer_q4_bytes() == 26_320_896
+    assert c.step_weight_bytes() == 868_550_656
+    assert c.kv_bytes_per_position() == 28_672
+
+
+def test_reference_layout_roundtrip(tmp_path):
+    mw = W.synth_model(SMALL, seed=3, device="cpu")
+    W.save_reference_layout(mw, str(tmp_path))
+    assert (tmp_path / "layer1" / "q_proj_4bit.bin").exists()
+    assert (tmp_path / "global" / "embed_tokens.bin").exists()
+    back = W.load_reference_layout(str(tmp_path), SMALL, device="cpu")
+    for a, b in zip(mw.layers, back.layers):
+        for f in ("qkv_packed", "qkv_scales", "qkv_bias", "o_packed", "down_scales", "in_norm"):
+            assert torch.equal(getattr(a, f), getattr(b, f)), f
+    assert torch.equal(mw.lm_packed, back.lm_packed) and torch.equal(mw.embed, back.embed)
+
+
+def test_missing_weight_file_raises(tmp_path):
+    with pytest.raises(FileNotFoundError, match="Missing weight file"):
+        W.load_reference_layout(str(tmp_path), SMALL, device="cpu")
+
+
+def test_wrong_sized_weight_file_rejected(tmp_path):
+    mw = W.synth_model(SMALL, seed=3, device="cpu")
+    W.save_reference_layout(mw, str(tmp_path))
+    np.zeros(10, np.uint8).tofile(tmp_path / "layer0" / "o_proj_4bit.bin")
+    with pytest.raises(ValueError, match="o_proj"):
+        W.load_reference_layout(str(tmp_path), SMALL, device="cpu")
+
+
+def test_host_arrays_match_packed_layout():
+    mw = W.synth_model(SMALL, seed=4, device="cpu")
+    d = W.layer_host_arrays(mw.layers[0], SMALL)
+    assert d["q"].size == SMALL.q_dim * SMALL.hidden // 2
+    assert d["k"].size == d["v"].size == SMALL.kv_dim * SMALL.hidden // 2
+    assert d["bq"].size == SMALL.q_dim and d["bv"].size == SMALL.kv_dim
+
+
+def test_paged_cache_permuted_pages_roundtrip():
+    order = list(np.random.default_rng(0).permutation(2 * 3))
+    kv = PagedKVCache(SMALL, n_layers=2, max_batch=2, max_seq_len=40, page_size=16, device="cpu",
+                      page_order=order)
+    rng = np.random.default_rng(1)
+    k = torch.from_numpy(rng.normal(0, 1, (37, SMALL.kv_dim)).astype(np.float16))
+    v = torch.from_numpy(rng.normal(0, 1, (37, SMALL.kv_dim)).astype(np.float16))
+    kv.write_positions(1, 1, 0, k, v)
+    assert kv.pages(1) == order[:3]
+    kb, vb = kv.read_positions(1, 1, 37)
+    assert torch.equal(kb, k) and torch.equal(vb, v)
+    assert kv.block_table[1].tolist() == order[:3]
+
+
+def test_paged_cache_exhaustion_and_release():
+    kv = PagedKVCache(SMALL, 1, max_batch=2, max_seq_len=32, page_size=16, device="cpu", n_pages=3)
+    kv.reserve(0, 32)
+    with pytest.raises(MemoryError):
+        kv.reserve(1, 32)
+    kv.release(0)
+    kv.reserve(1, 32)
+    with pytest.raises(ValueError):
+        kv.reserve(1, 33)
+
+
+def test_synth_one_layer_case_shapes():
+    parts, x, kp, vp = W.synth_one_layer_case(QWEN2_5_1_5B, seed=0)
+    assert parts["gate_packed"].size == 8960 * 1536 // 2 and parts["down_scales"].size == 8960 * 1536 // 32
+    assert x.shape == (1536,) and kp.shape == (31, 256) and vp.shape == (31, 256)
+    assert x.dtype == np.float16
