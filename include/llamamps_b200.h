@@ -151,6 +151,27 @@ int lmps_gqa_decode_attention(const uint16_t* q, const uint16_t* k_pool, const u
                               int page_size, int n_q_heads, int n_kv_heads, int head_dim,
                               int batch, int max_seq_len, int n_splits, void* stream);
 
+/* Size of the fixed device scratch used by lmps_gqa_decode_attention_noalloc. */
+#define LMPS_GQA_ATTENTION_NOALLOC_SCRATCH_BYTES (4u * 1024u * 1024u)
+
+/* No counterpart in the reference.  lmps_gqa_decode_attention for callers
+ * that cannot allocate device memory where they call it (a binding that only
+ * receives device pointers from another runtime, code under a global-mode
+ * stream capture, a serving loop that bans allocation after warm-up): the
+ * split partials live in a 4 MiB array compiled into the library and resident
+ * on every GPU that loads it until exit, so no workspace is passed and nothing
+ * is allocated.  The first call on each device looks the array's device
+ * address up (cudaGetSymbolAddress) and should come before any stream
+ * capture.  Returns LMPS_ERR_WORKSPACE without launching when
+ * lmps_gqa_attention_workspace_size(batch, n_q_heads, head_dim, n_splits)
+ * exceeds LMPS_GQA_ATTENTION_NOALLOC_SCRATCH_BYTES.  All calls share the
+ * array: calls that overlap on the GPU race. */
+int lmps_gqa_decode_attention_noalloc(const uint16_t* q, const uint16_t* k_pool,
+                                      const uint16_t* v_pool, const int32_t* block_table,
+                                      const int32_t* seq_lens, uint16_t* out, int max_pages,
+                                      int page_size, int n_q_heads, int n_kv_heads, int head_dim,
+                                      int batch, int max_seq_len, int n_splits, void* stream);
+
 /* ---- weight format ---------------------------------------------------- */
 
 /* Device Q4 packer, bit-exact with utils/pack_weights.py:42-60

@@ -42,6 +42,8 @@ _SIGS = {
     "lmps_gqa_attention_workspace_size": (c_size, [c_int, c_int, c_int, c_int]),
     "lmps_gqa_decode_attention": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_size, c_int,
                                           c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_vp]),
+    "lmps_gqa_decode_attention_noalloc": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int,
+                                                  c_int, c_int, c_int, c_int, c_int, c_int, c_vp]),
     "lmps_q4_pack": (c_int, [c_vp, c_ll, c_vp, c_vp, c_vp]),
     "lmps_decode_advance": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_vp]),
 }

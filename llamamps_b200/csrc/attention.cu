@@ -283,3 +283,74 @@ extern "C" int lmps_gqa_decode_attention(const uint16_t* q, const uint16_t* k_po
   gqa_combine_kernel<<<dim3(n_q_heads, batch), kHeadDim, 0, st>>>(P);
   return lmps_launch_status();
 }
+
+// ---------------------------------------------------------------------------
+// lmps_gqa_decode_attention_noalloc: the same attention with its split
+// partials kept in a fixed, library-owned device array instead of a
+// caller-provided workspace.
+//
+// Who needs it: callers that cannot allocate device memory where they call
+// the attention -- a foreign-language binding that only receives device
+// pointers from another runtime and has no allocator behind this C interface,
+// code running under a global-mode stream capture (where cudaMalloc is not
+// permitted), or a serving loop that forbids allocation after warm-up because
+// cudaMalloc/cudaFree can synchronise the device.
+//
+// The array below is LMPS_GQA_ATTENTION_NOALLOC_SCRATCH_BYTES (4 MiB) and is
+// resident on every GPU that loads this library until the process exits.  In
+// host code its name is only a host-side stand-in, not a device address, so
+// the host looks the device address up with cudaGetSymbolAddress, once per
+// device (with that device current) on the first call made on that device,
+// and hands that address to the kernels as their workspace.  That first call
+// should therefore come before any stream capture.  Every call shares the one
+// array and it keeps whatever the previous call left there; nothing in it has
+// to start at zero, because the combine kernel only reads partial slots that
+// the partial kernel of the same call has written.  Calls whose work overlaps
+// on the GPU (different streams, or different host threads without ordering)
+// race on the array.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[LMPS_GQA_ATTENTION_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_scratch_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of the scratch array on the current device (looked up once).
+int noalloc_scratch_address(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return LMPS_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) return e != cudaSuccess ? static_cast<int>(e) : LMPS_ERR_UNSUPPORTED;
+    g_noalloc_scratch_ptr[dev] = p;
+  }
+  *out = g_noalloc_scratch_ptr[dev];
+  return LMPS_OK;
+}
+}  // namespace
+
+extern "C" int lmps_gqa_decode_attention_noalloc(const uint16_t* q, const uint16_t* k_pool,
+                                                 const uint16_t* v_pool,
+                                                 const int32_t* block_table,
+                                                 const int32_t* seq_lens, uint16_t* out,
+                                                 int max_pages, int page_size, int n_q_heads,
+                                                 int n_kv_heads, int head_dim, int batch,
+                                                 int max_seq_len, int n_splits, void* stream) {
+  if (batch <= 0 || n_q_heads <= 0 || head_dim <= 0 || n_splits < 1) return LMPS_ERR_INVALID_ARGUMENT;
+  const size_t need = lmps_gqa_attention_workspace_size(batch, n_q_heads, head_dim, n_splits);
+  if (need > LMPS_GQA_ATTENTION_NOALLOC_SCRATCH_BYTES) return LMPS_ERR_WORKSPACE;
+  void* scratch = nullptr;
+  const int st = noalloc_scratch_address(&scratch);
+  if (st != LMPS_OK) return st;
+  return lmps_gqa_decode_attention(q, k_pool, v_pool, block_table, seq_lens, out, scratch,
+                                   LMPS_GQA_ATTENTION_NOALLOC_SCRATCH_BYTES, max_pages, page_size,
+                                   n_q_heads, n_kv_heads, head_dim, batch, max_seq_len, n_splits,
+                                   stream);
+}
