@@ -246,7 +246,7 @@ def run_ours(args):
     B = 1
     mw = synth_model(cfg, seed=1, device=dev)
     max_seq = PROMPT_LEN + args.warmup + 2 * args.steps + 8
-    eng = QwenEngine(weights=mw, device=dev, max_batch=B, max_seq_len=max_seq)
+    eng = QwenEngine(weights=mw, device=dev, max_batch=B, max_seq_len=max_seq, decoder=args.decoder)
     prompt = np.random.default_rng(1 + rank).integers(0, cfg.vocab, (B, PROMPT_LEN))
     eng.reset(B)
     eng.prefill(torch.from_numpy(prompt))
@@ -265,10 +265,11 @@ def run_ours(args):
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         e0.record(st)
-        for _ in range(args.steps):
-            eng.decode_step(record=False)
+        eng.decode_steps(args.steps, record=False)   # persistent: one launch for all K steps
         e1.record(st)
         torch.cuda.synchronize()
+    if eng.pdec is not None:
+        eng.pdec.check_error()
     barrier()
     t_local = e0.elapsed_time(e1) / 1e3
     t = torch.tensor([t_local], dtype=torch.float64, device=dev)
@@ -300,9 +301,21 @@ def run_ours(args):
     e2e_value = world * args.steps / float(te.item())
 
     peak, peak_kind = _peaks()
-    roof = gemv_roofline(eng, peak, peak_kind)
-    step_bytes = cfg.step_weight_bytes() + cfg.kv_bytes_per_position() * (PROMPT_LEN + args.warmup + args.steps / 2)
+    # algorithmic bytes of one decode step: all Q4 weights + norms + biases +
+    # one embedding row, plus K and V of every attended position
+    mean_T = PROMPT_LEN + args.warmup + (args.steps + 1) / 2
+    step_bytes = cfg.step_weight_bytes() + cfg.kv_bytes_per_position() * mean_T
     step_gbs = step_bytes / (t_max / args.steps) / 1e9
+    if eng.pdec is not None:
+        roof = {"kernel": "decode_persistent_kernel<1> (one launch = all timed steps)", "bound": "hbm",
+                "achieved": round(step_gbs, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                "frac": round(step_gbs / peak, 4), "traffic": None,
+                "bytes_per_step": int(step_bytes), "steps_per_launch": args.steps,
+                "us_per_step": round(t_max / args.steps * 1e6, 2)}
+        gemv = None
+    else:
+        roof = gemv_roofline(eng, peak, peak_kind)
+        gemv = roof
     clocks = clk.summary()
     if rank == 0:
         line = {
@@ -318,11 +331,13 @@ def run_ours(args):
                        "l2": "inputs larger than L2"},
             "roofline": roof,
             "step_roofline": {"bytes_per_step": int(step_bytes), "achieved_gbs": round(step_gbs, 1),
-                              "peak": peak, "frac": round(step_gbs / peak, 4), "unit": "GB/s"},
+                              "peak": peak, "frac": round(step_gbs / peak, 4), "unit": "GB/s",
+                              "frac_of_8TBs": round(step_gbs / 8000.0, 4)},
+            "decoder": eng.decoder,
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": cfg.hidden * 2,
                     "d2h_bytes_per_step": cfg.vocab * 2,
                     "api": "QwenEngine.run_inference + predict_next_token"},
-            "gpu_launches": eng.launches_per_step() * args.steps,
+            "gpu_launches": 1 if eng.pdec is not None else eng.launches_per_step() * args.steps,
             "clocks": clocks,
         }
         if not args.no_cpu_baseline:
@@ -340,6 +355,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decoder", choices=["persistent", "kernels"], default=None)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -188,6 +188,78 @@ int lmps_decode_advance(const int32_t* next, int32_t* tokens, int32_t* pos, int3
                         int32_t* history, int32_t* step, int max_steps, int batch,
                         void* stream);
 
+/* ---- persistent decode step -----------------------------------------------
+ * The whole of runners/engine.py:157-181 (28 x _execute_block, final norm,
+ * LM head, argmax) for `batch` sequences as ONE cooperative kernel launch of
+ * one CTA per SM, repeated for n_steps tokens: weights stream from HBM into a
+ * shared-memory ring through TMA bulk copies issued by a producer warp while
+ * consumer warps compute, and stages hand activations to each other through
+ * device-side counters instead of kernel boundaries. */
+
+typedef struct lmps_layer_desc {
+  const uint8_t* qkv_packed;    /* [n_q+2*n_kv)*head_dim, hidden] Q4 (q|k|v rows) */
+  const uint16_t* qkv_scales;
+  const uint16_t* qkv_bias;     /* fp16 [(n_q+2*n_kv)*head_dim] */
+  const uint8_t* o_packed;      /* [hidden, n_q*head_dim] */
+  const uint16_t* o_scales;
+  const uint8_t* gate_packed;   /* [intermediate, hidden] */
+  const uint16_t* gate_scales;
+  const uint8_t* up_packed;     /* [intermediate, hidden] */
+  const uint16_t* up_scales;
+  const uint8_t* down_packed;   /* [hidden, intermediate] */
+  const uint16_t* down_scales;
+  const uint16_t* in_norm;      /* fp16 [hidden] */
+  const uint16_t* post_norm;    /* fp16 [hidden] */
+  uint16_t* k_pool;             /* fp16 [n_pages, n_kv, page_size, head_dim] */
+  uint16_t* v_pool;
+} lmps_layer_desc;
+
+typedef struct lmps_model_desc {
+  int n_layers, hidden, intermediate, vocab, n_q_heads, n_kv_heads, head_dim;
+  float eps;
+  int rope_style;                   /* LMPS_ROPE_* */
+  const lmps_layer_desc* layers;    /* DEVICE array of n_layers descriptors */
+  const uint16_t* final_norm;       /* fp16 [hidden] */
+  const uint8_t* lm_packed;         /* [vocab, hidden] Q4 tied head */
+  const uint16_t* lm_scales;
+  const uint16_t* embed;            /* fp16 [vocab, hidden] */
+  const float* inv_freq;            /* fp32 [head_dim/2] */
+} lmps_model_desc;
+
+typedef struct lmps_decode_state {
+  int batch, page_size, max_pages, max_seq_len;
+  const int32_t* block_table;   /* [batch, max_pages] */
+  int32_t* tokens;              /* [batch] token fed at the next step; updated */
+  int32_t* pos;                 /* [batch] position of that token; updated */
+  const int32_t* forced;        /* [batch, forced_stride] tokens fed after steps 0..n_forced-1 (or NULL) */
+  int forced_stride, n_forced;
+  const uint16_t* x_in;         /* fp16 [batch, hidden] replaces the step-0 embedding (or NULL) */
+  uint16_t* logits;             /* fp16 [batch, vocab] of the last step (or NULL) */
+  int32_t* history;             /* [history_rows, batch] argmax of every step (or NULL) */
+  int32_t* step_counter;        /* [1] history row of the first step (rows outside
+                                   [0, history_rows) are skipped); advanced by n_steps */
+  int history_rows;
+  void* workspace;              /* lmps_decode_persistent_workspace_size() bytes, zeroed once */
+  size_t workspace_bytes;
+  int32_t* error;               /* [1] set to 1 when a bounded device wait gives up */
+} lmps_decode_state;
+
+/* Bytes of workspace the persistent step needs (activations, split partials,
+ * counters).  The workspace must be zero-filled before the first call; each
+ * call leaves it ready for the next one. */
+size_t lmps_decode_persistent_workspace_size(const lmps_model_desc* model, int batch,
+                                             int max_seq_len);
+
+/* Run n_steps decode steps (1 <= batch <= 4, head_dim 128, hidden a multiple
+ * of 512 and <= 2048, intermediate a multiple of 256).  model/state are HOST
+ * structs (copied into the launch).  Failures found on the device are reported
+ * through state->error, which the caller reads after synchronising: 1 = a
+ * bounded wait timed out, 2 = a position past max_seq_len or a token id
+ * outside the vocabulary (nothing ran), 3 = no finite logit.  After a non-zero
+ * error the workspace must be zeroed again. */
+int lmps_decode_persistent(const lmps_model_desc* model, const lmps_decode_state* state,
+                           int n_steps, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -48,7 +48,8 @@ class QwenEngine:
     def __init__(self, weights_dir: Optional[str] = None, device=None, *,
                  weights: Optional[ModelWeights] = None, config: ModelConfig = QWEN2_5_1_5B,
                  max_batch: int = 1, max_seq_len: int = 2048, page_size: int = 64,
-                 use_graphs: bool = True, page_order: Optional[List[int]] = None):
+                 use_graphs: bool = True, page_order: Optional[List[int]] = None,
+                 decoder: Optional[str] = None):
         if not torch.cuda.is_available():
             raise RuntimeError("QwenEngine needs a CUDA device (B200); there is no CPU path.")
         self.device = torch.device(device if device is not None else "cuda")
@@ -71,6 +72,19 @@ class QwenEngine:
         self.n_splits = K.attention_splits(max_batch, self.cfg.n_kv_heads, self.max_seq_len, page_size)
         self._create_buffer_pool()
         self._graphs = {}
+        # "persistent": one cooperative kernel per launch runs whole decode
+        # steps (csrc/decode_persistent.cu, batch <= 4); "kernels": one kernel
+        # per stage, replayed as a CUDA graph (any batch <= 8).
+        from .persistent import MAX_BATCH as PERSISTENT_MAX_BATCH
+        if decoder is None:
+            decoder = "persistent" if max_batch <= PERSISTENT_MAX_BATCH else "kernels"
+        if decoder not in ("persistent", "kernels"):
+            raise ValueError(f"unknown decoder {decoder!r}")
+        self.decoder = decoder
+        self.pdec = None
+        if decoder == "persistent":
+            from .persistent import PersistentDecoder
+            self.pdec = PersistentDecoder(self.weights, self.cache, self.inv_freq, max_batch)
         self.batch = 1
         self.reset(1)
 
@@ -176,12 +190,17 @@ class QwenEngine:
             raise ValueError(f"input vector has {vec.size} elements, expected {self.cfg.hidden}")
         self._pin_vec.numpy()[:] = vec
         self.buf_residual[0].copy_(self._pin_vec, non_blocking=True)
-        if self.use_graphs:
+        if self.pdec is not None:
+            self.pdec.run(1, self.tokens, self.pos, 1, x_in=self.buf_residual[:1],
+                          logits=self.buf_logits[:1])
+        elif self.use_graphs:
             self._graph_for(1, record=False, vector=True).replay()
         else:
             self._vector_step()
         self._pin_logits.copy_(self.buf_logits[0], non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
+        if self.pdec is not None:
+            self.pdec.check_error()
         self.host_pos += 1
         return self._pin_logits.numpy().copy()
 
@@ -221,7 +240,10 @@ class QwenEngine:
         return g
 
     def launches_per_step(self) -> int:
-        """Kernels one decode step launches (what a graph replay runs)."""
+        """Kernels one decode step launches (what a graph replay runs); the
+        persistent decoder runs any number of steps in one launch."""
+        if self.pdec is not None:
+            return 1
         per_layer = 8 + (1 if self.n_splits > 1 else 0)
         return 1 + self.layers * per_layer + 1 + 2 + 1
 
@@ -237,18 +259,33 @@ class QwenEngine:
         self.decode_step(record=False)
         self._pin_next.copy_(self.tokens, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
+        if self.pdec is not None:
+            self.pdec.check_error()
         return self._pin_next.numpy()[:B].copy()
 
     def decode_step(self, record: bool = True) -> None:
         """Advance every active sequence by one token (device-resident state)."""
+        self.decode_steps(1, record)
+
+    def decode_steps(self, n: int, record: bool = True) -> None:
+        """Advance every active sequence by ``n`` tokens: one persistent launch,
+        or ``n`` graph replays of the per-stage kernels."""
         B = self.batch
-        if self.host_pos >= self.max_seq_len:
+        if n <= 0:
+            return
+        if self.host_pos + n > self.max_seq_len:
             raise RuntimeError("KV cache full")
-        if self.use_graphs:
-            self._graph_for(B, record).replay()
+        if self.pdec is not None:
+            self.pdec.run(B, self.tokens, self.pos, n,
+                          history=self.history if record else None,
+                          step_counter=self.step_counter if record else None)
         else:
-            self._device_step(B, record=record)
-        self.host_pos += 1
+            for _ in range(n):
+                if self.use_graphs:
+                    self._graph_for(B, record).replay()
+                else:
+                    self._device_step(B, record=record)
+        self.host_pos += n
 
     def _ensure_history(self, steps: int) -> None:
         if self.history.shape[0] < steps or self.history.shape[1] != self.max_batch:
@@ -262,6 +299,18 @@ class QwenEngine:
         if P + 1 > self.max_seq_len:
             raise ValueError("prompt longer than the KV cache")
         prompts = prompts.to(self.device, torch.int32)
+        if self.pdec is not None:
+            # tokens <- prompt[:, 0]; steps 0..P-2 feed prompt[:, 1:]; the last
+            # step's argmax (the first generated token) lands in history row 0.
+            self.tokens[:B].copy_(prompts[:, 0])
+            forced = prompts[:, 1:].contiguous() if P > 1 else None
+            self.step_counter.fill_(-(P - 1))
+            if self.host_pos + P > self.max_seq_len:
+                raise RuntimeError("KV cache full")
+            self.pdec.run(B, self.tokens, self.pos, P, forced=forced, history=self.history,
+                          step_counter=self.step_counter)
+            self.host_pos += P
+            return
         for t in range(P):
             self.tokens[:B].copy_(prompts[:, t])
             if t == P - 1:
@@ -277,11 +326,14 @@ class QwenEngine:
         if P + max_new_tokens > self.max_seq_len:
             raise ValueError("prompt + generation exceed the KV cache")
         self._ensure_history(max_new_tokens)
+        if int(p.min()) < 0 or int(p.max()) >= self.cfg.vocab:
+            raise ValueError("token id outside the vocabulary")
         self.reset(B)
         self.prefill(p)
-        for _ in range(max_new_tokens - 1):
-            self.decode_step(record=True)
+        self.decode_steps(max_new_tokens - 1, record=True)
         torch.cuda.synchronize(self.device)
+        if self.pdec is not None:
+            self.pdec.check_error()
         if int(self.bad_ids.item()) != 0:
             self.bad_ids.zero_()
             raise ValueError("token id outside the vocabulary")

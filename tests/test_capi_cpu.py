@@ -22,7 +22,25 @@ def test_library_exports_every_header_symbol():
 
 
 def test_every_header_symbol_has_a_python_signature():
-    assert set(_lib.header_symbols()) == set(_lib._SIGS)
+    from llamamps_b200 import persistent
+    assert set(_lib.header_symbols()) == set(_lib._SIGS) | set(persistent._SIGS)
+
+
+def test_persistent_descriptor_layouts_match_the_header():
+    """ctypes mirrors of lmps_layer_desc / lmps_model_desc / lmps_decode_state."""
+    import ctypes
+    from llamamps_b200 import persistent as P
+    assert ctypes.sizeof(P.LayerDesc) == 15 * 8
+    assert P.ModelDesc.layers.offset == 40 and ctypes.sizeof(P.ModelDesc) == 40 + 6 * 8
+    assert P.DecodeState.block_table.offset == 16 and P.DecodeState.error.offset == 112
+    L = _lib.lib()
+    P._declare()
+    m = P.ModelDesc(28, 1536, 8960, 151936, 12, 2, 128, 1e-6, 0, None, None, None, None, None, None)
+    ws = L.lmps_decode_persistent_workspace_size(ctypes.byref(m), 1, 4096)
+    assert ws > 0 and ws % 256 == 0
+    # argument validation happens before any device work
+    st = P.DecodeState()
+    assert L.lmps_decode_persistent(ctypes.byref(m), ctypes.byref(st), 1, None) == -1
 
 
 def test_status_strings():
