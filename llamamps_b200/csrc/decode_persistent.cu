@@ -40,12 +40,12 @@
 namespace lmps {
 namespace pk {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kConsumers = kConsumerWarps * kWarp;        // 256
+constexpr int kConsumerWarps = 11;   // + 1 producer warp = 12 warps (registers are allocated per 4 warps)
+constexpr int kConsumers = kConsumerWarps * kWarp;        // 352
 constexpr int kThreads = kConsumers + kWarp;              // + producer warp
-constexpr int kSlotBytes = 20480;
-constexpr int kRows1536 = 16;     // rows per ring chunk when k = hidden
-constexpr int kPairsGU = 8;       // gate/up row pairs per chunk
+constexpr int kSlotBytes = 20160;
+constexpr int kRows1536 = 2 * kConsumerWarps;  // rows per ring chunk when k = hidden
+constexpr int kPairsGU = kConsumerWarps;    // gate/up row pairs per chunk
 constexpr int kRowsDown = 4;      // rows per chunk when k = intermediate
 constexpr int kAttnTile = 64;
 constexpr int kHD = 128;
@@ -101,48 +101,7 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-
-__device__ __forceinline__ float fma_hhf(uint16_t a, uint16_t b, float c) {
-  float d;
-  asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
-  return d;
-}
-__device__ __forceinline__ uint16_t lo16(uint32_t v) { return static_cast<uint16_t>(v & 0xFFFFu); }
-__device__ __forceinline__ uint16_t hi16(uint32_t v) { return static_cast<uint16_t>(v >> 16); }
-
-// 8 nibbles of w (elements e0..e7) times 8 fp16 activations, fp32 accumulate.
-__device__ __forceinline__ float dot8(uint32_t w, const uint4& xv, float acc) {
-  const uint32_t kMask = 0x000F000Fu, kMagic = 0x64006400u;
-  const __half2 kBias = __halves2half2(__ushort_as_half(0xE408u), __ushort_as_half(0xE408u));
-  uint32_t t0 = (w & kMask) | kMagic, t1 = ((w >> 4) & kMask) | kMagic;
-  uint32_t t2 = ((w >> 8) & kMask) | kMagic, t3 = ((w >> 12) & kMask) | kMagic;
-  __half2 h0 = __hadd2(*reinterpret_cast<__half2*>(&t0), kBias);
-  __half2 h1 = __hadd2(*reinterpret_cast<__half2*>(&t1), kBias);
-  __half2 h2 = __hadd2(*reinterpret_cast<__half2*>(&t2), kBias);
-  __half2 h3 = __hadd2(*reinterpret_cast<__half2*>(&t3), kBias);
-  const uint32_t c0 = *reinterpret_cast<uint32_t*>(&h0), c1 = *reinterpret_cast<uint32_t*>(&h1);
-  const uint32_t c2 = *reinterpret_cast<uint32_t*>(&h2), c3 = *reinterpret_cast<uint32_t*>(&h3);
-  acc = fma_hhf(lo16(c0), lo16(xv.x), acc);
-  acc = fma_hhf(lo16(c1), hi16(xv.x), acc);
-  acc = fma_hhf(lo16(c2), lo16(xv.y), acc);
-  acc = fma_hhf(lo16(c3), hi16(xv.y), acc);
-  acc = fma_hhf(hi16(c0), lo16(xv.z), acc);
-  acc = fma_hhf(hi16(c1), hi16(xv.z), acc);
-  acc = fma_hhf(hi16(c2), lo16(xv.w), acc);
-  acc = fma_hhf(hi16(c3), hi16(xv.w), acc);
-  return acc;
-}
-__device__ __forceinline__ int xswz(int vi) { return (vi & ~7) | ((vi & 7) ^ ((vi >> 3) & 7)); }
-__device__ __forceinline__ float group_dot(const uint4& wv, const uint4* xrow, int g) {
-  const int v0 = g * 4;
-  const uint4 x0 = xrow[xswz(v0)], x1 = xrow[xswz(v0 + 1)];
-  const uint4 x2 = xrow[xswz(v0 + 2)], x3 = xrow[xswz(v0 + 3)];
-  float a0 = dot8(wv.x, x0, 0.0f), a1 = dot8(wv.y, x1, 0.0f);
-  a0 = dot8(wv.z, x2, a0);
-  a1 = dot8(wv.w, x3, a1);
-  return a0 + a1;
-}
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory"); }
 
 struct Params {
   lmps_model_desc m;
@@ -175,6 +134,7 @@ struct Smem {
   float* red8;       // [8 * kMaxB] block-reduction scratch
   unsigned long long* best;  // [8 warps][kMaxB]
   int* misc;         // [0] abort, [1] is_last, [2..] tok[kMaxB], pos[kMaxB]
+  float* inv_freq;   // [head_dim/2] RoPE frequencies, staged once per launch
 };
 
 __device__ __forceinline__ void row_range(int rows, int cta, int ctas, int& r0, int& r1) {
@@ -219,6 +179,19 @@ __device__ __forceinline__ Chunking stage_chunks(const Params& P, int kind, int 
   return c;
 }
 
+// Optional timeline: one %globaltimer stamp per event and row (see the header).
+__device__ __forceinline__ void trace_event(const Params& P, int row, int& ev,
+                                            unsigned long long wait_ns = ~0ull) {
+  if (P.s.trace) {
+    if (ev < P.s.trace_events) {
+      P.s.trace[static_cast<size_t>(row) * P.s.trace_events + ev] = globaltimer();
+      if (wait_ns != ~0ull)   // consumer rows: cumulative ring wait in rows [2*grid, 3*grid)
+        P.s.trace[(static_cast<size_t>(row) + 2 * gridDim.x) * P.s.trace_events + ev] = wait_ns;
+    }
+    ++ev;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Producer: one lane streams every chunk of every stage into the ring.
 // ---------------------------------------------------------------------------
@@ -226,6 +199,7 @@ __device__ void producer(const Params& P, Smem& S) {
   const uint64_t policy = evict_first_policy();
   uint32_t chunk = 0;
   bool ok = true;
+  int pev = 0;
   const int kinds[4] = {ST_QKV, ST_O, ST_GU, ST_DN};
   for (int step = 0; step < P.n_steps && ok; ++step) {
     for (int l = 0; l <= P.m.n_layers && ok; ++l) {
@@ -235,6 +209,7 @@ __device__ void producer(const Params& P, Smem& S) {
         const Chunking c = stage_chunks(P, kind, l);
         const size_t row_bytes = static_cast<size_t>(c.k) / 2;
         const size_t row_scales = static_cast<size_t>(c.k) / 32;
+        trace_event(P, gridDim.x + blockIdx.x, pev);
         for (int r = c.r0; r < c.r1 && ok; r += c.rows_per_chunk, ++chunk) {
           const int n = min(c.rows_per_chunk, c.r1 - r);
           const int slot = chunk % P.slots;
@@ -265,6 +240,7 @@ __device__ void producer(const Params& P, Smem& S) {
             bulk_g2s(dst + pbytes, c.s + r * row_scales, sbytes, &S.full[slot], policy);
           }
         }
+        trace_event(P, gridDim.x + blockIdx.x, pev);
       }
     }
   }
@@ -288,6 +264,7 @@ struct CState {
   uint32_t chunk;     // ring chunk counter (same sequence as the producer)
   uint32_t arrivals;  // grid arrivals expected so far
   bool ok;
+  unsigned long long wait_ns;  // time thread 0 spent waiting for ring chunks (timeline only)
 };
 
 // All CTAs finished the previous stage?  Thread 0 polls, then the consumers sync.
@@ -325,6 +302,7 @@ __device__ void slot_wait(Smem& S, const Params& P, CState& cs, int& slot) {
   slot = cs.chunk % P.slots;
   const uint32_t phase = (cs.chunk / P.slots) & 1u;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(&S.misc[0]);
+  if (mbar_try_wait(&S.full[slot], phase)) return;
   const uint64_t t0 = globaltimer();
   while (!mbar_try_wait(&S.full[slot], phase)) {
     if (*abort_flag) return;
@@ -334,6 +312,7 @@ __device__ void slot_wait(Smem& S, const Params& P, CState& cs, int& slot) {
       return;
     }
   }
+  if (P.s.trace && threadIdx.x == 0) cs.wait_ns += globaltimer() - t0;
 }
 
 __device__ __forceinline__ void slot_release(Smem& S, CState& cs, int slot) {
@@ -354,14 +333,92 @@ __device__ __forceinline__ float consumer_sum(float v, float* red8) {
   return t;
 }
 
-// act[b] <- fp16(fp16(x*scale) * gamma) with x = rows[b] (k elements, swizzled
-// 16-byte chunks) -- rms_norm.metal:20-39 over the full vector.
+// ---------------------------------------------------------------------------
+// Activation planes.  A staged activation vector (RMSNorm'd x, attention
+// output, SwiGLU output) is kept per 32-element group -- the Q4 group of the
+// weights it meets -- as a 16-bit block fixed point X = rint(x * 2^(15-e)),
+// with e the smallest exponent such that every |x| of the group is < 2^e,
+// split into a signed high byte H and an unsigned low byte L (X = 256 H + L).
+// With the weight nibbles n (0..15) as bytes, dp4a gives the group's dot
+// product exactly in integers:
+//     sum_k (n_k - 8) X_k = 256 * sum n H + sum n L - 8 * sum X,
+// and the fp32 accumulation across groups applies scale * 2^(e-15) once per
+// group.  The only rounding is x -> X (below 2^-15 of the group's largest
+// |x|).  Word layout of one group: He[4] Ho[4] Le[4] Lo[4]; word c of He holds
+// H of elements 8c, 8c+2, 8c+4, 8c+6 (the low nibbles of packed bytes
+// 4c..4c+3), Ho the odd elements 8c+1, 8c+3, 8c+5, 8c+7.
+// ---------------------------------------------------------------------------
+struct Planes {
+  uint32_t* w;  // [NB][G][16]
+  float* scl;   // [NB][G]   2^(e-15)
+  int* xs8;     // [NB][G]   8 * sum X
+  int G;
+};
+
+__device__ __forceinline__ Planes planes_view(Smem& S, int G, int nb) {
+  Planes pl;
+  pl.w = reinterpret_cast<uint32_t*>(S.act);
+  pl.scl = reinterpret_cast<float*>(pl.w + static_cast<size_t>(nb) * G * 16);
+  pl.xs8 = reinterpret_cast<int*>(pl.scl + nb * G);
+  pl.G = G;
+  return pl;
+}
+
+// Convert the 8 values v (elements 8c..8c+7 of group g, c = lane & 3; the 4
+// lanes of a group are consecutive) into their plane words.  Every lane of the
+// warp must call this (shuffles); `active` marks lanes holding real data.
+__device__ __forceinline__ void store_planes(const float (&v)[8], bool active, const Planes& pl,
+                                             int b, int g) {
+  float mx = 0.0f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(v[e]));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  // frexp exponent: mx = f * 2^e, f in [0.5, 1); e = 0 for mx == 0
+  const int ebits = (__float_as_int(mx) >> 23) & 0xFF;
+  const int e = (mx > 0.0f) ? ebits - 126 : 0;
+  const float q = __int_as_float((127 + 15 - e) << 23);   // 2^(15-e)
+  int X[8], sx = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    int xi = __float2int_rn(v[i] * q);
+    xi = max(-32768, min(32767, xi));
+    X[i] = xi;
+    sx += xi;
+  }
+  sx += __shfl_xor_sync(0xffffffffu, sx, 1);
+  sx += __shfl_xor_sync(0xffffffffu, sx, 2);
+  if (active) {
+    uint32_t he = 0, ho = 0, le = 0, lo = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      he |= (static_cast<uint32_t>(X[2 * k] >> 8) & 0xFFu) << (8 * k);
+      ho |= (static_cast<uint32_t>(X[2 * k + 1] >> 8) & 0xFFu) << (8 * k);
+      le |= (static_cast<uint32_t>(X[2 * k]) & 0xFFu) << (8 * k);
+      lo |= (static_cast<uint32_t>(X[2 * k + 1]) & 0xFFu) << (8 * k);
+    }
+    const int c = threadIdx.x & 3;
+    const int sw = (g >> 1) & 3;  // quad swizzle, see load_xgroup
+    uint32_t* gw = pl.w + (static_cast<size_t>(b) * pl.G + g) * 16;
+    gw[4 * (0 ^ sw) + c] = he;
+    gw[4 * (1 ^ sw) + c] = ho;
+    gw[4 * (2 ^ sw) + c] = le;
+    gw[4 * (3 ^ sw) + c] = lo;
+    if (c == 0) {
+      pl.scl[b * pl.G + g] = __int_as_float((127 + e - 15) << 23);  // 2^(e-15)
+      pl.xs8[b * pl.G + g] = 8 * sx;
+    }
+  }
+}
+
+// Planes of fp16(fp16(x*scale) * gamma), x = rows[b] -- rms_norm.metal:20-39
+// over the full vector (k <= 4096).
 template <int NB>
 __device__ void stage_norm(const Params& P, Smem& S, const __half* const* rows, bool rows_nc,
                            const __half* gamma, int k) {
-  const int vpr = k / 8;  // 16-byte chunks per row (multiple of 8)
-  uint4* act = reinterpret_cast<uint4*>(S.act);
-  constexpr int kMaxV = 2;  // k <= 2 * 8 * 256 = 4096
+  const int vpr = k / 8;
+  const Planes pl = planes_view(S, k / 32, NB);
+  constexpr int kMaxV = 1;  // vpr <= 512 chunks
   for (int b = 0; b < NB; ++b) {
     if (b >= P.s.batch) break;
     uint4 v[kMaxV];
@@ -387,69 +444,152 @@ __device__ void stage_norm(const Params& P, Smem& S, const __half* const* rows, 
 #pragma unroll
     for (int i = 0; i < kMaxV; ++i) {
       const int c = threadIdx.x + i * kConsumers;
-      if (c < vpr) {
-        const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gamma) + c);
-        const __half* xh = reinterpret_cast<const __half*>(&v[i]);
-        const __half* gh = reinterpret_cast<const __half*>(&gv);
-        uint4 o;
-        __half* oh = reinterpret_cast<__half*>(&o);
+      const bool active = c < vpr;
+      float nv[8];
+      uint4 gv = make_uint4(0u, 0u, 0u, 0u);
+      if (active) gv = __ldg(reinterpret_cast<const uint4*>(gamma) + c);
+      const __half* xh = reinterpret_cast<const __half*>(&v[i]);
+      const __half* gh = reinterpret_cast<const __half*>(&gv);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const __half nrm = __float2half_rn(__half2float(xh[e]) * scale);
-          oh[e] = __float2half_rn(__half2float(nrm) * __half2float(gh[e]));
-        }
-        act[b * vpr + xswz(c)] = o;
+      for (int e = 0; e < 8; ++e) {
+        const __half nrm = __float2half_rn(__half2float(xh[e]) * scale);
+        nv[e] = __half2float(__float2half_rn(__half2float(nrm) * __half2float(gh[e])));
+      }
+      store_planes(nv, active, pl, b, c >> 2);
+    }
+  }
+  consumer_sync();
+}
+
+// Planes of src[b] (k fp16 elements, row stride ld) for every sequence.
+template <int NB>
+__device__ void stage_copy(const Params& P, Smem& S, const __half* src, int ld, int k) {
+  const int vpr = k / 8;
+  const Planes pl = planes_view(S, k / 32, NB);
+  const int total = NB * vpr;
+  const int rounds = (total + kConsumers - 1) / kConsumers;
+  constexpr int kBatch = 4;  // loads in flight per thread
+  for (int r0 = 0; r0 < rounds; r0 += kBatch) {
+    uint4 v[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int i = threadIdx.x + (r0 + k) * kConsumers;
+      const int b = i / vpr, c = i - b * vpr;
+      v[k] = make_uint4(0u, 0u, 0u, 0u);
+      if (r0 + k < rounds && i < total && b < P.s.batch)
+        v[k] = __ldcg(reinterpret_cast<const uint4*>(src + static_cast<size_t>(b) * ld) + c);
+    }
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      if (r0 + k < rounds) {  // uniform across the CTA
+        const int i = threadIdx.x + (r0 + k) * kConsumers;
+        const int b = i / vpr, c = i - b * vpr;
+        const bool active = i < total && b < P.s.batch;
+        const __half* h = reinterpret_cast<const __half*>(&v[k]);
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = __half2float(h[e]);
+        store_planes(f, active, pl, active ? b : 0, c >> 2);
       }
     }
   }
   consumer_sync();
 }
 
-// act[b] <- src[b] (k elements) for every sequence.
-template <int NB>
-__device__ void stage_copy(const Params& P, Smem& S, const __half* src, int ld, int k) {
-  const int vpr = k / 8;
-  uint4* act = reinterpret_cast<uint4*>(S.act);
-  for (int i = threadIdx.x; i < NB * vpr; i += kConsumers) {
-    const int b = i / vpr, c = i - b * vpr;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (b < P.s.batch) v = __ldcg(reinterpret_cast<const uint4*>(src + static_cast<size_t>(b) * ld) + c);
-    act[b * vpr + xswz(c)] = v;
-  }
-  consumer_sync();
+__device__ __forceinline__ void dp4a_us(int& acc, uint32_t a, uint32_t b) {
+  asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(a), "r"(b));
 }
+__device__ __forceinline__ void dp4a_uu(uint32_t& acc, uint32_t a, uint32_t b) {
+  asm("dp4a.u32.u32 %0, %1, %2, %0;" : "+r"(acc) : "r"(a), "r"(b));
+}
+
+// Exact sum_k (n_k - 8) X_k of one group: wv = 16 packed bytes, x = plane words.
+__device__ __forceinline__ int group_idot(const uint4& wv, const uint32_t (&x)[16], int xs8) {
+  int sh = 0;
+  uint32_t sl = 0u;
+  const uint32_t ws[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint32_t ne = ws[c] & 0x0F0F0F0Fu, no = (ws[c] >> 4) & 0x0F0F0F0Fu;
+    dp4a_us(sh, ne, x[c]);
+    dp4a_us(sh, no, x[4 + c]);
+    dp4a_uu(sl, ne, x[8 + c]);
+    dp4a_uu(sl, no, x[12 + c]);
+  }
+  return sh * 256 + static_cast<int>(sl) - xs8;
+}
+
+struct XGroup {
+  uint32_t w[16];
+  float scl;
+  int xs8;
+};
+
+// A group's four 16-byte quads (He, Ho, Le, Lo) are stored in the order
+// q ^ ((g >> 1) & 3): lanes reading the same quad of 8 consecutive groups then
+// touch 8 different 16-byte bank groups (one wavefront) instead of two.
+__device__ __forceinline__ void load_xgroup(const Planes& pl, int b, int g, XGroup& x) {
+  const uint4* src = reinterpret_cast<const uint4*>(pl.w + (static_cast<size_t>(b) * pl.G + g) * 16);
+  const int sw = (g >> 1) & 3;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 v = src[q ^ sw];
+    x.w[4 * q] = v.x;
+    x.w[4 * q + 1] = v.y;
+    x.w[4 * q + 2] = v.z;
+    x.w[4 * q + 3] = v.w;
+  }
+  x.scl = pl.scl[b * pl.G + g];
+  x.xs8 = pl.xs8[b * pl.G + g];
+}
+
+constexpr int kMaxJ = 4;  // groups per lane: G / 16 <= 3 (hidden <= 1536); down: ceil(G / warps / 8) <= 4
 
 // ---------------------------------------------------------------------------
 // GEMV stages over ring chunks
 // ---------------------------------------------------------------------------
-// k = hidden stages (QKV, O, HEAD): chunk of <= 16 rows; warp w owns rows
-// 2w (lanes 0-15) and 2w+1 (lanes 16-31); lane sub walks groups sub, sub+16, ...
+// k = hidden stages (QKV, O, HEAD): chunk of <= 2*warps rows; warp w owns
+// rows 2w (lanes 0-15) and 2w+1 (lanes 16-31); lane sub takes groups sub,
+// sub+16, sub+32 of its row (weights and activation planes from shared memory).
 template <int NB, int KIND>
 __device__ void gemv_hidden(const Params& P, Smem& S, CState& cs, const Chunking& c,
                             const __half* bias, const __half* const* res_rows, __half* out, int ldo,
                             unsigned long long* best) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = c.k / 32;
-  const int vpr = c.k / 8;
-  const uint4* act = reinterpret_cast<const uint4*>(S.act);
+  const int G = c.k / 32, JG = G / 16;
+  const int sub = lane & 15;
+  const Planes pl = planes_view(S, G, NB);
   for (int r = c.r0; r < c.r1; r += c.rows_per_chunk) {
     const int n = min(c.rows_per_chunk, c.r1 - r);
     int slot;
     slot_wait(S, P, cs, slot);
     const unsigned char* base = S.ring + static_cast<size_t>(slot) * kSlotBytes;
     const int lrow = 2 * warp + (lane >> 4);
-    const int sub = lane & 15;
     float acc[NB];
 #pragma unroll
     for (int b = 0; b < NB; ++b) acc[b] = 0.0f;
     if (lrow < n) {
       const unsigned char* wrow = base + static_cast<size_t>(lrow) * (c.k / 2);
       const __half* srow = reinterpret_cast<const __half*>(base + static_cast<size_t>(n) * (c.k / 2)) + lrow * G;
-      for (int g = sub; g < G; g += 16) {
-        const uint4 wv = *reinterpret_cast<const uint4*>(wrow + g * 16);
-        const float sc = __half2float(srow[g]);
+      uint4 wv[kMaxJ];
+      float sc[kMaxJ];
 #pragma unroll
-        for (int b = 0; b < NB; ++b) acc[b] = fmaf(sc, group_dot(wv, act + b * vpr, g), acc[b]);
+      for (int j = 0; j < kMaxJ; ++j) {
+        if (j < JG) {
+          wv[j] = *reinterpret_cast<const uint4*>(wrow + (sub + 16 * j) * 16);
+          sc[j] = __half2float(srow[sub + 16 * j]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kMaxJ; ++j) {
+        if (j < JG) {
+#pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            XGroup xg;
+            load_xgroup(pl, b, sub + 16 * j, xg);
+            acc[b] = fmaf(sc[j] * xg.scl, static_cast<float>(group_idot(wv[j], xg.w, xg.xs8)), acc[b]);
+          }
+        }
       }
     }
     slot_release(S, cs, slot);
@@ -476,14 +616,15 @@ __device__ void gemv_hidden(const Params& P, Smem& S, CState& cs, const Chunking
   }
 }
 
-// Gate/up: chunk of <= 8 row pairs; warp w: gate row w on lanes 0-15, up row w
-// on lanes 16-31; lane 0 applies SwiGLU (swiglu.metal:19-22).
+// Gate/up: chunk of <= 16 row pairs; warp w: gate row w on lanes 0-15, up row
+// w on lanes 16-31; lane 0 applies SwiGLU (swiglu.metal:19-22).
 template <int NB>
 __device__ void gemv_gateup(const Params& P, Smem& S, CState& cs, const Chunking& c) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = c.k / 32, vpr = c.k / 8;
-  const uint4* act = reinterpret_cast<const uint4*>(S.act);
+  const int G = c.k / 32, JG = G / 16;
+  const int up = lane >> 4, sub = lane & 15;
   const int inter = P.m.intermediate;
+  const Planes pl = planes_view(S, G, NB);
   for (int r = c.r0; r < c.r1; r += c.rows_per_chunk) {
     const int n = min(c.rows_per_chunk, c.r1 - r);
     int slot;
@@ -491,18 +632,31 @@ __device__ void gemv_gateup(const Params& P, Smem& S, CState& cs, const Chunking
     const unsigned char* base = S.ring + static_cast<size_t>(slot) * kSlotBytes;
     const size_t pbytes = static_cast<size_t>(n) * (c.k / 2);
     const size_t sbytes = static_cast<size_t>(n) * G * 2;
-    const int up = lane >> 4, sub = lane & 15;
     float acc[NB];
 #pragma unroll
     for (int b = 0; b < NB; ++b) acc[b] = 0.0f;
     if (warp < n) {
       const unsigned char* wrow = base + up * pbytes + static_cast<size_t>(warp) * (c.k / 2);
       const __half* srow = reinterpret_cast<const __half*>(base + 2 * pbytes + up * sbytes) + warp * G;
-      for (int g = sub; g < G; g += 16) {
-        const uint4 wv = *reinterpret_cast<const uint4*>(wrow + g * 16);
-        const float sc = __half2float(srow[g]);
+      uint4 wv[kMaxJ];
+      float sc[kMaxJ];
 #pragma unroll
-        for (int b = 0; b < NB; ++b) acc[b] = fmaf(sc, group_dot(wv, act + b * vpr, g), acc[b]);
+      for (int j = 0; j < kMaxJ; ++j) {
+        if (j < JG) {
+          wv[j] = *reinterpret_cast<const uint4*>(wrow + (sub + 16 * j) * 16);
+          sc[j] = __half2float(srow[sub + 16 * j]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kMaxJ; ++j) {
+        if (j < JG) {
+#pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            XGroup xg;
+            load_xgroup(pl, b, sub + 16 * j, xg);
+            acc[b] = fmaf(sc[j] * xg.scl, static_cast<float>(group_idot(wv[j], xg.w, xg.xs8)), acc[b]);
+          }
+        }
       }
     }
     slot_release(S, cs, slot);
@@ -521,33 +675,42 @@ __device__ void gemv_gateup(const Params& P, Smem& S, CState& cs, const Chunking
 }
 
 // Down projection (k = intermediate): chunk of <= 4 rows; warp w sums groups
-// [G*w/8, G*(w+1)/8) of every row (lane = row*8 + sub), partials meet in
-// shared memory and warp 0 finishes: x = x1 + fp16(acc).
+// [G*w/16, G*(w+1)/16) of every row (lane = row*8 + sub, groups g0+sub+8j),
+// partials meet in shared memory and one thread per row finishes:
+// x = x1 + fp16(acc).
 template <int NB>
 __device__ void gemv_down(const Params& P, Smem& S, CState& cs, const Chunking& c) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = c.k / 32, vpr = c.k / 8;
+  const int G = c.k / 32;
   const int g0 = G * warp / kConsumerWarps, g1 = G * (warp + 1) / kConsumerWarps;
-  const uint4* act = reinterpret_cast<const uint4*>(S.act);
+  const int lrow = lane >> 3, sub = lane & 7;
   const int hidden = P.m.hidden;
+  const Planes pl = planes_view(S, G, NB);
   int par = 0;
   for (int r = c.r0; r < c.r1; r += c.rows_per_chunk, par ^= 1) {
     const int n = min(c.rows_per_chunk, c.r1 - r);
     int slot;
     slot_wait(S, P, cs, slot);
     const unsigned char* base = S.ring + static_cast<size_t>(slot) * kSlotBytes;
-    const int lrow = lane >> 3, sub = lane & 7;
     float acc[NB];
 #pragma unroll
     for (int b = 0; b < NB; ++b) acc[b] = 0.0f;
     if (lrow < n) {
       const unsigned char* wrow = base + static_cast<size_t>(lrow) * (c.k / 2);
       const __half* srow = reinterpret_cast<const __half*>(base + static_cast<size_t>(n) * (c.k / 2)) + lrow * G;
-      for (int g = g0 + sub; g < g1; g += 8) {
-        const uint4 wv = *reinterpret_cast<const uint4*>(wrow + g * 16);
-        const float sc = __half2float(srow[g]);
 #pragma unroll
-        for (int b = 0; b < NB; ++b) acc[b] = fmaf(sc, group_dot(wv, act + b * vpr, g), acc[b]);
+      for (int j = 0; j < kMaxJ; ++j) {
+        const int g = g0 + sub + 8 * j;
+        if (g < g1) {
+          const uint4 wv = *reinterpret_cast<const uint4*>(wrow + g * 16);
+          const float sc = __half2float(srow[g]);
+#pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            XGroup xg;
+            load_xgroup(pl, b, g, xg);
+            acc[b] = fmaf(sc * xg.scl, static_cast<float>(group_idot(wv, xg.w, xg.xs8)), acc[b]);
+          }
+        }
       }
     }
     slot_release(S, cs, slot);
@@ -573,19 +736,61 @@ __device__ void gemv_down(const Params& P, Smem& S, CState& cs, const Chunking& 
   }
 }
 
+// Attention sub-phase stamps of CTA 0 (timeline row 3*grid, when allocated).
+__device__ __forceinline__ void attn_stamp(const Params& P, int& aev) {
+  if (P.s.trace && P.s.trace_rows > 3 * static_cast<int>(gridDim.x) && blockIdx.x == 0 && threadIdx.x == 0) {
+    if (aev < P.s.trace_events)
+      P.s.trace[static_cast<size_t>(3 * gridDim.x) * P.s.trace_events + aev] = globaltimer();
+    ++aev;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Attention stage: one work item = (sequence b, kv head, split of positions)
 // ---------------------------------------------------------------------------
+// Decode-attention tiles go through the tensor cores with mma.sync m16n8k16
+// (fp16 in, fp32 accumulate): the G query heads of a KV head are the M rows
+// (padded to 16), positions are N for the scores and K for P.V.  At decode
+// these tiles are tiny and latency-bound; the MMAs replace 128-long dependent
+// FMA chains per (position, head).
 struct AttnSmemP {
-  float q[kMaxG][kHD];
+  __half qh[16][kKStride];            // rotated q (fp16); rows >= G are zero
+  __half knew[kHD];                   // this step's rotated k / raw v (position pos)
+  __half vnew[kHD];
   __half k[kAttnTile][kKStride];
-  __half v[kAttnTile][kHD];
-  float p[kMaxG][kAttnTile];
+  __half v[kAttnTile][kKStride];
+  float p[kMaxG][kAttnTile];          // scores
+  __half ph[16][kAttnTile + 8];       // exp(scores - max) in fp16; rows >= G are zero
   float m[kMaxG];
   float l[kMaxG];
   float alpha[kMaxG];
   int is_last;
 };
+
+__device__ __forceinline__ void ldsm_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x2(const void* p, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r0), "=r"(r1)
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x2_trans(const void* p, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r0), "=r"(r1)
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 
 __device__ __forceinline__ void rope_pair(int j, int style, int& i1, int& i2) {
   if (style == LMPS_ROPE_INTERLEAVED) {
@@ -598,7 +803,7 @@ __device__ __forceinline__ void rope_pair(int j, int style, int& i1, int& i2) {
 }
 
 __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, int b, int kvh,
-                          int split, int n_splits, int chunk, int pos) {
+                          int split, int n_splits, int chunk, int pos, int& aev) {
   AttnSmemP& A = *reinterpret_cast<AttnSmemP*>(S.act);
   const lmps_model_desc& m = P.m;
   const int tid = threadIdx.x;
@@ -613,91 +818,155 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
   __half* kpool = reinterpret_cast<__half*>(L.k_pool);
   __half* vpool = reinterpret_cast<__half*>(L.v_pool);
 
+  // K/V rows of one 64-position tile, loaded straight into registers so the
+  // loads of the first tile overlap the q/k/v loads and RoPE below.  The new
+  // position `pos` is not read from the cache: it comes from A.knew/A.vnew.
+  constexpr int kTileVec = kAttnTile * (kHD / 8);                       // 16-byte chunks per tile
+  constexpr int kLd = (kTileVec + kConsumers - 1) / kConsumers;
+  uint4 kreg[kLd], vreg[kLd];
+  auto load_tile = [&](int t0) {
+    const int n = min(kAttnTile, end - t0);
+#pragma unroll
+    for (int it = 0; it < kLd; ++it) {
+      const int i = tid + it * kConsumers;
+      const int r = i / (kHD / 8), c = i - r * (kHD / 8);
+      kreg[it] = make_uint4(0u, 0u, 0u, 0u);
+      vreg[it] = make_uint4(0u, 0u, 0u, 0u);
+      const int p = t0 + r;
+      if (i < kTileVec && r < n && p != pos) {
+        const size_t off = ((static_cast<size_t>(bt[p / ps]) * Hkv + kvh) * ps + p % ps) * kHD + c * 8;
+        kreg[it] = __ldcg(reinterpret_cast<const uint4*>(kpool + off));
+        vreg[it] = __ldcg(reinterpret_cast<const uint4*>(vpool + off));
+      }
+    }
+  };
+  auto store_tile = [&](int t0) {
+#pragma unroll
+    for (int it = 0; it < kLd; ++it) {
+      const int i = tid + it * kConsumers;
+      if (i < kTileVec) {
+        const int r = i / (kHD / 8), c = i - r * (kHD / 8);
+        uint4 kv = kreg[it], vv = vreg[it];
+        if (t0 + r == pos) {
+          kv = *reinterpret_cast<const uint4*>(&A.knew[c * 8]);
+          vv = *reinterpret_cast<const uint4*>(&A.vnew[c * 8]);
+        }
+        *reinterpret_cast<uint4*>(&A.k[r][c * 8]) = kv;
+        *reinterpret_cast<uint4*>(&A.v[r][c * 8]) = vv;
+      }
+    }
+  };
+  attn_stamp(P, aev);
+  // Every global load of the prologue is issued before any of them is used:
+  // the first K/V tile, this group's q pairs, the new k pair and v element.
+  if (start < end) load_tile(start);
+  constexpr int kQ = (kMaxG * (kHD / 2) + kConsumers - 1) / kConsumers;
+  float qa[kQ], qb[kQ];
+#pragma unroll
+  for (int it = 0; it < kQ; ++it) {
+    const int i = tid + it * kConsumers;
+    qa[it] = qb[it] = 0.0f;
+    if (i < G * (kHD / 2)) {
+      const int h = i / (kHD / 2), j = i - h * (kHD / 2);
+      int i1, i2;
+      rope_pair(j, m.rope_style, i1, i2);
+      const __half* qh = row + (kvh * G + h) * kHD;
+      qa[it] = __half2float(__ldcg(qh + i1));
+      qb[it] = __half2float(__ldcg(qh + i2));
+    }
+  }
+  const bool has_pos = pos >= start && pos < end;
+  const __half* kh = row + (Hq + kvh) * kHD;
+  const __half* vh = row + (Hq + Hkv + kvh) * kHD;
+  float ka = 0.0f, kb = 0.0f;
+  __half vnew = __float2half_rn(0.0f);
+  int ki1 = 0, ki2 = 0;
+  if (has_pos) {
+    if (tid < kHD / 2) {
+      rope_pair(tid, m.rope_style, ki1, ki2);
+      ka = __half2float(__ldcg(kh + ki1));
+      kb = __half2float(__ldcg(kh + ki2));
+    } else if (tid < kHD / 2 + kHD) {
+      vnew = __ldcg(vh + (tid - kHD / 2));
+    }
+  }
   // RoPE'd q of the G heads sharing this KV head (rope.metal:19-40), fp16-rounded.
-  for (int i = tid; i < G * (kHD / 2); i += kConsumers) {
-    const int h = i / (kHD / 2), j = i - h * (kHD / 2);
-    int i1, i2;
-    rope_pair(j, m.rope_style, i1, i2);
-    const __half* qh = row + (kvh * G + h) * kHD;
-    const float x1 = __half2float(__ldcg(qh + i1)), x2 = __half2float(__ldcg(qh + i2));
-    float sn, cs;
-    sincosf(fpos * __ldg(m.inv_freq + j), &sn, &cs);
-    A.q[h][i1] = __half2float(__float2half_rn(x1 * cs - x2 * sn));
-    A.q[h][i2] = __half2float(__float2half_rn(x1 * sn + x2 * cs));
+#pragma unroll
+  for (int it = 0; it < kQ; ++it) {
+    const int i = tid + it * kConsumers;
+    if (i < G * (kHD / 2)) {
+      const int h = i / (kHD / 2), j = i - h * (kHD / 2);
+      int i1, i2;
+      rope_pair(j, m.rope_style, i1, i2);
+      float sn, cs;
+      sincosf(fpos * S.inv_freq[j], &sn, &cs);
+      A.qh[h][i1] = __float2half_rn(qa[it] * cs - qb[it] * sn);
+      A.qh[h][i2] = __float2half_rn(qa[it] * sn + qb[it] * cs);
+    }
   }
   // The split holding the new position appends its rotated k and raw v.
-  if (pos >= start && pos < end) {
+  if (has_pos) {
     const int page = bt[pos / ps], off = pos % ps;
     const size_t base = ((static_cast<size_t>(page) * Hkv + kvh) * ps + off) * kHD;
-    const __half* kh = row + (Hq + kvh) * kHD;
-    const __half* vh = row + (Hq + Hkv + kvh) * kHD;
     if (tid < kHD / 2) {
-      int i1, i2;
-      rope_pair(tid, m.rope_style, i1, i2);
-      const float x1 = __half2float(__ldcg(kh + i1)), x2 = __half2float(__ldcg(kh + i2));
       float sn, cs;
-      sincosf(fpos * __ldg(m.inv_freq + tid), &sn, &cs);
-      kpool[base + i1] = __float2half_rn(x1 * cs - x2 * sn);
-      kpool[base + i2] = __float2half_rn(x1 * sn + x2 * cs);
+      sincosf(fpos * S.inv_freq[tid], &sn, &cs);
+      const __half k1 = __float2half_rn(ka * cs - kb * sn), k2 = __float2half_rn(ka * sn + kb * cs);
+      kpool[base + ki1] = k1;
+      kpool[base + ki2] = k2;
+      A.knew[ki1] = k1;
+      A.knew[ki2] = k2;
     } else if (tid < kHD / 2 + kHD) {
       const int d = tid - kHD / 2;
-      vpool[base + d] = __ldcg(vh + d);
+      vpool[base + d] = vnew;
+      A.vnew[d] = vnew;
     }
   }
   if (tid < kMaxG) {
     A.m[tid] = -INFINITY;
     A.l[tid] = 0.0f;
   }
-  float acc[kMaxG / 2];
+  for (int i = tid; i < (16 - G) * kKStride; i += kConsumers)
+    A.qh[G + i / kKStride][i % kKStride] = __float2half_rn(0.0f);
+  for (int i = tid; i < (16 - G) * (kAttnTile + 8); i += kConsumers)
+    A.ph[G + i / (kAttnTile + 8)][i % (kAttnTile + 8)] = __float2half_rn(0.0f);
+  constexpr int kHPT = (kMaxG + kConsumers / kHD - 1) / (kConsumers / kHD);   // heads per combine thread
+  const int warp = tid >> 5, lane = tid & 31;
+  const int g8 = lane >> 2, t4 = lane & 3;           // mma fragment row / column pair
+  const int mi = lane >> 3, r8 = lane & 7;           // ldmatrix lane -> matrix, row
+  constexpr int kNT = kHD / 8;                       // P.V output n-tiles (8 dims each)
+  constexpr int kNTW = (kNT + kConsumerWarps - 1) / kConsumerWarps;
+  float o[kNTW][4];
 #pragma unroll
-  for (int j = 0; j < kMaxG / 2; ++j) acc[j] = 0.0f;
+  for (int j = 0; j < kNTW; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
   consumer_sync();
+  attn_stamp(P, aev);
 
   for (int t0 = start; t0 < end; t0 += kAttnTile) {
     const int n = min(kAttnTile, end - t0);
-    for (int i = tid; i < kAttnTile * (kHD / 8); i += kConsumers) {
-      const int r = i / (kHD / 8), c = i - r * (kHD / 8);
-      uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = make_uint4(0u, 0u, 0u, 0u);
-      if (r < n) {
-        const int p = t0 + r;
-        const size_t off = ((static_cast<size_t>(bt[p / ps]) * Hkv + kvh) * ps + p % ps) * kHD + c * 8;
-        kv = __ldcg(reinterpret_cast<const uint4*>(kpool + off));
-        vv = __ldcg(reinterpret_cast<const uint4*>(vpool + off));
-      }
-      *reinterpret_cast<uint4*>(&A.k[r][c * 8]) = kv;
-      *reinterpret_cast<uint4*>(&A.v[r][c * 8]) = vv;
-    }
+    if (t0 != start) load_tile(t0);
+    store_tile(t0);
     consumer_sync();
-    {  // scores: thread -> (position r, heads hq, hq+4)
-      const int r = tid & (kAttnTile - 1), hq = tid >> 6;
-      float dots[2] = {0.0f, 0.0f};
-#pragma unroll 4
-      for (int c = 0; c < kHD / 8; ++c) {
-        const uint4 kk = *reinterpret_cast<const uint4*>(&A.k[r][c * 8]);
-        const __half2* k2 = reinterpret_cast<const __half2*>(&kk);
-        float kf[8];
+    attn_stamp(P, aev);
+    // scores S = Q K^T * 0.088388 (attention.metal:32-40): warp w < 8 owns
+    // positions 8w..8w+7, eight k-steps over the 128 dims.
+    if (warp < kAttnTile / 8) {
+      float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __half22float2(k2[e]);
-          kf[2 * e] = f.x;
-          kf[2 * e + 1] = f.y;
-        }
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int h = hq + 4 * j;
-          if (h < G) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) dots[j] = fmaf(A.q[h][c * 8 + e], kf[e], dots[j]);
-          }
-        }
+      for (int ks = 0; ks < kHD / 16; ++ks) {
+        uint32_t a0, a1, a2, a3, b0, b1;
+        ldsm_x4(&A.qh[(mi & 1) * 8 + r8][16 * ks + (mi >> 1) * 8], a0, a1, a2, a3);
+        ldsm_x2(&A.k[8 * warp + r8][16 * ks + (mi & 1) * 8], b0, b1);
+        mma_16816(d, a0, a1, a2, a3, b0, b1);
       }
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int h = hq + 4 * j;
-        if (h < G) A.p[h][r] = (r < n) ? dots[j] * kAttnScale : -INFINITY;
+      if (g8 < G) {
+        const int p0 = 8 * warp + 2 * t4;
+        A.p[g8][p0] = (p0 < n) ? d[0] * kAttnScale : -INFINITY;
+        A.p[g8][p0 + 1] = (p0 + 1 < n) ? d[1] * kAttnScale : -INFINITY;
       }
     }
     consumer_sync();
+    attn_stamp(P, aev);
     {  // online softmax, one warp per head (softmax.metal:23-36)
       const int warp = tid >> 5, lane = tid & 31;
       if (warp < G) {
@@ -712,8 +981,8 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
           alpha = expf(m_old - m_new);
         }
         const float sum = warp_sum(e0 + e1);
-        A.p[h][lane] = e0;
-        A.p[h][lane + 32] = e1;
+        A.ph[h][lane] = __float2half_rn(e0);
+        A.ph[h][lane + 32] = __float2half_rn(e1);
         __syncwarp();
         if (lane == 0) {
           A.alpha[h] = alpha;
@@ -723,49 +992,69 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
       }
     }
     consumer_sync();
-    {  // P.V (attn_sum.metal:26-32): thread -> (dim d, heads hh, hh+2, ...)
-      const int d = tid & (kHD - 1), hh = tid >> 7;
+    attn_stamp(P, aev);
+    // O += P V (attn_sum.metal:26-32): warp w owns output dims 8nt..8nt+7 for
+    // nt = w, w + warps; the running sums are rescaled by this tile's alpha.
+    {
+      const float al0 = (g8 < G) ? A.alpha[g8] : 1.0f;
 #pragma unroll
-      for (int j = 0; j < kMaxG / 2; ++j) {
-        const int h = hh + 2 * j;
-        if (h < G) acc[j] *= A.alpha[h];
+      for (int j = 0; j < kNTW; ++j) {
+        o[j][0] *= al0;
+        o[j][1] *= al0;
       }
-      for (int r = 0; r < n; ++r) {
-        const float v = __half2float(A.v[r][d]);
 #pragma unroll
-        for (int j = 0; j < kMaxG / 2; ++j) {
-          const int h = hh + 2 * j;
-          if (h < G) acc[j] = fmaf(A.p[h][r], v, acc[j]);
+      for (int ks = 0; ks < kAttnTile / 16; ++ks) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(&A.ph[(mi & 1) * 8 + r8][16 * ks + (mi >> 1) * 8], a0, a1, a2, a3);
+#pragma unroll
+        for (int j = 0; j < kNTW; ++j) {
+          const int nt = warp + kConsumerWarps * j;
+          if (nt < kNT) {
+            uint32_t b0, b1;
+            ldsm_x2_trans(&A.v[16 * ks + (mi & 1) * 8 + r8][8 * nt], b0, b1);
+            mma_16816(o[j], a0, a1, a2, a3, b0, b1);
+          }
         }
       }
     }
     consumer_sync();
+    attn_stamp(P, aev);
   }
 
-  const int d = tid & (kHD - 1), hh = tid >> 7;
   if (n_splits == 1) {
+    if (g8 < G) {
+      const float l = A.l[g8];
+      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
 #pragma unroll
-    for (int j = 0; j < kMaxG / 2; ++j) {
-      const int h = hh + 2 * j;
-      if (h < G) {
-        const float l = A.l[h];
-        P.attn[static_cast<size_t>(b) * Hq * kHD + (kvh * G + h) * kHD + d] =
-            __float2half_rn(l > 0.0f ? acc[j] / l : 0.0f);
+      for (int j = 0; j < kNTW; ++j) {
+        const int nt = warp + kConsumerWarps * j;
+        if (nt < kNT) {
+          __half* dst = P.attn + static_cast<size_t>(b) * Hq * kHD + (kvh * G + g8) * kHD + 8 * nt + 2 * t4;
+          dst[0] = __float2half_rn(o[j][0] * inv);
+          dst[1] = __float2half_rn(o[j][1] * inv);
+        }
       }
     }
     consumer_sync();
     return;
   }
   const size_t ms = P.max_splits;
+  if (g8 < G) {
+    const size_t prow = (static_cast<size_t>(b) * Hq + kvh * G + g8) * ms + split;
 #pragma unroll
-  for (int j = 0; j < kMaxG / 2; ++j) {
-    const int h = hh + 2 * j;
-    if (h < G) {
-      const size_t prow = (static_cast<size_t>(b) * Hq + kvh * G + h) * ms + split;
-      P.part_o[prow * kHD + d] = acc[j];
-      if (d == 0) P.part_ml[prow] = make_float2(A.m[h], A.l[h]);
+    for (int j = 0; j < kNTW; ++j) {
+      const int nt = warp + kConsumerWarps * j;
+      if (nt < kNT) {
+        P.part_o[prow * kHD + 8 * nt + 2 * t4] = o[j][0];
+        P.part_o[prow * kHD + 8 * nt + 2 * t4 + 1] = o[j][1];
+      }
     }
   }
+  if (tid < G) {
+    const size_t prow = (static_cast<size_t>(b) * Hq + kvh * G + tid) * ms + split;
+    P.part_ml[prow] = make_float2(A.m[tid], A.l[tid]);
+  }
+  const int d = tid & (kHD - 1), hh = (tid < (kConsumers / kHD) * kHD) ? tid / kHD : kMaxG;
   __threadfence();
   consumer_sync();
   if (tid == 0) {
@@ -776,8 +1065,8 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
   if (A.is_last) {  // the last split merges all partials of (b, kvh)
     __threadfence();
 #pragma unroll
-    for (int j = 0; j < kMaxG / 2; ++j) {
-      const int h = hh + 2 * j;
+    for (int j = 0; j < kHPT; ++j) {
+      const int h = hh + (kConsumers / kHD) * j;
       if (h < G) {
         const size_t prow0 = (static_cast<size_t>(b) * Hq + kvh * G + h) * ms;
         float M = -INFINITY;
@@ -815,7 +1104,7 @@ __device__ __forceinline__ int attn_chunk_len(const int* pos, int batch, int n_k
 // ---------------------------------------------------------------------------
 template <int NB>
 __device__ void consumer(const Params& P, Smem& S) {
-  CState cs{0u, 0u, true};
+  CState cs{0u, 0u, true, 0ull};
   const lmps_model_desc& m = P.m;
   const int B = P.s.batch;
   const int hidden = m.hidden, Hq = m.n_q_heads, Hkv = m.n_kv_heads;
@@ -828,6 +1117,8 @@ __device__ void consumer(const Params& P, Smem& S) {
   }
   const int hist0 = (P.s.history && P.s.step_counter) ? P.s.step_counter[0] : 0;
   bool first_stage = true;
+  int ev = 0, aev = 0;
+  const bool tr = threadIdx.x == 0;
 
   for (int step = 0; step < P.n_steps; ++step) {
     const int par = step & 1;
@@ -873,15 +1164,18 @@ __device__ void consumer(const Params& P, Smem& S) {
         if (!grid_wait(P, S, cs)) return;
       }
       first_stage = false;
+      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
       stage_norm<NB>(P, S, l == 0 ? xin : xres, l == 0, reinterpret_cast<const __half*>(L.in_norm), hidden);
       {
         const Chunking c = stage_chunks(P, ST_QKV, l);
         gemv_hidden<NB, ST_QKV>(P, S, cs, c, reinterpret_cast<const __half*>(L.qkv_bias), nullptr, P.qkv,
                                 qkv_rows, nullptr);
       }
+      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
       grid_arrive(P, cs);
       // ---- ATT
       if (!grid_wait(P, S, cs)) return;
+      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
       if (l == 0 && step > 0 && blockIdx.x == 0 && threadIdx.x < B)
         P.keys[(par ^ 1) * B + threadIdx.x] = 0ull;  // everyone has read the previous argmax
       {
@@ -907,37 +1201,45 @@ __device__ void consumer(const Params& P, Smem& S) {
 #pragma unroll
           for (int b = 0; b < NB; ++b)
             if (b == bsel) pb = pos[b];
-          attn_item(P, S, L, bsel, kvh, sp, nsp, chunk, pb);
+          attn_item(P, S, L, bsel, kvh, sp, nsp, chunk, pb, aev);
         }
       }
+      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
       grid_arrive(P, cs);
       // ---- O
       if (!grid_wait(P, S, cs)) return;
+      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
       stage_copy<NB>(P, S, P.attn, q_dim, q_dim);
       {
         const Chunking c = stage_chunks(P, ST_O, l);
         gemv_hidden<NB, ST_O>(P, S, cs, c, nullptr, l == 0 ? xin : xres, P.x1, hidden, nullptr);
       }
+      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
       grid_arrive(P, cs);
       // ---- GU
       if (!grid_wait(P, S, cs)) return;
+      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
       stage_norm<NB>(P, S, x1rows, false, reinterpret_cast<const __half*>(L.post_norm), hidden);
       {
         const Chunking c = stage_chunks(P, ST_GU, l);
         gemv_gateup<NB>(P, S, cs, c);
       }
+      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
       grid_arrive(P, cs);
       // ---- DN
       if (!grid_wait(P, S, cs)) return;
+      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
       stage_copy<NB>(P, S, P.a, m.intermediate, m.intermediate);
       {
         const Chunking c = stage_chunks(P, ST_DN, l);
         gemv_down<NB>(P, S, cs, c);
       }
+      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
       grid_arrive(P, cs);
     }
     // ---- HEAD
     if (!grid_wait(P, S, cs)) return;
+    if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
     stage_norm<NB>(P, S, xres, false, reinterpret_cast<const __half*>(m.final_norm), hidden);
     {
       unsigned long long best[NB];
@@ -959,6 +1261,7 @@ __device__ void consumer(const Params& P, Smem& S) {
         if (v) atomicMax(P.keys + par * B + threadIdx.x, v);
       }
     }
+    if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
     grid_arrive(P, cs);
   }
   // ---- final tokens, state write-back, exit barrier
@@ -1002,6 +1305,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
   S.red8 = S.red + 2 * kConsumerWarps * kRowsDown * kMaxB;
   S.best = reinterpret_cast<unsigned long long*>(S.red8 + 8 * kMaxB);
   S.misc = reinterpret_cast<int*>(S.best + kConsumerWarps * kMaxB);
+  S.inv_freq = reinterpret_cast<float*>(S.misc + 16);
+  for (int i = threadIdx.x; i < kHD / 2; i += blockDim.x) S.inv_freq[i] = P.m.inv_freq[i];
   // Every position this launch touches must be inside the cache and every fed
   // token inside the vocabulary; all CTAs read the same values, so all leave
   // together (nothing has been issued yet).
@@ -1068,8 +1373,9 @@ static WsLayout ws_layout(const lmps_model_desc& m, int B, int max_seq_len) {
 
 static int act_bytes_for(const lmps_model_desc& m, int nb) {
   size_t a = sizeof(AttnSmemP);
-  const size_t stage = static_cast<size_t>(nb) * (m.intermediate > m.hidden ? m.intermediate : m.hidden) * 2;
-  if (stage > a) a = stage;
+  const int kmax = m.intermediate > m.hidden ? m.intermediate : m.hidden;
+  const size_t planes = static_cast<size_t>(nb) * (kmax / 32) * (16 * 4 + 4 + 4);  // words + scl + xs8
+  if (planes > a) a = planes;
   return static_cast<int>((a + 127) & ~static_cast<size_t>(127));
 }
 
@@ -1081,18 +1387,25 @@ static int launch(const Params& P0, const lmps_model_desc& m, cudaStream_t st) {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   P.act_bytes = act_bytes_for(m, NB);
+  auto kern = decode_persistent_kernel<NB>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                       cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  // As many ring slots as fit next to one resident CTA per SM.
   int slots = (max_smem - P.act_bytes - kTailBytes) / kSlotBytes;
   if (slots > 16) slots = 16;
+  size_t smem = 0;
+  for (; slots >= 3; --slots) {
+    smem = static_cast<size_t>(slots) * kSlotBytes + P.act_bytes + kTailBytes;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return static_cast<int>(e);
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    if (per_sm >= 1) break;
+  }
   if (slots < 3) return LMPS_ERR_UNSUPPORTED;
   P.slots = slots;
-  const size_t smem = static_cast<size_t>(slots) * kSlotBytes + P.act_bytes + kTailBytes;
-  auto kern = decode_persistent_kernel<NB>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (e != cudaSuccess) return static_cast<int>(e);
-  int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
-  if (e != cudaSuccess) return static_cast<int>(e);
-  if (per_sm < 1) return LMPS_ERR_UNSUPPORTED;
   void* args[] = {&P};
   e = cudaLaunchCooperativeKernel(reinterpret_cast<void*>(kern), dim3(sms), dim3(kThreads), args, smem, st);
   return e == cudaSuccess ? LMPS_OK : static_cast<int>(e);
@@ -1117,11 +1430,15 @@ extern "C" int lmps_decode_persistent(const lmps_model_desc* model, const lmps_d
   LMPS_CHECK_ARG(m.layers && m.final_norm && m.lm_packed && m.lm_scales && m.embed && m.inv_freq);
   LMPS_CHECK_ARG(m.n_layers >= 1 && m.n_kv_heads >= 1 && m.n_q_heads % m.n_kv_heads == 0);
   if (m.head_dim != pk::kHD || m.n_q_heads / m.n_kv_heads > pk::kMaxG) return LMPS_ERR_UNSUPPORTED;
-  if (m.hidden % 512 != 0 || m.hidden > 2048 || m.intermediate % 256 != 0 ||
+  // lanes own hidden/512 groups of a row (<= 3) and G_down/16/8 groups of the
+  // down projection (<= 3); see gemv_hidden / gemv_down
+  if (m.hidden % 512 != 0 || m.hidden > 1536 || m.intermediate % 32 != 0 ||
+      (m.intermediate / 32 + pk::kConsumerWarps - 1) / pk::kConsumerWarps > 8 * pk::kMaxJ ||
       m.n_q_heads * m.head_dim != m.hidden)
     return LMPS_ERR_UNSUPPORTED;
   // ring chunks must fit a slot
   if (static_cast<size_t>(pk::kRows1536) * (m.hidden / 2 + m.hidden / 16) > pk::kSlotBytes ||
+      static_cast<size_t>(2 * pk::kPairsGU) * (m.hidden / 2 + m.hidden / 16) > pk::kSlotBytes ||
       static_cast<size_t>(pk::kRowsDown) * (m.intermediate / 2 + m.intermediate / 16) > pk::kSlotBytes)
     return LMPS_ERR_UNSUPPORTED;
   LMPS_CHECK_ARG(s.batch >= 1 && s.batch <= pk::kMaxB);

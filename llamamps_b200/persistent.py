@@ -36,7 +36,8 @@ class DecodeState(ctypes.Structure):
                 ("block_table", c_vp), ("tokens", c_vp), ("pos", c_vp), ("forced", c_vp),
                 ("forced_stride", c_int), ("n_forced", c_int), ("x_in", c_vp), ("logits", c_vp),
                 ("history", c_vp), ("step_counter", c_vp), ("history_rows", c_int),
-                ("workspace", c_vp), ("workspace_bytes", c_size), ("error", c_vp)]
+                ("workspace", c_vp), ("workspace_bytes", c_size), ("error", c_vp),
+                ("trace", c_vp), ("trace_events", c_int), ("trace_rows", c_int)]
 
 
 _SIGS = {
@@ -104,7 +105,8 @@ class PersistentDecoder:
     def run(self, batch: int, tokens: torch.Tensor, pos: torch.Tensor, n_steps: int, *,
             forced: Optional[torch.Tensor] = None, x_in: Optional[torch.Tensor] = None,
             logits: Optional[torch.Tensor] = None, history: Optional[torch.Tensor] = None,
-            step_counter: Optional[torch.Tensor] = None) -> None:
+            step_counter: Optional[torch.Tensor] = None,
+            trace: Optional[torch.Tensor] = None) -> None:
         if not 1 <= batch <= self.max_batch:
             raise ValueError(f"batch {batch} outside [1, {self.max_batch}]")
         cache = self.cache
@@ -129,6 +131,13 @@ class PersistentDecoder:
         st.workspace = self.ws_view.data_ptr()
         st.workspace_bytes = self.ws_view.numel()
         st.error = self.error.data_ptr()
+        if trace is not None:
+            sms = torch.cuda.get_device_properties(trace.device).multi_processor_count
+            if trace.dtype != torch.int64 or trace.dim() != 2 or trace.shape[0] < 3 * sms:
+                raise ValueError("trace must be int64 [>= 3 * n_SMs, events]")
+            st.trace = trace.data_ptr()
+            st.trace_events = trace.shape[1]
+            st.trace_rows = trace.shape[0]
         check(self.L.lmps_decode_persistent(ctypes.byref(self.model), ctypes.byref(st), int(n_steps),
                                             torch.cuda.current_stream().cuda_stream),
               "lmps_decode_persistent")
