@@ -1357,6 +1357,11 @@ static WsLayout ws_layout(const lmps_model_desc& m, int B, int max_seq_len) {
   const size_t q_dim = static_cast<size_t>(m.n_q_heads) * m.head_dim;
   w.max_splits = (max_seq_len + kAttnTile - 1) / kAttnTile;
   size_t off = 0;
+  // Counters that persist from one launch to the next come first, at offsets
+  // that do not depend on the batch size of the launch.
+  w.arrive = off; off = align256(off + sizeof(uint32_t));
+  w.keys = off; off = align256(off + sizeof(unsigned long long) * 2 * kMaxB);
+  w.att_cnt = off; off = align256(off + sizeof(uint32_t) * kMaxB * m.n_kv_heads);
   w.x = off; off = align256(off + sizeof(__half) * B * m.hidden);
   w.x1 = off; off = align256(off + sizeof(__half) * B * m.hidden);
   w.qkv = off; off = align256(off + sizeof(__half) * B * qkv_rows);
@@ -1364,9 +1369,6 @@ static WsLayout ws_layout(const lmps_model_desc& m, int B, int max_seq_len) {
   w.a = off; off = align256(off + sizeof(__half) * B * m.intermediate);
   w.part_o = off; off = align256(off + sizeof(float) * B * m.n_q_heads * w.max_splits * m.head_dim);
   w.part_ml = off; off = align256(off + sizeof(float2) * B * m.n_q_heads * w.max_splits);
-  w.att_cnt = off; off = align256(off + sizeof(uint32_t) * B * m.n_kv_heads);
-  w.keys = off; off = align256(off + sizeof(unsigned long long) * 2 * B);
-  w.arrive = off; off = align256(off + sizeof(uint32_t));
   w.total = off;
   return w;
 }

@@ -129,3 +129,34 @@ def test_persistent_rejects_positions_past_the_cache(cuda, two_layer_small_vocab
     torch.cuda.synchronize()
     eng.pdec.check_error()
     assert int(eng.pos[0].item()) == 1
+
+
+@pytest.mark.parametrize("B", [2, 3, 4])
+def test_persistent_batch_logits_match_single_sequence(cuda, two_layer_small_vocab, B):
+    """Each sequence of a batch must produce (within tolerance) the logits it
+    produces alone, and the oracle's, after a short prompt."""
+    cfg, mw, host = two_layer_small_vocab
+    rng = np.random.default_rng(40 + B)
+    prompts = rng.integers(0, cfg.vocab, (B, 5))
+    eng = _engine(mw, max_batch=4, max_seq_len=64, decoder="persistent")
+    logits = torch.zeros(4, cfg.vocab, dtype=torch.float16, device="cuda")
+
+    def run(ps):
+        n = ps.shape[0]
+        eng.reset(n)
+        eng.tokens[:n].copy_(torch.from_numpy(ps[:, 0]).to(torch.int32))
+        forced = torch.from_numpy(ps[:, 1:]).to("cuda", torch.int32).contiguous()
+        eng.pdec.run(n, eng.tokens, eng.pos, ps.shape[1], forced=forced, logits=logits[:n])
+        torch.cuda.synchronize()
+        eng.pdec.check_error()
+        return logits[:n].cpu().numpy().copy()
+
+    batched = run(prompts)
+    for b in range(B):
+        single = run(prompts[b:b + 1])[0]
+        assert_close(batched[b], single, what=f"seq {b} batched vs alone")
+        orc = M.OracleModel(host, M.OracleConfig(n_layers=2, vocab=cfg.vocab))
+        ref = None
+        for t in prompts[b]:
+            ref = orc.step_token(int(t))
+        assert_close(batched[b], ref, what=f"seq {b} vs oracle")
