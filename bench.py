@@ -244,8 +244,11 @@ def run_ours(args):
     from llamamps_b200.weights import synth_model
 
     B = 1
+    if args.layers is not None:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, n_layers=args.layers)
     mw = synth_model(cfg, seed=1, device=dev)
-    max_seq = PROMPT_LEN + args.warmup + 2 * args.steps + 8
+    max_seq = PROMPT_LEN + args.warmup + 2 * args.steps + 16
     eng = QwenEngine(weights=mw, device=dev, max_batch=B, max_seq_len=max_seq, decoder=args.decoder)
     prompt = np.random.default_rng(1 + rank).integers(0, cfg.vocab, (B, PROMPT_LEN))
     eng.reset(B)
@@ -277,6 +280,11 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     t_max = float(t.item())
     value = world * B * args.steps / t_max
+
+    if args.timeline and eng.pdec is not None and rank == 0:
+        from llamamps_b200.timeline import capture
+        with open(args.timeline, "w") as f:
+            json.dump(capture(eng, 4), f, indent=1)
 
     # -- end to end through the reference-facing API ------------------------
     # run_inference(vector) -> fp16 logits on the host -> predict_next_token,
@@ -324,8 +332,10 @@ def run_ours(args):
             "ms_per_step": round(t_max / args.steps * 1e3, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16 act / int4 weights, f32 accumulate",
             "data": "synthetic (random-init Q4 weights, random token ids)",
-            "config": {"workload": "c1: Qwen2.5-1.5B-Q4 (28 layers, vocab 151936) bs1 per GPU, 32-id "
-                                   "prompt then greedy decode; weights 868.6 MB/step > L2, no flush",
+            "config": {"workload": ("c1: Qwen2.5-1.5B-Q4 (28 layers, vocab 151936) bs1 per GPU, 32-id "
+                                    "prompt then greedy decode; weights 868.6 MB/step > L2, no flush")
+                       if args.layers is None else
+                       f"PROFILING ONLY: {cfg.n_layers}-layer reduction of c1 (not a benchmark)",
                        "model": "Qwen2.5-1.5B", "batch_per_gpu": B, "global_batch": B * world,
                        "prompt_len": PROMPT_LEN, "parallelism": f"dp{world} (independent requests)",
                        "l2": "inputs larger than L2"},
@@ -356,6 +366,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--decoder", choices=["persistent", "kernels"], default=None)
+    ap.add_argument("--timeline", default=None,
+                    help="after the timed region, write the persistent kernel's stage timeline "
+                         "(4 traced steps) as JSON to this path")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="profiling only: build a model with fewer decoder layers (the JSON line "
+                         "then names the reduced workload and is not a measurement of it)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
