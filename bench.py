@@ -51,62 +51,74 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled through NVML from a
+    background thread about once a millisecond while the timed region runs
+    (read-only queries).  ``mark(True/False)`` brackets the timed region; only
+    samples taken inside it are summarised."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
-        self.proc = None
-        self.path = os.path.join("/tmp", f"lmps_clocks_{os.getpid()}.csv")
+        self.samples = []
+        self.inside = False
+        self.stop = False
+        self.thread = None
+        self.nvml = None
 
     def __enter__(self):
         try:
-            self.fh = open(self.path, "w")
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-i", str(self.gpu), "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nvml = None
+            return self
+        import threading
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
         return self
 
+    def _run(self):
+        nv = self.nvml
+        while not self.stop:
+            if self.inside:
+                try:
+                    mhz = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                    rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                    self.samples.append((mhz, rs))
+                except Exception:
+                    pass
+            time.sleep(0.001)
+
+    def mark(self, inside: bool):
+        self.inside = inside
+
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
+        self.stop = True
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+        if self.nvml is not None:
             try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            self.fh.close()
+                self.nvml.nvmlShutdown()
+            except Exception:
+                pass
 
     def summary(self):
-        if self.proc is None:
+        if self.nvml is None or not self.samples:
             return None
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        try:
-            with open(self.path) as f:
-                for line in f:
-                    parts = [p.strip() for p in line.split(",")]
-                    if len(parts) < 9:
-                        continue
-                    try:
-                        sm.append(float(parts[1]))
-                        mx.append(float(parts[2]))
-                    except ValueError:
-                        continue
-                    for n, v in zip(names, parts[5:9]):
-                        if v.lower() == "active":
-                            reasons.add(n)
-            os.unlink(self.path)
-        except OSError:
-            return None
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        reasons = set()
+        for _, rs in self.samples:
+            for name, attr in self.REASONS:
+                if rs & getattr(self.nvml, attr, 0):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(self.samples), "source": "nvml"}
 
 
 def cpu_baseline_sample(seconds: float = 15.0):
@@ -267,10 +279,12 @@ def run_ours(args):
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
+        clk.mark(True)
         e0.record(st)
         eng.decode_steps(args.steps, record=False)   # persistent: one launch for all K steps
         e1.record(st)
         torch.cuda.synchronize()
+        clk.mark(False)
     if eng.pdec is not None:
         eng.pdec.check_error()
     barrier()

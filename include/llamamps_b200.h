@@ -244,21 +244,24 @@ typedef struct lmps_decode_state {
   int32_t* error;               /* [1] set to 1 when a bounded device wait gives up */
   unsigned long long* trace;    /* optional stage timeline (or NULL): [3 * grid, trace_events]
                                    %globaltimer stamps; rows 0..grid-1 compute warps (stage
-                                   start after its wait, stage end), rows grid.. the producer
+                                   start after its wait, input staged, stage end; three
+                                   per stage), rows grid.. the producer
                                    (first and last chunk issue of each stage), rows 2*grid..
                                    the compute warps' cumulative ns spent waiting for weights */
   int trace_events;
   int trace_rows;               /* rows allocated in trace (>= 3 * grid) */
 } lmps_decode_state;
 
-/* Bytes of workspace the persistent step needs (activations, split partials,
- * counters).  The workspace must be zero-filled before the first call; each
- * call leaves it ready for the next one. */
+/* Bytes of workspace the persistent step needs (tagged activations, split
+ * partials, counters, the launch sequence number the activation tags are
+ * derived from).  The workspace must be zero-filled before the first call;
+ * each call leaves it ready for the next one. */
 size_t lmps_decode_persistent_workspace_size(const lmps_model_desc* model, int batch,
                                              int max_seq_len);
 
 /* Run n_steps decode steps (1 <= batch <= 4, head_dim 128, hidden a multiple
- * of 512 and <= 1536, intermediate a multiple of 32 and <= 12288).  model/state are HOST
+ * of 512 and <= 1536, intermediate a multiple of 32 and <= 11264, vocab <=
+ * 262144).  model/state are HOST
  * structs (copied into the launch).  Failures found on the device are reported
  * through state->error, which the caller reads after synchronising: 1 = a
  * bounded wait timed out, 2 = a position past max_seq_len or a token id

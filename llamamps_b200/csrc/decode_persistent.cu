@@ -6,22 +6,26 @@
 // latency and a cold start of its memory stream (the fused gate/up GEMV alone
 // reaches ~23% of HBM bandwidth).  Here the weight stream never stops:
 //
-//  * warp 8 of every CTA (the producer) walks the same static schedule as the
+//  * the last warp of every CTA (the producer) walks the same static schedule as the
 //    compute warps and issues TMA bulk copies (cp.async.bulk, L2 evict-first)
 //    of the CTA's row slice of every matrix, layer after layer, into a ring of
 //    shared-memory slots guarded by full/empty mbarriers.  Weights do not
 //    depend on activations, so the producer runs up to a ring (~160 KB, about
 //    one layer per SM) ahead of the compute;
-//  * warps 0-7 (the consumers) wait for a stage's input activation, stage it
-//    in shared memory (RMSNorm'd where the reference normalises), consume
-//    their slots (unpack nibbles -> fp16 codes, sm_100 mixed-precision FMA
-//    into fp32, scale per group, warp-shuffle reduction) and write the stage
-//    output with the fused epilogue;
-//  * stages hand data across CTAs through global memory and one monotonic
-//    arrival counter (fence + atomic add; a CTA waits with ld.acquire.gpu for
-//    all CTAs to have finished the previous stage).  Every wait is bounded
-//    (2 s of %globaltimer): on expiry the CTA raises state.error, stops the
-//    producer, drains its in-flight copies and returns.
+//  * the other warps (the consumers) wait for a stage's input activation, stage it
+//    in shared memory (RMSNorm'd where the reference normalises) as exact
+//    integer activation planes, consume their slots (dp4a group dots of the
+//    weight nibbles against the planes, scaled per group into fp32, warp-
+//    shuffle reduction) and publish the stage output with the fused epilogue;
+//  * stages hand data across CTAs through global memory as tagged words: a
+//    64-bit word holds two fp16 outputs and the 32-bit tag of the stage (and
+//    step and launch) that wrote them, stored with st.relaxed.gpu.  A reader
+//    polls the words it needs until every tag matches -- the data is its own
+//    flag, so there is no grid-wide barrier in a step and a stage starts as
+//    soon as its inputs exist.  The LM head publishes one tagged argmax slot
+//    per CTA.  Every wait is bounded (2 s of %globaltimer): on expiry the CTA
+//    raises state.error, stops the producer, drains its in-flight copies and
+//    returns.
 //
 // Stages per layer (rows split evenly over the CTAs):
 //   QKV  rmsnorm(x, in_norm) -> q|k|v = Wqkv x + b              (engine.py:188-195)
@@ -53,6 +57,11 @@ constexpr int kMaxG = 8;
 constexpr int kKStride = kHD + 8;
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
 constexpr int kMaxB = 4;
+constexpr int kOwnMax = 32;  // hidden / qkv rows one CTA owns
+constexpr int kOutMax = 128; // gate/up output rows one CTA owns
+constexpr int kMaxGrid = 256;
+constexpr int kMaxLayers = 64;
+constexpr int kRedFloats = 2 * kConsumerWarps * kRowsDown * kMaxB;  // down-projection partials, double-buffered
 
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
@@ -71,6 +80,17 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Non-blocking probe of a phase (try_wait may suspend the thread for a while).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
 }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -109,17 +129,19 @@ struct Params {
   int n_steps;
   int slots;       // ring slots
   int act_bytes;   // activation / attention staging bytes
-  // workspace carve-up
-  __half* x;        // [B, hidden] residual after a layer
-  __half* x1;       // [B, hidden] residual after attention
-  __half* qkv;      // [B, qkv_rows]
-  __half* attn;     // [B, q_dim]
-  __half* a;        // [B, intermediate]
+  // workspace carve-up.  Stage outputs are tagged words: two fp16 values (low
+  // 32 bits, element 2i in the low half) and the 32-bit tag of the stage that
+  // wrote them (high 32 bits); readers poll the words themselves.
+  unsigned long long* xt;     // [B, hidden/2] residual after a layer (down stage)
+  unsigned long long* x1t;    // [B, hidden/2] residual after attention (o stage)
+  unsigned long long* qkvt;   // [B, qkv_rows/2]
+  unsigned long long* attnt;  // [B, q_dim/2]
+  unsigned long long* at;     // [B, intermediate/2] SwiGLU output
+  unsigned long long* kslot;  // [grid, kMaxB] per-CTA argmax of the LM head rows, tagged
   float* part_o;    // [B, Hq, max_splits, 128]
   float2* part_ml;  // [B, Hq, max_splits]
-  uint32_t* att_cnt;  // [B, Hkv]
-  unsigned long long* keys;  // [2, B]
-  uint32_t* arrive;          // [1]
+  uint32_t* att_cnt;  // [kMaxB, Hkv] split arrivals (reset by the last split)
+  uint32_t* epoch;    // [1] tag base of the next launch
   int max_splits;
 };
 
@@ -130,16 +152,23 @@ struct Smem {
   unsigned char* act;
   uint64_t* full;
   uint64_t* empty;
-  float* red;        // [2][8 warps][4 rows][kMaxB]
-  float* red8;       // [8 * kMaxB] block-reduction scratch
-  unsigned long long* best;  // [8 warps][kMaxB]
-  int* misc;         // [0] abort, [1] is_last, [2..] tok[kMaxB], pos[kMaxB]
+  float* red;        // [2][warps][4 rows][kMaxB] down-projection partials
+  float* red8;       // [warps * kMaxB] block-reduction scratch
+  unsigned long long* best;  // [warps][kMaxB]
+  int* misc;         // [0] abort
   float* inv_freq;   // [head_dim/2] RoPE frequencies, staged once per launch
+  __half* xown;      // [kMaxB][kOwnMax] residual x of the hidden rows this CTA owns
+  __half* x1own;     // [kMaxB][kOwnMax] residual after attention, same rows
+  __half* outb;      // [kMaxB][kOutMax] stage output rows before they are published
+  __half* bias_own;  // [n_layers][kOwnMax] q|k|v bias of the qkv rows this CTA owns
 };
 
+// Rows [r0, r1) of a stage this CTA computes: row pairs split evenly over the
+// CTAs (stage outputs are published as pairs).  rows * ctas < 2^32.
 __device__ __forceinline__ void row_range(int rows, int cta, int ctas, int& r0, int& r1) {
-  r0 = static_cast<int>((static_cast<long long>(rows) * cta) / ctas);
-  r1 = static_cast<int>((static_cast<long long>(rows) * (cta + 1)) / ctas);
+  const uint32_t pairs = static_cast<uint32_t>(rows) / 2;
+  r0 = 2 * static_cast<int>(pairs * cta / static_cast<uint32_t>(ctas));
+  r1 = 2 * static_cast<int>(pairs * (cta + 1) / static_cast<uint32_t>(ctas));
 }
 
 // Weight chunk geometry of a stage for this CTA.
@@ -197,51 +226,49 @@ __device__ __forceinline__ void trace_event(const Params& P, int row, int& ev,
 // ---------------------------------------------------------------------------
 __device__ void producer(const Params& P, Smem& S) {
   const uint64_t policy = evict_first_policy();
-  uint32_t chunk = 0;
+  uint32_t chunk = 0, pphase = 0;
+  int pslot = 0;
   bool ok = true;
   int pev = 0;
-  const int kinds[4] = {ST_QKV, ST_O, ST_GU, ST_DN};
+  const int n_stages = P.m.n_layers * 4 + 1;  // q|k|v, o, gate/up, down per layer, then the LM head
   for (int step = 0; step < P.n_steps && ok; ++step) {
-    for (int l = 0; l <= P.m.n_layers && ok; ++l) {
-      const int nk = (l < P.m.n_layers) ? 4 : 1;
-      for (int ki = 0; ki < nk && ok; ++ki) {
-        const int kind = (l < P.m.n_layers) ? kinds[ki] : ST_HEAD;
-        const Chunking c = stage_chunks(P, kind, l);
-        const size_t row_bytes = static_cast<size_t>(c.k) / 2;
-        const size_t row_scales = static_cast<size_t>(c.k) / 32;
-        trace_event(P, gridDim.x + blockIdx.x, pev);
-        for (int r = c.r0; r < c.r1 && ok; r += c.rows_per_chunk, ++chunk) {
-          const int n = min(c.rows_per_chunk, c.r1 - r);
-          const int slot = chunk % P.slots;
-          const uint32_t phase = (chunk / P.slots) & 1u;
-          // wait until the consumers released this slot's previous contents
-          if (chunk >= static_cast<uint32_t>(P.slots)) {
-            const uint64_t t0 = globaltimer();
-            while (!mbar_try_wait(&S.empty[slot], phase ^ 1u)) {
-              if (*reinterpret_cast<volatile int*>(&S.misc[0]) || globaltimer() - t0 > kTimeoutNs) {
-                ok = false;
-                break;
-              }
-            }
-            if (!ok) break;
-          }
-          unsigned char* dst = S.ring + static_cast<size_t>(slot) * kSlotBytes;
-          const uint32_t pbytes = static_cast<uint32_t>(n * row_bytes);
-          const uint32_t sbytes = static_cast<uint32_t>(n * row_scales * 2);
-          const uint32_t total = (kind == ST_GU) ? 2 * (pbytes + sbytes) : pbytes + sbytes;
-          mbar_expect_tx(&S.full[slot], total);
-          if (kind == ST_GU) {
-            bulk_g2s(dst, c.w + r * row_bytes, pbytes, &S.full[slot], policy);
-            bulk_g2s(dst + pbytes, c.w2 + r * row_bytes, pbytes, &S.full[slot], policy);
-            bulk_g2s(dst + 2 * pbytes, c.s + r * row_scales, sbytes, &S.full[slot], policy);
-            bulk_g2s(dst + 2 * pbytes + sbytes, c.s2 + r * row_scales, sbytes, &S.full[slot], policy);
-          } else {
-            bulk_g2s(dst, c.w + r * row_bytes, pbytes, &S.full[slot], policy);
-            bulk_g2s(dst + pbytes, c.s + r * row_scales, sbytes, &S.full[slot], policy);
-          }
+    for (int st = 0; st < n_stages && ok; ++st) {
+      const int kind = (st == n_stages - 1) ? ST_HEAD : (st & 3);
+      const Chunking c = stage_chunks(P, kind, st >> 2);
+      const uint32_t row_bytes = c.k / 2, row_sbytes = c.k / 16;
+      const uint32_t ncopy = (kind == ST_GU) ? 2u : 1u;
+      trace_event(P, gridDim.x + blockIdx.x, pev);
+      for (int r = c.r0; r < c.r1 && ok; r += c.rows_per_chunk, ++chunk) {
+        const uint32_t n = min(c.rows_per_chunk, c.r1 - r);
+        const int slot = pslot;
+        const uint32_t phase = pphase;
+        if (++pslot == P.slots) {
+          pslot = 0;
+          pphase ^= 1u;
         }
-        trace_event(P, gridDim.x + blockIdx.x, pev);
+        // wait until the consumers released this slot's previous contents
+        if (chunk >= static_cast<uint32_t>(P.slots)) {
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(&S.empty[slot], phase ^ 1u)) {
+            if (*reinterpret_cast<volatile int*>(&S.misc[0]) || globaltimer() - t0 > kTimeoutNs) {
+              ok = false;
+              break;
+            }
+          }
+          if (!ok) break;
+        }
+        // slot layout: packed rows [, second matrix's packed rows], scales [, second matrix's scales]
+        unsigned char* dst = S.ring + static_cast<size_t>(slot) * kSlotBytes;
+        const uint32_t pb = n * row_bytes, sb = n * row_sbytes;
+        mbar_expect_tx(&S.full[slot], ncopy * (pb + sb));
+        for (uint32_t i = 0; i < ncopy; ++i) {
+          const uint8_t* w = i ? c.w2 : c.w;
+          const unsigned char* s = reinterpret_cast<const unsigned char*>(i ? c.s2 : c.s);
+          bulk_g2s(dst + i * pb, w + static_cast<size_t>(r) * row_bytes, pb, &S.full[slot], policy);
+          bulk_g2s(dst + ncopy * pb + i * sb, s + static_cast<size_t>(r) * row_sbytes, sb, &S.full[slot], policy);
+        }
       }
+      trace_event(P, gridDim.x + blockIdx.x, pev);
     }
   }
   // Drain: every issued copy must land before this CTA may exit.
@@ -261,76 +288,150 @@ __device__ void producer(const Params& P, Smem& S) {
 // Consumer helpers
 // ---------------------------------------------------------------------------
 struct CState {
-  uint32_t chunk;     // ring chunk counter (same sequence as the producer)
-  uint32_t arrivals;  // grid arrivals expected so far
-  bool ok;
+  int slot;           // ring slot of the next chunk (same sequence as the producer)
+  uint32_t phase;     // its full-barrier phase parity
   unsigned long long wait_ns;  // time thread 0 spent waiting for ring chunks (timeline only)
 };
 
-// All CTAs finished the previous stage?  Thread 0 polls, then the consumers sync.
-__device__ bool grid_wait(const Params& P, Smem& S, CState& cs) {
-  if (threadIdx.x == 0 && *reinterpret_cast<volatile int*>(&S.misc[0]) == 0) {
-    const uint32_t target = cs.arrivals;
+__device__ __forceinline__ bool aborting(Smem& S) { return *reinterpret_cast<volatile int*>(&S.misc[0]) != 0; }
+__device__ __forceinline__ void raise_abort(const Params& P, Smem& S, int code) {
+  atomicExch(P.s.error, code);
+  *reinterpret_cast<volatile int*>(&S.misc[0]) = 1;
+}
+
+__device__ __forceinline__ void ld_tagged2(const unsigned long long* p, unsigned long long& a,
+                                           unsigned long long& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0,%1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_tagged_acquire(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_tagged(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long tagged(uint32_t tag, uint32_t payload) {
+  return (static_cast<unsigned long long>(tag) << 32) | payload;
+}
+__device__ __forceinline__ bool has_tag(unsigned long long w, uint32_t tag) {
+  return static_cast<uint32_t>(w >> 32) == tag;
+}
+
+// Eight fp16 values from four tagged words at p (16-byte aligned) once all
+// four carry `tag`: tagged4_issue loads them, tagged4_finish checks the tags
+// and re-polls if needed (bounded: on timeout the CTA's abort flag is raised
+// and zeros are returned).  Issuing several groups before finishing any keeps
+// their loads in flight together.
+struct Tagged4 {
+  unsigned long long w[4];
+};
+__device__ __forceinline__ void tagged4_issue(const unsigned long long* p, Tagged4& t) {
+  ld_tagged2(p, t.w[0], t.w[1]);
+  ld_tagged2(p + 2, t.w[2], t.w[3]);
+}
+__device__ __forceinline__ bool tagged4_ok(const Tagged4& t, uint32_t tag) {
+  return has_tag(t.w[0], tag) && has_tag(t.w[1], tag) && has_tag(t.w[2], tag) && has_tag(t.w[3], tag);
+}
+__device__ __forceinline__ uint4 tagged4_payload(const Tagged4& t) {
+  return make_uint4(static_cast<uint32_t>(t.w[0]), static_cast<uint32_t>(t.w[1]), static_cast<uint32_t>(t.w[2]),
+                    static_cast<uint32_t>(t.w[3]));
+}
+__device__ __noinline__ uint4 tagged4_spin(int32_t* error, volatile int* abort_flag, const unsigned long long* p,
+                                           uint32_t tag) {
+  const uint64_t t0 = globaltimer();
+  Tagged4 t;
+  while (true) {
+    tagged4_issue(p, t);
+    if (tagged4_ok(t, tag)) return tagged4_payload(t);
+    if (*abort_flag || globaltimer() - t0 > kTimeoutNs) break;
+  }
+  if (!*abort_flag) {
+    atomicExch(error, 1);
+    *abort_flag = 1;
+  }
+  return make_uint4(0u, 0u, 0u, 0u);
+}
+__device__ __forceinline__ uint4 tagged4_finish(const Params& P, Smem& S, const unsigned long long* p,
+                                                uint32_t tag, const Tagged4& t) {
+  if (tagged4_ok(t, tag)) return tagged4_payload(t);
+  return tagged4_spin(P.s.error, reinterpret_cast<volatile int*>(&S.misc[0]), p, tag);
+}
+
+// One tagged word (acquire: later loads of this thread see what the writer
+// published before it).
+__device__ __forceinline__ uint32_t poll1(const Params& P, Smem& S, const unsigned long long* p, uint32_t tag) {
+  unsigned long long w = ld_tagged_acquire(p);
+  if (!has_tag(w, tag)) {
     const uint64_t t0 = globaltimer();
-    while (ld_acquire_u32(P.arrive) < target) {
+    while (true) {
+      w = ld_tagged_acquire(p);
+      if (has_tag(w, tag)) break;
+      if (aborting(S)) return 0u;
       if (globaltimer() - t0 > kTimeoutNs) {
-        atomicExch(P.s.error, 1);
-        *reinterpret_cast<volatile int*>(&S.misc[0]) = 1;
-        break;
+        raise_abort(P, S, 1);
+        return 0u;
       }
     }
   }
-  consumer_sync();
-  cs.ok = *reinterpret_cast<volatile int*>(&S.misc[0]) == 0;
-  return cs.ok;
+  return static_cast<uint32_t>(w);
 }
 
-// This CTA finished a stage: publish its writes, then count it.
-__device__ void grid_arrive(const Params& P, CState& cs) {
-  __threadfence();
+// Publish output rows [r0, r1) (an even range) of the NB sequences from
+// shared memory (src[b * sld + i] = row r0 + i) as tagged pairs.
+template <int NB>
+__device__ void publish(const Params& P, const __half* src, int sld, unsigned long long* dst, int dld, int r0,
+                        int r1, uint32_t tag) {
   consumer_sync();
-  if (threadIdx.x == 0) atomicAdd(P.arrive, 1u);
-  cs.arrivals += gridDim.x;
+  const int np = (r1 - r0) / 2;
+  for (int i = threadIdx.x; i < NB * np; i += kConsumers) {
+    const int b = i / np, pr = i - b * np;
+    if (b < P.s.batch) {
+      const uint32_t pay = *reinterpret_cast<const uint32_t*>(src + b * sld + 2 * pr);
+      st_tagged(dst + static_cast<size_t>(b) * dld + r0 / 2 + pr, tagged(tag, pay));
+    }
+  }
 }
 
 // Wait for the next ring chunk.  Control flow stays uniform across the
 // consumers: a thread that gives up (timeout, or the CTA already aborting)
 // raises the abort flag and carries on with the slot's stale contents -- all
 // reads stay inside shared memory and all writes inside the stage's outputs --
-// and the CTA leaves together at its next grid_wait.
-__device__ void slot_wait(Smem& S, const Params& P, CState& cs, int& slot) {
-  slot = cs.chunk % P.slots;
-  const uint32_t phase = (cs.chunk / P.slots) & 1u;
+// and the CTA leaves together at its next abort check (after a block sync).
+__device__ void slot_wait(Smem& S, const Params& P, CState& cs) {
+  const int slot = cs.slot;
+  const uint32_t phase = cs.phase;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(&S.misc[0]);
-  if (mbar_try_wait(&S.full[slot], phase)) return;
+  if (mbar_test_wait(&S.full[slot], phase)) return;
   const uint64_t t0 = globaltimer();
   while (!mbar_try_wait(&S.full[slot], phase)) {
     if (*abort_flag) return;
     if (globaltimer() - t0 > kTimeoutNs) {
-      atomicExch(P.s.error, 1);
-      *abort_flag = 1;
+      raise_abort(P, S, 1);
       return;
     }
   }
   if (P.s.trace && threadIdx.x == 0) cs.wait_ns += globaltimer() - t0;
 }
 
-__device__ __forceinline__ void slot_release(Smem& S, CState& cs, int slot) {
-  __syncwarp();
-  if ((threadIdx.x & 31) == 0) mbar_arrive(&S.empty[slot]);
-}
-
-// Block (consumer) sum of one float per thread; every consumer gets the total.
-__device__ __forceinline__ float consumer_sum(float v, float* red8) {
-  v = warp_sum(v);
+// Block (consumer) sums of NB floats per thread; every consumer gets the totals.
+template <int NB>
+__device__ __forceinline__ void consumer_sum_n(float (&v)[NB], float* red8) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) red8[warp] = v;
-  consumer_sync();
-  float t = 0.0f;
 #pragma unroll
-  for (int w = 0; w < kConsumerWarps; ++w) t += red8[w];
+  for (int b = 0; b < NB; ++b) {
+    const float w = warp_sum(v[b]);
+    if (lane == 0) red8[warp * kMaxB + b] = w;
+  }
   consumer_sync();
-  return t;
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    float t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) t += red8[w * kMaxB + b];
+    v[b] = t;
+  }
+  consumer_sync();
 }
 
 // ---------------------------------------------------------------------------
@@ -389,14 +490,11 @@ __device__ __forceinline__ void store_planes(const float (&v)[8], bool active, c
   sx += __shfl_xor_sync(0xffffffffu, sx, 1);
   sx += __shfl_xor_sync(0xffffffffu, sx, 2);
   if (active) {
-    uint32_t he = 0, ho = 0, le = 0, lo = 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      he |= (static_cast<uint32_t>(X[2 * k] >> 8) & 0xFFu) << (8 * k);
-      ho |= (static_cast<uint32_t>(X[2 * k + 1] >> 8) & 0xFFu) << (8 * k);
-      le |= (static_cast<uint32_t>(X[2 * k]) & 0xFFu) << (8 * k);
-      lo |= (static_cast<uint32_t>(X[2 * k + 1]) & 0xFFu) << (8 * k);
-    }
+    // byte 0 (L) and byte 1 (H) of the even / odd elements, four per word
+    const uint32_t pe0 = __byte_perm(X[0], X[2], 0x5140), pe1 = __byte_perm(X[4], X[6], 0x5140);
+    const uint32_t po0 = __byte_perm(X[1], X[3], 0x5140), po1 = __byte_perm(X[5], X[7], 0x5140);
+    const uint32_t le = __byte_perm(pe0, pe1, 0x5410), he = __byte_perm(pe0, pe1, 0x7632);
+    const uint32_t lo = __byte_perm(po0, po1, 0x5410), ho = __byte_perm(po0, po1, 0x7632);
     const int c = threadIdx.x & 3;
     const int sw = (g >> 1) & 3;  // quad swizzle, see load_xgroup
     uint32_t* gw = pl.w + (static_cast<size_t>(b) * pl.G + g) * 16;
@@ -411,81 +509,101 @@ __device__ __forceinline__ void store_planes(const float (&v)[8], bool active, c
   }
 }
 
-// Planes of fp16(fp16(x*scale) * gamma), x = rows[b] -- rms_norm.metal:20-39
-// over the full vector (k <= 4096).
+// Planes of fp16(fp16(x*scale) * gamma) -- rms_norm.metal:20-39 over the full
+// vector (k <= 8 * consumer threads) -- for every sequence; the sums of squares
+// share one block reduction.  x comes from the tagged rows tsrc[b * k/2 ..]
+// written by the stage tagged `tag`, or (tsrc == nullptr) from the plain fp16
+// rows[b] (embedding / caller input).
 template <int NB>
-__device__ void stage_norm(const Params& P, Smem& S, const __half* const* rows, bool rows_nc,
-                           const __half* gamma, int k) {
+__device__ void stage_norm(const Params& P, Smem& S, const __half* const (&rows)[NB],
+                           const unsigned long long* tsrc, uint32_t tag, const __half* gamma, int k) {
   const int vpr = k / 8;
   const Planes pl = planes_view(S, k / 32, NB);
-  constexpr int kMaxV = 1;  // vpr <= 512 chunks
+  const int c = threadIdx.x;
+  const bool active = c < vpr;
+  uint4 gv = make_uint4(0u, 0u, 0u, 0u);
+  if (active) gv = __ldg(reinterpret_cast<const uint4*>(gamma) + c);
+  uint4 v[NB];
+  float ss[NB];
+  if (tsrc) {
+    Tagged4 t[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+      if (active && b < P.s.batch) tagged4_issue(tsrc + static_cast<size_t>(b) * (k / 2) + 4 * c, t[b]);
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      v[b] = make_uint4(0u, 0u, 0u, 0u);
+      if (active && b < P.s.batch) v[b] = tagged4_finish(P, S, tsrc + static_cast<size_t>(b) * (k / 2) + 4 * c, tag, t[b]);
+    }
+  } else {
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      v[b] = make_uint4(0u, 0u, 0u, 0u);
+      if (active && b < P.s.batch) v[b] = __ldg(reinterpret_cast<const uint4*>(rows[b]) + c);
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < NB; ++b) ss[b] = 0.0f;
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    const __half2* h = reinterpret_cast<const __half2*>(&v[b]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h[e]);
+      ss[b] = fmaf(f.x, f.x, ss[b]);
+      ss[b] = fmaf(f.y, f.y, ss[b]);
+    }
+  }
+  consumer_sum_n<NB>(ss, S.red8);
+  const __half* gh = reinterpret_cast<const __half*>(&gv);
+#pragma unroll
   for (int b = 0; b < NB; ++b) {
     if (b >= P.s.batch) break;
-    uint4 v[kMaxV];
-    float ss = 0.0f;
+    const float scale = 1.0f / sqrtf(ss[b] / static_cast<float>(k) + P.m.eps);
+    const __half* xh = reinterpret_cast<const __half*>(&v[b]);
+    float nv[8];
 #pragma unroll
-    for (int i = 0; i < kMaxV; ++i) {
-      const int c = threadIdx.x + i * kConsumers;
-      v[i] = make_uint4(0u, 0u, 0u, 0u);
-      if (c < vpr) {
-        const uint4* src = reinterpret_cast<const uint4*>(rows[b]) + c;
-        v[i] = rows_nc ? __ldg(src) : __ldcg(src);
-        const __half2* h = reinterpret_cast<const __half2*>(&v[i]);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __half22float2(h[e]);
-          ss = fmaf(f.x, f.x, ss);
-          ss = fmaf(f.y, f.y, ss);
-        }
-      }
+    for (int e = 0; e < 8; ++e) {
+      const __half nrm = __float2half_rn(__half2float(xh[e]) * scale);
+      nv[e] = __half2float(__float2half_rn(__half2float(nrm) * __half2float(gh[e])));
     }
-    ss = consumer_sum(ss, S.red8);
-    const float scale = 1.0f / sqrtf(ss / static_cast<float>(k) + P.m.eps);
-#pragma unroll
-    for (int i = 0; i < kMaxV; ++i) {
-      const int c = threadIdx.x + i * kConsumers;
-      const bool active = c < vpr;
-      float nv[8];
-      uint4 gv = make_uint4(0u, 0u, 0u, 0u);
-      if (active) gv = __ldg(reinterpret_cast<const uint4*>(gamma) + c);
-      const __half* xh = reinterpret_cast<const __half*>(&v[i]);
-      const __half* gh = reinterpret_cast<const __half*>(&gv);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const __half nrm = __float2half_rn(__half2float(xh[e]) * scale);
-        nv[e] = __half2float(__float2half_rn(__half2float(nrm) * __half2float(gh[e])));
-      }
-      store_planes(nv, active, pl, b, c >> 2);
-    }
+    store_planes(nv, active, pl, b, c >> 2);
   }
   consumer_sync();
 }
 
-// Planes of src[b] (k fp16 elements, row stride ld) for every sequence.
+// Planes of the tagged rows src[b * k/2 ..] (k fp16 elements) of every sequence.
 template <int NB>
-__device__ void stage_copy(const Params& P, Smem& S, const __half* src, int ld, int k) {
+__device__ void stage_copy(const Params& P, Smem& S, const unsigned long long* src, uint32_t tag, int k) {
   const int vpr = k / 8;
   const Planes pl = planes_view(S, k / 32, NB);
   const int total = NB * vpr;
   const int rounds = (total + kConsumers - 1) / kConsumers;
-  constexpr int kBatch = 4;  // loads in flight per thread
+  constexpr int kBatch = 4;  // chunks in flight per thread
   for (int r0 = 0; r0 < rounds; r0 += kBatch) {
+    Tagged4 t[kBatch];
+#pragma unroll
+    for (int q = 0; q < kBatch; ++q) {
+      const int i = threadIdx.x + (r0 + q) * kConsumers;
+      const int b = i / vpr, c = i - b * vpr;
+      if (r0 + q < rounds && i < total && b < P.s.batch) tagged4_issue(src + static_cast<size_t>(b) * (k / 2) + 4 * c, t[q]);
+    }
     uint4 v[kBatch];
 #pragma unroll
-    for (int k = 0; k < kBatch; ++k) {
-      const int i = threadIdx.x + (r0 + k) * kConsumers;
+    for (int q = 0; q < kBatch; ++q) {
+      const int i = threadIdx.x + (r0 + q) * kConsumers;
       const int b = i / vpr, c = i - b * vpr;
-      v[k] = make_uint4(0u, 0u, 0u, 0u);
-      if (r0 + k < rounds && i < total && b < P.s.batch)
-        v[k] = __ldcg(reinterpret_cast<const uint4*>(src + static_cast<size_t>(b) * ld) + c);
+      v[q] = make_uint4(0u, 0u, 0u, 0u);
+      if (r0 + q < rounds && i < total && b < P.s.batch)
+        v[q] = tagged4_finish(P, S, src + static_cast<size_t>(b) * (k / 2) + 4 * c, tag, t[q]);
     }
 #pragma unroll
-    for (int k = 0; k < kBatch; ++k) {
-      if (r0 + k < rounds) {  // uniform across the CTA
-        const int i = threadIdx.x + (r0 + k) * kConsumers;
+    for (int q = 0; q < kBatch; ++q) {
+      if (r0 + q < rounds) {  // uniform across the CTA
+        const int i = threadIdx.x + (r0 + q) * kConsumers;
         const int b = i / vpr, c = i - b * vpr;
         const bool active = i < total && b < P.s.batch;
-        const __half* h = reinterpret_cast<const __half*>(&v[k]);
+        const __half* h = reinterpret_cast<const __half*>(&v[q]);
         float f[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) f[e] = __half2float(h[e]);
@@ -543,183 +661,156 @@ __device__ __forceinline__ void load_xgroup(const Planes& pl, int b, int g, XGro
   x.xs8 = pl.xs8[b * pl.G + g];
 }
 
-constexpr int kMaxJ = 4;  // groups per lane: G / 16 <= 3 (hidden <= 1536); down: ceil(G / warps / 8) <= 4
+constexpr int kJH = 3;    // groups per lane when k = hidden: G / 16 <= 3 (hidden <= 1536)
+constexpr int kMaxJ = 4;  // groups per lane in the down projection: ceil(G / warps / 8) <= 4
+
+__device__ __forceinline__ void slot_release(Smem& S, const Params& P, CState& cs) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&S.empty[cs.slot]);
+  if (++cs.slot == P.slots) {
+    cs.slot = 0;
+    cs.phase ^= 1u;
+  }
+}
+
+// acc[b] += scale * dot(weights of group gi, activation group gi of sequence b)
+template <int NB>
+__device__ __forceinline__ void group_fma(const Planes& pl, int gi, const uint4& wv, float sc, float (&acc)[NB]) {
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    XGroup xg;
+    load_xgroup(pl, b, gi, xg);
+    acc[b] = fmaf(sc * xg.scl, static_cast<float>(group_idot(wv, xg.w, xg.xs8)), acc[b]);
+  }
+}
 
 // ---------------------------------------------------------------------------
 // GEMV stages over ring chunks
 // ---------------------------------------------------------------------------
-// k = hidden stages (QKV, O, HEAD): chunk of <= 2*warps rows; warp w owns
-// rows 2w (lanes 0-15) and 2w+1 (lanes 16-31); lane sub takes groups sub,
-// sub+16, sub+32 of its row (weights and activation planes from shared memory).
-template <int NB, int KIND>
-__device__ void gemv_hidden(const Params& P, Smem& S, CState& cs, const Chunking& c,
-                            const __half* bias, const __half* const* res_rows, __half* out, int ldo,
-                            unsigned long long* best) {
+// Row GEMVs with k = hidden: q|k|v (+bias), o (+residual), gate/up (SwiGLU) and
+// the LM head (argmax).  A chunk holds <= 2*warps rows (gate/up: <= warps row
+// pairs); warp w takes rows 2w (lanes 0-15) and 2w+1 (lanes 16-31) -- for
+// gate/up, gate row w and up row w -- and lane sub groups sub, sub+16, sub+32.
+// One code path for every kind keeps the kernel's instruction footprint small.
+template <int NB>
+__device__ void gemv_rows(const Params& P, Smem& S, CState& cs, int kind, int layer, __half* logits, uint32_t tag) {
+  const Chunking c = stage_chunks(P, kind, layer);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = c.k / 32, JG = G / 16;
-  const int sub = lane & 15;
+  const int half = lane >> 4, sub = lane & 15;
+  const bool gu = kind == ST_GU;
+  const int lrow = gu ? warp : 2 * warp + half;  // row of the chunk this half-warp computes
+  const int rpc = c.rows_per_chunk;
+  const size_t rb = c.k / 2;
   const Planes pl = planes_view(S, G, NB);
-  for (int r = c.r0; r < c.r1; r += c.rows_per_chunk) {
-    const int n = min(c.rows_per_chunk, c.r1 - r);
-    int slot;
-    slot_wait(S, P, cs, slot);
-    const unsigned char* base = S.ring + static_cast<size_t>(slot) * kSlotBytes;
-    const int lrow = 2 * warp + (lane >> 4);
+  unsigned long long best[NB];
+#pragma unroll
+  for (int b = 0; b < NB; ++b) best[b] = 0ull;
+  for (int r = c.r0; r < c.r1; r += rpc) {
+    const int n = min(rpc, c.r1 - r);
+    const int slot = cs.slot;
+    slot_wait(S, P, cs);
     float acc[NB];
 #pragma unroll
     for (int b = 0; b < NB; ++b) acc[b] = 0.0f;
     if (lrow < n) {
-      const unsigned char* wrow = base + static_cast<size_t>(lrow) * (c.k / 2);
-      const __half* srow = reinterpret_cast<const __half*>(base + static_cast<size_t>(n) * (c.k / 2)) + lrow * G;
-      uint4 wv[kMaxJ];
-      float sc[kMaxJ];
+      const unsigned char* base = S.ring + static_cast<size_t>(slot) * kSlotBytes;
+      const size_t pbytes = n * rb * (gu ? 2 : 1);
+      const int srow_i = gu ? half * n + warp : lrow;  // scale row within the slot's scale block
+      const unsigned char* wrow = base + (gu ? half * n * rb : 0) + lrow * rb;
+      const __half* srow = reinterpret_cast<const __half*>(base + pbytes) + srow_i * G;
 #pragma unroll
-      for (int j = 0; j < kMaxJ; ++j) {
+      for (int j = 0; j < kJH; ++j) {
         if (j < JG) {
-          wv[j] = *reinterpret_cast<const uint4*>(wrow + (sub + 16 * j) * 16);
-          sc[j] = __half2float(srow[sub + 16 * j]);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < kMaxJ; ++j) {
-        if (j < JG) {
-#pragma unroll
-          for (int b = 0; b < NB; ++b) {
-            XGroup xg;
-            load_xgroup(pl, b, sub + 16 * j, xg);
-            acc[b] = fmaf(sc[j] * xg.scl, static_cast<float>(group_idot(wv[j], xg.w, xg.xs8)), acc[b]);
-          }
+          const int g = sub + 16 * j;
+          const uint4 wv = *reinterpret_cast<const uint4*>(wrow + g * 16);
+          group_fma<NB>(pl, g, wv, __half2float(srow[g]), acc);
         }
       }
     }
-    slot_release(S, cs, slot);
-    ++cs.chunk;
+    slot_release(S, P, cs);
 #pragma unroll
     for (int b = 0; b < NB; ++b) acc[b] = segment_sum<16>(acc[b]);
-    if (sub == 0 && lrow < n) {
-      const int row = r + lrow;
+    if (gu) {
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        const float u = __shfl_sync(0xffffffffu, acc[b], 16);
+        if (lane == 0 && warp < n && b < P.s.batch) {
+          const float gf = __half2float(__float2half_rn(acc[b]));
+          const float uf = __half2float(__float2half_rn(u));
+          S.outb[b * kOutMax + r + warp - c.r0] = __float2half_rn(silu_mul(gf, uf));
+        }
+      }
+    } else if (sub == 0 && lrow < n) {
+      const int row = r + lrow, i = row - c.r0;
 #pragma unroll
       for (int b = 0; b < NB; ++b) {
         if (b >= P.s.batch) break;
-        if constexpr (KIND == ST_QKV) {
-          out[static_cast<size_t>(b) * ldo + row] = __float2half_rn(acc[b] + __half2float(bias[row]));
-        } else if constexpr (KIND == ST_O) {
-          const __half o = __float2half_rn(acc[b]);
-          out[static_cast<size_t>(b) * ldo + row] = __hadd(__ldcg(res_rows[b] + row), o);
+        if (kind == ST_QKV) {
+          S.outb[b * kOutMax + i] = __float2half_rn(acc[b] + __half2float(S.bias_own[layer * kOwnMax + i]));
+        } else if (kind == ST_O) {
+          S.x1own[b * kOwnMax + i] = __hadd(S.xown[b * kOwnMax + i], __float2half_rn(acc[b]));
         } else {  // ST_HEAD
           const __half v = __float2half_rn(acc[b]);
-          if (out) out[static_cast<size_t>(b) * ldo + row] = v;
+          if (logits) logits[static_cast<size_t>(b) * P.m.vocab + row] = v;
           best[b] = u64_max(best[b], argmax_key(__half2float(v), static_cast<uint32_t>(row)));
         }
       }
     }
   }
-}
-
-// Gate/up: chunk of <= 16 row pairs; warp w: gate row w on lanes 0-15, up row
-// w on lanes 16-31; lane 0 applies SwiGLU (swiglu.metal:19-22).
-template <int NB>
-__device__ void gemv_gateup(const Params& P, Smem& S, CState& cs, const Chunking& c) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = c.k / 32, JG = G / 16;
-  const int up = lane >> 4, sub = lane & 15;
-  const int inter = P.m.intermediate;
-  const Planes pl = planes_view(S, G, NB);
-  for (int r = c.r0; r < c.r1; r += c.rows_per_chunk) {
-    const int n = min(c.rows_per_chunk, c.r1 - r);
-    int slot;
-    slot_wait(S, P, cs, slot);
-    const unsigned char* base = S.ring + static_cast<size_t>(slot) * kSlotBytes;
-    const size_t pbytes = static_cast<size_t>(n) * (c.k / 2);
-    const size_t sbytes = static_cast<size_t>(n) * G * 2;
-    float acc[NB];
-#pragma unroll
-    for (int b = 0; b < NB; ++b) acc[b] = 0.0f;
-    if (warp < n) {
-      const unsigned char* wrow = base + up * pbytes + static_cast<size_t>(warp) * (c.k / 2);
-      const __half* srow = reinterpret_cast<const __half*>(base + 2 * pbytes + up * sbytes) + warp * G;
-      uint4 wv[kMaxJ];
-      float sc[kMaxJ];
-#pragma unroll
-      for (int j = 0; j < kMaxJ; ++j) {
-        if (j < JG) {
-          wv[j] = *reinterpret_cast<const uint4*>(wrow + (sub + 16 * j) * 16);
-          sc[j] = __half2float(srow[sub + 16 * j]);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < kMaxJ; ++j) {
-        if (j < JG) {
-#pragma unroll
-          for (int b = 0; b < NB; ++b) {
-            XGroup xg;
-            load_xgroup(pl, b, sub + 16 * j, xg);
-            acc[b] = fmaf(sc[j] * xg.scl, static_cast<float>(group_idot(wv[j], xg.w, xg.xs8)), acc[b]);
-          }
-        }
-      }
-    }
-    slot_release(S, cs, slot);
-    ++cs.chunk;
+  if (kind == ST_HEAD) {
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
-      acc[b] = segment_sum<16>(acc[b]);
-      const float u = __shfl_sync(0xffffffffu, acc[b], 16);
-      if (lane == 0 && warp < n && b < P.s.batch) {
-        const float gf = __half2float(__float2half_rn(acc[b]));
-        const float uf = __half2float(__float2half_rn(u));
-        P.a[static_cast<size_t>(b) * inter + r + warp] = __float2half_rn(silu_mul(gf, uf));
-      }
+      const unsigned long long w = warp_max_u64(best[b]);
+      if (lane == 0) S.best[warp * kMaxB + b] = w;
     }
+  } else if (kind == ST_O) {
+    publish<NB>(P, S.x1own, kOwnMax, P.x1t, P.m.hidden / 2, c.r0, c.r1, tag);
+  } else if (kind == ST_QKV) {
+    publish<NB>(P, S.outb, kOutMax, P.qkvt, (P.m.n_q_heads + 2 * P.m.n_kv_heads) * kHD / 2, c.r0, c.r1, tag);
+  } else {
+    publish<NB>(P, S.outb, kOutMax, P.at, P.m.intermediate / 2, c.r0, c.r1, tag);
   }
 }
 
-// Down projection (k = intermediate): chunk of <= 4 rows; warp w sums groups
-// [G*w/16, G*(w+1)/16) of every row (lane = row*8 + sub, groups g0+sub+8j),
-// partials meet in shared memory and one thread per row finishes:
-// x = x1 + fp16(acc).
+// Down projection (k = intermediate): chunks of <= 4 rows; warp w sums groups
+// [G*w/warps, G*(w+1)/warps) of every row (lane = row*8 + sub, groups
+// g0+sub+8j), partials meet in shared memory and one thread per (row,
+// sequence) finishes: x = x1 + fp16(acc).
 template <int NB>
-__device__ void gemv_down(const Params& P, Smem& S, CState& cs, const Chunking& c) {
+__device__ void gemv_down(const Params& P, Smem& S, CState& cs, int layer, uint32_t tag) {
+  const Chunking c = stage_chunks(P, ST_DN, layer);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = c.k / 32;
   const int g0 = G * warp / kConsumerWarps, g1 = G * (warp + 1) / kConsumerWarps;
   const int lrow = lane >> 3, sub = lane & 7;
   const int hidden = P.m.hidden;
+  const int rpc = c.rows_per_chunk;
   const Planes pl = planes_view(S, G, NB);
   int par = 0;
-  for (int r = c.r0; r < c.r1; r += c.rows_per_chunk, par ^= 1) {
-    const int n = min(c.rows_per_chunk, c.r1 - r);
-    int slot;
-    slot_wait(S, P, cs, slot);
-    const unsigned char* base = S.ring + static_cast<size_t>(slot) * kSlotBytes;
+  for (int r = c.r0; r < c.r1; r += rpc, par ^= 1) {
+    const int n = min(rpc, c.r1 - r);
+    const int slot = cs.slot;
+    slot_wait(S, P, cs);
     float acc[NB];
 #pragma unroll
     for (int b = 0; b < NB; ++b) acc[b] = 0.0f;
     if (lrow < n) {
+      const unsigned char* base = S.ring + static_cast<size_t>(slot) * kSlotBytes;
       const unsigned char* wrow = base + static_cast<size_t>(lrow) * (c.k / 2);
       const __half* srow = reinterpret_cast<const __half*>(base + static_cast<size_t>(n) * (c.k / 2)) + lrow * G;
 #pragma unroll
       for (int j = 0; j < kMaxJ; ++j) {
         const int g = g0 + sub + 8 * j;
-        if (g < g1) {
-          const uint4 wv = *reinterpret_cast<const uint4*>(wrow + g * 16);
-          const float sc = __half2float(srow[g]);
-#pragma unroll
-          for (int b = 0; b < NB; ++b) {
-            XGroup xg;
-            load_xgroup(pl, b, g, xg);
-            acc[b] = fmaf(sc * xg.scl, static_cast<float>(group_idot(wv, xg.w, xg.xs8)), acc[b]);
-          }
-        }
+        if (g < g1) group_fma<NB>(pl, g, *reinterpret_cast<const uint4*>(wrow + g * 16), __half2float(srow[g]), acc);
       }
     }
-    slot_release(S, cs, slot);
-    ++cs.chunk;
+    slot_release(S, P, cs);
     float* red = S.red + par * (kConsumerWarps * kRowsDown * kMaxB);
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
-      acc[b] = segment_sum<8>(acc[b]);
-      if (sub == 0) red[(warp * kRowsDown + lrow) * kMaxB + b] = acc[b];
+      const float v = segment_sum<8>(acc[b]);
+      if (sub == 0) red[(warp * kRowsDown + lrow) * kMaxB + b] = v;
     }
     consumer_sync();
     if (threadIdx.x < n * NB) {
@@ -728,21 +819,12 @@ __device__ void gemv_down(const Params& P, Smem& S, CState& cs, const Chunking& 
         float t = 0.0f;
 #pragma unroll
         for (int w = 0; w < kConsumerWarps; ++w) t += red[(w * kRowsDown + lr) * kMaxB + b];
-        const int row = r + lr;
-        const __half d = __float2half_rn(t);
-        P.x[static_cast<size_t>(b) * hidden + row] = __hadd(__ldcg(P.x1 + static_cast<size_t>(b) * hidden + row), d);
+        const int row = r + lr, i = row - c.r0;
+        S.xown[b * kOwnMax + i] = __hadd(S.x1own[b * kOwnMax + i], __float2half_rn(t));
       }
     }
   }
-}
-
-// Attention sub-phase stamps of CTA 0 (timeline row 3*grid, when allocated).
-__device__ __forceinline__ void attn_stamp(const Params& P, int& aev) {
-  if (P.s.trace && P.s.trace_rows > 3 * static_cast<int>(gridDim.x) && blockIdx.x == 0 && threadIdx.x == 0) {
-    if (aev < P.s.trace_events)
-      P.s.trace[static_cast<size_t>(3 * gridDim.x) * P.s.trace_events + aev] = globaltimer();
-    ++aev;
-  }
+  publish<NB>(P, S.xown, kOwnMax, P.xt, hidden / 2, c.r0, c.r1, tag);
 }
 
 // ---------------------------------------------------------------------------
@@ -764,6 +846,8 @@ struct AttnSmemP {
   float m[kMaxG];
   float l[kMaxG];
   float alpha[kMaxG];
+  float2 rot[kHD / 2];                // (cos, sin) of pos * inv_freq[j]
+  __half raw[(kMaxG + 2) * kHD];      // this step's q heads, k, v rows before RoPE
   int is_last;
 };
 
@@ -803,7 +887,7 @@ __device__ __forceinline__ void rope_pair(int j, int style, int& i1, int& i2) {
 }
 
 __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, int b, int kvh,
-                          int split, int n_splits, int chunk, int pos, int& aev) {
+                          int split, int n_splits, int chunk, int pos, uint32_t in_tag, uint32_t out_tag) {
   AttnSmemP& A = *reinterpret_cast<AttnSmemP*>(S.act);
   const lmps_model_desc& m = P.m;
   const int tid = threadIdx.x;
@@ -811,7 +895,8 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
   const int qkv_rows = (Hq + 2 * Hkv) * kHD;
   const int T = pos + 1;
   const int start = split * chunk, end = min(T, start + chunk);
-  const __half* row = P.qkv + static_cast<size_t>(b) * qkv_rows;
+  const unsigned long long* row = P.qkvt + static_cast<size_t>(b) * (qkv_rows / 2);
+  unsigned long long* out = P.attnt + static_cast<size_t>(b) * (Hq * kHD / 2);
   const float fpos = static_cast<float>(pos);
   const int ps = P.s.page_size;
   const int32_t* bt = P.s.block_table + static_cast<size_t>(b) * P.s.max_pages;
@@ -856,71 +941,27 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
       }
     }
   };
-  attn_stamp(P, aev);
   // Every global load of the prologue is issued before any of them is used:
-  // the first K/V tile, this group's q pairs, the new k pair and v element.
+  // the first K/V tile, then this group's q rows and (the split holding the
+  // new position) the k and v rows, polled from the tagged q|k|v output.
   if (start < end) load_tile(start);
-  constexpr int kQ = (kMaxG * (kHD / 2) + kConsumers - 1) / kConsumers;
-  float qa[kQ], qb[kQ];
-#pragma unroll
-  for (int it = 0; it < kQ; ++it) {
-    const int i = tid + it * kConsumers;
-    qa[it] = qb[it] = 0.0f;
-    if (i < G * (kHD / 2)) {
-      const int h = i / (kHD / 2), j = i - h * (kHD / 2);
-      int i1, i2;
-      rope_pair(j, m.rope_style, i1, i2);
-      const __half* qh = row + (kvh * G + h) * kHD;
-      qa[it] = __half2float(__ldcg(qh + i1));
-      qb[it] = __half2float(__ldcg(qh + i2));
-    }
-  }
   const bool has_pos = pos >= start && pos < end;
-  const __half* kh = row + (Hq + kvh) * kHD;
-  const __half* vh = row + (Hq + Hkv + kvh) * kHD;
-  float ka = 0.0f, kb = 0.0f;
-  __half vnew = __float2half_rn(0.0f);
-  int ki1 = 0, ki2 = 0;
-  if (has_pos) {
-    if (tid < kHD / 2) {
-      rope_pair(tid, m.rope_style, ki1, ki2);
-      ka = __half2float(__ldcg(kh + ki1));
-      kb = __half2float(__ldcg(kh + ki2));
-    } else if (tid < kHD / 2 + kHD) {
-      vnew = __ldcg(vh + (tid - kHD / 2));
+  {
+    const int nq4 = G * (kHD / 8), n4 = nq4 + (has_pos ? 2 * (kHD / 8) : 0);  // 4-word groups
+    if (tid < n4) {
+      const int seg = tid < nq4 ? kvh * G + tid / (kHD / 8)                          // q head
+                                : (tid - nq4 < kHD / 8 ? Hq + kvh : Hq + Hkv + kvh);  // k / v row
+      const unsigned long long* src = row + seg * (kHD / 2) + 4 * (tid % (kHD / 8));
+      Tagged4 t;
+      tagged4_issue(src, t);
+      *reinterpret_cast<uint4*>(&A.raw[8 * tid]) = tagged4_finish(P, S, src, in_tag, t);
     }
   }
-  // RoPE'd q of the G heads sharing this KV head (rope.metal:19-40), fp16-rounded.
-#pragma unroll
-  for (int it = 0; it < kQ; ++it) {
-    const int i = tid + it * kConsumers;
-    if (i < G * (kHD / 2)) {
-      const int h = i / (kHD / 2), j = i - h * (kHD / 2);
-      int i1, i2;
-      rope_pair(j, m.rope_style, i1, i2);
-      float sn, cs;
-      sincosf(fpos * S.inv_freq[j], &sn, &cs);
-      A.qh[h][i1] = __float2half_rn(qa[it] * cs - qb[it] * sn);
-      A.qh[h][i2] = __float2half_rn(qa[it] * sn + qb[it] * cs);
-    }
-  }
-  // The split holding the new position appends its rotated k and raw v.
-  if (has_pos) {
-    const int page = bt[pos / ps], off = pos % ps;
-    const size_t base = ((static_cast<size_t>(page) * Hkv + kvh) * ps + off) * kHD;
-    if (tid < kHD / 2) {
-      float sn, cs;
-      sincosf(fpos * S.inv_freq[tid], &sn, &cs);
-      const __half k1 = __float2half_rn(ka * cs - kb * sn), k2 = __float2half_rn(ka * sn + kb * cs);
-      kpool[base + ki1] = k1;
-      kpool[base + ki2] = k2;
-      A.knew[ki1] = k1;
-      A.knew[ki2] = k2;
-    } else if (tid < kHD / 2 + kHD) {
-      const int d = tid - kHD / 2;
-      vpool[base + d] = vnew;
-      A.vnew[d] = vnew;
-    }
+  // RoPE angles of this position (rope.metal:19-40), one table for q and k.
+  if (tid < kHD / 2) {
+    float sn, cs;
+    sincosf(fpos * S.inv_freq[tid], &sn, &cs);
+    A.rot[tid] = make_float2(cs, sn);
   }
   if (tid < kMaxG) {
     A.m[tid] = -INFINITY;
@@ -930,7 +971,39 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
     A.qh[G + i / kKStride][i % kKStride] = __float2half_rn(0.0f);
   for (int i = tid; i < (16 - G) * (kAttnTile + 8); i += kConsumers)
     A.ph[G + i / (kAttnTile + 8)][i % (kAttnTile + 8)] = __float2half_rn(0.0f);
-  constexpr int kHPT = (kMaxG + kConsumers / kHD - 1) / (kConsumers / kHD);   // heads per combine thread
+  consumer_sync();
+  // RoPE'd q of the G heads sharing this KV head, fp16-rounded.
+  for (int i = tid; i < G * (kHD / 2); i += kConsumers) {
+    const int h = i / (kHD / 2), j = i - h * (kHD / 2);
+    int i1, i2;
+    rope_pair(j, m.rope_style, i1, i2);
+    const float2 r = A.rot[j];
+    const float qa = __half2float(A.raw[h * kHD + i1]), qb = __half2float(A.raw[h * kHD + i2]);
+    A.qh[h][i1] = __float2half_rn(qa * r.x - qb * r.y);
+    A.qh[h][i2] = __float2half_rn(qa * r.y + qb * r.x);
+  }
+  // The split holding the new position appends its rotated k and raw v.
+  if (has_pos) {
+    const int page = bt[pos / ps], off = pos % ps;
+    const size_t base = ((static_cast<size_t>(page) * Hkv + kvh) * ps + off) * kHD;
+    const __half* kraw = A.raw + G * kHD;
+    if (tid < kHD / 2) {
+      int i1, i2;
+      rope_pair(tid, m.rope_style, i1, i2);
+      const float2 r = A.rot[tid];
+      const float ka = __half2float(kraw[i1]), kb = __half2float(kraw[i2]);
+      const __half k1 = __float2half_rn(ka * r.x - kb * r.y), k2 = __float2half_rn(ka * r.y + kb * r.x);
+      kpool[base + i1] = k1;
+      kpool[base + i2] = k2;
+      A.knew[i1] = k1;
+      A.knew[i2] = k2;
+    } else if (tid < kHD / 2 + kHD) {
+      const int d = tid - kHD / 2;
+      const __half v = kraw[kHD + d];
+      vpool[base + d] = v;
+      A.vnew[d] = v;
+    }
+  }
   const int warp = tid >> 5, lane = tid & 31;
   const int g8 = lane >> 2, t4 = lane & 3;           // mma fragment row / column pair
   const int mi = lane >> 3, r8 = lane & 7;           // ldmatrix lane -> matrix, row
@@ -940,14 +1013,12 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
 #pragma unroll
   for (int j = 0; j < kNTW; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
   consumer_sync();
-  attn_stamp(P, aev);
 
   for (int t0 = start; t0 < end; t0 += kAttnTile) {
     const int n = min(kAttnTile, end - t0);
     if (t0 != start) load_tile(t0);
     store_tile(t0);
     consumer_sync();
-    attn_stamp(P, aev);
     // scores S = Q K^T * 0.088388 (attention.metal:32-40): warp w < 8 owns
     // positions 8w..8w+7, eight k-steps over the 128 dims.
     if (warp < kAttnTile / 8) {
@@ -966,7 +1037,6 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
       }
     }
     consumer_sync();
-    attn_stamp(P, aev);
     {  // online softmax, one warp per head (softmax.metal:23-36)
       const int warp = tid >> 5, lane = tid & 31;
       if (warp < G) {
@@ -992,7 +1062,6 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
       }
     }
     consumer_sync();
-    attn_stamp(P, aev);
     // O += P V (attn_sum.metal:26-32): warp w owns output dims 8nt..8nt+7 for
     // nt = w, w + warps; the running sums are rescaled by this tile's alpha.
     {
@@ -1018,7 +1087,6 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
       }
     }
     consumer_sync();
-    attn_stamp(P, aev);
   }
 
   if (n_splits == 1) {
@@ -1029,9 +1097,9 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
       for (int j = 0; j < kNTW; ++j) {
         const int nt = warp + kConsumerWarps * j;
         if (nt < kNT) {
-          __half* dst = P.attn + static_cast<size_t>(b) * Hq * kHD + (kvh * G + g8) * kHD + 8 * nt + 2 * t4;
-          dst[0] = __float2half_rn(o[j][0] * inv);
-          dst[1] = __float2half_rn(o[j][1] * inv);
+          const __half2 v = __halves2half2(__float2half_rn(o[j][0] * inv), __float2half_rn(o[j][1] * inv));
+          st_tagged(out + (kvh * G + g8) * (kHD / 2) + 4 * nt + t4,
+                    tagged(out_tag, *reinterpret_cast<const uint32_t*>(&v)));
         }
       }
     }
@@ -1044,17 +1112,13 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
 #pragma unroll
     for (int j = 0; j < kNTW; ++j) {
       const int nt = warp + kConsumerWarps * j;
-      if (nt < kNT) {
-        P.part_o[prow * kHD + 8 * nt + 2 * t4] = o[j][0];
-        P.part_o[prow * kHD + 8 * nt + 2 * t4 + 1] = o[j][1];
-      }
+      if (nt < kNT) *reinterpret_cast<float2*>(&P.part_o[prow * kHD + 8 * nt + 2 * t4]) = make_float2(o[j][0], o[j][1]);
     }
   }
   if (tid < G) {
     const size_t prow = (static_cast<size_t>(b) * Hq + kvh * G + tid) * ms + split;
     P.part_ml[prow] = make_float2(A.m[tid], A.l[tid]);
   }
-  const int d = tid & (kHD - 1), hh = (tid < (kConsumers / kHD) * kHD) ? tid / kHD : kMaxG;
   __threadfence();
   consumer_sync();
   if (tid == 0) {
@@ -1062,29 +1126,36 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
     A.is_last = (old == static_cast<uint32_t>(n_splits - 1)) ? 1 : 0;
   }
   consumer_sync();
-  if (A.is_last) {  // the last split merges all partials of (b, kvh)
-    __threadfence();
-#pragma unroll
-    for (int j = 0; j < kHPT; ++j) {
-      const int h = hh + (kConsumers / kHD) * j;
-      if (h < G) {
-        const size_t prow0 = (static_cast<size_t>(b) * Hq + kvh * G + h) * ms;
-        float M = -INFINITY;
-        for (int sp = 0; sp < n_splits; ++sp) M = fmaxf(M, __ldcg(&P.part_ml[prow0 + sp].x));
-        float num = 0.0f, den = 0.0f;
-        for (int sp = 0; sp < n_splits; ++sp) {
-          const float2 ml = __ldcg(&P.part_ml[prow0 + sp]);
-          if (ml.y > 0.0f) {
-            const float w = expf(ml.x - M);
-            num = fmaf(w, __ldcg(&P.part_o[(prow0 + sp) * kHD + d]), num);
-            den = fmaf(w, ml.y, den);
-          }
-        }
-        P.attn[static_cast<size_t>(b) * Hq * kHD + (kvh * G + h) * kHD + d] =
-            __float2half_rn(den > 0.0f ? num / den : 0.0f);
-      }
+  if (A.is_last) {  // the last split merges all partials of (b, kvh) by log-sum-exp
+    if (tid == 0) {   // ready for the next layer before any output is published
+      P.att_cnt[b * Hkv + kvh] = 0u;
+      __threadfence();
     }
-    if (tid == 0) P.att_cnt[b * Hkv + kvh] = 0u;
+    consumer_sync();
+    __threadfence();
+#pragma unroll 1
+    for (int w = tid; w < G * (kHD / 2); w += kConsumers) {
+      const int h = w / (kHD / 2), dp = w - h * (kHD / 2);
+      const size_t prow0 = (static_cast<size_t>(b) * Hq + kvh * G + h) * ms;
+      float M = -INFINITY;
+#pragma unroll 1
+      for (int sp = 0; sp < n_splits; ++sp) M = fmaxf(M, __ldcg(&P.part_ml[prow0 + sp].x));
+      float n0 = 0.0f, n1 = 0.0f, den = 0.0f;
+#pragma unroll 1
+      for (int sp = 0; sp < n_splits; ++sp) {
+        const float2 ml = __ldcg(&P.part_ml[prow0 + sp]);
+        if (ml.y > 0.0f) {
+          const float wgt = expf(ml.x - M);
+          const float2 po = __ldcg(reinterpret_cast<const float2*>(&P.part_o[(prow0 + sp) * kHD + 2 * dp]));
+          n0 = fmaf(wgt, po.x, n0);
+          n1 = fmaf(wgt, po.y, n1);
+          den = fmaf(wgt, ml.y, den);
+        }
+      }
+      const __half2 v = den > 0.0f ? __halves2half2(__float2half_rn(n0 / den), __float2half_rn(n1 / den))
+                                   : __halves2half2(__float2half_rn(0.0f), __float2half_rn(0.0f));
+      st_tagged(out + (kvh * G + h) * (kHD / 2) + dp, tagged(out_tag, *reinterpret_cast<const uint32_t*>(&v)));
+    }
   }
   consumer_sync();
 }
@@ -1099,16 +1170,77 @@ __device__ __forceinline__ int attn_chunk_len(const int* pos, int batch, int n_k
   return static_cast<int>(c < kAttnTile ? kAttnTile : c);
 }
 
+// The next token of every sequence from the tagged per-CTA argmax slots of a
+// LM head stage (tag14 = low 14 bits of its tag): slot = value key (32) |
+// (0x3FFFF - row) (18) | tag14 (14).  Every consumer thread gets the rows.
+template <int NB>
+__device__ void gather_argmax(const Params& P, Smem& S, uint32_t tag14, int (&row)[NB]) {
+  const int B = P.s.batch;
+  const int n = gridDim.x * kMaxB;
+  unsigned long long best[NB];
+#pragma unroll
+  for (int b = 0; b < NB; ++b) best[b] = 0ull;
+  unsigned long long w[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int i = threadIdx.x + q * kConsumers;
+    w[q] = (i < n && (i % kMaxB) < B) ? ld_tagged_acquire(P.kslot + i) : 0ull;
+  }
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int i = threadIdx.x + q * kConsumers;
+    if (i < n && (i % kMaxB) < B) {
+      if ((w[q] & 0x3FFFull) != tag14) {
+        const uint64_t t0 = globaltimer();
+        while (true) {
+          w[q] = ld_tagged_acquire(P.kslot + i);
+          if ((w[q] & 0x3FFFull) == tag14) break;
+          if (aborting(S)) break;
+          if (globaltimer() - t0 > kTimeoutNs) {
+            raise_abort(P, S, 1);
+            break;
+          }
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < NB; ++b)
+        if (b == i % kMaxB) best[b] = u64_max(best[b], w[q]);
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    const unsigned long long v = warp_max_u64(best[b]);
+    if (lane == 0) S.best[warp * kMaxB + b] = v;
+  }
+  consumer_sync();
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    unsigned long long v = 0ull;
+#pragma unroll
+    for (int ww = 0; ww < kConsumerWarps; ++ww) v = u64_max(v, S.best[ww * kMaxB + b]);
+    row[b] = 0x3FFFF - static_cast<int>((v >> 14) & 0x3FFFFull);
+  }
+  consumer_sync();
+}
+
 // ---------------------------------------------------------------------------
 // Consumers: the decode loop
 // ---------------------------------------------------------------------------
+// Stages of a step in order: per layer q|k|v, attention, o, gate/up, down;
+// then the LM head.  Each stage function has exactly one call site below, so
+// the kernel's code is one copy of every stage.  Stage si of step `step`
+// publishes its output with tag epoch + step * n_stage + si + 1; the next
+// stage polls for that tag, so no grid-wide barrier is needed.
+enum StepStage { K_QKV = 0, K_ATT = 1, K_O = 2, K_GU = 3, K_DN = 4, K_HEAD = 5 };
+
 template <int NB>
-__device__ void consumer(const Params& P, Smem& S) {
-  CState cs{0u, 0u, true, 0ull};
+__device__ void consumer(const Params& P, Smem& S, uint32_t epoch) {
+  CState cs{0, 0u, 0ull};
   const lmps_model_desc& m = P.m;
   const int B = P.s.batch;
-  const int hidden = m.hidden, Hq = m.n_q_heads, Hkv = m.n_kv_heads;
-  const int q_dim = Hq * kHD, qkv_rows = (Hq + 2 * Hkv) * kHD;
+  const int hidden = m.hidden, Hkv = m.n_kv_heads;
+  const int q_dim = m.n_q_heads * kHD;
   int tok[NB], pos[NB];
 #pragma unroll
   for (int b = 0; b < NB; ++b) {
@@ -1116,69 +1248,71 @@ __device__ void consumer(const Params& P, Smem& S) {
     pos[b] = b < B ? P.s.pos[b] : 0;
   }
   const int hist0 = (P.s.history && P.s.step_counter) ? P.s.step_counter[0] : 0;
-  bool first_stage = true;
-  int ev = 0, aev = 0;
+  int ev = 0;
   const bool tr = threadIdx.x == 0;
+  const int n_stage = m.n_layers * 5 + 1;
+  int o0, o1;
+  row_range(hidden, blockIdx.x, gridDim.x, o0, o1);
+  const __half* embed = reinterpret_cast<const __half*>(m.embed);
+  const __half* x_in = reinterpret_cast<const __half*>(P.s.x_in);
 
   for (int step = 0; step < P.n_steps; ++step) {
-    const int par = step & 1;
-    if (!first_stage) {
-      // previous step's HEAD finished everywhere: next tokens from its argmax
-      if (!grid_wait(P, S, cs)) return;
-      const int pp = par ^ 1;
+    const uint32_t tag0 = epoch + static_cast<uint32_t>(step * n_stage) + 1u;  // tag of stage 0
+    if (step > 0) {
+      // next tokens from the previous step's LM head
+      int nxt[NB];
+      gather_argmax<NB>(P, S, (tag0 - 1u) & 0x3FFFu, nxt);
+      if (aborting(S)) return;
 #pragma unroll
       for (int b = 0; b < NB; ++b) {
         if (b < B) {
-          const unsigned long long key = __ldcg(P.keys + pp * B + b);
-          int nxt = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(key & 0xFFFFFFFFull));
-          if (nxt < 0 || nxt >= m.vocab) {  // no logit won (non-finite head output)
+          if (nxt[b] >= m.vocab) {  // no logit won (non-finite head output)
             if (threadIdx.x == 0) atomicExch(P.s.error, 3);
-            nxt = 0;
+            nxt[b] = 0;
           }
           if (blockIdx.x == 0 && threadIdx.x == 0 && P.s.history && hist0 + step - 1 >= 0 &&
               hist0 + step - 1 < P.s.history_rows)
-            P.s.history[static_cast<size_t>(hist0 + step - 1) * B + b] = nxt;
-          tok[b] = (step - 1 < P.s.n_forced && P.s.forced) ? P.s.forced[static_cast<size_t>(b) * P.s.forced_stride + step - 1] : nxt;
+            P.s.history[static_cast<size_t>(hist0 + step - 1) * B + b] = nxt[b];
+          tok[b] = (step - 1 < P.s.n_forced && P.s.forced) ? P.s.forced[static_cast<size_t>(b) * P.s.forced_stride + step - 1] : nxt[b];
           pos[b] += 1;
         }
       }
     }
-    const __half* xin[NB];
+    const bool from_x_in = step == 0 && x_in;
+    {  // residual rows this CTA owns start as the step's input rows
+      const int bb = threadIdx.x / kOwnMax, i = threadIdx.x - bb * kOwnMax;
 #pragma unroll
-    for (int b = 0; b < NB; ++b) {
-      const int bb = b < B ? b : 0;
-      xin[b] = (step == 0 && P.s.x_in) ? reinterpret_cast<const __half*>(P.s.x_in) + static_cast<size_t>(bb) * hidden
-                                       : reinterpret_cast<const __half*>(m.embed) + static_cast<size_t>(tok[bb]) * hidden;
+      for (int b = 0; b < NB; ++b) {
+        if (b == bb && b < B && i < o1 - o0) {
+          const __half* src = from_x_in ? x_in + static_cast<size_t>(b) * hidden : embed + static_cast<size_t>(tok[b]) * hidden;
+          S.xown[b * kOwnMax + i] = src[o0 + i];
+        }
+      }
     }
-    const __half* xres[NB];
+    for (int si = 0; si < n_stage; ++si) {
+      if (aborting(S)) return;  // uniform: every wait that raises it is followed by a block sync
+      const int l = si / 5;
+      const int kind = (l == m.n_layers) ? K_HEAD : si - 5 * l;
+      const uint32_t tag = tag0 + static_cast<uint32_t>(si), in_tag = tag - 1u;
+      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
+      const lmps_layer_desc& L = m.layers[kind == K_HEAD ? 0 : l];
+      // -- stage the input activation in shared memory
+      if (kind == K_QKV || kind == K_GU || kind == K_HEAD) {
+        const __half* rows[NB];
 #pragma unroll
-    for (int b = 0; b < NB; ++b) xres[b] = P.x + static_cast<size_t>(b < B ? b : 0) * hidden;
-    const __half* x1rows[NB];
-#pragma unroll
-    for (int b = 0; b < NB; ++b) x1rows[b] = P.x1 + static_cast<size_t>(b < B ? b : 0) * hidden;
-
-    for (int l = 0; l < m.n_layers; ++l) {
-      const lmps_layer_desc& L = m.layers[l];
-      // ---- QKV
-      if (!first_stage && l > 0) {
-        if (!grid_wait(P, S, cs)) return;
-      }
-      first_stage = false;
-      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
-      stage_norm<NB>(P, S, l == 0 ? xin : xres, l == 0, reinterpret_cast<const __half*>(L.in_norm), hidden);
-      {
-        const Chunking c = stage_chunks(P, ST_QKV, l);
-        gemv_hidden<NB, ST_QKV>(P, S, cs, c, reinterpret_cast<const __half*>(L.qkv_bias), nullptr, P.qkv,
-                                qkv_rows, nullptr);
+        for (int b = 0; b < NB; ++b) {
+          const int bb = b < B ? b : 0;
+          rows[b] = from_x_in ? x_in + static_cast<size_t>(bb) * hidden : embed + static_cast<size_t>(tok[bb]) * hidden;
+        }
+        const unsigned long long* tsrc = (kind == K_QKV && l == 0) ? nullptr : kind == K_GU ? P.x1t : P.xt;
+        const void* gamma = kind == K_QKV ? L.in_norm : kind == K_GU ? L.post_norm : m.final_norm;
+        stage_norm<NB>(P, S, rows, tsrc, in_tag, reinterpret_cast<const __half*>(gamma), hidden);
+      } else if (kind == K_O || kind == K_DN) {
+        stage_copy<NB>(P, S, kind == K_O ? P.attnt : P.at, in_tag, kind == K_O ? q_dim : m.intermediate);
       }
       if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
-      grid_arrive(P, cs);
-      // ---- ATT
-      if (!grid_wait(P, S, cs)) return;
-      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
-      if (l == 0 && step > 0 && blockIdx.x == 0 && threadIdx.x < B)
-        P.keys[(par ^ 1) * B + threadIdx.x] = 0ull;  // everyone has read the previous argmax
-      {
+      // -- compute and publish
+      if (kind == K_ATT) {
         const int chunk = attn_chunk_len(pos, B, Hkv);
         int n_items = 0;
 #pragma unroll
@@ -1201,94 +1335,53 @@ __device__ void consumer(const Params& P, Smem& S) {
 #pragma unroll
           for (int b = 0; b < NB; ++b)
             if (b == bsel) pb = pos[b];
-          attn_item(P, S, L, bsel, kvh, sp, nsp, chunk, pb, aev);
+          attn_item(P, S, L, bsel, kvh, sp, nsp, chunk, pb, in_tag, tag);
+        }
+      } else if (kind == K_DN) {
+        gemv_down<NB>(P, S, cs, l, tag);
+      } else {
+        const int wk = kind == K_QKV ? ST_QKV : kind == K_O ? ST_O : kind == K_GU ? ST_GU : ST_HEAD;
+        __half* lg = (kind == K_HEAD && step == P.n_steps - 1) ? reinterpret_cast<__half*>(P.s.logits) : nullptr;
+        gemv_rows<NB>(P, S, cs, wk, l, lg, tag);
+        if (kind == K_HEAD) {
+          consumer_sync();
+          if (threadIdx.x < B) {
+            unsigned long long v = 0ull;
+            for (int w = 0; w < kConsumerWarps; ++w) v = u64_max(v, S.best[w * kMaxB + threadIdx.x]);
+            const uint32_t row = 0xFFFFFFFFu - static_cast<uint32_t>(v);
+            const unsigned long long slot =
+                v ? ((v >> 32) << 32) | (static_cast<unsigned long long>(0x3FFFFu - row) << 14) : 0ull;
+            st_tagged(P.kslot + blockIdx.x * kMaxB + threadIdx.x, slot | (tag & 0x3FFFu));
+          }
         }
       }
       if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
-      grid_arrive(P, cs);
-      // ---- O
-      if (!grid_wait(P, S, cs)) return;
-      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
-      stage_copy<NB>(P, S, P.attn, q_dim, q_dim);
-      {
-        const Chunking c = stage_chunks(P, ST_O, l);
-        gemv_hidden<NB, ST_O>(P, S, cs, c, nullptr, l == 0 ? xin : xres, P.x1, hidden, nullptr);
-      }
-      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
-      grid_arrive(P, cs);
-      // ---- GU
-      if (!grid_wait(P, S, cs)) return;
-      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
-      stage_norm<NB>(P, S, x1rows, false, reinterpret_cast<const __half*>(L.post_norm), hidden);
-      {
-        const Chunking c = stage_chunks(P, ST_GU, l);
-        gemv_gateup<NB>(P, S, cs, c);
-      }
-      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
-      grid_arrive(P, cs);
-      // ---- DN
-      if (!grid_wait(P, S, cs)) return;
-      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
-      stage_copy<NB>(P, S, P.a, m.intermediate, m.intermediate);
-      {
-        const Chunking c = stage_chunks(P, ST_DN, l);
-        gemv_down<NB>(P, S, cs, c);
-      }
-      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
-      grid_arrive(P, cs);
     }
-    // ---- HEAD
-    if (!grid_wait(P, S, cs)) return;
-    if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
-    stage_norm<NB>(P, S, xres, false, reinterpret_cast<const __half*>(m.final_norm), hidden);
-    {
-      unsigned long long best[NB];
-#pragma unroll
-      for (int b = 0; b < NB; ++b) best[b] = 0ull;
-      const Chunking c = stage_chunks(P, ST_HEAD, 0);
-      __half* lg = (step == P.n_steps - 1 && P.s.logits) ? reinterpret_cast<__half*>(P.s.logits) : nullptr;
-      gemv_hidden<NB, ST_HEAD>(P, S, cs, c, nullptr, nullptr, lg, m.vocab, best);
-      const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  }
+  // ---- CTA 0: final tokens, state write-back, next launch's tag base
+  if (blockIdx.x != 0) return;
+  {
+    const int last = P.n_steps - 1;
+    int nxt[NB];
+    gather_argmax<NB>(P, S, (epoch + static_cast<uint32_t>(P.n_steps * n_stage)) & 0x3FFFu, nxt);
+    if (aborting(S)) return;
+    if (threadIdx.x == 0) {
 #pragma unroll
       for (int b = 0; b < NB; ++b) {
-        const unsigned long long w = warp_max_u64(best[b]);
-        if (lane == 0) S.best[warp * kMaxB + b] = w;
-      }
-      consumer_sync();
-      if (threadIdx.x < B) {
-        unsigned long long v = 0ull;
-        for (int w = 0; w < kConsumerWarps; ++w) v = u64_max(v, S.best[w * kMaxB + threadIdx.x]);
-        if (v) atomicMax(P.keys + par * B + threadIdx.x, v);
-      }
-    }
-    if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
-    grid_arrive(P, cs);
-  }
-  // ---- final tokens, state write-back, exit barrier
-  if (!grid_wait(P, S, cs)) return;
-  {
-    const int last = P.n_steps - 1, pp = last & 1;
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
-      for (int b = 0; b < B; ++b) {
-        const unsigned long long key = __ldcg(P.keys + pp * B + b);
-        const int nxt = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(key & 0xFFFFFFFFull));
-        if (P.s.history && hist0 + last >= 0 && hist0 + last < P.s.history_rows)
-          P.s.history[static_cast<size_t>(hist0 + last) * B + b] = nxt;
-        int p_fin = 0;
-#pragma unroll
-        for (int bb = 0; bb < NB; ++bb)
-          if (bb == b) p_fin = pos[bb];
-        P.s.tokens[b] = (last < P.s.n_forced && P.s.forced) ? P.s.forced[static_cast<size_t>(b) * P.s.forced_stride + last] : nxt;
-        P.s.pos[b] = p_fin + 1;
+        if (b < B) {
+          if (nxt[b] >= m.vocab) {
+            atomicExch(P.s.error, 3);
+            nxt[b] = 0;
+          }
+          if (P.s.history && hist0 + last >= 0 && hist0 + last < P.s.history_rows)
+            P.s.history[static_cast<size_t>(hist0 + last) * B + b] = nxt[b];
+          P.s.tokens[b] = (last < P.s.n_forced && P.s.forced) ? P.s.forced[static_cast<size_t>(b) * P.s.forced_stride + last] : nxt[b];
+          P.s.pos[b] = pos[b] + 1;
+        }
       }
       if (P.s.history && P.s.step_counter) P.s.step_counter[0] = hist0 + P.n_steps;
+      *P.epoch = epoch + static_cast<uint32_t>(P.n_steps * n_stage) + 1u;
     }
-  }
-  grid_arrive(P, cs);
-  if (blockIdx.x == 0) {
-    if (!grid_wait(P, S, cs)) return;
-    if (threadIdx.x < 2 * B) P.keys[threadIdx.x] = 0ull;
-    if (threadIdx.x == 0) *P.arrive = 0u;
   }
 }
 
@@ -1302,11 +1395,26 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
   S.full = reinterpret_cast<uint64_t*>(tail);
   S.empty = S.full + 16;
   S.red = reinterpret_cast<float*>(S.empty + 16);
-  S.red8 = S.red + 2 * kConsumerWarps * kRowsDown * kMaxB;
-  S.best = reinterpret_cast<unsigned long long*>(S.red8 + 8 * kMaxB);
+  S.red8 = S.red + kRedFloats;
+  S.best = reinterpret_cast<unsigned long long*>(S.red8 + kConsumerWarps * kMaxB);
   S.misc = reinterpret_cast<int*>(S.best + kConsumerWarps * kMaxB);
   S.inv_freq = reinterpret_cast<float*>(S.misc + 16);
+  S.xown = reinterpret_cast<__half*>(S.inv_freq + kHD / 2);
+  S.x1own = S.xown + kMaxB * kOwnMax;
+  S.outb = S.x1own + kMaxB * kOwnMax;
+  S.bias_own = S.outb + kMaxB * kOutMax;
+  // tag base of this launch (CTA 0 advances it after every CTA has used it)
+  const uint32_t epoch = __ldcg(P.epoch);
   for (int i = threadIdx.x; i < kHD / 2; i += blockDim.x) S.inv_freq[i] = P.m.inv_freq[i];
+  {  // q|k|v bias of this CTA's qkv rows, every layer
+    const int qkv_rows = (P.m.n_q_heads + 2 * P.m.n_kv_heads) * kHD;
+    int q0, q1;
+    row_range(qkv_rows, blockIdx.x, gridDim.x, q0, q1);
+    for (int i = threadIdx.x; i < P.m.n_layers * kOwnMax; i += blockDim.x) {
+      const int l = i / kOwnMax, r = i - l * kOwnMax;
+      if (r < q1 - q0) S.bias_own[i] = reinterpret_cast<const __half*>(P.m.layers[l].qkv_bias)[q0 + r];
+    }
+  }
   // Every position this launch touches must be inside the cache and every fed
   // token inside the vocabulary; all CTAs read the same values, so all leave
   // together (nothing has been issued yet).
@@ -1339,13 +1447,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
     if (threadIdx.x == kConsumers) producer(P, S);
     return;
   }
-  consumer<NB>(P, S);
+  consumer<NB>(P, S, epoch);
 }
 
-constexpr int kTailBytes = 4096;
+// Shared-memory tail after the ring and the activation area.
+static int tail_bytes(int n_layers) {
+  const size_t fixed = 32 * sizeof(uint64_t) + kRedFloats * sizeof(float) +
+                       kConsumerWarps * kMaxB * (sizeof(float) + sizeof(unsigned long long)) + 16 * sizeof(int) +
+                       kHD / 2 * sizeof(float) + (2 * kOwnMax + kOutMax) * kMaxB * sizeof(__half);
+  const size_t t = fixed + static_cast<size_t>(n_layers) * kOwnMax * sizeof(__half);
+  return static_cast<int>((t + 127) & ~static_cast<size_t>(127));
+}
 
 struct WsLayout {
-  size_t x, x1, qkv, attn, a, part_o, part_ml, att_cnt, keys, arrive, total;
+  size_t xt, x1t, qkvt, attnt, at, kslot, part_o, part_ml, att_cnt, epoch, total;
   int max_splits;
 };
 
@@ -1355,18 +1470,19 @@ static WsLayout ws_layout(const lmps_model_desc& m, int B, int max_seq_len) {
   WsLayout w{};
   const size_t qkv_rows = static_cast<size_t>(m.n_q_heads + 2 * m.n_kv_heads) * m.head_dim;
   const size_t q_dim = static_cast<size_t>(m.n_q_heads) * m.head_dim;
+  const size_t tw = sizeof(unsigned long long) / 2;  // tagged bytes per element
   w.max_splits = (max_seq_len + kAttnTile - 1) / kAttnTile;
   size_t off = 0;
-  // Counters that persist from one launch to the next come first, at offsets
+  // State that persists from one launch to the next comes first, at offsets
   // that do not depend on the batch size of the launch.
-  w.arrive = off; off = align256(off + sizeof(uint32_t));
-  w.keys = off; off = align256(off + sizeof(unsigned long long) * 2 * kMaxB);
+  w.epoch = off; off = align256(off + sizeof(uint32_t));
   w.att_cnt = off; off = align256(off + sizeof(uint32_t) * kMaxB * m.n_kv_heads);
-  w.x = off; off = align256(off + sizeof(__half) * B * m.hidden);
-  w.x1 = off; off = align256(off + sizeof(__half) * B * m.hidden);
-  w.qkv = off; off = align256(off + sizeof(__half) * B * qkv_rows);
-  w.attn = off; off = align256(off + sizeof(__half) * B * q_dim);
-  w.a = off; off = align256(off + sizeof(__half) * B * m.intermediate);
+  w.kslot = off; off = align256(off + sizeof(unsigned long long) * kMaxGrid * kMaxB);
+  w.xt = off; off = align256(off + tw * B * m.hidden);
+  w.x1t = off; off = align256(off + tw * B * m.hidden);
+  w.qkvt = off; off = align256(off + tw * B * qkv_rows);
+  w.attnt = off; off = align256(off + tw * B * q_dim);
+  w.at = off; off = align256(off + tw * B * m.intermediate);
   w.part_o = off; off = align256(off + sizeof(float) * B * m.n_q_heads * w.max_splits * m.head_dim);
   w.part_ml = off; off = align256(off + sizeof(float2) * B * m.n_q_heads * w.max_splits);
   w.total = off;
@@ -1389,16 +1505,24 @@ static int launch(const Params& P0, const lmps_model_desc& m, cudaStream_t st) {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   P.act_bytes = act_bytes_for(m, NB);
+  // rows of the hidden and q|k|v outputs one CTA owns (residual / bias kept in shared memory)
+  const int qkv_rows = (m.n_q_heads + 2 * m.n_kv_heads) * m.head_dim;
+  // (pair-aligned partitions: at most 2 * ceil(rows / 2 / sms) rows per CTA)
+  auto per_cta = [&](int rows) { return 2 * ((rows / 2 + sms - 1) / sms); };
+  if (per_cta(m.hidden) > kOwnMax || per_cta(qkv_rows) > kOwnMax || per_cta(m.intermediate) > kOutMax ||
+      m.n_layers > kMaxLayers || sms > kMaxGrid || m.vocab > 0x40000 || 2 * kConsumers < sms * kMaxB)
+    return LMPS_ERR_UNSUPPORTED;
   auto kern = decode_persistent_kernel<NB>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                                        cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) return static_cast<int>(e);
   // As many ring slots as fit next to one resident CTA per SM.
-  int slots = (max_smem - P.act_bytes - kTailBytes) / kSlotBytes;
+  const int tail = tail_bytes(m.n_layers);
+  int slots = (max_smem - P.act_bytes - tail) / kSlotBytes;
   if (slots > 16) slots = 16;
   size_t smem = 0;
   for (; slots >= 3; --slots) {
-    smem = static_cast<size_t>(slots) * kSlotBytes + P.act_bytes + kTailBytes;
+    smem = static_cast<size_t>(slots) * kSlotBytes + P.act_bytes + tail;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return static_cast<int>(e);
     int per_sm = 0;
@@ -1457,16 +1581,16 @@ extern "C" int lmps_decode_persistent(const lmps_model_desc* model, const lmps_d
   P.s = s;
   P.n_steps = n_steps;
   char* ws = reinterpret_cast<char*>(s.workspace);
-  P.x = reinterpret_cast<__half*>(ws + w.x);
-  P.x1 = reinterpret_cast<__half*>(ws + w.x1);
-  P.qkv = reinterpret_cast<__half*>(ws + w.qkv);
-  P.attn = reinterpret_cast<__half*>(ws + w.attn);
-  P.a = reinterpret_cast<__half*>(ws + w.a);
+  P.xt = reinterpret_cast<unsigned long long*>(ws + w.xt);
+  P.x1t = reinterpret_cast<unsigned long long*>(ws + w.x1t);
+  P.qkvt = reinterpret_cast<unsigned long long*>(ws + w.qkvt);
+  P.attnt = reinterpret_cast<unsigned long long*>(ws + w.attnt);
+  P.at = reinterpret_cast<unsigned long long*>(ws + w.at);
+  P.kslot = reinterpret_cast<unsigned long long*>(ws + w.kslot);
   P.part_o = reinterpret_cast<float*>(ws + w.part_o);
   P.part_ml = reinterpret_cast<float2*>(ws + w.part_ml);
   P.att_cnt = reinterpret_cast<uint32_t*>(ws + w.att_cnt);
-  P.keys = reinterpret_cast<unsigned long long*>(ws + w.keys);
-  P.arrive = reinterpret_cast<uint32_t*>(ws + w.arrive);
+  P.epoch = reinterpret_cast<uint32_t*>(ws + w.epoch);
   P.max_splits = w.max_splits;
   cudaStream_t st = lmps_stream(stream);
   switch (s.batch) {

@@ -1,13 +1,14 @@
 """Stage timeline of the persistent decode kernel.
 
 ``capture(engine, steps)`` runs ``steps`` decode steps in one traced launch
-(``lmps_decode_state.trace``: a %globaltimer stamp per CTA at the start and
-end of every stage, the producer's first/last chunk issue per stage and the
-consumers' cumulative wait for weights) and reduces it to per-stage-kind
-numbers: the hand-off latency (last CTA's end of the previous stage to the
-first CTA's start), the stage span, the median per-CTA compute time, the
-median time spent waiting for the weight ring, and how far ahead of the
-consumers the producer finished issuing.
+(``lmps_decode_state.trace``: a %globaltimer stamp per CTA at the start of
+every stage, once its input is staged in shared memory, and at its end; the
+producer's first/last chunk issue per stage and the consumers' cumulative
+wait for weights) and reduces it to per-stage-kind numbers: the hand-off
+latency (last CTA's end of the previous stage to the first CTA's start), the
+stage span, the median per-CTA compute time and its staging part, the median
+time spent waiting for the weight ring, and how far ahead of the consumers the
+producer finished issuing.
 """
 from __future__ import annotations
 
@@ -26,7 +27,7 @@ def capture(engine, steps: int = 4) -> Dict:
     L = engine.layers
     sms = torch.cuda.get_device_properties(engine.device).multi_processor_count
     n_stage = L * len(KINDS) + 1
-    events = steps * n_stage * 2 + 8
+    events = steps * n_stage * 3 + 8
     trace = torch.zeros(3 * sms, events, dtype=torch.int64, device=engine.device)
     B = engine.batch
     engine.pdec.run(B, engine.tokens, engine.pos, steps, trace=trace)
@@ -41,26 +42,28 @@ def capture(engine, steps: int = 4) -> Dict:
     agg: Dict[str, Dict[str, list]] = {}
     prev_end = None
     for i, n in enumerate(names):
-        e = (step * n_stage + i) * 2
-        st, en = cons[:, e], cons[:, e + 1]
+        e = (step * n_stage + i) * 3
+        st, sg, en = cons[:, e], cons[:, e + 1], cons[:, e + 2]
         kind = n.split(".")[-1]
-        a = agg.setdefault(kind, {"handoff_us": [], "span_us": [], "cta_us": [], "ring_wait_us": []})
+        a = agg.setdefault(kind, {"handoff_us": [], "span_us": [], "cta_us": [], "staging_us": [],
+                                  "ring_wait_us": []})
         if prev_end is not None:
             a["handoff_us"].append((st.min() - prev_end) / 1e3)
         a["span_us"].append((en.max() - st.min()) / 1e3)
         a["cta_us"].append(float(np.median((en - st) / 1e3)))
-        a["ring_wait_us"].append(float(np.median((wait[:, e + 1] - wait[:, e]) / 1e3)))
+        a["staging_us"].append(float(np.median((sg - st) / 1e3)))
+        a["ring_wait_us"].append(float(np.median((wait[:, e + 2] - wait[:, e]) / 1e3)))
         prev_end = en.max()
     for i, n in enumerate(pnames):
         e = (step * len(pnames) + i) * 2
         kind = n.split(".")[-1]
         ci = names.index(n)
-        ce = (step * n_stage + ci) * 2
+        ce = (step * n_stage + ci) * 3
         lead = np.median((cons[:, ce] - prod[:, e + 1]) / 1e3)
         agg[kind].setdefault("producer_lead_us", []).append(float(lead))
     step_us = []
     for s in range(steps):
-        e0, e1 = (s * n_stage) * 2, (s * n_stage + n_stage - 1) * 2 + 1
+        e0, e1 = (s * n_stage) * 3, (s * n_stage + n_stage - 1) * 3 + 2
         step_us.append(float((cons[:, e1].max() - cons[:, e0].min()) / 1e3))
     out = {"steps": steps, "step_span_us": step_us, "stages": {}}
     for k, a in agg.items():
