@@ -51,17 +51,14 @@ constexpr int kSlotBytes = 20160;
 constexpr int kRows1536 = 2 * kConsumerWarps;  // rows per ring chunk when k = hidden
 constexpr int kPairsGU = kConsumerWarps;    // gate/up row pairs per chunk
 constexpr int kRowsDown = 4;      // rows per chunk when k = intermediate
-constexpr int kAttnTile = 64;
 constexpr int kHD = 128;
 constexpr int kMaxG = 8;
-constexpr int kKStride = kHD + 8;
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
 constexpr int kMaxB = 4;
 constexpr int kOwnMax = 32;  // hidden / qkv rows one CTA owns
-constexpr int kOutMax = 128; // gate/up output rows one CTA owns
+constexpr int kOutMax = 128; // gate/up output rows one CTA computes
 constexpr int kMaxGrid = 256;
 constexpr int kMaxLayers = 64;
-constexpr int kRedFloats = 2 * kConsumerWarps * kRowsDown * kMaxB;  // down-projection partials, double-buffered
 
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
@@ -92,13 +89,16 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Potentially blocking probe: the thread is suspended (it issues nothing)
+// until the phase completes or about kSuspendNs pass.
+constexpr uint32_t kSuspendNs = 20000;
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
       " selp.u32 %0, 1, 0, p;\n}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
@@ -152,14 +152,12 @@ struct Smem {
   unsigned char* act;
   uint64_t* full;
   uint64_t* empty;
-  float* red;        // [2][warps][4 rows][kMaxB] down-projection partials
   float* red8;       // [warps * kMaxB] block-reduction scratch
   unsigned long long* best;  // [warps][kMaxB]
   int* misc;         // [0] abort
   float* inv_freq;   // [head_dim/2] RoPE frequencies, staged once per launch
   __half* xown;      // [kMaxB][kOwnMax] residual x of the hidden rows this CTA owns
   __half* x1own;     // [kMaxB][kOwnMax] residual after attention, same rows
-  __half* outb;      // [kMaxB][kOutMax] stage output rows before they are published
   __half* bias_own;  // [n_layers][kOwnMax] q|k|v bias of the qkv rows this CTA owns
 };
 
@@ -323,6 +321,10 @@ __device__ __forceinline__ bool has_tag(unsigned long long w, uint32_t tag) {
 // and re-polls if needed (bounded: on timeout the CTA's abort flag is raised
 // and zeros are returned).  Issuing several groups before finishing any keeps
 // their loads in flight together.
+// Pause between re-polls of words that are not ready yet: every CTA polls
+// the same few KB of a stage output, so unthrottled polling crowds the L2
+// slices holding them.
+constexpr unsigned kPollBackoffNs = 0;
 struct Tagged4 {
   unsigned long long w[4];
 };
@@ -342,6 +344,7 @@ __device__ __noinline__ uint4 tagged4_spin(int32_t* error, volatile int* abort_f
   const uint64_t t0 = globaltimer();
   Tagged4 t;
   while (true) {
+    if (kPollBackoffNs) __nanosleep(kPollBackoffNs);
     tagged4_issue(p, t);
     if (tagged4_ok(t, tag)) return tagged4_payload(t);
     if (*abort_flag || globaltimer() - t0 > kTimeoutNs) break;
@@ -377,21 +380,6 @@ __device__ __forceinline__ uint32_t poll1(const Params& P, Smem& S, const unsign
   return static_cast<uint32_t>(w);
 }
 
-// Publish output rows [r0, r1) (an even range) of the NB sequences from
-// shared memory (src[b * sld + i] = row r0 + i) as tagged pairs.
-template <int NB>
-__device__ void publish(const Params& P, const __half* src, int sld, unsigned long long* dst, int dld, int r0,
-                        int r1, uint32_t tag) {
-  consumer_sync();
-  const int np = (r1 - r0) / 2;
-  for (int i = threadIdx.x; i < NB * np; i += kConsumers) {
-    const int b = i / np, pr = i - b * np;
-    if (b < P.s.batch) {
-      const uint32_t pay = *reinterpret_cast<const uint32_t*>(src + b * sld + 2 * pr);
-      st_tagged(dst + static_cast<size_t>(b) * dld + r0 / 2 + pr, tagged(tag, pay));
-    }
-  }
-}
 
 // Wait for the next ring chunk.  Control flow stays uniform across the
 // consumers: a thread that gives up (timeout, or the CTA already aborting)
@@ -614,27 +602,23 @@ __device__ void stage_copy(const Params& P, Smem& S, const unsigned long long* s
   consumer_sync();
 }
 
-__device__ __forceinline__ void dp4a_us(int& acc, uint32_t a, uint32_t b) {
-  asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(a), "r"(b));
-}
-__device__ __forceinline__ void dp4a_uu(uint32_t& acc, uint32_t a, uint32_t b) {
-  asm("dp4a.u32.u32 %0, %1, %2, %0;" : "+r"(acc) : "r"(a), "r"(b));
-}
-
-// Exact sum_k (n_k - 8) X_k of one group: wv = 16 packed bytes, x = plane words.
+// Exact sum_k (n_k - 8) X_k of one group: wv = 16 packed bytes, x = plane
+// words.  The nibble bytes (0..15) are non-negative, so the signed dp4a is
+// exact for the signed H plane and the unsigned one for the L plane; four
+// independent accumulators keep the dependent chains short.
 __device__ __forceinline__ int group_idot(const uint4& wv, const uint32_t (&x)[16], int xs8) {
-  int sh = 0;
-  uint32_t sl = 0u;
   const uint32_t ws[4] = {wv.x, wv.y, wv.z, wv.w};
+  int he = 0, ho = 0;
+  unsigned le = 0u, lo = 0u;
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     const uint32_t ne = ws[c] & 0x0F0F0F0Fu, no = (ws[c] >> 4) & 0x0F0F0F0Fu;
-    dp4a_us(sh, ne, x[c]);
-    dp4a_us(sh, no, x[4 + c]);
-    dp4a_uu(sl, ne, x[8 + c]);
-    dp4a_uu(sl, no, x[12 + c]);
+    he = __dp4a(static_cast<int>(ne), static_cast<int>(x[c]), he);
+    ho = __dp4a(static_cast<int>(no), static_cast<int>(x[4 + c]), ho);
+    le = __dp4a(ne, x[8 + c], le);
+    lo = __dp4a(no, x[12 + c], lo);
   }
-  return sh * 256 + static_cast<int>(sl) - xs8;
+  return (he + ho) * 256 + static_cast<int>(le + lo) - xs8;
 }
 
 struct XGroup {
@@ -687,6 +671,26 @@ __device__ __forceinline__ void group_fma(const Planes& pl, int gi, const uint4&
 // ---------------------------------------------------------------------------
 // GEMV stages over ring chunks
 // ---------------------------------------------------------------------------
+// A chunk only computes: every lane stores its partial dot products in shared
+// memory and the chunk's slot is released; the reductions and epilogues of
+// all rows run once per stage, spread over the block, fused with publishing
+// the tagged output.  (Per-chunk shuffle trees and single-lane epilogues were
+// a serial tail after every chunk.)
+constexpr int kPartRows = 2 * kOutMax;  // row entries of a stage (gate/up: a gate and an up entry per row)
+
+// Partial-sum area after the activation planes of a k = hidden stage:
+// [NB][kPartRows][16 lanes] floats.
+__device__ __forceinline__ float* partials_view(const Planes& pl, int nb) {
+  return reinterpret_cast<float*>(pl.xs8 + nb * pl.G);
+}
+
+__device__ __forceinline__ float sum16(const float* p) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  const float4 c = *reinterpret_cast<const float4*>(p + 8), d = *reinterpret_cast<const float4*>(p + 12);
+  return ((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w)) + ((c.x + c.y) + (c.z + c.w)) +
+         ((d.x + d.y) + (d.z + d.w));
+}
+
 // Row GEMVs with k = hidden: q|k|v (+bias), o (+residual), gate/up (SwiGLU) and
 // the LM head (argmax).  A chunk holds <= 2*warps rows (gate/up: <= warps row
 // pairs); warp w takes rows 2w (lanes 0-15) and 2w+1 (lanes 16-31) -- for
@@ -698,11 +702,12 @@ __device__ void gemv_rows(const Params& P, Smem& S, CState& cs, int kind, int la
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = c.k / 32, JG = G / 16;
   const int half = lane >> 4, sub = lane & 15;
-  const bool gu = kind == ST_GU;
+  const bool gu = kind == ST_GU, head = kind == ST_HEAD;
   const int lrow = gu ? warp : 2 * warp + half;  // row of the chunk this half-warp computes
   const int rpc = c.rows_per_chunk;
   const size_t rb = c.k / 2;
   const Planes pl = planes_view(S, G, NB);
+  float* part = partials_view(pl, NB);
   unsigned long long best[NB];
 #pragma unroll
   for (int b = 0; b < NB; ++b) best[b] = 0ull;
@@ -727,30 +732,21 @@ __device__ void gemv_rows(const Params& P, Smem& S, CState& cs, int kind, int la
           group_fma<NB>(pl, g, wv, __half2float(srow[g]), acc);
         }
       }
+      if (!head) {
+        const int e = gu ? 2 * (r - c.r0 + warp) + half : r - c.r0 + lrow;
+#pragma unroll
+        for (int b = 0; b < NB; ++b) part[(b * kPartRows + e) * 16 + sub] = acc[b];
+      }
     }
     slot_release(S, P, cs);
+    if (head) {  // LM head: argmax keys only, kept per lane-0 of each row
 #pragma unroll
-    for (int b = 0; b < NB; ++b) acc[b] = segment_sum<16>(acc[b]);
-    if (gu) {
+      for (int b = 0; b < NB; ++b) acc[b] = segment_sum<16>(acc[b]);
+      if (sub == 0 && lrow < n) {
+        const int row = r + lrow;
 #pragma unroll
-      for (int b = 0; b < NB; ++b) {
-        const float u = __shfl_sync(0xffffffffu, acc[b], 16);
-        if (lane == 0 && warp < n && b < P.s.batch) {
-          const float gf = __half2float(__float2half_rn(acc[b]));
-          const float uf = __half2float(__float2half_rn(u));
-          S.outb[b * kOutMax + r + warp - c.r0] = __float2half_rn(silu_mul(gf, uf));
-        }
-      }
-    } else if (sub == 0 && lrow < n) {
-      const int row = r + lrow, i = row - c.r0;
-#pragma unroll
-      for (int b = 0; b < NB; ++b) {
-        if (b >= P.s.batch) break;
-        if (kind == ST_QKV) {
-          S.outb[b * kOutMax + i] = __float2half_rn(acc[b] + __half2float(S.bias_own[layer * kOwnMax + i]));
-        } else if (kind == ST_O) {
-          S.x1own[b * kOwnMax + i] = __hadd(S.xown[b * kOwnMax + i], __float2half_rn(acc[b]));
-        } else {  // ST_HEAD
+        for (int b = 0; b < NB; ++b) {
+          if (b >= P.s.batch) break;
           const __half v = __float2half_rn(acc[b]);
           if (logits) logits[static_cast<size_t>(b) * P.m.vocab + row] = v;
           best[b] = u64_max(best[b], argmax_key(__half2float(v), static_cast<uint32_t>(row)));
@@ -758,25 +754,52 @@ __device__ void gemv_rows(const Params& P, Smem& S, CState& cs, int kind, int la
       }
     }
   }
-  if (kind == ST_HEAD) {
+  if (head) {
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
       const unsigned long long w = warp_max_u64(best[b]);
       if (lane == 0) S.best[warp * kMaxB + b] = w;
     }
-  } else if (kind == ST_O) {
-    publish<NB>(P, S.x1own, kOwnMax, P.x1t, P.m.hidden / 2, c.r0, c.r1, tag);
-  } else if (kind == ST_QKV) {
-    publish<NB>(P, S.outb, kOutMax, P.qkvt, (P.m.n_q_heads + 2 * P.m.n_kv_heads) * kHD / 2, c.r0, c.r1, tag);
-  } else {
-    publish<NB>(P, S.outb, kOutMax, P.at, P.m.intermediate / 2, c.r0, c.r1, tag);
+    return;
   }
+  // -- epilogue of every row pair, published as tagged words
+  consumer_sync();
+  const int np = (c.r1 - c.r0) / 2;
+  unsigned long long* dst = kind == ST_QKV ? P.qkvt : kind == ST_O ? P.x1t : P.at;
+  const int dld = kind == ST_QKV ? (P.m.n_q_heads + 2 * P.m.n_kv_heads) * kHD / 2
+                                 : (kind == ST_O ? P.m.hidden : P.m.intermediate) / 2;
+  for (int t = threadIdx.x; t < NB * np; t += kConsumers) {
+    const int b = t / np, p = t - b * np;
+    if (b < P.s.batch) {
+      __half h[2];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int i = 2 * p + q;  // row - c.r0
+        if (kind == ST_GU) {
+          const float g = sum16(part + (b * kPartRows + 2 * i) * 16);
+          const float u = sum16(part + (b * kPartRows + 2 * i + 1) * 16);
+          h[q] = __float2half_rn(silu_mul(__half2float(__float2half_rn(g)), __half2float(__float2half_rn(u))));
+        } else {
+          const float v = sum16(part + (b * kPartRows + i) * 16);
+          if (kind == ST_QKV) {
+            h[q] = __float2half_rn(v + __half2float(S.bias_own[layer * kOwnMax + i]));
+          } else {  // ST_O
+            h[q] = __hadd(S.xown[b * kOwnMax + i], __float2half_rn(v));
+            S.x1own[b * kOwnMax + i] = h[q];
+          }
+        }
+      }
+      const __half2 v2 = __halves2half2(h[0], h[1]);
+      st_tagged(dst + static_cast<size_t>(b) * dld + c.r0 / 2 + p, tagged(tag, *reinterpret_cast<const uint32_t*>(&v2)));
+    }
+  }
+  consumer_sync();  // the partials' area is the next stage's staging area
 }
 
 // Down projection (k = intermediate): chunks of <= 4 rows; warp w sums groups
 // [G*w/warps, G*(w+1)/warps) of every row (lane = row*8 + sub, groups
-// g0+sub+8j), partials meet in shared memory and one thread per (row,
-// sequence) finishes: x = x1 + fp16(acc).
+// g0+sub+8j); each warp leaves one partial per (row, sequence) in shared
+// memory and the block finishes all rows at the end: x = x1 + fp16(sum).
 template <int NB>
 __device__ void gemv_down(const Params& P, Smem& S, CState& cs, int layer, uint32_t tag) {
   const Chunking c = stage_chunks(P, ST_DN, layer);
@@ -784,11 +807,10 @@ __device__ void gemv_down(const Params& P, Smem& S, CState& cs, int layer, uint3
   const int G = c.k / 32;
   const int g0 = G * warp / kConsumerWarps, g1 = G * (warp + 1) / kConsumerWarps;
   const int lrow = lane >> 3, sub = lane & 7;
-  const int hidden = P.m.hidden;
   const int rpc = c.rows_per_chunk;
   const Planes pl = planes_view(S, G, NB);
-  int par = 0;
-  for (int r = c.r0; r < c.r1; r += rpc, par ^= 1) {
+  float* red = partials_view(pl, NB);  // [NB][kOwnMax rows][warps]
+  for (int r = c.r0; r < c.r1; r += rpc) {
     const int n = min(rpc, c.r1 - r);
     const int slot = cs.slot;
     slot_wait(S, P, cs);
@@ -806,66 +828,92 @@ __device__ void gemv_down(const Params& P, Smem& S, CState& cs, int layer, uint3
       }
     }
     slot_release(S, P, cs);
-    float* red = S.red + par * (kConsumerWarps * kRowsDown * kMaxB);
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
       const float v = segment_sum<8>(acc[b]);
-      if (sub == 0) red[(warp * kRowsDown + lrow) * kMaxB + b] = v;
-    }
-    consumer_sync();
-    if (threadIdx.x < n * NB) {
-      const int lr = threadIdx.x / NB, b = threadIdx.x % NB;
-      if (b < P.s.batch) {
-        float t = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) t += red[(w * kRowsDown + lr) * kMaxB + b];
-        const int row = r + lr, i = row - c.r0;
-        S.xown[b * kOwnMax + i] = __hadd(S.x1own[b * kOwnMax + i], __float2half_rn(t));
-      }
+      if (sub == 0 && lrow < n) red[(b * kOwnMax + r - c.r0 + lrow) * kConsumerWarps + warp] = v;
     }
   }
-  publish<NB>(P, S.xown, kOwnMax, P.xt, hidden / 2, c.r0, c.r1, tag);
+  consumer_sync();
+  const int np = (c.r1 - c.r0) / 2;
+  for (int t = threadIdx.x; t < NB * np; t += kConsumers) {
+    const int b = t / np, p = t - b * np;
+    if (b < P.s.batch) {
+      __half h[2];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int i = 2 * p + q;
+        const float* rr = red + (b * kOwnMax + i) * kConsumerWarps;
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) s += rr[w];
+        h[q] = __hadd(S.x1own[b * kOwnMax + i], __float2half_rn(s));
+        S.xown[b * kOwnMax + i] = h[q];
+      }
+      const __half2 v2 = __halves2half2(h[0], h[1]);
+      st_tagged(P.xt + static_cast<size_t>(b) * (P.m.hidden / 2) + c.r0 / 2 + p,
+                tagged(tag, *reinterpret_cast<const uint32_t*>(&v2)));
+    }
+  }
+  consumer_sync();  // the partials' area is the next stage's staging area
 }
 
 // ---------------------------------------------------------------------------
 // Attention stage: one work item = (sequence b, kv head, split of positions)
 // ---------------------------------------------------------------------------
-// Decode-attention tiles go through the tensor cores with mma.sync m16n8k16
-// (fp16 in, fp32 accumulate): the G query heads of a KV head are the M rows
-// (padded to 16), positions are N for the scores and K for P.V.  At decode
-// these tiles are tiny and latency-bound; the MMAs replace 128-long dependent
-// FMA chains per (position, head).
-struct AttnSmemP {
-  __half qh[16][kKStride];            // rotated q (fp16); rows >= G are zero
-  __half knew[kHD];                   // this step's rotated k / raw v (position pos)
-  __half vnew[kHD];
-  __half k[kAttnTile][kKStride];
-  __half v[kAttnTile][kKStride];
-  float p[kMaxG][kAttnTile];          // scores
-  __half ph[16][kAttnTile + 8];       // exp(scores - max) in fp16; rows >= G are zero
-  float m[kMaxG];
-  float l[kMaxG];
-  float alpha[kMaxG];
-  float2 rot[kHD / 2];                // (cos, sin) of pos * inv_freq[j]
-  __half raw[(kMaxG + 2) * kHD];      // this step's q heads, k, v rows before RoPE
+// Flash-decoding inside the CTA: every warp takes 16-position blocks of the
+// split and keeps its own online softmax (softmax.metal:23-36); the warps'
+// (max, sum, output) meet in shared memory at the end.  Per block, on the
+// tensor cores (mma.sync m16n8k16, fp16 in, fp32 accumulate):
+//   S^T  = K Q^T   (M = 16 positions, N = 8 heads, K = 128 dims)   attention.metal:32-40
+//   O^T += V^T P^T (M = 16 dims per m-tile, N = 8 heads, K = 16 positions)   attn_sum.metal:26-32
+// Both products sum over dims or positions, so the order of the dims inside
+// them is free: logical dim (k-step ks, fragment column 2t+e, upper half +8)
+// is physical dim 32t + 4ks + e (+2), and output row r of m-tile mt is
+// physical dim 32(r>>1 & 3) + 4mt + 2(r>>3) + (r&1).  Every lane's K and V
+// operands are then one contiguous 64-byte run of a cache row (four 16-byte
+// loads), and movmatrix transposes V rows and probabilities in registers.
+constexpr int kBlk = 16;        // positions per warp block
+constexpr int kMinSplit = 512;  // positions per work item before the positions split across CTAs
+
+struct AttnSmem {
+  __half raw[(kMaxG + 2) * kHD];          // polled q heads, k, v (before RoPE)
+  float2 rot[kHD / 2];                    // (cos, sin) of pos * inv_freq[j]
+  __half q[kMaxG][kHD];                   // rotated q, natural dim order
+  float wm[kConsumerWarps][kMaxG];        // per-warp running max and sum (then merge weights)
+  float wl[kConsumerWarps][kMaxG];
+  float wo[kConsumerWarps][32][32];       // per-warp unnormalised O^T fragments, [lane][value, rotated by 4*lane]
   int is_last;
 };
 
-__device__ __forceinline__ void ldsm_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                        uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(smem_u32(p)));
+// KV cache rows are written (and prefetched) with an L2 evict_last policy so
+// that they stay in L2 while the weight stream passes through evict_first.
+__device__ __forceinline__ uint64_t evict_last_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
 }
-__device__ __forceinline__ void ldsm_x2(const void* p, uint32_t& r0, uint32_t& r1) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
-               : "=r"(r0), "=r"(r1)
-               : "r"(smem_u32(p)));
+__device__ __forceinline__ void st_kv(__half* p, __half v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.b16 [%0], %1, %2;" ::"l"(p), "h"(__half_as_ushort(v)), "l"(pol) : "memory");
 }
-__device__ __forceinline__ void ldsm_x2_trans(const void* p, uint32_t& r0, uint32_t& r1) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
-               : "=r"(r0), "=r"(r1)
-               : "r"(smem_u32(p)));
+__device__ __forceinline__ void st_kv8(__half* p, const uint4& v, uint64_t pol) {  // 8 values, 16-byte aligned
+  asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1,%2,%3,%4}, %5;" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w), "l"(pol)
+               : "memory");
+}
+
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  return d;
+}
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t word_of(const uint4 (&v)[4], int w) {
+  const uint4 q = v[w >> 2];
+  return (w & 3) == 0 ? q.x : (w & 3) == 1 ? q.y : (w & 3) == 2 ? q.z : q.w;
 }
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                           uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -888,236 +936,276 @@ __device__ __forceinline__ void rope_pair(int j, int style, int& i1, int& i2) {
 
 __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, int b, int kvh,
                           int split, int n_splits, int chunk, int pos, uint32_t in_tag, uint32_t out_tag) {
-  AttnSmemP& A = *reinterpret_cast<AttnSmemP*>(S.act);
+  AttnSmem& A = *reinterpret_cast<AttnSmem*>(S.act);
   const lmps_model_desc& m = P.m;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g8 = lane >> 2, t4 = lane & 3;
   const int Hq = m.n_q_heads, Hkv = m.n_kv_heads, G = Hq / Hkv;
   const int qkv_rows = (Hq + 2 * Hkv) * kHD;
   const int T = pos + 1;
   const int start = split * chunk, end = min(T, start + chunk);
   const unsigned long long* row = P.qkvt + static_cast<size_t>(b) * (qkv_rows / 2);
   unsigned long long* out = P.attnt + static_cast<size_t>(b) * (Hq * kHD / 2);
-  const float fpos = static_cast<float>(pos);
   const int ps = P.s.page_size;
   const int32_t* bt = P.s.block_table + static_cast<size_t>(b) * P.s.max_pages;
   __half* kpool = reinterpret_cast<__half*>(L.k_pool);
   __half* vpool = reinterpret_cast<__half*>(L.v_pool);
-
-  // K/V rows of one 64-position tile, loaded straight into registers so the
-  // loads of the first tile overlap the q/k/v loads and RoPE below.  The new
-  // position `pos` is not read from the cache: it comes from A.knew/A.vnew.
-  constexpr int kTileVec = kAttnTile * (kHD / 8);                       // 16-byte chunks per tile
-  constexpr int kLd = (kTileVec + kConsumers - 1) / kConsumers;
-  uint4 kreg[kLd], vreg[kLd];
-  auto load_tile = [&](int t0) {
-    const int n = min(kAttnTile, end - t0);
-#pragma unroll
-    for (int it = 0; it < kLd; ++it) {
-      const int i = tid + it * kConsumers;
-      const int r = i / (kHD / 8), c = i - r * (kHD / 8);
-      kreg[it] = make_uint4(0u, 0u, 0u, 0u);
-      vreg[it] = make_uint4(0u, 0u, 0u, 0u);
-      const int p = t0 + r;
-      if (i < kTileVec && r < n && p != pos) {
-        const size_t off = ((static_cast<size_t>(bt[p / ps]) * Hkv + kvh) * ps + p % ps) * kHD + c * 8;
-        kreg[it] = __ldcg(reinterpret_cast<const uint4*>(kpool + off));
-        vreg[it] = __ldcg(reinterpret_cast<const uint4*>(vpool + off));
-      }
-    }
-  };
-  auto store_tile = [&](int t0) {
-#pragma unroll
-    for (int it = 0; it < kLd; ++it) {
-      const int i = tid + it * kConsumers;
-      if (i < kTileVec) {
-        const int r = i / (kHD / 8), c = i - r * (kHD / 8);
-        uint4 kv = kreg[it], vv = vreg[it];
-        if (t0 + r == pos) {
-          kv = *reinterpret_cast<const uint4*>(&A.knew[c * 8]);
-          vv = *reinterpret_cast<const uint4*>(&A.vnew[c * 8]);
-        }
-        *reinterpret_cast<uint4*>(&A.k[r][c * 8]) = kv;
-        *reinterpret_cast<uint4*>(&A.v[r][c * 8]) = vv;
-      }
-    }
-  };
-  // Every global load of the prologue is issued before any of them is used:
-  // the first K/V tile, then this group's q rows and (the split holding the
-  // new position) the k and v rows, polled from the tagged q|k|v output.
-  if (start < end) load_tile(start);
   const bool has_pos = pos >= start && pos < end;
+  const uint64_t kvpol = evict_last_policy();
+
+  // Cache rows of positions < pos do not depend on this step's q|k|v: the
+  // first block of every warp is prefetched into L2 before anything waits.
+  const int nblk = (end - start + kBlk - 1) / kBlk;
+  auto row_off = [&](int p) {
+    return ((static_cast<size_t>(__ldg(bt + p / ps)) * Hkv + kvh) * ps + p % ps) * kHD + 32 * t4;
+  };
+  if (warp < nblk) {
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const int p = start + warp * kBlk + 8 * h2 + g8;
+      if (p < end && p != pos) {
+        const size_t off = row_off(p);
+        asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(kpool + off));
+        asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(vpool + off));
+      }
+    }
+  }
+  // cache offset of position pos (the KV append of the split holding it)
+  const size_t app = has_pos ? ((static_cast<size_t>(__ldg(bt + pos / ps)) * Hkv + kvh) * ps + pos % ps) * kHD : 0;
+  // q rows of this KV head's G query heads and (the split holding the new
+  // position) its k and v rows, polled from the tagged q|k|v output as groups
+  // of 8 dims.  With adjacent RoPE pairs (rope.metal:19-40) a group holds
+  // whole pairs: the polling thread rotates it in registers, with its four
+  // angles computed while it waits.
+  const bool adj = m.rope_style == LMPS_ROPE_INTERLEAVED;
   {
-    const int nq4 = G * (kHD / 8), n4 = nq4 + (has_pos ? 2 * (kHD / 8) : 0);  // 4-word groups
+    const int nq4 = G * (kHD / 8), n4 = nq4 + (has_pos ? 2 * (kHD / 8) : 0);
     if (tid < n4) {
-      const int seg = tid < nq4 ? kvh * G + tid / (kHD / 8)                          // q head
-                                : (tid - nq4 < kHD / 8 ? Hq + kvh : Hq + Hkv + kvh);  // k / v row
-      const unsigned long long* src = row + seg * (kHD / 2) + 4 * (tid % (kHD / 8));
+      const int c8 = tid % (kHD / 8);  // dims 8*c8 .. 8*c8+7
+      const int kind = tid < nq4 ? 0 : (tid - nq4 < kHD / 8 ? 1 : 2);  // q, k, v
+      const int seg = kind == 0 ? kvh * G + tid / (kHD / 8) : kind == 1 ? Hq + kvh : Hq + Hkv + kvh;
+      const unsigned long long* src = row + seg * (kHD / 2) + 4 * c8;
       Tagged4 t;
       tagged4_issue(src, t);
-      *reinterpret_cast<uint4*>(&A.raw[8 * tid]) = tagged4_finish(P, S, src, in_tag, t);
+      float cs[4], sn[4];
+      if (adj && kind < 2) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sincosf(static_cast<float>(pos) * S.inv_freq[4 * c8 + e], &sn[e], &cs[e]);
+      }
+      uint4 v = tagged4_finish(P, S, src, in_tag, t);
+      if (adj && kind < 2) {
+        uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+          w[e] = pack_half2(f.x * cs[e] - f.y * sn[e], f.x * sn[e] + f.y * cs[e]);
+        }
+      }
+      if (!adj) {
+        *reinterpret_cast<uint4*>(&A.raw[8 * tid]) = v;
+      } else if (kind == 0) {
+        *reinterpret_cast<uint4*>(&A.q[tid / (kHD / 8)][8 * c8]) = v;
+      } else {
+        st_kv8((kind == 1 ? kpool : vpool) + app + 8 * c8, v, kvpol);
+      }
     }
   }
-  // RoPE angles of this position (rope.metal:19-40), one table for q and k.
-  if (tid < kHD / 2) {
+  if (!adj && tid < kHD / 2) {  // RoPE angles of this position, (j, j + head_dim/2) pairs
     float sn, cs;
-    sincosf(fpos * S.inv_freq[tid], &sn, &cs);
+    sincosf(static_cast<float>(pos) * S.inv_freq[tid], &sn, &cs);
     A.rot[tid] = make_float2(cs, sn);
   }
-  if (tid < kMaxG) {
-    A.m[tid] = -INFINITY;
-    A.l[tid] = 0.0f;
-  }
-  for (int i = tid; i < (16 - G) * kKStride; i += kConsumers)
-    A.qh[G + i / kKStride][i % kKStride] = __float2half_rn(0.0f);
-  for (int i = tid; i < (16 - G) * (kAttnTile + 8); i += kConsumers)
-    A.ph[G + i / (kAttnTile + 8)][i % (kAttnTile + 8)] = __float2half_rn(0.0f);
   consumer_sync();
-  // RoPE'd q of the G heads sharing this KV head, fp16-rounded.
-  for (int i = tid; i < G * (kHD / 2); i += kConsumers) {
-    const int h = i / (kHD / 2), j = i - h * (kHD / 2);
-    int i1, i2;
-    rope_pair(j, m.rope_style, i1, i2);
-    const float2 r = A.rot[j];
-    const float qa = __half2float(A.raw[h * kHD + i1]), qb = __half2float(A.raw[h * kHD + i2]);
-    A.qh[h][i1] = __float2half_rn(qa * r.x - qb * r.y);
-    A.qh[h][i2] = __float2half_rn(qa * r.y + qb * r.x);
-  }
-  // The split holding the new position appends its rotated k and raw v.
-  if (has_pos) {
-    const int page = bt[pos / ps], off = pos % ps;
-    const size_t base = ((static_cast<size_t>(page) * Hkv + kvh) * ps + off) * kHD;
-    const __half* kraw = A.raw + G * kHD;
-    if (tid < kHD / 2) {
+  if (!adj) {
+    for (int i = tid; i < G * (kHD / 2); i += kConsumers) {  // RoPE'd q, fp16-rounded
+      const int h = i / (kHD / 2), j = i - h * (kHD / 2);
       int i1, i2;
-      rope_pair(tid, m.rope_style, i1, i2);
-      const float2 r = A.rot[tid];
-      const float ka = __half2float(kraw[i1]), kb = __half2float(kraw[i2]);
-      const __half k1 = __float2half_rn(ka * r.x - kb * r.y), k2 = __float2half_rn(ka * r.y + kb * r.x);
-      kpool[base + i1] = k1;
-      kpool[base + i2] = k2;
-      A.knew[i1] = k1;
-      A.knew[i2] = k2;
-    } else if (tid < kHD / 2 + kHD) {
-      const int d = tid - kHD / 2;
-      const __half v = kraw[kHD + d];
-      vpool[base + d] = v;
-      A.vnew[d] = v;
+      rope_pair(j, m.rope_style, i1, i2);
+      const float2 r = A.rot[j];
+      const float qa = __half2float(A.raw[h * kHD + i1]), qb = __half2float(A.raw[h * kHD + i2]);
+      A.q[h][i1] = __float2half_rn(qa * r.x - qb * r.y);
+      A.q[h][i2] = __float2half_rn(qa * r.y + qb * r.x);
     }
-  }
-  const int warp = tid >> 5, lane = tid & 31;
-  const int g8 = lane >> 2, t4 = lane & 3;           // mma fragment row / column pair
-  const int mi = lane >> 3, r8 = lane & 7;           // ldmatrix lane -> matrix, row
-  constexpr int kNT = kHD / 8;                       // P.V output n-tiles (8 dims each)
-  constexpr int kNTW = (kNT + kConsumerWarps - 1) / kConsumerWarps;
-  float o[kNTW][4];
-#pragma unroll
-  for (int j = 0; j < kNTW; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
-  consumer_sync();
-
-  for (int t0 = start; t0 < end; t0 += kAttnTile) {
-    const int n = min(kAttnTile, end - t0);
-    if (t0 != start) load_tile(t0);
-    store_tile(t0);
-    consumer_sync();
-    // scores S = Q K^T * 0.088388 (attention.metal:32-40): warp w < 8 owns
-    // positions 8w..8w+7, eight k-steps over the 128 dims.
-    if (warp < kAttnTile / 8) {
-      float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-      for (int ks = 0; ks < kHD / 16; ++ks) {
-        uint32_t a0, a1, a2, a3, b0, b1;
-        ldsm_x4(&A.qh[(mi & 1) * 8 + r8][16 * ks + (mi >> 1) * 8], a0, a1, a2, a3);
-        ldsm_x2(&A.k[8 * warp + r8][16 * ks + (mi & 1) * 8], b0, b1);
-        mma_16816(d, a0, a1, a2, a3, b0, b1);
-      }
-      if (g8 < G) {
-        const int p0 = 8 * warp + 2 * t4;
-        A.p[g8][p0] = (p0 < n) ? d[0] * kAttnScale : -INFINITY;
-        A.p[g8][p0 + 1] = (p0 + 1 < n) ? d[1] * kAttnScale : -INFINITY;
-      }
-    }
-    consumer_sync();
-    {  // online softmax, one warp per head (softmax.metal:23-36)
-      const int warp = tid >> 5, lane = tid & 31;
-      if (warp < G) {
-        const int h = warp;
-        const float s0 = A.p[h][lane], s1 = A.p[h][lane + 32];
-        const float m_old = A.m[h];
-        const float m_new = fmaxf(m_old, warp_max(fmaxf(s0, s1)));
-        float e0 = 0.0f, e1 = 0.0f, alpha = 1.0f;
-        if (m_new != -INFINITY) {
-          e0 = expf(s0 - m_new);
-          e1 = expf(s1 - m_new);
-          alpha = expf(m_old - m_new);
-        }
-        const float sum = warp_sum(e0 + e1);
-        A.ph[h][lane] = __float2half_rn(e0);
-        A.ph[h][lane + 32] = __float2half_rn(e1);
-        __syncwarp();
-        if (lane == 0) {
-          A.alpha[h] = alpha;
-          A.m[h] = m_new;
-          A.l[h] = A.l[h] * alpha + sum;
-        }
-      }
-    }
-    consumer_sync();
-    // O += P V (attn_sum.metal:26-32): warp w owns output dims 8nt..8nt+7 for
-    // nt = w, w + warps; the running sums are rescaled by this tile's alpha.
-    {
-      const float al0 = (g8 < G) ? A.alpha[g8] : 1.0f;
-#pragma unroll
-      for (int j = 0; j < kNTW; ++j) {
-        o[j][0] *= al0;
-        o[j][1] *= al0;
-      }
-#pragma unroll
-      for (int ks = 0; ks < kAttnTile / 16; ++ks) {
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4(&A.ph[(mi & 1) * 8 + r8][16 * ks + (mi >> 1) * 8], a0, a1, a2, a3);
-#pragma unroll
-        for (int j = 0; j < kNTW; ++j) {
-          const int nt = warp + kConsumerWarps * j;
-          if (nt < kNT) {
-            uint32_t b0, b1;
-            ldsm_x2_trans(&A.v[16 * ks + (mi & 1) * 8 + r8][8 * nt], b0, b1);
-            mma_16816(o[j], a0, a1, a2, a3, b0, b1);
-          }
-        }
+    if (has_pos) {  // KV append: rotated k and raw v at position pos
+      const __half* kraw = A.raw + G * kHD;
+      if (tid < kHD / 2) {
+        int i1, i2;
+        rope_pair(tid, m.rope_style, i1, i2);
+        const float2 r = A.rot[tid];
+        const float ka = __half2float(kraw[i1]), kb = __half2float(kraw[i2]);
+        st_kv(kpool + app + i1, __float2half_rn(ka * r.x - kb * r.y), kvpol);
+        st_kv(kpool + app + i2, __float2half_rn(ka * r.y + kb * r.x), kvpol);
+      } else if (tid < kHD / 2 + kHD) {
+        st_kv(vpool + app + tid - kHD / 2, kraw[kHD + tid - kHD / 2], kvpol);
       }
     }
     consumer_sync();
   }
+  // rotated q in shared memory, the new k/v row in the cache
 
-  if (n_splits == 1) {
-    if (g8 < G) {
-      const float l = A.l[g8];
-      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+  // -- per-warp flash loop over 16-position blocks
+  uint32_t qf[16];  // B operand Q^T: head g8, physical dims 32*t4 .. 32*t4+31
+  {
+    const uint4* qs = reinterpret_cast<const uint4*>(&A.q[g8 < G ? g8 : 0][32 * t4]);
 #pragma unroll
-      for (int j = 0; j < kNTW; ++j) {
-        const int nt = warp + kConsumerWarps * j;
-        if (nt < kNT) {
-          const __half2 v = __halves2half2(__float2half_rn(o[j][0] * inv), __float2half_rn(o[j][1] * inv));
-          st_tagged(out + (kvh * G + g8) * (kHD / 2) + 4 * nt + t4,
-                    tagged(out_tag, *reinterpret_cast<const uint32_t*>(&v)));
+    for (int c = 0; c < 4; ++c) {
+      const uint4 v = g8 < G ? qs[c] : make_uint4(0u, 0u, 0u, 0u);
+      qf[4 * c] = v.x;
+      qf[4 * c + 1] = v.y;
+      qf[4 * c + 2] = v.z;
+      qf[4 * c + 3] = v.w;
+    }
+  }
+  float o[8][4];
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.0f;
+  float mrun0 = -INFINITY, mrun1 = -INFINITY, lrun0 = 0.0f, lrun1 = 0.0f;  // heads 2*t4, 2*t4+1
+  for (int bi = warp; bi < nblk; bi += kConsumerWarps) {
+    const int p0 = start + bi * kBlk;
+    // Cache rows p0+g8 and p0+8+g8, dims 32*t4 .. 32*t4+31 (the row of pos was
+    // appended by this CTA before the last block sync).
+    uint4 kr[2][4], vr[2][4];
+    size_t off[2];
+    bool ok[2];
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const int p = p0 + 8 * h2 + g8;
+      ok[h2] = p < end;
+      off[h2] = ok[h2] ? row_off(p) : 0;
+    }
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        kr[h2][c] = ok[h2] ? __ldcg(reinterpret_cast<const uint4*>(kpool + off[h2]) + c) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        vr[h2][c] = ok[h2] ? __ldcg(reinterpret_cast<const uint4*>(vpool + off[h2]) + c) : make_uint4(0u, 0u, 0u, 0u);
+    // S^T = K Q^T
+    float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int ks = 0; ks < kHD / 16; ++ks)
+      mma_16816(s, word_of(kr[0], 2 * ks), word_of(kr[1], 2 * ks), word_of(kr[0], 2 * ks + 1),
+                word_of(kr[1], 2 * ks + 1), qf[2 * ks], qf[2 * ks + 1]);
+    const bool v0 = p0 + g8 < end, v1 = p0 + 8 + g8 < end;
+    s[0] = v0 ? s[0] * kAttnScale : -INFINITY;
+    s[1] = v0 ? s[1] * kAttnScale : -INFINITY;
+    s[2] = v1 ? s[2] * kAttnScale : -INFINITY;
+    s[3] = v1 ? s[3] * kAttnScale : -INFINITY;
+    // online softmax per head (columns 2*t4, 2*t4+1; positions over g8 and the two row halves)
+    float mx0 = fmaxf(s[0], s[2]), mx1 = fmaxf(s[1], s[3]);
+#pragma unroll
+    for (int ofs = 4; ofs < 32; ofs <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, ofs));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, ofs));
+    }
+    const float mn0 = fmaxf(mrun0, mx0), mn1 = fmaxf(mrun1, mx1);  // finite: position p0 is valid
+    const float al0 = expf(mrun0 - mn0), al1 = expf(mrun1 - mn1);
+    const float e0 = expf(s[0] - mn0), e1 = expf(s[1] - mn1), e2 = expf(s[2] - mn0), e3 = expf(s[3] - mn1);
+    float su0 = e0 + e2, su1 = e1 + e3;
+#pragma unroll
+    for (int ofs = 4; ofs < 32; ofs <<= 1) {
+      su0 += __shfl_xor_sync(0xffffffffu, su0, ofs);
+      su1 += __shfl_xor_sync(0xffffffffu, su1, ofs);
+    }
+    lrun0 = lrun0 * al0 + su0;
+    lrun1 = lrun1 * al1 + su1;
+    mrun0 = mn0;
+    mrun1 = mn1;
+    // O^T = O^T * alpha + V^T P^T
+    const uint32_t pb0 = movmatrix_t(pack_half2(e0, e1)), pb1 = movmatrix_t(pack_half2(e2, e3));
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      o[mt][0] *= al0;
+      o[mt][2] *= al0;
+      o[mt][1] *= al1;
+      o[mt][3] *= al1;
+      mma_16816(o[mt], movmatrix_t(word_of(vr[0], 2 * mt)), movmatrix_t(word_of(vr[0], 2 * mt + 1)),
+                movmatrix_t(word_of(vr[1], 2 * mt)), movmatrix_t(word_of(vr[1], 2 * mt + 1)), pb0, pb1);
+    }
+  }
+  const int nw = min(kConsumerWarps, nblk);  // warps that saw positions
+  const size_t ms = P.max_splits;
+  if (nw == 1 && n_splits == 1) {
+    // one warp saw every position: normalise and publish from registers.
+    // Lanes g8 and g8^1 hold dims d and d+1; they swap one value so that
+    // the even lane owns the (d, d+1) pair of head 2*t4, the odd lane that
+    // of head 2*t4+1.
+    if (warp == 0) {
+      const bool odd = g8 & 1;
+      const int h = 2 * t4 + (odd ? 1 : 0);
+      const float inv = odd ? (lrun1 > 0.0f ? 1.0f / lrun1 : 0.0f) : (lrun0 > 0.0f ? 1.0f / lrun0 : 0.0f);
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const float mine = odd ? o[mt][2 * hh + 1] : o[mt][2 * hh];
+          const float other = __shfl_xor_sync(0xffffffffu, odd ? o[mt][2 * hh] : o[mt][2 * hh + 1], 4);
+          const int d = 32 * (g8 >> 1) + 4 * mt + 2 * hh;  // even dim of the pair
+          if (h < G)
+            st_tagged(out + (kvh * G + h) * (kHD / 2) + d / 2,
+                      tagged(out_tag, odd ? pack_half2(other * inv, mine * inv) : pack_half2(mine * inv, other * inv)));
         }
       }
     }
-    consumer_sync();
+    consumer_sync();  // the shared area is the next stage's staging area
     return;
   }
-  const size_t ms = P.max_splits;
-  if (g8 < G) {
-    const size_t prow = (static_cast<size_t>(b) * Hq + kvh * G + g8) * ms + split;
+  // -- warps meet in shared memory: merged maxima first, then every warp
+  // rescales its sums to them, then the block adds the warps up
+  if (warp < nw && g8 == 0) {
+    A.wm[warp][2 * t4] = mrun0;
+    A.wm[warp][2 * t4 + 1] = mrun1;
+  }
+  consumer_sync();
+  if (warp < nw) {
+    float M0 = -INFINITY, M1 = -INFINITY;
+    for (int ww = 0; ww < nw; ++ww) {
+      M0 = fmaxf(M0, A.wm[ww][2 * t4]);
+      M1 = fmaxf(M1, A.wm[ww][2 * t4 + 1]);
+    }
+    const float f0 = expf(mrun0 - M0), f1 = expf(mrun1 - M1);
+    if (g8 == 0) {
+      A.wl[warp][2 * t4] = lrun0 * f0;
+      A.wl[warp][2 * t4 + 1] = lrun1 * f1;
+    }
 #pragma unroll
-    for (int j = 0; j < kNTW; ++j) {
-      const int nt = warp + kConsumerWarps * j;
-      if (nt < kNT) *reinterpret_cast<float2*>(&P.part_o[prow * kHD + 8 * nt + 2 * t4]) = make_float2(o[j][0], o[j][1]);
+    for (int mt = 0; mt < 8; ++mt)  // 16-byte stores, value k of this lane at (k + 4 lane) mod 32
+      *reinterpret_cast<float4*>(&A.wo[warp][lane][(4 * mt + 4 * lane) & 31]) =
+          make_float4(o[mt][0] * f0, o[mt][1] * f1, o[mt][2] * f0, o[mt][3] * f1);
+  }
+  consumer_sync();
+  for (int w = tid; w < G * (kHD / 2); w += kConsumers) {
+    const int h = w / (kHD / 2), dp = w - h * (kHD / 2);
+    // dims 2dp, 2dp+1 of head h: fragment value 4mt + 2hh + (h & 1) of lanes
+    // (g8, t4) = (2 (d >> 5) + e, h >> 1), d = 2dp = 32 (g8 >> 1) + 4 mt + 2 hh
+    const int d = 2 * dp, k = 4 * ((d & 31) >> 2) + 2 * (((d & 31) >> 1) & 1) + (h & 1);
+    const int la = 4 * (2 * (d >> 5)) + (h >> 1);
+    const int ka = (k + 4 * la) & 31, kb = (k + 4 * (la + 4)) & 31;
+    float n0 = 0.0f, n1 = 0.0f, den = 0.0f;
+    for (int ww = 0; ww < nw; ++ww) {
+      n0 += A.wo[ww][la][ka];
+      n1 += A.wo[ww][la + 4][kb];
+      den += A.wl[ww][h];
+    }
+    if (n_splits == 1) {
+      const float inv = den > 0.0f ? 1.0f / den : 0.0f;
+      st_tagged(out + (kvh * G + h) * (kHD / 2) + dp, tagged(out_tag, pack_half2(n0 * inv, n1 * inv)));
+    } else {
+      const size_t prow = (static_cast<size_t>(b) * Hq + kvh * G + h) * ms + split;
+      *reinterpret_cast<float2*>(&P.part_o[prow * kHD + 2 * dp]) = make_float2(n0, n1);
+      if (dp == 0) {
+        float M = -INFINITY;
+        for (int ww = 0; ww < nw; ++ww) M = fmaxf(M, A.wm[ww][h]);
+        P.part_ml[prow] = make_float2(M, den);
+      }
     }
   }
-  if (tid < G) {
-    const size_t prow = (static_cast<size_t>(b) * Hq + kvh * G + tid) * ms + split;
-    P.part_ml[prow] = make_float2(A.m[tid], A.l[tid]);
+  if (n_splits == 1) {
+    consumer_sync();  // the shared area is the next stage's staging area
+    return;
   }
   __threadfence();
   consumer_sync();
@@ -1152,22 +1240,22 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
           den = fmaf(wgt, ml.y, den);
         }
       }
-      const __half2 v = den > 0.0f ? __halves2half2(__float2half_rn(n0 / den), __float2half_rn(n1 / den))
-                                   : __halves2half2(__float2half_rn(0.0f), __float2half_rn(0.0f));
-      st_tagged(out + (kvh * G + h) * (kHD / 2) + dp, tagged(out_tag, *reinterpret_cast<const uint32_t*>(&v)));
+      const float inv = den > 0.0f ? 1.0f / den : 0.0f;
+      st_tagged(out + (kvh * G + h) * (kHD / 2) + dp, tagged(out_tag, pack_half2(n0 * inv, n1 * inv)));
     }
   }
   consumer_sync();
 }
 
-// Positions per attention split this step (all CTAs compute the same value):
-// at least one 64-position tile, and about two work items per CTA overall.
+// Positions per attention work item this step (all CTAs compute the same
+// value): a whole sequence up to kMinSplit positions (one CTA, no cross-CTA
+// merge), longer contexts split so that the items about fill the grid.
 __device__ __forceinline__ int attn_chunk_len(const int* pos, int batch, int n_kv) {
   long long total = 0;
   for (int b = 0; b < batch; ++b) total += pos[b] + 1;
-  long long c = (total * n_kv + 2 * gridDim.x - 1) / (2 * gridDim.x);
-  c = (c + kAttnTile - 1) / kAttnTile * kAttnTile;
-  return static_cast<int>(c < kAttnTile ? kAttnTile : c);
+  long long c = (total * n_kv + gridDim.x - 1) / gridDim.x;
+  c = (c + kBlk - 1) / kBlk * kBlk;
+  return static_cast<int>(c < kMinSplit ? kMinSplit : c);
 }
 
 // The next token of every sequence from the tagged per-CTA argmax slots of a
@@ -1394,15 +1482,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
   unsigned char* tail = S.act + P.act_bytes;
   S.full = reinterpret_cast<uint64_t*>(tail);
   S.empty = S.full + 16;
-  S.red = reinterpret_cast<float*>(S.empty + 16);
-  S.red8 = S.red + kRedFloats;
+  S.red8 = reinterpret_cast<float*>(S.empty + 16);
   S.best = reinterpret_cast<unsigned long long*>(S.red8 + kConsumerWarps * kMaxB);
   S.misc = reinterpret_cast<int*>(S.best + kConsumerWarps * kMaxB);
   S.inv_freq = reinterpret_cast<float*>(S.misc + 16);
   S.xown = reinterpret_cast<__half*>(S.inv_freq + kHD / 2);
   S.x1own = S.xown + kMaxB * kOwnMax;
-  S.outb = S.x1own + kMaxB * kOwnMax;
-  S.bias_own = S.outb + kMaxB * kOutMax;
+  S.bias_own = S.x1own + kMaxB * kOwnMax;
   // tag base of this launch (CTA 0 advances it after every CTA has used it)
   const uint32_t epoch = __ldcg(P.epoch);
   for (int i = threadIdx.x; i < kHD / 2; i += blockDim.x) S.inv_freq[i] = P.m.inv_freq[i];
@@ -1452,9 +1538,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
 
 // Shared-memory tail after the ring and the activation area.
 static int tail_bytes(int n_layers) {
-  const size_t fixed = 32 * sizeof(uint64_t) + kRedFloats * sizeof(float) +
+  const size_t fixed = 32 * sizeof(uint64_t) +
                        kConsumerWarps * kMaxB * (sizeof(float) + sizeof(unsigned long long)) + 16 * sizeof(int) +
-                       kHD / 2 * sizeof(float) + (2 * kOwnMax + kOutMax) * kMaxB * sizeof(__half);
+                       kHD / 2 * sizeof(float) + 2 * kOwnMax * kMaxB * sizeof(__half);
   const size_t t = fixed + static_cast<size_t>(n_layers) * kOwnMax * sizeof(__half);
   return static_cast<int>((t + 127) & ~static_cast<size_t>(127));
 }
@@ -1471,7 +1557,7 @@ static WsLayout ws_layout(const lmps_model_desc& m, int B, int max_seq_len) {
   const size_t qkv_rows = static_cast<size_t>(m.n_q_heads + 2 * m.n_kv_heads) * m.head_dim;
   const size_t q_dim = static_cast<size_t>(m.n_q_heads) * m.head_dim;
   const size_t tw = sizeof(unsigned long long) / 2;  // tagged bytes per element
-  w.max_splits = (max_seq_len + kAttnTile - 1) / kAttnTile;
+  w.max_splits = (max_seq_len + kMinSplit - 1) / kMinSplit;
   size_t off = 0;
   // State that persists from one launch to the next comes first, at offsets
   // that do not depend on the batch size of the launch.
@@ -1490,10 +1576,15 @@ static WsLayout ws_layout(const lmps_model_desc& m, int B, int max_seq_len) {
 }
 
 static int act_bytes_for(const lmps_model_desc& m, int nb) {
-  size_t a = sizeof(AttnSmemP);
-  const int kmax = m.intermediate > m.hidden ? m.intermediate : m.hidden;
-  const size_t planes = static_cast<size_t>(nb) * (kmax / 32) * (16 * 4 + 4 + 4);  // words + scl + xs8
-  if (planes > a) a = planes;
+  size_t a = sizeof(AttnSmem);
+  const size_t grp = 16 * 4 + 4 + 4;  // plane words + scl + xs8 per group
+  // k = hidden stages: planes + per-lane partials of every row entry
+  const size_t hid = static_cast<size_t>(nb) * (m.hidden / 32) * grp + static_cast<size_t>(nb) * kPartRows * 16 * 4;
+  // down projection: planes + one partial per (row, warp)
+  const size_t dn = static_cast<size_t>(nb) * (m.intermediate / 32) * grp +
+                    static_cast<size_t>(nb) * kOwnMax * kConsumerWarps * 4;
+  a = a > hid ? a : hid;
+  a = a > dn ? a : dn;
   return static_cast<int>((a + 127) & ~static_cast<size_t>(127));
 }
 
