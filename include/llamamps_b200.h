@@ -172,6 +172,23 @@ int lmps_gqa_decode_attention_noalloc(const uint16_t* q, const uint16_t* k_pool,
                                       int page_size, int n_q_heads, int n_kv_heads, int head_dim,
                                       int batch, int max_seq_len, int n_splits, void* stream);
 
+/* ---- prefill / large-batch projections ------------------------------------ */
+
+/* W4A16 GEMM on the tcgen05 tensor cores (TMEM accumulators), for prefill and
+ * large-batch decode where the Q4 projections of quant_matmul.metal:15-69 are
+ * dense contractions: y[m, :n] = x[m, :k] . W^T with W the Q4 [n, k] layout of
+ * lmps_gemv_q4_0 (dequantised to fp16 tile by tile), fp32 accumulate, fp16 out.
+ * epilogue: 0 none, 1 + bias[n], 2 residual[m, n] + fp16(acc) (residual may
+ * alias y).  n must be a multiple of 128 and k of 64 (else UNSUPPORTED); any
+ * m >= 1.  error[0] is set to 1 if a bounded wait for the tensor core gives up.
+ * Replaces the per-token dispatch of runners/engine.py:188-243 at B > 1. */
+#define LMPS_EPI_NONE 0
+#define LMPS_EPI_BIAS 1
+#define LMPS_EPI_RESIDUAL 2
+int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed, const uint16_t* scales,
+                    const uint16_t* bias, const uint16_t* residual, int ldr, uint16_t* y, int ldy,
+                    int m, int n, int k, int epilogue, int32_t* error, void* stream);
+
 /* ---- weight format ---------------------------------------------------- */
 
 /* Device Q4 packer, bit-exact with utils/pack_weights.py:42-60

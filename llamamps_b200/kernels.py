@@ -194,3 +194,31 @@ def decode_advance(next_ids, tokens, pos, seq_lens, history=None, step=None):
          _dev(pos, "pos", torch.int32), _dev(seq_lens, "seq_lens", torch.int32),
          _dev(history, "history", torch.int32) if history is not None else None,
          _dev(step, "step", torch.int32) if step is not None else None, max_steps, B, _stream())
+
+
+EPI_NONE, EPI_BIAS, EPI_RESIDUAL = 0, 1, 2
+
+
+def w4a16_gemm(x, packed, scales, n: int, k: int, *, bias=None, residual=None, out=None,
+               error: Optional[torch.Tensor] = None):
+    """tcgen05 W4A16 GEMM: out[m] = x[m] . W^T (+ bias | residual + fp16(.)).
+
+    x is fp16 [m, k] (token-major); W the Q4 [n, k] layout.  Used where the
+    projections of many tokens at once are dense contractions (prefill, large
+    batches)."""
+    x2, m = _x2d(x)
+    y = out if out is not None else torch.empty(m, n, dtype=FP16, device=x.device)
+    epi, b_ptr, r_ptr, ldr = EPI_NONE, None, None, 0
+    if bias is not None:
+        epi, b_ptr = EPI_BIAS, _dev(bias, "bias", FP16)
+    if residual is not None:
+        if bias is not None:
+            raise ValueError("bias and residual epilogues are exclusive")
+        r2 = residual if residual.dim() == 2 else residual.reshape(1, -1)
+        epi, r_ptr, ldr = EPI_RESIDUAL, _dev(r2, "residual", FP16), r2.shape[1]
+    err = error if error is not None else torch.zeros(1, dtype=torch.int32, device=x.device)
+    call("lmps_w4a16_gemm", _dev(x2, "x", FP16), x2.shape[1], _dev(packed, "packed", torch.uint8),
+         _dev(scales, "scales", FP16), b_ptr, r_ptr, ldr, _dev(y, "y", FP16), y.shape[-1], m, n, k, epi,
+         _dev(err, "error", torch.int32), _stream())
+    return y
+
