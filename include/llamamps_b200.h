@@ -189,6 +189,10 @@ int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed, const uin
                     const uint16_t* bias, const uint16_t* residual, int ldr, uint16_t* y, int ldy,
                     int m, int n, int k, int epilogue, int32_t* error, void* stream);
 
+/* First-index argmax of each row of fp16 logits [rows, ld] over n columns
+ * (runners/engine.py:180-181), the large-batch companion of the LM-head GEMM. */
+int lmps_argmax_rows(const uint16_t* logits, int ld, int rows, int n, int32_t* ids, void* stream);
+
 /* ---- weight format ---------------------------------------------------- */
 
 /* Device Q4 packer, bit-exact with utils/pack_weights.py:42-60

@@ -251,6 +251,24 @@ __global__ void decode_advance_kernel(const int32_t* next, int32_t* tokens, int3
   if (threadIdx.x == 0 && history && step) step[0] = s + 1;
 }
 
+// Row-wise first-index argmax of fp16 logits (runners/engine.py:180-181:
+// numpy.argmax over fp32(logits)); one block per row.
+__global__ void argmax_rows_kernel(const __half* logits, int ld, int n, int32_t* ids) {
+  const __half* row = logits + static_cast<size_t>(blockIdx.x) * ld;
+  unsigned long long best = 0ull;
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    best = u64_max(best, argmax_key(__half2float(row[i]), static_cast<uint32_t>(i)));
+  best = warp_max_u64(best);
+  __shared__ unsigned long long red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) best = u64_max(best, red[w]);
+    best = u64_max(best, red[0]);
+    ids[blockIdx.x] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(best & 0xFFFFFFFFull));
+  }
+}
+
 }  // namespace lmps
 
 using namespace lmps;
@@ -372,5 +390,11 @@ extern "C" int lmps_decode_advance(const int32_t* next, int32_t* tokens, int32_t
   LMPS_CHECK_ARG(!history || (step && max_steps > 0));
   decode_advance_kernel<<<1, 256, 0, lmps_stream(stream)>>>(next, tokens, pos, seq_lens, history,
                                                             step, max_steps, batch);
+  return lmps_launch_status();
+}
+
+extern "C" int lmps_argmax_rows(const uint16_t* logits, int ld, int rows, int n, int32_t* ids, void* stream) {
+  LMPS_CHECK_ARG(logits && ids && rows > 0 && n > 0 && ld >= n);
+  argmax_rows_kernel<<<rows, 512, 0, lmps_stream(stream)>>>(CH(logits), ld, n, ids);
   return lmps_launch_status();
 }

@@ -38,6 +38,10 @@ from .kv_cache import PagedKVCache
 from .weights import ModelWeights, load_reference_layout
 
 
+GEMV_MAX_BATCH = 8  # the CUDA-core GEMV serves up to 8 sequences; larger batches use the tensor-core GEMM
+DENSE_PREFILL_TOKENS = 256  # prompts with at least this many tokens in total prefill on the GEMM path
+
+
 def rope_inv_freq(head_dim: int, theta: float) -> np.ndarray:
     """base^-(2i/head_dim) in fp32 (kernels/rope.metal:28-30 with idx % 128 = 2i)."""
     i2 = np.arange(0, head_dim, 2, dtype=np.float32)
@@ -98,6 +102,9 @@ class QwenEngine:
         self.buf_q = torch.zeros(B, c.q_dim, dtype=h, device=dev)
         self.buf_attn = torch.zeros(B, c.q_dim, dtype=h, device=dev)
         self.buf_mlp = torch.zeros(B, c.intermediate, dtype=h, device=dev)
+        # gate/up outputs of the tensor-core GEMM path (batches past the GEMV's 8)
+        self.buf_up = torch.zeros(B if B > GEMV_MAX_BATCH else 1, c.intermediate, dtype=h, device=dev)
+        self.gemm_err = torch.zeros(1, dtype=torch.int32, device=dev)
         self.buf_logits = torch.zeros(B, c.vocab, dtype=h, device=dev)
         ws = K.attention_workspace_size(B, c.n_q_heads, c.head_dim, self.n_splits)
         self.attn_ws = torch.zeros(max(ws, 16), dtype=torch.uint8, device=dev)
@@ -135,11 +142,16 @@ class QwenEngine:
         c, w = self.cfg, self.weights
         x = self.buf_residual[:B]
         xn = self.buf_normed[:B]
+        gemm = B > GEMV_MAX_BATCH   # dense contraction: tcgen05 W4A16 GEMM
         for li, lw in enumerate(w.layers):
             kp, vp = self.cache.layer(li)
             K.rms_norm(x, lw.in_norm, c.eps, out=xn)
-            K.gemv_q4_bias(lw.qkv_packed, lw.qkv_scales, lw.qkv_bias, xn, c.qkv_rows, c.hidden,
-                           out=self.buf_qkv[:B])
+            if gemm:
+                K.w4a16_gemm(xn, lw.qkv_packed, lw.qkv_scales, c.qkv_rows, c.hidden, bias=lw.qkv_bias,
+                             out=self.buf_qkv[:B], error=self.gemm_err)
+            else:
+                K.gemv_q4_bias(lw.qkv_packed, lw.qkv_scales, lw.qkv_bias, xn, c.qkv_rows, c.hidden,
+                               out=self.buf_qkv[:B])
             K.rope_kv_append(self.buf_qkv[:B], self.pos, self.inv_freq, self.buf_q[:B], kp, vp,
                              self.cache.block_table, self.cache.page_size, c.n_q_heads,
                              c.n_kv_heads, c.head_dim, c.rope_style_code)
@@ -147,19 +159,36 @@ class QwenEngine:
                                    self.buf_attn[:B], self.attn_ws, self.cache.page_size,
                                    c.n_q_heads, c.n_kv_heads, c.head_dim, self.max_seq_len,
                                    self.n_splits)
-            K.gemv_q4_residual(lw.o_packed, lw.o_scales, self.buf_attn[:B], x, c.hidden, c.q_dim, out=x)
-            K.rms_norm(x, lw.post_norm, c.eps, out=xn)
-            K.gemv_q4_swiglu(lw.gate_packed, lw.gate_scales, lw.up_packed, lw.up_scales, xn,
-                             c.intermediate, c.hidden, out=self.buf_mlp[:B])
-            K.gemv_q4_residual(lw.down_packed, lw.down_scales, self.buf_mlp[:B], x, c.hidden,
-                               c.intermediate, out=x)
+            if gemm:
+                K.w4a16_gemm(self.buf_attn[:B], lw.o_packed, lw.o_scales, c.hidden, c.q_dim, residual=x,
+                             out=x, error=self.gemm_err)
+                K.rms_norm(x, lw.post_norm, c.eps, out=xn)
+                K.w4a16_gemm(xn, lw.gate_packed, lw.gate_scales, c.intermediate, c.hidden,
+                             out=self.buf_mlp[:B], error=self.gemm_err)
+                K.w4a16_gemm(xn, lw.up_packed, lw.up_scales, c.intermediate, c.hidden,
+                             out=self.buf_up[:B], error=self.gemm_err)
+                K.swiglu(self.buf_mlp[:B], self.buf_up[:B], out=self.buf_mlp[:B])
+                K.w4a16_gemm(self.buf_mlp[:B], lw.down_packed, lw.down_scales, c.hidden, c.intermediate,
+                             residual=x, out=x, error=self.gemm_err)
+            else:
+                K.gemv_q4_residual(lw.o_packed, lw.o_scales, self.buf_attn[:B], x, c.hidden, c.q_dim, out=x)
+                K.rms_norm(x, lw.post_norm, c.eps, out=xn)
+                K.gemv_q4_swiglu(lw.gate_packed, lw.gate_scales, lw.up_packed, lw.up_scales, xn,
+                                 c.intermediate, c.hidden, out=self.buf_mlp[:B])
+                K.gemv_q4_residual(lw.down_packed, lw.down_scales, self.buf_mlp[:B], x, c.hidden,
+                                   c.intermediate, out=x)
 
     def _head(self, B: int, want_logits: bool) -> None:
         c, w = self.cfg, self.weights
         K.rms_norm(self.buf_residual[:B], w.final_norm, c.eps, out=self.buf_normed[:B])
-        K.lm_head_argmax(w.lm_packed, w.lm_scales, self.buf_normed[:B], c.vocab, c.hidden,
-                         self.argmax_keys[:B], self.next_ids[:B],
-                         logits=self.buf_logits[:B] if want_logits else None)
+        if B > GEMV_MAX_BATCH:
+            K.w4a16_gemm(self.buf_normed[:B], w.lm_packed, w.lm_scales, c.vocab, c.hidden,
+                         out=self.buf_logits[:B], error=self.gemm_err)
+            K.argmax_rows(self.buf_logits[:B], c.vocab, self.next_ids[:B])
+        else:
+            K.lm_head_argmax(w.lm_packed, w.lm_scales, self.buf_normed[:B], c.vocab, c.hidden,
+                             self.argmax_keys[:B], self.next_ids[:B],
+                             logits=self.buf_logits[:B] if want_logits else None)
 
     def _device_step(self, B: int, want_logits: bool = False, record: bool = True) -> None:
         """Embed -> layers -> head -> advance; device-only, graph-capturable."""
@@ -292,13 +321,23 @@ class QwenEngine:
             self.history = torch.zeros(steps, self.max_batch, dtype=torch.int32, device=self.device)
             self._graphs.clear()  # graphs captured the old history pointer
 
-    def prefill(self, prompts: torch.Tensor) -> None:
-        """Feed prompt tokens [B, P] position by position (causal); afterwards
-        ``tokens`` holds each sequence's first generated token."""
+    def prefill(self, prompts: torch.Tensor, dense: Optional[bool] = None) -> None:
+        """Feed prompt tokens [B, P] (causal); afterwards ``tokens`` holds each
+        sequence's first generated token (also history row 0).
+
+        ``dense`` (default: B*P >= DENSE_PREFILL_TOKENS) runs every prompt
+        token of every sequence through each layer at once on the tensor-core
+        GEMM (:meth:`prefill_dense`); otherwise the tokens go through the
+        decode path one position at a time."""
         B, P = prompts.shape
         if P + 1 > self.max_seq_len:
             raise ValueError("prompt longer than the KV cache")
         prompts = prompts.to(self.device, torch.int32)
+        if dense is None:
+            dense = B * P >= DENSE_PREFILL_TOKENS
+        if dense:
+            self.prefill_dense(prompts)
+            return
         if self.pdec is not None:
             # tokens <- prompt[:, 0]; steps 0..P-2 feed prompt[:, 1:]; the last
             # step's argmax (the first generated token) lands in history row 0.
@@ -316,6 +355,60 @@ class QwenEngine:
             if t == P - 1:
                 self.step_counter.zero_()
             self.decode_step(record=True)
+
+    def prefill_dense(self, prompts: torch.Tensor) -> None:
+        """All B*P prompt tokens through every layer at once: the projections
+        are W4A16 tensor-core GEMMs over M = B*P token rows, RoPE and the KV
+        append run on every (sequence, position) row, and causal attention is
+        one decode-attention query per row against the positions up to its
+        own.  The LM head runs on each sequence's last row only."""
+        c, w, dev = self.cfg, self.weights, self.device
+        B, P = prompts.shape
+        if self.host_pos != 0:
+            raise RuntimeError("dense prefill starts fresh sequences (call reset first)")
+        Mt = B * P
+        h, i32 = torch.float16, torch.int32
+        ids = prompts.reshape(-1).contiguous()
+        rows_pos = torch.arange(P, dtype=i32, device=dev).repeat(B)
+        rows_len = rows_pos + 1
+        rows_bt = self.cache.block_table[:B].repeat_interleave(P, dim=0).contiguous()
+        x = torch.empty(Mt, c.hidden, dtype=h, device=dev)
+        xn = torch.empty_like(x)
+        qkv = torch.empty(Mt, c.qkv_rows, dtype=h, device=dev)
+        q = torch.empty(Mt, c.q_dim, dtype=h, device=dev)
+        att = torch.empty(Mt, c.q_dim, dtype=h, device=dev)
+        gate = torch.empty(Mt, c.intermediate, dtype=h, device=dev)
+        up = torch.empty_like(gate)
+        splits = K.attention_splits(Mt, c.n_kv_heads, P, self.cache.page_size)
+        ws = torch.zeros(max(K.attention_workspace_size(Mt, c.n_q_heads, c.head_dim, splits), 16),
+                         dtype=torch.uint8, device=dev)
+        err = self.gemm_err
+        K.embed_gather(w.embed, ids, x, self.bad_ids)
+        for li, lw in enumerate(w.layers):
+            kp, vp = self.cache.layer(li)
+            K.rms_norm(x, lw.in_norm, c.eps, out=xn)
+            K.w4a16_gemm(xn, lw.qkv_packed, lw.qkv_scales, c.qkv_rows, c.hidden, bias=lw.qkv_bias,
+                         out=qkv, error=err)
+            K.rope_kv_append(qkv, rows_pos, self.inv_freq, q, kp, vp, rows_bt, self.cache.page_size,
+                             c.n_q_heads, c.n_kv_heads, c.head_dim, c.rope_style_code)
+            K.gqa_decode_attention(q, kp, vp, rows_bt, rows_len, att, ws, self.cache.page_size,
+                                   c.n_q_heads, c.n_kv_heads, c.head_dim, P, splits)
+            K.w4a16_gemm(att, lw.o_packed, lw.o_scales, c.hidden, c.q_dim, residual=x, out=x, error=err)
+            K.rms_norm(x, lw.post_norm, c.eps, out=xn)
+            K.w4a16_gemm(xn, lw.gate_packed, lw.gate_scales, c.intermediate, c.hidden, out=gate, error=err)
+            K.w4a16_gemm(xn, lw.up_packed, lw.up_scales, c.intermediate, c.hidden, out=up, error=err)
+            K.swiglu(gate, up, out=gate)
+            K.w4a16_gemm(gate, lw.down_packed, lw.down_scales, c.hidden, c.intermediate, residual=x, out=x,
+                         error=err)
+        # last position of every sequence -> final norm, LM head, argmax
+        self.buf_residual[:B].copy_(x.view(B, P, c.hidden)[:, P - 1])
+        self._head(B, want_logits=False)
+        self.tokens[:B].copy_(self.next_ids[:B])
+        self.pos[:B].fill_(P)
+        self.seq_lens[:B].fill_(P + 1)
+        self.history[0, :B].copy_(self.next_ids[:B])
+        self.step_counter.fill_(1)
+        self.host_pos += P
 
     def generate_batch(self, prompts, max_new_tokens: int) -> np.ndarray:
         """Greedy decode of B equal-length prompts; returns int32 [B, max_new_tokens]."""

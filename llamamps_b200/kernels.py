@@ -222,3 +222,10 @@ def w4a16_gemm(x, packed, scales, n: int, k: int, *, bias=None, residual=None, o
          _dev(err, "error", torch.int32), _stream())
     return y
 
+
+def argmax_rows(logits, n: int, ids):
+    """First-index argmax of each fp16 row of logits[:, :n] into int32 ids."""
+    call("lmps_argmax_rows", _dev(logits, "logits", FP16), logits.shape[-1], logits.shape[0], n,
+         _dev(ids, "ids", torch.int32), _stream())
+    return ids
+
