@@ -181,13 +181,18 @@ int lmps_gqa_decode_attention_noalloc(const uint16_t* q, const uint16_t* k_pool,
  * epilogue: 0 none, 1 + bias[n], 2 residual[m, n] + fp16(acc) (residual may
  * alias y).  n must be a multiple of 128 and k of 64 (else UNSUPPORTED); any
  * m >= 1.  error[0] is set to 1 if a bounded wait for the tensor core gives up.
- * Replaces the per-token dispatch of runners/engine.py:188-243 at B > 1. */
+ * With a workspace of lmps_w4a16_gemm_workspace_size(m, n) bytes (256-byte
+ * aligned, zero-filled once; every call leaves it zero) small-m calls split K
+ * over more CTAs; NULL runs unsplit.  Replaces the per-token dispatch of
+ * runners/engine.py:188-243 at B > 1. */
 #define LMPS_EPI_NONE 0
 #define LMPS_EPI_BIAS 1
 #define LMPS_EPI_RESIDUAL 2
+size_t lmps_w4a16_gemm_workspace_size(int m, int n);
 int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed, const uint16_t* scales,
                     const uint16_t* bias, const uint16_t* residual, int ldr, uint16_t* y, int ldy,
-                    int m, int n, int k, int epilogue, int32_t* error, void* stream);
+                    int m, int n, int k, int epilogue, int32_t* error, void* workspace,
+                    size_t workspace_bytes, void* stream);
 
 /* First-index argmax of each row of fp16 logits [rows, ld] over n columns
  * (runners/engine.py:180-181), the large-batch companion of the LM-head GEMM. */

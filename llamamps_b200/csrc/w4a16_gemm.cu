@@ -49,6 +49,11 @@ struct Params {
   int ldy;
   int m, n, k, epi;
   int* error;
+  // split-K (gridDim.z > 1): fp32 partial tiles meet in acc32 [m_tiles*128, n]
+  // (zero between calls); the last CTA of a tile finishes it and re-zeroes it
+  float* acc32;
+  uint32_t* tile_cnt;  // [m_tiles * n_tiles], zero between calls
+  int ksteps_per_split;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -138,7 +143,9 @@ __global__ void __launch_bounds__(kThreads, 1) w4a16_gemm_kernel(const __grid_co
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
-  const int K = P.k, ksteps = K / kBK;
+  const int K = P.k;
+  const int kbeg = blockIdx.z * P.ksteps_per_split;
+  const int ksteps = min(P.ksteps_per_split, K / kBK - kbeg);
 
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i)
@@ -157,6 +164,26 @@ __global__ void __launch_bounds__(kThreads, 1) w4a16_gemm_kernel(const __grid_co
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
 
+  // Global loads run one K step ahead of the shared-memory stores: step
+  // kt+1's X rows and packed weights are in flight while step kt is staged
+  // and its MMAs are issued.
+  constexpr int kPer = (kBM * kBK / 8) / kThreads;  // 16-byte chunks per thread and operand
+  uint4 xr[kPer];
+  uint32_t wr[kPer];
+  __half sr[kPer];
+  auto load_step = [&](int kt) {
+    const int k0 = (kbeg + kt) * kBK;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int idx = tid + i * kThreads, r = idx >> 3, c = idx & 7;
+      xr[i] = (m0 + r < P.m) ? __ldg(reinterpret_cast<const uint4*>(P.x + static_cast<size_t>(m0 + r) * P.ldx + k0 + 8 * c))
+                             : make_uint4(0u, 0u, 0u, 0u);
+      const size_t row = static_cast<size_t>(n0 + r);
+      wr[i] = __ldg(reinterpret_cast<const uint32_t*>(P.w + row * (K / 2) + (k0 + 8 * c) / 2));
+      sr[i] = P.s[row * (K / 32) + (k0 + 8 * c) / 32];
+    }
+  };
+  if (ksteps > 0) load_step(0);
   for (int kt = 0; kt < ksteps; ++kt) {
     const int st = kt % kStages;
     if (kt >= kStages) {  // the MMAs that read this stage two steps ago are done
@@ -164,24 +191,15 @@ __global__ void __launch_bounds__(kThreads, 1) w4a16_gemm_kernel(const __grid_co
       __syncthreads();
       if (*abort_flag) break;
     }
-    const int k0 = kt * kBK;
     unsigned char* at = a_tiles + st * kTileBytes;
     unsigned char* bt = b_tiles + st * kTileBytes;
 #pragma unroll
-    for (int i = 0; i < (kBM * kBK / 8) / kThreads; ++i) {
+    for (int i = 0; i < kPer; ++i) {
       const int idx = tid + i * kThreads, r = idx >> 3, c = idx & 7;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (m0 + r < P.m) v = __ldg(reinterpret_cast<const uint4*>(P.x + static_cast<size_t>(m0 + r) * P.ldx + k0 + 8 * c));
-      *reinterpret_cast<uint4*>(at + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+      *reinterpret_cast<uint4*>(at + r * 128 + ((c ^ (r & 7)) << 4)) = xr[i];
+      *reinterpret_cast<uint4*>(bt + r * 128 + ((c ^ (r & 7)) << 4)) = dequant8(wr[i], sr[i]);
     }
-#pragma unroll
-    for (int i = 0; i < (kBN * kBK / 8) / kThreads; ++i) {
-      const int idx = tid + i * kThreads, r = idx >> 3, c = idx & 7;
-      const size_t row = static_cast<size_t>(n0 + r);
-      const uint32_t pk = __ldg(reinterpret_cast<const uint32_t*>(P.w + row * (K / 2) + (k0 + 8 * c) / 2));
-      const __half sc = P.s[row * (K / 32) + (k0 + 8 * c) / 32];
-      *reinterpret_cast<uint4*>(bt + r * 128 + ((c ^ (r & 7)) << 4)) = dequant8(pk, sc);
-    }
+    if (kt + 1 < ksteps) load_step(kt + 1);
     // generic-proxy shared-memory writes -> visible to the tensor core
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
@@ -201,7 +219,75 @@ __global__ void __launch_bounds__(kThreads, 1) w4a16_gemm_kernel(const __grid_co
   }
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  if (!*abort_flag) {
+  const bool split = gridDim.z > 1;
+  if (!*abort_flag && split) {
+    // fp32 partial tile -> acc32 (red.add); the last split of the tile finishes it
+    const int trow = m0 + warp * 32 + lane;
+#pragma unroll 1
+    for (int cc = 0; cc < kBN / 32; ++cc) {
+      uint32_t r[32];
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16) + cc * 32;
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+          "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+          : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+            "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+            "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+            "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+          : "r"(taddr)
+          : "memory");
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      if (trow < P.m) {
+        float* dst = P.acc32 + static_cast<size_t>(trow) * P.n + n0 + cc * 32;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          asm volatile("red.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(dst + j), "f"(__uint_as_float(r[j])),
+                       "f"(__uint_as_float(r[j + 1])), "f"(__uint_as_float(r[j + 2])), "f"(__uint_as_float(r[j + 3]))
+                       : "memory");
+      }
+    }
+    __threadfence();
+    __syncthreads();
+    uint32_t* cnt = P.tile_cnt + blockIdx.y * gridDim.x + blockIdx.x;
+    if (tid == 0) *abort_flag = (atomicAdd(cnt, 1u) == gridDim.z - 1) ? 2 : 0;
+    __syncthreads();
+    if (*abort_flag == 2) {  // last split of this tile: epilogue from acc32, then clear it
+      __threadfence();
+      for (int i = tid; i < kBM * (kBN / 8); i += kThreads) {
+        const int rr = i / (kBN / 8), c8 = i - rr * (kBN / 8);
+        const int row = m0 + rr;
+        if (row >= P.m) continue;
+        float* src = P.acc32 + static_cast<size_t>(row) * P.n + n0 + 8 * c8;
+        const float4 a = __ldcg(reinterpret_cast<const float4*>(src));
+        const float4 b = __ldcg(reinterpret_cast<const float4*>(src + 4));
+        const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        *reinterpret_cast<float4*>(src) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(src + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+        const int col = n0 + 8 * c8;
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          __half h0, h1;
+          if (P.epi == EPI_BIAS) {
+            h0 = __float2half_rn(v[2 * e] + __half2float(P.bias[col + 2 * e]));
+            h1 = __float2half_rn(v[2 * e + 1] + __half2float(P.bias[col + 2 * e + 1]));
+          } else if (P.epi == EPI_RESIDUAL) {
+            const __half* rr2 = P.res + static_cast<size_t>(row) * P.ldr + col + 2 * e;
+            h0 = __hadd(rr2[0], __float2half_rn(v[2 * e]));
+            h1 = __hadd(rr2[1], __float2half_rn(v[2 * e + 1]));
+          } else {
+            h0 = __float2half_rn(v[2 * e]);
+            h1 = __float2half_rn(v[2 * e + 1]);
+          }
+          const __half2 hh = __halves2half2(h0, h1);
+          o[e] = *reinterpret_cast<const uint32_t*>(&hh);
+        }
+        *reinterpret_cast<uint4*>(P.y + static_cast<size_t>(row) * P.ldy + col) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      if (tid == 0) *cnt = 0u;
+    }
+  }
+  if (!*abort_flag && !split) {
     const int row = m0 + warp * 32 + lane;  // token of this thread's TMEM lane
 #pragma unroll 1
     for (int cc = 0; cc < kBN / 32; ++cc) {
@@ -259,9 +345,24 @@ constexpr size_t kSmemBytes = 2 * kStages * kTileBytes + 1024 /* alignment */ + 
 
 using namespace lmps;
 
+extern "C" size_t lmps_w4a16_gemm_workspace_size(int m, int n) {
+  if (m <= 0 || n <= 0) return 0;
+  const size_t mt = (m + w4::kBM - 1) / w4::kBM, nt = (n + w4::kBN - 1) / w4::kBN;
+  return mt * w4::kBM * n * sizeof(float) + ((mt * nt * sizeof(uint32_t) + 255) & ~static_cast<size_t>(255));
+}
+
+// Splits of K for a grid of `tiles` output tiles: about two CTAs per SM, at
+// least two 64-wide K steps per split.
+static int choose_splits(int tiles, int ksteps, int sms) {
+  int s = (2 * sms) / (tiles > 0 ? tiles : 1);
+  if (s > ksteps / 2) s = ksteps / 2;
+  return s < 1 ? 1 : s;
+}
+
 extern "C" int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed, const uint16_t* scales,
                                const uint16_t* bias, const uint16_t* residual, int ldr, uint16_t* y, int ldy,
-                               int m, int n, int k, int epilogue, int32_t* error, void* stream) {
+                               int m, int n, int k, int epilogue, int32_t* error, void* workspace,
+                               size_t workspace_bytes, void* stream) {
   LMPS_CHECK_ARG(x && packed && scales && y && error);
   LMPS_CHECK_ARG(m >= 1 && n >= 1 && k >= 1);
   if (n % w4::kBN != 0 || k % w4::kBK != 0) return LMPS_ERR_UNSUPPORTED;
@@ -285,10 +386,26 @@ extern "C" int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed
   P.k = k;
   P.epi = epilogue;
   P.error = error;
+  const int ksteps = k / w4::kBK, mt = (m + w4::kBM - 1) / w4::kBM, nt = n / w4::kBN;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int splits = 1;
+  if (workspace && workspace_bytes >= lmps_w4a16_gemm_workspace_size(m, n)) {
+    LMPS_CHECK_ARG(lmps_aligned(workspace, 256));
+    splits = choose_splits(mt * nt, ksteps, sms);
+  }
+  P.ksteps_per_split = (ksteps + splits - 1) / splits;
+  splits = (ksteps + P.ksteps_per_split - 1) / P.ksteps_per_split;
+  if (splits > 1) {
+    P.acc32 = reinterpret_cast<float*>(workspace);
+    P.tile_cnt = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(workspace) +
+                                             static_cast<size_t>(mt) * w4::kBM * n * sizeof(float));
+  }
   cudaError_t e = cudaFuncSetAttribute(w4::w4a16_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(w4::kSmemBytes));
   if (e != cudaSuccess) return static_cast<int>(e);
-  dim3 grid(n / w4::kBN, (m + w4::kBM - 1) / w4::kBM);
+  dim3 grid(nt, mt, splits);
   w4::w4a16_gemm_kernel<<<grid, w4::kThreads, w4::kSmemBytes, lmps_stream(stream)>>>(P);
   return lmps_launch_status();
 }

@@ -105,6 +105,11 @@ class QwenEngine:
         # gate/up outputs of the tensor-core GEMM path (batches past the GEMV's 8)
         self.buf_up = torch.zeros(B if B > GEMV_MAX_BATCH else 1, c.intermediate, dtype=h, device=dev)
         self.gemm_err = torch.zeros(1, dtype=torch.int32, device=dev)
+        # split-K partial tiles of the small-m GEMMs (zero between calls)
+        ws = K.w4a16_gemm_workspace_size(B, c.intermediate) if B > GEMV_MAX_BATCH else 0
+        self.gemm_ws = torch.zeros(ws + 256, dtype=torch.uint8, device=dev)
+        off = (-self.gemm_ws.data_ptr()) % 256
+        self.gemm_ws = self.gemm_ws[off:off + ws] if ws else None
         self.buf_logits = torch.zeros(B, c.vocab, dtype=h, device=dev)
         ws = K.attention_workspace_size(B, c.n_q_heads, c.head_dim, self.n_splits)
         self.attn_ws = torch.zeros(max(ws, 16), dtype=torch.uint8, device=dev)
@@ -148,7 +153,7 @@ class QwenEngine:
             K.rms_norm(x, lw.in_norm, c.eps, out=xn)
             if gemm:
                 K.w4a16_gemm(xn, lw.qkv_packed, lw.qkv_scales, c.qkv_rows, c.hidden, bias=lw.qkv_bias,
-                             out=self.buf_qkv[:B], error=self.gemm_err)
+                             out=self.buf_qkv[:B], error=self.gemm_err, workspace=self.gemm_ws)
             else:
                 K.gemv_q4_bias(lw.qkv_packed, lw.qkv_scales, lw.qkv_bias, xn, c.qkv_rows, c.hidden,
                                out=self.buf_qkv[:B])
@@ -161,15 +166,15 @@ class QwenEngine:
                                    self.n_splits)
             if gemm:
                 K.w4a16_gemm(self.buf_attn[:B], lw.o_packed, lw.o_scales, c.hidden, c.q_dim, residual=x,
-                             out=x, error=self.gemm_err)
+                             out=x, error=self.gemm_err, workspace=self.gemm_ws)
                 K.rms_norm(x, lw.post_norm, c.eps, out=xn)
                 K.w4a16_gemm(xn, lw.gate_packed, lw.gate_scales, c.intermediate, c.hidden,
-                             out=self.buf_mlp[:B], error=self.gemm_err)
+                             out=self.buf_mlp[:B], error=self.gemm_err, workspace=self.gemm_ws)
                 K.w4a16_gemm(xn, lw.up_packed, lw.up_scales, c.intermediate, c.hidden,
-                             out=self.buf_up[:B], error=self.gemm_err)
+                             out=self.buf_up[:B], error=self.gemm_err, workspace=self.gemm_ws)
                 K.swiglu(self.buf_mlp[:B], self.buf_up[:B], out=self.buf_mlp[:B])
                 K.w4a16_gemm(self.buf_mlp[:B], lw.down_packed, lw.down_scales, c.hidden, c.intermediate,
-                             residual=x, out=x, error=self.gemm_err)
+                             residual=x, out=x, error=self.gemm_err, workspace=self.gemm_ws)
             else:
                 K.gemv_q4_residual(lw.o_packed, lw.o_scales, self.buf_attn[:B], x, c.hidden, c.q_dim, out=x)
                 K.rms_norm(x, lw.post_norm, c.eps, out=xn)
@@ -183,7 +188,7 @@ class QwenEngine:
         K.rms_norm(self.buf_residual[:B], w.final_norm, c.eps, out=self.buf_normed[:B])
         if B > GEMV_MAX_BATCH:
             K.w4a16_gemm(self.buf_normed[:B], w.lm_packed, w.lm_scales, c.vocab, c.hidden,
-                         out=self.buf_logits[:B], error=self.gemm_err)
+                         out=self.buf_logits[:B], error=self.gemm_err, workspace=self.gemm_ws)
             K.argmax_rows(self.buf_logits[:B], c.vocab, self.next_ids[:B])
         else:
             K.lm_head_argmax(w.lm_packed, w.lm_scales, self.buf_normed[:B], c.vocab, c.hidden,

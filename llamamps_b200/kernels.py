@@ -199,13 +199,18 @@ def decode_advance(next_ids, tokens, pos, seq_lens, history=None, step=None):
 EPI_NONE, EPI_BIAS, EPI_RESIDUAL = 0, 1, 2
 
 
+def w4a16_gemm_workspace_size(m: int, n: int) -> int:
+    return int(lib().lmps_w4a16_gemm_workspace_size(m, n))
+
+
 def w4a16_gemm(x, packed, scales, n: int, k: int, *, bias=None, residual=None, out=None,
-               error: Optional[torch.Tensor] = None):
+               error: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None):
     """tcgen05 W4A16 GEMM: out[m] = x[m] . W^T (+ bias | residual + fp16(.)).
 
     x is fp16 [m, k] (token-major); W the Q4 [n, k] layout.  Used where the
     projections of many tokens at once are dense contractions (prefill, large
-    batches)."""
+    batches).  ``workspace`` (uint8, w4a16_gemm_workspace_size(m, n) bytes,
+    zero-filled once, 256-byte aligned) lets small-m calls split K."""
     x2, m = _x2d(x)
     y = out if out is not None else torch.empty(m, n, dtype=FP16, device=x.device)
     epi, b_ptr, r_ptr, ldr = EPI_NONE, None, None, 0
@@ -217,9 +222,12 @@ def w4a16_gemm(x, packed, scales, n: int, k: int, *, bias=None, residual=None, o
         r2 = residual if residual.dim() == 2 else residual.reshape(1, -1)
         epi, r_ptr, ldr = EPI_RESIDUAL, _dev(r2, "residual", FP16), r2.shape[1]
     err = error if error is not None else torch.zeros(1, dtype=torch.int32, device=x.device)
+    ws_ptr, ws_bytes = None, 0
+    if workspace is not None:
+        ws_ptr, ws_bytes = _dev(workspace, "workspace", torch.uint8), workspace.numel()
     call("lmps_w4a16_gemm", _dev(x2, "x", FP16), x2.shape[1], _dev(packed, "packed", torch.uint8),
          _dev(scales, "scales", FP16), b_ptr, r_ptr, ldr, _dev(y, "y", FP16), y.shape[-1], m, n, k, epi,
-         _dev(err, "error", torch.int32), _stream())
+         _dev(err, "error", torch.int32), ws_ptr, ws_bytes, _stream())
     return y
 
 
