@@ -164,24 +164,41 @@ class QwenEngine:
                                    self.buf_attn[:B], self.attn_ws, self.cache.page_size,
                                    c.n_q_heads, c.n_kv_heads, c.head_dim, self.max_seq_len,
                                    self.n_splits)
+            self._o_proj(lw, self.buf_attn[:B], x, gemm)
+            K.rms_norm(x, lw.post_norm, c.eps, out=xn)
             if gemm:
-                K.w4a16_gemm(self.buf_attn[:B], lw.o_packed, lw.o_scales, c.hidden, c.q_dim, residual=x,
-                             out=x, error=self.gemm_err, workspace=self.gemm_ws)
-                K.rms_norm(x, lw.post_norm, c.eps, out=xn)
                 K.w4a16_gemm(xn, lw.gate_packed, lw.gate_scales, c.intermediate, c.hidden,
                              out=self.buf_mlp[:B], error=self.gemm_err, workspace=self.gemm_ws)
                 K.w4a16_gemm(xn, lw.up_packed, lw.up_scales, c.intermediate, c.hidden,
                              out=self.buf_up[:B], error=self.gemm_err, workspace=self.gemm_ws)
                 K.swiglu(self.buf_mlp[:B], self.buf_up[:B], out=self.buf_mlp[:B])
-                K.w4a16_gemm(self.buf_mlp[:B], lw.down_packed, lw.down_scales, c.hidden, c.intermediate,
-                             residual=x, out=x, error=self.gemm_err, workspace=self.gemm_ws)
             else:
-                K.gemv_q4_residual(lw.o_packed, lw.o_scales, self.buf_attn[:B], x, c.hidden, c.q_dim, out=x)
-                K.rms_norm(x, lw.post_norm, c.eps, out=xn)
                 K.gemv_q4_swiglu(lw.gate_packed, lw.gate_scales, lw.up_packed, lw.up_scales, xn,
                                  c.intermediate, c.hidden, out=self.buf_mlp[:B])
-                K.gemv_q4_residual(lw.down_packed, lw.down_scales, self.buf_mlp[:B], x, c.hidden,
-                                   c.intermediate, out=x)
+            self._down_proj(lw, self.buf_mlp[:B], x, gemm)
+
+    # x <- x + fp16(W_o attn) and x <- x + fp16(W_down a) (runners/engine.py:215-221,237-243);
+    # the tensor-parallel engine overrides these with partial products and an all-reduce
+    def _ws(self, ws):
+        """Split-K workspace of a GEMM call: the decode buffer by default,
+        none (unsplit) for the token rows of a dense prefill (ws=False)."""
+        return None if ws is False else (ws if ws is not None else self.gemm_ws)
+
+    def _o_proj(self, lw, att, x, gemm: bool, ws=None) -> None:
+        c = self.cfg
+        if gemm:
+            K.w4a16_gemm(att, lw.o_packed, lw.o_scales, c.hidden, c.q_dim, residual=x, out=x,
+                         error=self.gemm_err, workspace=self._ws(ws))
+        else:
+            K.gemv_q4_residual(lw.o_packed, lw.o_scales, att, x, c.hidden, c.q_dim, out=x)
+
+    def _down_proj(self, lw, a, x, gemm: bool, ws=None) -> None:
+        c = self.cfg
+        if gemm:
+            K.w4a16_gemm(a, lw.down_packed, lw.down_scales, c.hidden, c.intermediate, residual=x, out=x,
+                         error=self.gemm_err, workspace=self._ws(ws))
+        else:
+            K.gemv_q4_residual(lw.down_packed, lw.down_scales, a, x, c.hidden, c.intermediate, out=x)
 
     def _head(self, B: int, want_logits: bool) -> None:
         c, w = self.cfg, self.weights
@@ -398,13 +415,12 @@ class QwenEngine:
                              c.n_q_heads, c.n_kv_heads, c.head_dim, c.rope_style_code)
             K.gqa_decode_attention(q, kp, vp, rows_bt, rows_len, att, ws, self.cache.page_size,
                                    c.n_q_heads, c.n_kv_heads, c.head_dim, P, splits)
-            K.w4a16_gemm(att, lw.o_packed, lw.o_scales, c.hidden, c.q_dim, residual=x, out=x, error=err)
+            self._o_proj(lw, att, x, True, ws=False)
             K.rms_norm(x, lw.post_norm, c.eps, out=xn)
             K.w4a16_gemm(xn, lw.gate_packed, lw.gate_scales, c.intermediate, c.hidden, out=gate, error=err)
             K.w4a16_gemm(xn, lw.up_packed, lw.up_scales, c.intermediate, c.hidden, out=up, error=err)
             K.swiglu(gate, up, out=gate)
-            K.w4a16_gemm(gate, lw.down_packed, lw.down_scales, c.hidden, c.intermediate, residual=x, out=x,
-                         error=err)
+            self._down_proj(lw, gate, x, True, ws=False)
         # last position of every sequence -> final norm, LM head, argmax
         self.buf_residual[:B].copy_(x.view(B, P, c.hidden)[:, P - 1])
         self._head(B, want_logits=False)
