@@ -242,6 +242,106 @@ def gemv_roofline(eng, peak_gbs, peak_kind, reps: int = 3):
             "bytes_per_launch": bytes_per_launch, "us_per_launch": round(per_launch_s * 1e6, 3)}
 
 
+def _timed(fn, world, dist):
+    """Device time of fn() bracketed by a barrier and synchronizes, max over ranks."""
+    import torch
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    fn()
+    e1.record(st)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / 1e3], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def extra_configs(mw, cfg, args, rank, world, dist, peak):
+    """The other configurations of the headline metric, each measured on the
+    device (CUDA events, max over ranks) after the bs1 line:
+      c2  batched decode, 64 sequences over the job (64/N per GPU), 128-id prompts;
+      c3  prefill of 8 x 2048 ids on the tensor-core GEMM path, then decode (1 GPU);
+      c4  long-context decode, 4 sequences per GPU over a 32768-position KV cache."""
+    import numpy as np
+    import torch
+    from llamamps_b200.engine import QwenEngine
+    out = {}
+    steps = max(4, min(args.steps, 16))
+    # -- c2
+    try:
+        B = max(1, 64 // world)
+        eng = QwenEngine(weights=mw, device=torch.device("cuda"), max_batch=B,
+                         max_seq_len=128 + args.warmup + steps + 8, decoder="kernels")
+        prompt = np.random.default_rng(2 + rank).integers(0, cfg.vocab, (B, 128))
+        eng.reset(B)
+        eng.prefill(torch.from_numpy(prompt))
+        eng.decode_steps(args.warmup, record=False)
+        t = _timed(lambda: eng.decode_steps(steps, record=False), world, dist)
+        mean_T = 128 + args.warmup + (steps + 1) / 2
+        step_bytes = cfg.step_weight_bytes() + B * cfg.kv_bytes_per_position() * mean_T
+        out["c2_batched_decode"] = {
+            "value": round(world * B * steps / t, 1), "unit": "tok/s", "batch_per_gpu": B,
+            "global_batch": B * world, "ms_per_step": round(t / steps * 1e3, 3),
+            "hbm_frac_of_measured": round(step_bytes / (t / steps) / 1e9 / peak, 4),
+            "path": "per-stage kernels; projections and LM head on the tcgen05 W4A16 GEMM (split-K)"}
+        del eng
+    except Exception as e:  # a sub-measurement never hides the headline line
+        out["c2_batched_decode"] = {"error": repr(e)[:200]}
+    # -- c3 (one GPU)
+    if world == 1:
+        try:
+            B, P = 8, 2048
+            eng = QwenEngine(weights=mw, device=torch.device("cuda"), max_batch=B, max_seq_len=P + 32,
+                             decoder="kernels")
+            prompt = torch.from_numpy(np.random.default_rng(3).integers(0, cfg.vocab, (B, P)))
+            eng.reset(B)
+            eng.prefill(prompt, dense=True)  # warm-up
+            eng.reset(B)
+            t = _timed(lambda: eng.prefill(prompt, dense=True), world, dist)
+            lin_flops = 2.0 * B * P * (cfg.n_layers * (cfg.qkv_rows + cfg.q_dim + 3 * cfg.intermediate)
+                                       * cfg.hidden)
+            att_flops = 2.0 * 2 * cfg.n_layers * B * cfg.n_q_heads * cfg.head_dim * P * (P + 1) / 2
+            eng.decode_steps(2, record=False)   # graph capture outside the timed region
+            td = _timed(lambda: eng.decode_steps(16, record=False), world, dist)
+            out["c3_prefill"] = {
+                "value": round(B * P / t, 1), "unit": "prompt tok/s", "ms": round(t * 1e3, 2),
+                "tflops": round((lin_flops + att_flops) / t / 1e12, 1),
+                "decode_after_prefill_tok_s": round(B * 16 / td, 1),
+                "path": "dense prefill: W4A16 tcgen05 GEMMs over 16384 token rows, causal attention as "
+                        "per-row decode attention; then bs8 decode on the per-stage kernels"}
+            del eng
+        except Exception as e:
+            out["c3_prefill"] = {"error": repr(e)[:200]}
+    # -- c4
+    try:
+        B, T = 4, 32768
+        eng = QwenEngine(weights=mw, device=torch.device("cuda"), max_batch=B,
+                         max_seq_len=T + args.warmup + steps + 8, decoder="persistent")
+        eng.reset(B, start_pos=T)
+        g = torch.Generator(device="cuda").manual_seed(4 + rank)
+        for layer in range(cfg.n_layers):   # the KV cache of T positions, fp16 N(0,1)
+            eng.cache.k[layer].normal_(generator=g)
+            eng.cache.v[layer].normal_(generator=g)
+        eng.tokens[:B].copy_(torch.from_numpy(np.random.default_rng(4).integers(0, cfg.vocab, B)))
+        eng.decode_steps(args.warmup, record=False)
+        t = _timed(lambda: eng.decode_steps(steps, record=False), world, dist)
+        eng.pdec.check_error()
+        kv = B * cfg.kv_bytes_per_position() * (T + args.warmup + steps / 2)
+        out["c4_long_context"] = {
+            "value": round(world * B * steps / t, 1), "unit": "tok/s", "batch_per_gpu": B, "kv_positions": T,
+            "ms_per_step": round(t / steps * 1e3, 3),
+            "hbm_frac_of_measured": round((cfg.step_weight_bytes() + kv) / (t / steps) / 1e9 / peak, 4),
+            "path": "persistent decode kernel"}
+        del eng
+    except Exception as e:
+        out["c4_long_context"] = {"error": repr(e)[:200]}
+    return out
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -364,6 +464,12 @@ def run_ours(args):
             "gpu_launches": 1 if eng.pdec is not None else eng.launches_per_step() * args.steps,
             "clocks": clocks,
         }
+    extras = None
+    if not args.no_extra and args.layers is None:
+        extras = extra_configs(mw, cfg, args, rank, world, dist, peak)
+    if rank == 0:
+        if extras is not None:
+            line["configs"] = extras
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_sample()
         print(json.dumps(line))
@@ -379,6 +485,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the c2/c3/c4 sub-measurements (batch 64, 8x2048 prefill, 32K context)")
     ap.add_argument("--decoder", choices=["persistent", "kernels"], default=None)
     ap.add_argument("--timeline", default=None,
                     help="after the timed region, write the persistent kernel's stage timeline "
