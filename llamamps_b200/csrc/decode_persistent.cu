@@ -1062,6 +1062,17 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
   float mrun0 = -INFINITY, mrun1 = -INFINITY, lrun0 = 0.0f, lrun1 = 0.0f;  // heads 2*t4, 2*t4+1
   for (int bi = warp; bi < nblk; bi += kConsumerWarps) {
     const int p0 = start + bi * kBlk;
+    if (bi + kConsumerWarps < nblk) {  // this warp's next block into L2 while this one computes
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int p = p0 + kConsumerWarps * kBlk + 8 * h2 + g8;
+        if (p < end && p != pos) {
+          const size_t off = row_off(p);
+          asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(kpool + off));
+          asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(vpool + off));
+        }
+      }
+    }
     // Cache rows p0+g8 and p0+8+g8, dims 32*t4 .. 32*t4+31 (the row of pos was
     // appended by this CTA before the last block sync).
     uint4 kr[2][4], vr[2][4];
@@ -1253,7 +1264,10 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
 __device__ __forceinline__ int attn_chunk_len(const int* pos, int batch, int n_kv) {
   long long total = 0;
   for (int b = 0; b < batch; ++b) total += pos[b] + 1;
-  long long c = (total * n_kv + gridDim.x - 1) / gridDim.x;
+  // ceil() of each (sequence, KV head) adds at most one item: keep the
+  // item count within the grid so no CTA gets a second item
+  const long long slots = static_cast<long long>(gridDim.x) - static_cast<long long>(batch) * n_kv;
+  long long c = (total * n_kv + (slots > 0 ? slots : 1) - 1) / (slots > 0 ? slots : 1);
   c = (c + kBlk - 1) / kBlk * kBlk;
   return static_cast<int>(c < kMinSplit ? kMinSplit : c);
 }
