@@ -311,8 +311,8 @@ def extra_configs(mw, cfg, args, rank, world, dist, peak):
                 "value": round(B * P / t, 1), "unit": "prompt tok/s", "ms": round(t * 1e3, 2),
                 "tflops": round((lin_flops + att_flops) / t / 1e12, 1),
                 "decode_after_prefill_tok_s": round(B * 16 / td, 1),
-                "path": "dense prefill: W4A16 tcgen05 GEMMs over 16384 token rows, causal attention as "
-                        "per-row decode attention; then bs8 decode on the per-stage kernels"}
+                "path": "dense prefill: W4A16 tcgen05 GEMMs over 16384 token rows, causal flash "
+                        "attention over the paged cache; then bs8 decode on the per-stage kernels"}
             del eng
         except Exception as e:
             out["c3_prefill"] = {"error": repr(e)[:200]}

@@ -194,6 +194,17 @@ int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed, const uin
                     int m, int n, int k, int epilogue, int32_t* error, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* Causal prefill attention (attention.metal + softmax.metal + attn_sum.metal,
+ * runners/engine.py:202-212, for every prompt position at once): q holds the
+ * rotated queries of seq_len positions of each of `batch` sequences, row
+ * b*seq_len + p, [.., n_q_heads*head_dim] with leading dimension ldq; their
+ * K/V rows are already in the paged cache (block_table [batch, max_pages]).
+ * Query p attends to positions 0..p; out has q's row layout.  head_dim 128,
+ * n_q_heads / n_kv_heads <= 8. */
+int lmps_prefill_attention(const uint16_t* q, int ldq, const uint16_t* k_pool, const uint16_t* v_pool,
+                           const int32_t* block_table, int max_pages, int page_size, uint16_t* out, int ldo,
+                           int batch, int seq_len, int n_q_heads, int n_kv_heads, int head_dim, void* stream);
+
 /* First-index argmax of each row of fp16 logits [rows, ld] over n columns
  * (runners/engine.py:180-181), the large-batch companion of the LM-head GEMM. */
 int lmps_argmax_rows(const uint16_t* logits, int ld, int rows, int n, int32_t* ids, void* stream);

@@ -46,6 +46,8 @@ _SIGS = {
                                                   c_int, c_int, c_int, c_int, c_int, c_int, c_vp]),
     "lmps_q4_pack": (c_int, [c_vp, c_ll, c_vp, c_vp, c_vp]),
     "lmps_decode_advance": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_vp]),
+    "lmps_prefill_attention": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_vp, c_int, c_int, c_int,
+                                       c_int, c_int, c_int, c_vp]),
     "lmps_argmax_rows": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_vp]),
     "lmps_w4a16_gemm_workspace_size": (c_size, [c_int, c_int]),
     "lmps_w4a16_gemm": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_vp, c_int, c_int, c_int, c_int,

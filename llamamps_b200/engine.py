@@ -381,9 +381,9 @@ class QwenEngine:
     def prefill_dense(self, prompts: torch.Tensor) -> None:
         """All B*P prompt tokens through every layer at once: the projections
         are W4A16 tensor-core GEMMs over M = B*P token rows, RoPE and the KV
-        append run on every (sequence, position) row, and causal attention is
-        one decode-attention query per row against the positions up to its
-        own.  The LM head runs on each sequence's last row only."""
+        append run on every (sequence, position) row, and the causal
+        attention of all rows is one flash-attention launch over the paged
+        cache.  The LM head runs on each sequence's last row only."""
         c, w, dev = self.cfg, self.weights, self.device
         B, P = prompts.shape
         if self.host_pos != 0:
@@ -392,7 +392,6 @@ class QwenEngine:
         h, i32 = torch.float16, torch.int32
         ids = prompts.reshape(-1).contiguous()
         rows_pos = torch.arange(P, dtype=i32, device=dev).repeat(B)
-        rows_len = rows_pos + 1
         rows_bt = self.cache.block_table[:B].repeat_interleave(P, dim=0).contiguous()
         x = torch.empty(Mt, c.hidden, dtype=h, device=dev)
         xn = torch.empty_like(x)
@@ -401,9 +400,6 @@ class QwenEngine:
         att = torch.empty(Mt, c.q_dim, dtype=h, device=dev)
         gate = torch.empty(Mt, c.intermediate, dtype=h, device=dev)
         up = torch.empty_like(gate)
-        splits = K.attention_splits(Mt, c.n_kv_heads, P, self.cache.page_size)
-        ws = torch.zeros(max(K.attention_workspace_size(Mt, c.n_q_heads, c.head_dim, splits), 16),
-                         dtype=torch.uint8, device=dev)
         err = self.gemm_err
         K.embed_gather(w.embed, ids, x, self.bad_ids)
         for li, lw in enumerate(w.layers):
@@ -413,8 +409,8 @@ class QwenEngine:
                          out=qkv, error=err)
             K.rope_kv_append(qkv, rows_pos, self.inv_freq, q, kp, vp, rows_bt, self.cache.page_size,
                              c.n_q_heads, c.n_kv_heads, c.head_dim, c.rope_style_code)
-            K.gqa_decode_attention(q, kp, vp, rows_bt, rows_len, att, ws, self.cache.page_size,
-                                   c.n_q_heads, c.n_kv_heads, c.head_dim, P, splits)
+            K.prefill_attention(q, kp, vp, self.cache.block_table[:B], att, B, P, self.cache.page_size,
+                                c.n_q_heads, c.n_kv_heads, c.head_dim)
             self._o_proj(lw, att, x, True, ws=False)
             K.rms_norm(x, lw.post_norm, c.eps, out=xn)
             K.w4a16_gemm(xn, lw.gate_packed, lw.gate_scales, c.intermediate, c.hidden, out=gate, error=err)

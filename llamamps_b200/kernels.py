@@ -237,3 +237,13 @@ def argmax_rows(logits, n: int, ids):
          _dev(ids, "ids", torch.int32), _stream())
     return ids
 
+
+def prefill_attention(q, k_pool, v_pool, block_table, out, batch: int, seq_len: int, page_size: int,
+                      n_q_heads: int, n_kv_heads: int, head_dim: int):
+    """Causal attention of every prompt position (q rows b*seq_len + p) over the paged cache."""
+    call("lmps_prefill_attention", _dev(q, "q", FP16), q.shape[-1], _dev(k_pool, "k_pool", FP16),
+         _dev(v_pool, "v_pool", FP16), _dev(block_table, "block_table", torch.int32), block_table.shape[1],
+         page_size, _dev(out, "out", FP16), out.shape[-1], batch, seq_len, n_q_heads, n_kv_heads, head_dim,
+         _stream())
+    return out
+

@@ -93,3 +93,27 @@ def test_dense_and_stepwise_prefill_fill_the_same_cache(cuda, small_model):
             assert torch.allclose(ka.float(), kb.float(), atol=2e-2, rtol=1e-2)
             assert torch.allclose(va.float(), vb.float(), atol=2e-2, rtol=1e-2)
     assert torch.equal(a.pos[:2], b.pos[:2])
+
+
+@pytest.mark.parametrize("P", [1, 37, 130])
+def test_prefill_attention_matches_per_row_decode_attention(cuda, P):
+    """The causal prefill kernel against the decode attention kernel run with
+    one query row per position (seq_len = p + 1) on the same paged cache."""
+    from llamamps_b200 import kernels as K
+    B, Hq, Hkv, hd, ps = 2, 12, 2, 128, 64
+    g = torch.Generator(device="cuda").manual_seed(P)
+    pages = (P + ps - 1) // ps
+    kp = torch.randn(B * pages, Hkv, ps, hd, generator=g, device="cuda").half()
+    vp = torch.randn(B * pages, Hkv, ps, hd, generator=g, device="cuda").half()
+    bt = torch.randperm(B * pages, generator=g, device="cuda").to(torch.int32).reshape(B, pages)
+    q = torch.randn(B * P, Hq * hd, generator=g, device="cuda").half()
+    out = torch.empty_like(q)
+    K.prefill_attention(q, kp, vp, bt, out, B, P, ps, Hq, Hkv, hd)
+    rows_bt = bt.repeat_interleave(P, dim=0).contiguous()
+    lens = (torch.arange(P, device="cuda", dtype=torch.int32) + 1).repeat(B)
+    ref = torch.empty_like(q)
+    splits = K.attention_splits(B * P, Hkv, P, ps)
+    ws = torch.zeros(max(K.attention_workspace_size(B * P, Hq, hd, splits), 16), dtype=torch.uint8, device="cuda")
+    K.gqa_decode_attention(q, kp, vp, rows_bt, lens, ref, ws, ps, Hq, Hkv, hd, P, splits)
+    torch.cuda.synchronize()
+    assert torch.allclose(out.float(), ref.float(), atol=4e-3, rtol=1e-2), float((out.float() - ref.float()).abs().max())
