@@ -181,10 +181,11 @@ int lmps_gqa_decode_attention_noalloc(const uint16_t* q, const uint16_t* k_pool,
  * epilogue: 0 none, 1 + bias[n], 2 residual[m, n] + fp16(acc) (residual may
  * alias y).  n must be a multiple of 128 and k of 64 (else UNSUPPORTED); any
  * m >= 1.  error[0] is set to 1 if a bounded wait for the tensor core gives up.
- * With a workspace of lmps_w4a16_gemm_workspace_size(m, n) bytes (256-byte
- * aligned, zero-filled once; every call leaves it zero) small-m calls split K
- * over more CTAs; NULL runs unsplit.  Replaces the per-token dispatch of
- * runners/engine.py:188-243 at B > 1. */
+ * Calls with fewer than 128 tokens split K over the CTAs of a thread-block
+ * cluster and sum the partial tiles in distributed shared memory, so the
+ * workspace arguments are unused (lmps_w4a16_gemm_workspace_size returns 0;
+ * pass NULL, 0).  packed must be 16-byte aligned (TMA).  Replaces the
+ * per-token dispatch of runners/engine.py:188-243 at B > 1. */
 #define LMPS_EPI_NONE 0
 #define LMPS_EPI_BIAS 1
 #define LMPS_EPI_RESIDUAL 2
@@ -264,8 +265,10 @@ typedef struct lmps_model_desc {
 } lmps_model_desc;
 
 typedef struct lmps_decode_state {
-  int batch, page_size, max_pages, max_seq_len;
+  int batch, page_size, max_pages, max_seq_len;   /* page_size: a power of two */
   const int32_t* block_table;   /* [batch, max_pages] */
+  const float* rope_table;      /* fp32 [max_seq_len, head_dim/2, 2]: cos and sin of the
+                                   fp32 angle p * inv_freq[j] (rope.metal:28-33) */
   int32_t* tokens;              /* [batch] token fed at the next step; updated */
   int32_t* pos;                 /* [batch] position of that token; updated */
   const int32_t* forced;        /* [batch, forced_stride] tokens fed after steps 0..n_forced-1 (or NULL) */

@@ -147,6 +147,15 @@ struct Params {
 
 enum StageKind { ST_QKV = 0, ST_O = 1, ST_GU = 2, ST_DN = 3, ST_HEAD = 4 };
 
+// Shared-memory copy of the per-layer pointers on the consumers' critical
+// path (the descriptor array itself is in global memory).
+struct LayerPtrs {
+  const __half* in_norm;
+  const __half* post_norm;
+  __half* k_pool;
+  __half* v_pool;
+};
+
 struct Smem {
   unsigned char* ring;
   unsigned char* act;
@@ -155,8 +164,8 @@ struct Smem {
   float* red8;       // [warps * kMaxB] block-reduction scratch
   unsigned long long* best;  // [warps][kMaxB]
   int* misc;         // [0] abort
-  float* inv_freq;   // [head_dim/2] RoPE frequencies, staged once per launch
-  __half* xown;      // [kMaxB][kOwnMax] residual x of the hidden rows this CTA owns
+  struct LayerPtrs* lp;  // [n_layers] the layer pointers the consumers read, staged once per launch
+  __half* xown;     // [kMaxB][kOwnMax] residual x of the hidden rows this CTA owns
   __half* x1own;     // [kMaxB][kOwnMax] residual after attention, same rows
   __half* bias_own;  // [n_layers][kOwnMax] q|k|v bias of the qkv rows this CTA owns
 };
@@ -576,27 +585,22 @@ __device__ void stage_copy(const Params& P, Smem& S, const unsigned long long* s
       const int b = i / vpr, c = i - b * vpr;
       if (r0 + q < rounds && i < total && b < P.s.batch) tagged4_issue(src + static_cast<size_t>(b) * (k / 2) + 4 * c, t[q]);
     }
-    uint4 v[kBatch];
-#pragma unroll
-    for (int q = 0; q < kBatch; ++q) {
+    // One loop body finishes and converts the chunks in turn (t[0] is the
+    // current one; the array shifts down), keeping the code compact.
+#pragma unroll 1
+    for (int q = 0; q < kBatch && r0 + q < rounds; ++q) {  // uniform across the CTA
       const int i = threadIdx.x + (r0 + q) * kConsumers;
       const int b = i / vpr, c = i - b * vpr;
-      v[q] = make_uint4(0u, 0u, 0u, 0u);
-      if (r0 + q < rounds && i < total && b < P.s.batch)
-        v[q] = tagged4_finish(P, S, src + static_cast<size_t>(b) * (k / 2) + 4 * c, tag, t[q]);
-    }
+      const bool active = i < total && b < P.s.batch;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (active) v = tagged4_finish(P, S, src + static_cast<size_t>(b) * (k / 2) + 4 * c, tag, t[0]);
+      const __half* h = reinterpret_cast<const __half*>(&v);
+      float f[8];
 #pragma unroll
-    for (int q = 0; q < kBatch; ++q) {
-      if (r0 + q < rounds) {  // uniform across the CTA
-        const int i = threadIdx.x + (r0 + q) * kConsumers;
-        const int b = i / vpr, c = i - b * vpr;
-        const bool active = i < total && b < P.s.batch;
-        const __half* h = reinterpret_cast<const __half*>(&v[q]);
-        float f[8];
+      for (int e = 0; e < 8; ++e) f[e] = __half2float(h[e]);
+      store_planes(f, active, pl, active ? b : 0, c >> 2);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] = __half2float(h[e]);
-        store_planes(f, active, pl, active ? b : 0, c >> 2);
-      }
+      for (int j = 0; j + 1 < kBatch; ++j) t[j] = t[j + 1];
     }
   }
   consumer_sync();
@@ -677,18 +681,14 @@ __device__ __forceinline__ void group_fma(const Planes& pl, int gi, const uint4&
 // the tagged output.  (Per-chunk shuffle trees and single-lane epilogues were
 // a serial tail after every chunk.)
 constexpr int kPartRows = 2 * kOutMax;  // row entries of a stage (gate/up: a gate and an up entry per row)
+constexpr int kRedStride = 16;          // down projection: per-row stride of the warp partials
 
 // Partial-sum area after the activation planes of a k = hidden stage:
 // [NB][kPartRows][16 lanes] floats.
 __device__ __forceinline__ float* partials_view(const Planes& pl, int nb) {
-  return reinterpret_cast<float*>(pl.xs8 + nb * pl.G);
-}
-
-__device__ __forceinline__ float sum16(const float* p) {
-  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
-  const float4 c = *reinterpret_cast<const float4*>(p + 8), d = *reinterpret_cast<const float4*>(p + 12);
-  return ((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w)) + ((c.x + c.y) + (c.z + c.w)) +
-         ((d.x + d.y) + (d.z + d.w));
+  // 16-byte aligned: the epilogues read the partials as float4
+  const uintptr_t p = reinterpret_cast<uintptr_t>(pl.xs8 + nb * pl.G);
+  return reinterpret_cast<float*>((p + 15) & ~static_cast<uintptr_t>(15));
 }
 
 // Row GEMVs with k = hidden: q|k|v (+bias), o (+residual), gate/up (SwiGLU) and
@@ -711,45 +711,87 @@ __device__ void gemv_rows(const Params& P, Smem& S, CState& cs, int kind, int la
   unsigned long long best[NB];
 #pragma unroll
   for (int b = 0; b < NB; ++b) best[b] = 0ull;
-  for (int r = c.r0; r < c.r1; r += rpc) {
-    const int n = min(rpc, c.r1 - r);
-    const int slot = cs.slot;
+  // Two ring chunks per pass (when the stage has them): every activation
+  // group is read from shared memory once for both chunks' rows.
+  for (int r = c.r0; r < c.r1; r += 2 * rpc) {
+    const int nc[2] = {min(rpc, c.r1 - r), min(rpc, max(0, c.r1 - r - rpc))};  // nc[1] == 0: one chunk
+    const int slot0 = cs.slot;
     slot_wait(S, P, cs);
-    float acc[NB];
+    int slot1 = slot0;
+    if (nc[1] > 0) {
+      CState nx = cs;
+      if (++nx.slot == P.slots) {
+        nx.slot = 0;
+        nx.phase ^= 1u;
+      }
+      slot1 = nx.slot;
+      slot_wait(S, P, nx);
+      cs.wait_ns = nx.wait_ns;
+    }
+    float acc[2][NB];
 #pragma unroll
-    for (int b = 0; b < NB; ++b) acc[b] = 0.0f;
-    if (lrow < n) {
-      const unsigned char* base = S.ring + static_cast<size_t>(slot) * kSlotBytes;
+    for (int b = 0; b < NB; ++b) acc[0][b] = acc[1][b] = 0.0f;
+    const unsigned char* wrow[2];
+    const __half* srow[2];
+    bool ok[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int n = nc[q];
+      ok[q] = lrow < n;
+      const unsigned char* base = S.ring + static_cast<size_t>(q ? slot1 : slot0) * kSlotBytes;
       const size_t pbytes = n * rb * (gu ? 2 : 1);
       const int srow_i = gu ? half * n + warp : lrow;  // scale row within the slot's scale block
-      const unsigned char* wrow = base + (gu ? half * n * rb : 0) + lrow * rb;
-      const __half* srow = reinterpret_cast<const __half*>(base + pbytes) + srow_i * G;
+      wrow[q] = base + (gu ? half * n * rb : 0) + lrow * rb;
+      srow[q] = reinterpret_cast<const __half*>(base + pbytes) + srow_i * G;
+    }
 #pragma unroll
-      for (int j = 0; j < kJH; ++j) {
-        if (j < JG) {
-          const int g = sub + 16 * j;
-          const uint4 wv = *reinterpret_cast<const uint4*>(wrow + g * 16);
-          group_fma<NB>(pl, g, wv, __half2float(srow[g]), acc);
+    for (int j = 0; j < kJH; ++j) {
+      if (j < JG) {
+        const int g = sub + 16 * j;
+        uint4 wv[2];
+        float sc[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          wv[q] = ok[q] ? *reinterpret_cast<const uint4*>(wrow[q] + g * 16) : make_uint4(0u, 0u, 0u, 0u);
+          sc[q] = ok[q] ? __half2float(srow[q][g]) : 0.0f;
+        }
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          XGroup xg;
+          load_xgroup(pl, b, g, xg);
+          acc[0][b] = fmaf(sc[0] * xg.scl, static_cast<float>(group_idot(wv[0], xg.w, xg.xs8)), acc[0][b]);
+          if (nc[1] > 0)
+            acc[1][b] = fmaf(sc[1] * xg.scl, static_cast<float>(group_idot(wv[1], xg.w, xg.xs8)), acc[1][b]);
         }
       }
-      if (!head) {
-        const int e = gu ? 2 * (r - c.r0 + warp) + half : r - c.r0 + lrow;
+    }
+    if (!head) {
 #pragma unroll
-        for (int b = 0; b < NB; ++b) part[(b * kPartRows + e) * 16 + sub] = acc[b];
+      for (int q = 0; q < 2; ++q) {
+        if (ok[q]) {
+          const int r0 = r + q * rpc - c.r0;
+          const int e = gu ? 2 * (r0 + warp) + half : r0 + lrow;
+#pragma unroll
+          for (int b = 0; b < NB; ++b) part[(b * kPartRows + e) * 16 + sub] = acc[q][b];
+        }
       }
     }
     slot_release(S, P, cs);
+    if (nc[1] > 0) slot_release(S, P, cs);
     if (head) {  // LM head: argmax keys only, kept per lane-0 of each row
 #pragma unroll
-      for (int b = 0; b < NB; ++b) acc[b] = segment_sum<16>(acc[b]);
-      if (sub == 0 && lrow < n) {
-        const int row = r + lrow;
+      for (int q = 0; q < 2; ++q) {
 #pragma unroll
-        for (int b = 0; b < NB; ++b) {
-          if (b >= P.s.batch) break;
-          const __half v = __float2half_rn(acc[b]);
-          if (logits) logits[static_cast<size_t>(b) * P.m.vocab + row] = v;
-          best[b] = u64_max(best[b], argmax_key(__half2float(v), static_cast<uint32_t>(row)));
+        for (int b = 0; b < NB; ++b) acc[q][b] = segment_sum<16>(acc[q][b]);
+        if (sub == 0 && ok[q]) {
+          const int row = r + q * rpc + lrow;
+#pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            if (b >= P.s.batch) break;
+            const __half v = __float2half_rn(acc[q][b]);
+            if (logits) logits[static_cast<size_t>(b) * P.m.vocab + row] = v;
+            best[b] = u64_max(best[b], argmax_key(__half2float(v), static_cast<uint32_t>(row)));
+          }
         }
       }
     }
@@ -762,36 +804,43 @@ __device__ void gemv_rows(const Params& P, Smem& S, CState& cs, int kind, int la
     }
     return;
   }
-  // -- epilogue of every row pair, published as tagged words
+  // -- epilogue of every row pair, published as tagged words.  Four lanes
+  // reduce one row entry (16 partials, one float4 each); the entries of a
+  // row pair are 2 (gate/up: 4) consecutive ones, so the pair's lanes are an
+  // aligned group of 8 (16) in one warp.
   consumer_sync();
-  const int np = (c.r1 - c.r0) / 2;
   unsigned long long* dst = kind == ST_QKV ? P.qkvt : kind == ST_O ? P.x1t : P.at;
   const int dld = kind == ST_QKV ? (P.m.n_q_heads + 2 * P.m.n_kv_heads) * kHD / 2
                                  : (kind == ST_O ? P.m.hidden : P.m.intermediate) / 2;
-  for (int t = threadIdx.x; t < NB * np; t += kConsumers) {
-    const int b = t / np, p = t - b * np;
-    if (b < P.s.batch) {
-      __half h[2];
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const int i = 2 * p + q;  // row - c.r0
-        if (kind == ST_GU) {
-          const float g = sum16(part + (b * kPartRows + 2 * i) * 16);
-          const float u = sum16(part + (b * kPartRows + 2 * i + 1) * 16);
-          h[q] = __float2half_rn(silu_mul(__half2float(__float2half_rn(g)), __half2float(__float2half_rn(u))));
-        } else {
-          const float v = sum16(part + (b * kPartRows + i) * 16);
-          if (kind == ST_QKV) {
-            h[q] = __float2half_rn(v + __half2float(S.bias_own[layer * kOwnMax + i]));
-          } else {  // ST_O
-            h[q] = __hadd(S.xown[b * kOwnMax + i], __float2half_rn(v));
-            S.x1own[b * kOwnMax + i] = h[q];
-          }
-        }
-      }
-      const __half2 v2 = __halves2half2(h[0], h[1]);
-      st_tagged(dst + static_cast<size_t>(b) * dld + c.r0 / 2 + p, tagged(tag, *reinterpret_cast<const uint32_t*>(&v2)));
+  const int per_b = (c.r1 - c.r0) * (gu ? 8 : 4);  // lanes per sequence
+  for (int t0 = 0; t0 < NB * per_b; t0 += kConsumers) {
+    const int t = t0 + threadIdx.x;
+    const int b = t / per_b, rem = t - b * per_b;
+    const int e = rem >> 2, qq = rem & 3;
+    const bool live = t < NB * per_b && b < P.s.batch;
+    float v = 0.0f;
+    if (live) {
+      const float4 p4 = *reinterpret_cast<const float4*>(part + (b * kPartRows + e) * 16 + 4 * qq);
+      v = (p4.x + p4.y) + (p4.z + p4.w);
     }
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    const float u = __shfl_down_sync(0xffffffffu, v, 4);  // gate/up: the up entry of the row
+    const int i = gu ? (e >> 1) : e;                       // row - c.r0
+    const bool row_lane = live && qq == 0 && (!gu || (e & 1) == 0);
+    __half h;
+    if (gu) {
+      h = __float2half_rn(silu_mul(__half2float(__float2half_rn(v)), __half2float(__float2half_rn(u))));
+    } else if (kind == ST_QKV) {
+      h = __float2half_rn(v + __half2float(S.bias_own[layer * kOwnMax + i]));
+    } else {  // ST_O
+      h = __hadd(S.xown[(live ? b : 0) * kOwnMax + i], __float2half_rn(v));
+      if (row_lane) S.x1own[b * kOwnMax + i] = h;
+    }
+    const uint32_t hb = __half_as_ushort(h);
+    const uint32_t hp = __shfl_down_sync(0xffffffffu, hb, gu ? 8 : 4);  // the pair's second row
+    if (row_lane && (i & 1) == 0)
+      st_tagged(dst + static_cast<size_t>(b) * dld + (c.r0 + i) / 2, tagged(tag, hb | (hp << 16)));
   }
   consumer_sync();  // the partials' area is the next stage's staging area
 }
@@ -809,7 +858,7 @@ __device__ void gemv_down(const Params& P, Smem& S, CState& cs, int layer, uint3
   const int lrow = lane >> 3, sub = lane & 7;
   const int rpc = c.rows_per_chunk;
   const Planes pl = planes_view(S, G, NB);
-  float* red = partials_view(pl, NB);  // [NB][kOwnMax rows][warps]
+  float* red = partials_view(pl, NB);  // [NB][kOwnMax rows][kRedStride >= warps]
   for (int r = c.r0; r < c.r1; r += rpc) {
     const int n = min(rpc, c.r1 - r);
     const int slot = cs.slot;
@@ -831,29 +880,32 @@ __device__ void gemv_down(const Params& P, Smem& S, CState& cs, int layer, uint3
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
       const float v = segment_sum<8>(acc[b]);
-      if (sub == 0 && lrow < n) red[(b * kOwnMax + r - c.r0 + lrow) * kConsumerWarps + warp] = v;
+      if (sub == 0 && lrow < n) red[(b * kOwnMax + r - c.r0 + lrow) * kRedStride + warp] = v;
     }
   }
+  // -- epilogue: four lanes per row (quarters of the 11 warp partials), the
+  // two rows of a pair in an aligned group of 8 lanes
   consumer_sync();
-  const int np = (c.r1 - c.r0) / 2;
-  for (int t = threadIdx.x; t < NB * np; t += kConsumers) {
-    const int b = t / np, p = t - b * np;
-    if (b < P.s.batch) {
-      __half h[2];
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const int i = 2 * p + q;
-        const float* rr = red + (b * kOwnMax + i) * kConsumerWarps;
-        float s = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) s += rr[w];
-        h[q] = __hadd(S.x1own[b * kOwnMax + i], __float2half_rn(s));
-        S.xown[b * kOwnMax + i] = h[q];
-      }
-      const __half2 v2 = __halves2half2(h[0], h[1]);
-      st_tagged(P.xt + static_cast<size_t>(b) * (P.m.hidden / 2) + c.r0 / 2 + p,
-                tagged(tag, *reinterpret_cast<const uint32_t*>(&v2)));
+  const int per_b = (c.r1 - c.r0) * 4;
+  for (int t0 = 0; t0 < NB * per_b; t0 += kConsumers) {
+    const int t = t0 + threadIdx.x;
+    const int b = t / per_b, rem = t - b * per_b;
+    const int i = rem >> 2, qq = rem & 3;
+    const bool live = t < NB * per_b && b < P.s.batch;
+    float v = 0.0f;
+    if (live && 4 * qq < kConsumerWarps) {
+      const float4 p4 = *reinterpret_cast<const float4*>(red + (b * kOwnMax + i) * kRedStride + 4 * qq);
+      v = (p4.x + p4.y) + (p4.z + (4 * qq + 3 < kConsumerWarps ? p4.w : 0.0f));
     }
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    const __half h = __hadd(S.x1own[(live ? b : 0) * kOwnMax + i], __float2half_rn(v));
+    const bool row_lane = live && qq == 0;
+    if (row_lane) S.xown[b * kOwnMax + i] = h;
+    const uint32_t hb = __half_as_ushort(h);
+    const uint32_t hp = __shfl_down_sync(0xffffffffu, hb, 4);
+    if (row_lane && (i & 1) == 0)
+      st_tagged(P.xt + static_cast<size_t>(b) * (P.m.hidden / 2) + (c.r0 + i) / 2, tagged(tag, hb | (hp << 16)));
   }
   consumer_sync();  // the partials' area is the next stage's staging area
 }
@@ -934,7 +986,7 @@ __device__ __forceinline__ void rope_pair(int j, int style, int& i1, int& i2) {
   }
 }
 
-__device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, int b, int kvh,
+__device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, int kvh,
                           int split, int n_splits, int chunk, int pos, uint32_t in_tag, uint32_t out_tag) {
   AttnSmem& A = *reinterpret_cast<AttnSmem*>(S.act);
   const lmps_model_desc& m = P.m;
@@ -946,10 +998,10 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
   const int start = split * chunk, end = min(T, start + chunk);
   const unsigned long long* row = P.qkvt + static_cast<size_t>(b) * (qkv_rows / 2);
   unsigned long long* out = P.attnt + static_cast<size_t>(b) * (Hq * kHD / 2);
-  const int ps = P.s.page_size;
+  const int ps = P.s.page_size, pshift = __ffs(ps) - 1;  // page_size is a power of two
   const int32_t* bt = P.s.block_table + static_cast<size_t>(b) * P.s.max_pages;
-  __half* kpool = reinterpret_cast<__half*>(L.k_pool);
-  __half* vpool = reinterpret_cast<__half*>(L.v_pool);
+  __half* kpool = L.k_pool;
+  __half* vpool = L.v_pool;
   const bool has_pos = pos >= start && pos < end;
   const uint64_t kvpol = evict_last_policy();
 
@@ -957,7 +1009,7 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
   // first block of every warp is prefetched into L2 before anything waits.
   const int nblk = (end - start + kBlk - 1) / kBlk;
   auto row_off = [&](int p) {
-    return ((static_cast<size_t>(__ldg(bt + p / ps)) * Hkv + kvh) * ps + p % ps) * kHD + 32 * t4;
+    return ((static_cast<size_t>(__ldg(bt + (p >> pshift))) * Hkv + kvh) * ps + (p & (ps - 1))) * kHD + 32 * t4;
   };
   if (warp < nblk) {
 #pragma unroll
@@ -971,13 +1023,16 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
     }
   }
   // cache offset of position pos (the KV append of the split holding it)
-  const size_t app = has_pos ? ((static_cast<size_t>(__ldg(bt + pos / ps)) * Hkv + kvh) * ps + pos % ps) * kHD : 0;
+  const size_t app =
+      has_pos ? ((static_cast<size_t>(__ldg(bt + (pos >> pshift))) * Hkv + kvh) * ps + (pos & (ps - 1))) * kHD : 0;
   // q rows of this KV head's G query heads and (the split holding the new
   // position) its k and v rows, polled from the tagged q|k|v output as groups
   // of 8 dims.  With adjacent RoPE pairs (rope.metal:19-40) a group holds
-  // whole pairs: the polling thread rotates it in registers, with its four
-  // angles computed while it waits.
+  // whole pairs: the polling thread rotates it in registers, with the cos/sin
+  // of its four pairs (a row of the position's RoPE table) loaded while it
+  // waits.
   const bool adj = m.rope_style == LMPS_ROPE_INTERLEAVED;
+  const float4* rope_row = reinterpret_cast<const float4*>(P.s.rope_table + static_cast<size_t>(pos) * kHD);
   {
     const int nq4 = G * (kHD / 8), n4 = nq4 + (has_pos ? 2 * (kHD / 8) : 0);
     if (tid < n4) {
@@ -987,18 +1042,19 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
       const unsigned long long* src = row + seg * (kHD / 2) + 4 * c8;
       Tagged4 t;
       tagged4_issue(src, t);
-      float cs[4], sn[4];
+      float4 cs[2];  // (cos, sin) of pairs 4*c8 .. 4*c8+3 at this position
       if (adj && kind < 2) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) sincosf(static_cast<float>(pos) * S.inv_freq[4 * c8 + e], &sn[e], &cs[e]);
+        cs[0] = __ldg(rope_row + 2 * c8);
+        cs[1] = __ldg(rope_row + 2 * c8 + 1);
       }
       uint4 v = tagged4_finish(P, S, src, in_tag, t);
       if (adj && kind < 2) {
         uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+        const float* r = reinterpret_cast<const float*>(cs);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
-          w[e] = pack_half2(f.x * cs[e] - f.y * sn[e], f.x * sn[e] + f.y * cs[e]);
+          w[e] = pack_half2(f.x * r[2 * e] - f.y * r[2 * e + 1], f.x * r[2 * e + 1] + f.y * r[2 * e]);
         }
       }
       if (!adj) {
@@ -1010,11 +1066,8 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
       }
     }
   }
-  if (!adj && tid < kHD / 2) {  // RoPE angles of this position, (j, j + head_dim/2) pairs
-    float sn, cs;
-    sincosf(static_cast<float>(pos) * S.inv_freq[tid], &sn, &cs);
-    A.rot[tid] = make_float2(cs, sn);
-  }
+  if (!adj && tid < kHD / 2)  // RoPE (cos, sin) of this position, (j, j + head_dim/2) pairs
+    A.rot[tid] = __ldg(reinterpret_cast<const float2*>(rope_row) + tid);
   consumer_sync();
   if (!adj) {
     for (int i = tid; i < G * (kHD / 2); i += kConsumers) {  // RoPE'd q, fp16-rounded
@@ -1139,31 +1192,6 @@ __device__ void attn_item(const Params& P, Smem& S, const lmps_layer_desc& L, in
   }
   const int nw = min(kConsumerWarps, nblk);  // warps that saw positions
   const size_t ms = P.max_splits;
-  if (nw == 1 && n_splits == 1) {
-    // one warp saw every position: normalise and publish from registers.
-    // Lanes g8 and g8^1 hold dims d and d+1; they swap one value so that
-    // the even lane owns the (d, d+1) pair of head 2*t4, the odd lane that
-    // of head 2*t4+1.
-    if (warp == 0) {
-      const bool odd = g8 & 1;
-      const int h = 2 * t4 + (odd ? 1 : 0);
-      const float inv = odd ? (lrun1 > 0.0f ? 1.0f / lrun1 : 0.0f) : (lrun0 > 0.0f ? 1.0f / lrun0 : 0.0f);
-#pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const float mine = odd ? o[mt][2 * hh + 1] : o[mt][2 * hh];
-          const float other = __shfl_xor_sync(0xffffffffu, odd ? o[mt][2 * hh] : o[mt][2 * hh + 1], 4);
-          const int d = 32 * (g8 >> 1) + 4 * mt + 2 * hh;  // even dim of the pair
-          if (h < G)
-            st_tagged(out + (kvh * G + h) * (kHD / 2) + d / 2,
-                      tagged(out_tag, odd ? pack_half2(other * inv, mine * inv) : pack_half2(mine * inv, other * inv)));
-        }
-      }
-    }
-    consumer_sync();  // the shared area is the next stage's staging area
-    return;
-  }
   // -- warps meet in shared memory: merged maxima first, then every warp
   // rescales its sums to them, then the block adds the warps up
   if (warp < nw && g8 == 0) {
@@ -1397,7 +1425,7 @@ __device__ void consumer(const Params& P, Smem& S, uint32_t epoch) {
       const int kind = (l == m.n_layers) ? K_HEAD : si - 5 * l;
       const uint32_t tag = tag0 + static_cast<uint32_t>(si), in_tag = tag - 1u;
       if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
-      const lmps_layer_desc& L = m.layers[kind == K_HEAD ? 0 : l];
+      const LayerPtrs& L = S.lp[kind == K_HEAD ? 0 : l];
       // -- stage the input activation in shared memory
       if (kind == K_QKV || kind == K_GU || kind == K_HEAD) {
         const __half* rows[NB];
@@ -1407,8 +1435,9 @@ __device__ void consumer(const Params& P, Smem& S, uint32_t epoch) {
           rows[b] = from_x_in ? x_in + static_cast<size_t>(bb) * hidden : embed + static_cast<size_t>(tok[bb]) * hidden;
         }
         const unsigned long long* tsrc = (kind == K_QKV && l == 0) ? nullptr : kind == K_GU ? P.x1t : P.xt;
-        const void* gamma = kind == K_QKV ? L.in_norm : kind == K_GU ? L.post_norm : m.final_norm;
-        stage_norm<NB>(P, S, rows, tsrc, in_tag, reinterpret_cast<const __half*>(gamma), hidden);
+        const __half* gamma = kind == K_QKV ? L.in_norm : kind == K_GU ? L.post_norm
+                                                       : reinterpret_cast<const __half*>(m.final_norm);
+        stage_norm<NB>(P, S, rows, tsrc, in_tag, gamma, hidden);
       } else if (kind == K_O || kind == K_DN) {
         stage_copy<NB>(P, S, kind == K_O ? P.attnt : P.at, in_tag, kind == K_O ? q_dim : m.intermediate);
       }
@@ -1499,13 +1528,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
   S.red8 = reinterpret_cast<float*>(S.empty + 16);
   S.best = reinterpret_cast<unsigned long long*>(S.red8 + kConsumerWarps * kMaxB);
   S.misc = reinterpret_cast<int*>(S.best + kConsumerWarps * kMaxB);
-  S.inv_freq = reinterpret_cast<float*>(S.misc + 16);
-  S.xown = reinterpret_cast<__half*>(S.inv_freq + kHD / 2);
+  S.lp = reinterpret_cast<LayerPtrs*>(S.misc + 16);
+  S.xown = reinterpret_cast<__half*>(S.lp + P.m.n_layers);
   S.x1own = S.xown + kMaxB * kOwnMax;
   S.bias_own = S.x1own + kMaxB * kOwnMax;
   // tag base of this launch (CTA 0 advances it after every CTA has used it)
   const uint32_t epoch = __ldcg(P.epoch);
-  for (int i = threadIdx.x; i < kHD / 2; i += blockDim.x) S.inv_freq[i] = P.m.inv_freq[i];
+  for (int i = threadIdx.x; i < P.m.n_layers; i += blockDim.x) {
+    const lmps_layer_desc& L = P.m.layers[i];
+    S.lp[i] = LayerPtrs{reinterpret_cast<const __half*>(L.in_norm), reinterpret_cast<const __half*>(L.post_norm),
+                        reinterpret_cast<__half*>(L.k_pool), reinterpret_cast<__half*>(L.v_pool)};
+  }
   {  // q|k|v bias of this CTA's qkv rows, every layer
     const int qkv_rows = (P.m.n_q_heads + 2 * P.m.n_kv_heads) * kHD;
     int q0, q1;
@@ -1554,8 +1587,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
 static int tail_bytes(int n_layers) {
   const size_t fixed = 32 * sizeof(uint64_t) +
                        kConsumerWarps * kMaxB * (sizeof(float) + sizeof(unsigned long long)) + 16 * sizeof(int) +
-                       kHD / 2 * sizeof(float) + 2 * kOwnMax * kMaxB * sizeof(__half);
-  const size_t t = fixed + static_cast<size_t>(n_layers) * kOwnMax * sizeof(__half);
+                       2 * kOwnMax * kMaxB * sizeof(__half);
+  const size_t t = fixed + static_cast<size_t>(n_layers) * (kOwnMax * sizeof(__half) + sizeof(LayerPtrs));
   return static_cast<int>((t + 127) & ~static_cast<size_t>(127));
 }
 
@@ -1593,10 +1626,12 @@ static int act_bytes_for(const lmps_model_desc& m, int nb) {
   size_t a = sizeof(AttnSmem);
   const size_t grp = 16 * 4 + 4 + 4;  // plane words + scl + xs8 per group
   // k = hidden stages: planes + per-lane partials of every row entry
-  const size_t hid = static_cast<size_t>(nb) * (m.hidden / 32) * grp + static_cast<size_t>(nb) * kPartRows * 16 * 4;
+  // (+16: the partials start 16-byte aligned)
+  const size_t hid =
+      static_cast<size_t>(nb) * (m.hidden / 32) * grp + static_cast<size_t>(nb) * kPartRows * 16 * 4 + 16;
   // down projection: planes + one partial per (row, warp)
   const size_t dn = static_cast<size_t>(nb) * (m.intermediate / 32) * grp +
-                    static_cast<size_t>(nb) * kOwnMax * kConsumerWarps * 4;
+                    static_cast<size_t>(nb) * kOwnMax * kRedStride * 4 + 16;
   a = a > hid ? a : hid;
   a = a > dn ? a : dn;
   return static_cast<int>((a + 127) & ~static_cast<size_t>(127));
@@ -1673,9 +1708,10 @@ extern "C" int lmps_decode_persistent(const lmps_model_desc* model, const lmps_d
       static_cast<size_t>(pk::kRowsDown) * (m.intermediate / 2 + m.intermediate / 16) > pk::kSlotBytes)
     return LMPS_ERR_UNSUPPORTED;
   LMPS_CHECK_ARG(s.batch >= 1 && s.batch <= pk::kMaxB);
-  LMPS_CHECK_ARG(s.block_table && s.tokens && s.pos && s.workspace && s.error);
-  LMPS_CHECK_ARG(s.page_size > 0 && s.max_pages > 0 && s.max_seq_len > 0 &&
-                 s.max_seq_len <= s.max_pages * s.page_size);
+  LMPS_CHECK_ARG(s.block_table && s.rope_table && s.tokens && s.pos && s.workspace && s.error);
+  LMPS_CHECK_ARG(s.page_size > 0 && (s.page_size & (s.page_size - 1)) == 0 && s.max_pages > 0 &&
+                 s.max_seq_len > 0 && s.max_seq_len <= s.max_pages * s.page_size);
+  LMPS_CHECK_ARG(lmps_aligned(s.rope_table, 16));
   LMPS_CHECK_ARG(!s.forced || s.forced_stride >= s.n_forced);
   LMPS_CHECK_ARG(!s.history || (s.step_counter && s.history_rows > 0));
   const pk::WsLayout w = pk::ws_layout(m, s.batch, s.max_seq_len);

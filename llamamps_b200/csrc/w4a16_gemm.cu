@@ -9,38 +9,50 @@
 // nibble of byte b, fp16 scales [N, K/32], w = (nibble - 8) * scale
 // (quant_matmul.metal:39-47).
 //
-// One CTA computes a 128 x 128 tile of Y over K in steps of 64:
-//   * all four warps stage the step's X tile (128 tokens x 64) and dequantise
-//     the W tile (128 rows x 64, fp16 (nibble - 8) * scale) into shared
-//     memory, in the 128-byte-swizzled K-major layout the tensor core reads
-//     (16-byte chunk c of row r at chunk c ^ (r % 8));
-//   * one thread issues four tcgen05.mma.kind::f16 (K = 16 each; M = 128
-//     tokens, N = 128 rows) into the TMEM accumulator and commits them to the
-//     stage's mbarrier, so the next step's staging overlaps the MMAs (two
-//     stages);
-//   * the epilogue reads the accumulator with tcgen05.ld (warp w owns TMEM
-//     lanes 32w..32w+31 = tokens), applies bias / residual and writes fp16.
+// One CTA owns 128 weight rows and a tile of tokens, over K in stages of 64
+// (one 128-byte swizzle atom of fp16).  Warp-specialised pipeline:
+//   * warp 0 (one lane) issues the TMA loads of a stage: the X tile (tokens x
+//     64, written by the TMA unit in the 128-byte-swizzled K-major layout the
+//     tensor core reads) and the packed W tile (128 rows x 32 bytes);
+//   * warps 2-5 dequantise the packed tile (thread t = weight row t) into a
+//     swizzled fp16 tile: (nibble | 0x6400) is the fp16 1024 + nibble, minus
+//     1032 gives nibble - 8 exactly, times the group scale rounds once;
+//   * warp 1 (one lane) issues four tcgen05.mma (K = 16 each) per stage and
+//     commits them to the stage's `empty` barrier, which frees the stage for
+//     the next TMA load and dequantisation;
+//   * warps 2-5 then read the accumulator (tcgen05.ld; warp w reads TMEM
+//     lanes 32 (w % 4) ..) and apply bias / residual.
+// Two tile shapes share the pipeline:
+//   * tokens >= 128 (prefill): A = X (M = 128 tokens), B = W (N = 128 rows);
+//   * fewer tokens (decode batches): A = W (M = 128 rows), B = X (N = the
+//     token count rounded up to 16), so no tensor-core row is padding and W
+//     is read once.  K is then split across the CTAs of a thread-block
+//     cluster to fill the GPU; the fp32 partial tiles are summed through
+//     distributed shared memory, each CTA finishing a slice of the rows.
 // Every mbarrier wait is bounded (error flag, no hang).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 
 namespace lmps {
 namespace w4 {
 
-constexpr int kBM = 128;  // tokens per tile (TMEM lanes)
-constexpr int kBN = 128;  // weight rows per tile (TMEM columns)
-constexpr int kBK = 64;   // K per stage: one 128-byte swizzle atom of fp16
-constexpr int kStages = 2;
-constexpr int kThreads = 128;
-constexpr uint32_t kTmemCols = 128;
-constexpr int kTileBytes = kBM * kBK * 2;
+constexpr int kBK = 64;        // K per stage
+constexpr int kRows = 128;     // weight rows per tile
+constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 dequantise + epilogue
+constexpr int kMaxStages = 8;
+constexpr int kMaxSplits = 8;  // K splits of a tile = CTAs of one (portable) cluster
+constexpr int kScaleAhead = 6; // K steps a dequantising thread's scale loads run ahead
+constexpr int kStepBytes = kRows * kBK / 2;   // packed W bytes of one K step (4 KB)
+constexpr int kWTileBytes = kRows * kBK * 2;  // 16 KB fp16
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
 
 enum Epilogue { EPI_NONE = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2 };
 
-struct Params {
-  const __half* x;
-  int ldx;
-  const uint8_t* w;
+struct __align__(64) Params {
+  CUtensorMap tx;  // X [m, k] fp16, box {64, xrows}, 128-byte swizzle
+  CUtensorMap tw;  // packed W [n, k/2] u8, box {128, 128}, 128-byte swizzle
   const __half* s;
   const __half* bias;
   const __half* res;
@@ -48,12 +60,14 @@ struct Params {
   __half* y;
   int ldy;
   int m, n, k, epi;
+  int swap;    // 1: A = W (M = 128 rows), B = X (N = xrows tokens)
+  int xrows;   // tokens per tile: 128, or (swap) 16..256 in steps of 16
+  int xstages;  // X tiles in flight
+  int dstages;  // dequantised W tiles
+  int wslots;   // packed-W blocks in flight
+  int wspb;     // K steps per packed-W block: 4 (128-byte rows, 128-byte swizzle) or 1 (32-byte rows)
   int* error;
-  // split-K (gridDim.z > 1): fp32 partial tiles meet in acc32 [m_tiles*128, n]
-  // (zero between calls); the last CTA of a tile finishes it and re-zeroes it
-  float* acc32;
-  uint32_t* tile_cnt;  // [m_tiles * n_tiles], zero between calls
-  int ksteps_per_split;
+  int ksteps_per_split;  // split K (gridDim.z > 1, swap tiles): K steps per cluster CTA
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -78,18 +92,30 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 
 // Instruction descriptor of kind::f16: fp16 A and B, fp32 D, both K-major,
 // N >> 3 at bit 17, M >> 4 at bit 24.
-constexpr uint32_t kIdesc = (1u << 4) | (static_cast<uint32_t>(kBN >> 3) << 17) |
-                            (static_cast<uint32_t>(kBM >> 4) << 24);
+__device__ __forceinline__ uint32_t idesc_f16(int m, int n) {
+  return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
 
-__device__ __forceinline__ void mma_f16(uint32_t tmem, uint64_t adesc, uint64_t bdesc, uint32_t acc) {
+__device__ __forceinline__ void mma_f16(uint32_t tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(acc)
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
       : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                : "memory");
 }
 __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
@@ -102,60 +128,404 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait of the whole CTA for a phase of `bar`; false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+// Bounded wait for a phase of `bar`: false when the CTA is aborting or the
+// wait timed out (which raises the error flag and the CTA's abort flag).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (!mbar_try(bar, parity)) {
+    if (*abort_flag) return false;
     if (globaltimer() - t0 > kTimeoutNs) {
       atomicExch(err, 1);
+      *abort_flag = 1;
       return false;
     }
   }
   return true;
 }
-
-// fp16 (nibble - 8) * scale of 8 consecutive elements (4 packed bytes).
-__device__ __forceinline__ uint4 dequant8(uint32_t packed, __half scale) {
-  const __half2 s2 = __halves2half2(scale, scale);
-  uint32_t out[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const uint32_t byte = (packed >> (8 * e)) & 0xFFu;
-    const __half lo = __int2half_rn(static_cast<int>(byte & 0xFu) - 8);
-    const __half hi = __int2half_rn(static_cast<int>(byte >> 4) - 8);
-    const __half2 v = __hmul2(__halves2half2(lo, hi), s2);
-    out[e] = *reinterpret_cast<const uint32_t*>(&v);
-  }
-  return make_uint4(out[0], out[1], out[2], out[3]);
+// 2-D tiled TMA load (no multicast) into this CTA's shared memory.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
 }
 
-__global__ void __launch_bounds__(kThreads, 1) w4a16_gemm_kernel(const __grid_constant__ Params P) {
+// 4-byte asynchronous global -> shared copy (completion by commit groups).
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// fp16 (nibble - 8) * scale of the 8 elements of one packed word, in element
+// order.  Halves of t_i hold the nibbles (i, i + 4) as 1024 + n.
+__device__ __forceinline__ uint4 dequant8(uint32_t w, __half2 s2) {
+  const __half2 k1032 = __halves2half2(__ushort_as_half(0x6408u), __ushort_as_half(0x6408u));
+  uint32_t t[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t v = ((w >> (4 * i)) & 0x000F000Fu) | 0x64006400u;
+    const __half2 h = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&v), k1032), s2);
+    t[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(__byte_perm(t[0], t[1], 0x5410), __byte_perm(t[2], t[3], 0x5410),
+                    __byte_perm(t[0], t[1], 0x7632), __byte_perm(t[2], t[3], 0x7632));
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Y[row][col] from an fp32 accumulator value and the epilogue operands.
+__device__ __forceinline__ __half epi_value(const Params& P, float v, int row, int col) {
+  if (P.epi == EPI_BIAS) return __float2half_rn(v + __half2float(P.bias[col]));
+  if (P.epi == EPI_RESIDUAL) return __hadd(P.res[static_cast<size_t>(row) * P.ldr + col], __float2half_rn(v));
+  return __float2half_rn(v);
+}
+
+__global__ void __launch_bounds__(kThreads) w4a16_gemm_kernel(const __grid_constant__ Params P) {
   extern __shared__ unsigned char smem_raw[];
-  // 1024-byte aligned operand tiles
+  const int SX = P.xstages, SD = P.dstages, R = P.wslots, SPB = P.wspb;
+  const int wblk = kStepBytes * SPB;
+  const int xbytes = P.xrows * 128;
+  // 1024-byte aligned rings: [R] packed W blocks (128 rows x 128 bytes = 4 K
+  // steps, 128-byte swizzle), [SX] X tiles, [SD] dequantised W tiles
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  unsigned char* a_tiles = base;                                   // [kStages][16 KB]
-  unsigned char* b_tiles = base + kStages * kTileBytes;            // [kStages][16 KB]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base + 2 * kStages * kTileBytes);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kStages);
+  unsigned char* wr = base;
+  unsigned char* xs = wr + static_cast<size_t>(R) * wblk;
+  unsigned char* wd = xs + static_cast<size_t>(SX) * xbytes;
+  uint64_t* fullw = reinterpret_cast<uint64_t*>(wd + static_cast<size_t>(SD) * kWTileBytes);
+  uint64_t* emptyw = fullw + kMaxStages;
+  uint64_t* fullx = emptyw + kMaxStages;
+  uint64_t* emptyx = fullx + kMaxStages;
+  uint64_t* deq = emptyx + kMaxStages;
+  uint64_t* emptyd = deq + kMaxStages;
+  uint64_t* done = emptyd + kMaxStages;
+  uint32_t* scale_ring = reinterpret_cast<uint32_t*>(done + 1);  // [kScaleAhead][128]
+  uint32_t* tmem_slot = scale_ring + kScaleAhead * 128;
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  volatile int* abort_v = abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
-  const int K = P.k;
+  const int n0 = blockIdx.x * kRows, m0 = blockIdx.y * P.xrows;
   const int kbeg = blockIdx.z * P.ksteps_per_split;
-  const int ksteps = min(P.ksteps_per_split, K / kBK - kbeg);
+  const int ksteps = max(0, min(P.ksteps_per_split, P.k / kBK - kbeg));
+  const int nwb = (ksteps + SPB - 1) / SPB;  // packed W blocks of this CTA
+  const uint32_t tcols = P.swap ? (P.xrows <= 32 ? 32u : P.xrows <= 64 ? 64u : P.xrows <= 128 ? 128u : 256u) : 128u;
+  // split K (swap tiles only): CTA c of the cluster receives, from every
+  // split, the partial rows [c * 128 / splits, ..) of the tile, fp32, in the
+  // pipeline buffers (idle by then): [splits][128 / splits][xrows + 4]
+  const bool split = gridDim.z > 1;
+  float* red = reinterpret_cast<float*>(base);
+  const int rs = P.xrows + 4;
 
   if (tid == 0) {
-    for (int i = 0; i < kStages; ++i)
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bars[i])) : "memory");
+    for (int i = 0; i < R; ++i) {
+      mbar_init(&fullw[i], 1);
+      mbar_init(&emptyw[i], 128);
+    }
+    for (int i = 0; i < SX; ++i) {
+      mbar_init(&fullx[i], 1);
+      mbar_init(&emptyx[i], 1);
+    }
+    for (int i = 0; i < SD; ++i) {
+      mbar_init(&deq[i], 128);
+      mbar_init(&emptyd[i], 1);
+    }
+    mbar_init(done, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 0) {
+  if (tid == 64) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&P.tx)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&P.tw)) : "memory");
+  }
+  if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kTmemCols)
+                 "r"(tcols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  // ---- TMA producer (thread 0).  Packed W blocks run up to R blocks (4R K
+  // steps) ahead, X tiles SX steps; the loads that need no free slot go out
+  // before the block-wide sync.
+  int wk = 0, xk = 0;
+  auto issue_w = [&]() {
+    mbar_expect_tx(&fullw[wk % R], static_cast<uint32_t>(wblk));
+    tma_load_2d(wr + static_cast<size_t>(wk % R) * wblk, &P.tw, (kbeg + wk * SPB) * (kBK / 2), n0,
+                &fullw[wk % R]);
+    ++wk;
+  };
+  auto issue_x = [&]() {
+    mbar_expect_tx(&fullx[xk % SX], static_cast<uint32_t>(xbytes));
+    tma_load_2d(xs + static_cast<size_t>(xk % SX) * xbytes, &P.tx, (kbeg + xk) * kBK, m0, &fullx[xk % SX]);
+    ++xk;
+  };
+  if (tid == 0) {
+    while (wk < nwb && wk < R) issue_w();
+    while (xk < ksteps && xk < SX) issue_x();
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (tid == 0) {
+    uint64_t t0 = globaltimer();
+    while (wk < nwb || xk < ksteps) {
+      bool progress = false;
+      if (wk < nwb && mbar_try(&emptyw[wk % R], ((wk / R) - 1) & 1)) {
+        issue_w();
+        progress = true;
+      }
+      if (xk < ksteps && mbar_try(&emptyx[xk % SX], ((xk / SX) - 1) & 1)) {
+        issue_x();
+        progress = true;
+      }
+      if (progress) {
+        t0 = globaltimer();
+      } else if (*abort_v || globaltimer() - t0 > kTimeoutNs) {
+        if (!*abort_v) {
+          atomicExch(P.error, 1);
+          *abort_flag = 1;
+        }
+        break;
+      }
+    }
+    // every issued copy lands before the CTA may exit
+    for (int b = max(0, wk - R); b < wk; ++b) {
+      const uint64_t t1 = globaltimer();
+      while (!mbar_try(&fullw[b % R], (b / R) & 1))
+        if (globaltimer() - t1 > kTimeoutNs) break;
+    }
+    for (int kt = max(0, xk - SX); kt < xk; ++kt) {
+      const uint64_t t1 = globaltimer();
+      while (!mbar_try(&fullx[kt % SX], (kt / SX) & 1))
+        if (globaltimer() - t1 > kTimeoutNs) break;
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = P.swap ? idesc_f16(128, P.xrows) : idesc_f16(128, 128);
+      for (int kt = 0; kt < ksteps; ++kt) {
+        const int sx = kt % SX, sd = kt % SD;
+        if (!mbar_wait(&fullx[sx], (kt / SX) & 1, P.error, abort_v)) break;
+        if (!mbar_wait(&deq[sd], (kt / SD) & 1, P.error, abort_v)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint64_t xd = sw128_desc(smem_u32(xs + static_cast<size_t>(sx) * xbytes));
+        const uint64_t wdd = sw128_desc(smem_u32(wd + static_cast<size_t>(sd) * kWTileBytes));
+        const uint64_t ad = P.swap ? wdd : xd, bd = P.swap ? xd : wdd;
+#pragma unroll
+        for (int j = 0; j < kBK / 16; ++j)  // K = 16 per MMA: 32 bytes further into the swizzle atom
+          mma_f16(tmem, ad + 2 * j, bd + 2 * j, idesc, (kt > 0 || j > 0) ? 1u : 0u);
+        mma_commit(&emptyx[sx]);
+        mma_commit(&emptyd[sd]);
+      }
+      mma_commit(done);  // tracks every MMA issued above
+    }
+  } else if (warp >= 2) {
+    // ---- dequantisation (thread t = weight row n0 + t)
+    const int t = tid - 64;
+    const uint32_t* srow = reinterpret_cast<const uint32_t*>(P.s + static_cast<size_t>(n0 + t) * (P.k / 32) + 2 * kbeg);
+    // The two group scales of a step arrive kScaleAhead steps early through
+    // cp.async into this thread's slots of a shared-memory ring (one commit
+    // group per step, empty groups included, so wait_group counts steps).
+    uint32_t* sring = scale_ring + t;
+#pragma unroll
+    for (int i = 0; i < kScaleAhead; ++i) {
+      if (i < ksteps) cp_async4(sring + i * 128, srow + i);
+      cp_async_commit();
+    }
+    const int sw = t & 7;
+    for (int kt = 0; kt < ksteps; ++kt) {
+      const int s = kt % SD, wb = kt / SPB, wsl = wb % R, sub = kt % SPB;
+      cp_async_wait<kScaleAhead - 1>();
+      const int slot = kt % kScaleAhead;
+      const uint32_t sc = sring[slot * 128];
+      if (kt + kScaleAhead < ksteps) cp_async4(sring + slot * 128, srow + kt + kScaleAhead);
+      cp_async_commit();
+      if (sub == 0 && !mbar_wait(&fullw[wsl], (wb / R) & 1, P.error, abort_v)) break;
+      if (kt >= SD && !mbar_wait(&emptyd[s], ((kt / SD) - 1) & 1, P.error, abort_v)) break;  // MMA done with wd[s]
+      // packed row t, bytes 32 sub .. 32 sub + 31: 16-byte chunks 2 sub and
+      // 2 sub + 1 of a 32 SPB-byte row (128-byte rows are swizzled)
+      const unsigned char* rrow = wr + static_cast<size_t>(wsl) * wblk + t * (32 * SPB);
+      const int rsw = SPB == 4 ? sw : 0;
+      const uint4 g0 = *reinterpret_cast<const uint4*>(rrow + (((2 * sub) ^ rsw) << 4));
+      const uint4 g1 = *reinterpret_cast<const uint4*>(rrow + (((2 * sub + 1) ^ rsw) << 4));
+      if (sub == SPB - 1 || kt == ksteps - 1) mbar_arrive(&emptyw[wsl]);  // packed block consumed
+      const __half2 sc2 = *reinterpret_cast<const __half2*>(&sc);
+      const __half2 s0 = __low2half2(sc2), s1 = __high2half2(sc2);
+      unsigned char* row = wd + static_cast<size_t>(s) * kWTileBytes + t * 128;
+      *reinterpret_cast<uint4*>(row + ((0 ^ sw) << 4)) = dequant8(g0.x, s0);
+      *reinterpret_cast<uint4*>(row + ((1 ^ sw) << 4)) = dequant8(g0.y, s0);
+      *reinterpret_cast<uint4*>(row + ((2 ^ sw) << 4)) = dequant8(g0.z, s0);
+      *reinterpret_cast<uint4*>(row + ((3 ^ sw) << 4)) = dequant8(g0.w, s0);
+      *reinterpret_cast<uint4*>(row + ((4 ^ sw) << 4)) = dequant8(g1.x, s1);
+      *reinterpret_cast<uint4*>(row + ((5 ^ sw) << 4)) = dequant8(g1.y, s1);
+      *reinterpret_cast<uint4*>(row + ((6 ^ sw) << 4)) = dequant8(g1.z, s1);
+      *reinterpret_cast<uint4*>(row + ((7 ^ sw) << 4)) = dequant8(g1.w, s1);
+      // generic-proxy shared-memory writes -> visible to the tensor core
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive(&deq[s]);
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");  // no copy in flight past the loop (abort path)
+  }
+  // ---- epilogue (warps 2-5: warp w reads TMEM lanes 32 (w % 4) ..)
+  __syncwarp();
+  const bool epi_warp = warp >= 2;
+  bool ok = false;
+  if (epi_warp) {
+    ok = ksteps > 0 && mbar_wait(done, 0, P.error, abort_v);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  }
+  const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
+  const uint32_t tl = tmem + (static_cast<uint32_t>(32 * q) << 16);
+  if (split) {
+    // Reduce-scatter over the cluster.  Barrier 1: every CTA is past its
+    // main loop, so its pipeline buffers may receive partial rows.
+    asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+    uint32_t rank;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+    const int nsplit = gridDim.z, rows_per = kRows / nsplit;
+    if (epi_warp) {
+      const int row = 32 * q + lane;  // weight row within the tile
+      const uint32_t dst = static_cast<uint32_t>(row / rows_per);
+      const uint32_t laddr =
+          smem_u32(red) + static_cast<uint32_t>(((static_cast<int>(rank) * rows_per + row % rows_per) * rs) * 4);
+      uint32_t raddr;
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(raddr) : "r"(laddr), "r"(dst));
+      for (int c0 = 0; c0 < P.xrows; c0 += 32) {
+        uint32_t r[32];
+        if (ok) {
+          tmem_ld32(tl + c0, r);
+        } else {  // no K steps (or aborted): this split adds zeros
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = 0u;
+        }
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          if (c0 + j < P.xrows)
+            asm volatile("st.shared::cluster.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(raddr + (c0 + j) * 4),
+                         "f"(__uint_as_float(r[j])), "f"(__uint_as_float(r[j + 1])), "f"(__uint_as_float(r[j + 2])),
+                         "f"(__uint_as_float(r[j + 3]))
+                         : "memory");
+      }
+    }
+    // Barrier 2: every partial row has arrived; each CTA sums and writes its rows.
+    asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+    const int tok = min(P.xrows, P.m - m0), tok4 = (tok + 3) / 4;
+    for (int i = tid; i < rows_per * tok4; i += kThreads) {
+      const int lr = i % rows_per, j = 4 * (i / rows_per);
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c = 0; c < nsplit; ++c) {
+        const float4 v = *reinterpret_cast<const float4*>(red + (c * rows_per + lr) * rs + j);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      const float a[4] = {acc.x, acc.y, acc.z, acc.w};
+      const int col = n0 + static_cast<int>(rank) * rows_per + lr;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int rw = m0 + j + e;
+        if (j + e < tok) P.y[static_cast<size_t>(rw) * P.ldy + col] = epi_value(P, a[e], rw, col);
+      }
+    }
+  } else if (ok && P.swap) {
+    // lane = weight row n0 + 32q + lane, columns = tokens m0 ..
+    const int col = n0 + 32 * q + lane;
+    for (int c0 = 0; c0 < P.xrows; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld32(tl + c0, r);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int rw = m0 + c0 + j;
+        if (rw < P.m) P.y[static_cast<size_t>(rw) * P.ldy + col] = epi_value(P, __uint_as_float(r[j]), rw, col);
+      }
+    }
+  } else if (ok) {
+    // lane = token m0 + 32q + lane, columns = weight rows n0 ..
+    const int rw = m0 + 32 * q + lane;
+#pragma unroll 1
+    for (int c0 = 0; c0 < kRows; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld32(tl + c0, r);
+      if (rw < P.m) {
+        __half* yrow = P.y + static_cast<size_t>(rw) * P.ldy + n0 + c0;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {  // 8 columns per 16-byte store
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int cc = n0 + c0 + 8 * g + 2 * e;
+            const __half2 hh = __halves2half2(epi_value(P, __uint_as_float(r[8 * g + 2 * e]), rw, cc),
+                                              epi_value(P, __uint_as_float(r[8 * g + 2 * e + 1]), rw, cc + 1));
+            o[e] = *reinterpret_cast<const uint32_t*>(&hh);
+          }
+          *reinterpret_cast<uint4*>(yrow + 8 * g) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols) : "memory");
+}
+
+// Prefill tiles (128 tokens x 128 weight rows): one ring of S stages, each
+// holding the X tile, the step's packed W (128 rows x 32 bytes, one TMA
+// box) and the dequantised W tile.  Warp 0 lane 0 loads, warps 2-5
+// dequantise and then run the epilogue, warp 1 lane 0 issues the MMAs.
+__global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid_constant__ Params P) {
+  extern __shared__ unsigned char smem_raw[];
+  const int S = P.xstages;
+  constexpr int kX = 128 * 128;  // X tile bytes
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  unsigned char* xs = base;
+  unsigned char* wd = xs + static_cast<size_t>(S) * kX;
+  unsigned char* wr = wd + static_cast<size_t>(S) * kWTileBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(wr + static_cast<size_t>(S) * kStepBytes);
+  uint64_t* deq = full + kMaxStages;
+  uint64_t* empty = deq + kMaxStages;
+  uint64_t* done = empty + kMaxStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  volatile int* abort_v = abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = blockIdx.x * kRows, m0 = blockIdx.y * 128;
+  const int ksteps = P.k / kBK;
+  if (tid == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&deq[i], 128);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(128)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -164,199 +534,164 @@ __global__ void __launch_bounds__(kThreads, 1) w4a16_gemm_kernel(const __grid_co
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
 
-  // Global loads run one K step ahead of the shared-memory stores: step
-  // kt+1's X rows and packed weights are in flight while step kt is staged
-  // and its MMAs are issued.
-  constexpr int kPer = (kBM * kBK / 8) / kThreads;  // 16-byte chunks per thread and operand
-  uint4 xr[kPer];
-  uint32_t wr[kPer];
-  __half sr[kPer];
-  auto load_step = [&](int kt) {
-    const int k0 = (kbeg + kt) * kBK;
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const int idx = tid + i * kThreads, r = idx >> 3, c = idx & 7;
-      xr[i] = (m0 + r < P.m) ? __ldg(reinterpret_cast<const uint4*>(P.x + static_cast<size_t>(m0 + r) * P.ldx + k0 + 8 * c))
-                             : make_uint4(0u, 0u, 0u, 0u);
-      const size_t row = static_cast<size_t>(n0 + r);
-      wr[i] = __ldg(reinterpret_cast<const uint32_t*>(P.w + row * (K / 2) + (k0 + 8 * c) / 2));
-      sr[i] = P.s[row * (K / 32) + (k0 + 8 * c) / 32];
-    }
-  };
-  if (ksteps > 0) load_step(0);
-  for (int kt = 0; kt < ksteps; ++kt) {
-    const int st = kt % kStages;
-    if (kt >= kStages) {  // the MMAs that read this stage two steps ago are done
-      if (tid == 0 && !mbar_wait(&bars[st], (kt / kStages - 1) & 1, P.error)) *abort_flag = 1;
-      __syncthreads();
-      if (*abort_flag) break;
-    }
-    unsigned char* at = a_tiles + st * kTileBytes;
-    unsigned char* bt = b_tiles + st * kTileBytes;
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const int idx = tid + i * kThreads, r = idx >> 3, c = idx & 7;
-      *reinterpret_cast<uint4*>(at + r * 128 + ((c ^ (r & 7)) << 4)) = xr[i];
-      *reinterpret_cast<uint4*>(bt + r * 128 + ((c ^ (r & 7)) << 4)) = dequant8(wr[i], sr[i]);
-    }
-    if (kt + 1 < ksteps) load_step(kt + 1);
-    // generic-proxy shared-memory writes -> visible to the tensor core
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncthreads();
-    if (tid == 0) {
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint64_t ad = sw128_desc(smem_u32(at)), bd = sw128_desc(smem_u32(bt));
-#pragma unroll
-      for (int j = 0; j < kBK / 16; ++j)  // K = 16 per MMA: 32 bytes further into the swizzle atom
-        mma_f16(tmem, ad + 2 * j, bd + 2 * j, (kt > 0 || j > 0) ? 1u : 0u);
-      mma_commit(&bars[st]);
-    }
-  }
-  // all MMAs done (the last commit covers every earlier one)
-  if (!*abort_flag && ksteps > 0) {
-    const int last = ksteps - 1;
-    if (tid == 0 && !mbar_wait(&bars[last % kStages], (last / kStages) & 1, P.error)) *abort_flag = 1;
-  }
-  __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const bool split = gridDim.z > 1;
-  if (!*abort_flag && split) {
-    // fp32 partial tile -> acc32 (red.add); the last split of the tile finishes it
-    const int trow = m0 + warp * 32 + lane;
-#pragma unroll 1
-    for (int cc = 0; cc < kBN / 32; ++cc) {
-      uint32_t r[32];
-      const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16) + cc * 32;
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-          "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-          : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-            "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-            "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-            "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-          : "r"(taddr)
-          : "memory");
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      if (trow < P.m) {
-        float* dst = P.acc32 + static_cast<size_t>(trow) * P.n + n0 + cc * 32;
-#pragma unroll
-        for (int j = 0; j < 32; j += 4)
-          asm volatile("red.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(dst + j), "f"(__uint_as_float(r[j])),
-                       "f"(__uint_as_float(r[j + 1])), "f"(__uint_as_float(r[j + 2])), "f"(__uint_as_float(r[j + 3]))
-                       : "memory");
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer
+      int issued = 0;
+      for (int kt = 0; kt < ksteps; ++kt) {
+        const int s = kt % S;
+        if (kt >= S && !mbar_wait(&empty[s], ((kt / S) - 1) & 1, P.error, abort_v)) break;
+        mbar_expect_tx(&full[s], static_cast<uint32_t>(kX + kStepBytes));
+        tma_load_2d(xs + static_cast<size_t>(s) * kX, &P.tx, kt * kBK, m0, &full[s]);
+        tma_load_2d(wr + static_cast<size_t>(s) * kStepBytes, &P.tw, kt * (kBK / 2), n0, &full[s]);
+        issued = kt + 1;
+      }
+      for (int kt = max(0, issued - S); kt < issued; ++kt) {  // every issued copy lands before exit
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try(&full[kt % S], (kt / S) & 1))
+          if (globaltimer() - t0 > kTimeoutNs) break;
       }
     }
-    __threadfence();
-    __syncthreads();
-    uint32_t* cnt = P.tile_cnt + blockIdx.y * gridDim.x + blockIdx.x;
-    if (tid == 0) *abort_flag = (atomicAdd(cnt, 1u) == gridDim.z - 1) ? 2 : 0;
-    __syncthreads();
-    if (*abort_flag == 2) {  // last split of this tile: epilogue from acc32, then clear it
-      __threadfence();
-      for (int i = tid; i < kBM * (kBN / 8); i += kThreads) {
-        const int rr = i / (kBN / 8), c8 = i - rr * (kBN / 8);
-        const int row = m0 + rr;
-        if (row >= P.m) continue;
-        float* src = P.acc32 + static_cast<size_t>(row) * P.n + n0 + 8 * c8;
-        const float4 a = __ldcg(reinterpret_cast<const float4*>(src));
-        const float4 b = __ldcg(reinterpret_cast<const float4*>(src + 4));
-        const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        *reinterpret_cast<float4*>(src) = make_float4(0.f, 0.f, 0.f, 0.f);
-        *reinterpret_cast<float4*>(src + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
-        const int col = n0 + 8 * c8;
-        uint32_t o[4];
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---- MMA issuer
+      const uint32_t idesc = idesc_f16(128, 128);
+      for (int kt = 0; kt < ksteps; ++kt) {
+        const int s = kt % S;
+        if (!mbar_wait(&deq[s], (kt / S) & 1, P.error, abort_v)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint64_t ad = sw128_desc(smem_u32(xs + static_cast<size_t>(s) * kX));
+        const uint64_t bd = sw128_desc(smem_u32(wd + static_cast<size_t>(s) * kWTileBytes));
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          __half h0, h1;
-          if (P.epi == EPI_BIAS) {
-            h0 = __float2half_rn(v[2 * e] + __half2float(P.bias[col + 2 * e]));
-            h1 = __float2half_rn(v[2 * e + 1] + __half2float(P.bias[col + 2 * e + 1]));
-          } else if (P.epi == EPI_RESIDUAL) {
-            const __half* rr2 = P.res + static_cast<size_t>(row) * P.ldr + col + 2 * e;
-            h0 = __hadd(rr2[0], __float2half_rn(v[2 * e]));
-            h1 = __hadd(rr2[1], __float2half_rn(v[2 * e + 1]));
-          } else {
-            h0 = __float2half_rn(v[2 * e]);
-            h1 = __float2half_rn(v[2 * e + 1]);
-          }
-          const __half2 hh = __halves2half2(h0, h1);
-          o[e] = *reinterpret_cast<const uint32_t*>(&hh);
-        }
-        *reinterpret_cast<uint4*>(P.y + static_cast<size_t>(row) * P.ldy + col) = make_uint4(o[0], o[1], o[2], o[3]);
+        for (int j = 0; j < kBK / 16; ++j)
+          mma_f16(tmem, ad + 2 * j, bd + 2 * j, idesc, (kt > 0 || j > 0) ? 1u : 0u);
+        mma_commit(&empty[s]);
       }
-      if (tid == 0) *cnt = 0u;
+      mma_commit(done);
     }
-  }
-  if (!*abort_flag && !split) {
-    const int row = m0 + warp * 32 + lane;  // token of this thread's TMEM lane
+  } else {
+    // ---- dequantisation (thread t = weight row n0 + t); the full barrier of
+    // a stage completes only after the MMAs that last read it (the producer
+    // waited for them before refilling), so wd[s] is free once it is full
+    const int t = tid - 64, sw = t & 7;
+    const uint32_t* srow = reinterpret_cast<const uint32_t*>(P.s + static_cast<size_t>(n0 + t) * (P.k / 32));
+    uint32_t sc_next = ksteps > 0 ? __ldg(srow) : 0u;
+    for (int kt = 0; kt < ksteps; ++kt) {
+      const int s = kt % S;
+      const uint32_t sc = sc_next;
+      if (kt + 1 < ksteps) sc_next = __ldg(srow + kt + 1);
+      if (!mbar_wait(&full[s], (kt / S) & 1, P.error, abort_v)) break;
+      const uint4* raw = reinterpret_cast<const uint4*>(wr + static_cast<size_t>(s) * kStepBytes + t * 32);
+      const uint4 g0 = raw[0], g1 = raw[1];
+      const __half2 sc2 = *reinterpret_cast<const __half2*>(&sc);
+      const __half2 s0 = __low2half2(sc2), s1 = __high2half2(sc2);
+      unsigned char* row = wd + static_cast<size_t>(s) * kWTileBytes + t * 128;
+      *reinterpret_cast<uint4*>(row + ((0 ^ sw) << 4)) = dequant8(g0.x, s0);
+      *reinterpret_cast<uint4*>(row + ((1 ^ sw) << 4)) = dequant8(g0.y, s0);
+      *reinterpret_cast<uint4*>(row + ((2 ^ sw) << 4)) = dequant8(g0.z, s0);
+      *reinterpret_cast<uint4*>(row + ((3 ^ sw) << 4)) = dequant8(g0.w, s0);
+      *reinterpret_cast<uint4*>(row + ((4 ^ sw) << 4)) = dequant8(g1.x, s1);
+      *reinterpret_cast<uint4*>(row + ((5 ^ sw) << 4)) = dequant8(g1.y, s1);
+      *reinterpret_cast<uint4*>(row + ((6 ^ sw) << 4)) = dequant8(g1.z, s1);
+      *reinterpret_cast<uint4*>(row + ((7 ^ sw) << 4)) = dequant8(g1.w, s1);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive(&deq[s]);
+    }
+    // ---- epilogue: lane = token m0 + 32q + lane, columns = weight rows n0 ..
+    const bool ok = ksteps > 0 && mbar_wait(done, 0, P.error, abort_v);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const int q = warp & 3;
+    const uint32_t tl = tmem + (static_cast<uint32_t>(32 * q) << 16);
+    const int rw = m0 + 32 * q + lane;
+    if (ok) {
 #pragma unroll 1
-    for (int cc = 0; cc < kBN / 32; ++cc) {
-      uint32_t r[32];
-      const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16) + cc * 32;
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-          "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-          : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-            "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-            "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-            "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-          : "r"(taddr)
-          : "memory");
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      if (row < P.m) {
-        const int c0 = n0 + cc * 32;
-        __half* yrow = P.y + static_cast<size_t>(row) * P.ldy + c0;
+      for (int c0 = 0; c0 < kRows; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tl + c0, r);
+        if (rw < P.m) {
+          __half* yrow = P.y + static_cast<size_t>(rw) * P.ldy + n0 + c0;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {  // 8 columns per 16-byte store
-          uint32_t o[4];
+          for (int g = 0; g < 4; ++g) {  // 8 columns per 16-byte store
+            uint32_t o[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float v0 = __uint_as_float(r[8 * q + 2 * e]), v1 = __uint_as_float(r[8 * q + 2 * e + 1]);
-            __half h0, h1;
-            if (P.epi == EPI_BIAS) {
-              h0 = __float2half_rn(v0 + __half2float(P.bias[c0 + 8 * q + 2 * e]));
-              h1 = __float2half_rn(v1 + __half2float(P.bias[c0 + 8 * q + 2 * e + 1]));
-            } else if (P.epi == EPI_RESIDUAL) {
-              const __half* rr = P.res + static_cast<size_t>(row) * P.ldr + c0 + 8 * q + 2 * e;
-              h0 = __hadd(rr[0], __float2half_rn(v0));
-              h1 = __hadd(rr[1], __float2half_rn(v1));
-            } else {
-              h0 = __float2half_rn(v0);
-              h1 = __float2half_rn(v1);
+            for (int e = 0; e < 4; ++e) {
+              const int cc = n0 + c0 + 8 * g + 2 * e;
+              const __half2 hh = __halves2half2(epi_value(P, __uint_as_float(r[8 * g + 2 * e]), rw, cc),
+                                                epi_value(P, __uint_as_float(r[8 * g + 2 * e + 1]), rw, cc + 1));
+              o[e] = *reinterpret_cast<const uint32_t*>(&hh);
             }
-            const __half2 hh = __halves2half2(h0, h1);
-            o[e] = *reinterpret_cast<const uint32_t*>(&hh);
+            *reinterpret_cast<uint4*>(yrow + 8 * g) = make_uint4(o[0], o[1], o[2], o[3]);
           }
-          *reinterpret_cast<uint4*>(yrow + 8 * q) = make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(128) : "memory");
 }
 
-constexpr size_t kSmemBytes = 2 * kStages * kTileBytes + 1024 /* alignment */ + 64;
+static size_t tiles_smem_bytes(int stages) {
+  return static_cast<size_t>(stages) * (128 * 128 + kWTileBytes + kStepBytes) + 1024 +
+         (3 * kMaxStages + 1) * sizeof(uint64_t) + 16;
+}
+
+static size_t ring_bytes(int xrows, int xstages, int dstages, int wslots, int spb) {
+  return static_cast<size_t>(wslots) * kStepBytes * spb + static_cast<size_t>(xstages) * xrows * 128 +
+         static_cast<size_t>(dstages) * kWTileBytes;
+}
+static size_t smem_bytes(int xrows, int xstages, int dstages, int wslots, int spb) {
+  return ring_bytes(xrows, xstages, dstages, wslots, spb) + 1024 + (6 * kMaxStages + 1) * sizeof(uint64_t) +
+         kScaleAhead * 128 * sizeof(uint32_t) + 16;
+}
 
 }  // namespace w4
 }  // namespace lmps
 
 using namespace lmps;
 
+// Token-tile geometry: fewer than 128 tokens run one token tile with the
+// weight rows as the MMA's M (rounded up to 16 tokens); otherwise 128-token
+// tiles.
+static int w4_xrows(int m) { return m < 128 ? ((m + 15) / 16) * 16 : 128; }
+
 extern "C" size_t lmps_w4a16_gemm_workspace_size(int m, int n) {
-  if (m <= 0 || n <= 0) return 0;
-  const size_t mt = (m + w4::kBM - 1) / w4::kBM, nt = (n + w4::kBN - 1) / w4::kBN;
-  return mt * w4::kBM * n * sizeof(float) + ((mt * nt * sizeof(uint32_t) + 255) & ~static_cast<size_t>(255));
+  (void)m;
+  (void)n;
+  return 0;  // split K reduces inside a thread-block cluster
 }
 
-// Splits of K for a grid of `tiles` output tiles: about two CTAs per SM, at
-// least two 64-wide K steps per split.
+// K splits of the swap tiles: about two CTAs per SM, a power of two up to the
+// portable cluster size, at least two 64-wide K steps per split.
 static int choose_splits(int tiles, int ksteps, int sms) {
-  int s = (2 * sms) / (tiles > 0 ? tiles : 1);
-  if (s > ksteps / 2) s = ksteps / 2;
-  return s < 1 ? 1 : s;
+  const int want = (2 * sms) / (tiles > 0 ? tiles : 1);
+  int s = 1;
+  while (2 * s <= want && 2 * s <= w4::kMaxSplits && 2 * (2 * s) <= ksteps) s *= 2;
+  return s;
+}
+
+// The driver's tensor-map encoder, looked up through the runtime (the
+// library has no link-time dependency on the driver library).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+static bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t inner, uint64_t outer,
+                      uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+  const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 extern "C" int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed, const uint16_t* scales,
@@ -365,16 +700,25 @@ extern "C" int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed
                                size_t workspace_bytes, void* stream) {
   LMPS_CHECK_ARG(x && packed && scales && y && error);
   LMPS_CHECK_ARG(m >= 1 && n >= 1 && k >= 1);
-  if (n % w4::kBN != 0 || k % w4::kBK != 0) return LMPS_ERR_UNSUPPORTED;
+  if (n % w4::kRows != 0 || k % w4::kBK != 0) return LMPS_ERR_UNSUPPORTED;
   LMPS_CHECK_ARG(epilogue >= w4::EPI_NONE && epilogue <= w4::EPI_RESIDUAL);
   LMPS_CHECK_ARG(epilogue != w4::EPI_BIAS || bias);
   LMPS_CHECK_ARG(epilogue != w4::EPI_RESIDUAL || (residual && ldr >= n));
   LMPS_CHECK_ARG(ldx >= k && ldx % 8 == 0 && ldy >= n && ldy % 8 == 0);
-  LMPS_CHECK_ARG(lmps_aligned(x, 16) && lmps_aligned(y, 16) && lmps_aligned(packed, 4) && lmps_aligned(scales, 2));
+  LMPS_CHECK_ARG(lmps_aligned(x, 16) && lmps_aligned(y, 16) && lmps_aligned(packed, 16) && lmps_aligned(scales, 4));
   w4::Params P{};
-  P.x = reinterpret_cast<const __half*>(x);
-  P.ldx = ldx;
-  P.w = packed;
+  const int xr = w4_xrows(m);
+  P.swap = m < 128 ? 1 : 0;
+  P.xrows = xr;
+  // decode tiles stream packed W in 128-byte row pieces (4 K steps per load);
+  // prefill tiles in 32-byte pieces, one per K step
+  P.wspb = P.swap ? 4 : 1;
+  if (!encode_2d(&P.tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, static_cast<uint64_t>(k), static_cast<uint64_t>(m),
+                 static_cast<uint64_t>(ldx) * 2, w4::kBK, static_cast<uint32_t>(xr), CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&P.tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, static_cast<uint64_t>(k / 2), static_cast<uint64_t>(n),
+                 static_cast<uint64_t>(k / 2), static_cast<uint32_t>(w4::kBK / 2 * P.wspb), w4::kRows,
+                 P.wspb == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE))
+    return LMPS_ERR_INVALID_ARGUMENT;
   P.s = reinterpret_cast<const __half*>(scales);
   P.bias = reinterpret_cast<const __half*>(bias);
   P.res = reinterpret_cast<const __half*>(residual);
@@ -386,26 +730,58 @@ extern "C" int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed
   P.k = k;
   P.epi = epilogue;
   P.error = error;
-  const int ksteps = k / w4::kBK, mt = (m + w4::kBM - 1) / w4::kBM, nt = n / w4::kBN;
+  const int ksteps = k / w4::kBK, mt = (m + xr - 1) / xr, nt = n / w4::kRows;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  int splits = 1;
-  if (workspace && workspace_bytes >= lmps_w4a16_gemm_workspace_size(m, n)) {
-    LMPS_CHECK_ARG(lmps_aligned(workspace, 256));
-    splits = choose_splits(mt * nt, ksteps, sms);
+  (void)workspace;
+  (void)workspace_bytes;
+  if (!P.swap) {  // prefill tiles: the single-ring kernel, three stages, two CTAs per SM
+    P.xstages = 3;
+    const size_t smem = w4::tiles_smem_bytes(P.xstages);
+    cudaError_t e = cudaFuncSetAttribute(w4::w4a16_gemm_tiles_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return static_cast<int>(e);
+    w4::w4a16_gemm_tiles_kernel<<<dim3(nt, mt), w4::kThreads, smem, lmps_stream(stream)>>>(P);
+    return lmps_launch_status();
   }
-  P.ksteps_per_split = (ksteps + splits - 1) / splits;
-  splits = (ksteps + P.ksteps_per_split - 1) / P.ksteps_per_split;
-  if (splits > 1) {
-    P.acc32 = reinterpret_cast<float*>(workspace);
-    P.tile_cnt = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(workspace) +
-                                             static_cast<size_t>(mt) * w4::kBM * n * sizeof(float));
-  }
+  const int splits = choose_splits(nt, ksteps, sms);
+  P.ksteps_per_split = (ksteps + splits - 1) / splits;  // trailing splits may get none: they add zeros
+  // Two CTAs per SM: 2 packed-W blocks (8 K steps), 3 dequantised-W stages,
+  // then as many X tiles as fit (up to 8).
+  int max_smem = 0;
+  cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  const size_t budget = static_cast<size_t>(max_smem) / 2 - 1024;
+  const int spb = P.wspb;
+  int xst = 2, dst = 3, wsl = 2;
+  if (w4::smem_bytes(xr, xst, dst, wsl, spb) > budget) dst = 2;
+  if (w4::smem_bytes(xr, xst, dst, wsl, spb) > budget) xst = 2;
+  if (w4::smem_bytes(xr, xst, dst, wsl, spb) > budget) return LMPS_ERR_UNSUPPORTED;
+  while (xst < w4::kMaxStages && w4::smem_bytes(xr, xst + 1, dst, wsl, spb) <= budget) ++xst;
+  P.xstages = xst;
+  P.dstages = dst;
+  P.wslots = wsl;
+  const size_t smem = w4::smem_bytes(xr, xst, dst, wsl, spb);
+  // the split partial rows reuse the pipeline buffers
+  if (splits > 1 &&
+      static_cast<size_t>(w4::kRows) * (xr + 4) * sizeof(float) > w4::ring_bytes(xr, xst, dst, wsl, spb))
+    return LMPS_ERR_UNSUPPORTED;
   cudaError_t e = cudaFuncSetAttribute(w4::w4a16_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(w4::kSmemBytes));
+                                       static_cast<int>(smem));
   if (e != cudaSuccess) return static_cast<int>(e);
-  dim3 grid(nt, mt, splits);
-  w4::w4a16_gemm_kernel<<<grid, w4::kThreads, w4::kSmemBytes, lmps_stream(stream)>>>(P);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(nt, mt, splits);
+  cfg.blockDim = dim3(w4::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = lmps_stream(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = static_cast<unsigned>(splits);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, w4::w4a16_gemm_kernel, P);
+  if (e != cudaSuccess) return static_cast<int>(e);
   return lmps_launch_status();
 }

@@ -209,8 +209,8 @@ def w4a16_gemm(x, packed, scales, n: int, k: int, *, bias=None, residual=None, o
 
     x is fp16 [m, k] (token-major); W the Q4 [n, k] layout.  Used where the
     projections of many tokens at once are dense contractions (prefill, large
-    batches).  ``workspace`` (uint8, w4a16_gemm_workspace_size(m, n) bytes,
-    zero-filled once, 256-byte aligned) lets small-m calls split K."""
+    batches).  Calls with m < 128 split K inside a thread-block cluster;
+    ``workspace`` is accepted for API stability and unused."""
     x2, m = _x2d(x)
     y = out if out is not None else torch.empty(m, n, dtype=FP16, device=x.device)
     epi, b_ptr, r_ptr, ldr = EPI_NONE, None, None, 0
@@ -223,7 +223,7 @@ def w4a16_gemm(x, packed, scales, n: int, k: int, *, bias=None, residual=None, o
         epi, r_ptr, ldr = EPI_RESIDUAL, _dev(r2, "residual", FP16), r2.shape[1]
     err = error if error is not None else torch.zeros(1, dtype=torch.int32, device=x.device)
     ws_ptr, ws_bytes = None, 0
-    if workspace is not None:
+    if workspace is not None and workspace.numel() > 0:
         ws_ptr, ws_bytes = _dev(workspace, "workspace", torch.uint8), workspace.numel()
     call("lmps_w4a16_gemm", _dev(x2, "x", FP16), x2.shape[1], _dev(packed, "packed", torch.uint8),
          _dev(scales, "scales", FP16), b_ptr, r_ptr, ldr, _dev(y, "y", FP16), y.shape[-1], m, n, k, epi,

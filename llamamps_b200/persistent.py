@@ -10,6 +10,7 @@ from __future__ import annotations
 import ctypes
 from typing import Optional
 
+import numpy as np
 import torch
 
 from ._lib import check, lib
@@ -33,7 +34,7 @@ class ModelDesc(ctypes.Structure):
 
 class DecodeState(ctypes.Structure):
     _fields_ = [("batch", c_int), ("page_size", c_int), ("max_pages", c_int), ("max_seq_len", c_int),
-                ("block_table", c_vp), ("tokens", c_vp), ("pos", c_vp), ("forced", c_vp),
+                ("block_table", c_vp), ("rope_table", c_vp), ("tokens", c_vp), ("pos", c_vp), ("forced", c_vp),
                 ("forced_stride", c_int), ("n_forced", c_int), ("x_in", c_vp), ("logits", c_vp),
                 ("history", c_vp), ("step_counter", c_vp), ("history_rows", c_int),
                 ("workspace", c_vp), ("workspace_bytes", c_size), ("error", c_vp),
@@ -66,6 +67,17 @@ def _p(t: Optional[torch.Tensor]):
     return t.data_ptr()
 
 
+def rope_table(inv_freq: torch.Tensor, positions: int) -> torch.Tensor:
+    """fp32 [positions, head_dim/2, 2]: cos and sin of the fp32 angle
+    p * inv_freq[j] (rope.metal:28-33 computes the angle in fp32), each
+    correctly rounded from a float64 evaluation."""
+    inv = inv_freq.detach().to("cpu", torch.float32).numpy()
+    ang = (np.arange(positions, dtype=np.float32)[:, None] * inv[None, :]).astype(np.float32)
+    ang64 = ang.astype(np.float64)
+    tab = np.stack([np.cos(ang64), np.sin(ang64)], axis=-1).astype(np.float32)
+    return torch.from_numpy(np.ascontiguousarray(tab))
+
+
 class PersistentDecoder:
     """Descriptors + workspace for one engine (weights, cache, max batch)."""
 
@@ -91,6 +103,7 @@ class PersistentDecoder:
                                self.layer_table.data_ptr(), _p(weights.final_norm), _p(weights.lm_packed),
                                _p(weights.lm_scales), _p(weights.embed), _p(inv_freq))
         self.max_batch = max_batch
+        self.rope_table = rope_table(inv_freq, cache.max_seq_len).to(weights.device)
         ws = self.L.lmps_decode_persistent_workspace_size(ctypes.byref(self.model), max_batch, cache.max_seq_len)
         self.workspace = torch.zeros(ws + 256, dtype=torch.uint8, device=weights.device)
         off = (-self.workspace.data_ptr()) % 256
@@ -116,6 +129,7 @@ class PersistentDecoder:
         st.max_pages = cache.pages_per_seq
         st.max_seq_len = cache.max_seq_len
         st.block_table = cache.block_table.data_ptr()
+        st.rope_table = _p(self.rope_table)
         st.tokens = _p(tokens)
         st.pos = _p(pos)
         if forced is not None:

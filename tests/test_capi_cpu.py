@@ -32,7 +32,8 @@ def test_persistent_descriptor_layouts_match_the_header():
     from llamamps_b200 import persistent as P
     assert ctypes.sizeof(P.LayerDesc) == 15 * 8
     assert P.ModelDesc.layers.offset == 40 and ctypes.sizeof(P.ModelDesc) == 40 + 6 * 8
-    assert P.DecodeState.block_table.offset == 16 and P.DecodeState.error.offset == 112
+    assert P.DecodeState.block_table.offset == 16 and P.DecodeState.rope_table.offset == 24
+    assert P.DecodeState.error.offset == 120
     L = _lib.lib()
     P._declare()
     m = P.ModelDesc(28, 1536, 8960, 151936, 12, 2, 128, 1e-6, 0, None, None, None, None, None, None)
