@@ -168,6 +168,8 @@ struct Smem {
   __half* xown;     // [kMaxB][kOwnMax] residual x of the hidden rows this CTA owns
   __half* x1own;     // [kMaxB][kOwnMax] residual after attention, same rows
   __half* bias_own;  // [n_layers][kOwnMax] q|k|v bias of the qkv rows this CTA owns
+  int gemv_grid;     // CTAs [0, gemv_grid) run the projections; the others attention only
+  int n_att;         // CTAs dedicated to attention (0: attention spread over every CTA)
 };
 
 // Rows [r0, r1) of a stage this CTA computes: row pairs split evenly over the
@@ -187,7 +189,7 @@ struct Chunking {
   int k, r0, r1, rows_per_chunk;
 };
 
-__device__ __forceinline__ Chunking stage_chunks(const Params& P, int kind, int layer) {
+__device__ __forceinline__ Chunking stage_chunks(const Params& P, int kind, int layer, int ctas) {
   Chunking c{};
   const lmps_model_desc& m = P.m;
   int rows = 0;
@@ -211,7 +213,7 @@ __device__ __forceinline__ Chunking stage_chunks(const Params& P, int kind, int 
       c.k = m.intermediate; rows = m.hidden; c.rows_per_chunk = kRowsDown;
     }
   }
-  row_range(rows, blockIdx.x, gridDim.x, c.r0, c.r1);
+  row_range(rows, blockIdx.x, ctas, c.r0, c.r1);
   return c;
 }
 
@@ -241,7 +243,7 @@ __device__ void producer(const Params& P, Smem& S) {
   for (int step = 0; step < P.n_steps && ok; ++step) {
     for (int st = 0; st < n_stages && ok; ++st) {
       const int kind = (st == n_stages - 1) ? ST_HEAD : (st & 3);
-      const Chunking c = stage_chunks(P, kind, st >> 2);
+      const Chunking c = stage_chunks(P, kind, st >> 2, S.gemv_grid);
       const uint32_t row_bytes = c.k / 2, row_sbytes = c.k / 16;
       const uint32_t ncopy = (kind == ST_GU) ? 2u : 1u;
       trace_event(P, gridDim.x + blockIdx.x, pev);
@@ -698,7 +700,7 @@ __device__ __forceinline__ float* partials_view(const Planes& pl, int nb) {
 // One code path for every kind keeps the kernel's instruction footprint small.
 template <int NB>
 __device__ void gemv_rows(const Params& P, Smem& S, CState& cs, int kind, int layer, __half* logits, uint32_t tag) {
-  const Chunking c = stage_chunks(P, kind, layer);
+  const Chunking c = stage_chunks(P, kind, layer, S.gemv_grid);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = c.k / 32, JG = G / 16;
   const int half = lane >> 4, sub = lane & 15;
@@ -851,7 +853,7 @@ __device__ void gemv_rows(const Params& P, Smem& S, CState& cs, int kind, int la
 // memory and the block finishes all rows at the end: x = x1 + fp16(sum).
 template <int NB>
 __device__ void gemv_down(const Params& P, Smem& S, CState& cs, int layer, uint32_t tag) {
-  const Chunking c = stage_chunks(P, ST_DN, layer);
+  const Chunking c = stage_chunks(P, ST_DN, layer, S.gemv_grid);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = c.k / 32;
   const int g0 = G * warp / kConsumerWarps, g1 = G * (warp + 1) / kConsumerWarps;
@@ -934,7 +936,10 @@ struct AttnSmem {
   __half q[kMaxG][kHD];                   // rotated q, natural dim order
   float wm[kConsumerWarps][kMaxG];        // per-warp running max and sum (then merge weights)
   float wl[kConsumerWarps][kMaxG];
-  float wo[kConsumerWarps][32][32];       // per-warp unnormalised O^T fragments, [lane][value, rotated by 4*lane]
+  union {
+    float wo[kConsumerWarps][32][32];     // per-warp unnormalised O^T fragments, [lane][value, rotated by 4*lane]
+    uint4 kst[kConsumerWarps][8][32];     // K rows of each warp's first block, [chunk][lane] (cp.async)
+  };
   int is_last;
 };
 
@@ -986,8 +991,22 @@ __device__ __forceinline__ void rope_pair(int j, int style, int& i1, int& i2) {
   }
 }
 
+// Shared-memory K/V tiles of the dedicated attention CTAs: per 16-position
+// block, K then V, each [chunk 4*h2 + c][lane 4*g8 + t4] of 16 bytes = dims
+// 32*t4 + 8*c .. +7 of row 8*h2 + g8 (the lanes' mma operand runs).
+constexpr int kKvTileBytes = 2 * 8 * 32 * 16;  // K and V of one block: 8 KB
+constexpr int kMaxAttCtas = 8;
+__device__ __forceinline__ int kv_tile_idx(int blk, int kv, int h2, int c, int lane) {
+  return ((blk * 2 + kv) * 8 + 4 * h2 + c) * 32 + lane;
+}
+__device__ __forceinline__ __half& tile_half(uint4* kvs, int rel, int kv, int d) {
+  uint4& u = kvs[kv_tile_idx(rel >> 4, kv, (rel >> 3) & 1, (d >> 3) & 3, 4 * (rel & 7) + (d >> 5))];
+  return reinterpret_cast<__half*>(&u)[d & 7];
+}
+
 __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, int kvh,
-                          int split, int n_splits, int chunk, int pos, uint32_t in_tag, uint32_t out_tag) {
+                          int split, int n_splits, int chunk, int pos, uint32_t in_tag, uint32_t out_tag,
+                          uint4* kvs) {
   AttnSmem& A = *reinterpret_cast<AttnSmem*>(S.act);
   const lmps_model_desc& m = P.m;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1005,19 +1024,29 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
   const bool has_pos = pos >= start && pos < end;
   const uint64_t kvpol = evict_last_policy();
 
-  // Cache rows of positions < pos do not depend on this step's q|k|v: the
-  // first block of every warp is prefetched into L2 before anything waits.
+  // Cache rows of positions < pos do not depend on this step's q|k|v: every
+  // warp loads the K/V rows of its first block into registers before anything
+  // waits (the row of pos itself is appended below and read after the sync).
   const int nblk = (end - start + kBlk - 1) / kBlk;
   auto row_off = [&](int p) {
     return ((static_cast<size_t>(__ldg(bt + (p >> pshift))) * Hkv + kvh) * ps + (p & (ps - 1))) * kHD + 32 * t4;
   };
-  if (warp < nblk) {
+  // The K rows (p0+g8, p0+8+g8; dims 32*t4 ..) of every warp's first block
+  // go to shared memory through cp.async before anything waits (no registers
+  // held across the waits); the V rows are prefetched into L2.  The row of
+  // pos itself is appended below and read after the sync.
+  // (kvs: the caller staged every K/V row before pos in shared-memory tiles)
+  if (!kvs && warp < nblk) {
 #pragma unroll
     for (int h2 = 0; h2 < 2; ++h2) {
       const int p = start + warp * kBlk + 8 * h2 + g8;
       if (p < end && p != pos) {
         const size_t off = row_off(p);
-        asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(kpool + off));
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(&A.kst[warp][4 * h2 + c][lane])),
+                       "l"(kpool + off + 8 * c)
+                       : "memory");
         asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(vpool + off));
       }
     }
@@ -1063,6 +1092,10 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
         *reinterpret_cast<uint4*>(&A.q[tid / (kHD / 8)][8 * c8]) = v;
       } else {
         st_kv8((kind == 1 ? kpool : vpool) + app + 8 * c8, v, kvpol);
+        if (kvs) {  // and into its tile: row pos, dims 8*c8 .. (lane (pos & 7, c8 / 4), chunk c8 % 4)
+          const int rel = pos - start;
+          kvs[kv_tile_idx(rel >> 4, kind - 1, (rel >> 3) & 1, c8 & 3, 4 * (rel & 7) + (c8 >> 2))] = v;
+        }
       }
     }
   }
@@ -1086,10 +1119,16 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
         rope_pair(tid, m.rope_style, i1, i2);
         const float2 r = A.rot[tid];
         const float ka = __half2float(kraw[i1]), kb = __half2float(kraw[i2]);
-        st_kv(kpool + app + i1, __float2half_rn(ka * r.x - kb * r.y), kvpol);
-        st_kv(kpool + app + i2, __float2half_rn(ka * r.y + kb * r.x), kvpol);
+        const __half k1 = __float2half_rn(ka * r.x - kb * r.y), k2 = __float2half_rn(ka * r.y + kb * r.x);
+        st_kv(kpool + app + i1, k1, kvpol);
+        st_kv(kpool + app + i2, k2, kvpol);
+        if (kvs) {
+          tile_half(kvs, pos - start, 0, i1) = k1;
+          tile_half(kvs, pos - start, 0, i2) = k2;
+        }
       } else if (tid < kHD / 2 + kHD) {
         st_kv(vpool + app + tid - kHD / 2, kraw[kHD + tid - kHD / 2], kvpol);
+        if (kvs) tile_half(kvs, pos - start, 1, tid - kHD / 2) = kraw[kHD + tid - kHD / 2];
       }
     }
     consumer_sync();
@@ -1097,6 +1136,7 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
   // rotated q in shared memory, the new k/v row in the cache
 
   // -- per-warp flash loop over 16-position blocks
+  asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's staged K rows
   uint32_t qf[16];  // B operand Q^T: head g8, physical dims 32*t4 .. 32*t4+31
   {
     const uint4* qs = reinterpret_cast<const uint4*>(&A.q[g8 < G ? g8 : 0][32 * t4]);
@@ -1115,7 +1155,7 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
   float mrun0 = -INFINITY, mrun1 = -INFINITY, lrun0 = 0.0f, lrun1 = 0.0f;  // heads 2*t4, 2*t4+1
   for (int bi = warp; bi < nblk; bi += kConsumerWarps) {
     const int p0 = start + bi * kBlk;
-    if (bi + kConsumerWarps < nblk) {  // this warp's next block into L2 while this one computes
+    if (!kvs && bi + kConsumerWarps < nblk) {  // this warp's next block into L2 while this one computes
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
         const int p = p0 + kConsumerWarps * kBlk + 8 * h2 + g8;
@@ -1126,8 +1166,9 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
         }
       }
     }
-    // Cache rows p0+g8 and p0+8+g8, dims 32*t4 .. 32*t4+31 (the row of pos was
-    // appended by this CTA before the last block sync).
+    // K/V rows p0+g8 and p0+8+g8, dims 32*t4 .. 32*t4+31 (the row of pos was
+    // appended by this CTA before the last block sync); the K rows of the
+    // first block other than pos's are already in shared memory
     uint4 kr[2][4], vr[2][4];
     size_t off[2];
     bool ok[2];
@@ -1135,18 +1176,40 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
     for (int h2 = 0; h2 < 2; ++h2) {
       const int p = p0 + 8 * h2 + g8;
       ok[h2] = p < end;
-      off[h2] = ok[h2] ? row_off(p) : 0;
+      off[h2] = ok[h2] && !kvs ? row_off(p) : 0;
     }
+    if (kvs) {  // every row in the shared-memory tiles (rows past the end: masked / zero V)
 #pragma unroll
-    for (int h2 = 0; h2 < 2; ++h2)
+      for (int h2 = 0; h2 < 2; ++h2)
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        kr[h2][c] = ok[h2] ? __ldcg(reinterpret_cast<const uint4*>(kpool + off[h2]) + c) : make_uint4(0u, 0u, 0u, 0u);
+        for (int c = 0; c < 4; ++c) {
+          kr[h2][c] = kvs[kv_tile_idx(bi, 0, h2, c, lane)];
+          vr[h2][c] = ok[h2] ? kvs[kv_tile_idx(bi, 1, h2, c, lane)] : make_uint4(0u, 0u, 0u, 0u);
+        }
+    } else if (bi == warp) {  // rows past the end are masked out of the scores below
 #pragma unroll
-    for (int h2 = 0; h2 < 2; ++h2)
+      for (int h2 = 0; h2 < 2; ++h2)
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        vr[h2][c] = ok[h2] ? __ldcg(reinterpret_cast<const uint4*>(vpool + off[h2]) + c) : make_uint4(0u, 0u, 0u, 0u);
+        for (int c = 0; c < 4; ++c) kr[h2][c] = A.kst[warp][4 * h2 + c][lane];
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2)
+        if (p0 + 8 * h2 + g8 == pos)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) kr[h2][c] = __ldcg(reinterpret_cast<const uint4*>(kpool + off[h2]) + c);
+    } else {
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          kr[h2][c] = ok[h2] ? __ldcg(reinterpret_cast<const uint4*>(kpool + off[h2]) + c) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    if (!kvs) {
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          vr[h2][c] = ok[h2] ? __ldcg(reinterpret_cast<const uint4*>(vpool + off[h2]) + c) : make_uint4(0u, 0u, 0u, 0u);
+    }
     // S^T = K Q^T
     float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
@@ -1192,28 +1255,19 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
   }
   const int nw = min(kConsumerWarps, nblk);  // warps that saw positions
   const size_t ms = P.max_splits;
-  // -- warps meet in shared memory: merged maxima first, then every warp
-  // rescales its sums to them, then the block adds the warps up
-  if (warp < nw && g8 == 0) {
-    A.wm[warp][2 * t4] = mrun0;
-    A.wm[warp][2 * t4 + 1] = mrun1;
-  }
-  consumer_sync();
+  // -- warps meet in shared memory: each leaves its running max, sum and
+  // output; the reducing thread rescales them to the merged max
   if (warp < nw) {
-    float M0 = -INFINITY, M1 = -INFINITY;
-    for (int ww = 0; ww < nw; ++ww) {
-      M0 = fmaxf(M0, A.wm[ww][2 * t4]);
-      M1 = fmaxf(M1, A.wm[ww][2 * t4 + 1]);
-    }
-    const float f0 = expf(mrun0 - M0), f1 = expf(mrun1 - M1);
     if (g8 == 0) {
-      A.wl[warp][2 * t4] = lrun0 * f0;
-      A.wl[warp][2 * t4 + 1] = lrun1 * f1;
+      A.wm[warp][2 * t4] = mrun0;
+      A.wm[warp][2 * t4 + 1] = mrun1;
+      A.wl[warp][2 * t4] = lrun0;
+      A.wl[warp][2 * t4 + 1] = lrun1;
     }
 #pragma unroll
     for (int mt = 0; mt < 8; ++mt)  // 16-byte stores, value k of this lane at (k + 4 lane) mod 32
       *reinterpret_cast<float4*>(&A.wo[warp][lane][(4 * mt + 4 * lane) & 31]) =
-          make_float4(o[mt][0] * f0, o[mt][1] * f1, o[mt][2] * f0, o[mt][3] * f1);
+          make_float4(o[mt][0], o[mt][1], o[mt][2], o[mt][3]);
   }
   consumer_sync();
   for (int w = tid; w < G * (kHD / 2); w += kConsumers) {
@@ -1223,11 +1277,14 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
     const int d = 2 * dp, k = 4 * ((d & 31) >> 2) + 2 * (((d & 31) >> 1) & 1) + (h & 1);
     const int la = 4 * (2 * (d >> 5)) + (h >> 1);
     const int ka = (k + 4 * la) & 31, kb = (k + 4 * (la + 4)) & 31;
+    float M = -INFINITY;
+    for (int ww = 0; ww < nw; ++ww) M = fmaxf(M, A.wm[ww][h]);
     float n0 = 0.0f, n1 = 0.0f, den = 0.0f;
     for (int ww = 0; ww < nw; ++ww) {
-      n0 += A.wo[ww][la][ka];
-      n1 += A.wo[ww][la + 4][kb];
-      den += A.wl[ww][h];
+      const float f = expf(A.wm[ww][h] - M);
+      n0 += A.wo[ww][la][ka] * f;
+      n1 += A.wo[ww][la + 4][kb] * f;
+      den += A.wl[ww][h] * f;
     }
     if (n_splits == 1) {
       const float inv = den > 0.0f ? 1.0f / den : 0.0f;
@@ -1235,11 +1292,7 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
     } else {
       const size_t prow = (static_cast<size_t>(b) * Hq + kvh * G + h) * ms + split;
       *reinterpret_cast<float2*>(&P.part_o[prow * kHD + 2 * dp]) = make_float2(n0, n1);
-      if (dp == 0) {
-        float M = -INFINITY;
-        for (int ww = 0; ww < nw; ++ww) M = fmaxf(M, A.wm[ww][h]);
-        P.part_ml[prow] = make_float2(M, den);
-      }
+      if (dp == 0) P.part_ml[prow] = make_float2(M, den);
     }
   }
   if (n_splits == 1) {
@@ -1290,14 +1343,16 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
 // value): a whole sequence up to kMinSplit positions (one CTA, no cross-CTA
 // merge), longer contexts split so that the items about fill the grid.
 __device__ __forceinline__ int attn_chunk_len(const int* pos, int batch, int n_kv) {
-  long long total = 0;
-  for (int b = 0; b < batch; ++b) total += pos[b] + 1;
+  uint32_t total = 0;  // < 2^32: max_seq_len * batch * n_kv is bounded on the host
+  for (int b = 0; b < batch; ++b) total += static_cast<uint32_t>(pos[b] + 1);
+  if (total * static_cast<uint32_t>(n_kv) <= static_cast<uint32_t>(kMinSplit)) return kMinSplit;
   // ceil() of each (sequence, KV head) adds at most one item: keep the
   // item count within the grid so no CTA gets a second item
-  const long long slots = static_cast<long long>(gridDim.x) - static_cast<long long>(batch) * n_kv;
-  long long c = (total * n_kv + (slots > 0 ? slots : 1) - 1) / (slots > 0 ? slots : 1);
+  const int slots_i = static_cast<int>(gridDim.x) - batch * n_kv;
+  const uint32_t slots = slots_i > 0 ? static_cast<uint32_t>(slots_i) : 1u;
+  uint32_t c = (total * static_cast<uint32_t>(n_kv) + slots - 1) / slots;
   c = (c + kBlk - 1) / kBlk * kBlk;
-  return static_cast<int>(c < kMinSplit ? kMinSplit : c);
+  return c < static_cast<uint32_t>(kMinSplit) ? kMinSplit : static_cast<int>(c);
 }
 
 // The next token of every sequence from the tagged per-CTA argmax slots of a
@@ -1306,7 +1361,7 @@ __device__ __forceinline__ int attn_chunk_len(const int* pos, int batch, int n_k
 template <int NB>
 __device__ void gather_argmax(const Params& P, Smem& S, uint32_t tag14, int (&row)[NB]) {
   const int B = P.s.batch;
-  const int n = gridDim.x * kMaxB;
+  const int n = S.gemv_grid * kMaxB;
   unsigned long long best[NB];
 #pragma unroll
   for (int b = 0; b < NB; ++b) best[b] = 0ull;
@@ -1354,6 +1409,61 @@ __device__ void gather_argmax(const Params& P, Smem& S, uint32_t tag14, int (&ro
   consumer_sync();
 }
 
+// Stages of a step (see consumer below).
+enum StepStage { K_QKV = 0, K_ATT = 1, K_O = 2, K_GU = 3, K_DN = 4, K_HEAD = 5 };
+
+// K/V rows [0, npos) of (sequence b, KV head kvh) of one layer into the
+// shared-memory tiles: warp w stages blocks w, w + warps, .. (the blocks it
+// reads in attn_item), each lane its own 16-byte runs (cp.async, waited for
+// in attn_item before the flash loop).
+__device__ void stage_kv_tiles(const Params& P, const LayerPtrs& L, int b, int kvh, int npos, uint4* kvs) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g8 = lane >> 2, t4 = lane & 3;
+  const int ps = P.s.page_size, pshift = __ffs(ps) - 1, Hkv = P.m.n_kv_heads;
+  const int32_t* bt = P.s.block_table + static_cast<size_t>(b) * P.s.max_pages;
+  for (int bi = warp; bi * kBlk < npos; bi += kConsumerWarps) {
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const int p = bi * kBlk + 8 * h2 + g8;
+      if (p < npos) {
+        const size_t off =
+            ((static_cast<size_t>(__ldg(bt + (p >> pshift))) * Hkv + kvh) * ps + (p & (ps - 1))) * kHD + 32 * t4;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(&kvs[kv_tile_idx(bi, 0, h2, c, lane)])),
+                       "l"(L.k_pool + off + 8 * c)
+                       : "memory");
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(&kvs[kv_tile_idx(bi, 1, h2, c, lane)])),
+                       "l"(L.v_pool + off + 8 * c)
+                       : "memory");
+        }
+      }
+    }
+  }
+}
+
+// A dedicated attention CTA: item (sequence b, KV head kvh) of every layer
+// and step.  While the projections of a layer run, it stages the next
+// layer's cached K/V rows; then it waits for the layer's q|k|v like any
+// attention item (attn_item, whole context, one split).
+__device__ void att_consumer(const Params& P, Smem& S, uint32_t epoch) {
+  const int a = static_cast<int>(blockIdx.x) - S.gemv_grid;
+  const int Hkv = P.m.n_kv_heads, b = a / Hkv, kvh = a - b * Hkv;
+  const int n_stage = P.m.n_layers * 5 + 1;
+  const int pos0 = P.s.pos[b];
+  uint4* kvs = reinterpret_cast<uint4*>(S.ring);
+  for (int step = 0; step < P.n_steps; ++step) {
+    const int pos = pos0 + step;
+    const uint32_t tag0 = epoch + static_cast<uint32_t>(step * n_stage) + 1u;
+    stage_kv_tiles(P, S.lp[0], b, kvh, pos, kvs);
+    for (int l = 0; l < P.m.n_layers; ++l) {
+      if (aborting(S)) return;
+      const uint32_t tag = tag0 + static_cast<uint32_t>(5 * l + K_ATT);
+      attn_item(P, S, S.lp[l], b, kvh, 0, 1, pos + 1, pos, tag - 1u, tag, kvs);
+      if (l + 1 < P.m.n_layers) stage_kv_tiles(P, S.lp[l + 1], b, kvh, pos, kvs);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Consumers: the decode loop
 // ---------------------------------------------------------------------------
@@ -1362,7 +1472,6 @@ __device__ void gather_argmax(const Params& P, Smem& S, uint32_t tag14, int (&ro
 // the kernel's code is one copy of every stage.  Stage si of step `step`
 // publishes its output with tag epoch + step * n_stage + si + 1; the next
 // stage polls for that tag, so no grid-wide barrier is needed.
-enum StepStage { K_QKV = 0, K_ATT = 1, K_O = 2, K_GU = 3, K_DN = 4, K_HEAD = 5 };
 
 template <int NB>
 __device__ void consumer(const Params& P, Smem& S, uint32_t epoch) {
@@ -1382,7 +1491,7 @@ __device__ void consumer(const Params& P, Smem& S, uint32_t epoch) {
   const bool tr = threadIdx.x == 0;
   const int n_stage = m.n_layers * 5 + 1;
   int o0, o1;
-  row_range(hidden, blockIdx.x, gridDim.x, o0, o1);
+  row_range(hidden, blockIdx.x, S.gemv_grid, o0, o1);
   const __half* embed = reinterpret_cast<const __half*>(m.embed);
   const __half* x_in = reinterpret_cast<const __half*>(P.s.x_in);
 
@@ -1444,11 +1553,12 @@ __device__ void consumer(const Params& P, Smem& S, uint32_t epoch) {
       if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
       // -- compute and publish
       if (kind == K_ATT) {
+        // (with dedicated attention CTAs they run this stage: no items here)
         const int chunk = attn_chunk_len(pos, B, Hkv);
         int n_items = 0;
 #pragma unroll
         for (int b = 0; b < NB; ++b)
-          if (b < B) n_items += Hkv * ((pos[b] + chunk) / chunk);
+          if (b < B && S.n_att == 0) n_items += Hkv * ((pos[b] + chunk) / chunk);
         for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
           int rem = it, bsel = 0, nsp = 1;
 #pragma unroll
@@ -1466,7 +1576,7 @@ __device__ void consumer(const Params& P, Smem& S, uint32_t epoch) {
 #pragma unroll
           for (int b = 0; b < NB; ++b)
             if (b == bsel) pb = pos[b];
-          attn_item(P, S, L, bsel, kvh, sp, nsp, chunk, pb, in_tag, tag);
+          attn_item(P, S, L, bsel, kvh, sp, nsp, chunk, pb, in_tag, tag, nullptr);
         }
       } else if (kind == K_DN) {
         gemv_down<NB>(P, S, cs, l, tag);
@@ -1534,15 +1644,29 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
   S.bias_own = S.x1own + kMaxB * kOwnMax;
   // tag base of this launch (CTA 0 advances it after every CTA has used it)
   const uint32_t epoch = __ldcg(P.epoch);
+  {
+    // Short contexts: the batch * n_kv attention items each get a CTA of
+    // their own (the last CTAs of the grid), whose code stays resident in its
+    // SM's instruction cache and which stages each layer's K/V rows in its
+    // shared memory while the projections run; the other CTAs run the
+    // projections.  Long contexts spread attention over every CTA.  Every CTA
+    // derives the same choice from the launch's positions.
+    int max_t = 0;
+    for (int b = 0; b < P.s.batch; ++b) max_t = max(max_t, P.s.pos[b] + P.n_steps);
+    const int items = P.s.batch * P.m.n_kv_heads;
+    const int tile_blocks = static_cast<int>((static_cast<size_t>(P.slots) * kSlotBytes) / kKvTileBytes);
+    S.n_att = (max_t <= tile_blocks * kBlk && items <= kMaxAttCtas) ? items : 0;
+    S.gemv_grid = static_cast<int>(gridDim.x) - S.n_att;
+  }
   for (int i = threadIdx.x; i < P.m.n_layers; i += blockDim.x) {
     const lmps_layer_desc& L = P.m.layers[i];
     S.lp[i] = LayerPtrs{reinterpret_cast<const __half*>(L.in_norm), reinterpret_cast<const __half*>(L.post_norm),
                         reinterpret_cast<__half*>(L.k_pool), reinterpret_cast<__half*>(L.v_pool)};
   }
-  {  // q|k|v bias of this CTA's qkv rows, every layer
+  if (static_cast<int>(blockIdx.x) < S.gemv_grid) {  // q|k|v bias of this CTA's qkv rows, every layer
     const int qkv_rows = (P.m.n_q_heads + 2 * P.m.n_kv_heads) * kHD;
     int q0, q1;
-    row_range(qkv_rows, blockIdx.x, gridDim.x, q0, q1);
+    row_range(qkv_rows, blockIdx.x, S.gemv_grid, q0, q1);
     for (int i = threadIdx.x; i < P.m.n_layers * kOwnMax; i += blockDim.x) {
       const int l = i / kOwnMax, r = i - l * kOwnMax;
       if (r < q1 - q0) S.bias_own[i] = reinterpret_cast<const __half*>(P.m.layers[l].qkv_bias)[q0 + r];
@@ -1576,11 +1700,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
+  const bool att_cta = static_cast<int>(blockIdx.x) >= S.gemv_grid;
   if (threadIdx.x >= kConsumers) {
-    if (threadIdx.x == kConsumers) producer(P, S);
+    if (threadIdx.x == kConsumers && !att_cta) producer(P, S);
     return;
   }
-  consumer<NB>(P, S, epoch);
+  if (att_cta)
+    att_consumer(P, S, epoch);
+  else
+    consumer<NB>(P, S, epoch);
 }
 
 // Shared-memory tail after the ring and the activation area.
@@ -1647,8 +1775,11 @@ static int launch(const Params& P0, const lmps_model_desc& m, cudaStream_t st) {
   P.act_bytes = act_bytes_for(m, NB);
   // rows of the hidden and q|k|v outputs one CTA owns (residual / bias kept in shared memory)
   const int qkv_rows = (m.n_q_heads + 2 * m.n_kv_heads) * m.head_dim;
-  // (pair-aligned partitions: at most 2 * ceil(rows / 2 / sms) rows per CTA)
-  auto per_cta = [&](int rows) { return 2 * ((rows / 2 + sms - 1) / sms); };
+  // (pair-aligned partitions: at most 2 * ceil(rows / 2 / ctas) rows per CTA,
+  // with up to kMaxAttCtas CTAs set aside for attention)
+  const int proj_ctas = sms - kMaxAttCtas;
+  if (proj_ctas < 1) return LMPS_ERR_UNSUPPORTED;
+  auto per_cta = [&](int rows) { return 2 * ((rows / 2 + proj_ctas - 1) / proj_ctas); };
   if (per_cta(m.hidden) > kOwnMax || per_cta(qkv_rows) > kOwnMax || per_cta(m.intermediate) > kOutMax ||
       m.n_layers > kMaxLayers || sms > kMaxGrid || m.vocab > 0x40000 || 2 * kConsumers < sms * kMaxB)
     return LMPS_ERR_UNSUPPORTED;
@@ -1711,6 +1842,8 @@ extern "C" int lmps_decode_persistent(const lmps_model_desc* model, const lmps_d
   LMPS_CHECK_ARG(s.block_table && s.rope_table && s.tokens && s.pos && s.workspace && s.error);
   LMPS_CHECK_ARG(s.page_size > 0 && (s.page_size & (s.page_size - 1)) == 0 && s.max_pages > 0 &&
                  s.max_seq_len > 0 && s.max_seq_len <= s.max_pages * s.page_size);
+  // attention work-item arithmetic runs in 32 bits
+  if (static_cast<long long>(s.max_seq_len) * pk::kMaxB * m.n_kv_heads >= (1LL << 31)) return LMPS_ERR_UNSUPPORTED;
   LMPS_CHECK_ARG(lmps_aligned(s.rope_table, 16));
   LMPS_CHECK_ARG(!s.forced || s.forced_stride >= s.n_forced);
   LMPS_CHECK_ARG(!s.history || (s.step_counter && s.history_rows > 0));

@@ -36,6 +36,9 @@ def capture(engine, steps: int = 4) -> Dict:
     engine.host_pos += steps
     t = trace.cpu().numpy().astype(np.int64)
     cons, prod, wait = t[:sms], t[sms:2 * sms], t[2 * sms:3 * sms]
+    # CTAs dedicated to attention (short contexts) record no stage events
+    active = (cons != 0).any(axis=1)
+    cons, prod, wait = cons[active], prod[active], wait[active]
     names = [f"L{l}.{k}" for l in range(L) for k in KINDS] + ["HEAD"]
     pnames = [f"L{l}.{k}" for l in range(L) for k in WEIGHT_KINDS] + ["HEAD"]
     step = steps // 2  # a middle step
