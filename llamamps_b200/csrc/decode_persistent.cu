@@ -699,8 +699,8 @@ __device__ __forceinline__ float* partials_view(const Planes& pl, int nb) {
 // gate/up, gate row w and up row w -- and lane sub groups sub, sub+16, sub+32.
 // One code path for every kind keeps the kernel's instruction footprint small.
 template <int NB>
-__device__ void gemv_rows(const Params& P, Smem& S, CState& cs, int kind, int layer, __half* logits, uint32_t tag) {
-  const Chunking c = stage_chunks(P, kind, layer, S.gemv_grid);
+__device__ void gemv_rows(const Params& P, Smem& S, CState& cs, int kind, int layer, __half* logits, uint32_t tag,
+                          const Chunking& c) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = c.k / 32, JG = G / 16;
   const int half = lane >> 4, sub = lane & 15;
@@ -852,8 +852,7 @@ __device__ void gemv_rows(const Params& P, Smem& S, CState& cs, int kind, int la
 // g0+sub+8j); each warp leaves one partial per (row, sequence) in shared
 // memory and the block finishes all rows at the end: x = x1 + fp16(sum).
 template <int NB>
-__device__ void gemv_down(const Params& P, Smem& S, CState& cs, int layer, uint32_t tag) {
-  const Chunking c = stage_chunks(P, ST_DN, layer, S.gemv_grid);
+__device__ void gemv_down(const Params& P, Smem& S, CState& cs, int layer, uint32_t tag, const Chunking& c) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = c.k / 32;
   const int g0 = G * warp / kConsumerWarps, g1 = G * (warp + 1) / kConsumerWarps;
@@ -1535,6 +1534,11 @@ __device__ void consumer(const Params& P, Smem& S, uint32_t epoch) {
       const uint32_t tag = tag0 + static_cast<uint32_t>(si), in_tag = tag - 1u;
       if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
       const LayerPtrs& L = S.lp[kind == K_HEAD ? 0 : l];
+      // the stage's weight chunking does not depend on its input: set up
+      // before the input is polled
+      const int wk = kind == K_QKV ? ST_QKV : kind == K_O ? ST_O : kind == K_GU ? ST_GU : kind == K_DN ? ST_DN : ST_HEAD;
+      Chunking ch{};
+      if (kind != K_ATT) ch = stage_chunks(P, wk, l, S.gemv_grid);
       // -- stage the input activation in shared memory
       if (kind == K_QKV || kind == K_GU || kind == K_HEAD) {
         const __half* rows[NB];
@@ -1579,11 +1583,10 @@ __device__ void consumer(const Params& P, Smem& S, uint32_t epoch) {
           attn_item(P, S, L, bsel, kvh, sp, nsp, chunk, pb, in_tag, tag, nullptr);
         }
       } else if (kind == K_DN) {
-        gemv_down<NB>(P, S, cs, l, tag);
+        gemv_down<NB>(P, S, cs, l, tag, ch);
       } else {
-        const int wk = kind == K_QKV ? ST_QKV : kind == K_O ? ST_O : kind == K_GU ? ST_GU : ST_HEAD;
         __half* lg = (kind == K_HEAD && step == P.n_steps - 1) ? reinterpret_cast<__half*>(P.s.logits) : nullptr;
-        gemv_rows<NB>(P, S, cs, wk, l, lg, tag);
+        gemv_rows<NB>(P, S, cs, wk, l, lg, tag, ch);
         if (kind == K_HEAD) {
           consumer_sync();
           if (threadIdx.x < B) {
