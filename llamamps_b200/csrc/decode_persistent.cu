@@ -430,7 +430,7 @@ __device__ __forceinline__ void consumer_sum_n(float (&v)[NB], float* red8) {
     for (int w = 0; w < kConsumerWarps; ++w) t += red8[w * kMaxB + b];
     v[b] = t;
   }
-  consumer_sync();
+  // (no trailing sync: red8 is written again only after later block syncs)
 }
 
 // ---------------------------------------------------------------------------
@@ -807,29 +807,34 @@ __device__ void gemv_rows(const Params& P, Smem& S, CState& cs, int kind, int la
     return;
   }
   // -- epilogue of every row pair, published as tagged words.  Four lanes
-  // reduce one row entry (16 partials, one float4 each); the entries of a
-  // row pair are 2 (gate/up: 4) consecutive ones, so the pair's lanes are an
-  // aligned group of 8 (16) in one warp.
+  // per row: they reduce its 16 partials (gate/up: lanes 0-1 the gate
+  // entry, 2-3 the up entry, eight partials each), and the two rows of a
+  // pair are an aligned group of 8 lanes in one warp.
   consumer_sync();
   unsigned long long* dst = kind == ST_QKV ? P.qkvt : kind == ST_O ? P.x1t : P.at;
   const int dld = kind == ST_QKV ? (P.m.n_q_heads + 2 * P.m.n_kv_heads) * kHD / 2
                                  : (kind == ST_O ? P.m.hidden : P.m.intermediate) / 2;
-  const int per_b = (c.r1 - c.r0) * (gu ? 8 : 4);  // lanes per sequence
+  const int per_b = (c.r1 - c.r0) * 4;  // lanes per sequence
   for (int t0 = 0; t0 < NB * per_b; t0 += kConsumers) {
     const int t = t0 + threadIdx.x;
     const int b = t / per_b, rem = t - b * per_b;
-    const int e = rem >> 2, qq = rem & 3;
+    const int i = rem >> 2, q4 = rem & 3;  // i = row - c.r0
     const bool live = t < NB * per_b && b < P.s.batch;
     float v = 0.0f;
     if (live) {
-      const float4 p4 = *reinterpret_cast<const float4*>(part + (b * kPartRows + e) * 16 + 4 * qq);
-      v = (p4.x + p4.y) + (p4.z + p4.w);
+      if (gu) {
+        const float* pp = part + (b * kPartRows + 2 * i + (q4 >> 1)) * 16 + 8 * (q4 & 1);
+        const float4 a0 = *reinterpret_cast<const float4*>(pp), a1 = *reinterpret_cast<const float4*>(pp + 4);
+        v = ((a0.x + a0.y) + (a0.z + a0.w)) + ((a1.x + a1.y) + (a1.z + a1.w));
+      } else {
+        const float4 p4 = *reinterpret_cast<const float4*>(part + (b * kPartRows + i) * 16 + 4 * q4);
+        v = (p4.x + p4.y) + (p4.z + p4.w);
+      }
     }
     v += __shfl_xor_sync(0xffffffffu, v, 1);
-    v += __shfl_xor_sync(0xffffffffu, v, 2);
-    const float u = __shfl_down_sync(0xffffffffu, v, 4);  // gate/up: the up entry of the row
-    const int i = gu ? (e >> 1) : e;                       // row - c.r0
-    const bool row_lane = live && qq == 0 && (!gu || (e & 1) == 0);
+    if (!gu) v += __shfl_xor_sync(0xffffffffu, v, 2);
+    const float u = __shfl_down_sync(0xffffffffu, v, 2);  // gate/up: the row's up entry
+    const bool row_lane = live && q4 == 0;
     __half h;
     if (gu) {
       h = __float2half_rn(silu_mul(__half2float(__float2half_rn(v)), __half2float(__float2half_rn(u))));
@@ -840,7 +845,7 @@ __device__ void gemv_rows(const Params& P, Smem& S, CState& cs, int kind, int la
       if (row_lane) S.x1own[b * kOwnMax + i] = h;
     }
     const uint32_t hb = __half_as_ushort(h);
-    const uint32_t hp = __shfl_down_sync(0xffffffffu, hb, gu ? 8 : 4);  // the pair's second row
+    const uint32_t hp = __shfl_down_sync(0xffffffffu, hb, 4);  // the pair's second row
     if (row_lane && (i & 1) == 0)
       st_tagged(dst + static_cast<size_t>(b) * dld + (c.r0 + i) / 2, tagged(tag, hb | (hp << 16)));
   }
