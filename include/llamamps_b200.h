@@ -101,6 +101,10 @@ int lmps_residual_add(const uint16_t* x, const uint16_t* y, uint16_t* out, int n
 
 /* Replaces kernels/swiglu.metal:13-23 `swiglu`. */
 int lmps_swiglu(const uint16_t* gate, const uint16_t* up, uint16_t* out, int n, void* stream);
+/* SwiGLU of a fused gate|up projection: out[r][i] = silu(gu[r][i]) * gu[r][n + i]
+ * for rows x n (swiglu.metal; the gate and up halves of one GEMM output row,
+ * row stride ld >= 2n; out row stride ldo). */
+int lmps_swiglu_rows(const uint16_t* gate_up, int ld, int rows, int n, uint16_t* out, int ldo, void* stream);
 
 /* Replaces the embedding-row lookup of utils/tokenizer.py:22-26 on the device:
  * out[b, :] = table[ids[b], :] for an fp16 [vocab, dim] table.  Ids outside

@@ -48,6 +48,7 @@ _SIGS = {
     "lmps_decode_advance": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_vp]),
     "lmps_prefill_attention": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_vp, c_int, c_int, c_int,
                                        c_int, c_int, c_int, c_vp]),
+    "lmps_swiglu_rows": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_int, c_vp]),
     "lmps_argmax_rows": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_vp]),
     "lmps_w4a16_gemm_workspace_size": (c_size, [c_int, c_int]),
     "lmps_w4a16_gemm": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_vp, c_int, c_int, c_int, c_int,

@@ -269,6 +269,64 @@ __global__ void argmax_rows_kernel(const __half* logits, int ld, int n, int32_t*
   }
 }
 
+// out[r][i] = silu(gu[r][i]) * gu[r][n + i]: SwiGLU of a fused gate|up
+// projection row (swiglu.metal over the two halves of one GEMM output).
+__global__ void swiglu_rows_kernel(const __half* gu, int ld, int n, __half* out, int ldo, int rows) {
+  const int total = rows * n;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int r = i / n, c = i - r * n;
+    const __half* row = gu + static_cast<size_t>(r) * ld;
+    out[static_cast<size_t>(r) * ldo + c] = __float2half_rn(silu_mul(__half2float(row[c]), __half2float(row[n + c])));
+  }
+}
+
+// First-index argmax of each row, one thread-block cluster of kArgSplit
+// CTAs per row: every CTA scans a contiguous slice with 16-byte loads, the
+// cluster's rank 0 combines the CTAs' keys through distributed shared memory.
+constexpr int kArgSplit = 8;
+__global__ void argmax_rows_cluster_kernel(const __half* logits, int ld, int n, int32_t* ids) {
+  __shared__ unsigned long long red[32];
+  __shared__ unsigned long long cta_best;
+  const int row = blockIdx.y;
+  uint32_t rank;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+  const int chunk = ((n + kArgSplit - 1) / kArgSplit + 7) & ~7;
+  const int lo = static_cast<int>(rank) * chunk, hi = min(n, lo + chunk);
+  const __half* r = logits + static_cast<size_t>(row) * ld;
+  unsigned long long best = 0ull;
+  const int hi8 = lo + ((max(hi - lo, 0)) & ~7);
+  for (int i = lo + 8 * static_cast<int>(threadIdx.x); i < hi8; i += 8 * blockDim.x) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(r + i));
+    const __half* h = reinterpret_cast<const __half*>(&v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) best = u64_max(best, argmax_key(__half2float(h[e]), static_cast<uint32_t>(i + e)));
+  }
+  for (int i = hi8 + threadIdx.x; i < hi; i += blockDim.x)
+    best = u64_max(best, argmax_key(__half2float(r[i]), static_cast<uint32_t>(i)));
+  best = warp_max_u64(best);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) best = u64_max(best, red[w]);
+    cta_best = u64_max(best, red[0]);
+  }
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+  if (rank == 0 && threadIdx.x == 0) {
+    unsigned long long b = 0ull;
+    const uint32_t local = static_cast<uint32_t>(__cvta_generic_to_shared(&cta_best));
+    for (uint32_t c = 0; c < kArgSplit; ++c) {
+      uint32_t ra;
+      unsigned long long v;
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(local), "r"(c));
+      asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(ra) : "memory");
+      b = u64_max(b, v);
+    }
+    ids[row] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(b & 0xFFFFFFFFull));
+  }
+  // no CTA leaves while rank 0 may still read its key
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 }  // namespace lmps
 
 using namespace lmps;
@@ -395,6 +453,32 @@ extern "C" int lmps_decode_advance(const int32_t* next, int32_t* tokens, int32_t
 
 extern "C" int lmps_argmax_rows(const uint16_t* logits, int ld, int rows, int n, int32_t* ids, void* stream) {
   LMPS_CHECK_ARG(logits && ids && rows > 0 && n > 0 && ld >= n);
+  if (ld % 8 == 0 && lmps_aligned(logits, 16) && rows <= 65535 && n >= 8 * kArgSplit) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(kArgSplit, rows);
+    cfg.blockDim = dim3(512);
+    cfg.stream = lmps_stream(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kArgSplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, argmax_rows_cluster_kernel, CH(logits), ld, n, ids);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    return lmps_launch_status();
+  }
   argmax_rows_kernel<<<rows, 512, 0, lmps_stream(stream)>>>(CH(logits), ld, n, ids);
+  return lmps_launch_status();
+}
+
+extern "C" int lmps_swiglu_rows(const uint16_t* gate_up, int ld, int rows, int n, uint16_t* out, int ldo,
+                                void* stream) {
+  LMPS_CHECK_ARG(gate_up && out && rows > 0 && n > 0 && ld >= 2 * n && ldo >= n);
+  const long long total = static_cast<long long>(rows) * n;
+  LMPS_CHECK_ARG(total < (1LL << 31));
+  const int blocks = static_cast<int>(min((total + 255) / 256, 148LL * 16));
+  swiglu_rows_kernel<<<blocks, 256, 0, lmps_stream(stream)>>>(CH(gate_up), ld, n, H(out), ldo, rows);
   return lmps_launch_status();
 }

@@ -103,7 +103,8 @@ class QwenEngine:
         self.buf_attn = torch.zeros(B, c.q_dim, dtype=h, device=dev)
         self.buf_mlp = torch.zeros(B, c.intermediate, dtype=h, device=dev)
         # gate/up outputs of the tensor-core GEMM path (batches past the GEMV's 8)
-        self.buf_up = torch.zeros(B if B > GEMV_MAX_BATCH else 1, c.intermediate, dtype=h, device=dev)
+        # fused gate|up GEMM output (batched path): [B, 2 * intermediate]
+        self.buf_up = torch.zeros(B if B > GEMV_MAX_BATCH else 1, 2 * c.intermediate, dtype=h, device=dev)
         self.gemm_err = torch.zeros(1, dtype=torch.int32, device=dev)
         # split-K partial tiles of the small-m GEMMs (zero between calls)
         ws = K.w4a16_gemm_workspace_size(B, c.intermediate) if B > GEMV_MAX_BATCH else 0
@@ -167,15 +168,27 @@ class QwenEngine:
             self._o_proj(lw, self.buf_attn[:B], x, gemm)
             K.rms_norm(x, lw.post_norm, c.eps, out=xn)
             if gemm:
-                K.w4a16_gemm(xn, lw.gate_packed, lw.gate_scales, c.intermediate, c.hidden,
-                             out=self.buf_mlp[:B], error=self.gemm_err, workspace=self.gemm_ws)
-                K.w4a16_gemm(xn, lw.up_packed, lw.up_scales, c.intermediate, c.hidden,
-                             out=self.buf_up[:B], error=self.gemm_err, workspace=self.gemm_ws)
-                K.swiglu(self.buf_mlp[:B], self.buf_up[:B], out=self.buf_mlp[:B])
+                self._gate_up(lw, xn, self.buf_up[:B], self.buf_mlp[:B])
             else:
                 K.gemv_q4_swiglu(lw.gate_packed, lw.gate_scales, lw.up_packed, lw.up_scales, xn,
                                  c.intermediate, c.hidden, out=self.buf_mlp[:B])
             self._down_proj(lw, self.buf_mlp[:B], x, gemm)
+
+    def _gate_up(self, lw, xn, gu, out, ws=None) -> None:
+        """a = SwiGLU(W_gate xn, W_up xn) on the GEMM path: one GEMM over the
+        fused gate|up rows when the layer stores them together, else two."""
+        c = self.cfg
+        if lw.gu_packed is not None:
+            K.w4a16_gemm(xn, lw.gu_packed, lw.gu_scales, 2 * c.intermediate, c.hidden, out=gu,
+                         error=self.gemm_err, workspace=self._ws(ws))
+            K.swiglu_rows(gu, c.intermediate, out)
+        else:
+            up = gu.reshape(-1)[:out.numel()].view(out.shape)  # contiguous [B, intermediate] scratch
+            K.w4a16_gemm(xn, lw.gate_packed, lw.gate_scales, c.intermediate, c.hidden, out=out,
+                         error=self.gemm_err, workspace=self._ws(ws))
+            K.w4a16_gemm(xn, lw.up_packed, lw.up_scales, c.intermediate, c.hidden, out=up,
+                         error=self.gemm_err, workspace=self._ws(ws))
+            K.swiglu(out, up, out=out)
 
     # x <- x + fp16(W_o attn) and x <- x + fp16(W_down a) (runners/engine.py:215-221,237-243);
     # the tensor-parallel engine overrides these with partial products and an all-reduce
@@ -399,7 +412,7 @@ class QwenEngine:
         q = torch.empty(Mt, c.q_dim, dtype=h, device=dev)
         att = torch.empty(Mt, c.q_dim, dtype=h, device=dev)
         gate = torch.empty(Mt, c.intermediate, dtype=h, device=dev)
-        up = torch.empty_like(gate)
+        gu = torch.empty(Mt, 2 * c.intermediate, dtype=h, device=dev)
         err = self.gemm_err
         K.embed_gather(w.embed, ids, x, self.bad_ids)
         for li, lw in enumerate(w.layers):
@@ -413,9 +426,7 @@ class QwenEngine:
                                 c.n_q_heads, c.n_kv_heads, c.head_dim)
             self._o_proj(lw, att, x, True, ws=False)
             K.rms_norm(x, lw.post_norm, c.eps, out=xn)
-            K.w4a16_gemm(xn, lw.gate_packed, lw.gate_scales, c.intermediate, c.hidden, out=gate, error=err)
-            K.w4a16_gemm(xn, lw.up_packed, lw.up_scales, c.intermediate, c.hidden, out=up, error=err)
-            K.swiglu(gate, up, out=gate)
+            self._gate_up(lw, xn, gu, gate, ws=False)
             self._down_proj(lw, gate, x, True, ws=False)
         # last position of every sequence -> final norm, LM head, argmax
         self.buf_residual[:B].copy_(x.view(B, P, c.hidden)[:, P - 1])

@@ -116,6 +116,13 @@ def swiglu(gate, up, out=None):
     return o
 
 
+def swiglu_rows(gate_up, n: int, out):
+    """out[r] = silu(gate_up[r, :n]) * gate_up[r, n:2n] (a fused gate|up GEMM output)."""
+    call("lmps_swiglu_rows", _dev(gate_up, "gate_up", FP16), gate_up.shape[-1], gate_up.shape[0], n,
+         _dev(out, "out", FP16), out.shape[-1], _stream())
+    return out
+
+
 def embed_gather(table, ids, out, bad: Optional[torch.Tensor] = None):
     V, D = table.shape
     call("lmps_embed_gather", _dev(table, "table", FP16), _dev(ids, "ids", torch.int32),

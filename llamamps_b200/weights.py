@@ -49,6 +49,11 @@ class LayerWeights:
     up_scales: torch.Tensor
     down_packed: torch.Tensor
     down_scales: torch.Tensor
+    # gate rows then up rows in one allocation (gate_* / up_* are views of
+    # it): the batched path runs both projections as one GEMM.  None when the
+    # two matrices are separate allocations.
+    gu_packed: Optional[torch.Tensor] = None
+    gu_scales: Optional[torch.Tensor] = None
 
     def q4_bytes(self) -> int:
         ts = [self.qkv_packed, self.qkv_scales, self.o_packed, self.o_scales, self.gate_packed,
@@ -87,6 +92,11 @@ def layer_from_parts(cfg: ModelConfig, parts: Dict[str, torch.Tensor], device) -
     for n, rows in (("q", cfg.q_dim), ("k", cfg.kv_dim), ("v", cfg.kv_dim)):
         b = parts.get(f"{n}_bias")
         bias.append(t(b, torch.float16) if b is not None else torch.zeros(rows, dtype=torch.float16, device=dev))
+    gp, gs = t(parts["gate_packed"], torch.uint8), t(parts["gate_scales"], torch.float16)
+    gu_packed = torch.cat([gp, t(parts["up_packed"], torch.uint8)])
+    gu_scales = torch.cat([gs, t(parts["up_scales"], torch.float16)])
+    ng, ngs = gp.numel(), gs.numel()
+    del gp, gs
     return LayerWeights(
         in_norm=t(parts["in_norm"], torch.float16),
         post_norm=t(parts["post_norm"], torch.float16),
@@ -94,9 +104,10 @@ def layer_from_parts(cfg: ModelConfig, parts: Dict[str, torch.Tensor], device) -
         qkv_scales=torch.cat([t(parts[f"{n}_scales"], torch.float16) for n in "qkv"]),
         qkv_bias=torch.cat(bias),
         o_packed=t(parts["o_packed"], torch.uint8), o_scales=t(parts["o_scales"], torch.float16),
-        gate_packed=t(parts["gate_packed"], torch.uint8), gate_scales=t(parts["gate_scales"], torch.float16),
-        up_packed=t(parts["up_packed"], torch.uint8), up_scales=t(parts["up_scales"], torch.float16),
+        gate_packed=gu_packed[:ng], gate_scales=gu_scales[:ngs],
+        up_packed=gu_packed[ng:], up_scales=gu_scales[ngs:],
         down_packed=t(parts["down_packed"], torch.uint8), down_scales=t(parts["down_scales"], torch.float16),
+        gu_packed=gu_packed, gu_scales=gu_scales,
     )
 
 

@@ -57,6 +57,35 @@ def test_argmax_rows_first_index(cuda):
     assert ids.tolist() == [5, 7, 999]
 
 
+def test_argmax_rows_cluster_path_and_ties_across_slices(cuda):
+    """Vocabulary-sized rows take the cluster path (8 CTAs per row, one
+    slice each): ties across slices resolve to the first index and the
+    ragged tail is scanned."""
+    from llamamps_b200 import kernels as K
+    V = 151936 + 8 * 3 + 5            # not a multiple of the slice alignment
+    x = torch.randn(6, V, generator=torch.Generator(device="cuda").manual_seed(4), device="cuda").half()
+    x[0, 100] = 9.0
+    x[0, V - 3] = 9.0                 # tie in the last slice: first index wins
+    x[1, V - 1] = 11.0                # the ragged tail
+    x[2, 50000] = 8.0
+    x[2, 19000] = 8.0                 # tie across slices
+    ids = torch.zeros(6, dtype=torch.int32, device="cuda")
+    K.argmax_rows(x, V, ids)
+    ref = [int(torch.argmax(x[r].float()).item()) for r in range(6)]
+    assert ids.tolist()[:3] == [100, V - 1, 19000]
+    assert ids.tolist() == ref
+
+
+def test_swiglu_rows_matches_two_input_swiglu(cuda):
+    from llamamps_b200 import kernels as K
+    g = torch.Generator(device="cuda").manual_seed(2)
+    gu = torch.randn(5, 2 * 300, generator=g, device="cuda").half()
+    out = torch.empty(5, 300, dtype=torch.float16, device="cuda")
+    K.swiglu_rows(gu, 300, out)
+    ref = K.swiglu(gu[:, :300].contiguous(), gu[:, 300:].contiguous())
+    assert torch.equal(out, ref)
+
+
 @pytest.mark.parametrize("decoder", ["kernels", "persistent"])
 def test_dense_prefill_matches_oracle(cuda, small_model, decoder):
     """Prompts prefilled all at once on the GEMM path (3 x 100 tokens), then
