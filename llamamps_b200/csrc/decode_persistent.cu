@@ -143,6 +143,7 @@ struct Params {
   uint32_t* att_cnt;  // [kMaxB, Hkv] split arrivals (reset by the last split)
   uint32_t* epoch;    // [1] tag base of the next launch
   int max_splits;
+  int kv_pipe;        // 1: a second per-warp K buffer follows the attention area (long caches)
 };
 
 enum StageKind { ST_QKV = 0, ST_O = 1, ST_GU = 2, ST_DN = 3, ST_HEAD = 4 };
@@ -1055,6 +1056,7 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
       }
     }
   }
+  asm volatile("cp.async.commit_group;" ::: "memory");  // (its own group: the flash loop counts them)
   // cache offset of position pos (the KV append of the split holding it)
   const size_t app =
       has_pos ? ((static_cast<size_t>(__ldg(bt + (pos >> pshift))) * Hkv + kvh) * ps + (pos & (ps - 1))) * kHD : 0;
@@ -1140,7 +1142,13 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
   // rotated q in shared memory, the new k/v row in the cache
 
   // -- per-warp flash loop over 16-position blocks
-  asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's staged K rows
+  // Long items (kv_pipe, more blocks than warps): a warp's K rows are
+  // double-buffered in shared memory -- block j+1's rows are copied
+  // (cp.async) while block j computes -- and its V rows come from L2 behind
+  // an L2 prefetch one block ahead.
+  const bool pipe = !kvs && P.kv_pipe && nblk > kConsumerWarps;
+  uint4* kbuf[2] = {&A.kst[0][0][0], reinterpret_cast<uint4*>(S.act + sizeof(AttnSmem))};
+  if (!pipe) asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's staged K rows
   uint32_t qf[16];  // B operand Q^T: head g8, physical dims 32*t4 .. 32*t4+31
   {
     const uint4* qs = reinterpret_cast<const uint4*>(&A.q[g8 < G ? g8 : 0][32 * t4]);
@@ -1159,16 +1167,30 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
   float mrun0 = -INFINITY, mrun1 = -INFINITY, lrun0 = 0.0f, lrun1 = 0.0f;  // heads 2*t4, 2*t4+1
   for (int bi = warp; bi < nblk; bi += kConsumerWarps) {
     const int p0 = start + bi * kBlk;
-    if (!kvs && bi + kConsumerWarps < nblk) {  // this warp's next block into L2 while this one computes
+    const int jb = (bi - warp) / kConsumerWarps;  // this warp's block ordinal
+    if (!kvs && bi + kConsumerWarps < nblk) {  // this warp's next block: K into shared memory (pipe) or L2
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
         const int p = p0 + kConsumerWarps * kBlk + 8 * h2 + g8;
-        if (p < end && p != pos) {
+        if (p < end) {
           const size_t off = row_off(p);
-          asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(kpool + off));
-          asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(vpool + off));
+          if (pipe) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(
+                               kbuf[(jb + 1) & 1] + (warp * 8 + 4 * h2 + c) * 32 + lane)),
+                           "l"(kpool + off + 8 * c)
+                           : "memory");
+          } else if (p != pos) {
+            asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(kpool + off));
+          }
+          if (p != pos) asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(vpool + off));
         }
       }
+    }
+    if (pipe) {  // block jb's group complete (the one just committed may stay in flight)
+      asm volatile("cp.async.commit_group;" ::: "memory");
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
     }
     // K/V rows p0+g8 and p0+8+g8, dims 32*t4 .. 32*t4+31 (the row of pos was
     // appended by this CTA before the last block sync); the K rows of the
@@ -1190,14 +1212,15 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
           kr[h2][c] = kvs[kv_tile_idx(bi, 0, h2, c, lane)];
           vr[h2][c] = ok[h2] ? kvs[kv_tile_idx(bi, 1, h2, c, lane)] : make_uint4(0u, 0u, 0u, 0u);
         }
-    } else if (bi == warp) {  // rows past the end are masked out of the scores below
+    } else if (bi == warp || pipe) {  // staged K rows; rows past the end are masked out of the scores
+      const uint4* kb = kbuf[jb & 1] + warp * 8 * 32;
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) kr[h2][c] = A.kst[warp][4 * h2 + c][lane];
+        for (int c = 0; c < 4; ++c) kr[h2][c] = kb[(4 * h2 + c) * 32 + lane];
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2)
-        if (p0 + 8 * h2 + g8 == pos)
+        if (bi == warp && p0 + 8 * h2 + g8 == pos)  // (staged before pos's row was appended)
 #pragma unroll
           for (int c = 0; c < 4; ++c) kr[h2][c] = __ldcg(reinterpret_cast<const uint4*>(kpool + off[h2]) + c);
     } else {
@@ -1317,26 +1340,45 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
     }
     consumer_sync();
     __threadfence();
-#pragma unroll 1
+    // split weights exp(m_sp - M) of every (head, split), one warp per head
+    // with the splits across its lanes; then every (head, dim pair) adds the
+    // weighted partial outputs (loads unrolled, several in flight)
+    float* wsm = &A.wo[0][0][0];      // [G][n_splits] weights
+    float* inv_den = wsm + G * n_splits;  // [G]
+    if (warp < G) {
+      const size_t prow0 = (static_cast<size_t>(b) * Hq + kvh * G + warp) * ms;
+      float M = -INFINITY;
+      for (int sp = lane; sp < n_splits; sp += kWarp) {
+        const float2 ml = __ldcg(&P.part_ml[prow0 + sp]);
+        if (ml.y > 0.0f) M = fmaxf(M, ml.x);
+      }
+      M = warp_max(M);
+      float den = 0.0f;
+      for (int sp = lane; sp < n_splits; sp += kWarp) {
+        const float2 ml = __ldcg(&P.part_ml[prow0 + sp]);
+        const float wgt = ml.y > 0.0f ? expf(ml.x - M) : 0.0f;
+        wsm[warp * n_splits + sp] = wgt;
+        den = fmaf(wgt, ml.y, den);
+      }
+      den = warp_sum(den);
+      if (lane == 0) inv_den[warp] = den > 0.0f ? 1.0f / den : 0.0f;
+    }
+    consumer_sync();
     for (int w = tid; w < G * (kHD / 2); w += kConsumers) {
       const int h = w / (kHD / 2), dp = w - h * (kHD / 2);
       const size_t prow0 = (static_cast<size_t>(b) * Hq + kvh * G + h) * ms;
-      float M = -INFINITY;
-#pragma unroll 1
-      for (int sp = 0; sp < n_splits; ++sp) M = fmaxf(M, __ldcg(&P.part_ml[prow0 + sp].x));
-      float n0 = 0.0f, n1 = 0.0f, den = 0.0f;
-#pragma unroll 1
+      const float* wh = wsm + h * n_splits;
+      float n0 = 0.0f, n1 = 0.0f;
+#pragma unroll 4
       for (int sp = 0; sp < n_splits; ++sp) {
-        const float2 ml = __ldcg(&P.part_ml[prow0 + sp]);
-        if (ml.y > 0.0f) {
-          const float wgt = expf(ml.x - M);
-          const float2 po = __ldcg(reinterpret_cast<const float2*>(&P.part_o[(prow0 + sp) * kHD + 2 * dp]));
+        const float wgt = wh[sp];
+        const float2 po = __ldcg(reinterpret_cast<const float2*>(&P.part_o[(prow0 + sp) * kHD + 2 * dp]));
+        if (wgt != 0.0f) {
           n0 = fmaf(wgt, po.x, n0);
           n1 = fmaf(wgt, po.y, n1);
-          den = fmaf(wgt, ml.y, den);
         }
       }
-      const float inv = den > 0.0f ? 1.0f / den : 0.0f;
+      const float inv = inv_den[h];
       st_tagged(out + (kvh * G + h) * (kHD / 2) + dp, tagged(out_tag, pack_half2(n0 * inv, n1 * inv)));
     }
   }
@@ -1758,8 +1800,8 @@ static WsLayout ws_layout(const lmps_model_desc& m, int B, int max_seq_len) {
   return w;
 }
 
-static int act_bytes_for(const lmps_model_desc& m, int nb) {
-  size_t a = sizeof(AttnSmem);
+static int act_bytes_for(const lmps_model_desc& m, int nb, int kv_pipe) {
+  size_t a = sizeof(AttnSmem) + (kv_pipe ? sizeof(uint4) * kConsumerWarps * 8 * 32 : 0);
   const size_t grp = 16 * 4 + 4 + 4;  // plane words + scl + xs8 per group
   // k = hidden stages: planes + per-lane partials of every row entry
   // (+16: the partials start 16-byte aligned)
@@ -1780,7 +1822,7 @@ static int launch(const Params& P0, const lmps_model_desc& m, cudaStream_t st) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  P.act_bytes = act_bytes_for(m, NB);
+  P.act_bytes = act_bytes_for(m, NB, P.kv_pipe);
   // rows of the hidden and q|k|v outputs one CTA owns (residual / bias kept in shared memory)
   const int qkv_rows = (m.n_q_heads + 2 * m.n_kv_heads) * m.head_dim;
   // (pair-aligned partitions: at most 2 * ceil(rows / 2 / ctas) rows per CTA,
@@ -1874,6 +1916,9 @@ extern "C" int lmps_decode_persistent(const lmps_model_desc* model, const lmps_d
   P.att_cnt = reinterpret_cast<uint32_t*>(ws + w.att_cnt);
   P.epoch = reinterpret_cast<uint32_t*>(ws + w.epoch);
   P.max_splits = w.max_splits;
+  // long caches: the attention items hold many blocks per warp, worth a
+  // second K buffer (and two fewer ring slots)
+  P.kv_pipe = s.max_seq_len > 2048 ? 1 : 0;
   cudaStream_t st = lmps_stream(stream);
   switch (s.batch) {
     case 1: return pk::launch<1>(P, m, st);
