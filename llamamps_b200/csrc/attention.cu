@@ -47,6 +47,8 @@ struct __align__(16) AttnSmem {
 };
 
 __global__ void __launch_bounds__(kAttnThreads) gqa_decode_attn_kernel(const AttnParams P) {
+  lmps_pdl_trigger();
+  lmps_pdl_wait();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   AttnSmem& S = *reinterpret_cast<AttnSmem*>(smem_raw);
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -73,20 +75,30 @@ __global__ void __launch_bounds__(kAttnThreads) gqa_decode_attn_kernel(const Att
   const int32_t* bt = P.block_table + static_cast<size_t>(b) * P.max_pages;
   for (int t0 = start; t0 < end; t0 += kAttnTile) {
     const int n = min(kAttnTile, end - t0);
-    // Stage K and V rows of this tile: 16 threads per 256-byte row.
-    for (int i = tid; i < kAttnTile * (kHeadDim / 8); i += kAttnThreads) {
-      const int r = i / (kHeadDim / 8), c = i - r * (kHeadDim / 8);
-      uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = make_uint4(0u, 0u, 0u, 0u);
+    // Stage K and V rows of this tile: 16 threads per 256-byte row.  All of a
+    // thread's loads are issued before any of its shared-memory stores, so
+    // the tile costs one memory round trip, not one per row it stages.
+    constexpr int kPer = kAttnTile * (kHeadDim / 8) / kAttnThreads;
+    uint4 kv[kPer], vv[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int i = tid + j * kAttnThreads, r = i / (kHeadDim / 8), c = i - r * (kHeadDim / 8);
+      kv[j] = make_uint4(0u, 0u, 0u, 0u);
+      vv[j] = kv[j];
       if (r < n) {
         const int pos = t0 + r;
-        const int page = bt[pos / P.page_size];
+        const int page = __ldg(bt + pos / P.page_size);
         const size_t off = ((static_cast<size_t>(page) * P.n_kv_heads + kvh) * P.page_size +
                              pos % P.page_size) * kHeadDim + c * 8;
-        kv = *reinterpret_cast<const uint4*>(P.k_pool + off);
-        vv = *reinterpret_cast<const uint4*>(P.v_pool + off);
+        kv[j] = __ldcg(reinterpret_cast<const uint4*>(P.k_pool + off));
+        vv[j] = __ldcg(reinterpret_cast<const uint4*>(P.v_pool + off));
       }
-      *reinterpret_cast<uint4*>(&S.k[r][c * 8]) = kv;
-      *reinterpret_cast<uint4*>(&S.v[r][c * 8]) = vv;
+    }
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int i = tid + j * kAttnThreads, r = i / (kHeadDim / 8), c = i - r * (kHeadDim / 8);
+      *reinterpret_cast<uint4*>(&S.k[r][c * 8]) = kv[j];
+      *reinterpret_cast<uint4*>(&S.v[r][c * 8]) = vv[j];
     }
     __syncthreads();
     // Scores: thread -> (position r, head parity hs); heads hs, hs+2, ...
@@ -188,6 +200,8 @@ __global__ void __launch_bounds__(kAttnThreads) gqa_decode_attn_kernel(const Att
 
 // Merge the per-split partials of one (sequence, query head): log-sum-exp.
 __global__ void __launch_bounds__(kHeadDim) gqa_combine_kernel(const AttnParams P) {
+  lmps_pdl_trigger();
+  lmps_pdl_wait();
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const size_t row0 = (static_cast<size_t>(b) * P.n_q_heads + h) * P.n_splits;
   float M = -INFINITY;
@@ -277,11 +291,9 @@ extern "C" int lmps_gqa_decode_attention(const uint16_t* q, const uint16_t* k_po
   }
   cudaStream_t st = lmps_stream(stream);
   dim3 grid(n_splits, n_kv_heads, batch);
-  gqa_decode_attn_kernel<<<grid, kAttnThreads, smem, st>>>(P);
-  int status = lmps_launch_status();
+  int status = lmps_launch_pdl(gqa_decode_attn_kernel, grid, dim3(kAttnThreads), smem, st, P);
   if (status || n_splits == 1) return status;
-  gqa_combine_kernel<<<dim3(n_q_heads, batch), kHeadDim, 0, st>>>(P);
-  return lmps_launch_status();
+  return lmps_launch_pdl(gqa_combine_kernel, dim3(n_q_heads, batch), dim3(kHeadDim), 0, st, P);
 }
 
 // ---------------------------------------------------------------------------

@@ -20,6 +20,32 @@ static inline int lmps_launch_status() {
 
 static inline cudaStream_t lmps_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Programmatic dependent launch: the kernel may begin while its predecessor
+// in the stream is still running.  Such a kernel triggers its own dependents
+// early (lmps_pdl_trigger) and calls lmps_pdl_wait() in every thread before
+// it reads or writes anything an earlier kernel writes or reads (waiting
+// means the predecessor -- and through it every earlier grid -- completed).
+// Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void lmps_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void lmps_pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+static inline int lmps_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                  Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  return e == cudaSuccess ? lmps_launch_status() : static_cast<int>(e);
+}
+
 static inline bool lmps_aligned(const void* p, uintptr_t a) {
   return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
 }

@@ -29,6 +29,8 @@ __device__ __forceinline__ float block_sum_256(float v, float* red) {
 __global__ void __launch_bounds__(kNormThreads)
 rms_norm_kernel(const __half* __restrict__ x, const __half* __restrict__ gamma,
                 __half* __restrict__ out, int dim, float eps) {
+  lmps_pdl_trigger();
+  lmps_pdl_wait();
   __shared__ float red[kNormThreads / kWarp];
   const __half* xr = x + static_cast<size_t>(blockIdx.x) * dim;
   __half* orow = out + static_cast<size_t>(blockIdx.x) * dim;
@@ -95,6 +97,8 @@ __global__ void rope_kv_append_kernel(const __half* __restrict__ qkv, const int3
                                       const int32_t* __restrict__ block_table, int max_pages,
                                       int page_size, int n_q_heads, int n_kv_heads, int head_dim,
                                       int style) {
+  lmps_pdl_trigger();
+  lmps_pdl_wait();
   const int b = blockIdx.x;
   const int q_dim = n_q_heads * head_dim, kv_dim = n_kv_heads * head_dim;
   const __half* row = qkv + static_cast<size_t>(b) * (q_dim + 2 * kv_dim);
@@ -141,6 +145,8 @@ __global__ void swiglu_kernel(const __half* g, const __half* u, __half* out, int
 // utils/tokenizer.py:22-26 -- one fp16 row per sequence.
 __global__ void embed_gather_kernel(const __half* table, const int32_t* ids, __half* out, int dim,
                                     int vocab, int32_t* bad) {
+  lmps_pdl_trigger();
+  lmps_pdl_wait();
   const int b = blockIdx.x;
   const int id = ids[b];
   const bool ok = id >= 0 && id < vocab;
@@ -239,6 +245,8 @@ __global__ void q4_pack_kernel(const float* __restrict__ w, long long n, uint8_t
 __global__ void decode_advance_kernel(const int32_t* next, int32_t* tokens, int32_t* pos,
                                       int32_t* seq_lens, int32_t* history, int32_t* step,
                                       int max_steps, int batch) {
+  lmps_pdl_trigger();
+  lmps_pdl_wait();
   const int s = (history && step) ? step[0] : 0;
   for (int b = threadIdx.x; b < batch; b += blockDim.x) {
     const int32_t t = next[b];
@@ -254,6 +262,8 @@ __global__ void decode_advance_kernel(const int32_t* next, int32_t* tokens, int3
 // Row-wise first-index argmax of fp16 logits (runners/engine.py:180-181:
 // numpy.argmax over fp32(logits)); one block per row.
 __global__ void argmax_rows_kernel(const __half* logits, int ld, int n, int32_t* ids) {
+  lmps_pdl_trigger();
+  lmps_pdl_wait();
   const __half* row = logits + static_cast<size_t>(blockIdx.x) * ld;
   unsigned long long best = 0ull;
   for (int i = threadIdx.x; i < n; i += blockDim.x)
@@ -272,6 +282,8 @@ __global__ void argmax_rows_kernel(const __half* logits, int ld, int n, int32_t*
 // out[r][i] = silu(gu[r][i]) * gu[r][n + i]: SwiGLU of a fused gate|up
 // projection row (swiglu.metal over the two halves of one GEMM output).
 __global__ void swiglu_rows_kernel(const __half* gu, int ld, int n, __half* out, int ldo, int rows) {
+  lmps_pdl_trigger();
+  lmps_pdl_wait();
   const int total = rows * n;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
     const int r = i / n, c = i - r * n;
@@ -285,6 +297,8 @@ __global__ void swiglu_rows_kernel(const __half* gu, int ld, int n, __half* out,
 // cluster's rank 0 combines the CTAs' keys through distributed shared memory.
 constexpr int kArgSplit = 8;
 __global__ void argmax_rows_cluster_kernel(const __half* logits, int ld, int n, int32_t* ids) {
+  lmps_pdl_trigger();
+  lmps_pdl_wait();
   __shared__ unsigned long long red[32];
   __shared__ unsigned long long cta_best;
   const int row = blockIdx.y;
@@ -352,8 +366,8 @@ extern "C" const char* lmps_status_string(int status) {
 extern "C" int lmps_rms_norm(const uint16_t* x, const uint16_t* gamma, uint16_t* out, int dim,
                              int batch, float eps, void* stream) {
   LMPS_CHECK_ARG(x && gamma && out && dim > 0 && batch > 0 && eps >= 0.0f);
-  rms_norm_kernel<<<batch, kNormThreads, 0, lmps_stream(stream)>>>(CH(x), CH(gamma), H(out), dim, eps);
-  return lmps_launch_status();
+  return lmps_launch_pdl(rms_norm_kernel, dim3(batch), dim3(kNormThreads), 0, lmps_stream(stream), CH(x), CH(gamma),
+                         H(out), dim, eps);
 }
 
 extern "C" int lmps_rope(uint16_t* vec, const int32_t* pos, const float* inv_freq, int n_heads,
@@ -376,10 +390,9 @@ extern "C" int lmps_rope_kv_append(const uint16_t* qkv, const int32_t* pos, cons
   LMPS_CHECK_ARG(max_pages > 0 && page_size > 0 && batch > 0 && head_dim > 0 && head_dim % 2 == 0);
   LMPS_CHECK_ARG(n_kv_heads > 0 && n_q_heads > 0 && n_q_heads % n_kv_heads == 0);
   LMPS_CHECK_ARG(style == LMPS_ROPE_INTERLEAVED || style == LMPS_ROPE_NEOX);
-  rope_kv_append_kernel<<<batch, 256, 0, lmps_stream(stream)>>>(
-      CH(qkv), pos, inv_freq, H(q_out), H(k_pool), H(v_pool), block_table, max_pages, page_size,
-      n_q_heads, n_kv_heads, head_dim, style);
-  return lmps_launch_status();
+  return lmps_launch_pdl(rope_kv_append_kernel, dim3(batch), dim3(256), 0, lmps_stream(stream), CH(qkv), pos,
+                         inv_freq, H(q_out), H(k_pool), H(v_pool), block_table, max_pages, page_size, n_q_heads,
+                         n_kv_heads, head_dim, style);
 }
 
 extern "C" int lmps_residual_add(const uint16_t* x, const uint16_t* y, uint16_t* out, int n,
@@ -399,8 +412,8 @@ extern "C" int lmps_swiglu(const uint16_t* gate, const uint16_t* up, uint16_t* o
 extern "C" int lmps_embed_gather(const uint16_t* table, const int32_t* ids, uint16_t* out, int dim,
                                  int vocab, int batch, int32_t* bad_ids, void* stream) {
   LMPS_CHECK_ARG(table && ids && out && dim > 0 && vocab > 0 && batch > 0);
-  embed_gather_kernel<<<batch, 256, 0, lmps_stream(stream)>>>(CH(table), ids, H(out), dim, vocab, bad_ids);
-  return lmps_launch_status();
+  return lmps_launch_pdl(embed_gather_kernel, dim3(batch), dim3(256), 0, lmps_stream(stream), CH(table), ids, H(out),
+                         dim, vocab, bad_ids);
 }
 
 extern "C" int lmps_attention_scores(const uint16_t* q, const uint16_t* k_cache, float* scores,
@@ -446,9 +459,8 @@ extern "C" int lmps_decode_advance(const int32_t* next, int32_t* tokens, int32_t
                                    int max_steps, int batch, void* stream) {
   LMPS_CHECK_ARG(next && tokens && batch > 0 && batch <= 4096);
   LMPS_CHECK_ARG(!history || (step && max_steps > 0));
-  decode_advance_kernel<<<1, 256, 0, lmps_stream(stream)>>>(next, tokens, pos, seq_lens, history,
-                                                            step, max_steps, batch);
-  return lmps_launch_status();
+  return lmps_launch_pdl(decode_advance_kernel, dim3(1), dim3(256), 0, lmps_stream(stream), next, tokens, pos,
+                         seq_lens, history, step, max_steps, batch);
 }
 
 extern "C" int lmps_argmax_rows(const uint16_t* logits, int ld, int rows, int n, int32_t* ids, void* stream) {
@@ -458,19 +470,20 @@ extern "C" int lmps_argmax_rows(const uint16_t* logits, int ld, int rows, int n,
     cfg.gridDim = dim3(kArgSplit, rows);
     cfg.blockDim = dim3(512);
     cfg.stream = lmps_stream(stream);
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = kArgSplit;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, argmax_rows_cluster_kernel, CH(logits), ld, n, ids);
     if (e != cudaSuccess) return static_cast<int>(e);
     return lmps_launch_status();
   }
-  argmax_rows_kernel<<<rows, 512, 0, lmps_stream(stream)>>>(CH(logits), ld, n, ids);
-  return lmps_launch_status();
+  return lmps_launch_pdl(argmax_rows_kernel, dim3(rows), dim3(512), 0, lmps_stream(stream), CH(logits), ld, n, ids);
 }
 
 extern "C" int lmps_swiglu_rows(const uint16_t* gate_up, int ld, int rows, int n, uint16_t* out, int ldo,
@@ -479,6 +492,6 @@ extern "C" int lmps_swiglu_rows(const uint16_t* gate_up, int ld, int rows, int n
   const long long total = static_cast<long long>(rows) * n;
   LMPS_CHECK_ARG(total < (1LL << 31));
   const int blocks = static_cast<int>(min((total + 255) / 256, 148LL * 16));
-  swiglu_rows_kernel<<<blocks, 256, 0, lmps_stream(stream)>>>(CH(gate_up), ld, n, H(out), ldo, rows);
-  return lmps_launch_status();
+  return lmps_launch_pdl(swiglu_rows_kernel, dim3(blocks), dim3(256), 0, lmps_stream(stream), CH(gate_up), ld, n,
+                         H(out), ldo, rows);
 }

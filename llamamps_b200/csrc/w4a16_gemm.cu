@@ -221,6 +221,7 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_kernel(const __grid_const
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   volatile int* abort_v = abort_flag;
 
+  lmps_pdl_trigger();  // the next kernel may start its own prologue
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * kRows, m0 = blockIdx.y * P.xrows;
   const int kbeg = blockIdx.z * P.ksteps_per_split;
@@ -276,9 +277,8 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_kernel(const __grid_const
     tma_load_2d(xs + static_cast<size_t>(xk % SX) * xbytes, &P.tx, (kbeg + xk) * kBK, m0, &fullx[xk % SX]);
     ++xk;
   };
-  if (tid == 0) {
+  if (tid == 0) {  // weights and scales are constant: they load before the previous kernel is done
     while (wk < nwb && wk < R) issue_w();
-    while (xk < ksteps && xk < SX) issue_x();
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -286,6 +286,8 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_kernel(const __grid_const
   const uint32_t tmem = *tmem_slot;
 
   if (tid == 0) {
+    lmps_pdl_wait();  // X is the previous kernel's output
+    while (xk < ksteps && xk < SX) issue_x();
     uint64_t t0 = globaltimer();
     while (wk < nwb || xk < ksteps) {
       bool progress = false;
@@ -387,6 +389,7 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_kernel(const __grid_const
   }
   // ---- epilogue (warps 2-5: warp w reads TMEM lanes 32 (w % 4) ..)
   __syncwarp();
+  lmps_pdl_wait();  // before any read of the residual or write of Y
   const bool epi_warp = warp >= 2;
   bool ok = false;
   if (epi_warp) {
@@ -510,6 +513,7 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   volatile int* abort_v = abort_flag;
 
+  lmps_pdl_trigger();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * kRows, m0 = blockIdx.y * 128;
   const int ksteps = P.k / kBK;
@@ -536,6 +540,7 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
 
   if (warp == 0) {
     if (lane == 0) {  // ---- TMA producer
+      lmps_pdl_wait();  // X is the previous kernel's output
       int issued = 0;
       for (int kt = 0; kt < ksteps; ++kt) {
         const int s = kt % S;
@@ -596,6 +601,7 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
       mbar_arrive(&deq[s]);
     }
     // ---- epilogue: lane = token m0 + 32q + lane, columns = weight rows n0 ..
+    lmps_pdl_wait();  // before any read of the residual or write of Y
     const bool ok = ksteps > 0 && mbar_wait(done, 0, P.error, abort_v);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const int q = warp & 3;
@@ -742,8 +748,8 @@ extern "C" int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed
     cudaError_t e = cudaFuncSetAttribute(w4::w4a16_gemm_tiles_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return static_cast<int>(e);
-    w4::w4a16_gemm_tiles_kernel<<<dim3(nt, mt), w4::kThreads, smem, lmps_stream(stream)>>>(P);
-    return lmps_launch_status();
+    return lmps_launch_pdl(w4::w4a16_gemm_tiles_kernel, dim3(nt, mt), dim3(w4::kThreads), smem, lmps_stream(stream),
+                           P);
   }
   const int splits = choose_splits(nt, ksteps, sms);
   P.ksteps_per_split = (ksteps + splits - 1) / splits;  // trailing splits may get none: they add zeros
@@ -774,13 +780,15 @@ extern "C" int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed
   cfg.blockDim = dim3(w4::kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = lmps_stream(stream);
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = static_cast<unsigned>(splits);
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, w4::w4a16_gemm_kernel, P);
   if (e != cudaSuccess) return static_cast<int>(e);
   return lmps_launch_status();
