@@ -316,6 +316,27 @@ def extra_configs(mw, cfg, args, rank, world, dist, peak):
             del eng
         except Exception as e:
             out["c3_prefill"] = {"error": repr(e)[:200]}
+    # -- c3 in 2-way tensor-parallel mode (both ranks run the same 8 prompts)
+    if world == 2:
+        try:
+            from llamamps_b200.tp import TPEngine
+            B, P = 8, 2048
+            eng = TPEngine(mw, rank, world, device=torch.device("cuda"), max_batch=B, max_seq_len=P + 32)
+            prompt = torch.from_numpy(np.random.default_rng(3).integers(0, cfg.vocab, (B, P)))
+            eng.reset(B)
+            eng.prefill(prompt, dense=True)  # warm-up
+            eng.reset(B)
+            t = _timed(lambda: eng.prefill(prompt, dense=True), world, dist)
+            eng.decode_steps(2, record=False)
+            td = _timed(lambda: eng.decode_steps(16, record=False), world, dist)
+            out["c3_prefill_tp2"] = {
+                "value": round(B * P / t, 1), "unit": "prompt tok/s", "ms": round(t * 1e3, 2),
+                "decode_after_prefill_tok_s": round(B * 16 / td, 1),
+                "path": "tp2: KV head r and its query heads on rank r, NCCL all-reduce (sum, fp16) "
+                        "after o_proj and down_proj; dense GEMM prefill, then bs8 decode"}
+            del eng
+        except Exception as e:
+            out["c3_prefill_tp2"] = {"error": repr(e)[:200]}
     # -- c4
     try:
         B, T = 4, 32768
