@@ -152,6 +152,20 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// Position in a ring of n stages: the slot of the current use and the
+// parity of its fill (the fill count of the slot, mod 2).  Stepped once per
+// use, so the loops carry no division by the run-time stage counts.
+struct RingPos {
+  int slot = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void next(int n) {
+    if (++slot == n) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
 // 4-byte asynchronous global -> shared copy (completion by commit groups).
 __device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
@@ -266,16 +280,19 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_kernel(const __grid_const
   // steps) ahead, X tiles SX steps; the loads that need no free slot go out
   // before the block-wide sync.
   int wk = 0, xk = 0;
+  RingPos wp, xp;  // ring positions of the next W block / X tile to load
   auto issue_w = [&]() {
-    mbar_expect_tx(&fullw[wk % R], static_cast<uint32_t>(wblk));
-    tma_load_2d(wr + static_cast<size_t>(wk % R) * wblk, &P.tw, (kbeg + wk * SPB) * (kBK / 2), n0,
-                &fullw[wk % R]);
+    mbar_expect_tx(&fullw[wp.slot], static_cast<uint32_t>(wblk));
+    tma_load_2d(wr + static_cast<size_t>(wp.slot) * wblk, &P.tw, (kbeg + wk * SPB) * (kBK / 2), n0,
+                &fullw[wp.slot]);
     ++wk;
+    wp.next(R);
   };
   auto issue_x = [&]() {
-    mbar_expect_tx(&fullx[xk % SX], static_cast<uint32_t>(xbytes));
-    tma_load_2d(xs + static_cast<size_t>(xk % SX) * xbytes, &P.tx, (kbeg + xk) * kBK, m0, &fullx[xk % SX]);
+    mbar_expect_tx(&fullx[xp.slot], static_cast<uint32_t>(xbytes));
+    tma_load_2d(xs + static_cast<size_t>(xp.slot) * xbytes, &P.tx, (kbeg + xk) * kBK, m0, &fullx[xp.slot]);
     ++xk;
+    xp.next(SX);
   };
   if (tid == 0) {  // weights and scales are constant: they load before the previous kernel is done
     while (wk < nwb && wk < R) issue_w();
@@ -291,11 +308,12 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_kernel(const __grid_const
     uint64_t t0 = globaltimer();
     while (wk < nwb || xk < ksteps) {
       bool progress = false;
-      if (wk < nwb && mbar_try(&emptyw[wk % R], ((wk / R) - 1) & 1)) {
+      // a slot's previous use was fill phase ^ 1: wait for its release
+      if (wk < nwb && mbar_try(&emptyw[wp.slot], wp.phase ^ 1u)) {
         issue_w();
         progress = true;
       }
-      if (xk < ksteps && mbar_try(&emptyx[xk % SX], ((xk / SX) - 1) & 1)) {
+      if (xk < ksteps && mbar_try(&emptyx[xp.slot], xp.phase ^ 1u)) {
         issue_x();
         progress = true;
       }
@@ -324,10 +342,11 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_kernel(const __grid_const
     // ---- MMA issuer
     if (lane == 0) {
       const uint32_t idesc = P.swap ? idesc_f16(128, P.xrows) : idesc_f16(128, 128);
-      for (int kt = 0; kt < ksteps; ++kt) {
-        const int sx = kt % SX, sd = kt % SD;
-        if (!mbar_wait(&fullx[sx], (kt / SX) & 1, P.error, abort_v)) break;
-        if (!mbar_wait(&deq[sd], (kt / SD) & 1, P.error, abort_v)) break;
+      RingPos px, pd;
+      for (int kt = 0; kt < ksteps; ++kt, px.next(SX), pd.next(SD)) {
+        const int sx = px.slot, sd = pd.slot;
+        if (!mbar_wait(&fullx[sx], px.phase, P.error, abort_v)) break;
+        if (!mbar_wait(&deq[sd], pd.phase, P.error, abort_v)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint64_t xd = sw128_desc(smem_u32(xs + static_cast<size_t>(sx) * xbytes));
         const uint64_t wdd = sw128_desc(smem_u32(wd + static_cast<size_t>(sd) * kWTileBytes));
@@ -354,15 +373,17 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_kernel(const __grid_const
       cp_async_commit();
     }
     const int sw = t & 7;
+    RingPos pd, pw;  // dequantised stage, packed-W block
+    int sub = 0, slot = 0;  // K step within the block, scale-ring slot
     for (int kt = 0; kt < ksteps; ++kt) {
-      const int s = kt % SD, wb = kt / SPB, wsl = wb % R, sub = kt % SPB;
+      const int s = pd.slot, wsl = pw.slot;
       cp_async_wait<kScaleAhead - 1>();
-      const int slot = kt % kScaleAhead;
       const uint32_t sc = sring[slot * 128];
       if (kt + kScaleAhead < ksteps) cp_async4(sring + slot * 128, srow + kt + kScaleAhead);
       cp_async_commit();
-      if (sub == 0 && !mbar_wait(&fullw[wsl], (wb / R) & 1, P.error, abort_v)) break;
-      if (kt >= SD && !mbar_wait(&emptyd[s], ((kt / SD) - 1) & 1, P.error, abort_v)) break;  // MMA done with wd[s]
+      slot = slot + 1 == kScaleAhead ? 0 : slot + 1;
+      if (sub == 0 && !mbar_wait(&fullw[wsl], pw.phase, P.error, abort_v)) break;
+      if (kt >= SD && !mbar_wait(&emptyd[s], pd.phase ^ 1u, P.error, abort_v)) break;  // MMA done with wd[s]
       // packed row t, bytes 32 sub .. 32 sub + 31: 16-byte chunks 2 sub and
       // 2 sub + 1 of a 32 SPB-byte row (128-byte rows are swizzled)
       const unsigned char* rrow = wr + static_cast<size_t>(wsl) * wblk + t * (32 * SPB);
@@ -384,6 +405,11 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_kernel(const __grid_const
       // generic-proxy shared-memory writes -> visible to the tensor core
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive(&deq[s]);
+      pd.next(SD);
+      if (++sub == SPB) {
+        sub = 0;
+        pw.next(R);
+      }
     }
     asm volatile("cp.async.wait_all;" ::: "memory");  // no copy in flight past the loop (abort path)
   }
@@ -542,9 +568,10 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
     if (lane == 0) {  // ---- TMA producer
       lmps_pdl_wait();  // X is the previous kernel's output
       int issued = 0;
-      for (int kt = 0; kt < ksteps; ++kt) {
-        const int s = kt % S;
-        if (kt >= S && !mbar_wait(&empty[s], ((kt / S) - 1) & 1, P.error, abort_v)) break;
+      RingPos ps;
+      for (int kt = 0; kt < ksteps; ++kt, ps.next(S)) {
+        const int s = ps.slot;
+        if (kt >= S && !mbar_wait(&empty[s], ps.phase ^ 1u, P.error, abort_v)) break;
         mbar_expect_tx(&full[s], static_cast<uint32_t>(kX + kStepBytes));
         tma_load_2d(xs + static_cast<size_t>(s) * kX, &P.tx, kt * kBK, m0, &full[s]);
         tma_load_2d(wr + static_cast<size_t>(s) * kStepBytes, &P.tw, kt * (kBK / 2), n0, &full[s]);
@@ -559,9 +586,10 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
   } else if (warp == 1) {
     if (lane == 0) {  // ---- MMA issuer
       const uint32_t idesc = idesc_f16(128, 128);
-      for (int kt = 0; kt < ksteps; ++kt) {
-        const int s = kt % S;
-        if (!mbar_wait(&deq[s], (kt / S) & 1, P.error, abort_v)) break;
+      RingPos ps;
+      for (int kt = 0; kt < ksteps; ++kt, ps.next(S)) {
+        const int s = ps.slot;
+        if (!mbar_wait(&deq[s], ps.phase, P.error, abort_v)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint64_t ad = sw128_desc(smem_u32(xs + static_cast<size_t>(s) * kX));
         const uint64_t bd = sw128_desc(smem_u32(wd + static_cast<size_t>(s) * kWTileBytes));
@@ -579,11 +607,12 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
     const int t = tid - 64, sw = t & 7;
     const uint32_t* srow = reinterpret_cast<const uint32_t*>(P.s + static_cast<size_t>(n0 + t) * (P.k / 32));
     uint32_t sc_next = ksteps > 0 ? __ldg(srow) : 0u;
-    for (int kt = 0; kt < ksteps; ++kt) {
-      const int s = kt % S;
+    RingPos ps;
+    for (int kt = 0; kt < ksteps; ++kt, ps.next(S)) {
+      const int s = ps.slot;
       const uint32_t sc = sc_next;
       if (kt + 1 < ksteps) sc_next = __ldg(srow + kt + 1);
-      if (!mbar_wait(&full[s], (kt / S) & 1, P.error, abort_v)) break;
+      if (!mbar_wait(&full[s], ps.phase, P.error, abort_v)) break;
       const uint4* raw = reinterpret_cast<const uint4*>(wr + static_cast<size_t>(s) * kStepBytes + t * 32);
       const uint4 g0 = raw[0], g1 = raw[1];
       const __half2 sc2 = *reinterpret_cast<const __half2*>(&sc);
