@@ -321,20 +321,32 @@ def extra_configs(mw, cfg, args, rank, world, dist, peak):
         try:
             from llamamps_b200.tp import TPEngine
             B, P = 8, 2048
-            eng = TPEngine(mw, rank, world, device=torch.device("cuda"), max_batch=B, max_seq_len=P + 32)
             prompt = torch.from_numpy(np.random.default_rng(3).integers(0, cfg.vocab, (B, P)))
-            eng.reset(B)
-            eng.prefill(prompt, dense=True)  # warm-up
-            eng.reset(B)
-            t = _timed(lambda: eng.prefill(prompt, dense=True), world, dist)
-            eng.decode_steps(2, record=False)
-            td = _timed(lambda: eng.decode_steps(16, record=False), world, dist)
+            res = {}
+            for comm in ("p2p", "nccl"):
+                eng = TPEngine(mw, rank, world, device=torch.device("cuda"), max_batch=B, max_seq_len=P + 32,
+                               comm=comm)
+                try:
+                    eng.reset(B)
+                    eng.prefill(prompt, dense=True)  # warm-up
+                    eng.reset(B)
+                    t = _timed(lambda: eng.prefill(prompt, dense=True), world, dist)
+                    eng.decode_steps(2, record=False)  # graph capture outside the timed region
+                    td = _timed(lambda: eng.decode_steps(16, record=False), world, dist)
+                    eng.check_comm()
+                    res[comm] = (t, td)
+                finally:
+                    eng.close()
+                del eng
+            t, td = res["p2p"]
             out["c3_prefill_tp2"] = {
                 "value": round(B * P / t, 1), "unit": "prompt tok/s", "ms": round(t * 1e3, 2),
                 "decode_after_prefill_tok_s": round(B * 16 / td, 1),
-                "path": "tp2: KV head r and its query heads on rank r, NCCL all-reduce (sum, fp16) "
-                        "after o_proj and down_proj; dense GEMM prefill, then bs8 decode"}
-            del eng
+                "decode_nccl_tok_s": round(B * 16 / res["nccl"][1], 1),
+                "path": "tp2: KV head r and its query heads on rank r; dense GEMM prefill with NCCL "
+                        "all-reduces (sum, fp16) after o_proj and down_proj, then bs8 decode as a CUDA graph "
+                        "with the all-reduces over peer memory (NVLink stores + flags, fused with the "
+                        "residual add); decode_nccl_tok_s: the same decode with NCCL all-reduces, eager"}
         except Exception as e:
             out["c3_prefill_tp2"] = {"error": repr(e)[:200]}
     # -- c4

@@ -214,6 +214,39 @@ int lmps_prefill_attention(const uint16_t* q, int ldq, const uint16_t* k_pool, c
  * (runners/engine.py:180-181), the large-batch companion of the LM-head GEMM. */
 int lmps_argmax_rows(const uint16_t* logits, int ld, int rows, int n, int32_t* ids, void* stream);
 
+/* ---- two-way tensor parallelism over peer memory ------------------------
+ * The all-reduce (sum) of the two ranks' partial o_proj / down_proj products
+ * that follows each split projection (runners/engine.py:215-221,237-243 with
+ * K split across two GPUs), fused with the residual add, over NVLink P2P
+ * stores into the peer's buffer (one process per GPU, CUDA IPC mapping).
+ *
+ * lmps_comm_alloc: a zero-filled device buffer of `bytes` (its own cudaMalloc,
+ * so an IPC handle covers it exactly); lmps_comm_free releases it.
+ * lmps_ipc_handle writes the 64-byte cudaIpcMemHandle_t of such a buffer;
+ * lmps_ipc_open maps a peer's handle (peer access enabled lazily);
+ * lmps_ipc_close unmaps it.
+ * lmps_tp2_comm_bytes: the exchange buffer size for n_sites call sites of at
+ * most max_n fp16 elements each (max_n a multiple of 8), 0 if invalid. */
+int lmps_comm_alloc(size_t bytes, void** ptr);
+int lmps_comm_free(void* ptr);
+int lmps_ipc_handle(const void* ptr, void* handle);
+int lmps_ipc_open(const void* handle, void** ptr);
+int lmps_ipc_close(void* ptr);
+size_t lmps_tp2_comm_bytes(int n_sites, int max_n);
+
+/* x[i] <- x[i] + (part[i] + peer's part[i]) for i < n (fp16; both ranks get
+ * bit-identical x).  comm = this rank's exchange buffer, peer_comm = the
+ * peer's, mapped; seen = this rank's private uint32 [n_sites * 64] call
+ * counters (zeroed with the buffers).  Both ranks must make the same calls
+ * (site, n) in the same order; calls on one site may follow each other
+ * directly.  A wait for the peer that runs out (5 s) sets *error and leaves
+ * x unchanged, and later calls return at once while *error is set; the
+ * buffers and counters of both ranks must then be zeroed again.  The grid
+ * is at most 64 CTAs, all resident at once. */
+int lmps_tp2_allreduce_residual(const uint16_t* part, uint16_t* x, int n, void* comm, void* peer_comm,
+                                uint32_t* seen, int site, int n_sites, int max_n, int32_t* error,
+                                void* stream);
+
 /* ---- weight format ---------------------------------------------------- */
 
 /* Device Q4 packer, bit-exact with utils/pack_weights.py:42-60

@@ -1,0 +1,176 @@
+// Two-way tensor-parallel exchange over peer memory (NVLink P2P, one process
+// per GPU): the all-reduce (sum) of the partial o_proj / down_proj products
+// that follows each of them in a tensor-parallel decoder layer
+// (runners/engine.py:215-221,237-243 with the projection split by K across
+// two GPUs), fused with the residual add:
+//
+//   x <- x + (part_self + part_peer)        (fp16, two roundings)
+//
+// which is what an NCCL fp16 sum of the two partials followed by
+// residual_add computes.  fp16 addition is commutative, so both ranks derive
+// bit-identical x.
+//
+// Each rank owns one exchange buffer (cudaMalloc'd here so that a CUDA IPC
+// handle covers it exactly) and maps the peer's through CUDA IPC.  Per call
+// site ("site": one all-reduce position in the decode step) the buffer
+// holds two receive slots of max_n halves and one flag word per CTA; the
+// rank keeps a private count of completed calls per (site, CTA).
+//
+// Call protocol, per CTA c of the grid (both ranks launch the same grid):
+//   1. store this rank's slice of `part` into the peer's receive slot
+//      (call count + 1) & 1 -- plain stores over NVLink, no multicast;
+//   2. fence (system scope), then release-store the new call count into the
+//      peer's flag c;
+//   3. wait (acquire, bounded) until this rank's flag c, written by the peer,
+//      has reached the same count; a wait that runs out raises *error and
+//      returns without touching x (and later calls return at once while
+//      *error is set);
+//   4. x <- x + (part + received) over the slice.
+// A CTA only waits for its counterpart CTA on the other GPU, so there is no
+// grid-wide barrier.  Two receive slots make back-to-back calls on one site
+// safe: the peer cannot start call k + 2 (slot k & 1 again) before this rank
+// has finished call k + 1, which is after it read call k.  The flags only
+// grow, so a peer that has already moved one call ahead still satisfies the
+// wait (>= in wrap-around arithmetic).
+#include <algorithm>
+#include <cstring>
+
+#include "common.cuh"
+
+namespace lmps {
+namespace tp {
+
+constexpr int kThreads = 256;
+constexpr int kMaxCtas = 64;  // flag words per site
+constexpr unsigned long long kTimeoutNs = 5000000000ull;  // host-side skew between the ranks stays far below
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ uint32_t hadd2u(uint32_t a, uint32_t b) {
+  const __half2 r = __hadd2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+
+__global__ void __launch_bounds__(kThreads)
+    allreduce_residual_kernel(const uint4* __restrict__ part, uint4* __restrict__ x, int n8, int slot8,
+                              uint4* peer_recv, const uint4* recv, uint32_t* peer_flags, const uint32_t* flags,
+                              uint32_t* seen, int32_t* error) {
+  __shared__ int ok;
+  if (*reinterpret_cast<volatile int32_t*>(error)) return;  // an earlier exchange failed: the pair is out of step
+  const int per = (n8 + gridDim.x - 1) / gridDim.x;
+  const int lo = blockIdx.x * per, hi = min(n8, lo + per);
+  const uint32_t want = seen[blockIdx.x] + 1u;
+  const int sl = static_cast<int>(want & 1u) * slot8;
+  for (int i = lo + threadIdx.x; i < hi; i += kThreads) peer_recv[sl + i] = part[i];
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    st_release_sys(peer_flags + blockIdx.x, want);
+    int good = 1;
+    const uint64_t t0 = globaltimer();
+    while (static_cast<int>(ld_acquire_sys(flags + blockIdx.x) - want) < 0) {
+      if (globaltimer() - t0 > kTimeoutNs) {
+        atomicExch(error, 1);
+        good = 0;
+        break;
+      }
+    }
+    if (good) seen[blockIdx.x] = want;
+    ok = good;
+  }
+  __syncthreads();
+  if (!ok) return;
+  __threadfence_system();
+  for (int i = lo + threadIdx.x; i < hi; i += kThreads) {
+    const uint4 a = part[i], b = __ldcg(recv + sl + i), r = x[i];
+    x[i] = make_uint4(hadd2u(r.x, hadd2u(a.x, b.x)), hadd2u(r.y, hadd2u(a.y, b.y)), hadd2u(r.z, hadd2u(a.z, b.z)),
+                      hadd2u(r.w, hadd2u(a.w, b.w)));
+  }
+}
+
+}  // namespace tp
+}  // namespace lmps
+
+using namespace lmps;
+
+extern "C" int lmps_comm_alloc(size_t bytes, void** ptr) {
+  LMPS_CHECK_ARG(ptr && bytes > 0);
+  *ptr = nullptr;
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  e = cudaMemset(*ptr, 0, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return static_cast<int>(e);
+  }
+  return LMPS_OK;
+}
+
+extern "C" int lmps_comm_free(void* ptr) {
+  LMPS_CHECK_ARG(ptr);
+  return static_cast<int>(cudaFree(ptr));
+}
+
+extern "C" int lmps_ipc_handle(const void* ptr, void* handle) {
+  LMPS_CHECK_ARG(ptr && handle);
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (e != cudaSuccess) return static_cast<int>(e);
+  memcpy(handle, &h, sizeof(h));
+  return LMPS_OK;
+}
+
+extern "C" int lmps_ipc_open(const void* handle, void** ptr) {
+  LMPS_CHECK_ARG(handle && ptr);
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  *ptr = nullptr;
+  return static_cast<int>(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+extern "C" int lmps_ipc_close(void* ptr) {
+  LMPS_CHECK_ARG(ptr);
+  return static_cast<int>(cudaIpcCloseMemHandle(ptr));
+}
+
+extern "C" size_t lmps_tp2_comm_bytes(int n_sites, int max_n) {
+  if (n_sites < 1 || max_n < 8 || max_n % 8) return 0;
+  return static_cast<size_t>(n_sites) * (2u * static_cast<size_t>(max_n) * 2u + tp::kMaxCtas * 4u);
+}
+
+extern "C" int lmps_tp2_allreduce_residual(const uint16_t* part, uint16_t* x, int n, void* comm, void* peer_comm,
+                                           uint32_t* seen, int site, int n_sites, int max_n, int32_t* error,
+                                           void* stream) {
+  LMPS_CHECK_ARG(part && x && comm && peer_comm && seen && error);
+  LMPS_CHECK_ARG(n_sites >= 1 && site >= 0 && site < n_sites && max_n >= 8 && max_n % 8 == 0);
+  LMPS_CHECK_ARG(n >= 8 && n % 8 == 0 && n <= max_n);
+  LMPS_CHECK_ARG(lmps_aligned(part, 16) && lmps_aligned(x, 16) && lmps_aligned(comm, 16) &&
+                 lmps_aligned(peer_comm, 16) && lmps_aligned(seen, 4));
+  // buffer layout: [n_sites][2][max_n] fp16 receive slots, then [n_sites][kMaxCtas] u32 flags
+  const size_t slots = static_cast<size_t>(n_sites) * 2u * static_cast<size_t>(max_n);
+  uint16_t* recv = static_cast<uint16_t*>(comm) + static_cast<size_t>(site) * 2u * max_n;
+  uint16_t* peer_recv = static_cast<uint16_t*>(peer_comm) + static_cast<size_t>(site) * 2u * max_n;
+  uint32_t* flags = reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(comm) + slots) + site * tp::kMaxCtas;
+  uint32_t* peer_flags = reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(peer_comm) + slots) + site * tp::kMaxCtas;
+  const int n8 = n / 8;
+  // one CTA per 2048 elements, at most kMaxCtas: every CTA of the grid is
+  // resident at once, so each one's counterpart on the peer GPU runs too
+  const int grid = std::min(tp::kMaxCtas, (n8 + tp::kThreads - 1) / tp::kThreads);
+  tp::allreduce_residual_kernel<<<grid, tp::kThreads, 0, lmps_stream(stream)>>>(
+      reinterpret_cast<const uint4*>(part), reinterpret_cast<uint4*>(x), n8, max_n / 8,
+      reinterpret_cast<uint4*>(peer_recv), reinterpret_cast<const uint4*>(recv), peer_flags, flags,
+      seen + site * tp::kMaxCtas, error);
+  return lmps_launch_status();
+}

@@ -254,3 +254,61 @@ def prefill_attention(q, k_pool, v_pool, block_table, out, batch: int, seq_len: 
          _stream())
     return out
 
+
+
+# -- two-way tensor parallelism over peer memory ----------------------------
+class PeerExchange:
+    """This rank's exchange buffer and the peer's, mapped through CUDA IPC,
+    for :func:`tp2_allreduce_residual` (``n_sites`` call sites of at most
+    ``max_n`` fp16 elements).  ``handle()`` gives the 64 bytes to send to the
+    peer, ``connect(peer_handle)`` maps the peer's buffer.  ``close()``
+    unmaps and frees; call it on both ranks after a barrier, with no call in
+    flight on either GPU."""
+
+    def __init__(self, n_sites: int, max_n: int, device):
+        import ctypes
+        self.n_sites, self.max_n, self.device = n_sites, max_n, torch.device(device)
+        nbytes = lib().lmps_tp2_comm_bytes(n_sites, max_n)
+        if nbytes == 0:
+            raise ValueError("max_n must be a positive multiple of 8")
+        with torch.cuda.device(self.device):
+            p = ctypes.c_void_p()
+            call("lmps_comm_alloc", nbytes, ctypes.byref(p))
+            self.comm = p.value
+            self.seen = torch.zeros(n_sites * 64, dtype=torch.int32, device=self.device)
+        self.peer = None
+
+    def handle(self) -> bytes:
+        import ctypes
+        buf = ctypes.create_string_buffer(64)
+        with torch.cuda.device(self.device):
+            call("lmps_ipc_handle", self.comm, buf)
+        return buf.raw
+
+    def connect(self, peer_handle: bytes) -> None:
+        import ctypes
+        if len(peer_handle) != 64:
+            raise ValueError("an IPC handle is 64 bytes")
+        p = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            call("lmps_ipc_open", ctypes.create_string_buffer(peer_handle, 64), ctypes.byref(p))
+        self.peer = p.value
+
+    def close(self) -> None:
+        with torch.cuda.device(self.device):
+            if self.peer is not None:
+                call("lmps_ipc_close", self.peer)
+                self.peer = None
+            if self.comm is not None:
+                call("lmps_comm_free", self.comm)
+                self.comm = None
+
+
+def tp2_allreduce_residual(part, x, ex: PeerExchange, site: int, error):
+    """x <- x + (part + the peer's part) through the peer's mapped buffer."""
+    if ex.peer is None:
+        raise RuntimeError("the peer exchange is not connected")
+    call("lmps_tp2_allreduce_residual", _dev(part, "part", FP16), _dev(x, "x", FP16), part.numel(), ex.comm,
+         ex.peer, _dev(ex.seen, "seen", torch.int32), site, ex.n_sites, ex.max_n,
+         _dev(error, "error", torch.int32), _stream())
+    return x

@@ -87,20 +87,61 @@ class TPEngine(QwenEngine):
     """QwenEngine on one rank of a tensor-parallel group: the per-stage
     kernels on the rank's slice, an all-reduce after o_proj and down_proj.
 
-    Every rank must make the same calls in the same order (the collectives
-    pair up by order).  CUDA graphs are off: each step launches eagerly."""
+    ``comm="p2p"`` (two ranks): decode steps exchange the partial products
+    through the peer's memory (:func:`kernels.tp2_allreduce_residual`, NVLink
+    stores + flags, fused with the residual add), so a step has no host-side
+    collective and runs as a CUDA graph; dense prefill, whose partials are
+    [tokens, hidden], keeps NCCL.  ``comm="nccl"``: every all-reduce is
+    NCCL's and steps launch eagerly.
 
-    def __init__(self, weights: ModelWeights, rank: int, world: int, group=None, **kw):
+    Every rank must make the same calls in the same order (the exchanges pair
+    up by order).  Call :meth:`close` on every rank before the process group
+    is destroyed."""
+
+    def __init__(self, weights: ModelWeights, rank: int, world: int, group=None, comm: str = "p2p", **kw):
         kw.setdefault("decoder", "kernels")
         if kw["decoder"] != "kernels":
             raise ValueError("the tensor-parallel engine runs the per-stage kernels")
+        if comm not in ("p2p", "nccl"):
+            raise ValueError("comm is 'p2p' or 'nccl'")
         self.rank, self.world, self.group = rank, world, group
         self.full_cfg = weights.cfg
         super().__init__(weights=shard_model(weights, rank, world), **kw)
-        self.use_graphs = False
         self._part = torch.zeros(self.max_batch, self.cfg.hidden, dtype=torch.float16, device=self.device)
+        self._site = {id(lw): 2 * li for li, lw in enumerate(self.weights.layers)}
+        self.comm_err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.exchange = None
+        if comm == "p2p" and world == 2 and self.device.type == "cuda":
+            self.exchange = K.PeerExchange(2 * self.cfg.n_layers, self.max_batch * self.cfg.hidden, self.device)
+            handles = [None] * world
+            dist.all_gather_object(handles, self.exchange.handle(), group=group)
+            self.exchange.connect(handles[1 - rank])
+            dist.barrier(group=group)
+        self.use_graphs = self.exchange is not None
 
-    def _reduce_add(self, part: torch.Tensor, x: torch.Tensor) -> None:
+    def close(self) -> None:
+        """Unmap and free the peer exchange (collective: every rank calls it)."""
+        if self.exchange is not None:
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+            self._graphs.clear()
+            self.exchange.close()
+            self.exchange = None
+            dist.barrier(group=self.group)
+
+    def check_comm(self) -> None:
+        if self.exchange is not None and int(self.comm_err.item()) != 0:
+            raise RuntimeError("tensor-parallel exchange: a wait for the peer GPU timed out")
+
+    def generate_batch(self, prompts, max_new_tokens: int):
+        out = super().generate_batch(prompts, max_new_tokens)
+        self.check_comm()
+        return out
+
+    def _reduce_add(self, part: torch.Tensor, x: torch.Tensor, site: int = -1) -> None:
+        if self.exchange is not None and site >= 0 and part.numel() <= self.exchange.max_n:
+            K.tp2_allreduce_residual(part, x, self.exchange, site, self.comm_err)
+            return
         dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
         K.residual_add(x, part, out=x)
 
@@ -115,7 +156,7 @@ class TPEngine(QwenEngine):
                          workspace=self._ws(ws))
         else:
             K.gemv_q4(lw.o_packed, lw.o_scales, att, c.hidden, c.q_dim, out=part)
-        self._reduce_add(part, x)
+        self._reduce_add(part, x, self._site[id(lw)])
 
     def _down_proj(self, lw, a, x, gemm: bool, ws=None) -> None:
         c, part = self.cfg, self._partial(x.shape[0])
@@ -124,7 +165,7 @@ class TPEngine(QwenEngine):
                          error=self.gemm_err, workspace=self._ws(ws))
         else:
             K.gemv_q4(lw.down_packed, lw.down_scales, a, c.hidden, c.intermediate, out=part)
-        self._reduce_add(part, x)
+        self._reduce_add(part, x, self._site[id(lw)] + 1)
 
 
 def init_from_env(backend: str = "nccl", timeout_s: Optional[float] = 60.0):

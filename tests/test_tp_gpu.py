@@ -22,9 +22,13 @@ def _cfg():
     return dataclasses.replace(QWEN2_5_1_5B, n_layers=2, vocab=8192)
 
 
-def _rank(rank, world, port, out, dense):
+def _env(rank, world, port):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
-                      LOCAL_RANK=str(rank))
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+
+
+def _rank(rank, world, port, out, dense, comm):
+    _env(rank, world, port)
     import torch.distributed as dist
     from llamamps_b200.tp import TPEngine, init_from_env
     from llamamps_b200.weights import synth_model
@@ -32,10 +36,50 @@ def _rank(rank, world, port, out, dense):
     try:
         mw = synth_model(_cfg(), seed=17, device=f"cuda:{rank}")
         prompts = np.random.default_rng(PROMPT_SEED).integers(0, 8192, (2, 150 if dense else 9))
-        eng = TPEngine(mw, rank, world, max_batch=2, max_seq_len=256, device=f"cuda:{rank}")
-        got = eng.generate_batch(prompts, STEPS)
-        out[rank] = got.tolist()
+        eng = TPEngine(mw, rank, world, max_batch=2, max_seq_len=256, device=f"cuda:{rank}", comm=comm)
+        try:
+            got = eng.generate_batch(prompts, STEPS)
+            out[rank] = got.tolist()
+        finally:
+            eng.close()
     finally:
+        dist.destroy_process_group()
+
+
+def _exchange_rank(rank, world, port, out):
+    """Peer-memory all-reduce + residual against NCCL's sum + residual_add:
+    several sites, back-to-back calls on one site, 1 to 8 rows."""
+    _env(rank, world, port)
+    import torch.distributed as dist
+    from llamamps_b200 import kernels as K
+    from llamamps_b200.tp import init_from_env
+    init_from_env("nccl", timeout_s=60)
+    dev = torch.device(f"cuda:{rank}")
+    ex = K.PeerExchange(3, 8 * 1536, dev)
+    try:
+        handles = [None] * world
+        dist.all_gather_object(handles, ex.handle())
+        ex.connect(handles[1 - rank])
+        dist.barrier()
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        g = torch.Generator(device=dev).manual_seed(100 + rank)
+        xg = torch.Generator(device=dev).manual_seed(7)       # same residual on both ranks
+        mism = 0
+        for site, rows in [(0, 1), (1, 8), (0, 1), (0, 8), (0, 8), (2, 3), (1, 1), (0, 1)]:
+            part = (torch.randn(rows, 1536, generator=g, device=dev) * 4).half()
+            x = torch.randn(rows, 1536, generator=xg, device=dev).half()
+            ref = part.clone()
+            dist.all_reduce(ref)
+            ref = K.residual_add(x.clone(), ref, out=torch.empty_like(x))
+            K.tp2_allreduce_residual(part, x, ex, site, err)
+            torch.cuda.synchronize(dev)
+            mism += int((x.view(torch.int16) != ref.view(torch.int16)).sum().item())
+        out[rank] = (mism, int(err.item()))
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+    finally:
+        ex.close()
+        dist.barrier()
         dist.destroy_process_group()
 
 
@@ -45,15 +89,35 @@ def _free_port():
         return s.getsockname()[1]
 
 
+def _spawn(target, *args):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, 2, port, out) + args) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+        assert p.exitcode == 0
+    return out
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("dense", [False, True])
-def test_tp2_generate_matches_oracle(cuda, dense):
+def test_tp2_peer_allreduce_equals_nccl(cuda):
+    out = _spawn(_exchange_rank)
+    assert out[0] == (0, 0) and out[1] == (0, 0), dict(out)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("dense,comm", [(False, "p2p"), (True, "p2p"), (False, "nccl")])
+def test_tp2_generate_matches_oracle(cuda, dense, comm):
     import torch.multiprocessing as mp
     from llamamps_b200.weights import model_host_arrays, synth_model
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, out, dense)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, out, dense, comm)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
