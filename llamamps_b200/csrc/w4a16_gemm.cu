@@ -44,7 +44,6 @@ constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 dequantise +
 constexpr int kMaxStages = 8;
 constexpr int kMaxSplits = 8;  // K splits of a tile = CTAs of one (portable) cluster
 constexpr int kScaleAhead = 6; // K steps a dequantising thread's scale loads run ahead
-constexpr int kTileScaleAhead = 4;  // the same for prefill tiles (a power of two)
 constexpr int kStepBytes = kRows * kBK / 2;   // packed W bytes of one K step (4 KB)
 constexpr int kWTileBytes = kRows * kBK * 2;  // 16 KB fp16
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
@@ -536,8 +535,7 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
   uint64_t* deq = full + kMaxStages;
   uint64_t* empty = deq + kMaxStages;
   uint64_t* done = empty + kMaxStages;
-  uint32_t* scale_ring = reinterpret_cast<uint32_t*>(done + 1);  // [kTileScaleAhead][128]
-  uint32_t* tmem_slot = scale_ring + kTileScaleAhead * 128;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   volatile int* abort_v = abort_flag;
 
@@ -608,24 +606,12 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
     // waited for them before refilling), so wd[s] is free once it is full
     const int t = tid - 64, sw = t & 7;
     const uint32_t* srow = reinterpret_cast<const uint32_t*>(P.s + static_cast<size_t>(n0 + t) * (P.k / 32));
-    // the two group scales of a step arrive kTileScaleAhead steps early
-    // through cp.async into this thread's slots of a shared-memory ring (one
-    // commit group per step, empty ones included, so wait_group counts steps)
-    uint32_t* sring = scale_ring + t;
-#pragma unroll
-    for (int i = 0; i < kTileScaleAhead; ++i) {
-      if (i < ksteps) cp_async4(sring + i * 128, srow + i);
-      cp_async_commit();
-    }
+    uint32_t sc_next = ksteps > 0 ? __ldg(srow) : 0u;
     RingPos ps;
-    int slot = 0;
     for (int kt = 0; kt < ksteps; ++kt, ps.next(S)) {
       const int s = ps.slot;
-      cp_async_wait<kTileScaleAhead - 1>();
-      const uint32_t sc = sring[slot * 128];
-      if (kt + kTileScaleAhead < ksteps) cp_async4(sring + slot * 128, srow + kt + kTileScaleAhead);
-      cp_async_commit();
-      slot = (slot + 1) & (kTileScaleAhead - 1);
+      const uint32_t sc = sc_next;
+      if (kt + 1 < ksteps) sc_next = __ldg(srow + kt + 1);
       if (!mbar_wait(&full[s], ps.phase, P.error, abort_v)) break;
       const uint4* raw = reinterpret_cast<const uint4*>(wr + static_cast<size_t>(s) * kStepBytes + t * 32);
       const uint4 g0 = raw[0], g1 = raw[1];
@@ -643,7 +629,6 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive(&deq[s]);
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");  // no copy in flight past the loop (abort path)
     // ---- epilogue: lane = token m0 + 32q + lane, columns = weight rows n0 ..
     lmps_pdl_wait();  // before any read of the residual or write of Y
     const bool ok = ksteps > 0 && mbar_wait(done, 0, P.error, abort_v);
@@ -681,7 +666,7 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
 
 static size_t tiles_smem_bytes(int stages) {
   return static_cast<size_t>(stages) * (128 * 128 + kWTileBytes + kStepBytes) + 1024 +
-         (3 * kMaxStages + 1) * sizeof(uint64_t) + kTileScaleAhead * 128 * sizeof(uint32_t) + 16;
+         (3 * kMaxStages + 1) * sizeof(uint64_t) + 16;
 }
 
 static size_t ring_bytes(int xrows, int xstages, int dstages, int wslots, int spb) {
