@@ -271,28 +271,32 @@ def extra_configs(mw, cfg, args, rank, world, dist, peak):
     from llamamps_b200.engine import QwenEngine
     out = {}
     steps = max(4, min(args.steps, 16))
+
+    def want(name):
+        return args.only is None or args.only == name
     # -- c2
-    try:
-        B = max(1, 64 // world)
-        eng = QwenEngine(weights=mw, device=torch.device("cuda"), max_batch=B,
-                         max_seq_len=128 + args.warmup + steps + 8, decoder="kernels")
-        prompt = np.random.default_rng(2 + rank).integers(0, cfg.vocab, (B, 128))
-        eng.reset(B)
-        eng.prefill(torch.from_numpy(prompt))
-        eng.decode_steps(args.warmup, record=False)
-        t = _timed(lambda: eng.decode_steps(steps, record=False), world, dist)
-        mean_T = 128 + args.warmup + (steps + 1) / 2
-        step_bytes = cfg.step_weight_bytes() + B * cfg.kv_bytes_per_position() * mean_T
-        out["c2_batched_decode"] = {
-            "value": round(world * B * steps / t, 1), "unit": "tok/s", "batch_per_gpu": B,
-            "global_batch": B * world, "ms_per_step": round(t / steps * 1e3, 3),
-            "hbm_frac_of_measured": round(step_bytes / (t / steps) / 1e9 / peak, 4),
-            "path": "per-stage kernels; projections and LM head on the tcgen05 W4A16 GEMM (split-K)"}
-        del eng
-    except Exception as e:  # a sub-measurement never hides the headline line
-        out["c2_batched_decode"] = {"error": repr(e)[:200]}
+    if want("c2"):
+        try:
+            B = max(1, 64 // world)
+            eng = QwenEngine(weights=mw, device=torch.device("cuda"), max_batch=B,
+                             max_seq_len=128 + args.warmup + steps + 8, decoder="kernels")
+            prompt = np.random.default_rng(2 + rank).integers(0, cfg.vocab, (B, 128))
+            eng.reset(B)
+            eng.prefill(torch.from_numpy(prompt))
+            eng.decode_steps(args.warmup, record=False)
+            t = _timed(lambda: eng.decode_steps(steps, record=False), world, dist)
+            mean_T = 128 + args.warmup + (steps + 1) / 2
+            step_bytes = cfg.step_weight_bytes() + B * cfg.kv_bytes_per_position() * mean_T
+            out["c2_batched_decode"] = {
+                "value": round(world * B * steps / t, 1), "unit": "tok/s", "batch_per_gpu": B,
+                "global_batch": B * world, "ms_per_step": round(t / steps * 1e3, 3),
+                "hbm_frac_of_measured": round(step_bytes / (t / steps) / 1e9 / peak, 4),
+                "path": "per-stage kernels; projections and LM head on the tcgen05 W4A16 GEMM (split-K)"}
+            del eng
+        except Exception as e:  # a sub-measurement never hides the headline line
+            out["c2_batched_decode"] = {"error": repr(e)[:200]}
     # -- c3 (one GPU)
-    if world == 1:
+    if world == 1 and want("c3"):
         try:
             B, P = 8, 2048
             eng = QwenEngine(weights=mw, device=torch.device("cuda"), max_batch=B, max_seq_len=P + 32,
@@ -317,7 +321,7 @@ def extra_configs(mw, cfg, args, rank, world, dist, peak):
         except Exception as e:
             out["c3_prefill"] = {"error": repr(e)[:200]}
     # -- c3 in 2-way tensor-parallel mode (both ranks run the same 8 prompts)
-    if world == 2:
+    if world == 2 and want("c3_tp2"):
         try:
             from llamamps_b200.tp import TPEngine
             B, P = 8, 2048
@@ -350,28 +354,29 @@ def extra_configs(mw, cfg, args, rank, world, dist, peak):
         except Exception as e:
             out["c3_prefill_tp2"] = {"error": repr(e)[:200]}
     # -- c4
-    try:
-        B, T = 4, 32768
-        eng = QwenEngine(weights=mw, device=torch.device("cuda"), max_batch=B,
-                         max_seq_len=T + args.warmup + steps + 8, decoder="persistent")
-        eng.reset(B, start_pos=T)
-        g = torch.Generator(device="cuda").manual_seed(4 + rank)
-        for layer in range(cfg.n_layers):   # the KV cache of T positions, fp16 N(0,1)
-            eng.cache.k[layer].normal_(generator=g)
-            eng.cache.v[layer].normal_(generator=g)
-        eng.tokens[:B].copy_(torch.from_numpy(np.random.default_rng(4).integers(0, cfg.vocab, B)))
-        eng.decode_steps(args.warmup, record=False)
-        t = _timed(lambda: eng.decode_steps(steps, record=False), world, dist)
-        eng.pdec.check_error()
-        kv = B * cfg.kv_bytes_per_position() * (T + args.warmup + steps / 2)
-        out["c4_long_context"] = {
-            "value": round(world * B * steps / t, 1), "unit": "tok/s", "batch_per_gpu": B, "kv_positions": T,
-            "ms_per_step": round(t / steps * 1e3, 3),
-            "hbm_frac_of_measured": round((cfg.step_weight_bytes() + kv) / (t / steps) / 1e9 / peak, 4),
-            "path": "persistent decode kernel"}
-        del eng
-    except Exception as e:
-        out["c4_long_context"] = {"error": repr(e)[:200]}
+    if want("c4"):
+        try:
+            B, T = 4, 32768
+            eng = QwenEngine(weights=mw, device=torch.device("cuda"), max_batch=B,
+                             max_seq_len=T + args.warmup + steps + 8, decoder="persistent")
+            eng.reset(B, start_pos=T)
+            g = torch.Generator(device="cuda").manual_seed(4 + rank)
+            for layer in range(cfg.n_layers):   # the KV cache of T positions, fp16 N(0,1)
+                eng.cache.k[layer].normal_(generator=g)
+                eng.cache.v[layer].normal_(generator=g)
+            eng.tokens[:B].copy_(torch.from_numpy(np.random.default_rng(4).integers(0, cfg.vocab, B)))
+            eng.decode_steps(args.warmup, record=False)
+            t = _timed(lambda: eng.decode_steps(steps, record=False), world, dist)
+            eng.pdec.check_error()
+            kv = B * cfg.kv_bytes_per_position() * (T + args.warmup + steps / 2)
+            out["c4_long_context"] = {
+                "value": round(world * B * steps / t, 1), "unit": "tok/s", "batch_per_gpu": B, "kv_positions": T,
+                "ms_per_step": round(t / steps * 1e3, 3),
+                "hbm_frac_of_measured": round((cfg.step_weight_bytes() + kv) / (t / steps) / 1e9 / peak, 4),
+                "path": "persistent decode kernel"}
+            del eng
+        except Exception as e:
+            out["c4_long_context"] = {"error": repr(e)[:200]}
     return out
 
 
@@ -520,6 +525,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the c2/c3/c4 sub-measurements (batch 64, 8x2048 prefill, 32K context)")
+    ap.add_argument("--only", choices=["c2", "c3", "c3_tp2", "c4"], default=None,
+                    help="run only this sub-measurement after the headline line (for profiling)")
     ap.add_argument("--decoder", choices=["persistent", "kernels"], default=None)
     ap.add_argument("--timeline", default=None,
                     help="after the timed region, write the persistent kernel's stage timeline "
