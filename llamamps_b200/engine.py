@@ -39,6 +39,28 @@ from .weights import ModelWeights, load_reference_layout
 
 
 GEMV_MAX_BATCH = 8  # the CUDA-core GEMV serves up to 8 sequences; larger batches use the tensor-core GEMM
+
+
+def argmax_first(logits) -> int:
+    """runners/engine.py:180-181, ``np.argmax(logits.astype(np.float32))``:
+    the first index of the largest value.
+
+    For a contiguous 1-D fp16 array the fp32 copy is skipped: fp16 -> fp32 is
+    exact and keeps the order, and the fp16 bit patterns map to int16 keys
+    in the same order (negative values: magnitude bits flipped), so the
+    int16 argmax is the same index -- except where fp32 comparison and the
+    bit patterns disagree: a NaN (np.argmax returns the first NaN) or a
+    maximum of zero (-0 and +0 compare equal).  Those arrays take the fp32
+    path.  ~6x faster on the 151936 LM-head logits."""
+    x = np.asarray(logits)
+    if x.dtype == np.float16 and x.ndim == 1 and x.flags.c_contiguous and x.size:
+        b = x.view(np.int16)
+        if not np.any((b & 0x7FFF) > 0x7C00):             # no NaN
+            key = b ^ ((b >> 15) & 0x7FFF)
+            i = int(np.argmax(key))
+            if key[i] != 0 and key[i] != -1:              # the maximum is not +0 / -0
+                return i
+    return int(np.argmax(x.astype(np.float32)))
 DENSE_PREFILL_TOKENS = 256  # prompts with at least this many tokens in total prefill on the GEMM path
 
 
@@ -128,6 +150,7 @@ class QwenEngine:
         self._pin_logits = torch.zeros(c.vocab, dtype=h).pin_memory()
         self._pin_ids = torch.zeros(B, dtype=i32).pin_memory()
         self._pin_next = torch.zeros(B, dtype=i32).pin_memory()
+        self._pin_err = torch.zeros(1, dtype=i32).pin_memory()
 
     def reset(self, batch: Optional[int] = None, start_pos: int = 0) -> None:
         """Start ``batch`` fresh sequences (slots 0..batch-1) at ``start_pos``."""
@@ -262,15 +285,17 @@ class QwenEngine:
         else:
             self._vector_step()
         self._pin_logits.copy_(self.buf_logits[0], non_blocking=True)
+        if self.pdec is not None:  # the device error word rides along with the logits
+            self._pin_err.copy_(self.pdec.error, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
-        if self.pdec is not None:
+        if self.pdec is not None and int(self._pin_err[0]) != 0:
             self.pdec.check_error()
         self.host_pos += 1
         return self._pin_logits.numpy().copy()
 
     def predict_next_token(self, logits: np.ndarray) -> int:
         """engine.py:180-181: argmax over fp32(logits), first index on ties."""
-        return int(np.argmax(np.asarray(logits).astype(np.float32)))
+        return argmax_first(logits)
 
     # -- decode loop ---------------------------------------------------------
     def _graph_for(self, B: int, record: bool, vector: bool = False):

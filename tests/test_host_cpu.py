@@ -81,3 +81,41 @@ def test_synth_one_layer_case_shapes():
     assert parts["gate_packed"].size == 8960 * 1536 // 2 and parts["down_scales"].size == 8960 * 1536 // 32
     assert x.shape == (1536,) and kp.shape == (31, 256) and vp.shape == (31, 256)
     assert x.dtype == np.float16
+
+
+def test_argmax_first_equals_fp32_argmax():
+    """predict_next_token's fast path (int16 keys on the fp16 bits) against
+    the reference expression np.argmax(logits.astype(np.float32)), on random
+    logits and the cases where bit order and fp32 order could part: ties,
+    +0 / -0 at the maximum, infinities, NaNs, subnormals."""
+    import numpy as np
+    from llamamps_b200.engine import argmax_first
+    rng = np.random.default_rng(5)
+    cases = [rng.normal(0, 3, 151936).astype(np.float16) for _ in range(4)]
+    t = rng.normal(0, 1, 1000).astype(np.float16)
+    t[[10, 500]] = np.float16(9.0)                         # tie: first index
+    cases.append(t)
+    z = -np.abs(rng.normal(0, 1, 64)).astype(np.float16)
+    z[7], z[20] = np.float16(-0.0), np.float16(0.0)        # max is zero, -0 first
+    cases.append(z)
+    z2 = z.copy()
+    z2[20] = np.float16(-0.0)                              # only -0 at the max
+    cases.append(z2)
+    n = -np.abs(rng.normal(0, 1, 64)).astype(np.float16)
+    cases.append(n)                                        # all negative
+    inf = rng.normal(0, 1, 64).astype(np.float16)
+    inf[[3, 30]] = np.inf
+    inf[1] = -np.inf
+    cases.append(inf)
+    nan = rng.normal(0, 1, 64).astype(np.float16)
+    nan[40], nan[50] = np.nan, np.inf
+    cases.append(nan)
+    neg_nan = rng.normal(0, 1, 64).astype(np.float16)
+    neg_nan.view(np.int16)[9] = np.int16(-512)             # 0xFE00: a negative NaN
+    cases.append(neg_nan)
+    sub = (rng.normal(0, 1, 64) * 1e-6).astype(np.float16)  # subnormals
+    cases.append(sub)
+    cases.append(rng.normal(0, 1, 100).astype(np.float32))  # fp32 input: general path
+    cases.append(rng.normal(0, 1, 200).astype(np.float16)[::2])  # strided view
+    for i, c in enumerate(cases):
+        assert argmax_first(c) == int(np.argmax(np.asarray(c).astype(np.float32))), f"case {i}"
