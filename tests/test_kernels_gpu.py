@@ -223,7 +223,12 @@ def test_gqa_decode_attention(cuda, T_list, page_size, max_seq):
     q = rng.normal(0, 1, (B, 1536)).astype(np.float16)
     seq_lens = _t(np.array(T_list, np.int32))
     kp, vp = kv.layer(0)
-    for n_splits in sorted({1, K.attention_splits(B, 2, kv.max_seq_len, page_size), 5}):
+    # 2..8 splits merge inside a thread-block cluster (empty splits included:
+    # 5 splits of a 64-position cache), more through the combine kernel
+    splits = {1, K.attention_splits(B, 2, kv.max_seq_len, page_size), 2, 3, 5}
+    if kv.max_seq_len >= 9 * 64:
+        splits |= {8, 9}
+    for n_splits in sorted(splits):
         ws = torch.zeros(max(16, K.attention_workspace_size(B, 12, 128, n_splits)), dtype=torch.uint8, device="cuda")
         buf, out = _padded(B * 1536)
         K.gqa_decode_attention(_t(q), kp, vp, kv.block_table, seq_lens, out.view(B, 1536), ws,
