@@ -55,11 +55,13 @@ def argmax_first(logits) -> int:
     x = np.asarray(logits)
     if x.dtype == np.float16 and x.ndim == 1 and x.flags.c_contiguous and x.size:
         b = x.view(np.int16)
-        if not np.any((b & 0x7FFF) > 0x7C00):             # no NaN
-            key = b ^ ((b >> 15) & 0x7FFF)
-            i = int(np.argmax(key))
-            if key[i] != 0 and key[i] != -1:              # the maximum is not +0 / -0
-                return i
+        key = b ^ ((b >> 15) & np.int16(0x7FFF))
+        i = int(np.argmax(key))
+        k = int(key[i])
+        # keys of +inf / -inf are 31744 / -31745: anything beyond is a NaN;
+        # keys 0 / -1 are +0 / -0
+        if k <= 31744 and k != 0 and k != -1 and int(key.min()) >= -31745:
+            return i
     return int(np.argmax(x.astype(np.float32)))
 DENSE_PREFILL_TOKENS = 256  # prompts with at least this many tokens in total prefill on the GEMM path
 

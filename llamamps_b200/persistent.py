@@ -109,6 +109,7 @@ class PersistentDecoder:
         off = (-self.workspace.data_ptr()) % 256
         self.ws_view = self.workspace[off:off + ws]
         self.error = torch.zeros(1, dtype=torch.int32, device=weights.device)
+        self._states = {}  # launch state by argument pointers (the per-token path reuses one)
 
     def reset_workspace(self):
         """Zero the workspace (needed once, and after a launch that reported an error)."""
@@ -122,6 +123,22 @@ class PersistentDecoder:
             trace: Optional[torch.Tensor] = None) -> None:
         if not 1 <= batch <= self.max_batch:
             raise ValueError(f"batch {batch} outside [1, {self.max_batch}]")
+        if forced is None and history is None and trace is None:
+            # the per-token path: the state of (batch, tokens, pos, x_in, logits) is built once
+            key = (batch, tokens.data_ptr(), pos.data_ptr(), x_in.data_ptr() if x_in is not None else 0,
+                   logits.data_ptr() if logits is not None else 0, self.cache.block_table.data_ptr())
+            st = self._states.get(key)
+            if st is None:
+                st = self._state(batch, tokens, pos, None, x_in, logits, None, None, None)
+                if len(self._states) < 64:
+                    self._states[key] = st
+        else:
+            st = self._state(batch, tokens, pos, forced, x_in, logits, history, step_counter, trace)
+        check(self.L.lmps_decode_persistent(ctypes.byref(self.model), ctypes.byref(st), int(n_steps),
+                                            torch.cuda.current_stream().cuda_stream),
+              "lmps_decode_persistent")
+
+    def _state(self, batch, tokens, pos, forced, x_in, logits, history, step_counter, trace):
         cache = self.cache
         st = DecodeState()
         st.batch = batch
@@ -152,9 +169,7 @@ class PersistentDecoder:
             st.trace = trace.data_ptr()
             st.trace_events = trace.shape[1]
             st.trace_rows = trace.shape[0]
-        check(self.L.lmps_decode_persistent(ctypes.byref(self.model), ctypes.byref(st), int(n_steps),
-                                            torch.cuda.current_stream().cuda_stream),
-              "lmps_decode_persistent")
+        return st
 
     def check_error(self) -> None:
         e = int(self.error.item())
