@@ -247,6 +247,21 @@ int lmps_tp2_allreduce_residual(const uint16_t* part, uint16_t* x, int n, void* 
                                 uint32_t* seen, int site, int n_sites, int max_n, int32_t* error,
                                 void* stream);
 
+/* The split o_proj / down_proj GEMV and its all-reduce in ONE kernel
+ * (kernels/quant_matmul.metal:15-69 on this rank's K slice, then
+ * runners/engine.py:219-221 / 241-243 over both ranks): part[b, r] =
+ * fp16(W_r . a[b]) for the `rows` rows, stored locally and into the peer's
+ * receive slot; after a hand-off between the same CTA on both GPUs,
+ * x[b, r] <- x[b, r] + (part[b, r] + peer's part[b, r]).  x and part are
+ * [batch, rows] contiguous, batch * rows <= max_n; same exchange buffers,
+ * counters, call rules and error behaviour as lmps_tp2_allreduce_residual
+ * (use other sites than it).  LMPS_ERR_UNSUPPORTED when the GEMV grid would
+ * exceed 64 CTAs. */
+int lmps_gemv_q4_tp2_residual(const uint8_t* packed, const uint16_t* scales, const uint16_t* a, int lda,
+                              uint16_t* x, uint16_t* part, int rows, int k, int batch, void* comm,
+                              void* peer_comm, uint32_t* seen, int site, int n_sites, int max_n,
+                              int32_t* error, void* stream);
+
 /* ---- weight format ---------------------------------------------------- */
 
 /* Device Q4 packer, bit-exact with utils/pack_weights.py:42-60

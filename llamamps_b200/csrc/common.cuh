@@ -122,3 +122,54 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 }
 
 }  // namespace lmps
+
+// Exchange-buffer layout of the two-way tensor-parallel kernels (tp_comm.cu,
+// q4_gemv.cu): [n_sites][2][max_n] fp16 receive slots, then
+// [n_sites][kTp2MaxCtas] uint32 flags, in this rank's buffer and the peer's.
+constexpr int kTp2MaxCtas = 64;
+struct Tp2Site {
+  uint16_t* recv;       // this rank's two slots of the site
+  uint16_t* peer_recv;  // the peer's two slots (mapped)
+  uint32_t* flags;      // this rank's flag words of the site (written by the peer)
+  uint32_t* peer_flags;
+};
+static inline Tp2Site lmps_tp2_site(void* comm, void* peer_comm, int site, int n_sites, int max_n) {
+  const size_t slots = static_cast<size_t>(n_sites) * 2u * static_cast<size_t>(max_n);
+  const size_t off = static_cast<size_t>(site) * 2u * static_cast<size_t>(max_n);
+  Tp2Site t;
+  t.recv = static_cast<uint16_t*>(comm) + off;
+  t.peer_recv = static_cast<uint16_t*>(peer_comm) + off;
+  t.flags = reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(comm) + slots) + site * kTp2MaxCtas;
+  t.peer_flags = reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(peer_comm) + slots) + site * kTp2MaxCtas;
+  return t;
+}
+__device__ __forceinline__ void lmps_st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t lmps_ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long lmps_globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Thread 0 of a CTA: publish `want` to the peer's flag `cta`, then wait
+// (bounded) until this rank's flag `cta` reaches it.  False after a timeout
+// (error raised).
+__device__ __forceinline__ bool lmps_tp2_handshake(uint32_t* peer_flags, const uint32_t* flags, int cta,
+                                                   uint32_t want, int32_t* error) {
+  constexpr unsigned long long kTimeoutNs = 5000000000ull;  // host-side skew between the ranks stays far below
+  lmps_st_release_sys(peer_flags + cta, want);
+  const unsigned long long t0 = lmps_globaltimer();
+  while (static_cast<int>(lmps_ld_acquire_sys(flags + cta) - want) < 0) {
+    if (lmps_globaltimer() - t0 > kTimeoutNs) {
+      atomicExch(error, 1);
+      return false;
+    }
+  }
+  return true;
+}
+

@@ -16,13 +16,15 @@
 //    memory with an XOR swizzle on 16-byte chunks so the strided group reads
 //    are bank-conflict free.
 // Epilogues fuse what follows the GEMV in runners/engine.py: q/k/v bias,
-// residual add (residual.metal), SwiGLU over a gate/up pair (swiglu.metal) and
-// the LM-head argmax (engine.py:180-181).
+// residual add (residual.metal), SwiGLU over a gate/up pair (swiglu.metal),
+// the LM-head argmax (engine.py:180-181), and -- for two-way tensor
+// parallelism -- the all-reduce of the partial o/down products with the
+// residual add, over NVLink peer memory in the same kernel (EPI_TP2).
 #include "common.cuh"
 
 namespace lmps {
 
-enum GemvEpi { EPI_PLAIN = 0, EPI_BIAS = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
+enum GemvEpi { EPI_PLAIN = 0, EPI_BIAS = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4, EPI_TP2 = 5 };
 
 struct GemvParams {
   const uint8_t* w;
@@ -37,6 +39,16 @@ struct GemvParams {
   const __half* res;            // EPI_RESID
   unsigned long long* keys;     // EPI_ARGMAX
   int rows, k, batch;
+  // EPI_TP2: y = this rank's partial [batch, ldy]; x_io the residual (same
+  // layout), updated to x + (partial + the peer's partial)
+  __half* x_io;
+  __half* tp_peer_recv;         // the peer's two receive slots of the site
+  const __half* tp_recv;        // this rank's
+  uint32_t* tp_peer_flags;
+  const uint32_t* tp_flags;
+  uint32_t* tp_seen;            // this rank's call counts of the site, per CTA
+  int32_t* tp_error;
+  int tp_slot;                  // elements per receive slot
 };
 
 constexpr int kGemvThreads = 256;
@@ -110,6 +122,17 @@ __global__ void __launch_bounds__(kGemvThreads) q4_gemv_kernel(const GemvParams 
   extern __shared__ __align__(16) unsigned char smem_raw[];
   uint4* xs = reinterpret_cast<uint4*>(smem_raw);  // [NB][k/8] swizzled 16-byte chunks
   const int k = p.k;
+  // EPI_TP2: thread 0's decisions reach the CTA through __syncthreads_or
+  // (no static shared memory: the dynamic limit is set to the maximum)
+  bool tp_go = false;
+  uint32_t tp_want = 0;
+  size_t tp_sl = 0;
+  if constexpr (EPI == EPI_TP2) {
+    // one reading of the error word per CTA (an earlier exchange failed: leave)
+    if (threadIdx.x == 0) tp_go = *reinterpret_cast<volatile int32_t*>(p.tp_error) == 0;
+    tp_want = p.tp_seen[blockIdx.x] + 1u;
+    tp_sl = static_cast<size_t>(tp_want & 1u) * p.tp_slot;
+  }
   const int G = k / kQ4Group;
   const int vpr_real = k / 8;
   const int vpr = (vpr_real + 7) & ~7;  // row stride in chunks: whole 128-byte lines
@@ -121,7 +144,11 @@ __global__ void __launch_bounds__(kGemvThreads) q4_gemv_kernel(const GemvParams 
       v = *reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(b) * p.ldx + c * 8);
     xs[b * vpr + xswz(c)] = v;
   }
-  __syncthreads();
+  if constexpr (EPI == EPI_TP2) {
+    if (!__syncthreads_or(tp_go)) return;
+  } else {
+    __syncthreads();
+  }
 
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
   constexpr int RPW = kWarp / LPR;
@@ -185,6 +212,11 @@ __global__ void __launch_bounds__(kGemvThreads) q4_gemv_kernel(const GemvParams 
           // residual.metal:19 adds the fp16 GEMV output to the fp16 residual.
           const __half o = __float2half_rn(acc[b]);
           *yp = __hadd(p.res[static_cast<size_t>(b) * p.ldy + row], o);
+        } else if constexpr (EPI == EPI_TP2) {
+          // this rank's fp16 partial: kept, and stored into the peer's slot
+          const __half o = __float2half_rn(acc[b]);
+          *yp = o;
+          p.tp_peer_recv[tp_sl + static_cast<size_t>(b) * p.ldy + row] = o;
         } else if constexpr (EPI == EPI_SWIGLU) {
           const float g = __half2float(__float2half_rn(acc[b]));
           const float u = __half2float(__float2half_rn(acc2[b]));
@@ -202,6 +234,30 @@ __global__ void __launch_bounds__(kGemvThreads) q4_gemv_kernel(const GemvParams 
     for (int b = 0; b < NB; ++b) {
       const unsigned long long m = warp_max_u64(best[b]);
       if (lane == 0 && b < p.batch && m != 0ull) atomicMax(p.keys + b, m);
+    }
+  }
+  if constexpr (EPI == EPI_TP2) {
+    // hand-off with the same CTA of the peer (same rows), then the rows of
+    // this CTA: x + (own partial + the peer's), fp16, the peer computing the
+    // same sums in the other order (commutative: bit-identical)
+    __threadfence_system();
+    __syncthreads();
+    bool good = false;
+    if (threadIdx.x == 0) {
+      good = lmps_tp2_handshake(p.tp_peer_flags, p.tp_flags, blockIdx.x, tp_want, p.tp_error);
+      if (good) p.tp_seen[blockIdx.x] = tp_want;
+    }
+    if (!__syncthreads_or(good)) return;
+    __threadfence_system();
+    for (int r0 = (blockIdx.x * kGemvWarps + warp) * RPW; r0 < p.rows; r0 += gridDim.x * kGemvWarps * RPW) {
+      const int row = r0 + rsub;
+      if (row < p.rows && sub == 0) {
+        for (int b = 0; b < p.batch; ++b) {
+          const size_t i = static_cast<size_t>(b) * p.ldy + row;
+          const __half s = __hadd(p.y[i], __ldcg(p.tp_recv + tp_sl + i));  // own write, same thread
+          p.x_io[i] = __hadd(p.x_io[i], s);
+        }
+      }
     }
   }
 }
@@ -325,6 +381,35 @@ extern "C" int lmps_gemv_q4_residual(const uint8_t* packed, const uint16_t* scal
   GemvParams p = make_params(packed, scales, x, ldx, y, ldy, rows, k, batch);
   p.res = reinterpret_cast<const __half*>(residual);
   return launch_gemv<EPI_RESID>(p, lmps_stream(stream));
+}
+
+extern "C" int lmps_gemv_q4_tp2_residual(const uint8_t* packed, const uint16_t* scales, const uint16_t* a,
+                                         int lda, uint16_t* x, uint16_t* part, int rows, int k, int batch,
+                                         void* comm, void* peer_comm, uint32_t* seen, int site, int n_sites,
+                                         int max_n, int32_t* error, void* stream) {
+  int st = check_common(packed, scales, a, lda, rows, k, batch);
+  if (st) return st;
+  LMPS_CHECK_ARG(x && part && comm && peer_comm && seen && error);
+  LMPS_CHECK_ARG(n_sites >= 1 && site >= 0 && site < n_sites && max_n >= 8 && max_n % 8 == 0);
+  LMPS_CHECK_ARG(static_cast<long long>(batch) * rows <= max_n);
+  LMPS_CHECK_ARG(lmps_aligned(comm, 16) && lmps_aligned(peer_comm, 16) && lmps_aligned(seen, 4));
+  // every CTA must have a flag word and be resident at once (its counterpart
+  // on the peer waits for it): at most kTp2MaxCtas CTAs, none grid-strided
+  const int G = k / kQ4Group;
+  const int lpr = G % 32 == 0 ? 32 : G % 16 == 0 ? 16 : G % 8 == 0 ? 8 : 4;
+  const int rows_per_cta = kGemvWarps * (kWarp / lpr);
+  if ((rows + rows_per_cta - 1) / rows_per_cta > kTp2MaxCtas) return LMPS_ERR_UNSUPPORTED;
+  GemvParams p = make_params(packed, scales, a, lda, part, rows, rows, k, batch);
+  const Tp2Site t = lmps_tp2_site(comm, peer_comm, site, n_sites, max_n);
+  p.x_io = reinterpret_cast<__half*>(x);
+  p.tp_peer_recv = reinterpret_cast<__half*>(t.peer_recv);
+  p.tp_recv = reinterpret_cast<const __half*>(t.recv);
+  p.tp_peer_flags = t.peer_flags;
+  p.tp_flags = t.flags;
+  p.tp_seen = seen + site * kTp2MaxCtas;
+  p.tp_error = error;
+  p.tp_slot = max_n;
+  return launch_gemv<EPI_TP2>(p, lmps_stream(stream));
 }
 
 extern "C" int lmps_gemv_q4_swiglu(const uint8_t* gate_packed, const uint16_t* gate_scales,

@@ -41,22 +41,8 @@ namespace lmps {
 namespace tp {
 
 constexpr int kThreads = 256;
-constexpr int kMaxCtas = 64;  // flag words per site
-constexpr unsigned long long kTimeoutNs = 5000000000ull;  // host-side skew between the ranks stays far below
+constexpr int kMaxCtas = kTp2MaxCtas;  // flag words per site
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ uint64_t globaltimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
 __device__ __forceinline__ uint32_t hadd2u(uint32_t a, uint32_t b) {
   const __half2 r = __hadd2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
   return *reinterpret_cast<const uint32_t*>(&r);
@@ -67,7 +53,11 @@ __global__ void __launch_bounds__(kThreads)
                               uint4* peer_recv, const uint4* recv, uint32_t* peer_flags, const uint32_t* flags,
                               uint32_t* seen, int32_t* error) {
   __shared__ int ok;
-  if (*reinterpret_cast<volatile int32_t*>(error)) return;  // an earlier exchange failed: the pair is out of step
+  // an earlier exchange failed (the pair is out of step): the whole CTA
+  // leaves, on one reading of the flag
+  if (threadIdx.x == 0) ok = *reinterpret_cast<volatile int32_t*>(error) == 0;
+  __syncthreads();
+  if (!ok) return;
   const int per = (n8 + gridDim.x - 1) / gridDim.x;
   const int lo = blockIdx.x * per, hi = min(n8, lo + per);
   const uint32_t want = seen[blockIdx.x] + 1u;
@@ -76,18 +66,9 @@ __global__ void __launch_bounds__(kThreads)
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
-    st_release_sys(peer_flags + blockIdx.x, want);
-    int good = 1;
-    const uint64_t t0 = globaltimer();
-    while (static_cast<int>(ld_acquire_sys(flags + blockIdx.x) - want) < 0) {
-      if (globaltimer() - t0 > kTimeoutNs) {
-        atomicExch(error, 1);
-        good = 0;
-        break;
-      }
-    }
+    const bool good = lmps_tp2_handshake(peer_flags, flags, blockIdx.x, want, error);
     if (good) seen[blockIdx.x] = want;
-    ok = good;
+    ok = good ? 1 : 0;
   }
   __syncthreads();
   if (!ok) return;
@@ -158,19 +139,14 @@ extern "C" int lmps_tp2_allreduce_residual(const uint16_t* part, uint16_t* x, in
   LMPS_CHECK_ARG(n >= 8 && n % 8 == 0 && n <= max_n);
   LMPS_CHECK_ARG(lmps_aligned(part, 16) && lmps_aligned(x, 16) && lmps_aligned(comm, 16) &&
                  lmps_aligned(peer_comm, 16) && lmps_aligned(seen, 4));
-  // buffer layout: [n_sites][2][max_n] fp16 receive slots, then [n_sites][kMaxCtas] u32 flags
-  const size_t slots = static_cast<size_t>(n_sites) * 2u * static_cast<size_t>(max_n);
-  uint16_t* recv = static_cast<uint16_t*>(comm) + static_cast<size_t>(site) * 2u * max_n;
-  uint16_t* peer_recv = static_cast<uint16_t*>(peer_comm) + static_cast<size_t>(site) * 2u * max_n;
-  uint32_t* flags = reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(comm) + slots) + site * tp::kMaxCtas;
-  uint32_t* peer_flags = reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(peer_comm) + slots) + site * tp::kMaxCtas;
+  const Tp2Site t = lmps_tp2_site(comm, peer_comm, site, n_sites, max_n);
   const int n8 = n / 8;
   // one CTA per 2048 elements, at most kMaxCtas: every CTA of the grid is
   // resident at once, so each one's counterpart on the peer GPU runs too
   const int grid = std::min(tp::kMaxCtas, (n8 + tp::kThreads - 1) / tp::kThreads);
   tp::allreduce_residual_kernel<<<grid, tp::kThreads, 0, lmps_stream(stream)>>>(
       reinterpret_cast<const uint4*>(part), reinterpret_cast<uint4*>(x), n8, max_n / 8,
-      reinterpret_cast<uint4*>(peer_recv), reinterpret_cast<const uint4*>(recv), peer_flags, flags,
+      reinterpret_cast<uint4*>(t.peer_recv), reinterpret_cast<const uint4*>(t.recv), t.peer_flags, t.flags,
       seen + site * tp::kMaxCtas, error);
   return lmps_launch_status();
 }

@@ -312,3 +312,18 @@ def tp2_allreduce_residual(part, x, ex: PeerExchange, site: int, error):
          ex.peer, _dev(ex.seen, "seen", torch.int32), site, ex.n_sites, ex.max_n,
          _dev(error, "error", torch.int32), _stream())
     return x
+
+
+def gemv_q4_tp2_residual(packed, scales, a, rows: int, k: int, x, part, ex: PeerExchange, site: int, error):
+    """One kernel: part = W a (this rank's K slice, fp16), stored into the
+    peer's receive slot over NVLink, then x <- x + (part + the peer's part)
+    after a per-CTA hand-off with the peer's same CTA."""
+    if ex.peer is None:
+        raise RuntimeError("the peer exchange is not connected")
+    a2, B = _x2d(a)
+    call("lmps_gemv_q4_tp2_residual", _dev(packed, "packed", torch.uint8), _dev(scales, "scales", FP16),
+         _dev(a2, "a", FP16), a2.shape[1], _dev(x, "x", FP16), _dev(part, "part", FP16), rows, k, B, ex.comm,
+         ex.peer, _dev(ex.seen, "seen", torch.int32), site, ex.n_sites, ex.max_n,
+         _dev(error, "error", torch.int32), _stream())
+    return x
+

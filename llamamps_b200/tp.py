@@ -88,9 +88,12 @@ class TPEngine(QwenEngine):
     kernels on the rank's slice, an all-reduce after o_proj and down_proj.
 
     ``comm="p2p"`` (two ranks): decode steps exchange the partial products
-    through the peer's memory (:func:`kernels.tp2_allreduce_residual`, NVLink
-    stores + flags, fused with the residual add), so a step has no host-side
-    collective and runs as a CUDA graph; dense prefill, whose partials are
+    through the peer's memory, so a step has no host-side collective and runs
+    as a CUDA graph: on the GEMV path (batch <= 8) the o / down projection,
+    the NVLink stores into the peer's buffer and the residual add are one
+    kernel (:func:`kernels.gemv_q4_tp2_residual`); on the GEMM path the
+    exchange follows the GEMM (:func:`kernels.tp2_allreduce_residual`).  The
+    two use separate call sites.  Dense prefill, whose partials are
     [tokens, hidden], keeps NCCL.  ``comm="nccl"``: every all-reduce is
     NCCL's and steps launch eagerly.
 
@@ -112,7 +115,8 @@ class TPEngine(QwenEngine):
         self.comm_err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.exchange = None
         if comm == "p2p" and world == 2 and self.device.type == "cuda":
-            self.exchange = K.PeerExchange(2 * self.cfg.n_layers, self.max_batch * self.cfg.hidden, self.device)
+            # sites [0, 2L): exchanges after a GEMM; [2L, 4L): fused GEMV exchanges
+            self.exchange = K.PeerExchange(4 * self.cfg.n_layers, self.max_batch * self.cfg.hidden, self.device)
             handles = [None] * world
             dist.all_gather_object(handles, self.exchange.handle(), group=group)
             self.exchange.connect(handles[1 - rank])
@@ -145,6 +149,9 @@ class TPEngine(QwenEngine):
         dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
         K.residual_add(x, part, out=x)
 
+    def _fused(self, x: torch.Tensor) -> bool:
+        return self.exchange is not None and x.numel() <= self.exchange.max_n
+
     def _partial(self, rows: int) -> torch.Tensor:
         return self._part[:rows] if rows <= self._part.shape[0] else torch.empty(
             rows, self.cfg.hidden, dtype=torch.float16, device=self.device)
@@ -154,6 +161,10 @@ class TPEngine(QwenEngine):
         if gemm:
             K.w4a16_gemm(att, lw.o_packed, lw.o_scales, c.hidden, c.q_dim, out=part, error=self.gemm_err,
                          workspace=self._ws(ws))
+        elif self._fused(x):
+            K.gemv_q4_tp2_residual(lw.o_packed, lw.o_scales, att, c.hidden, c.q_dim, x, part, self.exchange,
+                                   2 * c.n_layers + self._site[id(lw)], self.comm_err)
+            return
         else:
             K.gemv_q4(lw.o_packed, lw.o_scales, att, c.hidden, c.q_dim, out=part)
         self._reduce_add(part, x, self._site[id(lw)])
@@ -163,6 +174,10 @@ class TPEngine(QwenEngine):
         if gemm:
             K.w4a16_gemm(a, lw.down_packed, lw.down_scales, c.hidden, c.intermediate, out=part,
                          error=self.gemm_err, workspace=self._ws(ws))
+        elif self._fused(x):
+            K.gemv_q4_tp2_residual(lw.down_packed, lw.down_scales, a, c.hidden, c.intermediate, x, part,
+                                   self.exchange, 2 * c.n_layers + self._site[id(lw)] + 1, self.comm_err)
+            return
         else:
             K.gemv_q4(lw.down_packed, lw.down_scales, a, c.hidden, c.intermediate, out=part)
         self._reduce_add(part, x, self._site[id(lw)] + 1)

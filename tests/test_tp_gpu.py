@@ -48,14 +48,16 @@ def _rank(rank, world, port, out, dense, comm):
 
 def _exchange_rank(rank, world, port, out):
     """Peer-memory all-reduce + residual against NCCL's sum + residual_add:
-    several sites, back-to-back calls on one site, 1 to 8 rows."""
+    several sites, back-to-back calls on one site, 1 to 8 rows; and the fused
+    GEMV + exchange at the o_proj (1536 x 768) and down_proj (1536 x 4480)
+    shapes of a 2-way split against GEMV, NCCL sum, residual_add."""
     _env(rank, world, port)
     import torch.distributed as dist
     from llamamps_b200 import kernels as K
     from llamamps_b200.tp import init_from_env
     init_from_env("nccl", timeout_s=60)
     dev = torch.device(f"cuda:{rank}")
-    ex = K.PeerExchange(3, 8 * 1536, dev)
+    ex = K.PeerExchange(5, 8 * 1536, dev)
     try:
         handles = [None] * world
         dist.all_gather_object(handles, ex.handle())
@@ -72,6 +74,21 @@ def _exchange_rank(rank, world, port, out):
             dist.all_reduce(ref)
             ref = K.residual_add(x.clone(), ref, out=torch.empty_like(x))
             K.tp2_allreduce_residual(part, x, ex, site, err)
+            torch.cuda.synchronize(dev)
+            mism += int((x.view(torch.int16) != ref.view(torch.int16)).sum().item())
+        wg = torch.Generator(device=dev).manual_seed(300 + rank)   # each rank its own K slice
+        mats = {k: (torch.randint(0, 256, (1536 * k // 2,), generator=wg, device=dev, dtype=torch.uint8),
+                    (torch.rand(1536 * k // 32, generator=wg, device=dev) * 0.04 + 0.005).half())
+                for k in (768, 4480)}
+        part = torch.empty(8 * 1536, dtype=torch.float16, device=dev)
+        for site, k, rows in [(3, 768, 1), (4, 4480, 1), (3, 768, 8), (3, 768, 8), (4, 4480, 5), (3, 768, 2)]:
+            packed, scales = mats[k]
+            a = torch.randn(rows, k, generator=g, device=dev).half()
+            x = torch.randn(rows, 1536, generator=xg, device=dev).half()
+            ref = K.gemv_q4(packed, scales, a, 1536, k)
+            dist.all_reduce(ref)
+            ref = K.residual_add(x.clone(), ref, out=torch.empty_like(x))
+            K.gemv_q4_tp2_residual(packed, scales, a, 1536, k, x, part[:rows * 1536].view(rows, 1536), ex, site, err)
             torch.cuda.synchronize(dev)
             mism += int((x.view(torch.int16) != ref.view(torch.int16)).sum().item())
         out[rank] = (mism, int(err.item()))
