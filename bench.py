@@ -327,9 +327,9 @@ def extra_configs(mw, cfg, args, rank, world, dist, peak):
             B, P = 8, 2048
             prompt = torch.from_numpy(np.random.default_rng(3).integers(0, cfg.vocab, (B, P)))
             res = {}
-            for comm in ("p2p", "nccl"):
+            for comm, fuse in (("p2p", False), ("p2p", True), ("nccl", False)):
                 eng = TPEngine(mw, rank, world, device=torch.device("cuda"), max_batch=B, max_seq_len=P + 32,
-                               comm=comm)
+                               comm=comm, fuse_exchange=fuse)
                 try:
                     eng.reset(B)
                     eng.prefill(prompt, dense=True)  # warm-up
@@ -338,7 +338,7 @@ def extra_configs(mw, cfg, args, rank, world, dist, peak):
                     eng.decode_steps(2, record=False)  # graph capture outside the timed region
                     td = _timed(lambda: eng.decode_steps(16, record=False), world, dist)
                     eng.check_comm()
-                    res[comm] = (t, td)
+                    res[comm + ("_fused" if fuse else "")] = (t, td)
                 finally:
                     eng.close()
                 del eng
@@ -346,11 +346,13 @@ def extra_configs(mw, cfg, args, rank, world, dist, peak):
             out["c3_prefill_tp2"] = {
                 "value": round(B * P / t, 1), "unit": "prompt tok/s", "ms": round(t * 1e3, 2),
                 "decode_after_prefill_tok_s": round(B * 16 / td, 1),
+                "decode_fused_gemv_exchange_tok_s": round(B * 16 / res["p2p_fused"][1], 1),
                 "decode_nccl_tok_s": round(B * 16 / res["nccl"][1], 1),
                 "path": "tp2: KV head r and its query heads on rank r; dense GEMM prefill with NCCL "
                         "all-reduces (sum, fp16) after o_proj and down_proj, then bs8 decode as a CUDA graph "
                         "with the all-reduces over peer memory (NVLink stores + flags, fused with the "
-                        "residual add); decode_nccl_tok_s: the same decode with NCCL all-reduces, eager"}
+                        "residual add); decode_fused_gemv_exchange_tok_s: GEMV and exchange in one kernel; "
+                        "decode_nccl_tok_s: the same decode with NCCL all-reduces, eager"}
         except Exception as e:
             out["c3_prefill_tp2"] = {"error": repr(e)[:200]}
     # -- c4

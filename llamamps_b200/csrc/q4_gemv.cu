@@ -239,8 +239,9 @@ __global__ void __launch_bounds__(kGemvThreads) q4_gemv_kernel(const GemvParams 
   if constexpr (EPI == EPI_TP2) {
     // hand-off with the same CTA of the peer (same rows), then the rows of
     // this CTA: x + (own partial + the peer's), fp16, the peer computing the
-    // same sums in the other order (commutative: bit-identical)
-    __threadfence_system();
+    // same sums in the other order (commutative: bit-identical).  Only the
+    // lanes that stored to the peer fence at system scope.
+    if (sub == 0) __threadfence_system();
     __syncthreads();
     bool good = false;
     if (threadIdx.x == 0) {
@@ -248,7 +249,7 @@ __global__ void __launch_bounds__(kGemvThreads) q4_gemv_kernel(const GemvParams 
       if (good) p.tp_seen[blockIdx.x] = tp_want;
     }
     if (!__syncthreads_or(good)) return;
-    __threadfence_system();
+    if (sub == 0) __threadfence_system();
     for (int r0 = (blockIdx.x * kGemvWarps + warp) * RPW; r0 < p.rows; r0 += gridDim.x * kGemvWarps * RPW) {
       const int row = r0 + rsub;
       if (row < p.rows && sub == 0) {

@@ -89,11 +89,11 @@ class TPEngine(QwenEngine):
 
     ``comm="p2p"`` (two ranks): decode steps exchange the partial products
     through the peer's memory, so a step has no host-side collective and runs
-    as a CUDA graph: on the GEMV path (batch <= 8) the o / down projection,
-    the NVLink stores into the peer's buffer and the residual add are one
-    kernel (:func:`kernels.gemv_q4_tp2_residual`); on the GEMM path the
-    exchange follows the GEMM (:func:`kernels.tp2_allreduce_residual`).  The
-    two use separate call sites.  Dense prefill, whose partials are
+    as a CUDA graph: the exchange kernel (:func:`kernels.tp2_allreduce_residual`)
+    follows the o / down projection; with ``fuse_exchange=True`` the GEMV path
+    (batch <= 8) instead does projection, NVLink stores into the peer's
+    buffer and residual add in one kernel (:func:`kernels.gemv_q4_tp2_residual`,
+    its own call sites).  Dense prefill, whose partials are
     [tokens, hidden], keeps NCCL.  ``comm="nccl"``: every all-reduce is
     NCCL's and steps launch eagerly.
 
@@ -101,7 +101,8 @@ class TPEngine(QwenEngine):
     up by order).  Call :meth:`close` on every rank before the process group
     is destroyed."""
 
-    def __init__(self, weights: ModelWeights, rank: int, world: int, group=None, comm: str = "p2p", **kw):
+    def __init__(self, weights: ModelWeights, rank: int, world: int, group=None, comm: str = "p2p",
+                 fuse_exchange: bool = False, **kw):
         kw.setdefault("decoder", "kernels")
         if kw["decoder"] != "kernels":
             raise ValueError("the tensor-parallel engine runs the per-stage kernels")
@@ -114,6 +115,7 @@ class TPEngine(QwenEngine):
         self._site = {id(lw): 2 * li for li, lw in enumerate(self.weights.layers)}
         self.comm_err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.exchange = None
+        self.fuse_exchange = fuse_exchange
         if comm == "p2p" and world == 2 and self.device.type == "cuda":
             # sites [0, 2L): exchanges after a GEMM; [2L, 4L): fused GEMV exchanges
             self.exchange = K.PeerExchange(4 * self.cfg.n_layers, self.max_batch * self.cfg.hidden, self.device)
@@ -150,7 +152,7 @@ class TPEngine(QwenEngine):
         K.residual_add(x, part, out=x)
 
     def _fused(self, x: torch.Tensor) -> bool:
-        return self.exchange is not None and x.numel() <= self.exchange.max_n
+        return self.fuse_exchange and self.exchange is not None and x.numel() <= self.exchange.max_n
 
     def _partial(self, rows: int) -> torch.Tensor:
         return self._part[:rows] if rows <= self._part.shape[0] else torch.empty(

@@ -36,7 +36,8 @@ def _rank(rank, world, port, out, dense, comm):
     try:
         mw = synth_model(_cfg(), seed=17, device=f"cuda:{rank}")
         prompts = np.random.default_rng(PROMPT_SEED).integers(0, 8192, (2, 150 if dense else 9))
-        eng = TPEngine(mw, rank, world, max_batch=2, max_seq_len=256, device=f"cuda:{rank}", comm=comm)
+        eng = TPEngine(mw, rank, world, max_batch=2, max_seq_len=256, device=f"cuda:{rank}",
+                       comm="nccl" if comm == "nccl" else "p2p", fuse_exchange=comm == "p2p_fused")
         try:
             got = eng.generate_batch(prompts, STEPS)
             out[rank] = got.tolist()
@@ -127,7 +128,7 @@ def test_tp2_peer_allreduce_equals_nccl(cuda):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("dense,comm", [(False, "p2p"), (True, "p2p"), (False, "nccl")])
+@pytest.mark.parametrize("dense,comm", [(False, "p2p"), (True, "p2p"), (False, "p2p_fused"), (False, "nccl")])
 def test_tp2_generate_matches_oracle(cuda, dense, comm):
     import torch.multiprocessing as mp
     from llamamps_b200.weights import model_host_arrays, synth_model
