@@ -155,6 +155,21 @@ int lmps_gqa_decode_attention(const uint16_t* q, const uint16_t* k_pool, const u
                               int page_size, int n_q_heads, int n_kv_heads, int head_dim,
                               int batch, int max_seq_len, int n_splits, void* stream);
 
+/* lmps_rope_kv_append followed by lmps_gqa_decode_attention in one launch
+ * (kernels/rope.metal + the cache append, then attention.metal, softmax.metal,
+ * attn_sum.metal): qkv is the biased q|k|v row of each sequence
+ * [batch, (n_q_heads + 2 n_kv_heads) * head_dim]; pos[b] is the new token's
+ * position and seq_lens[b] must be pos[b] + 1.  The rotated K row and the V
+ * row of pos[b] are written into the pools (as lmps_rope_kv_append writes
+ * them) and attended in the same call; out and the workspace as for
+ * lmps_gqa_decode_attention.  Outputs are bit-identical to the two calls. */
+int lmps_gqa_decode_attention_rope(const uint16_t* qkv, const int32_t* pos, const float* inv_freq,
+                                   int rope_style, uint16_t* k_pool, uint16_t* v_pool,
+                                   const int32_t* block_table, const int32_t* seq_lens, uint16_t* out,
+                                   void* workspace, size_t workspace_bytes, int max_pages, int page_size,
+                                   int n_q_heads, int n_kv_heads, int head_dim, int batch, int max_seq_len,
+                                   int n_splits, void* stream);
+
 /* Size of the fixed device scratch used by lmps_gqa_decode_attention_noalloc. */
 #define LMPS_GQA_ATTENTION_NOALLOC_SCRATCH_BYTES (4u * 1024u * 1024u)
 

@@ -49,6 +49,9 @@ _SIGS = {
     "lmps_prefill_attention": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_vp, c_int, c_int, c_int,
                                        c_int, c_int, c_int, c_vp]),
     "lmps_swiglu_rows": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_int, c_vp]),
+    "lmps_gqa_decode_attention_rope": (c_int, [c_vp, c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                               c_size, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                               c_vp]),
     "lmps_comm_alloc": (c_int, [c_size, ctypes.POINTER(c_vp)]),
     "lmps_comm_free": (c_int, [c_vp]),
     "lmps_ipc_handle": (c_int, [c_vp, c_vp]),

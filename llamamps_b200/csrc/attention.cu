@@ -12,6 +12,11 @@
 // each split writes an unnormalised partial (acc, max, sum) that a combine
 // kernel merges with a log-sum-exp rescale.  With one split the CTA writes
 // the normalised output directly.
+// The _rope entry point also does rope_kv_append's work (kernels/rope.metal
+// on q and k, then the cache append): each CTA rotates the query heads of its
+// KV head from the q|k|v row, and the split that attends the new position
+// rotates and writes that K row (and the V row) into the paged cache before
+// it stages its tiles.
 #include <cmath>
 
 #include "common.cuh"
@@ -34,6 +39,14 @@ struct AttnParams {
   float* part_o;               // [B, Hq, splits, 128]
   float2* part_ml;             // [B, Hq, splits]
   int max_pages, page_size, n_q_heads, n_kv_heads, n_splits, chunk;
+  // fused RoPE + append (qkv != nullptr): q|k|v rows [B, (Hq + 2 Hkv) * 128]
+  // (bias applied), position of the new token per sequence (seq_lens = pos + 1)
+  const __half* qkv;
+  const int32_t* pos;
+  const float* inv_freq;
+  int rope_style;
+  __half* k_new;  // the pools, writable
+  __half* v_new;
 };
 
 struct __align__(16) AttnSmem {
@@ -59,9 +72,42 @@ __global__ void __launch_bounds__(kAttnThreads) gqa_decode_attn_kernel(const Att
   const int end = min(T, start + P.chunk);
   const int q_dim = P.n_q_heads * kHeadDim;
 
-  for (int i = tid; i < G * kHeadDim; i += kAttnThreads) {
-    const int h = i / kHeadDim, d = i - h * kHeadDim;
-    S.q[h][d] = __half2float(P.q[static_cast<size_t>(b) * q_dim + (kvh * G + h) * kHeadDim + d]);
+  if (P.qkv != nullptr) {
+    // RoPE of the G query heads (rounded to fp16 as rope_kv_append's output)
+    const int kv_dim = P.n_kv_heads * kHeadDim;
+    const __half* row = P.qkv + static_cast<size_t>(b) * (q_dim + 2 * kv_dim);
+    const int p = P.pos[b];
+    const float m = static_cast<float>(p);
+    for (int t = tid; t < G * (kHeadDim / 2); t += kAttnThreads) {
+      const int hl = t / (kHeadDim / 2);
+      int i1, i2, fi;
+      rope_pair_index(t - hl * (kHeadDim / 2), kHeadDim, P.rope_style, i1, i2, fi);
+      const __half* src = row + (kvh * G + hl) * kHeadDim;
+      __half a = src[i1], c = src[i2];
+      rope_rotate(a, c, m * P.inv_freq[fi]);
+      S.q[hl][i1] = __half2float(a);
+      S.q[hl][i2] = __half2float(c);
+    }
+    if (p >= start && p < end) {  // this split attends the new position: append its K/V rows first
+      const int page = P.block_table[static_cast<size_t>(b) * P.max_pages + p / P.page_size];
+      const size_t dst = ((static_cast<size_t>(page) * P.n_kv_heads + kvh) * P.page_size + p % P.page_size) * kHeadDim;
+      const __half* ksrc = row + q_dim + kvh * kHeadDim;
+      for (int t = tid; t < kHeadDim / 2; t += kAttnThreads) {
+        int i1, i2, fi;
+        rope_pair_index(t, kHeadDim, P.rope_style, i1, i2, fi);
+        __half a = ksrc[i1], c = ksrc[i2];
+        rope_rotate(a, c, m * P.inv_freq[fi]);
+        P.k_new[dst + i1] = a;
+        P.k_new[dst + i2] = c;
+      }
+      for (int t = tid; t < kHeadDim; t += kAttnThreads) P.v_new[dst + t] = row[q_dim + kv_dim + kvh * kHeadDim + t];
+      __threadfence();  // the rows are read back below through L2 by the tile staging
+    }
+  } else {
+    for (int i = tid; i < G * kHeadDim; i += kAttnThreads) {
+      const int h = i / kHeadDim, d = i - h * kHeadDim;
+      S.q[h][d] = __half2float(P.q[static_cast<size_t>(b) * q_dim + (kvh * G + h) * kHeadDim + d]);
+    }
   }
   if (tid < kMaxGroup) {
     S.m[tid] = -INFINITY;
@@ -256,13 +302,48 @@ extern "C" size_t lmps_gqa_attention_workspace_size(int batch, int n_q_heads, in
   return rows * head_dim * sizeof(float) + rows * sizeof(float2);
 }
 
+static int attention_launch(AttnParams P, const uint16_t* k_pool, const uint16_t* v_pool,
+                            const int32_t* block_table, const int32_t* seq_lens, uint16_t* out, void* workspace,
+                            size_t workspace_bytes, int max_pages, int page_size, int n_q_heads, int n_kv_heads,
+                            int head_dim, int batch, int max_seq_len, int n_splits, void* stream);
+
 extern "C" int lmps_gqa_decode_attention(const uint16_t* q, const uint16_t* k_pool,
                                          const uint16_t* v_pool, const int32_t* block_table,
                                          const int32_t* seq_lens, uint16_t* out, void* workspace,
                                          size_t workspace_bytes, int max_pages, int page_size,
                                          int n_q_heads, int n_kv_heads, int head_dim, int batch,
                                          int max_seq_len, int n_splits, void* stream) {
-  LMPS_CHECK_ARG(q && k_pool && v_pool && block_table && seq_lens && out);
+  LMPS_CHECK_ARG(q);
+  AttnParams P{};
+  P.q = reinterpret_cast<const __half*>(q);
+  return attention_launch(P, k_pool, v_pool, block_table, seq_lens, out, workspace, workspace_bytes, max_pages,
+                          page_size, n_q_heads, n_kv_heads, head_dim, batch, max_seq_len, n_splits, stream);
+}
+
+extern "C" int lmps_gqa_decode_attention_rope(const uint16_t* qkv, const int32_t* pos, const float* inv_freq,
+                                              int rope_style, uint16_t* k_pool, uint16_t* v_pool,
+                                              const int32_t* block_table, const int32_t* seq_lens, uint16_t* out,
+                                              void* workspace, size_t workspace_bytes, int max_pages,
+                                              int page_size, int n_q_heads, int n_kv_heads, int head_dim,
+                                              int batch, int max_seq_len, int n_splits, void* stream) {
+  LMPS_CHECK_ARG(qkv && pos && inv_freq);
+  LMPS_CHECK_ARG(rope_style == LMPS_ROPE_INTERLEAVED || rope_style == LMPS_ROPE_NEOX);
+  AttnParams P{};
+  P.qkv = reinterpret_cast<const __half*>(qkv);
+  P.pos = pos;
+  P.inv_freq = inv_freq;
+  P.rope_style = rope_style;
+  P.k_new = reinterpret_cast<__half*>(k_pool);
+  P.v_new = reinterpret_cast<__half*>(v_pool);
+  return attention_launch(P, k_pool, v_pool, block_table, seq_lens, out, workspace, workspace_bytes, max_pages,
+                          page_size, n_q_heads, n_kv_heads, head_dim, batch, max_seq_len, n_splits, stream);
+}
+
+static int attention_launch(AttnParams P, const uint16_t* k_pool, const uint16_t* v_pool,
+                            const int32_t* block_table, const int32_t* seq_lens, uint16_t* out, void* workspace,
+                            size_t workspace_bytes, int max_pages, int page_size, int n_q_heads, int n_kv_heads,
+                            int head_dim, int batch, int max_seq_len, int n_splits, void* stream) {
+  LMPS_CHECK_ARG(k_pool && v_pool && block_table && seq_lens && out);
   LMPS_CHECK_ARG(batch > 0 && max_pages > 0 && page_size > 0 && max_seq_len > 0);
   LMPS_CHECK_ARG(max_seq_len <= max_pages * page_size);
   LMPS_CHECK_ARG(n_kv_heads > 0 && n_q_heads % n_kv_heads == 0);
@@ -271,8 +352,6 @@ extern "C" int lmps_gqa_decode_attention(const uint16_t* q, const uint16_t* k_po
   LMPS_CHECK_ARG(lmps_aligned(k_pool, 16) && lmps_aligned(v_pool, 16));
   const size_t need = lmps_gqa_attention_workspace_size(batch, n_q_heads, head_dim, n_splits);
   if (need > 0 && (!workspace || workspace_bytes < need)) return LMPS_ERR_WORKSPACE;
-  AttnParams P{};
-  P.q = reinterpret_cast<const __half*>(q);
   P.k_pool = reinterpret_cast<const __half*>(k_pool);
   P.v_pool = reinterpret_cast<const __half*>(v_pool);
   P.block_table = block_table;

@@ -121,6 +121,33 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
   return (g / (1.0f + expf(-g))) * u;
 }
 
+// ---------------------------------------------------------------------------
+// RoPE -- kernels/rope.metal:19-40 with the position and frequency table as
+// inputs: angle = float(pos) * inv_freq[i]; (x1, x2) -> (x1 c - x2 s, x1 s + x2 c).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void rope_pair_index(int pair, int head_dim, int style, int& i1, int& i2,
+                                                int& fi) {
+  const int half_d = head_dim / 2;
+  const int h = pair / half_d;
+  const int j = pair - h * half_d;
+  if (style == LMPS_ROPE_INTERLEAVED) {
+    i1 = h * head_dim + 2 * j;
+    i2 = i1 + 1;
+  } else {
+    i1 = h * head_dim + j;
+    i2 = i1 + half_d;
+  }
+  fi = j;
+}
+
+__device__ __forceinline__ void rope_rotate(__half& a, __half& b, float ang) {
+  float s, c;
+  sincosf(ang, &s, &c);
+  const float x1 = __half2float(a), x2 = __half2float(b);
+  a = __float2half_rn(x1 * c - x2 * s);
+  b = __float2half_rn(x1 * s + x2 * c);
+}
+
 }  // namespace lmps
 
 // Exchange-buffer layout of the two-way tensor-parallel kernels (tp_comm.cu,

@@ -183,13 +183,12 @@ class QwenEngine:
             else:
                 K.gemv_q4_bias(lw.qkv_packed, lw.qkv_scales, lw.qkv_bias, xn, c.qkv_rows, c.hidden,
                                out=self.buf_qkv[:B])
-            K.rope_kv_append(self.buf_qkv[:B], self.pos, self.inv_freq, self.buf_q[:B], kp, vp,
-                             self.cache.block_table, self.cache.page_size, c.n_q_heads,
-                             c.n_kv_heads, c.head_dim, c.rope_style_code)
-            K.gqa_decode_attention(self.buf_q[:B], kp, vp, self.cache.block_table, self.seq_lens,
-                                   self.buf_attn[:B], self.attn_ws, self.cache.page_size,
-                                   c.n_q_heads, c.n_kv_heads, c.head_dim, self.max_seq_len,
-                                   self.n_splits)
+            # RoPE + KV append + attention in one launch (rope_kv_append's work
+            # done by the attention CTAs)
+            K.gqa_decode_attention_rope(self.buf_qkv[:B], self.pos, self.inv_freq, kp, vp,
+                                        self.cache.block_table, self.seq_lens, self.buf_attn[:B],
+                                        self.attn_ws, self.cache.page_size, c.n_q_heads, c.n_kv_heads,
+                                        c.head_dim, self.max_seq_len, self.n_splits, c.rope_style_code)
             self._o_proj(lw, self.buf_attn[:B], x, gemm)
             K.rms_norm(x, lw.post_norm, c.eps, out=xn)
             if gemm:
@@ -335,7 +334,11 @@ class QwenEngine:
         persistent decoder runs any number of steps in one launch."""
         if self.pdec is not None:
             return 1
-        per_layer = 8 + (1 if self.n_splits > 1 else 0)
+        # norm, q|k|v, RoPE + append + attention (+ split combine), o, norm,
+        # gate/up (+ SwiGLU on the GEMM path), down; then embed, final norm, the
+        # LM head with its argmax (two launches on either path), advance
+        gemm = self.batch > GEMV_MAX_BATCH
+        per_layer = 7 + (1 if self.n_splits > 1 else 0) + (1 if gemm else 0)
         return 1 + self.layers * per_layer + 1 + 2 + 1
 
     def step_tokens(self, token_ids) -> np.ndarray:

@@ -161,6 +161,21 @@ def rope_kv_append(qkv, pos, inv_freq, q_out, k_pool, v_pool, block_table, page_
     return q_out
 
 
+def gqa_decode_attention_rope(qkv, pos, inv_freq, k_pool, v_pool, block_table, seq_lens, out, workspace,
+                              page_size: int, n_q_heads: int, n_kv_heads: int, head_dim: int,
+                              max_seq_len: int, n_splits: int, style: int = 0):
+    """rope_kv_append + gqa_decode_attention in one launch (seq_lens = pos + 1)."""
+    B = qkv.shape[0]
+    ws_ptr = workspace.data_ptr() if workspace is not None and workspace.numel() else None
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    call("lmps_gqa_decode_attention_rope", _dev(qkv, "qkv", FP16), _dev(pos, "pos", torch.int32),
+         _dev(inv_freq, "inv_freq", torch.float32), style, _dev(k_pool, "k_pool", FP16),
+         _dev(v_pool, "v_pool", FP16), _dev(block_table, "block_table", torch.int32),
+         _dev(seq_lens, "seq_lens", torch.int32), _dev(out, "out", FP16), ws_ptr, ws_bytes,
+         block_table.shape[1], page_size, n_q_heads, n_kv_heads, head_dim, B, max_seq_len, n_splits, _stream())
+    return out
+
+
 def attention_splits(batch: int, n_kv_heads: int, max_seq_len: int, page_size: int) -> int:
     return int(lib().lmps_gqa_attention_splits(batch, n_kv_heads, max_seq_len, page_size))
 

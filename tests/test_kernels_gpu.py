@@ -274,3 +274,35 @@ def test_q4_pack_device_bit_exact(cuda):
     p, s = K.q4_pack_device(_t(w.reshape(-1)))
     rp, rs = M.q4_pack(w)
     assert np.array_equal(p.cpu().numpy(), rp) and f16_bits_equal(s.cpu().numpy(), rs)
+
+
+@pytest.mark.parametrize("T_list,max_seq,n_splits", [([5, 16, 40], 64, 1), ([65, 1, 200], 256, 3), ([130, 7], 192, 2)])
+def test_attention_rope_equals_rope_append_then_attention(cuda, T_list, max_seq, n_splits):
+    """The one-launch RoPE + KV append + attention against lmps_rope_kv_append
+    followed by lmps_gqa_decode_attention: same output and same cache, bit for
+    bit (the new position is the last one of each sequence)."""
+    from llamamps_b200 import kernels as K
+    from llamamps_b200.engine import rope_inv_freq
+    rng = np.random.default_rng(sum(T_list) + n_splits)
+    B, ps = len(T_list), 64
+    pos_np = np.array([t - 1 for t in T_list], np.int32)
+    kv_a, _ = _paged_setup(rng, B, [max(t - 1, 1) for t in T_list], ps, max_seq)
+    kv_b, _ = _paged_setup(np.random.default_rng(sum(T_list) + n_splits), B, [max(t - 1, 1) for t in T_list], ps,
+                           max_seq)
+    qkv = _t(rng.normal(0, 1, (B, 2048)).astype(np.float16))
+    pos, seq_lens = _t(pos_np), _t(pos_np + 1)
+    inv = torch.from_numpy(rope_inv_freq(128, 1e6)).cuda()
+    ws = torch.zeros(max(16, K.attention_workspace_size(B, 12, 128, n_splits)), dtype=torch.uint8, device="cuda")
+    ka, va = kv_a.layer(0)
+    q = torch.empty(B, 1536, dtype=torch.float16, device="cuda")
+    K.rope_kv_append(qkv, pos, inv, q, ka, va, kv_a.block_table, ps, 12, 2, 128)
+    ref = torch.empty(B, 1536, dtype=torch.float16, device="cuda")
+    K.gqa_decode_attention(q, ka, va, kv_a.block_table, seq_lens, ref, ws, ps, 12, 2, 128, kv_a.max_seq_len, n_splits)
+    kb, vb = kv_b.layer(0)
+    got = torch.empty(B, 1536, dtype=torch.float16, device="cuda")
+    K.gqa_decode_attention_rope(qkv, pos, inv, kb, vb, kv_b.block_table, seq_lens, got, ws, ps, 12, 2, 128,
+                                kv_b.max_seq_len, n_splits)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+    assert torch.equal(kb.view(torch.int16), ka.view(torch.int16))
+    assert torch.equal(vb.view(torch.int16), va.view(torch.int16))
