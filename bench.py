@@ -31,6 +31,12 @@ sys.path.insert(0, ROOT)
 
 METRIC = "Qwen2.5-1.5B-Q4 decode tok/s (bs1, bs64); Q4 GEMV GB/s vs HBM peak"
 PROMPT_LEN = 32
+# DRAM bytes per algorithmic byte of the persistent decode kernel, from one
+# ncu capture of a 4-layer, one-step launch (`bench.py --layers 4 --steps 1`):
+# dram__bytes_read.sum + dram__bytes_write.sum = 236.9 MB + 4.7 MB against
+# 236.8 MB of algorithmic bytes.  Every layer's weights are read once, so the
+# ratio carries over to the 28-layer launch.
+PERSISTENT_TRAFFIC_PER_ALGO_BYTE = (236.9 + 4.7) / 236.8
 
 
 def _dist_env():
@@ -471,7 +477,11 @@ def run_ours(args):
     if eng.pdec is not None:
         roof = {"kernel": "decode_persistent_kernel<1> (one launch = all timed steps)", "bound": "hbm",
                 "achieved": round(step_gbs, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                "frac": round(step_gbs / peak, 4), "traffic": None,
+                "frac": round(step_gbs / peak, 4),
+                "traffic": int(step_bytes * PERSISTENT_TRAFFIC_PER_ALGO_BYTE * args.steps),
+                "traffic_unit": "DRAM bytes per launch",
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a 4-layer one-step "
+                                  "launch, scaled to this launch by its algorithmic bytes",
                 "bytes_per_step": int(step_bytes), "steps_per_launch": args.steps,
                 "us_per_step": round(t_max / args.steps * 1e6, 2)}
         gemv = None
