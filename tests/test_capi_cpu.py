@@ -84,3 +84,39 @@ def test_split_heuristic():
     assert L.lmps_gqa_attention_splits(16, 2, 1024, 64) == 16       # one tile per split
     assert L.lmps_gqa_attention_splits(128, 2, 4096, 64) == 2       # 256 items: two splits fit
     assert L.lmps_gqa_attention_splits(256, 2, 4096, 64) == 1       # 512 items fill the GPU
+
+
+def test_tensor_parallel_exchange_validation():
+    """Buffer size of the peer exchange and the checks of both exchange entry
+    points, all before any device work (fake, aligned addresses)."""
+    L = _lib.lib()
+    assert L.lmps_tp2_comm_bytes(56, 8 * 1536) == 56 * (2 * 8 * 1536 * 2 + 64 * 4)
+    assert L.lmps_tp2_comm_bytes(0, 8) == 0 and L.lmps_tp2_comm_bytes(1, 12) == 0
+    a = 1 << 20                                                   # 16-byte aligned, never dereferenced
+    ok = dict(part=a, x=a, n=1536, comm=a, peer=a, seen=a, site=0, n_sites=4, max_n=1536, err=a)
+
+    def ar(**kw):
+        v = {**ok, **kw}
+        return L.lmps_tp2_allreduce_residual(v["part"], v["x"], v["n"], v["comm"], v["peer"], v["seen"], v["site"],
+                                             v["n_sites"], v["max_n"], v["err"], None)
+    assert ar(peer=None) == -1
+    assert ar(site=4) == -1                                       # site outside n_sites
+    assert ar(n=1544, max_n=1536) == -1                           # more than a slot holds
+    assert ar(n=1537) == -1                                       # not a multiple of 8
+    assert ar(part=a + 8) == -1                                   # misaligned
+    # fused GEMV exchange: rows x batch beyond the slot, and a grid beyond 64 CTAs
+    g = L.lmps_gemv_q4_tp2_residual
+    assert g(a, a, a, 768, None, a, 1536, 768, 1, a, a, a, 0, 4, 1536, a, None) == -1
+    assert g(a, a, a, 768, a, a, 1536, 768, 2, a, a, a, 0, 4, 1536, a, None) == -1
+    assert g(a, a, a, 768, a, a, 4096, 768, 1, a, a, a, 0, 4, 4096, a, None) == -2   # 128 CTAs
+
+
+def test_attention_rope_validation():
+    L = _lib.lib()
+    a = 1 << 20
+    bad_style = L.lmps_gqa_decode_attention_rope(a, a, a, 5, a, a, a, a, a, None, 0, 1, 64, 12, 2, 128, 1, 64, 1,
+                                                 None)
+    assert bad_style == -1
+    no_pos = L.lmps_gqa_decode_attention_rope(a, None, a, 0, a, a, a, a, a, None, 0, 1, 64, 12, 2, 128, 1, 64, 1,
+                                              None)
+    assert no_pos == -1
