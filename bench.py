@@ -333,9 +333,18 @@ def extra_configs(mw, cfg, args, rank, world, dist, peak):
             B, P = 8, 2048
             prompt = torch.from_numpy(np.random.default_rng(3).integers(0, cfg.vocab, (B, P)))
             res = {}
+            # parity: greedy ids of every variant against the single-GPU engine
+            # on the same prompts (64-id prefix of each prompt, 12 new tokens)
+            n_new = 12
+            one = QwenEngine(weights=mw, device=torch.device("cuda"), max_batch=B, max_seq_len=P + 32,
+                             decoder="kernels")
+            ref_ids = one.generate_batch(prompt[:, :64].numpy(), n_new)
+            del one
+            parity = {}
             for comm, fuse in (("p2p", False), ("p2p", True), ("nccl", False)):
                 eng = TPEngine(mw, rank, world, device=torch.device("cuda"), max_batch=B, max_seq_len=P + 32,
                                comm=comm, fuse_exchange=fuse)
+                name = comm + ("_fused" if fuse else "")
                 try:
                     eng.reset(B)
                     eng.prefill(prompt, dense=True)  # warm-up
@@ -344,7 +353,13 @@ def extra_configs(mw, cfg, args, rank, world, dist, peak):
                     eng.decode_steps(2, record=False)  # graph capture outside the timed region
                     td = _timed(lambda: eng.decode_steps(16, record=False), world, dist)
                     eng.check_comm()
-                    res[comm + ("_fused" if fuse else "")] = (t, td)
+                    res[name] = (t, td)
+                    ids = eng.generate_batch(prompt[:, :64].numpy(), n_new)
+                    eng.check_comm()
+                    # ids up to each sequence's first difference (after it the sequences differ)
+                    same = [int(np.argmax(np.append(ids[b] != ref_ids[b], True))) for b in range(B)]
+                    parity[name] = {"sequences_identical": sum(x == n_new for x in same), "sequences": B,
+                                    "first_difference_steps": [x for x in same if x < n_new]}
                 finally:
                     eng.close()
                 del eng
@@ -354,6 +369,9 @@ def extra_configs(mw, cfg, args, rank, world, dist, peak):
                 "decode_after_prefill_tok_s": round(B * 16 / td, 1),
                 "decode_fused_gemv_exchange_tok_s": round(B * 16 / res["p2p_fused"][1], 1),
                 "decode_nccl_tok_s": round(B * 16 / res["nccl"][1], 1),
+                "tp_parity": all(v["sequences_identical"] == B for v in parity.values()),
+                "tp_parity_detail": {"against": "greedy ids of the single-GPU engine, same weights and prompts "
+                                                "(8 x 64-id prompts, 12 new tokens)", **parity},
                 "path": "tp2: KV head r and its query heads on rank r; dense GEMM prefill with NCCL "
                         "all-reduces (sum, fp16) after o_proj and down_proj, then bs8 decode as a CUDA graph "
                         "with the all-reduces over peer memory (NVLink stores + flags, fused with the "
@@ -386,6 +404,99 @@ def extra_configs(mw, cfg, args, rank, world, dist, peak):
         except Exception as e:
             out["c4_long_context"] = {"error": repr(e)[:200]}
     return out
+
+
+# -- per-kernel timing tables (the commands behind the profiles/ summaries) --
+GEMM_SHAPES = [(16384, 2048, 1536), (16384, 8960, 1536), (16384, 1536, 8960), (16384, 1536, 1536),
+               (64, 2048, 1536), (64, 8960, 1536), (64, 1536, 8960), (64, 151936, 1536)]
+ATTN_SHAPES = [(64, 400, 416), (64, 1000, 1024), (8, 2100, 2144), (4, 300, 320), (16, 1000, 1024), (64, 140, 155)]
+
+
+def time_gemm(m: int, n: int, k: int, iters: int = 20, warmup: int = 3) -> dict:
+    """The tcgen05 W4A16 GEMM alone: random Q4 weights, fp16 activations,
+    CUDA events around ``iters`` back-to-back calls."""
+    import torch
+    from llamamps_b200 import kernels as K
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(m, k, dtype=torch.float16, device="cuda", generator=g)
+    pk = torch.randint(0, 256, (n * k // 2,), dtype=torch.uint8, device="cuda", generator=g)
+    sc = (torch.rand(n * k // 32, device="cuda", generator=g) * 0.01).half()
+    y = torch.empty(m, n, dtype=torch.float16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    wsb = K.w4a16_gemm_workspace_size(m, n)
+    ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda") if m <= 128 and wsb < (1 << 28) else None
+    for _ in range(warmup):
+        K.w4a16_gemm(x, pk, sc, n, k, out=y, error=err, workspace=ws)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        K.w4a16_gemm(x, pk, sc, n, k, out=y, error=err, workspace=ws)
+    b.record()
+    torch.cuda.synchronize()
+    t = a.elapsed_time(b) / iters / 1e3
+    return {"kernel": "w4a16_gemm", "m": m, "n": n, "k": k, "us": round(t * 1e6, 2),
+            "tflops": round(2.0 * m * n * k / t / 1e12, 1),
+            "weight_gbs": round((n * k / 2 + n * k / 16) / t / 1e9, 1), "split_k": ws is not None,
+            "error": int(err.item())}
+
+
+def time_attention(B: int, T: int, maxlen: int, calls: int = 20) -> dict:
+    """The split-KV decode attention (attention + combine) over a paged fp16
+    cache of ``maxlen`` positions, ``T`` attended, for a range of split
+    counts: a CUDA graph of ``calls`` calls, us per call; ``auto`` is the
+    count lmps_gqa_attention_splits picks."""
+    import torch
+    from llamamps_b200 import kernels as K
+    hq, hkv, hd, page = 12, 2, 128, 64
+    dev = torch.device("cuda")
+    pages = (maxlen + page - 1) // page
+    g = torch.Generator(device=dev).manual_seed(1)
+    kp = torch.randn(B * pages, hkv, page, hd, generator=g, device=dev).half()
+    vp = torch.randn(B * pages, hkv, page, hd, generator=g, device=dev).half()
+    bt = torch.randperm(B * pages, generator=g, device=dev).to(torch.int32).reshape(B, pages)
+    q = torch.randn(B, hq * hd, generator=g, device=dev).half()
+    lens = torch.full((B,), min(T, maxlen), dtype=torch.int32, device=dev)
+    auto = K.attention_splits(B, hkv, maxlen, page)
+    tiles = (maxlen + 63) // 64
+    us = {}
+    for sp in sorted({1, 2, 3, 4, 6, 8, 12, 16, 24, 32, auto}):
+        if sp > tiles:
+            continue
+        ws = torch.zeros(max(K.attention_workspace_size(B, hq, hd, sp), 16), dtype=torch.uint8, device=dev)
+        out = torch.empty_like(q)
+
+        def call():
+            K.gqa_decode_attention(q, kp, vp, bt, lens, out, ws, page, hq, hkv, hd, maxlen, sp)
+        for _ in range(3):
+            call()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(calls):
+                call()
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us[sp] = round(e0.elapsed_time(e1) / calls * 1e3, 2)
+    return {"kernel": "gqa_decode_attention", "batch": B, "attended": T, "cache": maxlen, "auto_splits": auto,
+            "us_by_splits": us}
+
+
+def run_kernel_timing(args) -> int:
+    """--time gemm|attention: one JSON line per shape (not a benchmark line)."""
+    if args.time == "gemm":
+        shapes = [tuple(int(v) for v in s.split(",")) for s in args.shape] if args.shape else GEMM_SHAPES
+        for m, n, k in shapes:
+            print(json.dumps(time_gemm(m, n, k, args.iters, args.warmup)))
+    else:
+        shapes = [tuple(int(v) for v in s.split(",")) for s in args.shape] if args.shape else ATTN_SHAPES
+        for b, t, c in shapes:
+            print(json.dumps(time_attention(b, t, c)))
+    return 0
 
 
 def run_ours(args):
@@ -546,7 +657,14 @@ def main():
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling only: build a model with fewer decoder layers (the JSON line "
                          "then names the reduced workload and is not a measurement of it)")
+    ap.add_argument("--time", choices=["gemm", "attention"], default=None,
+                    help="kernel timing tables instead of the benchmark: the tcgen05 W4A16 GEMM or the "
+                         "split-KV decode attention, per --shape (m,n,k or batch,attended,cache)")
+    ap.add_argument("--shape", action="append", default=None, help="shape for --time (repeatable)")
+    ap.add_argument("--iters", type=int, default=20, help="calls per timing for --time gemm")
     args = ap.parse_args()
+    if args.time is not None:
+        return run_kernel_timing(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

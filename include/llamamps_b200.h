@@ -12,7 +12,7 @@
  *   - no entry point allocates device memory: scratch is passed in, with a
  *     *_workspace_size() query beside the call that needs it.
  *
- * Weight format (utils/pack_weights.py:42-60): a [rows, k] matrix is packed
+ * Weight format (utils/pack_weights.py:18-46): a [rows, k] matrix is packed
  * row-major as uint8[rows*k/2] (element 2b in the low nibble of byte b, 2b+1
  * in the high nibble, code+8) plus fp16 scales[rows*k/32] (one per 32
  * consecutive elements, code = round(w / scale), scale = max|w| / 7).
@@ -254,13 +254,15 @@ size_t lmps_tp2_comm_bytes(int n_sites, int max_n);
  * peer's, mapped; seen = this rank's private uint32 [n_sites * 64] call
  * counters (zeroed with the buffers).  Both ranks must make the same calls
  * (site, n) in the same order; calls on one site may follow each other
- * directly.  A wait for the peer that runs out (5 s) sets *error and leaves
- * x unchanged, and later calls return at once while *error is set; the
- * buffers and counters of both ranks must then be zeroed again.  The grid
- * is at most 64 CTAs, all resident at once. */
+ * directly, with any n <= max_n.  A wait for the peer that runs out
+ * (wait_ns nanoseconds of the GPU's global timer; 0 = 5 s) sets *error and
+ * leaves x unchanged, and later calls return at once while *error is set;
+ * the buffers and counters of both ranks must then be zeroed again.  The
+ * grid is ceil(max_n / 2048) CTAs, at most 64, all resident at once; it
+ * depends on max_n only, so every CTA takes part in every call of a site. */
 int lmps_tp2_allreduce_residual(const uint16_t* part, uint16_t* x, int n, void* comm, void* peer_comm,
                                 uint32_t* seen, int site, int n_sites, int max_n, int32_t* error,
-                                void* stream);
+                                unsigned long long wait_ns, void* stream);
 
 /* The split o_proj / down_proj GEMV and its all-reduce in ONE kernel
  * (kernels/quant_matmul.metal:15-69 on this rank's K slice, then
@@ -269,17 +271,18 @@ int lmps_tp2_allreduce_residual(const uint16_t* part, uint16_t* x, int n, void* 
  * receive slot; after a hand-off between the same CTA on both GPUs,
  * x[b, r] <- x[b, r] + (part[b, r] + peer's part[b, r]).  x and part are
  * [batch, rows] contiguous, batch * rows <= max_n; same exchange buffers,
- * counters, call rules and error behaviour as lmps_tp2_allreduce_residual
- * (use other sites than it).  LMPS_ERR_UNSUPPORTED when the GEMV grid would
+ * counters, call rules, wait limit and error behaviour as
+ * lmps_tp2_allreduce_residual (use other sites than it; the grid depends on
+ * rows only).  LMPS_ERR_UNSUPPORTED when the GEMV grid would
  * exceed 64 CTAs. */
 int lmps_gemv_q4_tp2_residual(const uint8_t* packed, const uint16_t* scales, const uint16_t* a, int lda,
                               uint16_t* x, uint16_t* part, int rows, int k, int batch, void* comm,
                               void* peer_comm, uint32_t* seen, int site, int n_sites, int max_n,
-                              int32_t* error, void* stream);
+                              int32_t* error, unsigned long long wait_ns, void* stream);
 
 /* ---- weight format ---------------------------------------------------- */
 
-/* Device Q4 packer, bit-exact with utils/pack_weights.py:42-60
+/* Device Q4 packer, bit-exact with utils/pack_weights.py:18-46
  * `pack_tensor_4bit`: w is fp32[n]; packed receives ceil(n/32)*16 bytes and
  * scales ceil(n/32) fp16 values (the tail group is zero-padded). */
 int lmps_q4_pack(const float* w, long long n, uint8_t* packed, uint16_t* scales, void* stream);

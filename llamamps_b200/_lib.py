@@ -58,9 +58,10 @@ _SIGS = {
     "lmps_ipc_open": (c_int, [c_vp, ctypes.POINTER(c_vp)]),
     "lmps_ipc_close": (c_int, [c_vp]),
     "lmps_tp2_comm_bytes": (c_size, [c_int, c_int]),
-    "lmps_tp2_allreduce_residual": (c_int, [c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp]),
+    "lmps_tp2_allreduce_residual": (c_int, [c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp,
+                                            ctypes.c_ulonglong, c_vp]),
     "lmps_gemv_q4_tp2_residual": (c_int, [c_vp, c_vp, c_vp, c_int, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp,
-                                          c_vp, c_int, c_int, c_int, c_vp, c_vp]),
+                                          c_vp, c_int, c_int, c_int, c_vp, ctypes.c_ulonglong, c_vp]),
     "lmps_argmax_rows": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_vp]),
     "lmps_w4a16_gemm_workspace_size": (c_size, [c_int, c_int]),
     "lmps_w4a16_gemm": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_vp, c_int, c_int, c_int, c_int,

@@ -368,14 +368,9 @@ static int attention_launch(AttnParams P, const uint16_t* k_pool, const uint16_t
     P.part_o = reinterpret_cast<float*>(workspace);
     P.part_ml = reinterpret_cast<float2*>(reinterpret_cast<char*>(workspace) + rows * head_dim * sizeof(float));
   }
-  static bool configured = false;
   const size_t smem = sizeof(AttnSmem);
-  if (!configured) {
-    if (cudaFuncSetAttribute(gqa_decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
-      return lmps_launch_status();
-    configured = true;
-  }
+  const int st_attr = lmps_max_dyn_smem<gqa_decode_attn_kernel>(static_cast<int>(smem));
+  if (st_attr != LMPS_OK) return st_attr;
   cudaStream_t st = lmps_stream(stream);
   dim3 grid(n_splits, n_kv_heads, batch);
   int status = lmps_launch_pdl(gqa_decode_attn_kernel, grid, dim3(kAttnThreads), smem, st, P);

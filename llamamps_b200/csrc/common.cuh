@@ -50,6 +50,30 @@ static inline bool lmps_aligned(const void* p, uintptr_t a) {
   return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
 }
 
+// Opt a kernel into `bytes` of dynamic shared memory on the current device.
+// The attribute belongs to the kernel in one device's context, so it is set
+// once per (kernel, device): a process that drives several GPUs sets it on
+// each of them before that device's first launch above 48 KB.  `Kern` is the
+// kernel itself (one flag table per kernel, not per signature).
+template <auto Kern>
+static inline int lmps_max_dyn_smem(int bytes) {
+  constexpr int kMaxDevices = 64;
+  static int done[kMaxDevices] = {};  // largest size set so far, per device
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (dev >= 0 && dev < kMaxDevices && __atomic_load_n(&done[dev], __ATOMIC_ACQUIRE) >= bytes) return LMPS_OK;
+  e = cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (dev >= 0 && dev < kMaxDevices) {
+    int cur = __atomic_load_n(&done[dev], __ATOMIC_ACQUIRE);
+    while (cur < bytes && !__atomic_compare_exchange_n(&done[dev], &cur, bytes, false, __ATOMIC_ACQ_REL,
+                                                        __ATOMIC_ACQUIRE)) {
+    }
+  }
+  return LMPS_OK;
+}
+
 namespace lmps {
 
 constexpr int kWarp = 32;
@@ -183,16 +207,18 @@ __device__ __forceinline__ unsigned long long lmps_globaltimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+// Default limit of the peer wait (wait_ns = 0): the host-side skew between
+// two ranks that make the same calls stays far below it.
+constexpr unsigned long long kTp2DefaultWaitNs = 5000000000ull;
 // Thread 0 of a CTA: publish `want` to the peer's flag `cta`, then wait
-// (bounded) until this rank's flag `cta` reaches it.  False after a timeout
-// (error raised).
+// (bounded by wait_ns of %globaltimer) until this rank's flag `cta` reaches
+// it.  False after a timeout (error raised).
 __device__ __forceinline__ bool lmps_tp2_handshake(uint32_t* peer_flags, const uint32_t* flags, int cta,
-                                                   uint32_t want, int32_t* error) {
-  constexpr unsigned long long kTimeoutNs = 5000000000ull;  // host-side skew between the ranks stays far below
+                                                   uint32_t want, int32_t* error, unsigned long long wait_ns) {
   lmps_st_release_sys(peer_flags + cta, want);
   const unsigned long long t0 = lmps_globaltimer();
   while (static_cast<int>(lmps_ld_acquire_sys(flags + cta) - want) < 0) {
-    if (lmps_globaltimer() - t0 > kTimeoutNs) {
+    if (lmps_globaltimer() - t0 > wait_ns) {
       atomicExch(error, 1);
       return false;
     }

@@ -184,7 +184,7 @@ __global__ void attn_weighted_sum_kernel(const float* scores, const __half* v_ca
 }
 
 // ---------------------------------------------------------------------------
-// Device Q4 packer -- utils/pack_weights.py:42-60: one thread per group of 32.
+// Device Q4 packer -- utils/pack_weights.py:18-46: one thread per group of 32.
 // scale = max|w| / 7 (IEEE division), 0 -> 1; code = rint(w / scale) (ties to
 // even, like torch.round) clamped to [-8, 7]; nibble = code + 8; byte b =
 // nib[2b] | nib[2b+1] << 4; scale stored fp16 (round to nearest even).

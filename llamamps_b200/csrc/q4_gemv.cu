@@ -49,6 +49,7 @@ struct GemvParams {
   uint32_t* tp_seen;            // this rank's call counts of the site, per CTA
   int32_t* tp_error;
   int tp_slot;                  // elements per receive slot
+  unsigned long long tp_wait_ns;  // limit of the peer wait
 };
 
 constexpr int kGemvThreads = 256;
@@ -245,7 +246,7 @@ __global__ void __launch_bounds__(kGemvThreads) q4_gemv_kernel(const GemvParams 
     __syncthreads();
     bool good = false;
     if (threadIdx.x == 0) {
-      good = lmps_tp2_handshake(p.tp_peer_flags, p.tp_flags, blockIdx.x, tp_want, p.tp_error);
+      good = lmps_tp2_handshake(p.tp_peer_flags, p.tp_flags, blockIdx.x, tp_want, p.tp_error, p.tp_wait_ns);
       if (good) p.tp_seen[blockIdx.x] = tp_want;
     }
     if (!__syncthreads_or(good)) return;
@@ -289,13 +290,8 @@ static int launch_lpr_nb(const GemvParams& p, cudaStream_t st) {
   const size_t smem = static_cast<size_t>(NB) * ((p.k / 8 + 7) & ~7) * 16;
   auto kern = q4_gemv_kernel<LPR, NB, EPI>;
   if (smem > 48 * 1024) {
-    static bool configured = false;  // per instantiation
-    if (!configured) {
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
-          cudaSuccess)
-        return lmps_launch_status();
-      configured = true;
-    }
+    const int st_attr = lmps_max_dyn_smem<q4_gemv_kernel<LPR, NB, EPI>>(227 * 1024);
+    if (st_attr != LMPS_OK) return st_attr;
   }
   constexpr int rows_per_cta = kGemvWarps * (kWarp / LPR);
   long long blocks = (p.rows + rows_per_cta - 1) / rows_per_cta;
@@ -387,7 +383,7 @@ extern "C" int lmps_gemv_q4_residual(const uint8_t* packed, const uint16_t* scal
 extern "C" int lmps_gemv_q4_tp2_residual(const uint8_t* packed, const uint16_t* scales, const uint16_t* a,
                                          int lda, uint16_t* x, uint16_t* part, int rows, int k, int batch,
                                          void* comm, void* peer_comm, uint32_t* seen, int site, int n_sites,
-                                         int max_n, int32_t* error, void* stream) {
+                                         int max_n, int32_t* error, unsigned long long wait_ns, void* stream) {
   int st = check_common(packed, scales, a, lda, rows, k, batch);
   if (st) return st;
   LMPS_CHECK_ARG(x && part && comm && peer_comm && seen && error);
@@ -410,6 +406,7 @@ extern "C" int lmps_gemv_q4_tp2_residual(const uint8_t* packed, const uint16_t* 
   p.tp_seen = seen + site * kTp2MaxCtas;
   p.tp_error = error;
   p.tp_slot = max_n;
+  p.tp_wait_ns = wait_ns ? wait_ns : kTp2DefaultWaitNs;
   return launch_gemv<EPI_TP2>(p, lmps_stream(stream));
 }
 

@@ -51,7 +51,7 @@ __device__ __forceinline__ uint32_t hadd2u(uint32_t a, uint32_t b) {
 __global__ void __launch_bounds__(kThreads)
     allreduce_residual_kernel(const uint4* __restrict__ part, uint4* __restrict__ x, int n8, int slot8,
                               uint4* peer_recv, const uint4* recv, uint32_t* peer_flags, const uint32_t* flags,
-                              uint32_t* seen, int32_t* error) {
+                              uint32_t* seen, int32_t* error, unsigned long long wait_ns) {
   __shared__ int ok;
   // an earlier exchange failed (the pair is out of step): the whole CTA
   // leaves, on one reading of the flag
@@ -66,7 +66,7 @@ __global__ void __launch_bounds__(kThreads)
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
-    const bool good = lmps_tp2_handshake(peer_flags, flags, blockIdx.x, want, error);
+    const bool good = lmps_tp2_handshake(peer_flags, flags, blockIdx.x, want, error, wait_ns);
     if (good) seen[blockIdx.x] = want;
     ok = good ? 1 : 0;
   }
@@ -133,7 +133,7 @@ extern "C" size_t lmps_tp2_comm_bytes(int n_sites, int max_n) {
 
 extern "C" int lmps_tp2_allreduce_residual(const uint16_t* part, uint16_t* x, int n, void* comm, void* peer_comm,
                                            uint32_t* seen, int site, int n_sites, int max_n, int32_t* error,
-                                           void* stream) {
+                                           unsigned long long wait_ns, void* stream) {
   LMPS_CHECK_ARG(part && x && comm && peer_comm && seen && error);
   LMPS_CHECK_ARG(n_sites >= 1 && site >= 0 && site < n_sites && max_n >= 8 && max_n % 8 == 0);
   LMPS_CHECK_ARG(n >= 8 && n % 8 == 0 && n <= max_n);
@@ -141,12 +141,17 @@ extern "C" int lmps_tp2_allreduce_residual(const uint16_t* part, uint16_t* x, in
                  lmps_aligned(peer_comm, 16) && lmps_aligned(seen, 4));
   const Tp2Site t = lmps_tp2_site(comm, peer_comm, site, n_sites, max_n);
   const int n8 = n / 8;
-  // one CTA per 2048 elements, at most kMaxCtas: every CTA of the grid is
-  // resident at once, so each one's counterpart on the peer GPU runs too
-  const int grid = std::min(tp::kMaxCtas, (n8 + tp::kThreads - 1) / tp::kThreads);
+  // One CTA per 2048 elements of the site's largest call, at most kMaxCtas:
+  // every CTA of the grid is resident at once, so each one's counterpart on
+  // the peer GPU runs too.  The grid depends on max_n only, never on n: every
+  // CTA of a site takes part in every call of that site (a CTA whose slice is
+  // empty still hands off), so the per-CTA call counts -- and with them the
+  // receive slot each call uses -- stay equal across the CTAs of the site
+  // whatever sizes successive calls have.
+  const int grid = std::min(tp::kMaxCtas, (max_n / 8 + tp::kThreads - 1) / tp::kThreads);
   tp::allreduce_residual_kernel<<<grid, tp::kThreads, 0, lmps_stream(stream)>>>(
       reinterpret_cast<const uint4*>(part), reinterpret_cast<uint4*>(x), n8, max_n / 8,
       reinterpret_cast<uint4*>(t.peer_recv), reinterpret_cast<const uint4*>(t.recv), t.peer_flags, t.flags,
-      seen + site * tp::kMaxCtas, error);
+      seen + site * tp::kMaxCtas, error, wait_ns ? wait_ns : kTp2DefaultWaitNs);
   return lmps_launch_status();
 }

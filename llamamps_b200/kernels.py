@@ -280,9 +280,11 @@ class PeerExchange:
     unmaps and frees; call it on both ranks after a barrier, with no call in
     flight on either GPU."""
 
-    def __init__(self, n_sites: int, max_n: int, device):
+    def __init__(self, n_sites: int, max_n: int, device, wait_ns: int = 0):
         import ctypes
         self.n_sites, self.max_n, self.device = n_sites, max_n, torch.device(device)
+        # limit of every wait for the peer, in GPU global-timer nanoseconds (0: 5 s)
+        self.wait_ns = int(wait_ns)
         nbytes = lib().lmps_tp2_comm_bytes(n_sites, max_n)
         if nbytes == 0:
             raise ValueError("max_n must be a positive multiple of 8")
@@ -320,12 +322,13 @@ class PeerExchange:
 
 
 def tp2_allreduce_residual(part, x, ex: PeerExchange, site: int, error):
-    """x <- x + (part + the peer's part) through the peer's mapped buffer."""
+    """x <- x + (part + the peer's part) through the peer's mapped buffer.
+    A wait for the peer longer than ``ex.wait_ns`` sets ``error``."""
     if ex.peer is None:
         raise RuntimeError("the peer exchange is not connected")
     call("lmps_tp2_allreduce_residual", _dev(part, "part", FP16), _dev(x, "x", FP16), part.numel(), ex.comm,
          ex.peer, _dev(ex.seen, "seen", torch.int32), site, ex.n_sites, ex.max_n,
-         _dev(error, "error", torch.int32), _stream())
+         _dev(error, "error", torch.int32), ex.wait_ns, _stream())
     return x
 
 
@@ -339,6 +342,6 @@ def gemv_q4_tp2_residual(packed, scales, a, rows: int, k: int, x, part, ex: Peer
     call("lmps_gemv_q4_tp2_residual", _dev(packed, "packed", torch.uint8), _dev(scales, "scales", FP16),
          _dev(a2, "a", FP16), a2.shape[1], _dev(x, "x", FP16), _dev(part, "part", FP16), rows, k, B, ex.comm,
          ex.peer, _dev(ex.seen, "seen", torch.int32), site, ex.n_sites, ex.max_n,
-         _dev(error, "error", torch.int32), _stream())
+         _dev(error, "error", torch.int32), ex.wait_ns, _stream())
     return x
 

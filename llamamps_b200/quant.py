@@ -1,6 +1,6 @@
 """Q4 weight format (utils/pack_weights.py) -- packing on the host or device.
 
-Format (utils/pack_weights.py:42-60): the tensor is flattened row-major,
+Format (utils/pack_weights.py:18-46): the tensor is flattened row-major,
 zero-padded to a multiple of 32, and split into groups of 32; scale =
 max|w|/7 in fp32 (0 -> 1.0); code = round-half-even(w/scale) clamped to
 [-8, 7]; nibble = code + 8; byte b = nib[2b] | nib[2b+1] << 4; scales are

@@ -72,14 +72,14 @@ class OracleConfig:
 # --------------------------------------------------------------------------
 
 def q4_pack(w: np.ndarray):
-    """Symmetric int4 quantisation, utils/pack_weights.py:42-60.
+    """Symmetric int4 quantisation, utils/pack_weights.py:18-46.
 
-    The tensor is flattened row-major (``:42``), zero-padded to a multiple of
-    32 (``:43-44``), split into groups of 32 (``:46``); scale = max|w|/7 in
-    fp32 with 0 replaced by 1.0 (``:49-50``); code = round-half-even(w/scale)
-    clamped to [-8, 7] (``:53``); stored +8 as a nibble (``:56``), element 2b
-    in the low nibble of byte b and 2b+1 in the high nibble (``:58-60``); the
-    scale is saved as fp16 (``:70``).
+    The tensor is flattened row-major and zero-padded to a multiple of 32
+    (``:18-20``), split into groups of 32 (``:22``); scale = max|w|/7 in fp32
+    with 0 replaced by 1.0 (``:25-26``); code = round-half-even(w/scale)
+    clamped to [-8, 7] (``:29``); stored +8 as a nibble (``:32``), element 2b
+    in the low nibble of byte b and 2b+1 in the high nibble (``:34-36``); the
+    scale is saved as fp16 (``:46``).
     Returns (packed uint8[n_pad/2], scales float16[n_pad/32]).
     """
     flat = np.asarray(w, dtype=F32).reshape(-1)
@@ -398,4 +398,72 @@ class OracleModel:
             out.append(nxt)
             if i + 1 < max_new_tokens:
                 logits = self.step_token(nxt)
+        return out
+
+
+class OracleBatch:
+    """``batch`` independent sequences stepped together: row b is exactly the
+    computation of :class:`OracleModel` on sequence b alone (every stage is
+    row-wise; runners/engine.py:157-181 per row), but the Q4 projections of all
+    rows run as one matrix product per matrix, so full-shape batches (64
+    sequences, 128-id prompts) stay affordable on the host.  Each sequence has
+    its own KV cache and position."""
+
+    def __init__(self, weights: dict, cfg: OracleConfig, batch: int):
+        self.w = weights
+        self.cfg = cfg
+        self.batch = batch
+        self.dq = DequantCache()
+        self.caches = [KVCache(len(weights["layers"]), cfg.kv_dim) for _ in range(batch)]
+        self.pos = np.zeros(batch, dtype=np.int64)
+
+    def _layer(self, x: np.ndarray, lw: dict, li: int) -> np.ndarray:
+        cfg, D, hd, dq = self.cfg, self.cfg.hidden, self.cfg.head_dim, self.dq
+        xn = rms_norm(x, lw["in_norm"], cfg.eps)                       # engine.py:188-190
+        accq = _gemv_acc(lw, "q", xn, cfg.q_dim, D, dq)                # engine.py:192-195
+        acck = _gemv_acc(lw, "k", xn, cfg.kv_dim, D, dq)
+        accv = _gemv_acc(lw, "v", xn, cfg.kv_dim, D, dq)
+        q = add_bias(accq.astype(F16), accq, lw.get("bq"))
+        k = add_bias(acck.astype(F16), acck, lw.get("bk"))
+        v = add_bias(accv.astype(F16), accv, lw.get("bv"))
+        q = rope(q, self.pos, hd, cfg.rope_theta, cfg.rope_style)     # engine.py:198-200
+        k = rope(k, self.pos, hd, cfg.rope_theta, cfg.rope_style)
+        attn = np.empty((self.batch, cfg.q_dim), dtype=F16)
+        for b, cache in enumerate(self.caches):                        # engine.py:202-212
+            cache.append(li, int(self.pos[b]), k[b], v[b])
+            kc, vc = cache.rows(li)
+            p = softmax(attention_scores(q[b], kc, cfg.n_q_heads, cfg.n_kv_heads, hd))
+            attn[b] = attn_weighted_sum(p, vc, cfg.n_q_heads, cfg.n_kv_heads, hd)
+        o = _gemv_acc(lw, "o", attn, D, cfg.q_dim, dq).astype(F16)    # engine.py:215-221
+        x1 = residual_add(x, o)
+        hn = rms_norm(x1, lw["post_norm"], cfg.eps)                    # engine.py:224-235
+        g = _gemv_acc(lw, "gt", hn, cfg.intermediate, D, dq).astype(F16)
+        u = _gemv_acc(lw, "up", hn, cfg.intermediate, D, dq).astype(F16)
+        a = swiglu(g, u)
+        d = _gemv_acc(lw, "dn", a, D, cfg.intermediate, dq).astype(F16)  # engine.py:237-243
+        return residual_add(x1, d)
+
+    def step_tokens(self, ids) -> np.ndarray:
+        """One token per sequence at its current position -> fp16 logits [batch, V]."""
+        x = np.stack([embed_row(self.w["embed"], int(t), self.cfg.hidden) for t in ids])
+        for li, lw in enumerate(self.w["layers"]):
+            x = self._layer(x, lw, li)
+        self.pos += 1
+        return final_logits(x, self.w["final_norm"], self.w["lm_packed"], self.w["lm_scales"], self.cfg, self.dq)
+
+    def generate(self, prompts, max_new_tokens: int, record: Optional[list] = None) -> np.ndarray:
+        """Greedy loop of every row (prompts int [batch, P]); returns int [batch, max_new_tokens].
+        ``record`` receives the logits [batch, V] behind each generated column."""
+        prompts = np.asarray(prompts)
+        logits = None
+        for t in range(prompts.shape[1]):
+            logits = self.step_tokens(prompts[:, t])
+        out = np.zeros((self.batch, max_new_tokens), dtype=np.int64)
+        for i in range(max_new_tokens):
+            nxt = [predict_next_token(logits[b]) for b in range(self.batch)]
+            if record is not None:
+                record.append(logits)
+            out[:, i] = nxt
+            if i + 1 < max_new_tokens:
+                logits = self.step_tokens(nxt)
         return out

@@ -1,9 +1,9 @@
 """Generate the golden fixtures that pin the oracle to the reference itself.
 
-Run in a container that has the LlamaMPS sources (read-only) at
-``$LLAMAMPS_REF`` (default ``/root/reference``):
+Run where a checkout of the LlamaMPS sources is available (it is only read),
+giving its path as the argument or in ``$LLAMAMPS_REF``:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <path to the LlamaMPS checkout>
 
 It imports the reference's own Python functions and records their outputs on
 seeded inputs:
@@ -16,8 +16,18 @@ seeded inputs:
   one cached position.
 * ``utils/verify_swiglu.py::verify_swiglu`` -- SiLU(gate) * up, fp16 out.
 
-Outputs (small .npz files, committed): ``pack_cases.npz``, ``verify_cases.npz``.
-Nothing at test time reads the reference; the tests read these files.
+* ``scripts/extract_all.py`` with ``extract_layernorm``, ``extract_attn``,
+  ``extract_post_norm``, ``extract_mlp``, ``copy_layer_weights`` and
+  ``scripts/extract_global.py::extract_tied_weights`` -- the checkpoint
+  converter that writes the flat-.bin layout the engine loads.  They run
+  from a temporary copy of ``scripts/`` and ``utils/pack_weights.py`` (they
+  read and write ``<project>/weights``) on a small seeded Qwen2-named
+  checkpoint (``llamamps_b200.convert.write_synthetic_checkpoint``), and the
+  sha256 of every file they write is recorded.
+
+Outputs (small files, committed): ``pack_cases.npz``, ``verify_cases.npz``,
+``reference_layout.json``.  Nothing at test time reads the reference; the
+tests read these files.
 """
 from __future__ import annotations
 
@@ -30,7 +40,7 @@ import tempfile
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("LLAMAMPS_REF", "/root/reference")
+REF = ""  # the LlamaMPS checkout, set in __main__ from argv[1] or $LLAMAMPS_REF
 
 
 def _load_module(path: str, name: str):
@@ -104,8 +114,72 @@ def verify_cases():
     print("verify cases written")
 
 
+# The checkpoint of the layout case: small enough to convert in seconds, the
+# smallest shape the persistent decode kernel takes (hidden a multiple of 512,
+# head_dim 128).
+LAYOUT_CASE = {"hidden": 512, "intermediate": 512, "vocab": 1024, "n_layers": 2, "n_q_heads": 4,
+               "n_kv_heads": 2, "head_dim": 128, "seed": 11}
+
+
+def layout_case_config():
+    from llamamps_b200.config import ModelConfig
+    c = {k: v for k, v in LAYOUT_CASE.items() if k != "seed"}
+    return ModelConfig(**c)
+
+
+def reference_layout_case():
+    """Run the reference's extraction scripts on the seeded checkpoint and
+    record the sha256 of every file they write."""
+    import hashlib
+    import json
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    from llamamps_b200.convert import write_synthetic_checkpoint
+    cfg = layout_case_config()
+    tmp = tempfile.mkdtemp(prefix="lmps_layout_")
+    saved_path = list(sys.path)
+    try:
+        os.makedirs(os.path.join(tmp, "utils"))
+        os.makedirs(os.path.join(tmp, "scripts"))
+        os.makedirs(os.path.join(tmp, "weights"))
+        shutil.copy(os.path.join(REF, "utils", "pack_weights.py"), os.path.join(tmp, "utils"))
+        for f in ("extract_all.py", "extract_attn.py", "extract_mlp.py", "extract_layernorm.py",
+                  "extract_postnorm.py", "extract_global.py"):
+            shutil.copy(os.path.join(REF, "scripts", f), os.path.join(tmp, "scripts"))
+        model = os.path.join(tmp, "weights", "model.safetensors")
+        write_synthetic_checkpoint(model, cfg, LAYOUT_CASE["seed"])
+        for m in [m for m in sys.modules if m == "utils" or m.startswith(("utils.", "scripts"))]:
+            del sys.modules[m]
+        sys.path.insert(0, tmp)
+        ext_all = _load_module(os.path.join(tmp, "scripts", "extract_all.py"), "ref_extract_all")
+        ext_glob = _load_module(os.path.join(tmp, "scripts", "extract_global.py"), "ref_extract_global")
+        for layer in range(cfg.n_layers):      # extract_all.py:53-60
+            ext_all.extract_layernorm(layer)
+            ext_all.extract_attn(layer)
+            ext_all.extract_post_norm(layer)
+            ext_all.extract_mlp(layer)
+            ext_all.copy_layer_weights(layer)
+        ext_glob.extract_tied_weights(model, os.path.join(tmp, "weights", "global"))
+        files = {}
+        root = os.path.join(tmp, "weights")
+        for dirpath, _, names in os.walk(root):
+            for n in names:
+                path = os.path.join(dirpath, n)
+                if path == model:
+                    continue
+                with open(path, "rb") as f:
+                    files[os.path.relpath(path, root)] = hashlib.sha256(f.read()).hexdigest()
+        with open(os.path.join(HERE, "reference_layout.json"), "w") as f:
+            json.dump({"case": LAYOUT_CASE, "files": dict(sorted(files.items()))}, f, indent=1)
+        print("reference layout case:", len(files), "files")
+    finally:
+        sys.path[:] = saved_path
+        shutil.rmtree(tmp)
+
+
 if __name__ == "__main__":
-    if not os.path.isdir(REF):
-        sys.exit(f"reference sources not found at {REF}")
+    REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LLAMAMPS_REF", "")
+    if not REF or not os.path.isdir(REF):
+        sys.exit("usage: make_golden.py <path to the LlamaMPS checkout> (or set LLAMAMPS_REF)")
     pack_cases()
     verify_cases()
+    reference_layout_case()

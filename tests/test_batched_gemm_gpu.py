@@ -9,7 +9,7 @@ import pytest
 import torch
 
 from oracle import mirror as M
-from tests._util import greedy_ids_match
+from tests._util import assert_close, greedy_ids_match
 
 pytestmark = pytest.mark.gpu
 
@@ -43,6 +43,32 @@ def test_batch16_gemm_path_matches_oracle_and_small_batch(cuda, small_model):
         rec = []
         M.OracleModel(host, M.OracleConfig(n_layers=2, vocab=cfg.vocab)).generate(prompts[b].tolist(), 5, record=rec)
         assert greedy_ids_match(got[b].tolist(), alone[b].tolist(), rec) >= 3
+
+
+def test_batch64_c2_shape_matches_oracle(cuda, small_model):
+    """The batched-decode configuration's shape on two layers: 64 sequences
+    with 128-id prompts prefilled densely (tensor-core GEMMs over 8192 token
+    rows, causal prefill attention), then greedy decode on the GEMM path.
+    Every sequence follows the oracle (runners/engine.py:157-181 per row,
+    stepped as one batch), and where all its ids matched, the logits of the
+    last step are within the 2e-2 / 1e-2 tolerance."""
+    from llamamps_b200.engine import QwenEngine
+    cfg, mw, host = small_model
+    B, P, N = 64, 128, 4
+    prompts = np.random.default_rng(2).integers(0, cfg.vocab, (B, P))
+    eng = QwenEngine(weights=mw, max_batch=B, max_seq_len=P + N + 8, decoder="kernels")
+    got = eng.generate_batch(prompts, N)
+    assert int(eng.gemm_err.item()) == 0
+    last = eng.buf_logits[:B].cpu().numpy()
+    rec = []
+    ref = M.OracleBatch(host, M.OracleConfig(n_layers=2, vocab=cfg.vocab), B).generate(prompts, N, record=rec)
+    full = 0
+    for b in range(B):
+        n = greedy_ids_match(got[b].tolist(), ref[b].tolist(), [r[b] for r in rec])
+        if n == N:
+            full += 1
+            assert_close(last[b], rec[N - 1][b], what=f"sequence {b} last-step logits")
+    assert full >= B // 2, f"only {full} of {B} sequences matched every step"
 
 
 def test_argmax_rows_first_index(cuda):

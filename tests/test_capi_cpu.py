@@ -98,7 +98,7 @@ def test_tensor_parallel_exchange_validation():
     def ar(**kw):
         v = {**ok, **kw}
         return L.lmps_tp2_allreduce_residual(v["part"], v["x"], v["n"], v["comm"], v["peer"], v["seen"], v["site"],
-                                             v["n_sites"], v["max_n"], v["err"], None)
+                                             v["n_sites"], v["max_n"], v["err"], 0, None)
     assert ar(peer=None) == -1
     assert ar(site=4) == -1                                       # site outside n_sites
     assert ar(n=1544, max_n=1536) == -1                           # more than a slot holds
@@ -106,9 +106,9 @@ def test_tensor_parallel_exchange_validation():
     assert ar(part=a + 8) == -1                                   # misaligned
     # fused GEMV exchange: rows x batch beyond the slot, and a grid beyond 64 CTAs
     g = L.lmps_gemv_q4_tp2_residual
-    assert g(a, a, a, 768, None, a, 1536, 768, 1, a, a, a, 0, 4, 1536, a, None) == -1
-    assert g(a, a, a, 768, a, a, 1536, 768, 2, a, a, a, 0, 4, 1536, a, None) == -1
-    assert g(a, a, a, 768, a, a, 4096, 768, 1, a, a, a, 0, 4, 4096, a, None) == -2   # 128 CTAs
+    assert g(a, a, a, 768, None, a, 1536, 768, 1, a, a, a, 0, 4, 1536, a, 0, None) == -1
+    assert g(a, a, a, 768, a, a, 1536, 768, 2, a, a, a, 0, 4, 1536, a, 0, None) == -1
+    assert g(a, a, a, 768, a, a, 4096, 768, 1, a, a, a, 0, 4, 4096, a, 0, None) == -2   # 128 CTAs
 
 
 def test_attention_rope_validation():

@@ -77,18 +77,48 @@ def test_bad_token_id_raises(cuda, two_layer):
 
 
 @pytest.mark.slow
-def test_full_model_greedy_parity(cuda):
-    """Full 28-layer Qwen2.5-1.5B shape, random-init Q4 weights, a 32-id prompt
-    (numpy seed 1) and greedy decode against the oracle."""
+def test_full_model_c1_parity(cuda):
+    """The benchmark configuration end to end: full 28-layer Qwen2.5-1.5B
+    shape, random-init Q4 weights, a 32-id prompt (numpy seed 1) and 128
+    greedy steps (runners/engine.py:157-181 per token).
+
+    * logits at every one of the 160 positions through the reference API
+      (run_inference), fed the oracle's own token sequence, are within the
+      2e-2 / 1e-2 tolerance of the oracle's;
+    * at each of the 128 generating positions the GPU's argmax equals the
+      oracle's unless the oracle's top-2 margin is within that tolerance;
+    * the free-running greedy ids (generate) equal the oracle's up to the
+      first step whose top-2 margin is within that tolerance."""
     from llamamps_b200.config import QWEN2_5_1_5B as cfg
     from llamamps_b200.engine import QwenEngine
     from llamamps_b200.weights import model_host_arrays, synth_model
     mw = synth_model(cfg, seed=1, device="cuda")
-    prompt = np.random.default_rng(1).integers(0, cfg.vocab, 32)
-    eng = QwenEngine(weights=mw, max_seq_len=256)
-    got = eng.generate(prompt.tolist(), 8)
+    prompt = np.random.default_rng(1).integers(0, cfg.vocab, 32).tolist()
     host = model_host_arrays(mw)
-    rec = []
-    ref = M.OracleModel(host, M.OracleConfig()).generate(prompt.tolist(), 8, record=rec)
-    n = greedy_ids_match(got, ref, rec)
-    assert n >= 4
+    orc = M.OracleModel(host, M.OracleConfig())
+    n_new = 128
+    fed, ref_logits, ref_ids = [], [], []
+    lg = None
+    for t in prompt:
+        fed.append(t)
+        lg = orc.step_token(t)
+        ref_logits.append(lg)
+    for i in range(n_new):
+        nxt = M.predict_next_token(lg)
+        ref_ids.append(nxt)
+        if i + 1 < n_new:
+            fed.append(nxt)
+            lg = orc.step_token(nxt)
+            ref_logits.append(lg)
+    eng = QwenEngine(weights=mw, max_seq_len=256)
+    embed = host["embed"]
+    worst = 0.0
+    for i, t in enumerate(fed):
+        got = eng.run_inference(embed[t])
+        worst = max(worst, assert_close(got, ref_logits[i], what=f"logits at position {i}"))
+        if i >= len(prompt) - 1:
+            a, r = eng.predict_next_token(got), M.predict_next_token(ref_logits[i])
+            assert a == r or M.top2_margin(ref_logits[i]) <= 2e-2, f"argmax at position {i}: {a} != {r}"
+    got_ids = QwenEngine(weights=mw, max_seq_len=256).generate(prompt, n_new)
+    gen_logits = ref_logits[len(prompt) - 1:]
+    greedy_ids_match(got_ids, ref_ids, gen_logits)   # raises on a divergence above the margin

@@ -9,7 +9,7 @@ import pytest
 import torch
 
 from oracle import mirror as M
-from tests._util import f16_bits_equal
+from tests._util import assert_close, f16_bits_equal
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
 PACK_CASES = ["normal_64x96", "odd_7x33", "kproj_64x1536", "edge_4x32"]
@@ -129,3 +129,45 @@ def test_oracle_layer_one_token_is_reference_layer():
     a = M.swiglu(M.gemv_q4(lw["gt"], lw["gts"], hn, 8960, 1536), M.gemv_q4(lw["up"], lw["ups"], hn, 8960, 1536))
     x2 = M.residual_add(x1, M.gemv_q4(lw["dn"], lw["dns"], a, 1536, 8960))
     assert f16_bits_equal(out, x2)
+
+
+def _tiny_weights(rng, cfg, n_layers):
+    def mat(rows, k):
+        return M.q4_pack(rng.normal(0, 0.05, (rows, k)).astype(np.float32))
+    layers = []
+    for _ in range(n_layers):
+        lw = {}
+        for name, (r, k) in {"q": (cfg.q_dim, cfg.hidden), "k": (cfg.kv_dim, cfg.hidden), "v": (cfg.kv_dim, cfg.hidden),
+                             "o": (cfg.hidden, cfg.q_dim), "gt": (cfg.intermediate, cfg.hidden),
+                             "up": (cfg.intermediate, cfg.hidden), "dn": (cfg.hidden, cfg.intermediate)}.items():
+            lw[name], lw[name + "s"] = mat(r, k)
+        lw["bq"] = rng.normal(0, 0.02, cfg.q_dim).astype(np.float16)
+        lw["bk"] = rng.normal(0, 0.02, cfg.kv_dim).astype(np.float16)
+        lw["bv"] = rng.normal(0, 0.02, cfg.kv_dim).astype(np.float16)
+        lw["in_norm"] = (1 + rng.normal(0, 0.02, cfg.hidden)).astype(np.float16)
+        lw["post_norm"] = (1 + rng.normal(0, 0.02, cfg.hidden)).astype(np.float16)
+        layers.append(lw)
+    embed = rng.normal(0, 0.5, (cfg.vocab, cfg.hidden)).astype(np.float16)
+    lp, ls = M.q4_pack(embed.astype(np.float32))
+    return {"layers": layers, "final_norm": (1 + rng.normal(0, 0.02, cfg.hidden)).astype(np.float16),
+            "lm_packed": lp, "lm_scales": ls, "embed": embed}
+
+
+def test_batched_oracle_rows_equal_single_sequence_oracle():
+    """OracleBatch (used by the full-batch GPU tests) is the per-sequence
+    oracle row by row: same greedy ids, logits equal up to fp16 rounding of
+    sums taken in another order (GEMM vs GEMV)."""
+    cfg = M.OracleConfig(hidden=128, intermediate=256, vocab=300, n_layers=2, n_q_heads=4, n_kv_heads=2,
+                         head_dim=32)
+    w = _tiny_weights(np.random.default_rng(5), cfg, 2)
+    prompts = np.random.default_rng(6).integers(0, cfg.vocab, (3, 5))
+    rec_b = []
+    ids_b = M.OracleBatch(w, cfg, 3).generate(prompts, 4, record=rec_b)
+    for b in range(3):
+        rec = []
+        ids = M.OracleModel(w, cfg).generate(prompts[b].tolist(), 4, record=rec)
+        for i in range(4):
+            assert_close(rec_b[i][b], rec[i], what=f"row {b} step {i}")
+            if ids[i] != ids_b[b, i]:
+                assert M.top2_margin(rec[i]) < 2e-2
+                break

@@ -160,3 +160,52 @@ def test_persistent_batch_logits_match_single_sequence(cuda, two_layer_small_voc
         for t in prompts[b]:
             ref = orc.step_token(int(t))
         assert_close(batched[b], ref, what=f"seq {b} vs oracle")
+
+
+@pytest.mark.parametrize("B,lens,max_seq", [(1, [20000], 32768), (4, [3000, 2500, 3100, 2050], 4096)])
+def test_persistent_long_context_matches_oracle(cuda, two_layer_small_vocab, B, lens, max_seq):
+    """Cached contexts of thousands of positions (fp16 N(0,1) rows written
+    into the paged cache), so the persistent kernel takes its long-cache path:
+    positions split across CTAs in chunks, the second per-warp K buffer of the
+    flash loop (cache > 2048 positions) and the last-split log-sum-exp merge.
+    Logits of five single-step launches and of one three-step launch against
+    the oracle holding the same cache prefix (runners/engine.py:157-181,
+    kernels/attention.metal:22-40, softmax.metal:23-36, attn_sum.metal:22-33)."""
+    cfg, mw, host = two_layer_small_vocab
+    eng = _engine(mw, max_batch=4, max_seq_len=max_seq, decoder="persistent")
+    eng.reset(B)
+    rng = np.random.default_rng(60 + B)
+    orcs = []
+    for b in range(B):
+        orc = M.OracleModel(host, M.OracleConfig(n_layers=2, vocab=cfg.vocab))
+        for layer in range(2):
+            k = rng.normal(0, 1, (lens[b], cfg.kv_dim)).astype(np.float16)
+            v = rng.normal(0, 1, (lens[b], cfg.kv_dim)).astype(np.float16)
+            eng.cache.write_positions(b, layer, 0, torch.from_numpy(k), torch.from_numpy(v))
+            orc.cache.set_prefix(layer, k, v)
+        orc.pos = lens[b]
+        orcs.append(orc)
+    eng.pos[:B].copy_(torch.tensor(lens, dtype=torch.int32))
+    logits = torch.zeros(B, cfg.vocab, dtype=torch.float16, device="cuda")
+    toks = rng.integers(0, cfg.vocab, (B, 8))
+    for s in range(5):
+        eng.tokens[:B].copy_(torch.from_numpy(toks[:, s]).to(torch.int32))
+        eng.pdec.run(B, eng.tokens, eng.pos, 1, logits=logits)
+        torch.cuda.synchronize()
+        eng.pdec.check_error()
+        got = logits.cpu().numpy()
+        for b in range(B):
+            assert_close(got[b], orcs[b].step_token(int(toks[b, s])), what=f"seq {b} step {s}")
+    # three steps in one launch, the fed tokens forced: logits of the last one
+    eng.tokens[:B].copy_(torch.from_numpy(toks[:, 5]).to(torch.int32))
+    forced = torch.from_numpy(toks[:, 6:8]).to("cuda", torch.int32).contiguous()
+    eng.pdec.run(B, eng.tokens, eng.pos, 3, forced=forced, logits=logits)
+    torch.cuda.synchronize()
+    eng.pdec.check_error()
+    got = logits.cpu().numpy()
+    for b in range(B):
+        ref = None
+        for s in range(5, 8):
+            ref = orcs[b].step_token(int(toks[b, s]))
+        assert_close(got[b], ref, what=f"seq {b} after a three-step launch")
+    assert eng.pos[:B].cpu().tolist() == [n + 8 for n in lens]

@@ -150,3 +150,104 @@ def test_tp2_generate_matches_oracle(cuda, dense, comm):
         ref = M.OracleModel(host, M.OracleConfig(n_layers=2, vocab=8192)).generate(prompts[b].tolist(), STEPS,
                                                                                  record=rec)
         assert greedy_ids_match(out[0][b], ref, rec) >= 3, f"sequence {b}"
+
+
+WAIT_NS = 50_000_000   # 50 ms: the exchange's bounded wait, shortened so a missing peer shows up quickly
+
+
+def test_tp2_wait_runs_out_without_a_peer(cuda):
+    """Failure detection of the peer exchange on one GPU: a second local
+    buffer stands in for the peer's, so the flags this rank waits for are
+    never written.  Each kernel's bounded wait must run out (no trap, no
+    hang): the error word reads 1, x is left as it was, and a later call on
+    any site returns at once because the error word is set.  The engine-level
+    check then raises.  Same for the fused GEMV exchange."""
+    import time
+    import types
+    from llamamps_b200 import kernels as K
+    from llamamps_b200.tp import TPEngine
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(3)
+    for fused in (False, True):
+        ex = K.PeerExchange(4, 8 * 1536, dev, wait_ns=WAIT_NS)
+        stand_in = K.PeerExchange(4, 8 * 1536, dev)
+        ex.peer = stand_in.comm            # flags this rank publishes land here; nothing answers
+        try:
+            err = torch.zeros(1, dtype=torch.int32, device=dev)
+            x = torch.randn(2, 1536, generator=g, device=dev).half()
+            x0 = x.clone()
+            part = torch.empty(2, 1536, dtype=torch.float16, device=dev)
+            packed = torch.randint(0, 256, (1536 * 768 // 2,), generator=g, device=dev, dtype=torch.uint8)
+            scales = (torch.rand(1536 * 768 // 32, generator=g, device=dev) * 0.04 + 0.005).half()
+            a = torch.randn(2, 768, generator=g, device=dev).half()
+
+            def one(site):
+                if fused:
+                    K.gemv_q4_tp2_residual(packed, scales, a, 1536, 768, x, part, ex, site, err)
+                else:
+                    K.tp2_allreduce_residual(torch.randn(2, 1536, generator=g, device=dev).half(), x, ex, site, err)
+                torch.cuda.synchronize(dev)
+
+            torch.cuda.synchronize(dev)
+            t0 = time.perf_counter()
+            one(0)
+            waited = time.perf_counter() - t0
+            assert int(err.item()) == 1, "the wait did not report the missing peer"
+            assert torch.equal(x, x0), "x changed although the exchange failed"
+            assert 0.04 <= waited < 3.0, f"first call took {waited:.3f} s"
+            t0 = time.perf_counter()
+            one(1)
+            assert time.perf_counter() - t0 < 0.03, "a call after the error still waited"
+            assert int(err.item()) == 1 and torch.equal(x, x0)
+            if not fused:
+                # the engine-level check raises on the device error word
+                stub = types.SimpleNamespace(exchange=ex, comm_err=err)
+                with pytest.raises(RuntimeError, match="timed out"):
+                    TPEngine.check_comm(stub)
+        finally:
+            torch.cuda.synchronize(dev)
+            ex.peer = None                  # not an IPC mapping: nothing to unmap
+            ex.close()
+            stand_in.close()
+
+
+def _skip_rank(rank, world, port, out):
+    """Rank 1 skips the second exchange call: rank 0's bounded wait for it
+    runs out and reports through its error word; rank 1 saw nothing wrong.
+    No kernel of either rank is in flight when the ranks meet again."""
+    _env(rank, world, port)
+    import torch.distributed as dist
+    from llamamps_b200 import kernels as K
+    from llamamps_b200.tp import init_from_env
+    init_from_env("nccl", timeout_s=60)
+    dev = torch.device(f"cuda:{rank}")
+    ex = K.PeerExchange(2, 1536, dev, wait_ns=WAIT_NS)
+    try:
+        handles = [None] * world
+        dist.all_gather_object(handles, ex.handle())
+        ex.connect(handles[1 - rank])
+        dist.barrier()
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        x = torch.ones(1, 1536, dtype=torch.float16, device=dev)
+        part = torch.full((1, 1536), 0.5, dtype=torch.float16, device=dev)
+        K.tp2_allreduce_residual(part, x, ex, 0, err)        # both ranks: 1 + (0.5 + 0.5)
+        torch.cuda.synchronize(dev)
+        first = (int(err.item()), float(x[0, 0].item()))
+        dist.barrier()
+        if rank == 0:
+            K.tp2_allreduce_residual(part, x, ex, 0, err)    # the peer never makes this call
+            torch.cuda.synchronize(dev)
+        out[rank] = first + (int(err.item()), float(x[0, 0].item()))
+        dist.barrier()
+    finally:
+        torch.cuda.synchronize(dev)
+        ex.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_tp2_missing_peer_call_times_out(cuda):
+    out = _spawn(_skip_rank)
+    assert out[0] == (0, 2.0, 1, 2.0), dict(out)     # wait ran out, x untouched by the failed call
+    assert out[1] == (0, 2.0, 0, 2.0), dict(out)
