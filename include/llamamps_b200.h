@@ -354,7 +354,7 @@ typedef struct lmps_decode_state {
   int32_t* error;               /* [1] set to 1 when a bounded device wait gives up */
   unsigned long long* trace;    /* optional stage timeline (or NULL): [3 * grid, trace_events]
                                    %globaltimer stamps; rows 0..grid-1 compute warps (stage
-                                   start after its wait, input staged, stage end; three
+                                   start, input staged, compute done, stage end; four
                                    per stage), rows grid.. the producer
                                    (first and last chunk issue of each stage), rows 2*grid..
                                    the compute warps' cumulative ns spent waiting for weights */

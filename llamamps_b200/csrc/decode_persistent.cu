@@ -301,7 +301,14 @@ struct CState {
   int slot;           // ring slot of the next chunk (same sequence as the producer)
   uint32_t phase;     // its full-barrier phase parity
   unsigned long long wait_ns;  // time thread 0 spent waiting for ring chunks (timeline only)
+  int ev;             // next timeline event of this CTA (thread 0, timeline only)
 };
+
+// Timeline stamp of thread 0 between the stages' own stamps: where a
+// stage's compute ends and its epilogue (reduction, publish) begins.
+__device__ __forceinline__ void trace_mid(const Params& P, CState& cs) {
+  if (threadIdx.x == 0) trace_event(P, blockIdx.x, cs.ev, cs.wait_ns);
+}
 
 __device__ __forceinline__ bool aborting(Smem& S) { return *reinterpret_cast<volatile int*>(&S.misc[0]) != 0; }
 __device__ __forceinline__ void raise_abort(const Params& P, Smem& S, int code) {
@@ -799,6 +806,7 @@ __device__ void gemv_rows(const Params& P, Smem& S, CState& cs, int kind, int la
       }
     }
   }
+  trace_mid(P, cs);
   if (head) {
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
@@ -890,6 +898,7 @@ __device__ void gemv_down(const Params& P, Smem& S, CState& cs, int layer, uint3
       if (sub == 0 && lrow < n) red[(b * kOwnMax + r - c.r0 + lrow) * kRedStride + warp] = v;
     }
   }
+  trace_mid(P, cs);
   // -- epilogue: four lanes per row (quarters of the 11 warp partials), the
   // two rows of a pair in an aligned group of 8 lanes
   consumer_sync();
@@ -1521,7 +1530,7 @@ __device__ void att_consumer(const Params& P, Smem& S, uint32_t epoch) {
 
 template <int NB>
 __device__ void consumer(const Params& P, Smem& S, uint32_t epoch) {
-  CState cs{0, 0u, 0ull};
+  CState cs{0, 0u, 0ull, 0};
   const lmps_model_desc& m = P.m;
   const int B = P.s.batch;
   const int hidden = m.hidden, Hkv = m.n_kv_heads;
@@ -1533,7 +1542,6 @@ __device__ void consumer(const Params& P, Smem& S, uint32_t epoch) {
     pos[b] = b < B ? P.s.pos[b] : 0;
   }
   const int hist0 = (P.s.history && P.s.step_counter) ? P.s.step_counter[0] : 0;
-  int ev = 0;
   const bool tr = threadIdx.x == 0;
   const int n_stage = m.n_layers * 5 + 1;
   int o0, o1;
@@ -1579,7 +1587,7 @@ __device__ void consumer(const Params& P, Smem& S, uint32_t epoch) {
       const int l = si / 5;
       const int kind = (l == m.n_layers) ? K_HEAD : si - 5 * l;
       const uint32_t tag = tag0 + static_cast<uint32_t>(si), in_tag = tag - 1u;
-      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
+      if (tr) trace_event(P, blockIdx.x, cs.ev, cs.wait_ns);
       const LayerPtrs& L = S.lp[kind == K_HEAD ? 0 : l];
       // the stage's weight chunking does not depend on its input: set up
       // before the input is polled
@@ -1601,7 +1609,7 @@ __device__ void consumer(const Params& P, Smem& S, uint32_t epoch) {
       } else if (kind == K_O || kind == K_DN) {
         stage_copy<NB>(P, S, kind == K_O ? P.attnt : P.at, in_tag, kind == K_O ? q_dim : m.intermediate);
       }
-      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
+      if (tr) trace_event(P, blockIdx.x, cs.ev, cs.wait_ns);
       // -- compute and publish
       if (kind == K_ATT) {
         // (with dedicated attention CTAs they run this stage: no items here)
@@ -1629,6 +1637,7 @@ __device__ void consumer(const Params& P, Smem& S, uint32_t epoch) {
             if (b == bsel) pb = pos[b];
           attn_item(P, S, L, bsel, kvh, sp, nsp, chunk, pb, in_tag, tag, nullptr);
         }
+        trace_mid(P, cs);
       } else if (kind == K_DN) {
         gemv_down<NB>(P, S, cs, l, tag, ch);
       } else {
@@ -1646,7 +1655,7 @@ __device__ void consumer(const Params& P, Smem& S, uint32_t epoch) {
           }
         }
       }
-      if (tr) trace_event(P, blockIdx.x, ev, cs.wait_ns);
+      if (tr) trace_event(P, blockIdx.x, cs.ev, cs.wait_ns);
     }
   }
   // ---- CTA 0: final tokens, state write-back, next launch's tag base

@@ -2,7 +2,8 @@
 
 ``capture(engine, steps)`` runs ``steps`` decode steps in one traced launch
 (``lmps_decode_state.trace``: a %globaltimer stamp per CTA at the start of
-every stage, once its input is staged in shared memory, and at its end; the
+every stage, once its input is staged in shared memory, once its compute is
+done and at its end; the
 producer's first/last chunk issue per stage and the consumers' cumulative
 wait for weights) and reduces it to per-stage-kind numbers: the hand-off
 latency (last CTA's end of the previous stage to the first CTA's start), the
@@ -19,6 +20,9 @@ import torch
 
 KINDS = ("QKV", "ATT", "O", "GU", "DN")
 WEIGHT_KINDS = ("QKV", "O", "GU", "DN")
+# consumer stamps per stage: start (inputs polled from here), input staged,
+# compute done (the ring chunks consumed), end (epilogue published)
+EV = 4
 
 
 def capture(engine, steps: int = 4) -> Dict:
@@ -27,7 +31,7 @@ def capture(engine, steps: int = 4) -> Dict:
     L = engine.layers
     sms = torch.cuda.get_device_properties(engine.device).multi_processor_count
     n_stage = L * len(KINDS) + 1
-    events = steps * n_stage * 3 + 8
+    events = steps * n_stage * EV + 8
     trace = torch.zeros(3 * sms, events, dtype=torch.int64, device=engine.device)
     B = engine.batch
     engine.pdec.run(B, engine.tokens, engine.pos, steps, trace=trace)
@@ -45,31 +49,34 @@ def capture(engine, steps: int = 4) -> Dict:
     agg: Dict[str, Dict[str, list]] = {}
     prev_end = None
     for i, n in enumerate(names):
-        e = (step * n_stage + i) * 3
-        st, sg, en = cons[:, e], cons[:, e + 1], cons[:, e + 2]
+        e = (step * n_stage + i) * EV
+        st, sg, cm, en = cons[:, e], cons[:, e + 1], cons[:, e + 2], cons[:, e + 3]
         kind = n.split(".")[-1]
         a = agg.setdefault(kind, {"handoff_us": [], "span_us": [], "cta_us": [], "staging_us": [],
-                                  "ring_wait_us": []})
+                                  "compute_us": [], "epilogue_us": [], "ring_wait_us": []})
         if prev_end is not None:
             a["handoff_us"].append((st.min() - prev_end) / 1e3)
         a["span_us"].append((en.max() - st.min()) / 1e3)
         a["cta_us"].append(float(np.median((en - st) / 1e3)))
         a["staging_us"].append(float(np.median((sg - st) / 1e3)))
-        a["ring_wait_us"].append(float(np.median((wait[:, e + 2] - wait[:, e]) / 1e3)))
+        a["compute_us"].append(float(np.median((cm - sg) / 1e3)))
+        a["epilogue_us"].append(float(np.median((en - cm) / 1e3)))
+        a["ring_wait_us"].append(float(np.median((wait[:, e + 3] - wait[:, e]) / 1e3)))
         prev_end = en.max()
     for i, n in enumerate(pnames):
         e = (step * len(pnames) + i) * 2
         kind = n.split(".")[-1]
         ci = names.index(n)
-        ce = (step * n_stage + ci) * 3
+        ce = (step * n_stage + ci) * EV
         lead = np.median((cons[:, ce] - prod[:, e + 1]) / 1e3)
-        agg[kind].setdefault("producer_lead_us", []).append(float(lead))
+        agg.setdefault(kind, {}).setdefault("producer_lead_us", []).append(float(lead))
     step_us = []
     for s in range(steps):
-        e0, e1 = (s * n_stage) * 3, (s * n_stage + n_stage - 1) * 3 + 2
+        e0, e1 = (s * n_stage) * EV, (s * n_stage + n_stage - 1) * EV + EV - 1
         step_us.append(float((cons[:, e1].max() - cons[:, e0].min()) / 1e3))
     out = {"steps": steps, "step_span_us": step_us, "stages": {}}
     for k, a in agg.items():
         out["stages"][k] = {m: round(float(np.mean(v)), 3) for m, v in a.items() if v}
-        out["stages"][k]["count_per_step"] = len(a["span_us"])
+        if "span_us" in a:
+            out["stages"][k]["count_per_step"] = len(a["span_us"])
     return out
