@@ -229,6 +229,22 @@ int lmps_prefill_attention(const uint16_t* q, int ldq, const uint16_t* k_pool, c
  * (runners/engine.py:180-181), the large-batch companion of the LM-head GEMM. */
 int lmps_argmax_rows(const uint16_t* logits, int ld, int rows, int n, int32_t* ids, void* stream);
 
+/* Top-k / temperature sampling of each row of fp16 logits [rows, ld] over n
+ * columns, beside the greedy argmax of runners/engine.py:180-181 (the
+ * reference has no sampling).  The k largest logits (ties at the k-th value:
+ * lowest indices first) in ascending index order get weights
+ * exp((v - max) / temperature) (fp32); u = the top 24 bits of the first
+ * Philox4x32-10 word for key = seed and counter = (row, offset low 32 bits,
+ * offset high 32 bits, 0), times 2^-24; ids[row] = the first candidate whose
+ * running weight sum exceeds u times the total (sums in a fixed order: see
+ * csrc/sampling.cu).  Same seed, offset and logits give the same ids.
+ * temperature <= 0 or top_k == 1: the largest logit, lowest index on ties.
+ * NaN logits are never chosen.  1 <= top_k <= min(1024, n).  ids2, when not
+ * NULL, receives a copy (e.g. a history row). */
+int lmps_sample_rows(const uint16_t* logits, int ld, int rows, int n, int top_k, float temperature,
+                     unsigned long long seed, unsigned long long offset, int32_t* ids, int32_t* ids2,
+                     void* stream);
+
 /* ---- two-way tensor parallelism over peer memory ------------------------
  * The all-reduce (sum) of the two ranks' partial o_proj / down_proj products
  * that follows each split projection (runners/engine.py:215-221,237-243 with
@@ -279,6 +295,19 @@ int lmps_gemv_q4_tp2_residual(const uint8_t* packed, const uint16_t* scales, con
                               uint16_t* x, uint16_t* part, int rows, int k, int batch, void* comm,
                               void* peer_comm, uint32_t* seen, int site, int n_sites, int max_n,
                               int32_t* error, unsigned long long wait_ns, void* stream);
+
+/* Vocabulary-split LM head (runners/engine.py:171-181 with the head's rows
+ * divided between the two ranks): rank r ran lmps_lm_head_argmax over its
+ * own rows [row_offset, row_offset + its row count), writing its fp16
+ * logits [rows, ld] and local first-index argmax local_ids; this call
+ * exchanges (logit, global row) with the peer and writes the global
+ * first-index argmax to ids on both ranks (the larger logit, then the lower
+ * global row).  rows <= 256 sequences, 4 * rows <= max_n; same exchange
+ * buffers, counters, call rules, wait limit and error behaviour as
+ * lmps_tp2_allreduce_residual (a site of its own; one CTA). */
+int lmps_tp2_argmax_exchange(const uint16_t* logits, int ld, const int32_t* local_ids, int rows, int row_offset,
+                             int32_t* ids, void* comm, void* peer_comm, uint32_t* seen, int site, int n_sites,
+                             int max_n, int32_t* error, unsigned long long wait_ns, void* stream);
 
 /* ---- weight format ---------------------------------------------------- */
 

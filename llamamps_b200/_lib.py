@@ -63,6 +63,10 @@ _SIGS = {
     "lmps_gemv_q4_tp2_residual": (c_int, [c_vp, c_vp, c_vp, c_int, c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp,
                                           c_vp, c_int, c_int, c_int, c_vp, ctypes.c_ulonglong, c_vp]),
     "lmps_argmax_rows": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_vp]),
+    "lmps_tp2_argmax_exchange": (c_int, [c_vp, c_int, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_int,
+                                         c_int, c_vp, ctypes.c_ulonglong, c_vp]),
+    "lmps_sample_rows": (c_int, [c_vp, c_int, c_int, c_int, c_int, c_float, ctypes.c_ulonglong,
+                                 ctypes.c_ulonglong, c_vp, c_vp, c_vp]),
     "lmps_w4a16_gemm_workspace_size": (c_size, [c_int, c_int]),
     "lmps_w4a16_gemm": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_vp, c_int, c_int, c_int, c_int,
                                 c_int, c_vp, c_vp, c_size, c_vp]),

@@ -80,6 +80,49 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// Vocabulary-split LM head, the cross-rank step (runners/engine.py:171-181
+// with the head's rows divided between two GPUs): each rank found the
+// first-index argmax of its own rows; one CTA turns it into a key (value
+// key | 0xffffffff - global row, so the larger value and then the lower
+// global row wins, numpy's first-index rule), stores it into the peer's
+// receive slot, hands off with the peer's CTA and keeps the larger key.
+// Both ranks derive the same id.  Same slots, flags and error behaviour as
+// allreduce_residual_kernel (flag word 0 of the site).
+__global__ void argmax_exchange_kernel(const __half* __restrict__ logits, int ld, const int32_t* __restrict__ local,
+                                       int rows, uint32_t row_offset, int32_t* __restrict__ ids, int slot_u64,
+                                       unsigned long long* peer_recv, const unsigned long long* recv,
+                                       uint32_t* peer_flags, const uint32_t* flags, uint32_t* seen, int32_t* error,
+                                       unsigned long long wait_ns) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = *reinterpret_cast<volatile int32_t*>(error) == 0;
+  __syncthreads();
+  if (!ok) return;
+  const uint32_t want = seen[0] + 1u;
+  const int sl = static_cast<int>(want & 1u) * slot_u64;
+  const int b = threadIdx.x;
+  unsigned long long key = 0ull;
+  if (b < rows) {
+    const int32_t i = local[b];
+    const float v = __half2float(logits[static_cast<size_t>(b) * ld + i]);
+    key = argmax_key(v, row_offset + static_cast<uint32_t>(i));
+    peer_recv[sl + b] = key;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const bool good = lmps_tp2_handshake(peer_flags, flags, 0, want, error, wait_ns);
+    if (good) seen[0] = want;
+    ok = good ? 1 : 0;
+  }
+  __syncthreads();
+  if (!ok) return;
+  __threadfence_system();
+  if (b < rows) {
+    const unsigned long long best = u64_max(key, __ldcg(recv + sl + b));
+    ids[b] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(best & 0xFFFFFFFFull));
+  }
+}
+
 }  // namespace tp
 }  // namespace lmps
 
@@ -153,5 +196,22 @@ extern "C" int lmps_tp2_allreduce_residual(const uint16_t* part, uint16_t* x, in
       reinterpret_cast<const uint4*>(part), reinterpret_cast<uint4*>(x), n8, max_n / 8,
       reinterpret_cast<uint4*>(t.peer_recv), reinterpret_cast<const uint4*>(t.recv), t.peer_flags, t.flags,
       seen + site * tp::kMaxCtas, error, wait_ns ? wait_ns : kTp2DefaultWaitNs);
+  return lmps_launch_status();
+}
+
+extern "C" int lmps_tp2_argmax_exchange(const uint16_t* logits, int ld, const int32_t* local_ids, int rows,
+                                        int row_offset, int32_t* ids, void* comm, void* peer_comm, uint32_t* seen,
+                                        int site, int n_sites, int max_n, int32_t* error,
+                                        unsigned long long wait_ns, void* stream) {
+  LMPS_CHECK_ARG(logits && local_ids && ids && comm && peer_comm && seen && error);
+  LMPS_CHECK_ARG(rows >= 1 && rows <= tp::kThreads && ld >= 1 && row_offset >= 0);
+  LMPS_CHECK_ARG(n_sites >= 1 && site >= 0 && site < n_sites && max_n >= 8 && max_n % 8 == 0);
+  LMPS_CHECK_ARG(4LL * rows <= max_n);  // rows 64-bit keys per receive slot of max_n halves
+  LMPS_CHECK_ARG(lmps_aligned(comm, 16) && lmps_aligned(peer_comm, 16) && lmps_aligned(seen, 4));
+  const Tp2Site t = lmps_tp2_site(comm, peer_comm, site, n_sites, max_n);
+  tp::argmax_exchange_kernel<<<1, tp::kThreads, 0, lmps_stream(stream)>>>(
+      reinterpret_cast<const __half*>(logits), ld, local_ids, rows, static_cast<uint32_t>(row_offset), ids,
+      max_n / 4, reinterpret_cast<unsigned long long*>(t.peer_recv), reinterpret_cast<const unsigned long long*>(t.recv),
+      t.peer_flags, t.flags, seen + site * tp::kMaxCtas, error, wait_ns ? wait_ns : kTp2DefaultWaitNs);
   return lmps_launch_status();
 }

@@ -468,8 +468,43 @@ class QwenEngine:
         self.step_counter.fill_(1)
         self.host_pos += P
 
-    def generate_batch(self, prompts, max_new_tokens: int) -> np.ndarray:
-        """Greedy decode of B equal-length prompts; returns int32 [B, max_new_tokens]."""
+    def _logits_step(self, B: int) -> None:
+        """One decode step of every sequence that leaves the fp16 logits of
+        the step in buf_logits (tokens/pos advance as in decode_step)."""
+        if self.host_pos + 1 > self.max_seq_len:
+            raise RuntimeError("KV cache full")
+        if self.pdec is not None:
+            self.pdec.run(B, self.tokens, self.pos, 1, logits=self.buf_logits[:B])
+        else:
+            K.embed_gather(self.weights.embed, self.tokens[:B], self.buf_residual[:B], self.bad_ids)
+            self._layers(B)
+            self._head(B, want_logits=True)
+            K.decode_advance(self.next_ids[:B], self.tokens[:B], self.pos[:B], self.seq_lens[:B])
+        self.host_pos += 1
+
+    def _sample_generate(self, p: torch.Tensor, n: int, top_k: int, temperature: float, seed: int) -> None:
+        """generate_batch with sampling: the prompt fed token by token, then
+        every next token drawn by lmps_sample_rows from the step's logits
+        (Philox offset = the generated token's index, so a run is
+        reproducible from its seed); history rows 0..n-1 get the draws."""
+        B, P = p.shape
+        dev_p = p.to(self.device)
+        for t in range(P):
+            self.tokens[:B].copy_(dev_p[:, t])
+            self._logits_step(B)
+        hist = self.history.view(-1)  # [step, B] rows with the active batch as stride (as decode_advance)
+        for i in range(n):
+            K.sample_rows(self.buf_logits[:B], self.cfg.vocab, top_k, temperature, seed, i,
+                          self.tokens[:B], hist[i * B:(i + 1) * B])
+            if i + 1 < n:
+                self._logits_step(B)
+
+    def generate_batch(self, prompts, max_new_tokens: int, temperature: float = 0.0, top_k: int = 0,
+                       seed: int = 0) -> np.ndarray:
+        """Decode of B equal-length prompts; returns int32 [B, max_new_tokens].
+        Greedy (the reference's argmax, runners/engine.py:180-181) unless
+        temperature > 0 and top_k > 1: then each token is sampled among the
+        top_k logits at that temperature (lmps_sample_rows, seeded)."""
         p = torch.as_tensor(np.asarray(prompts), dtype=torch.int32)
         if p.dim() == 1:
             p = p[None]
@@ -480,8 +515,11 @@ class QwenEngine:
         if int(p.min()) < 0 or int(p.max()) >= self.cfg.vocab:
             raise ValueError("token id outside the vocabulary")
         self.reset(B)
-        self.prefill(p)
-        self.decode_steps(max_new_tokens - 1, record=True)
+        if temperature > 0 and top_k > 1:
+            self._sample_generate(p, max_new_tokens, top_k, temperature, seed)
+        else:
+            self.prefill(p)
+            self.decode_steps(max_new_tokens - 1, record=True)
         torch.cuda.synchronize(self.device)
         if self.pdec is not None:
             self.pdec.check_error()
@@ -492,6 +530,9 @@ class QwenEngine:
         hist = self.history.reshape(-1)[: max_new_tokens * B].reshape(max_new_tokens, B)
         return hist.t().cpu().numpy()
 
-    def generate(self, token_ids: Sequence[int], max_new_tokens: int) -> List[int]:
-        """Greedy continuation of one prompt (the demo.py flow with a real prompt)."""
-        return [int(t) for t in self.generate_batch(np.asarray(token_ids)[None], max_new_tokens)[0]]
+    def generate(self, token_ids: Sequence[int], max_new_tokens: int, temperature: float = 0.0, top_k: int = 0,
+                 seed: int = 0) -> List[int]:
+        """Continuation of one prompt (the demo.py flow with a real prompt):
+        greedy, or top-k / temperature sampling (see generate_batch)."""
+        return [int(t) for t in self.generate_batch(np.asarray(token_ids)[None], max_new_tokens, temperature,
+                                                    top_k, seed)[0]]

@@ -260,6 +260,16 @@ def argmax_rows(logits, n: int, ids):
     return ids
 
 
+def sample_rows(logits, n: int, top_k: int, temperature: float, seed: int, offset: int, ids, ids2=None):
+    """Top-k / temperature sample of each fp16 row of logits[:, :n] into int32
+    ids (and ids2): seeded Philox draw, reproducible (see include/llamamps_b200.h)."""
+    call("lmps_sample_rows", _dev(logits, "logits", FP16), logits.shape[-1], logits.shape[0], n, int(top_k),
+         float(temperature), int(seed) & 0xFFFFFFFFFFFFFFFF, int(offset) & 0xFFFFFFFFFFFFFFFF,
+         _dev(ids, "ids", torch.int32), _dev(ids2, "ids2", torch.int32) if ids2 is not None else None,
+         _stream())
+    return ids
+
+
 def prefill_attention(q, k_pool, v_pool, block_table, out, batch: int, seq_len: int, page_size: int,
                       n_q_heads: int, n_kv_heads: int, head_dim: int):
     """Causal attention of every prompt position (q rows b*seq_len + p) over the paged cache."""
@@ -330,6 +340,20 @@ def tp2_allreduce_residual(part, x, ex: PeerExchange, site: int, error):
          ex.peer, _dev(ex.seen, "seen", torch.int32), site, ex.n_sites, ex.max_n,
          _dev(error, "error", torch.int32), ex.wait_ns, _stream())
     return x
+
+
+def tp2_argmax_exchange(logits, local_ids, row_offset: int, ids, ex: PeerExchange, site: int, error):
+    """The global first-index argmax of a vocabulary split between two ranks:
+    this rank's fp16 logits [B, ld] and local argmax ids in, the winner over
+    both ranks' rows (global row numbers) out, on both ranks."""
+    if ex.peer is None:
+        raise RuntimeError("the peer exchange is not connected")
+    B = local_ids.numel()
+    call("lmps_tp2_argmax_exchange", _dev(logits, "logits", FP16), logits.shape[-1],
+         _dev(local_ids, "local_ids", torch.int32), B, int(row_offset), _dev(ids, "ids", torch.int32), ex.comm,
+         ex.peer, _dev(ex.seen, "seen", torch.int32), site, ex.n_sites, ex.max_n, _dev(error, "error", torch.int32),
+         ex.wait_ns, _stream())
+    return ids
 
 
 def gemv_q4_tp2_residual(packed, scales, a, rows: int, k: int, x, part, ex: PeerExchange, site: int, error):

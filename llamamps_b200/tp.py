@@ -16,6 +16,13 @@ computes partial o_proj / down_proj outputs; one all-reduce (sum, fp16) of
 embedding and the LM head are replicated, so every rank derives the same
 next token.  The collectives run on the process group handed in (NCCL over
 NVLink between GPUs; gloo for the host-side tests).
+
+With the peer exchange (two ranks) the LM head is split by vocabulary rows
+as well: rank r runs the Q4 head GEMV + first-index argmax over rows
+[r*V/2, (r+1)*V/2) only, and one exchange of (logit, global row) per
+sequence picks the winner on both ranks (lmps_tp2_argmax_exchange), so the
+131 MB head is read once per step across the pair instead of on both GPUs
+(runners/engine.py:171-181 with the rows divided).
 """
 from __future__ import annotations
 
@@ -27,7 +34,7 @@ import torch.distributed as dist
 
 from . import kernels as K
 from .config import ModelConfig
-from .engine import QwenEngine
+from .engine import GEMV_MAX_BATCH, QwenEngine
 from .weights import LayerWeights, ModelWeights
 
 
@@ -117,13 +124,23 @@ class TPEngine(QwenEngine):
         self.exchange = None
         self.fuse_exchange = fuse_exchange
         if comm == "p2p" and world == 2 and self.device.type == "cuda":
-            # sites [0, 2L): exchanges after a GEMM; [2L, 4L): fused GEMV exchanges
-            self.exchange = K.PeerExchange(4 * self.cfg.n_layers, self.max_batch * self.cfg.hidden, self.device)
+            # sites [0, 2L): exchanges after a GEMM; [2L, 4L): fused GEMV
+            # exchanges; 4L: the split LM head's argmax
+            self.exchange = K.PeerExchange(4 * self.cfg.n_layers + 1, self.max_batch * self.cfg.hidden, self.device)
             handles = [None] * world
             dist.all_gather_object(handles, self.exchange.handle(), group=group)
             self.exchange.connect(handles[1 - rank])
             dist.barrier(group=group)
         self.use_graphs = self.exchange is not None
+        self.split_head = self.exchange is not None
+        if self.split_head:  # this rank's vocabulary rows of the tied Q4 head (views, no copy)
+            c, w = self.cfg, self.weights
+            v0, v1 = rank * c.vocab // world, (rank + 1) * c.vocab // world
+            self._head_rows = (v0, v1)
+            self._head_p = w.lm_packed[v0 * c.hidden // 2:v1 * c.hidden // 2]
+            self._head_s = w.lm_scales[v0 * c.hidden // 32:v1 * c.hidden // 32]
+            self._head_logits = torch.zeros(self.max_batch, v1 - v0, dtype=torch.float16, device=self.device)
+            self._head_local = torch.zeros(self.max_batch, dtype=torch.int32, device=self.device)
 
     def close(self) -> None:
         """Unmap and free the peer exchange (collective: every rank calls it)."""
@@ -143,6 +160,21 @@ class TPEngine(QwenEngine):
         out = super().generate_batch(prompts, max_new_tokens)
         self.check_comm()
         return out
+
+    def _head(self, B: int, want_logits: bool) -> None:
+        """Final norm, LM head and argmax: split by vocabulary rows over the two
+        ranks when only the next ids are wanted (GEMV path); the replicated
+        head otherwise (full logits, or batches on the GEMM path)."""
+        if not (self.split_head and not want_logits and B <= GEMV_MAX_BATCH):
+            super()._head(B, want_logits)
+            return
+        c, w = self.cfg, self.weights
+        v0, v1 = self._head_rows
+        K.rms_norm(self.buf_residual[:B], w.final_norm, c.eps, out=self.buf_normed[:B])
+        K.lm_head_argmax(self._head_p, self._head_s, self.buf_normed[:B], v1 - v0, c.hidden,
+                         self.argmax_keys[:B], self._head_local[:B], logits=self._head_logits[:B])
+        K.tp2_argmax_exchange(self._head_logits[:B], self._head_local[:B], v0, self.next_ids[:B], self.exchange,
+                              4 * c.n_layers, self.comm_err)
 
     def _reduce_add(self, part: torch.Tensor, x: torch.Tensor, site: int = -1) -> None:
         if self.exchange is not None and site >= 0 and part.numel() <= self.exchange.max_n:

@@ -467,3 +467,88 @@ class OracleBatch:
             if i + 1 < max_new_tokens:
                 logits = self.step_tokens(nxt)
         return out
+
+
+# --------------------------------------------------------------------------
+# Sampling (no reference counterpart: runners/engine.py:180-181 is greedy)
+# --------------------------------------------------------------------------
+
+PHILOX_M0, PHILOX_M1 = 0xD2511F53, 0xCD9E8D57
+PHILOX_W0, PHILOX_W1 = 0x9E3779B9, 0xBB67AE85
+
+
+def philox4x32_10(counter, key):
+    """Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC 2011): 4 x 32-bit counter,
+    2 x 32-bit key -> 4 x 32-bit output words."""
+    c = [int(v) & 0xFFFFFFFF for v in counter]
+    k0, k1 = int(key[0]) & 0xFFFFFFFF, int(key[1]) & 0xFFFFFFFF
+    for _ in range(10):
+        p0, p1 = PHILOX_M0 * c[0], PHILOX_M1 * c[2]
+        hi0, lo0 = p0 >> 32, p0 & 0xFFFFFFFF
+        hi1, lo1 = p1 >> 32, p1 & 0xFFFFFFFF
+        c = [hi1 ^ c[1] ^ k0, lo1, hi0 ^ c[3] ^ k1, lo0]
+        k0 = (k0 + PHILOX_W0) & 0xFFFFFFFF
+        k1 = (k1 + PHILOX_W1) & 0xFFFFFFFF
+    return c
+
+
+def f16_order_keys(logits: np.ndarray) -> np.ndarray:
+    """Order-preserving 16-bit keys of fp16 values (NaN -> 0, below all numbers)."""
+    b = np.asarray(logits, F16).view(np.uint16).astype(np.uint32)
+    key = np.where(b & 0x8000, (~b) & 0xFFFF, b | 0x8000)
+    nan = ((b & 0x7C00) == 0x7C00) & ((b & 0x03FF) != 0)
+    return np.where(nan, 0, key).astype(np.uint32)
+
+
+def sample_top_k(logits: np.ndarray, top_k: int, temperature: float, seed: int, offset: int, row: int = 0,
+                 detail: bool = False):
+    """Top-k / temperature sampling as lmps_sample_rows defines it: the k
+    largest keys (ties at the threshold: lowest indices) in ascending index
+    order, fp32 weights exp((v - vmax) * (1/T)), sums in the kernel's fixed
+    order (32 contiguous segments of ceil(k/32) candidates, then the segment
+    sums in order), u from Philox4x32-10 (key = seed, counter = (row, offset
+    lo, offset hi, 0)).  ``detail`` also returns the target and the running
+    sums (to judge ties at a boundary)."""
+    x = np.asarray(logits, F16).reshape(-1)
+    k = 1 if temperature <= 0 else int(top_k)
+    keys = f16_order_keys(x)
+    order = np.lexsort((np.arange(x.size), -keys.astype(np.int64)))   # key desc, index asc
+    cand = np.sort(order[:k])
+    inv_t = F32(1.0) if k == 1 else F32(1.0) / F32(temperature)
+    v = x[cand].astype(F32)
+    vmax = v.max()
+    w = np.exp(((v - vmax) * inv_t).astype(F32)).astype(F32)
+    seg = (k + 31) // 32
+    lane_sum = []
+    for l in range(32):
+        s = F32(0.0)
+        for i in range(min(k, l * seg), min(k, l * seg + seg)):
+            s = F32(s + w[i])
+        lane_sum.append(s)
+    z = F32(0.0)
+    for s in lane_sum:
+        z = F32(z + s)
+    r = philox4x32_10((row, offset & 0xFFFFFFFF, (offset >> 32) & 0xFFFFFFFF, 0),
+                      (seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF))[0]
+    target = F32(F32(F32(r >> 8) * F32(1.0 / 16777216.0)) * z)
+    run = F32(0.0)
+    l = 0
+    while l < 31 and not (F32(run + lane_sum[l]) > target):
+        run = F32(run + lane_sum[l])
+        l += 1
+    pick = -1
+    sums = []
+    for i in range(min(k, l * seg), min(k, l * seg + seg)):
+        run = F32(run + w[i])
+        sums.append(float(run))
+        if run > target:
+            pick = i
+            break
+    if pick < 0:
+        pick = k - 1
+        while pick > 0 and w[pick] == 0:
+            pick -= 1
+    out = int(cand[pick])
+    if detail:
+        return out, float(target), float(z), cand, w
+    return out

@@ -171,3 +171,35 @@ def test_batched_oracle_rows_equal_single_sequence_oracle():
             if ids[i] != ids_b[b, i]:
                 assert M.top2_margin(rec[i]) < 2e-2
                 break
+
+
+def test_philox_known_answers():
+    """The Philox4x32-10 restatement against the published known-answer
+    vectors of its authors' Random123 distribution (counter, key -> output)."""
+    assert M.philox4x32_10((0, 0, 0, 0), (0, 0)) == [0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]
+    assert M.philox4x32_10((0xFFFFFFFF,) * 4, (0xFFFFFFFF,) * 2) == [0x408F276D, 0x41C83B0E, 0xA20BC7C6,
+                                                                        0x6D5451FD]
+    assert M.philox4x32_10((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0)) == \
+        [0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1]
+
+
+def test_sampling_restatement_properties():
+    """top-k = 1 is the first-index argmax; draws stay inside the top k;
+    temperature -> 0 concentrates on the maximum; the empirical frequencies
+    of many draws follow the softmax of the top k."""
+    rng = np.random.default_rng(3)
+    x = rng.normal(0, 1, 500).astype(np.float16)
+    x[[10, 200]] = np.float16(4.0)                           # tie at the maximum
+    assert M.sample_top_k(x, 1, 1.0, 5, 0) == 10
+    assert M.sample_top_k(x, 8, 0.0, 5, 0) == 10             # temperature 0: greedy
+    top8 = set(np.argsort(-x.astype(np.float32), kind="stable")[:8].tolist())
+    draws = [M.sample_top_k(x, 8, 1.0, 99, i) for i in range(3000)]
+    assert set(draws) <= top8
+    cand = sorted(top8)
+    p = np.exp(x[cand].astype(np.float64) - x[cand].max())
+    p /= p.sum()
+    freq = np.array([draws.count(c) for c in cand]) / len(draws)
+    assert np.max(np.abs(freq - p)) < 0.04
+    nan_x = x.copy()
+    nan_x[3] = np.float16(np.nan)
+    assert M.sample_top_k(nan_x, 5, 1.0, 1, 0) != 3

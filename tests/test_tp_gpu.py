@@ -51,14 +51,15 @@ def _exchange_rank(rank, world, port, out):
     """Peer-memory all-reduce + residual against NCCL's sum + residual_add:
     several sites, back-to-back calls on one site, 1 to 8 rows; and the fused
     GEMV + exchange at the o_proj (1536 x 768) and down_proj (1536 x 4480)
-    shapes of a 2-way split against GEMV, NCCL sum, residual_add."""
+    shapes of a 2-way split against GEMV, NCCL sum, residual_add; and the
+    split-vocabulary argmax exchange against the argmax of the whole rows."""
     _env(rank, world, port)
     import torch.distributed as dist
     from llamamps_b200 import kernels as K
     from llamamps_b200.tp import init_from_env
     init_from_env("nccl", timeout_s=60)
     dev = torch.device(f"cuda:{rank}")
-    ex = K.PeerExchange(5, 8 * 1536, dev)
+    ex = K.PeerExchange(6, 8 * 1536, dev)
     try:
         handles = [None] * world
         dist.all_gather_object(handles, ex.handle())
@@ -92,6 +93,23 @@ def _exchange_rank(rank, world, port, out):
             K.gemv_q4_tp2_residual(packed, scales, a, 1536, k, x, part[:rows * 1536].view(rows, 1536), ex, site, err)
             torch.cuda.synchronize(dev)
             mism += int((x.view(torch.int16) != ref.view(torch.int16)).sum().item())
+        # split-vocabulary argmax: each rank's half of 3 rows of logits,
+        # ties inside a half and across the halves (the lower global row wins)
+        vg = torch.Generator(device=dev).manual_seed(11)   # same full rows on both ranks
+        full = torch.randn(3, 2000, generator=vg, device=dev).half()
+        full[1, 1500] = full[1, 400] = 30.0                 # cross-half tie: 400 wins
+        full[2, 1200] = full[2, 1700] = 25.0                # tie inside rank 1's half: 1200 wins
+        want = torch.zeros(3, dtype=torch.int32, device=dev)
+        K.argmax_rows(full, 2000, want)
+        half = full[:, rank * 1000:(rank + 1) * 1000].contiguous()
+        local = torch.zeros(3, dtype=torch.int32, device=dev)
+        K.argmax_rows(half, 1000, local)
+        ids = torch.zeros(3, dtype=torch.int32, device=dev)
+        for _ in range(2):                                  # back-to-back calls on the site
+            K.tp2_argmax_exchange(half, local, rank * 1000, ids, ex, 5, err)
+            torch.cuda.synchronize(dev)
+            mism += int((ids != want).sum().item())
+        assert want.tolist()[1] == 400 and want.tolist()[2] == 1200
         out[rank] = (mism, int(err.item()))
         torch.cuda.synchronize(dev)
         dist.barrier()
@@ -168,7 +186,8 @@ def test_tp2_wait_runs_out_without_a_peer(cuda):
     from llamamps_b200.tp import TPEngine
     dev = torch.device("cuda")
     g = torch.Generator(device=dev).manual_seed(3)
-    for fused in (False, True):
+    for kind in ("exchange", "fused", "argmax"):
+        fused = kind == "fused"
         ex = K.PeerExchange(4, 8 * 1536, dev, wait_ns=WAIT_NS)
         stand_in = K.PeerExchange(4, 8 * 1536, dev)
         ex.peer = stand_in.comm            # flags this rank publishes land here; nothing answers
@@ -181,8 +200,14 @@ def test_tp2_wait_runs_out_without_a_peer(cuda):
             scales = (torch.rand(1536 * 768 // 32, generator=g, device=dev) * 0.04 + 0.005).half()
             a = torch.randn(2, 768, generator=g, device=dev).half()
 
+            lg = torch.randn(2, 1000, generator=g, device=dev).half()
+            local = torch.tensor([3, 999], dtype=torch.int32, device=dev)
+            ids = torch.full((2,), -7, dtype=torch.int32, device=dev)
+
             def one(site):
-                if fused:
+                if kind == "argmax":
+                    K.tp2_argmax_exchange(lg, local, 1000, ids, ex, site, err)
+                elif fused:
                     K.gemv_q4_tp2_residual(packed, scales, a, 1536, 768, x, part, ex, site, err)
                 else:
                     K.tp2_allreduce_residual(torch.randn(2, 1536, generator=g, device=dev).half(), x, ex, site, err)
@@ -194,12 +219,13 @@ def test_tp2_wait_runs_out_without_a_peer(cuda):
             waited = time.perf_counter() - t0
             assert int(err.item()) == 1, "the wait did not report the missing peer"
             assert torch.equal(x, x0), "x changed although the exchange failed"
+            assert ids.tolist() == [-7, -7], "ids written although the exchange failed"
             assert 0.04 <= waited < 3.0, f"first call took {waited:.3f} s"
             t0 = time.perf_counter()
             one(1)
             assert time.perf_counter() - t0 < 0.03, "a call after the error still waited"
             assert int(err.item()) == 1 and torch.equal(x, x0)
-            if not fused:
+            if kind == "exchange":
                 # the engine-level check raises on the device error word
                 stub = types.SimpleNamespace(exchange=ex, comm_err=err)
                 with pytest.raises(RuntimeError, match="timed out"):
