@@ -220,7 +220,7 @@ int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed, const uin
  * b*seq_len + p, [.., n_q_heads*head_dim] with leading dimension ldq; their
  * K/V rows are already in the paged cache (block_table [batch, max_pages]).
  * Query p attends to positions 0..p; out has q's row layout.  head_dim 128,
- * n_q_heads / n_kv_heads <= 8. */
+ * n_q_heads / n_kv_heads <= 6. */
 int lmps_prefill_attention(const uint16_t* q, int ldq, const uint16_t* k_pool, const uint16_t* v_pool,
                            const int32_t* block_table, int max_pages, int page_size, uint16_t* out, int ldo,
                            int batch, int seq_len, int n_q_heads, int n_kv_heads, int head_dim, void* stream);
