@@ -355,8 +355,9 @@ def extra_configs(mw, cfg, args, rank, world, dist, peak):
                 return float(top[0] - top[1])
             parity = {}
             for comm, fuse in (("p2p", False), ("p2p", True), ("nccl", False)):
+                # the fused GEMV exchange belongs to the GEMV path: keep batch 8 on it there
                 eng = TPEngine(mw, rank, world, device=torch.device("cuda"), max_batch=B, max_seq_len=P + 32,
-                               comm=comm, fuse_exchange=fuse)
+                               comm=comm, fuse_exchange=fuse, **({"gemv_max_batch": B} if fuse else {}))
                 name = comm + ("_fused" if fuse else "")
                 try:
                     eng.reset(B)
@@ -459,7 +460,7 @@ def time_gemm(m: int, n: int, k: int, iters: int = 20, warmup: int = 3) -> dict:
             "error": int(err.item())}
 
 
-def time_attention(B: int, T: int, maxlen: int, calls: int = 20) -> dict:
+def time_attention(B: int, T: int, maxlen: int, calls: int = 20, auto_only: bool = False) -> dict:
     """The split-KV decode attention (attention + combine) over a paged fp16
     cache of ``maxlen`` positions, ``T`` attended, for a range of split
     counts: a CUDA graph of ``calls`` calls, us per call; ``auto`` is the
@@ -478,7 +479,7 @@ def time_attention(B: int, T: int, maxlen: int, calls: int = 20) -> dict:
     auto = K.attention_splits(B, hkv, maxlen, page)
     tiles = (maxlen + 63) // 64
     us = {}
-    for sp in sorted({1, 2, 3, 4, 6, 8, 12, 16, 24, 32, auto}):
+    for sp in ([auto] if auto_only else sorted({1, 2, 3, 4, 6, 8, 12, 16, 24, 32, auto})):
         if sp > tiles:
             continue
         ws = torch.zeros(max(K.attention_workspace_size(B, hq, hd, sp), 16), dtype=torch.uint8, device=dev)
@@ -534,8 +535,50 @@ def time_prefill_attention(B: int, P: int, iters: int = 5) -> dict:
             "tflops": round(flops / t / 1e12, 1)}
 
 
+def time_gemv(rows: int, k: int, batch: int, iters: int = 20) -> dict:
+    """The CUDA-core Q4 GEMV alone (lmps_gemv_q4_swiglu when rows is a
+    gate|up pair count, i.e. the call reads 2 x rows x k weights; CUDA events
+    around ``iters`` calls that cycle over matrices larger than L2 together)."""
+    import torch
+    from llamamps_b200 import kernels as K
+    g = torch.Generator(device="cuda").manual_seed(2)
+    n_mats = max(2, (256 << 20) // (rows * k))   # > 126 MB of weights in rotation
+    mats = [(torch.randint(0, 256, (2 * rows * k // 2,), dtype=torch.uint8, device="cuda", generator=g),
+             (torch.rand(2 * rows * k // 32, device="cuda", generator=g) * 0.01).half()) for _ in range(n_mats)]
+    x = torch.randn(batch, k, generator=g, device="cuda").half()
+    out = torch.empty(batch, rows, dtype=torch.float16, device="cuda")
+
+    def call(i):
+        p, sc = mats[i % n_mats]
+        K.gemv_q4_swiglu(p[:rows * k // 2], sc[:rows * k // 32], p[rows * k // 2:], sc[rows * k // 32:], x, rows, k,
+                         out=out)
+    for i in range(3):
+        call(i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()   # the launches back to back, without the host in between
+    with torch.cuda.graph(graph):
+        for i in range(iters):
+            call(i)
+    graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    t = a.elapsed_time(b) / iters / 1e3
+    nbytes = 2 * (rows * k // 2 + rows * k // 32 * 2) + 2 * k * batch + 2 * rows * batch
+    return {"kernel": "q4_gemv_kernel (SwiGLU)", "rows": rows, "k": k, "batch": batch, "us": round(t * 1e6, 2),
+            "gbs": round(nbytes / t / 1e9, 1), "bytes_per_launch": nbytes}
+
+
 def run_kernel_timing(args) -> int:
-    """--time gemm|attention|prefill_attention: one JSON line per shape (not a benchmark line)."""
+    """--time gemm|attention|prefill_attention|gemv: one JSON line per shape (not a benchmark line)."""
+    if args.time == "gemv":
+        shapes = [tuple(int(v) for v in s.split(",")) for s in args.shape] if args.shape else [(8960, 1536, 1)]
+        for r, k, b in shapes:
+            print(json.dumps(time_gemv(r, k, b, args.iters)))
+        return 0
     if args.time == "prefill_attention":
         shapes = [tuple(int(v) for v in s.split(",")) for s in args.shape] if args.shape else [(8, 2048)]
         for b, p in shapes:
@@ -548,7 +591,7 @@ def run_kernel_timing(args) -> int:
     else:
         shapes = [tuple(int(v) for v in s.split(",")) for s in args.shape] if args.shape else ATTN_SHAPES
         for b, t, c in shapes:
-            print(json.dumps(time_attention(b, t, c)))
+            print(json.dumps(time_attention(b, t, c, auto_only=args.auto_splits)))
     return 0
 
 
@@ -710,12 +753,14 @@ def main():
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling only: build a model with fewer decoder layers (the JSON line "
                          "then names the reduced workload and is not a measurement of it)")
-    ap.add_argument("--time", choices=["gemm", "attention", "prefill_attention"], default=None,
+    ap.add_argument("--time", choices=["gemm", "attention", "prefill_attention", "gemv"], default=None,
                     help="kernel timing tables instead of the benchmark: the tcgen05 W4A16 GEMM, the "
-                         "split-KV decode attention or the causal prefill attention, per --shape "
-                         "(m,n,k / batch,attended,cache / batch,seq_len)")
+                         "split-KV decode attention, the causal prefill attention or the gate/up SwiGLU Q4 "
+                         "GEMV, per --shape (m,n,k / batch,attended,cache / batch,seq_len / rows,k,batch)")
     ap.add_argument("--shape", action="append", default=None, help="shape for --time (repeatable)")
-    ap.add_argument("--iters", type=int, default=20, help="calls per timing for --time gemm")
+    ap.add_argument("--iters", type=int, default=20, help="calls per timing for --time gemm / gemv")
+    ap.add_argument("--auto-splits", action="store_true",
+                    help="--time attention: only the split count the library picks")
     args = ap.parse_args()
     if args.time is not None:
         return run_kernel_timing(args)

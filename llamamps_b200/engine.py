@@ -38,7 +38,10 @@ from .kv_cache import PagedKVCache
 from .weights import ModelWeights, load_reference_layout
 
 
-GEMV_MAX_BATCH = 8  # the CUDA-core GEMV serves up to 8 sequences; larger batches use the tensor-core GEMM
+# The CUDA-core GEMV serves up to 4 sequences; larger batches use the
+# tensor-core GEMM (measured at batch 8, 128-position contexts: 1.73 ms per
+# step on the GEMM path against 2.88 ms on the batch-8 GEMV, 1 x B200).
+GEMV_MAX_BATCH = 4
 
 
 def argmax_first(logits) -> int:
@@ -77,7 +80,7 @@ class QwenEngine:
                  weights: Optional[ModelWeights] = None, config: ModelConfig = QWEN2_5_1_5B,
                  max_batch: int = 1, max_seq_len: int = 2048, page_size: int = 64,
                  use_graphs: bool = True, page_order: Optional[List[int]] = None,
-                 decoder: Optional[str] = None):
+                 decoder: Optional[str] = None, gemv_max_batch: int = GEMV_MAX_BATCH):
         if not torch.cuda.is_available():
             raise RuntimeError("QwenEngine needs a CUDA device (B200); there is no CPU path.")
         self.device = torch.device(device if device is not None else "cuda")
@@ -93,6 +96,8 @@ class QwenEngine:
         self.hidden_dim = self.cfg.hidden
         self.mlp_intermediate = self.cfg.intermediate
         self.max_batch = max_batch
+        # batches above this run the projections and LM head on the tensor-core GEMM
+        self.gemv_max_batch = gemv_max_batch
         self.use_graphs = use_graphs
         self.cache = PagedKVCache(self.cfg, self.layers, max_batch, max_seq_len, page_size,
                                   self.device, page_order=page_order)
@@ -102,7 +107,7 @@ class QwenEngine:
         self._graphs = {}
         # "persistent": one cooperative kernel per launch runs whole decode
         # steps (csrc/decode_persistent.cu, batch <= 4); "kernels": one kernel
-        # per stage, replayed as a CUDA graph (any batch <= 8).
+        # per stage, replayed as a CUDA graph (any batch).
         from .persistent import MAX_BATCH as PERSISTENT_MAX_BATCH
         if decoder is None:
             decoder = "persistent" if max_batch <= PERSISTENT_MAX_BATCH else "kernels"
@@ -128,10 +133,10 @@ class QwenEngine:
         self.buf_mlp = torch.zeros(B, c.intermediate, dtype=h, device=dev)
         # gate/up outputs of the tensor-core GEMM path (batches past the GEMV's 8)
         # fused gate|up GEMM output (batched path): [B, 2 * intermediate]
-        self.buf_up = torch.zeros(B if B > GEMV_MAX_BATCH else 1, 2 * c.intermediate, dtype=h, device=dev)
+        self.buf_up = torch.zeros(B if B > self.gemv_max_batch else 1, 2 * c.intermediate, dtype=h, device=dev)
         self.gemm_err = torch.zeros(1, dtype=torch.int32, device=dev)
         # split-K partial tiles of the small-m GEMMs (zero between calls)
-        ws = K.w4a16_gemm_workspace_size(B, c.intermediate) if B > GEMV_MAX_BATCH else 0
+        ws = K.w4a16_gemm_workspace_size(B, c.intermediate) if B > self.gemv_max_batch else 0
         self.gemm_ws = torch.zeros(ws + 256, dtype=torch.uint8, device=dev)
         off = (-self.gemm_ws.data_ptr()) % 256
         self.gemm_ws = self.gemm_ws[off:off + ws] if ws else None
@@ -173,7 +178,7 @@ class QwenEngine:
         c, w = self.cfg, self.weights
         x = self.buf_residual[:B]
         xn = self.buf_normed[:B]
-        gemm = B > GEMV_MAX_BATCH   # dense contraction: tcgen05 W4A16 GEMM
+        gemm = B > self.gemv_max_batch   # dense contraction: tcgen05 W4A16 GEMM
         for li, lw in enumerate(w.layers):
             kp, vp = self.cache.layer(li)
             K.rms_norm(x, lw.in_norm, c.eps, out=xn)
@@ -240,7 +245,7 @@ class QwenEngine:
     def _head(self, B: int, want_logits: bool) -> None:
         c, w = self.cfg, self.weights
         K.rms_norm(self.buf_residual[:B], w.final_norm, c.eps, out=self.buf_normed[:B])
-        if B > GEMV_MAX_BATCH:
+        if B > self.gemv_max_batch:
             K.w4a16_gemm(self.buf_normed[:B], w.lm_packed, w.lm_scales, c.vocab, c.hidden,
                          out=self.buf_logits[:B], error=self.gemm_err, workspace=self.gemm_ws)
             K.argmax_rows(self.buf_logits[:B], c.vocab, self.next_ids[:B])
@@ -337,7 +342,7 @@ class QwenEngine:
         # norm, q|k|v, RoPE + append + attention (+ split combine), o, norm,
         # gate/up (+ SwiGLU on the GEMM path), down; then embed, final norm, the
         # LM head with its argmax (two launches on either path), advance
-        gemm = self.batch > GEMV_MAX_BATCH
+        gemm = self.batch > self.gemv_max_batch
         per_layer = 7 + (1 if self.n_splits > 1 else 0) + (1 if gemm else 0)
         return 1 + self.layers * per_layer + 1 + 2 + 1
 

@@ -18,8 +18,9 @@ next token.  The collectives run on the process group handed in (NCCL over
 NVLink between GPUs; gloo for the host-side tests).
 
 With the peer exchange (two ranks) the LM head is split by vocabulary rows
-as well: rank r runs the Q4 head GEMV + first-index argmax over rows
-[r*V/2, (r+1)*V/2) only, and one exchange of (logit, global row) per
+as well: each rank runs the Q4 head (GEMV + first-index argmax, or GEMM +
+row argmax for larger batches) over its half of the rows only (the cut at a
+multiple of 128 rows near V/2), and one exchange of (logit, global row) per
 sequence picks the winner on both ranks (lmps_tp2_argmax_exchange), so the
 131 MB head is read once per step across the pair instead of on both GPUs
 (runners/engine.py:171-181 with the rows divided).
@@ -34,7 +35,7 @@ import torch.distributed as dist
 
 from . import kernels as K
 from .config import ModelConfig
-from .engine import GEMV_MAX_BATCH, QwenEngine
+from .engine import QwenEngine
 from .weights import LayerWeights, ModelWeights
 
 
@@ -98,7 +99,7 @@ class TPEngine(QwenEngine):
     through the peer's memory, so a step has no host-side collective and runs
     as a CUDA graph: the exchange kernel (:func:`kernels.tp2_allreduce_residual`)
     follows the o / down projection; with ``fuse_exchange=True`` the GEMV path
-    (batch <= 8) instead does projection, NVLink stores into the peer's
+    (batch <= gemv_max_batch) instead does projection, NVLink stores into the peer's
     buffer and residual add in one kernel (:func:`kernels.gemv_q4_tp2_residual`,
     its own call sites).  Dense prefill, whose partials are
     [tokens, hidden], keeps NCCL.  ``comm="nccl"``: every all-reduce is
@@ -135,7 +136,9 @@ class TPEngine(QwenEngine):
         self.split_head = self.exchange is not None
         if self.split_head:  # this rank's vocabulary rows of the tied Q4 head (views, no copy)
             c, w = self.cfg, self.weights
-            v0, v1 = rank * c.vocab // world, (rank + 1) * c.vocab // world
+            # split at a multiple of 128 rows: the GEMM path's row tiles
+            cut = (c.vocab // 2 + 64) // 128 * 128
+            v0, v1 = (0, cut) if rank == 0 else (cut, c.vocab)
             self._head_rows = (v0, v1)
             self._head_p = w.lm_packed[v0 * c.hidden // 2:v1 * c.hidden // 2]
             self._head_s = w.lm_scales[v0 * c.hidden // 32:v1 * c.hidden // 32]
@@ -163,16 +166,22 @@ class TPEngine(QwenEngine):
 
     def _head(self, B: int, want_logits: bool) -> None:
         """Final norm, LM head and argmax: split by vocabulary rows over the two
-        ranks when only the next ids are wanted (GEMV path); the replicated
-        head otherwise (full logits, or batches on the GEMM path)."""
-        if not (self.split_head and not want_logits and B <= GEMV_MAX_BATCH):
+        ranks when only the next ids are wanted (each rank's rows through the
+        GEMV + argmax, or for larger batches the GEMM + row argmax); the
+        replicated head when the full logits are wanted."""
+        if not (self.split_head and not want_logits):
             super()._head(B, want_logits)
             return
         c, w = self.cfg, self.weights
         v0, v1 = self._head_rows
         K.rms_norm(self.buf_residual[:B], w.final_norm, c.eps, out=self.buf_normed[:B])
-        K.lm_head_argmax(self._head_p, self._head_s, self.buf_normed[:B], v1 - v0, c.hidden,
-                         self.argmax_keys[:B], self._head_local[:B], logits=self._head_logits[:B])
+        if B > self.gemv_max_batch:
+            K.w4a16_gemm(self.buf_normed[:B], self._head_p, self._head_s, v1 - v0, c.hidden,
+                         out=self._head_logits[:B], error=self.gemm_err, workspace=self.gemm_ws)
+            K.argmax_rows(self._head_logits[:B], v1 - v0, self._head_local[:B])
+        else:
+            K.lm_head_argmax(self._head_p, self._head_s, self.buf_normed[:B], v1 - v0, c.hidden,
+                             self.argmax_keys[:B], self._head_local[:B], logits=self._head_logits[:B])
         K.tp2_argmax_exchange(self._head_logits[:B], self._head_local[:B], v0, self.next_ids[:B], self.exchange,
                               4 * c.n_layers, self.comm_err)
 
