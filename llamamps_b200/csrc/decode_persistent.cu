@@ -51,6 +51,10 @@ constexpr int kSlotBytes = 20160;
 constexpr int kRows1536 = 2 * kConsumerWarps;  // rows per ring chunk when k = hidden
 constexpr int kPairsGU = kConsumerWarps;    // gate/up row pairs per chunk
 constexpr int kRowsDown = 4;      // rows per chunk when k = intermediate
+// Batches of 2-4 (the tensor-core GEMV, see gemv_rows_mma): ring chunks of
+// 16 weight rows (one m16n8k32 tile; gate/up: 8 gate + 8 up rows); the down
+// projection's 16-row tile comes in k-parts of a few groups each.
+constexpr int kTileRows = 16;
 constexpr int kHD = 128;
 constexpr int kMaxG = 8;
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
@@ -144,6 +148,7 @@ struct Params {
   uint32_t* epoch;    // [1] tag base of the next launch
   int max_splits;
   int kv_pipe;        // 1: a second per-warp K buffer follows the attention area (long caches)
+  int mma;            // 1: batch > 1 -- the GEMV stages run on the tensor cores (16-row ring chunks)
 };
 
 enum StageKind { ST_QKV = 0, ST_O = 1, ST_GU = 2, ST_DN = 3, ST_HEAD = 4 };
@@ -188,7 +193,17 @@ struct Chunking {
   const uint8_t* w2;
   const __half* s2;
   int k, r0, r1, rows_per_chunk;
+  int kparts;  // tensor-core down projection: k-parts per 16-row tile (1 otherwise)
 };
+
+// k-parts of the down projection's 16-row tiles on the tensor-core path: the
+// fewest that keep a part's scales a multiple of 16 bytes and the part in a
+// ring slot.
+__host__ __device__ __forceinline__ int down_kparts(int groups) {
+  for (int kp = 1; kp <= groups; ++kp)
+    if (groups % kp == 0 && (groups / kp) % 8 == 0 && kTileRows * (groups / kp) * 18 <= kSlotBytes) return kp;
+  return 0;
+}
 
 __device__ __forceinline__ Chunking stage_chunks(const Params& P, int kind, int layer, int ctas) {
   Chunking c{};
@@ -196,25 +211,28 @@ __device__ __forceinline__ Chunking stage_chunks(const Params& P, int kind, int 
   int rows = 0;
   if (kind == ST_HEAD) {
     c.w = m.lm_packed; c.s = reinterpret_cast<const __half*>(m.lm_scales);
-    c.k = m.hidden; rows = m.vocab; c.rows_per_chunk = kRows1536;
+    c.k = m.hidden; rows = m.vocab; c.rows_per_chunk = P.mma ? kTileRows : kRows1536;
   } else {
     const lmps_layer_desc& L = m.layers[layer];
     if (kind == ST_QKV) {
       c.w = L.qkv_packed; c.s = reinterpret_cast<const __half*>(L.qkv_scales);
-      c.k = m.hidden; rows = (m.n_q_heads + 2 * m.n_kv_heads) * m.head_dim; c.rows_per_chunk = kRows1536;
+      c.k = m.hidden; rows = (m.n_q_heads + 2 * m.n_kv_heads) * m.head_dim;
+      c.rows_per_chunk = P.mma ? kTileRows : kRows1536;
     } else if (kind == ST_O) {
       c.w = L.o_packed; c.s = reinterpret_cast<const __half*>(L.o_scales);
-      c.k = m.n_q_heads * m.head_dim; rows = m.hidden; c.rows_per_chunk = kRows1536;
+      c.k = m.n_q_heads * m.head_dim; rows = m.hidden; c.rows_per_chunk = P.mma ? kTileRows : kRows1536;
     } else if (kind == ST_GU) {
       c.w = L.gate_packed; c.s = reinterpret_cast<const __half*>(L.gate_scales);
       c.w2 = L.up_packed; c.s2 = reinterpret_cast<const __half*>(L.up_scales);
-      c.k = m.hidden; rows = m.intermediate; c.rows_per_chunk = kPairsGU;
+      c.k = m.hidden; rows = m.intermediate; c.rows_per_chunk = P.mma ? kTileRows / 2 : kPairsGU;
     } else {
       c.w = L.down_packed; c.s = reinterpret_cast<const __half*>(L.down_scales);
-      c.k = m.intermediate; rows = m.hidden; c.rows_per_chunk = kRowsDown;
+      c.k = m.intermediate; rows = m.hidden; c.rows_per_chunk = P.mma ? kTileRows : kRowsDown;
+      if (P.mma) c.kparts = down_kparts(m.intermediate / kQ4Group);
     }
   }
   row_range(rows, blockIdx.x, ctas, c.r0, c.r1);
+  if (c.kparts == 0) c.kparts = 1;
   return c;
 }
 
@@ -248,7 +266,9 @@ __device__ void producer(const Params& P, Smem& S) {
       const uint32_t row_bytes = c.k / 2, row_sbytes = c.k / 16;
       const uint32_t ncopy = (kind == ST_GU) ? 2u : 1u;
       trace_event(P, gridDim.x + blockIdx.x, pev);
-      for (int r = c.r0; r < c.r1 && ok; r += c.rows_per_chunk, ++chunk) {
+      const int kparts = (kind == ST_DN) ? c.kparts : 1;
+      for (int ci = 0; ok && c.r0 + (ci / kparts) * c.rows_per_chunk < c.r1; ++ci, ++chunk) {
+        const int r = c.r0 + (ci / kparts) * c.rows_per_chunk, part = ci % kparts;
         const uint32_t n = min(c.rows_per_chunk, c.r1 - r);
         const int slot = pslot;
         const uint32_t phase = pphase;
@@ -269,6 +289,30 @@ __device__ void producer(const Params& P, Smem& S) {
         }
         // slot layout: packed rows [, second matrix's packed rows], scales [, second matrix's scales]
         unsigned char* dst = S.ring + static_cast<size_t>(slot) * kSlotBytes;
+        if (P.mma) {
+          // Tensor-core layout (batches 2-4): 16 tile rows at a padded stride
+          // (packed bytes + 16: the 8 rows one fragment load touches fall in
+          // different banks), then the rows' scales; gate/up: gate rows in
+          // tile rows 0-7, up rows in 8-15; the down projection one k-part.
+          const uint32_t pbr = row_bytes / kparts, sbr = row_sbytes / kparts, pbs = pbr + 16;
+          mbar_expect_tx(&S.full[slot], ncopy * n * (pbr + sbr));
+          for (uint32_t m2 = 0; m2 < ncopy; ++m2) {
+            const uint8_t* w = m2 ? c.w2 : c.w;
+            const unsigned char* sc = reinterpret_cast<const unsigned char*>(m2 ? c.s2 : c.s);
+            for (uint32_t i = 0; i < n; ++i) {
+              const uint32_t trow = m2 * (kTileRows / 2) + i;
+              bulk_g2s(dst + trow * pbs, w + static_cast<size_t>(r + i) * row_bytes + part * pbr, pbr, &S.full[slot],
+                       policy);
+              if (kparts > 1)
+                bulk_g2s(dst + kTileRows * pbs + trow * sbr, sc + static_cast<size_t>(r + i) * row_sbytes + part * sbr,
+                         sbr, &S.full[slot], policy);
+            }
+            if (kparts == 1)
+              bulk_g2s(dst + kTileRows * pbs + m2 * (kTileRows / 2) * sbr, sc + static_cast<size_t>(r) * row_sbytes,
+                       n * sbr, &S.full[slot], policy);
+          }
+          continue;
+        }
         const uint32_t pb = n * row_bytes, sb = n * row_sbytes;
         mbar_expect_tx(&S.full[slot], ncopy * (pb + sb));
         for (uint32_t i = 0; i < ncopy; ++i) {
@@ -457,10 +501,11 @@ __device__ __forceinline__ void consumer_sum_n(float (&v)[NB], float* red8) {
 // 4c..4c+3), Ho the odd elements 8c+1, 8c+3, 8c+5, 8c+7.
 // ---------------------------------------------------------------------------
 struct Planes {
-  uint32_t* w;  // [NB][G][16]
-  float* scl;   // [NB][G]   2^(e-15)
+  uint32_t* w;  // [NB][G][16]; the tensor-core path: [G][He, Le, Ho, Lo][NB][4]
+  float* scl;   // [NB][G]   2^(e-15) (tensor-core path: 2^(e-14))
   int* xs8;     // [NB][G]   8 * sum X
   int G;
+  int nb;
 };
 
 __device__ __forceinline__ Planes planes_view(Smem& S, int G, int nb) {
@@ -469,12 +514,18 @@ __device__ __forceinline__ Planes planes_view(Smem& S, int G, int nb) {
   pl.scl = reinterpret_cast<float*>(pl.w + static_cast<size_t>(nb) * G * 16);
   pl.xs8 = reinterpret_cast<int*>(pl.scl + nb * G);
   pl.G = G;
+  pl.nb = nb;
   return pl;
 }
 
 // Convert the 8 values v (elements 8c..8c+7 of group g, c = lane & 3; the 4
 // lanes of a group are consecutive) into their plane words.  Every lane of the
 // warp must call this (shuffles); `active` marks lanes holding real data.
+// S8 (the tensor-core path of batches 2-4): X = rint(x * 2^(14-e)) and both
+// planes signed bytes, L = ((X + 128) & 255) - 128, H = (X - L) / 256, so a
+// signed 8-bit mma multiplies them (|X| <= 2^14, |H| <= 64); the scale word
+// is then 2^(e-14).  Otherwise X = rint(x * 2^(15-e)) with an unsigned L.
+template <bool S8 = false>
 __device__ __forceinline__ void store_planes(const float (&v)[8], bool active, const Planes& pl,
                                              int b, int g) {
   float mx = 0.0f;
@@ -485,12 +536,20 @@ __device__ __forceinline__ void store_planes(const float (&v)[8], bool active, c
   // frexp exponent: mx = f * 2^e, f in [0.5, 1); e = 0 for mx == 0
   const int ebits = (__float_as_int(mx) >> 23) & 0xFF;
   const int e = (mx > 0.0f) ? ebits - 126 : 0;
-  const float q = __int_as_float((127 + 15 - e) << 23);   // 2^(15-e)
+  constexpr int kFrac = S8 ? 14 : 15;
+  const float q = __int_as_float((127 + kFrac - e) << 23);   // 2^(kFrac-e)
   int X[8], sx = 0;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     int xi = __float2int_rn(v[i] * q);
     xi = max(-32768, min(32767, xi));
+    if constexpr (S8) {  // H * 256 + L with L in [-128, 127]: store L and H as bytes
+      const int lo = ((xi + 128) & 255) - 128;
+      sx += xi;
+      xi = ((xi - lo) / 256) * 256 + (lo & 255);  // same byte layout as 256 H + L below
+      X[i] = xi;
+      continue;
+    }
     X[i] = xi;
     sx += xi;
   }
@@ -503,14 +562,22 @@ __device__ __forceinline__ void store_planes(const float (&v)[8], bool active, c
     const uint32_t le = __byte_perm(pe0, pe1, 0x5410), he = __byte_perm(pe0, pe1, 0x7632);
     const uint32_t lo = __byte_perm(po0, po1, 0x5410), ho = __byte_perm(po0, po1, 0x7632);
     const int c = threadIdx.x & 3;
-    const int sw = (g >> 1) & 3;  // quad swizzle, see load_xgroup
-    uint32_t* gw = pl.w + (static_cast<size_t>(b) * pl.G + g) * 16;
-    gw[4 * (0 ^ sw) + c] = he;
-    gw[4 * (1 ^ sw) + c] = ho;
-    gw[4 * (2 ^ sw) + c] = le;
-    gw[4 * (3 ^ sw) + c] = lo;
+    if constexpr (S8) {  // [g][He, Le, Ho, Lo][sequence][word]: one B fragment row per lane, no conflicts
+      uint32_t* gw = pl.w + static_cast<size_t>(g) * 16 * pl.nb + 4 * b + c;
+      gw[0] = he;
+      gw[4 * pl.nb] = le;
+      gw[8 * pl.nb] = ho;
+      gw[12 * pl.nb] = lo;
+    } else {
+      const int sw = (g >> 1) & 3;  // quad swizzle, see load_xgroup
+      uint32_t* gw = pl.w + (static_cast<size_t>(b) * pl.G + g) * 16;
+      gw[4 * (0 ^ sw) + c] = he;
+      gw[4 * (1 ^ sw) + c] = ho;
+      gw[4 * (2 ^ sw) + c] = le;
+      gw[4 * (3 ^ sw) + c] = lo;
+    }
     if (c == 0) {
-      pl.scl[b * pl.G + g] = __int_as_float((127 + e - 15) << 23);  // 2^(e-15)
+      pl.scl[b * pl.G + g] = __int_as_float((127 + e - kFrac) << 23);  // 2^(e-kFrac)
       pl.xs8[b * pl.G + g] = 8 * sx;
     }
   }
@@ -574,7 +641,7 @@ __device__ void stage_norm(const Params& P, Smem& S, const __half* const (&rows)
       const __half nrm = __float2half_rn(__half2float(xh[e]) * scale);
       nv[e] = __half2float(__float2half_rn(__half2float(nrm) * __half2float(gh[e])));
     }
-    store_planes(nv, active, pl, b, c >> 2);
+    store_planes<(NB > 1)>(nv, active, pl, b, c >> 2);
   }
   consumer_sync();
 }
@@ -608,7 +675,7 @@ __device__ void stage_copy(const Params& P, Smem& S, const unsigned long long* s
       float f[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) f[e] = __half2float(h[e]);
-      store_planes(f, active, pl, active ? b : 0, c >> 2);
+      store_planes<(NB > 1)>(f, active, pl, active ? b : 0, c >> 2);
 #pragma unroll
       for (int j = 0; j + 1 < kBatch; ++j) t[j] = t[j + 1];
     }
@@ -857,6 +924,213 @@ __device__ void gemv_rows(const Params& P, Smem& S, CState& cs, int kind, int la
     const uint32_t hp = __shfl_down_sync(0xffffffffu, hb, 4);  // the pair's second row
     if (row_lane && (i & 1) == 0)
       st_tagged(dst + static_cast<size_t>(b) * dld + (c.r0 + i) / 2, tagged(tag, hb | (hp << 16)));
+  }
+  consumer_sync();  // the partials' area is the next stage's staging area
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core GEMV stages for batches 2-4: mma.sync m16n8k32, s8 x s8 -> s32.
+// A = 16 weight rows x one 32-element group as bytes (the nibbles 0..15): a
+// lane's 32-bit word t of a row's group holds 8 nibbles, the even ones are
+// fragment k 4t..4t+3 and the odd ones k 16+4t..16+4t+3 -- the element order
+// of the activation planes' He / Ho words, so both fragments come straight
+// from shared memory.  B = the planes of the same group, column 2s = H and
+// 2s+1 = L of sequence s.  Per group the int32 results give each sequence's
+// exact dot 256 H + L - 8 sum X (4-bit codes times 15-bit fixed point),
+// scaled into fp32 by the row's scale and the group's 2^(e-14).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// The ring state `n` chunks after `c`.
+__device__ __forceinline__ CState cs_after(const Params& P, CState c, int n) {
+  const int t = c.slot + n;
+  if ((t / P.slots) & 1) c.phase ^= 1u;
+  c.slot = t % P.slots;
+  return c;
+}
+
+// acc0 / acc1 += the group dots of tile rows g / g + 8 with sequence t's
+// activation group gx (plane group index) -- one mma and its per-group scaling.
+template <int NB>
+__device__ __forceinline__ void tile_group(const Planes& pl, const unsigned char* wa, const unsigned char* wb,
+                                           float sa, float sb, int gx, float& acc0, float& acc1) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int seq = g >> 1, plane = g & 1;
+  const uint32_t w0 = *reinterpret_cast<const uint32_t*>(wa + 4 * t);
+  const uint32_t w1 = *reinterpret_cast<const uint32_t*>(wb + 4 * t);
+  const uint32_t* pw = pl.w + static_cast<size_t>(gx) * 16 * NB + 4 * seq + t;
+  uint32_t b0 = 0u, b1 = 0u;
+  if (seq < NB) {
+    b0 = pw[4 * NB * plane];          // He / Le
+    b1 = pw[4 * NB * (2 + plane)];    // Ho / Lo
+  }
+  int d[4];
+  mma_s8_16832(d, w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, (w0 >> 4) & 0x0F0F0F0Fu, (w1 >> 4) & 0x0F0F0F0Fu, b0, b1);
+  const int ts = t < NB ? t : 0;  // columns 2t, 2t+1: sequence t
+  const float xsc = pl.scl[ts * pl.G + gx];
+  const int xs = pl.xs8[ts * pl.G + gx];
+  acc0 = fmaf(sa * xsc, static_cast<float>(256 * d[0] + d[1] - xs), acc0);
+  acc1 = fmaf(sb * xsc, static_cast<float>(256 * d[2] + d[3] - xs), acc1);
+}
+
+// Row GEMVs with k = hidden (q|k|v, o, gate/up, LM head) for batches 2-4:
+// each warp takes whole 16-row ring chunks (chunk i of the stage goes to
+// warp i mod min(warps, slots), which releases its slot alone) and runs all groups of
+// its tile, so a lane ends with the dots of tile rows g and g + 8 for
+// sequence t and applies the stage's epilogue itself -- gate/up tiles hold
+// 8 gate and the matching 8 up rows, so SwiGLU needs no exchange either.
+template <int NB>
+__device__ void gemv_rows_mma(const Params& P, Smem& S, CState& cs, int kind, int layer, __half* logits,
+                              uint32_t tag, const Chunking& c) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int G = c.k / 32;
+  const bool gu = kind == ST_GU, head = kind == ST_HEAD;
+  const int rpc = c.rows_per_chunk;
+  const int nch = (c.r1 - c.r0 + rpc - 1) / rpc;
+  const size_t pbs = c.k / 2 + 16;
+  const Planes pl = planes_view(S, G, NB);
+  const int B = P.s.batch;
+  unsigned long long best = 0ull;  // LM head: this lane's sequence t
+  const CState base = cs;
+  unsigned long long wns = cs.wait_ns;  // warp 0's ring waits (timeline only)
+  unsigned long long* dst = kind == ST_QKV ? P.qkvt : kind == ST_O ? P.x1t : P.at;
+  const int dld = kind == ST_QKV ? (P.m.n_q_heads + 2 * P.m.n_kv_heads) * kHD / 2
+                                 : (kind == ST_O ? P.m.hidden : P.m.intermediate) / 2;
+  // At most `slots` warps take chunks: a warp then only ever waits on a chunk
+  // whose slot's previous contents (the chunk `slots` earlier) it has seen
+  // land already (its own previous chunk is no older), so the full barrier's
+  // parity cannot match a phase two fills old.
+  const int nw = min(kConsumerWarps, P.slots);
+  for (int ch = warp; warp < nw && ch < nch; ch += nw) {
+    CState my = cs_after(P, base, ch);
+    my.wait_ns = wns;
+    slot_wait(S, P, my);
+    wns = my.wait_ns;
+    const int r = c.r0 + ch * rpc;
+    const int n = min(rpc, c.r1 - r);
+    const unsigned char* sl = S.ring + static_cast<size_t>(my.slot) * kSlotBytes;
+    const __half* sc = reinterpret_cast<const __half*>(sl + kTileRows * pbs);
+    const unsigned char* wa = sl + g * pbs;
+    const unsigned char* wb = sl + (g + 8) * pbs;
+    const __half* sa = sc + g * G;
+    const __half* sb = sc + (g + 8) * G;
+    float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll 4
+    for (int grp = 0; grp < G; ++grp)
+      tile_group<NB>(pl, wa + grp * 16, wb + grp * 16, __half2float(sa[grp]), __half2float(sb[grp]), grp, acc0, acc1);
+    __syncwarp();
+    if (lane == 0)
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&S.empty[my.slot])),
+                   "r"(kConsumerWarps)
+                   : "memory");
+    // -- epilogue of the tile: rows (g, g + 8); gate/up: gate row g, up row g
+    const int i0 = r - c.r0 + g;  // row of the stage (gate/up: pair) held in acc0
+    const bool v0 = g < n, v1 = gu ? g < n : g + 8 < n;
+    const bool lt = t < B;
+    if (head) {
+      if (lt) {
+        if (v0) {
+          const __half h = __float2half_rn(acc0);
+          if (logits) logits[static_cast<size_t>(t) * P.m.vocab + r + g] = h;
+          best = u64_max(best, argmax_key(__half2float(h), static_cast<uint32_t>(r + g)));
+        }
+        if (v1) {
+          const __half h = __float2half_rn(acc1);
+          if (logits) logits[static_cast<size_t>(t) * P.m.vocab + r + g + 8] = h;
+          best = u64_max(best, argmax_key(__half2float(h), static_cast<uint32_t>(r + g + 8)));
+        }
+      }
+      continue;
+    }
+    __half h0, h1;
+    if (gu) {
+      h0 = __float2half_rn(silu_mul(__half2float(__float2half_rn(acc0)), __half2float(__float2half_rn(acc1))));
+      h1 = h0;
+    } else if (kind == ST_QKV) {
+      h0 = __float2half_rn(acc0 + __half2float(S.bias_own[layer * kOwnMax + min(i0, kOwnMax - 1)]));
+      h1 = __float2half_rn(acc1 + __half2float(S.bias_own[layer * kOwnMax + min(i0 + 8, kOwnMax - 1)]));
+    } else {  // ST_O
+      const int tb = lt ? t : 0;
+      h0 = __hadd(S.xown[tb * kOwnMax + min(i0, kOwnMax - 1)], __float2half_rn(acc0));
+      h1 = __hadd(S.xown[tb * kOwnMax + min(i0 + 8, kOwnMax - 1)], __float2half_rn(acc1));
+      if (lt && v0) S.x1own[t * kOwnMax + i0] = h0;
+      if (lt && v1) S.x1own[t * kOwnMax + i0 + 8] = h1;
+    }
+    // pairs (g, g + 1) for even g: the partner row is in lane + 4
+    const uint32_t b0 = __half_as_ushort(h0), b1 = __half_as_ushort(h1);
+    const uint32_t p0 = __shfl_down_sync(0xffffffffu, b0, 4), p1 = __shfl_down_sync(0xffffffffu, b1, 4);
+    if (lt && (g & 1) == 0) {
+      unsigned long long* row = dst + static_cast<size_t>(t) * dld;
+      if (v0) st_tagged(row + (r + g) / 2, tagged(tag, b0 | (p0 << 16)));
+      if (!gu && v1) st_tagged(row + (r + g + 8) / 2, tagged(tag, b1 | (p1 << 16)));
+    }
+  }
+  cs = cs_after(P, base, nch);
+  cs.wait_ns = wns;
+  trace_mid(P, cs);
+  if (head) {  // per sequence over the warp's lanes (same t), then one slot per warp
+    best = u64_max(best, __shfl_xor_sync(0xffffffffu, best, 4));
+    best = u64_max(best, __shfl_xor_sync(0xffffffffu, best, 8));
+    best = u64_max(best, __shfl_xor_sync(0xffffffffu, best, 16));
+    if (lane < kMaxB) S.best[warp * kMaxB + lane] = lane < NB ? best : 0ull;
+    return;
+  }
+  consumer_sync();  // the planes' area is the next stage's staging area
+}
+
+// Down projection (k = intermediate) for batches 2-4: the CTA's hidden rows
+// (<= 16) are one tile; its k-parts arrive as ring chunks every warp reads,
+// warp w taking groups w, w + warps, .. of each part; the warps' fp32
+// partials meet in shared memory: x = x1 + fp16(sum).
+template <int NB>
+__device__ void gemv_down_mma(const Params& P, Smem& S, CState& cs, uint32_t tag, const Chunking& c) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int G = c.k / 32, Gp = G / c.kparts;
+  const size_t pbs = static_cast<size_t>(Gp) * 16 + 16;
+  const Planes pl = planes_view(S, G, NB);
+  const int n = c.r1 - c.r0;  // <= kTileRows (host-checked)
+  float acc0 = 0.0f, acc1 = 0.0f;
+  for (int part = 0; part < c.kparts; ++part) {
+    const int slot = cs.slot;
+    slot_wait(S, P, cs);
+    const unsigned char* sl = S.ring + static_cast<size_t>(slot) * kSlotBytes;
+    const __half* sc = reinterpret_cast<const __half*>(sl + kTileRows * pbs);
+    for (int j = warp; j < Gp; j += kConsumerWarps)
+      tile_group<NB>(pl, sl + g * pbs + j * 16, sl + (g + 8) * pbs + j * 16, __half2float(sc[g * Gp + j]),
+                     __half2float(sc[(g + 8) * Gp + j]), part * Gp + j, acc0, acc1);
+    slot_release(S, P, cs);
+  }
+  trace_mid(P, cs);
+  // warp partials: red[warp][row][sequence] after the planes
+  float* red = reinterpret_cast<float*>(pl.xs8 + NB * G);
+  if (t < NB) {
+    red[(warp * kTileRows + g) * kMaxB + t] = acc0;
+    red[(warp * kTileRows + g + 8) * kMaxB + t] = acc1;
+  }
+  consumer_sync();
+  const int pairs = n / 2;
+  for (int q = threadIdx.x; q < NB * pairs; q += kConsumers) {
+    const int b = q / pairs, i = 2 * (q - b * pairs);
+    if (b >= P.s.batch) break;
+    float s0 = 0.0f, s1 = 0.0f;
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      s0 += red[(w * kTileRows + i) * kMaxB + b];
+      s1 += red[(w * kTileRows + i + 1) * kMaxB + b];
+    }
+    const __half h0 = __hadd(S.x1own[b * kOwnMax + i], __float2half_rn(s0));
+    const __half h1 = __hadd(S.x1own[b * kOwnMax + i + 1], __float2half_rn(s1));
+    S.xown[b * kOwnMax + i] = h0;
+    S.xown[b * kOwnMax + i + 1] = h1;
+    st_tagged(P.xt + static_cast<size_t>(b) * (P.m.hidden / 2) + (c.r0 + i) / 2,
+              tagged(tag, static_cast<uint32_t>(__half_as_ushort(h0)) |
+                              (static_cast<uint32_t>(__half_as_ushort(h1)) << 16)));
   }
   consumer_sync();  // the partials' area is the next stage's staging area
 }
@@ -1639,10 +1913,16 @@ __device__ void consumer(const Params& P, Smem& S, uint32_t epoch) {
         }
         trace_mid(P, cs);
       } else if (kind == K_DN) {
-        gemv_down<NB>(P, S, cs, l, tag, ch);
+        if constexpr (NB > 1)
+          gemv_down_mma<NB>(P, S, cs, tag, ch);
+        else
+          gemv_down<NB>(P, S, cs, l, tag, ch);
       } else {
         __half* lg = (kind == K_HEAD && step == P.n_steps - 1) ? reinterpret_cast<__half*>(P.s.logits) : nullptr;
-        gemv_rows<NB>(P, S, cs, wk, l, lg, tag, ch);
+        if constexpr (NB > 1)
+          gemv_rows_mma<NB>(P, S, cs, wk, l, lg, tag, ch);
+        else
+          gemv_rows<NB>(P, S, cs, wk, l, lg, tag, ch);
         if (kind == K_HEAD) {
           consumer_sync();
           if (threadIdx.x < B) {
@@ -1839,6 +2119,8 @@ static int launch(const Params& P0, const lmps_model_desc& m, cudaStream_t st) {
   const int proj_ctas = sms - kMaxAttCtas;
   if (proj_ctas < 1) return LMPS_ERR_UNSUPPORTED;
   auto per_cta = [&](int rows) { return 2 * ((rows / 2 + proj_ctas - 1) / proj_ctas); };
+  // tensor-core path: a CTA's hidden rows are one 16-row tile of the down projection
+  if (P.mma && per_cta(m.hidden) > kTileRows) return LMPS_ERR_UNSUPPORTED;
   if (per_cta(m.hidden) > kOwnMax || per_cta(qkv_rows) > kOwnMax || per_cta(m.intermediate) > kOutMax ||
       m.n_layers > kMaxLayers || sms > kMaxGrid || m.vocab > 0x40000 || 2 * kConsumers < sms * kMaxB)
     return LMPS_ERR_UNSUPPORTED;
@@ -1928,6 +2210,9 @@ extern "C" int lmps_decode_persistent(const lmps_model_desc* model, const lmps_d
   // long caches: the attention items hold many blocks per warp, worth a
   // second K buffer (and two fewer ring slots)
   P.kv_pipe = s.max_seq_len > 2048 ? 1 : 0;
+  // batches of 2-4: the GEMV stages on the tensor cores (16-row tiles)
+  P.mma = s.batch > 1 ? 1 : 0;
+  if (P.mma && pk::down_kparts(m.intermediate / 32) == 0) return LMPS_ERR_UNSUPPORTED;
   cudaStream_t st = lmps_stream(stream);
   switch (s.batch) {
     case 1: return pk::launch<1>(P, m, st);
