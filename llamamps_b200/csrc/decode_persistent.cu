@@ -147,7 +147,6 @@ struct Params {
   uint32_t* att_cnt;  // [kMaxB, Hkv] split arrivals (reset by the last split)
   uint32_t* epoch;    // [1] tag base of the next launch
   int max_splits;
-  int kv_pipe;        // 1: a second per-warp K buffer follows the attention area (long caches)
   int mma;            // 1: batch > 1 -- the GEMV stages run on the tensor cores (16-row ring chunks)
 };
 
@@ -250,8 +249,23 @@ __device__ __forceinline__ void trace_event(const Params& P, int row, int& ev,
 }
 
 // ---------------------------------------------------------------------------
-// Producer: one lane streams every chunk of every stage into the ring.
+// Producer: one lane streams every chunk of every stage into the ring (TMA
+// bulk copies): the weight rows of the projections and, with attention
+// spread over the CTAs, the cached K/V rows of the attention stages.
 // ---------------------------------------------------------------------------
+__device__ bool produce_kv(const Params& P, Smem& S, int layer, int step, uint32_t& chunk, int& pslot,
+                           uint32_t& pphase);
+
+// Wait until the consumers released ring slot `slot` from its previous fill
+// (chunk - slots).
+__device__ __forceinline__ bool acquire_slot(const Params& P, Smem& S, uint32_t chunk, int slot, uint32_t phase) {
+  if (chunk < static_cast<uint32_t>(P.slots)) return true;
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(&S.empty[slot], phase ^ 1u))
+    if (*reinterpret_cast<volatile int*>(&S.misc[0]) || globaltimer() - t0 > kTimeoutNs) return false;
+  return true;
+}
+
 __device__ void producer(const Params& P, Smem& S) {
   const uint64_t policy = evict_first_policy();
   uint32_t chunk = 0, pphase = 0;
@@ -262,6 +276,11 @@ __device__ void producer(const Params& P, Smem& S) {
   for (int step = 0; step < P.n_steps && ok; ++step) {
     for (int st = 0; st < n_stages && ok; ++st) {
       const int kind = (st == n_stages - 1) ? ST_HEAD : (st & 3);
+      // spread attention sits between a layer's q|k|v and o chunks
+      if (kind == ST_O && S.n_att == 0 && !produce_kv(P, S, st >> 2, step, chunk, pslot, pphase)) {
+        ok = false;
+        break;
+      }
       const Chunking c = stage_chunks(P, kind, st >> 2, S.gemv_grid);
       const uint32_t row_bytes = c.k / 2, row_sbytes = c.k / 16;
       const uint32_t ncopy = (kind == ST_GU) ? 2u : 1u;
@@ -276,16 +295,9 @@ __device__ void producer(const Params& P, Smem& S) {
           pslot = 0;
           pphase ^= 1u;
         }
-        // wait until the consumers released this slot's previous contents
-        if (chunk >= static_cast<uint32_t>(P.slots)) {
-          const uint64_t t0 = globaltimer();
-          while (!mbar_try_wait(&S.empty[slot], phase ^ 1u)) {
-            if (*reinterpret_cast<volatile int*>(&S.misc[0]) || globaltimer() - t0 > kTimeoutNs) {
-              ok = false;
-              break;
-            }
-          }
-          if (!ok) break;
+        if (!acquire_slot(P, S, chunk, slot, phase)) {
+          ok = false;
+          break;
         }
         // slot layout: packed rows [, second matrix's packed rows], scales [, second matrix's scales]
         unsigned char* dst = S.ring + static_cast<size_t>(slot) * kSlotBytes;
@@ -1210,13 +1222,15 @@ __device__ void gemv_down(const Params& P, Smem& S, CState& cs, int layer, uint3
 //   S^T  = K Q^T   (M = 16 positions, N = 8 heads, K = 128 dims)   attention.metal:32-40
 //   O^T += V^T P^T (M = 16 dims per m-tile, N = 8 heads, K = 16 positions)   attn_sum.metal:26-32
 // Both products sum over dims or positions, so the order of the dims inside
-// them is free: logical dim (k-step ks, fragment column 2t+e, upper half +8)
-// is physical dim 32t + 4ks + e (+2), and output row r of m-tile mt is
-// physical dim 32(r>>1 & 3) + 4mt + 2(r>>3) + (r&1).  Every lane's K and V
-// operands are then one contiguous 64-byte run of a cache row (four 16-byte
-// loads), and movmatrix transposes V rows and probabilities in registers.
+// them is free: fragment word w (k-step w >> 1) of lane t holds physical
+// dims 8t + 32(w >> 2) + 2(w & 3) + {0, 1}, so every lane's K and V operands
+// are four 16-byte runs of a cache row (runs t, t + 4, t + 8, t + 12), and
+// output row r of m-tile mt is physical dim
+// 8((r & 7) >> 1) + 32(mt >> 1) + 4(mt & 1) + 2(r >> 3) + (r & 1);
+// movmatrix transposes V rows and probabilities in registers.
 constexpr int kBlk = 16;        // positions per warp block
 constexpr int kMinSplit = 512;  // positions per work item before the positions split across CTAs
+constexpr int kKvSlotPos = 2 * kBlk;  // positions per ring slot (spread attention): K and V tiles, 16 KB
 
 struct AttnSmem {
   __half raw[(kMaxG + 2) * kHD];          // polled q heads, k, v (before RoPE)
@@ -1224,10 +1238,7 @@ struct AttnSmem {
   __half q[kMaxG][kHD];                   // rotated q, natural dim order
   float wm[kConsumerWarps][kMaxG];        // per-warp running max and sum (then merge weights)
   float wl[kConsumerWarps][kMaxG];
-  union {
-    float wo[kConsumerWarps][32][32];     // per-warp unnormalised O^T fragments, [lane][value, rotated by 4*lane]
-    uint4 kst[kConsumerWarps][8][32];     // K rows of each warp's first block, [chunk][lane] (cp.async)
-  };
+  float wo[kConsumerWarps][32][32];       // per-warp unnormalised O^T fragments, [lane][value, rotated by 4*lane]
   int is_last;
 };
 
@@ -1281,20 +1292,104 @@ __device__ __forceinline__ void rope_pair(int j, int style, int& i1, int& i2) {
 
 // Shared-memory K/V tiles of the dedicated attention CTAs: per 16-position
 // block, K then V, each [chunk 4*h2 + c][lane 4*g8 + t4] of 16 bytes = dims
-// 32*t4 + 8*c .. +7 of row 8*h2 + g8 (the lanes' mma operand runs).
+// 8*t4 + 32*c .. +7 of row 8*h2 + g8 (the lanes' mma operand runs).
 constexpr int kKvTileBytes = 2 * 8 * 32 * 16;  // K and V of one block: 8 KB
 constexpr int kMaxAttCtas = 8;
 __device__ __forceinline__ int kv_tile_idx(int blk, int kv, int h2, int c, int lane) {
   return ((blk * 2 + kv) * 8 + 4 * h2 + c) * 32 + lane;
 }
 __device__ __forceinline__ __half& tile_half(uint4* kvs, int rel, int kv, int d) {
-  uint4& u = kvs[kv_tile_idx(rel >> 4, kv, (rel >> 3) & 1, (d >> 3) & 3, 4 * (rel & 7) + (d >> 5))];
+  uint4& u = kvs[kv_tile_idx(rel >> 4, kv, (rel >> 3) & 1, d >> 5, 4 * (rel & 7) + ((d >> 3) & 3))];
   return reinterpret_cast<__half*>(&u)[d & 7];
+}
+
+// One 16-position block of a warp's flash loop from shared memory (block
+// bi; first position p0; positions >= end are masked and their V rows read
+// as zero): S^T = K Q^T, the online softmax of heads 2*t4, 2*t4+1,
+// O^T = O^T * alpha + V^T P^T.  kRows: K rows [32][head_dim] then V rows
+// (a ring slot, as in the cache), read conflict-free -- at load c the lanes
+// of even rows take their run c and those of odd rows run c ^ 1, which fall
+// in the other half of the banks, and swap back in registers; otherwise
+// the lane tiles of kv_tile_idx.
+template <bool kRows>
+__device__ __forceinline__ void flash_block(const uint4* tiles, int bi, int p0, int end, const uint32_t (&qf)[16],
+                                            float (&o)[8][4], float& mrun0, float& mrun1, float& lrun0,
+                                            float& lrun1) {
+  const int lane = threadIdx.x & 31, g8 = lane >> 2, t4 = lane & 3;
+  uint4 kr[2][4], vr[2][4];
+#pragma unroll
+  for (int h2 = 0; h2 < 2; ++h2) {
+    const bool ok = p0 + 8 * h2 + g8 < end;
+    if constexpr (kRows) {
+      const int odd = g8 & 1;
+      const uint4* krow = tiles + (kBlk * bi + 8 * h2 + g8) * (kHD / 8);
+      const uint4* vrow = krow + kKvSlotPos * (kHD / 8);
+      uint4 tk[4], tv[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        tk[c] = krow[t4 + 4 * (c ^ odd)];
+        tv[c] = ok ? vrow[t4 + 4 * (c ^ odd)] : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        kr[h2][c] = odd ? tk[c ^ 1] : tk[c];
+        vr[h2][c] = odd ? tv[c ^ 1] : tv[c];
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        kr[h2][c] = tiles[kv_tile_idx(bi, 0, h2, c, lane)];
+        vr[h2][c] = ok ? tiles[kv_tile_idx(bi, 1, h2, c, lane)] : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+  }
+  // S^T = K Q^T
+  float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int ks = 0; ks < kHD / 16; ++ks)
+    mma_16816(s, word_of(kr[0], 2 * ks), word_of(kr[1], 2 * ks), word_of(kr[0], 2 * ks + 1),
+              word_of(kr[1], 2 * ks + 1), qf[2 * ks], qf[2 * ks + 1]);
+  const bool v0 = p0 + g8 < end, v1 = p0 + 8 + g8 < end;
+  s[0] = v0 ? s[0] * kAttnScale : -INFINITY;
+  s[1] = v0 ? s[1] * kAttnScale : -INFINITY;
+  s[2] = v1 ? s[2] * kAttnScale : -INFINITY;
+  s[3] = v1 ? s[3] * kAttnScale : -INFINITY;
+  // online softmax per head (columns 2*t4, 2*t4+1; positions over g8 and the two row halves)
+  float mx0 = fmaxf(s[0], s[2]), mx1 = fmaxf(s[1], s[3]);
+#pragma unroll
+  for (int ofs = 4; ofs < 32; ofs <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, ofs));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, ofs));
+  }
+  const float mn0 = fmaxf(mrun0, mx0), mn1 = fmaxf(mrun1, mx1);  // finite: position p0 is valid
+  const float al0 = expf(mrun0 - mn0), al1 = expf(mrun1 - mn1);
+  const float e0 = expf(s[0] - mn0), e1 = expf(s[1] - mn1), e2 = expf(s[2] - mn0), e3 = expf(s[3] - mn1);
+  float su0 = e0 + e2, su1 = e1 + e3;
+#pragma unroll
+  for (int ofs = 4; ofs < 32; ofs <<= 1) {
+    su0 += __shfl_xor_sync(0xffffffffu, su0, ofs);
+    su1 += __shfl_xor_sync(0xffffffffu, su1, ofs);
+  }
+  lrun0 = lrun0 * al0 + su0;
+  lrun1 = lrun1 * al1 + su1;
+  mrun0 = mn0;
+  mrun1 = mn1;
+  // O^T = O^T * alpha + V^T P^T
+  const uint32_t pb0 = movmatrix_t(pack_half2(e0, e1)), pb1 = movmatrix_t(pack_half2(e2, e3));
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    o[mt][0] *= al0;
+    o[mt][2] *= al0;
+    o[mt][1] *= al1;
+    o[mt][3] *= al1;
+    mma_16816(o[mt], movmatrix_t(word_of(vr[0], 2 * mt)), movmatrix_t(word_of(vr[0], 2 * mt + 1)),
+              movmatrix_t(word_of(vr[1], 2 * mt)), movmatrix_t(word_of(vr[1], 2 * mt + 1)), pb0, pb1);
+  }
 }
 
 __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, int kvh,
                           int split, int n_splits, int chunk, int pos, uint32_t in_tag, uint32_t out_tag,
-                          uint4* kvs) {
+                          uint4* kvs, CState* ring) {
   AttnSmem& A = *reinterpret_cast<AttnSmem*>(S.act);
   const lmps_model_desc& m = P.m;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1312,34 +1407,11 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
   const bool has_pos = pos >= start && pos < end;
   const uint64_t kvpol = evict_last_policy();
 
-  // Cache rows of positions < pos do not depend on this step's q|k|v: every
-  // warp loads the K/V rows of its first block into registers before anything
-  // waits (the row of pos itself is appended below and read after the sync).
+  // Where the cached K/V rows come from: the caller's shared-memory tiles
+  // (dedicated attention CTAs, kvs), or ring slots of 32 positions that the
+  // producer warp fills while the q|k|v stage runs (produce_kv); the row of
+  // pos itself is appended below and patched into its tile after the sync.
   const int nblk = (end - start + kBlk - 1) / kBlk;
-  auto row_off = [&](int p) {
-    return ((static_cast<size_t>(__ldg(bt + (p >> pshift))) * Hkv + kvh) * ps + (p & (ps - 1))) * kHD + 32 * t4;
-  };
-  // The K rows (p0+g8, p0+8+g8; dims 32*t4 ..) of every warp's first block
-  // go to shared memory through cp.async before anything waits (no registers
-  // held across the waits); the V rows are prefetched into L2.  The row of
-  // pos itself is appended below and read after the sync.
-  // (kvs: the caller staged every K/V row before pos in shared-memory tiles)
-  if (!kvs && warp < nblk) {
-#pragma unroll
-    for (int h2 = 0; h2 < 2; ++h2) {
-      const int p = start + warp * kBlk + 8 * h2 + g8;
-      if (p < end && p != pos) {
-        const size_t off = row_off(p);
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(&A.kst[warp][4 * h2 + c][lane])),
-                       "l"(kpool + off + 8 * c)
-                       : "memory");
-        asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(vpool + off));
-      }
-    }
-  }
-  asm volatile("cp.async.commit_group;" ::: "memory");  // (its own group: the flash loop counts them)
   // cache offset of position pos (the KV append of the split holding it)
   const size_t app =
       has_pos ? ((static_cast<size_t>(__ldg(bt + (pos >> pshift))) * Hkv + kvh) * ps + (pos & (ps - 1))) * kHD : 0;
@@ -1383,7 +1455,7 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
         st_kv8((kind == 1 ? kpool : vpool) + app + 8 * c8, v, kvpol);
         if (kvs) {  // and into its tile: row pos, dims 8*c8 .. (lane (pos & 7, c8 / 4), chunk c8 % 4)
           const int rel = pos - start;
-          kvs[kv_tile_idx(rel >> 4, kind - 1, (rel >> 3) & 1, c8 & 3, 4 * (rel & 7) + (c8 >> 2))] = v;
+          kvs[kv_tile_idx(rel >> 4, kind - 1, (rel >> 3) & 1, c8 >> 2, 4 * (rel & 7) + (c8 & 3))] = v;
         }
       }
     }
@@ -1425,19 +1497,12 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
   // rotated q in shared memory, the new k/v row in the cache
 
   // -- per-warp flash loop over 16-position blocks
-  // Long items (kv_pipe, more blocks than warps): a warp's K rows are
-  // double-buffered in shared memory -- block j+1's rows are copied
-  // (cp.async) while block j computes -- and its V rows come from L2 behind
-  // an L2 prefetch one block ahead.
-  const bool pipe = !kvs && P.kv_pipe && nblk > kConsumerWarps;
-  uint4* kbuf[2] = {&A.kst[0][0][0], reinterpret_cast<uint4*>(S.act + sizeof(AttnSmem))};
-  if (!pipe) asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's staged K rows
-  uint32_t qf[16];  // B operand Q^T: head g8, physical dims 32*t4 .. 32*t4+31
+  uint32_t qf[16];  // B operand Q^T: head g8, physical dims 8*t4 + 32*c .. +7 (c = 0..3)
   {
-    const uint4* qs = reinterpret_cast<const uint4*>(&A.q[g8 < G ? g8 : 0][32 * t4]);
+    const uint4* qs = reinterpret_cast<const uint4*>(&A.q[g8 < G ? g8 : 0][8 * t4]);
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      const uint4 v = g8 < G ? qs[c] : make_uint4(0u, 0u, 0u, 0u);
+      const uint4 v = g8 < G ? qs[4 * c] : make_uint4(0u, 0u, 0u, 0u);
       qf[4 * c] = v.x;
       qf[4 * c + 1] = v.y;
       qf[4 * c + 2] = v.z;
@@ -1448,122 +1513,52 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
 #pragma unroll
   for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.0f;
   float mrun0 = -INFINITY, mrun1 = -INFINITY, lrun0 = 0.0f, lrun1 = 0.0f;  // heads 2*t4, 2*t4+1
-  for (int bi = warp; bi < nblk; bi += kConsumerWarps) {
-    const int p0 = start + bi * kBlk;
-    const int jb = (bi - warp) / kConsumerWarps;  // this warp's block ordinal
-    if (!kvs && bi + kConsumerWarps < nblk) {  // this warp's next block: K into shared memory (pipe) or L2
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        const int p = p0 + kConsumerWarps * kBlk + 8 * h2 + g8;
-        if (p < end) {
-          const size_t off = row_off(p);
-          if (pipe) {
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-              asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(
-                               kbuf[(jb + 1) & 1] + (warp * 8 + 4 * h2 + c) * 32 + lane)),
-                           "l"(kpool + off + 8 * c)
-                           : "memory");
-          } else if (p != pos) {
-            asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(kpool + off));
-          }
-          if (p != pos) asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(vpool + off));
-        }
+  // Work units: 16-position blocks of the caller's tiles (kvs: warp w takes
+  // blocks w, w + warps, ..), or ring slots of 32 positions (slot i of the
+  // item goes to warp i mod min(warps, slots) and is released by it alone;
+  // the bound keeps every wait within one fill of its slot).
+  if (kvs) asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's staged tile rows
+  const int n_units = kvs ? nblk : (end - start + kKvSlotPos - 1) / kKvSlotPos;
+  const int nwu = kvs ? kConsumerWarps : min(kConsumerWarps, P.slots);
+  const int upos = kvs ? kBlk : kKvSlotPos;
+  const CState base = ring ? *ring : CState{};
+  for (int i = warp; warp < nwu && i < n_units; i += nwu) {
+    const int s0 = start + i * upos;
+    const uint4* tiles = kvs;
+    int bi = i;
+    CState my{};
+    if (!kvs) {
+      my = cs_after(P, base, i);
+      slot_wait(S, P, my);
+      uint4* slot_tiles = reinterpret_cast<uint4*>(S.ring + static_cast<size_t>(my.slot) * kSlotBytes);
+      if (has_pos && pos >= s0 && pos < s0 + kKvSlotPos) {  // the new row (lanes 0-15 K, 16-31 V)
+        const int kv = lane >> 4, u = lane & 15;
+        slot_tiles[(kv * kKvSlotPos + pos - s0) * (kHD / 8) + u] =
+            __ldcg(reinterpret_cast<const uint4*>((kv ? vpool : kpool) + app) + u);
+        __syncwarp();
       }
+      tiles = slot_tiles;
+      bi = 0;
     }
-    if (pipe) {  // block jb's group complete (the one just committed may stay in flight)
-      asm volatile("cp.async.commit_group;" ::: "memory");
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-    }
-    // K/V rows p0+g8 and p0+8+g8, dims 32*t4 .. 32*t4+31 (the row of pos was
-    // appended by this CTA before the last block sync); the K rows of the
-    // first block other than pos's are already in shared memory
-    uint4 kr[2][4], vr[2][4];
-    size_t off[2];
-    bool ok[2];
-#pragma unroll
-    for (int h2 = 0; h2 < 2; ++h2) {
-      const int p = p0 + 8 * h2 + g8;
-      ok[h2] = p < end;
-      off[h2] = ok[h2] && !kvs ? row_off(p) : 0;
-    }
-    if (kvs) {  // every row in the shared-memory tiles (rows past the end: masked / zero V)
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          kr[h2][c] = kvs[kv_tile_idx(bi, 0, h2, c, lane)];
-          vr[h2][c] = ok[h2] ? kvs[kv_tile_idx(bi, 1, h2, c, lane)] : make_uint4(0u, 0u, 0u, 0u);
-        }
-    } else if (bi == warp || pipe) {  // staged K rows; rows past the end are masked out of the scores
-      const uint4* kb = kbuf[jb & 1] + warp * 8 * 32;
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) kr[h2][c] = kb[(4 * h2 + c) * 32 + lane];
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2)
-        if (bi == warp && p0 + 8 * h2 + g8 == pos)  // (staged before pos's row was appended)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) kr[h2][c] = __ldcg(reinterpret_cast<const uint4*>(kpool + off[h2]) + c);
-    } else {
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2)
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          kr[h2][c] = ok[h2] ? __ldcg(reinterpret_cast<const uint4*>(kpool + off[h2]) + c) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll 1
+    for (int p0 = s0; p0 < min(end, s0 + upos); p0 += kBlk, ++bi) {
+      if (kvs)
+        flash_block<false>(tiles, bi, p0, end, qf, o, mrun0, mrun1, lrun0, lrun1);
+      else
+        flash_block<true>(tiles, bi, p0, end, qf, o, mrun0, mrun1, lrun0, lrun1);
     }
     if (!kvs) {
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2)
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          vr[h2][c] = ok[h2] ? __ldcg(reinterpret_cast<const uint4*>(vpool + off[h2]) + c) : make_uint4(0u, 0u, 0u, 0u);
-    }
-    // S^T = K Q^T
-    float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-    for (int ks = 0; ks < kHD / 16; ++ks)
-      mma_16816(s, word_of(kr[0], 2 * ks), word_of(kr[1], 2 * ks), word_of(kr[0], 2 * ks + 1),
-                word_of(kr[1], 2 * ks + 1), qf[2 * ks], qf[2 * ks + 1]);
-    const bool v0 = p0 + g8 < end, v1 = p0 + 8 + g8 < end;
-    s[0] = v0 ? s[0] * kAttnScale : -INFINITY;
-    s[1] = v0 ? s[1] * kAttnScale : -INFINITY;
-    s[2] = v1 ? s[2] * kAttnScale : -INFINITY;
-    s[3] = v1 ? s[3] * kAttnScale : -INFINITY;
-    // online softmax per head (columns 2*t4, 2*t4+1; positions over g8 and the two row halves)
-    float mx0 = fmaxf(s[0], s[2]), mx1 = fmaxf(s[1], s[3]);
-#pragma unroll
-    for (int ofs = 4; ofs < 32; ofs <<= 1) {
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, ofs));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, ofs));
-    }
-    const float mn0 = fmaxf(mrun0, mx0), mn1 = fmaxf(mrun1, mx1);  // finite: position p0 is valid
-    const float al0 = expf(mrun0 - mn0), al1 = expf(mrun1 - mn1);
-    const float e0 = expf(s[0] - mn0), e1 = expf(s[1] - mn1), e2 = expf(s[2] - mn0), e3 = expf(s[3] - mn1);
-    float su0 = e0 + e2, su1 = e1 + e3;
-#pragma unroll
-    for (int ofs = 4; ofs < 32; ofs <<= 1) {
-      su0 += __shfl_xor_sync(0xffffffffu, su0, ofs);
-      su1 += __shfl_xor_sync(0xffffffffu, su1, ofs);
-    }
-    lrun0 = lrun0 * al0 + su0;
-    lrun1 = lrun1 * al1 + su1;
-    mrun0 = mn0;
-    mrun1 = mn1;
-    // O^T = O^T * alpha + V^T P^T
-    const uint32_t pb0 = movmatrix_t(pack_half2(e0, e1)), pb1 = movmatrix_t(pack_half2(e2, e3));
-#pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
-      o[mt][0] *= al0;
-      o[mt][2] *= al0;
-      o[mt][1] *= al1;
-      o[mt][3] *= al1;
-      mma_16816(o[mt], movmatrix_t(word_of(vr[0], 2 * mt)), movmatrix_t(word_of(vr[0], 2 * mt + 1)),
-                movmatrix_t(word_of(vr[1], 2 * mt)), movmatrix_t(word_of(vr[1], 2 * mt + 1)), pb0, pb1);
+      // (the slot's next fill may be a TMA copy: order this warp's writes before it)
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0)
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&S.empty[my.slot])),
+                     "r"(kConsumerWarps)
+                     : "memory");
     }
   }
-  const int nw = min(kConsumerWarps, nblk);  // warps that saw positions
+  if (ring) *ring = cs_after(P, base, n_units);
+  const int nw = min(nwu, n_units);  // warps that saw positions
   const size_t ms = P.max_splits;
   // -- warps meet in shared memory: each leaves its running max, sum and
   // output; the reducing thread rescales them to the merged max
@@ -1582,10 +1577,11 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
   consumer_sync();
   for (int w = tid; w < G * (kHD / 2); w += kConsumers) {
     const int h = w / (kHD / 2), dp = w - h * (kHD / 2);
-    // dims 2dp, 2dp+1 of head h: fragment value 4mt + 2hh + (h & 1) of lanes
-    // (g8, t4) = (2 (d >> 5) + e, h >> 1), d = 2dp = 32 (g8 >> 1) + 4 mt + 2 hh
-    const int d = 2 * dp, k = 4 * ((d & 31) >> 2) + 2 * (((d & 31) >> 1) & 1) + (h & 1);
-    const int la = 4 * (2 * (d >> 5)) + (h >> 1);
+    // dims d = 2dp, d + 1 of head h: fragment value 4mt + 2e + (h & 1) of
+    // lanes (g8, t4) = (2b + {0, 1}, h >> 1), d = 32(mt >> 1) + 8b + 4(mt & 1) + 2e
+    const int d = 2 * dp, mt = 2 * (d >> 5) + ((d >> 2) & 1);
+    const int k = 4 * mt + 2 * ((d >> 1) & 1) + (h & 1);
+    const int la = 4 * (2 * ((d >> 3) & 3)) + (h >> 1);
     const int ka = (k + 4 * la) & 31, kb = (k + 4 * (la + 4)) & 31;
     float M = -INFINITY;
     for (int ww = 0; ww < nw; ++ww) M = fmaxf(M, A.wm[ww][h]);
@@ -1680,8 +1676,65 @@ __device__ __forceinline__ int attn_chunk_len(const int* pos, int batch, int n_k
   const int slots_i = static_cast<int>(gridDim.x) - batch * n_kv;
   const uint32_t slots = slots_i > 0 ? static_cast<uint32_t>(slots_i) : 1u;
   uint32_t c = (total * static_cast<uint32_t>(n_kv) + slots - 1) / slots;
-  c = (c + kBlk - 1) / kBlk * kBlk;
+  c = (c + kKvSlotPos - 1) / kKvSlotPos * kKvSlotPos;  // ring slots never straddle two items
   return c < static_cast<uint32_t>(kMinSplit) ? kMinSplit : static_cast<int>(c);
+}
+
+// The cached K/V rows of this CTA's attention items of one layer (spread
+// attention: the items, in the order, the consumers' attention stage runs),
+// 32 positions per ring slot: K rows [32][head_dim] then V rows, as in the
+// cache.  Items start at multiples of 32 positions, so a slot's rows span
+// whole runs of cache pages: one TMA bulk copy per page run and matrix.
+// The row of the new position (appended by the consumers during the
+// stage; always the item's last row) is not copied.
+__device__ bool produce_kv(const Params& P, Smem& S, int layer, int step, uint32_t& chunk, int& pslot,
+                           uint32_t& pphase) {
+  const int B = P.s.batch, Hkv = P.m.n_kv_heads;
+  const int ps = P.s.page_size, pshift = __ffs(ps) - 1;  // a power of two
+  const LayerPtrs& L = S.lp[layer];
+  const uint64_t pol = evict_last_policy();
+  int pos[kMaxB];
+#pragma unroll
+  for (int b = 0; b < kMaxB; ++b) pos[b] = b < B ? P.s.pos[b] + step : 0;
+  const int chunk_len = attn_chunk_len(pos, B, Hkv);
+  int n_items = 0;
+  for (int b = 0; b < B; ++b) n_items += Hkv * ((pos[b] + chunk_len) / chunk_len);
+  for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+    // item -> (sequence, KV head, split) as the consumers number them
+    int rem = it, b = 0, nsp = (pos[0] + chunk_len) / chunk_len;
+    while (rem >= Hkv * nsp) {
+      rem -= Hkv * nsp;
+      ++b;
+      nsp = (pos[b] + chunk_len) / chunk_len;
+    }
+    const int kvh = rem / nsp, sp = rem - kvh * nsp;
+    const int start = sp * chunk_len, end = min(pos[b] + 1, start + chunk_len);
+    const int32_t* bt = P.s.block_table + static_cast<size_t>(b) * P.s.max_pages;
+    for (int s0 = start; s0 < end; s0 += kKvSlotPos) {
+      const int slot = pslot;
+      const uint32_t phase = pphase;
+      if (++pslot == P.slots) {
+        pslot = 0;
+        pphase ^= 1u;
+      }
+      if (!acquire_slot(P, S, chunk, slot, phase)) return false;
+      unsigned char* dst = S.ring + static_cast<size_t>(slot) * kSlotBytes;
+      const int e = min(end, s0 + kKvSlotPos);
+      const int e2 = (pos[b] >= s0 && pos[b] < e) ? pos[b] : e;  // rows [s0, e2) come from the cache
+      constexpr uint32_t kRowBytes = kHD * sizeof(__half);
+      mbar_expect_tx(&S.full[slot], 2u * static_cast<uint32_t>(e2 - s0) * kRowBytes);
+      for (int p = s0; p < e2;) {
+        const int in_page = p & (ps - 1), run = min(e2 - p, ps - in_page);
+        const size_t off = ((static_cast<size_t>(__ldg(bt + (p >> pshift))) * Hkv + kvh) * ps + in_page) * kHD;
+        unsigned char* d = dst + static_cast<size_t>(p - s0) * kRowBytes;
+        bulk_g2s(d, L.k_pool + off, run * kRowBytes, &S.full[slot], pol);
+        bulk_g2s(d + kKvSlotPos * kRowBytes, L.v_pool + off, run * kRowBytes, &S.full[slot], pol);
+        p += run;
+      }
+      ++chunk;
+    }
+  }
+  return true;
 }
 
 // The next token of every sequence from the tagged per-CTA argmax slots of a
@@ -1755,14 +1808,14 @@ __device__ void stage_kv_tiles(const Params& P, const LayerPtrs& L, int b, int k
       const int p = bi * kBlk + 8 * h2 + g8;
       if (p < npos) {
         const size_t off =
-            ((static_cast<size_t>(__ldg(bt + (p >> pshift))) * Hkv + kvh) * ps + (p & (ps - 1))) * kHD + 32 * t4;
+            ((static_cast<size_t>(__ldg(bt + (p >> pshift))) * Hkv + kvh) * ps + (p & (ps - 1))) * kHD + 8 * t4;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(&kvs[kv_tile_idx(bi, 0, h2, c, lane)])),
-                       "l"(L.k_pool + off + 8 * c)
+                       "l"(L.k_pool + off + 32 * c)
                        : "memory");
           asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(&kvs[kv_tile_idx(bi, 1, h2, c, lane)])),
-                       "l"(L.v_pool + off + 8 * c)
+                       "l"(L.v_pool + off + 32 * c)
                        : "memory");
         }
       }
@@ -1787,7 +1840,7 @@ __device__ void att_consumer(const Params& P, Smem& S, uint32_t epoch) {
     for (int l = 0; l < P.m.n_layers; ++l) {
       if (aborting(S)) return;
       const uint32_t tag = tag0 + static_cast<uint32_t>(5 * l + K_ATT);
-      attn_item(P, S, S.lp[l], b, kvh, 0, 1, pos + 1, pos, tag - 1u, tag, kvs);
+      attn_item(P, S, S.lp[l], b, kvh, 0, 1, pos + 1, pos, tag - 1u, tag, kvs, nullptr);
       if (l + 1 < P.m.n_layers) stage_kv_tiles(P, S.lp[l + 1], b, kvh, pos, kvs);
     }
   }
@@ -1909,7 +1962,7 @@ __device__ void consumer(const Params& P, Smem& S, uint32_t epoch) {
 #pragma unroll
           for (int b = 0; b < NB; ++b)
             if (b == bsel) pb = pos[b];
-          attn_item(P, S, L, bsel, kvh, sp, nsp, chunk, pb, in_tag, tag, nullptr);
+          attn_item(P, S, L, bsel, kvh, sp, nsp, chunk, pb, in_tag, tag, nullptr, &cs);
         }
         trace_mid(P, cs);
       } else if (kind == K_DN) {
@@ -2089,8 +2142,8 @@ static WsLayout ws_layout(const lmps_model_desc& m, int B, int max_seq_len) {
   return w;
 }
 
-static int act_bytes_for(const lmps_model_desc& m, int nb, int kv_pipe) {
-  size_t a = sizeof(AttnSmem) + (kv_pipe ? sizeof(uint4) * kConsumerWarps * 8 * 32 : 0);
+static int act_bytes_for(const lmps_model_desc& m, int nb) {
+  size_t a = sizeof(AttnSmem);
   const size_t grp = 16 * 4 + 4 + 4;  // plane words + scl + xs8 per group
   // k = hidden stages: planes + per-lane partials of every row entry
   // (+16: the partials start 16-byte aligned)
@@ -2111,7 +2164,7 @@ static int launch(const Params& P0, const lmps_model_desc& m, cudaStream_t st) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  P.act_bytes = act_bytes_for(m, NB, P.kv_pipe);
+  P.act_bytes = act_bytes_for(m, NB);
   // rows of the hidden and q|k|v outputs one CTA owns (residual / bias kept in shared memory)
   const int qkv_rows = (m.n_q_heads + 2 * m.n_kv_heads) * m.head_dim;
   // (pair-aligned partitions: at most 2 * ceil(rows / 2 / ctas) rows per CTA,
@@ -2207,9 +2260,6 @@ extern "C" int lmps_decode_persistent(const lmps_model_desc* model, const lmps_d
   P.att_cnt = reinterpret_cast<uint32_t*>(ws + w.att_cnt);
   P.epoch = reinterpret_cast<uint32_t*>(ws + w.epoch);
   P.max_splits = w.max_splits;
-  // long caches: the attention items hold many blocks per warp, worth a
-  // second K buffer (and two fewer ring slots)
-  P.kv_pipe = s.max_seq_len > 2048 ? 1 : 0;
   // batches of 2-4: the GEMV stages on the tensor cores (16-row tiles)
   P.mma = s.batch > 1 ? 1 : 0;
   if (P.mma && pk::down_kparts(m.intermediate / 32) == 0) return LMPS_ERR_UNSUPPORTED;
