@@ -196,11 +196,11 @@ struct Chunking {
 };
 
 // k-parts of the down projection's 16-row tiles on the tensor-core path: the
-// fewest that keep a part's scales a multiple of 16 bytes and the part in a
-// ring slot.
+// fewest that keep a part's scales a multiple of 16 bytes and the part
+// (padded rows and scales) in a ring slot.
 __host__ __device__ __forceinline__ int down_kparts(int groups) {
   for (int kp = 1; kp <= groups; ++kp)
-    if (groups % kp == 0 && (groups / kp) % 8 == 0 && kTileRows * (groups / kp) * 18 <= kSlotBytes) return kp;
+    if (groups % kp == 0 && (groups / kp) % 8 == 0 && kTileRows * ((groups / kp) * 18 + 16) <= kSlotBytes) return kp;
   return 0;
 }
 
@@ -301,27 +301,37 @@ __device__ void producer(const Params& P, Smem& S) {
         }
         // slot layout: packed rows [, second matrix's packed rows], scales [, second matrix's scales]
         unsigned char* dst = S.ring + static_cast<size_t>(slot) * kSlotBytes;
-        if (P.mma) {
-          // Tensor-core layout (batches 2-4): 16 tile rows at a padded stride
-          // (packed bytes + 16: the 8 rows one fragment load touches fall in
-          // different banks), then the rows' scales; gate/up: gate rows in
-          // tile rows 0-7, up rows in 8-15; the down projection one k-part.
+        if (P.mma && kind == ST_DN) {
+          // Down projection (batches 2-4): one k-part of 16 tile rows at a
+          // padded stride (part bytes + 16: the 8 rows one fragment load
+          // touches fall in different banks), then the rows' part scales.
           const uint32_t pbr = row_bytes / kparts, sbr = row_sbytes / kparts, pbs = pbr + 16;
-          mbar_expect_tx(&S.full[slot], ncopy * n * (pbr + sbr));
+          mbar_expect_tx(&S.full[slot], n * (pbr + sbr));
+          const unsigned char* sc = reinterpret_cast<const unsigned char*>(c.s);
+          for (uint32_t i = 0; i < n; ++i) {
+            bulk_g2s(dst + i * pbs, c.w + static_cast<size_t>(r + i) * row_bytes + part * pbr, pbr, &S.full[slot],
+                     policy);
+            bulk_g2s(dst + kTileRows * pbs + i * sbr, sc + static_cast<size_t>(r + i) * row_sbytes + part * sbr, sbr,
+                     &S.full[slot], policy);
+          }
+          continue;
+        }
+        if (P.mma) {
+          // Row tiles (batches 2-4): pairs of adjacent weight rows, one bulk
+          // copy each, at a padded pair stride (2 rows + 16 bytes): pair j
+          // holds tile rows j and j + 8, so the 8 rows one fragment load
+          // touches fall in different banks; then the rows' scales in weight
+          // row order.  Gate/up: gate pairs in pairs 0-3, up pairs in 4-7.
+          const uint32_t pps = 2 * row_bytes + 16;
+          mbar_expect_tx(&S.full[slot], ncopy * n * (row_bytes + row_sbytes));
           for (uint32_t m2 = 0; m2 < ncopy; ++m2) {
             const uint8_t* w = m2 ? c.w2 : c.w;
             const unsigned char* sc = reinterpret_cast<const unsigned char*>(m2 ? c.s2 : c.s);
-            for (uint32_t i = 0; i < n; ++i) {
-              const uint32_t trow = m2 * (kTileRows / 2) + i;
-              bulk_g2s(dst + trow * pbs, w + static_cast<size_t>(r + i) * row_bytes + part * pbr, pbr, &S.full[slot],
-                       policy);
-              if (kparts > 1)
-                bulk_g2s(dst + kTileRows * pbs + trow * sbr, sc + static_cast<size_t>(r + i) * row_sbytes + part * sbr,
-                         sbr, &S.full[slot], policy);
-            }
-            if (kparts == 1)
-              bulk_g2s(dst + kTileRows * pbs + m2 * (kTileRows / 2) * sbr, sc + static_cast<size_t>(r) * row_sbytes,
-                       n * sbr, &S.full[slot], policy);
+            for (uint32_t i = 0; 2 * i < n; ++i)
+              bulk_g2s(dst + (m2 * (kTileRows / 4) + i) * pps, w + static_cast<size_t>(r + 2 * i) * row_bytes,
+                       min(2u, n - 2 * i) * row_bytes, &S.full[slot], policy);
+            bulk_g2s(dst + (kTileRows / 2) * pps + m2 * (kTileRows / 2) * row_sbytes,
+                     sc + static_cast<size_t>(r) * row_sbytes, n * row_sbytes, &S.full[slot], policy);
           }
           continue;
         }
@@ -1006,7 +1016,7 @@ __device__ void gemv_rows_mma(const Params& P, Smem& S, CState& cs, int kind, in
   const bool gu = kind == ST_GU, head = kind == ST_HEAD;
   const int rpc = c.rows_per_chunk;
   const int nch = (c.r1 - c.r0 + rpc - 1) / rpc;
-  const size_t pbs = c.k / 2 + 16;
+  const size_t rb = c.k / 2, pps = 2 * rb + 16;  // row bytes, pair stride
   const Planes pl = planes_view(S, G, NB);
   const int B = P.s.batch;
   unsigned long long best = 0ull;  // LM head: this lane's sequence t
@@ -1028,11 +1038,14 @@ __device__ void gemv_rows_mma(const Params& P, Smem& S, CState& cs, int kind, in
     const int r = c.r0 + ch * rpc;
     const int n = min(rpc, c.r1 - r);
     const unsigned char* sl = S.ring + static_cast<size_t>(my.slot) * kSlotBytes;
-    const __half* sc = reinterpret_cast<const __half*>(sl + kTileRows * pbs);
-    const unsigned char* wa = sl + g * pbs;
-    const unsigned char* wb = sl + (g + 8) * pbs;
-    const __half* sa = sc + g * G;
-    const __half* sb = sc + (g + 8) * G;
+    // tile rows g, g + 8 = weight rows 2j, 2j + 1 of pair j = g (gate/up:
+    // gate pair g for g < 4, up pair g - 4 above)
+    const __half* sc = reinterpret_cast<const __half*>(sl + (kTileRows / 2) * pps);
+    const unsigned char* wa = sl + g * pps;
+    const unsigned char* wb = wa + rb;
+    const int srow = gu ? 8 * (g >> 2) + 2 * (g & 3) : 2 * g;  // scale row of tile row g
+    const __half* sa = sc + srow * G;
+    const __half* sb = sa + G;
     float acc0 = 0.0f, acc1 = 0.0f;
 #pragma unroll 4
     for (int grp = 0; grp < G; ++grp)
@@ -1042,47 +1055,45 @@ __device__ void gemv_rows_mma(const Params& P, Smem& S, CState& cs, int kind, in
       asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&S.empty[my.slot])),
                    "r"(kConsumerWarps)
                    : "memory");
-    // -- epilogue of the tile: rows (g, g + 8); gate/up: gate row g, up row g
-    const int i0 = r - c.r0 + g;  // row of the stage (gate/up: pair) held in acc0
-    const bool v0 = g < n, v1 = gu ? g < n : g + 8 < n;
+    // -- epilogue: this lane holds stage rows i0, i0 + 1 (gate/up: the
+    // gate rows, and lane + 16 the up rows) for sequence t
+    const int pr = gu ? 2 * (g & 3) : 2 * g;  // first row of the lane's pair within the chunk
+    const int i0 = r - c.r0 + pr;
+    const bool v = pr < n;  // (rows come in pairs)
     const bool lt = t < B;
     if (head) {
-      if (lt) {
-        if (v0) {
-          const __half h = __float2half_rn(acc0);
-          if (logits) logits[static_cast<size_t>(t) * P.m.vocab + r + g] = h;
-          best = u64_max(best, argmax_key(__half2float(h), static_cast<uint32_t>(r + g)));
+      if (lt && v) {
+        const __half h0 = __float2half_rn(acc0), h1 = __float2half_rn(acc1);
+        if (logits) {
+          logits[static_cast<size_t>(t) * P.m.vocab + r + pr] = h0;
+          logits[static_cast<size_t>(t) * P.m.vocab + r + pr + 1] = h1;
         }
-        if (v1) {
-          const __half h = __float2half_rn(acc1);
-          if (logits) logits[static_cast<size_t>(t) * P.m.vocab + r + g + 8] = h;
-          best = u64_max(best, argmax_key(__half2float(h), static_cast<uint32_t>(r + g + 8)));
-        }
+        best = u64_max(best, argmax_key(__half2float(h0), static_cast<uint32_t>(r + pr)));
+        best = u64_max(best, argmax_key(__half2float(h1), static_cast<uint32_t>(r + pr + 1)));
       }
       continue;
     }
     __half h0, h1;
     if (gu) {
-      h0 = __float2half_rn(silu_mul(__half2float(__float2half_rn(acc0)), __half2float(__float2half_rn(acc1))));
-      h1 = h0;
+      const float u0 = __shfl_down_sync(0xffffffffu, acc0, 16), u1 = __shfl_down_sync(0xffffffffu, acc1, 16);
+      h0 = __float2half_rn(silu_mul(__half2float(__float2half_rn(acc0)), __half2float(__float2half_rn(u0))));
+      h1 = __float2half_rn(silu_mul(__half2float(__float2half_rn(acc1)), __half2float(__float2half_rn(u1))));
     } else if (kind == ST_QKV) {
       h0 = __float2half_rn(acc0 + __half2float(S.bias_own[layer * kOwnMax + min(i0, kOwnMax - 1)]));
-      h1 = __float2half_rn(acc1 + __half2float(S.bias_own[layer * kOwnMax + min(i0 + 8, kOwnMax - 1)]));
+      h1 = __float2half_rn(acc1 + __half2float(S.bias_own[layer * kOwnMax + min(i0 + 1, kOwnMax - 1)]));
     } else {  // ST_O
       const int tb = lt ? t : 0;
       h0 = __hadd(S.xown[tb * kOwnMax + min(i0, kOwnMax - 1)], __float2half_rn(acc0));
-      h1 = __hadd(S.xown[tb * kOwnMax + min(i0 + 8, kOwnMax - 1)], __float2half_rn(acc1));
-      if (lt && v0) S.x1own[t * kOwnMax + i0] = h0;
-      if (lt && v1) S.x1own[t * kOwnMax + i0 + 8] = h1;
+      h1 = __hadd(S.xown[tb * kOwnMax + min(i0 + 1, kOwnMax - 1)], __float2half_rn(acc1));
+      if (lt && v) {
+        S.x1own[t * kOwnMax + i0] = h0;
+        S.x1own[t * kOwnMax + i0 + 1] = h1;
+      }
     }
-    // pairs (g, g + 1) for even g: the partner row is in lane + 4
-    const uint32_t b0 = __half_as_ushort(h0), b1 = __half_as_ushort(h1);
-    const uint32_t p0 = __shfl_down_sync(0xffffffffu, b0, 4), p1 = __shfl_down_sync(0xffffffffu, b1, 4);
-    if (lt && (g & 1) == 0) {
-      unsigned long long* row = dst + static_cast<size_t>(t) * dld;
-      if (v0) st_tagged(row + (r + g) / 2, tagged(tag, b0 | (p0 << 16)));
-      if (!gu && v1) st_tagged(row + (r + g + 8) / 2, tagged(tag, b1 | (p1 << 16)));
-    }
+    if (lt && v && (!gu || g < 4))
+      st_tagged(dst + static_cast<size_t>(t) * dld + (r + pr) / 2,
+                tagged(tag, static_cast<uint32_t>(__half_as_ushort(h0)) |
+                                (static_cast<uint32_t>(__half_as_ushort(h1)) << 16)));
   }
   cs = cs_after(P, base, nch);
   cs.wait_ns = wns;
@@ -1119,13 +1130,13 @@ __device__ void gemv_down_mma(const Params& P, Smem& S, CState& cs, uint32_t tag
                      __half2float(sc[(g + 8) * Gp + j]), part * Gp + j, acc0, acc1);
     slot_release(S, P, cs);
   }
-  trace_mid(P, cs);
   // warp partials: red[warp][row][sequence] after the planes
   float* red = reinterpret_cast<float*>(pl.xs8 + NB * G);
   if (t < NB) {
     red[(warp * kTileRows + g) * kMaxB + t] = acc0;
     red[(warp * kTileRows + g + 8) * kMaxB + t] = acc1;
   }
+  trace_mid(P, cs);
   consumer_sync();
   const int pairs = n / 2;
   for (int q = threadIdx.x; q < NB * pairs; q += kConsumers) {
