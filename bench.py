@@ -572,8 +572,58 @@ def time_gemv(rows: int, k: int, batch: int, iters: int = 20) -> dict:
             "gbs": round(nbytes / t / 1e9, 1), "bytes_per_launch": nbytes}
 
 
+def time_decode(B: int, T: int, n_layers: int, steps: int, launches: int = 3, timeline=None) -> dict:
+    """The persistent decoder alone: ``B`` sequences over a ``T``-position
+    fp16 N(0,1) KV cache (c4's shape at B=4, T=32768), ``n_layers`` decoder
+    layers, ``steps`` decode steps per launch; CUDA events around each of
+    ``launches`` launches after three warm-up launches (weights and KV > L2)."""
+    import dataclasses
+    import numpy as np
+    import torch
+    from llamamps_b200.config import QWEN2_5_1_5B
+    from llamamps_b200.engine import QwenEngine
+    from llamamps_b200.weights import synth_model
+    cfg = dataclasses.replace(QWEN2_5_1_5B, n_layers=n_layers)
+    mw = synth_model(cfg, seed=1, device="cuda")
+    eng = QwenEngine(weights=mw, max_batch=B, max_seq_len=T + (launches + 4) * steps + 8, decoder="persistent")
+    eng.reset(B, start_pos=T)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    for layer in range(cfg.n_layers):
+        eng.cache.k[layer].normal_(generator=g)
+        eng.cache.v[layer].normal_(generator=g)
+    eng.tokens[:B].copy_(torch.from_numpy(np.random.default_rng(4).integers(0, cfg.vocab, B)))
+    for _ in range(3):
+        eng.decode_steps(steps, record=False)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(launches):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        eng.decode_steps(steps, record=False)
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b) * 1e3 / steps)
+    eng.pdec.check_error()
+    kv = B * cfg.kv_bytes_per_position() * (T + 3 * steps + steps * launches / 2)
+    us = float(np.median(times))
+    out = {"kernel": f"decode_persistent_kernel (batch {B})", "batch": B, "kv_positions": T, "layers": n_layers,
+           "steps_per_launch": steps, "us_per_step": round(us, 1),
+           "bytes_per_step": int(cfg.step_weight_bytes() + kv),
+           "gbs": round((cfg.step_weight_bytes() + kv) / us / 1e3, 1)}
+    if timeline:
+        from llamamps_b200.timeline import capture
+        with open(timeline, "w") as f:
+            json.dump(capture(eng, 4), f)
+    return out
+
+
 def run_kernel_timing(args) -> int:
-    """--time gemm|attention|prefill_attention|gemv: one JSON line per shape (not a benchmark line)."""
+    """--time gemm|attention|prefill_attention|gemv|decode: one JSON line per shape (not a benchmark line)."""
+    if args.time == "decode":
+        shapes = [tuple(int(v) for v in s.split(",")) for s in args.shape] if args.shape else [(4, 32768)]
+        for b, t in shapes:
+            print(json.dumps(time_decode(b, t, args.layers or 28, args.iters, timeline=args.timeline)))
+        return 0
     if args.time == "gemv":
         shapes = [tuple(int(v) for v in s.split(",")) for s in args.shape] if args.shape else [(8960, 1536, 1)]
         for r, k, b in shapes:
@@ -753,12 +803,14 @@ def main():
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling only: build a model with fewer decoder layers (the JSON line "
                          "then names the reduced workload and is not a measurement of it)")
-    ap.add_argument("--time", choices=["gemm", "attention", "prefill_attention", "gemv"], default=None,
+    ap.add_argument("--time", choices=["gemm", "attention", "prefill_attention", "gemv", "decode"], default=None,
                     help="kernel timing tables instead of the benchmark: the tcgen05 W4A16 GEMM, the "
-                         "split-KV decode attention, the causal prefill attention or the gate/up SwiGLU Q4 "
-                         "GEMV, per --shape (m,n,k / batch,attended,cache / batch,seq_len / rows,k,batch)")
+                         "split-KV decode attention, the causal prefill attention, the gate/up SwiGLU Q4 "
+                         "GEMV or the persistent decoder (--layers, --iters steps per launch), per --shape "
+                         "(m,n,k / batch,attended,cache / batch,seq_len / rows,k,batch / batch,cached)")
     ap.add_argument("--shape", action="append", default=None, help="shape for --time (repeatable)")
-    ap.add_argument("--iters", type=int, default=20, help="calls per timing for --time gemm / gemv")
+    ap.add_argument("--iters", type=int, default=20,
+                    help="calls per timing for --time gemm / gemv; steps per launch for --time decode")
     ap.add_argument("--auto-splits", action="store_true",
                     help="--time attention: only the split count the library picks")
     args = ap.parse_args()
