@@ -7,27 +7,31 @@
 // Grid = (splits, kv heads, sequences).  A CTA owns one KV head of one
 // sequence and a contiguous range of positions; the G query heads that share
 // the KV head (GQA, attention.metal:23) are processed together so each K/V
-// tile is read from HBM once.  Tiles of 64 positions are staged in shared
-// memory; the softmax is computed online (running max / sum per head) and
-// each split writes an unnormalised partial (acc, max, sum) that a combine
-// kernel merges with a log-sum-exp rescale.  With one split the CTA writes
-// the normalised output directly.
+// row is read from HBM once.  Tiles of 64 positions (K and V rows in the
+// cache's layout, 32 KB) are staged in shared memory with cp.async, double
+// buffered; each of the 4 warps folds one 16-position block of a tile into
+// its own online softmax on the tensor cores (flash_decode.cuh), and the
+// warps' states meet in shared memory at the end.  Each split writes an
+// unnormalised partial (acc, max, sum) that a combine kernel merges with a
+// log-sum-exp rescale; with one split the CTA writes the normalised output.
 // The _rope entry point also does rope_kv_append's work (kernels/rope.metal
 // on q and k, then the cache append): each CTA rotates the query heads of its
 // KV head from the q|k|v row, and the split that attends the new position
-// rotates and writes that K row (and the V row) into the paged cache before
-// it stages its tiles.
+// rotates and writes that K row (and the V row) into the paged cache and
+// into its staged tile.
 #include <cmath>
 
 #include "common.cuh"
+#include "flash_decode.cuh"
 
 namespace lmps {
 
-constexpr int kAttnThreads = 128;
-constexpr int kAttnTile = 64;
+constexpr int kAttnWarps = 4;
+constexpr int kAttnThreads = kAttnWarps * kWarp;
+constexpr int kAttnTile = kAttnWarps * fd::kBlk;  // positions per staged tile
+constexpr int kAttnStages = 2;                     // tiles in shared memory: one in flight while one computes
 constexpr int kHeadDim = 128;
 constexpr int kMaxGroup = 8;
-constexpr int kKStride = kHeadDim + 8;  // padded K row (halves): conflict-free 16-byte row reads
 
 struct AttnParams {
   const __half* q;        // [B, Hq*128] (rotated)
@@ -39,6 +43,7 @@ struct AttnParams {
   float* part_o;               // [B, Hq, splits, 128]
   float2* part_ml;             // [B, Hq, splits]
   int max_pages, page_size, n_q_heads, n_kv_heads, n_splits, chunk;
+  int page_shift;  // log2(page_size) when it is a power of two, else -1
   // fused RoPE + append (qkv != nullptr): q|k|v rows [B, (Hq + 2 Hkv) * 128]
   // (bias applied), position of the new token per sequence (seq_lens = pos + 1)
   const __half* qkv;
@@ -50,13 +55,14 @@ struct AttnParams {
 };
 
 struct __align__(16) AttnSmem {
-  float q[kMaxGroup][kHeadDim];
-  __half k[kAttnTile][kKStride];
-  __half v[kAttnTile][kHeadDim];
-  float p[kMaxGroup][kAttnTile];
-  float m[kMaxGroup];
-  float l[kMaxGroup];
-  float alpha[kMaxGroup];
+  union {
+    uint4 kv[kAttnStages][2][kAttnTile][fd::kRowUnits];  // [stage][K, V][row][16-byte unit], the cache's layout
+    float wo[kAttnWarps][32][32];                         // after the tiles: per-warp O^T fragments
+  };
+  __half q[kMaxGroup][kHeadDim];             // rotated q, natural dim order
+  __half knew[kHeadDim], vnew[kHeadDim];     // the appended row (rope entry point)
+  float wm[kAttnWarps][kMaxGroup];           // per-warp running max and sum
+  float wl[kAttnWarps][kMaxGroup];
 };
 
 __global__ void __launch_bounds__(kAttnThreads) gqa_decode_attn_kernel(const AttnParams P) {
@@ -66,11 +72,12 @@ __global__ void __launch_bounds__(kAttnThreads) gqa_decode_attn_kernel(const Att
   AttnSmem& S = *reinterpret_cast<AttnSmem*>(smem_raw);
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int G = P.n_q_heads / P.n_kv_heads;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, t4 = lane & 3;
   const int T = P.seq_lens[b];
   const int start = split * P.chunk;
   const int end = min(T, start + P.chunk);
   const int q_dim = P.n_q_heads * kHeadDim;
+  int pnew = -1;  // position whose row comes from S.knew / S.vnew instead of the cache
 
   if (P.qkv != nullptr) {
     // RoPE of the G query heads (rounded to fp16 as rope_kv_append's output)
@@ -85,10 +92,11 @@ __global__ void __launch_bounds__(kAttnThreads) gqa_decode_attn_kernel(const Att
       const __half* src = row + (kvh * G + hl) * kHeadDim;
       __half a = src[i1], c = src[i2];
       rope_rotate(a, c, m * P.inv_freq[fi]);
-      S.q[hl][i1] = __half2float(a);
-      S.q[hl][i2] = __half2float(c);
+      S.q[hl][i1] = a;
+      S.q[hl][i2] = c;
     }
-    if (p >= start && p < end) {  // this split attends the new position: append its K/V rows first
+    if (p >= start && p < end) {  // this split attends the new position: append its K/V rows
+      pnew = p;
       const int page = P.block_table[static_cast<size_t>(b) * P.max_pages + p / P.page_size];
       const size_t dst = ((static_cast<size_t>(page) * P.n_kv_heads + kvh) * P.page_size + p % P.page_size) * kHeadDim;
       const __half* ksrc = row + q_dim + kvh * kHeadDim;
@@ -99,147 +107,115 @@ __global__ void __launch_bounds__(kAttnThreads) gqa_decode_attn_kernel(const Att
         rope_rotate(a, c, m * P.inv_freq[fi]);
         P.k_new[dst + i1] = a;
         P.k_new[dst + i2] = c;
+        S.knew[i1] = a;
+        S.knew[i2] = c;
       }
-      for (int t = tid; t < kHeadDim; t += kAttnThreads) P.v_new[dst + t] = row[q_dim + kv_dim + kvh * kHeadDim + t];
-      __threadfence();  // the rows are read back below through L2 by the tile staging
+      for (int t = tid; t < kHeadDim; t += kAttnThreads) {
+        const __half v = row[q_dim + kv_dim + kvh * kHeadDim + t];
+        P.v_new[dst + t] = v;
+        S.vnew[t] = v;
+      }
     }
   } else {
     for (int i = tid; i < G * kHeadDim; i += kAttnThreads) {
       const int h = i / kHeadDim, d = i - h * kHeadDim;
-      S.q[h][d] = __half2float(P.q[static_cast<size_t>(b) * q_dim + (kvh * G + h) * kHeadDim + d]);
+      S.q[h][d] = P.q[static_cast<size_t>(b) * q_dim + (kvh * G + h) * kHeadDim + d];
     }
   }
-  if (tid < kMaxGroup) {
-    S.m[tid] = -INFINITY;
-    S.l[tid] = 0.0f;
-  }
-  float acc[kMaxGroup];
-#pragma unroll
-  for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
-  __syncthreads();
+  __syncthreads();  // S.q, S.knew / S.vnew
 
+  // Stage tile ti (positions start + 64 ti ..) into buffer ti % stages: thread tid
+  // copies 16-byte unit (tid & 15) of rows (tid >> 4) + 8 j of K and of V,
+  // so a warp instruction reads two whole 256-byte rows.
   const int32_t* bt = P.block_table + static_cast<size_t>(b) * P.max_pages;
-  for (int t0 = start; t0 < end; t0 += kAttnTile) {
-    const int n = min(kAttnTile, end - t0);
-    // Stage K and V rows of this tile: 16 threads per 256-byte row.  All of a
-    // thread's loads are issued before any of its shared-memory stores, so
-    // the tile costs one memory round trip, not one per row it stages.
-    constexpr int kPer = kAttnTile * (kHeadDim / 8) / kAttnThreads;
-    uint4 kv[kPer], vv[kPer];
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int i = tid + j * kAttnThreads, r = i / (kHeadDim / 8), c = i - r * (kHeadDim / 8);
-      kv[j] = make_uint4(0u, 0u, 0u, 0u);
-      vv[j] = kv[j];
-      if (r < n) {
-        const int pos = t0 + r;
-        const int page = __ldg(bt + pos / P.page_size);
-        const size_t off = ((static_cast<size_t>(page) * P.n_kv_heads + kvh) * P.page_size +
-                             pos % P.page_size) * kHeadDim + c * 8;
-        kv[j] = __ldcg(reinterpret_cast<const uint4*>(P.k_pool + off));
-        vv[j] = __ldcg(reinterpret_cast<const uint4*>(P.v_pool + off));
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int i = tid + j * kAttnThreads, r = i / (kHeadDim / 8), c = i - r * (kHeadDim / 8);
-      *reinterpret_cast<uint4*>(&S.k[r][c * 8]) = kv[j];
-      *reinterpret_cast<uint4*>(&S.v[r][c * 8]) = vv[j];
-    }
-    __syncthreads();
-    // Scores: thread -> (position r, head parity hs); heads hs, hs+2, ...
-    {
-      const int r = tid % kAttnTile, hs = tid / kAttnTile;
-      float dots[kMaxGroup / 2];
-#pragma unroll
-      for (int j = 0; j < kMaxGroup / 2; ++j) dots[j] = 0.0f;
+  auto stage = [&](int ti) {
+    const int t0 = start + ti * kAttnTile, u = tid & (fd::kRowUnits - 1);
 #pragma unroll 4
-      for (int c = 0; c < kHeadDim / 8; ++c) {
-        const uint4 kk = *reinterpret_cast<const uint4*>(&S.k[r][c * 8]);
-        const __half2* k2 = reinterpret_cast<const __half2*>(&kk);
-        float kf[8];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __half22float2(k2[e]);
-          kf[2 * e] = f.x;
-          kf[2 * e + 1] = f.y;
-        }
-#pragma unroll
-        for (int j = 0; j < kMaxGroup / 2; ++j) {
-          const int h = hs + 2 * j;
-          if (h < G) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) dots[j] = fmaf(S.q[h][c * 8 + e], kf[e], dots[j]);
-          }
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < kMaxGroup / 2; ++j) {
-        const int h = hs + 2 * j;
-        if (h < G) S.p[h][r] = (r < n) ? dots[j] * kAttnScale : -INFINITY;
+    for (int j = 0; j < kAttnTile * fd::kRowUnits / kAttnThreads; ++j) {
+      const int r = (tid >> 4) + j * (kAttnThreads / fd::kRowUnits), p = t0 + r;
+      uint4* dk = &S.kv[ti % kAttnStages][0][r][u];
+      uint4* dv = &S.kv[ti % kAttnStages][1][r][u];
+      if (p == pnew) {
+        *dk = reinterpret_cast<const uint4*>(S.knew)[u];
+        *dv = reinterpret_cast<const uint4*>(S.vnew)[u];
+      } else if (p < end) {
+        const int pi = P.page_shift >= 0 ? p >> P.page_shift : p / P.page_size;
+        const int in_page = P.page_shift >= 0 ? p & (P.page_size - 1) : p - pi * P.page_size;
+        const size_t off =
+            ((static_cast<size_t>(__ldg(bt + pi)) * P.n_kv_heads + kvh) * P.page_size + in_page) * kHeadDim + 8 * u;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dk)), "l"(P.k_pool + off)
+                     : "memory");
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dv)), "l"(P.v_pool + off)
+                     : "memory");
       }
     }
-    __syncthreads();
-    // Online softmax update, one warp per head.
-    {
-      const int warp = tid / kWarp, lane = tid % kWarp;
-      for (int h = warp; h < G; h += kAttnThreads / kWarp) {
-        const float s0 = S.p[h][lane], s1 = S.p[h][lane + 32];
-        const float tmax = warp_max(fmaxf(s0, s1));
-        const float m_old = S.m[h];
-        const float m_new = fmaxf(m_old, tmax);
-        float e0 = 0.0f, e1 = 0.0f, alpha = 1.0f;
-        if (m_new != -INFINITY) {
-          e0 = expf(s0 - m_new);
-          e1 = expf(s1 - m_new);
-          alpha = expf(m_old - m_new);
-        }
-        const float sum = warp_sum(e0 + e1);
-        S.p[h][lane] = e0;
-        S.p[h][lane + 32] = e1;
-        __syncwarp();
-        if (lane == 0) {
-          S.alpha[h] = alpha;
-          S.m[h] = m_new;
-          S.l[h] = S.l[h] * alpha + sum;
-        }
-      }
-    }
-    __syncthreads();
-    // P.V: thread -> output dimension d.
-    {
-      const int d = tid;
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  const int n_tiles = end > start ? (end - start + kAttnTile - 1) / kAttnTile : 0;
+  for (int ti = 0; ti < n_tiles && ti < kAttnStages - 1; ++ti) stage(ti);
+
+  uint32_t qf[16];
+  fd::load_qf(&S.q[0][0], G, qf);
+  float o[8][4];
 #pragma unroll
-      for (int h = 0; h < kMaxGroup; ++h)
-        if (h < G) acc[h] *= S.alpha[h];
-      for (int r = 0; r < n; ++r) {
-        const float v = __half2float(S.v[r][d]);
-#pragma unroll
-        for (int h = 0; h < kMaxGroup; ++h)
-          if (h < G) acc[h] = fmaf(S.p[h][r], v, acc[h]);
-      }
+  for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.0f;
+  float mrun0 = -INFINITY, mrun1 = -INFINITY, lrun0 = 0.0f, lrun1 = 0.0f;  // heads 2*t4, 2*t4+1
+  for (int ti = 0; ti < n_tiles; ++ti) {
+    if (ti + kAttnStages - 1 < n_tiles) stage(ti + kAttnStages - 1);  // into the buffer tile ti - 1 used
+    // tile ti's group complete: the groups of later tiles may stay in flight
+    const int later = min(n_tiles - 1, ti + kAttnStages - 1) - ti;
+    if (later >= 2)
+      asm volatile("cp.async.wait_group 2;" ::: "memory");
+    else if (later == 1)
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();  // tile ti landed for every thread's copies
+    const int p0 = start + ti * kAttnTile + warp * fd::kBlk;
+    const int sb = ti % kAttnStages;
+    if (p0 < end) {
+      uint4 kr[2][4], vr[2][4];
+      fd::load_rows(&S.kv[sb][0][warp * fd::kBlk][0], &S.kv[sb][1][warp * fd::kBlk][0], p0, end, kr, vr);
+      fd::block_update(kr, vr, p0, end, qf, o, mrun0, mrun1, lrun0, lrun1);
     }
-    __syncthreads();
+    __syncthreads();  // buffer sb is free for tile ti + stages
   }
 
-  const int d = tid;
-  if (P.n_splits == 1) {
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h) {
-      if (h < G) {
-        const float l = S.l[h];
-        P.out[static_cast<size_t>(b) * q_dim + (kvh * G + h) * kHeadDim + d] =
-            __float2half_rn(l > 0.0f ? acc[h] / l : 0.0f);
-      }
+  // -- the warps meet in shared memory; the reducing thread rescales each
+  // warp's state to the merged max
+  const int nw = min(kAttnWarps, (max(end - start, 0) + fd::kBlk - 1) / fd::kBlk);  // warps that saw positions
+  if (warp < nw) {
+    if ((lane >> 2) == 0) {
+      S.wm[warp][2 * t4] = mrun0;
+      S.wm[warp][2 * t4 + 1] = mrun1;
+      S.wl[warp][2 * t4] = lrun0;
+      S.wl[warp][2 * t4 + 1] = lrun1;
     }
-  } else {
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h) {
-      if (h < G) {
-        const size_t row = (static_cast<size_t>(b) * P.n_q_heads + kvh * G + h) * P.n_splits + split;
-        P.part_o[row * kHeadDim + d] = acc[h];
-        if (d == 0) P.part_ml[row] = make_float2(S.m[h], S.l[h]);
-      }
+    fd::store_frags(S.wo[warp], o);
+  }
+  __syncthreads();
+  for (int w = tid; w < G * (kHeadDim / 2); w += kAttnThreads) {
+    const int h = w / (kHeadDim / 2), d = 2 * (w - h * (kHeadDim / 2));
+    int la, k;
+    fd::frag_slot(h, d, la, k);
+    float M = -INFINITY;
+    for (int ww = 0; ww < nw; ++ww) M = fmaxf(M, S.wm[ww][h]);
+    float n0 = 0.0f, n1 = 0.0f, den = 0.0f;
+    for (int ww = 0; ww < nw; ++ww) {
+      const float f = expf(S.wm[ww][h] - M);
+      const float2 v = fd::load_frag_pair(S.wo[ww], la, k);
+      n0 = fmaf(v.x, f, n0);
+      n1 = fmaf(v.y, f, n1);
+      den = fmaf(S.wl[ww][h], f, den);
+    }
+    if (P.n_splits == 1) {
+      const float inv = den > 0.0f ? 1.0f / den : 0.0f;
+      *reinterpret_cast<__half2*>(&P.out[static_cast<size_t>(b) * q_dim + (kvh * G + h) * kHeadDim + d]) =
+          __floats2half2_rn(n0 * inv, n1 * inv);
+    } else {
+      const size_t prow = (static_cast<size_t>(b) * P.n_q_heads + kvh * G + h) * P.n_splits + split;
+      *reinterpret_cast<float2*>(&P.part_o[prow * kHeadDim + d]) = make_float2(n0, n1);
+      if (d == 0) P.part_ml[prow] = make_float2(M, den);
     }
   }
 }
@@ -280,13 +256,15 @@ extern "C" int lmps_gqa_attention_splits(int batch, int n_kv_heads, int max_seq_
   (void)page_size;
   if (batch <= 0 || n_kv_heads <= 0 || max_seq_len <= 0) return 1;
   // The time of a call follows its longest split: take the fewest 64-position
-  // tiles per split that a grid of at most ~4 CTAs per SM (148 SMs) allows,
-  // then the fewest splits that reach it (a batch-64 sweep: 416-position
-  // cache 33.3 -> 27.7 us, 1024-position 60.8 -> 48.9 us; batch 16, 1024
-  // positions 27.8 -> 18.4 us against the earlier two-CTAs-per-SM rule).
+  // tiles per split that a grid of at most ~3 CTAs per SM (148 SMs; the
+  // kernel's 67 KB of shared memory allow three) permits, then the fewest
+  // splits that reach it.  Sweep, us per call with combine: batch 64,
+  // 155-position cache 1 split 9.1 / 2 10.5 / 3 8.8; 416: 17.3 / 14.8 /
+  // 3 13.4 / 4 14.5; 1024: 36.4 / 23.9 / 3 19.8 / 4 24.7 / 6 22.9; batch 16,
+  // 1024: 4 12.0 / 8 10.8 / 16 13.6; batch 8, 2144: 12 13.2 / 17 12.4 / 24 12.9.
   const int tiles = (max_seq_len + kAttnTile - 1) / kAttnTile;
   const int ctas = batch * n_kv_heads;
-  int cap = (4 * 148) / ctas;
+  int cap = (3 * 148) / ctas;
   if (cap < 1) cap = 1;
   if (cap > tiles) cap = tiles;
   if (cap > 256) cap = 256;
@@ -359,6 +337,7 @@ static int attention_launch(AttnParams P, const uint16_t* k_pool, const uint16_t
   P.out = reinterpret_cast<__half*>(out);
   P.max_pages = max_pages;
   P.page_size = page_size;
+  P.page_shift = (page_size & (page_size - 1)) == 0 ? __builtin_ctz(static_cast<unsigned>(page_size)) : -1;
   P.n_q_heads = n_q_heads;
   P.n_kv_heads = n_kv_heads;
   P.n_splits = n_splits;

@@ -81,6 +81,11 @@ constexpr int kQ4Group = 32;        // elements per scale (utils/pack_weights.py
 constexpr int kQ4GroupBytes = 16;   // 32 nibbles
 constexpr float kAttnScale = 0.088388f;  // kernels/attention.metal:40
 
+// Shared-memory address of a generic pointer into this CTA's shared memory.
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -147,7 +147,6 @@ struct Params {
   uint32_t* att_cnt;  // [kMaxB, Hkv] split arrivals (reset by the last split)
   uint32_t* epoch;    // [1] tag base of the next launch
   int max_splits;
-  int mma;            // 1: batch > 1 -- the GEMV stages run on the tensor cores (16-row ring chunks)
 };
 
 enum StageKind { ST_QKV = 0, ST_O = 1, ST_GU = 2, ST_DN = 3, ST_HEAD = 4 };
@@ -204,30 +203,33 @@ __host__ __device__ __forceinline__ int down_kparts(int groups) {
   return 0;
 }
 
+// kMma (batches 2-4, decided per kernel instantiation): the tensor-core
+// chunking of gemv_rows_mma / gemv_down_mma.
+template <bool kMma>
 __device__ __forceinline__ Chunking stage_chunks(const Params& P, int kind, int layer, int ctas) {
   Chunking c{};
   const lmps_model_desc& m = P.m;
   int rows = 0;
   if (kind == ST_HEAD) {
     c.w = m.lm_packed; c.s = reinterpret_cast<const __half*>(m.lm_scales);
-    c.k = m.hidden; rows = m.vocab; c.rows_per_chunk = P.mma ? kTileRows : kRows1536;
+    c.k = m.hidden; rows = m.vocab; c.rows_per_chunk = kMma ? kTileRows : kRows1536;
   } else {
     const lmps_layer_desc& L = m.layers[layer];
     if (kind == ST_QKV) {
       c.w = L.qkv_packed; c.s = reinterpret_cast<const __half*>(L.qkv_scales);
       c.k = m.hidden; rows = (m.n_q_heads + 2 * m.n_kv_heads) * m.head_dim;
-      c.rows_per_chunk = P.mma ? kTileRows : kRows1536;
+      c.rows_per_chunk = kMma ? kTileRows : kRows1536;
     } else if (kind == ST_O) {
       c.w = L.o_packed; c.s = reinterpret_cast<const __half*>(L.o_scales);
-      c.k = m.n_q_heads * m.head_dim; rows = m.hidden; c.rows_per_chunk = P.mma ? kTileRows : kRows1536;
+      c.k = m.n_q_heads * m.head_dim; rows = m.hidden; c.rows_per_chunk = kMma ? kTileRows : kRows1536;
     } else if (kind == ST_GU) {
       c.w = L.gate_packed; c.s = reinterpret_cast<const __half*>(L.gate_scales);
       c.w2 = L.up_packed; c.s2 = reinterpret_cast<const __half*>(L.up_scales);
-      c.k = m.hidden; rows = m.intermediate; c.rows_per_chunk = P.mma ? kTileRows / 2 : kPairsGU;
+      c.k = m.hidden; rows = m.intermediate; c.rows_per_chunk = kMma ? kTileRows / 2 : kPairsGU;
     } else {
       c.w = L.down_packed; c.s = reinterpret_cast<const __half*>(L.down_scales);
-      c.k = m.intermediate; rows = m.hidden; c.rows_per_chunk = P.mma ? kTileRows : kRowsDown;
-      if (P.mma) c.kparts = down_kparts(m.intermediate / kQ4Group);
+      c.k = m.intermediate; rows = m.hidden; c.rows_per_chunk = kMma ? kTileRows : kRowsDown;
+      if (kMma) c.kparts = down_kparts(m.intermediate / kQ4Group);
     }
   }
   row_range(rows, blockIdx.x, ctas, c.r0, c.r1);
@@ -266,6 +268,7 @@ __device__ __forceinline__ bool acquire_slot(const Params& P, Smem& S, uint32_t 
   return true;
 }
 
+template <bool kMma>
 __device__ void producer(const Params& P, Smem& S) {
   const uint64_t policy = evict_first_policy();
   uint32_t chunk = 0, pphase = 0;
@@ -281,7 +284,7 @@ __device__ void producer(const Params& P, Smem& S) {
         ok = false;
         break;
       }
-      const Chunking c = stage_chunks(P, kind, st >> 2, S.gemv_grid);
+      const Chunking c = stage_chunks<kMma>(P, kind, st >> 2, S.gemv_grid);
       const uint32_t row_bytes = c.k / 2, row_sbytes = c.k / 16;
       const uint32_t ncopy = (kind == ST_GU) ? 2u : 1u;
       trace_event(P, gridDim.x + blockIdx.x, pev);
@@ -301,7 +304,7 @@ __device__ void producer(const Params& P, Smem& S) {
         }
         // slot layout: packed rows [, second matrix's packed rows], scales [, second matrix's scales]
         unsigned char* dst = S.ring + static_cast<size_t>(slot) * kSlotBytes;
-        if (P.mma && kind == ST_DN) {
+        if (kMma && kind == ST_DN) {
           // Down projection (batches 2-4): one k-part of 16 tile rows at a
           // padded stride (part bytes + 16: the 8 rows one fragment load
           // touches fall in different banks), then the rows' part scales.
@@ -316,7 +319,7 @@ __device__ void producer(const Params& P, Smem& S) {
           }
           continue;
         }
-        if (P.mma) {
+        if (kMma) {
           // Row tiles (batches 2-4): pairs of adjacent weight rows, one bulk
           // copy each, at a padded pair stride (2 rows + 16 bytes): pair j
           // holds tile rows j and j + 8, so the 8 rows one fragment load
@@ -1931,7 +1934,7 @@ __device__ void consumer(const Params& P, Smem& S, uint32_t epoch) {
       // before the input is polled
       const int wk = kind == K_QKV ? ST_QKV : kind == K_O ? ST_O : kind == K_GU ? ST_GU : kind == K_DN ? ST_DN : ST_HEAD;
       Chunking ch{};
-      if (kind != K_ATT) ch = stage_chunks(P, wk, l, S.gemv_grid);
+      if (kind != K_ATT) ch = stage_chunks<(NB > 1)>(P, wk, l, S.gemv_grid);
       // -- stage the input activation in shared memory
       if (kind == K_QKV || kind == K_GU || kind == K_HEAD) {
         const __half* rows[NB];
@@ -2105,7 +2108,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
   __syncthreads();
   const bool att_cta = static_cast<int>(blockIdx.x) >= S.gemv_grid;
   if (threadIdx.x >= kConsumers) {
-    if (threadIdx.x == kConsumers && !att_cta) producer(P, S);
+    if (threadIdx.x == kConsumers && !att_cta) producer<(NB > 1)>(P, S);
     return;
   }
   if (att_cta)
@@ -2184,7 +2187,7 @@ static int launch(const Params& P0, const lmps_model_desc& m, cudaStream_t st) {
   if (proj_ctas < 1) return LMPS_ERR_UNSUPPORTED;
   auto per_cta = [&](int rows) { return 2 * ((rows / 2 + proj_ctas - 1) / proj_ctas); };
   // tensor-core path: a CTA's hidden rows are one 16-row tile of the down projection
-  if (P.mma && per_cta(m.hidden) > kTileRows) return LMPS_ERR_UNSUPPORTED;
+  if (NB > 1 && per_cta(m.hidden) > kTileRows) return LMPS_ERR_UNSUPPORTED;
   if (per_cta(m.hidden) > kOwnMax || per_cta(qkv_rows) > kOwnMax || per_cta(m.intermediate) > kOutMax ||
       m.n_layers > kMaxLayers || sms > kMaxGrid || m.vocab > 0x40000 || 2 * kConsumers < sms * kMaxB)
     return LMPS_ERR_UNSUPPORTED;
@@ -2272,8 +2275,7 @@ extern "C" int lmps_decode_persistent(const lmps_model_desc* model, const lmps_d
   P.epoch = reinterpret_cast<uint32_t*>(ws + w.epoch);
   P.max_splits = w.max_splits;
   // batches of 2-4: the GEMV stages on the tensor cores (16-row tiles)
-  P.mma = s.batch > 1 ? 1 : 0;
-  if (P.mma && pk::down_kparts(m.intermediate / 32) == 0) return LMPS_ERR_UNSUPPORTED;
+  if (s.batch > 1 && pk::down_kparts(m.intermediate / 32) == 0) return LMPS_ERR_UNSUPPORTED;
   cudaStream_t st = lmps_stream(stream);
   switch (s.batch) {
     case 1: return pk::launch<1>(P, m, st);

@@ -70,9 +70,6 @@ struct __align__(64) Params {
   int ksteps_per_split;  // split K (gridDim.z > 1, swap tiles): K steps per cluster CTA
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -78,12 +78,12 @@ def test_attention_unsupported_head_dim_and_workspace():
 def test_split_heuristic():
     L = _lib.lib()
     assert L.lmps_gqa_attention_splits(1, 2, 160, 64) == 3        # bounded by 64-position tiles
-    assert L.lmps_gqa_attention_splits(4, 2, 32768 + 128, 64) == 74    # 514 tiles, <= 592 CTAs: 7 tiles each
-    assert L.lmps_gqa_attention_splits(64, 2, 384, 64) == 3         # 6 tiles, at most 4 splits: 2 each
-    assert L.lmps_gqa_attention_splits(64, 2, 416, 64) == 4         # 7 tiles: 2, 2, 2, 1
-    assert L.lmps_gqa_attention_splits(16, 2, 1024, 64) == 16       # one tile per split
-    assert L.lmps_gqa_attention_splits(128, 2, 4096, 64) == 2       # 256 items: two splits fit
-    assert L.lmps_gqa_attention_splits(256, 2, 4096, 64) == 1       # 512 items fill the GPU
+    assert L.lmps_gqa_attention_splits(4, 2, 32768 + 128, 64) == 52    # 514 tiles, <= 444 CTAs: 10 tiles each
+    assert L.lmps_gqa_attention_splits(64, 2, 384, 64) == 3         # 6 tiles, at most 3 splits: 2 each
+    assert L.lmps_gqa_attention_splits(64, 2, 416, 64) == 3         # 7 tiles: 3, 3, 1
+    assert L.lmps_gqa_attention_splits(16, 2, 1024, 64) == 8        # two tiles per split
+    assert L.lmps_gqa_attention_splits(128, 2, 4096, 64) == 1       # 256 items: the grid is full
+    assert L.lmps_gqa_attention_splits(256, 2, 4096, 64) == 1
 
 
 def test_tensor_parallel_exchange_validation():
