@@ -40,6 +40,7 @@
 #include <cmath>
 
 #include "common.cuh"
+#include "flash_decode.cuh"
 
 namespace lmps {
 namespace pk {
@@ -1242,7 +1243,7 @@ __device__ void gemv_down(const Params& P, Smem& S, CState& cs, int layer, uint3
 // output row r of m-tile mt is physical dim
 // 8((r & 7) >> 1) + 32(mt >> 1) + 4(mt & 1) + 2(r >> 3) + (r & 1);
 // movmatrix transposes V rows and probabilities in registers.
-constexpr int kBlk = 16;        // positions per warp block
+using fd::kBlk;                 // positions per warp block
 constexpr int kMinSplit = 512;  // positions per work item before the positions split across CTAs
 constexpr int kKvSlotPos = 2 * kBlk;  // positions per ring slot (spread attention): K and V tiles, 16 KB
 
@@ -1272,27 +1273,11 @@ __device__ __forceinline__ void st_kv8(__half* p, const uint4& v, uint64_t pol) 
                : "memory");
 }
 
-__device__ __forceinline__ uint32_t movmatrix_t(uint32_t a) {
-  uint32_t d;
-  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
-  return d;
-}
-__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
-  const __half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
-__device__ __forceinline__ uint32_t word_of(const uint4 (&v)[4], int w) {
-  const uint4 q = v[w >> 2];
-  return (w & 3) == 0 ? q.x : (w & 3) == 1 ? q.y : (w & 3) == 2 ? q.z : q.w;
-}
-__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                          uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
+// mma / movmatrix helpers of flash_decode.cuh
+using fd::mma_16816;
+using fd::movmatrix_t;
+using fd::pack_half2;
+using fd::word_of;
 
 __device__ __forceinline__ void rope_pair(int j, int style, int& i1, int& i2) {
   if (style == LMPS_ROPE_INTERLEAVED) {

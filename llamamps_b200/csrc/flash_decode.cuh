@@ -1,6 +1,5 @@
-// Flash-decoding block math shared by the decode attention kernels (the
-// persistent decoder's attention stage and the split-KV gqa_decode_attn
-// kernel): one warp folds a 16-position block of one KV head's cache into
+// Flash-decoding block math of the decode attention kernels: one warp
+// folds a 16-position block of one KV head's cache into
 // its running softmax state for the G <= 8 query heads sharing that head
 // (softmax.metal:23-36 online; attention.metal:32-40 scores, attn_sum.metal:26-32
 // weighted sum), on the tensor cores (mma.sync m16n8k16, fp16 in, fp32
@@ -14,6 +13,11 @@
 // output row r of m-tile mt is physical dim
 // 8((r & 7) >> 1) + 32(mt >> 1) + 4(mt & 1) + 2(r >> 3) + (r & 1);
 // movmatrix transposes V rows and probabilities in registers.
+// The split-KV gqa_decode_attn kernel uses all of it; the persistent
+// decoder's attention stage uses the helpers and the same dim mapping with
+// its own inlined fold (one S accumulator chain: inside that kernel the two
+// chains below cost registers it does not have -- bs1 decode 662 vs 625
+// us/step).
 #pragma once
 
 #include "common.cuh"
