@@ -198,7 +198,10 @@ int lmps_gqa_decode_attention_noalloc(const uint16_t* q, const uint16_t* k_pool,
  * dense contractions: y[m, :n] = x[m, :k] . W^T with W the Q4 [n, k] layout of
  * lmps_gemv_q4_0 (dequantised to fp16 tile by tile), fp32 accumulate, fp16 out.
  * epilogue: 0 none, 1 + bias[n], 2 residual[m, n] + fp16(acc) (residual may
- * alias y).  n must be a multiple of 128 and k of 64 (else UNSUPPORTED); any
+ * alias y), 3 SwiGLU (swiglu.metal:13-23): W's rows interleave gate and up
+ * (row 2t = gate row t, 2t + 1 = up row t) and y[m, t] =
+ * fp16(silu(fp16(gate)) * fp16(up)) for t < n/2 (ldy >= n/2).
+ * n must be a multiple of 128 and k of 64 (else UNSUPPORTED); any
  * m >= 1.  error[0] is set to 1 if a bounded wait for the tensor core gives up.
  * Calls with fewer than 128 tokens split K over the CTAs of a thread-block
  * cluster and sum the partial tiles in distributed shared memory, so the
@@ -208,6 +211,7 @@ int lmps_gqa_decode_attention_noalloc(const uint16_t* q, const uint16_t* k_pool,
 #define LMPS_EPI_NONE 0
 #define LMPS_EPI_BIAS 1
 #define LMPS_EPI_RESIDUAL 2
+#define LMPS_EPI_SWIGLU 3
 size_t lmps_w4a16_gemm_workspace_size(int m, int n);
 int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed, const uint16_t* scales,
                     const uint16_t* bias, const uint16_t* residual, int ldr, uint16_t* y, int ldy,

@@ -48,7 +48,10 @@ constexpr int kStepBytes = kRows * kBK / 2;   // packed W bytes of one K step (4
 constexpr int kWTileBytes = kRows * kBK * 2;  // 16 KB fp16
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
 
-enum Epilogue { EPI_NONE = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2 };
+// EPI_SWIGLU: W holds gate and up rows interleaved (row 2t = gate row t, row
+// 2t + 1 = up row t) and Y[m][t] = fp16(silu(fp16(gate)) * fp16(up)), the
+// math of swiglu.metal:13-23 on the two fp16 projection outputs.
+enum Epilogue { EPI_NONE = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2, EPI_SWIGLU = 3 };
 
 struct __align__(64) Params {
   CUtensorMap tx;  // X [m, k] fp16, box {64, xrows}, 128-byte swizzle
@@ -206,6 +209,9 @@ __device__ __forceinline__ __half epi_value(const Params& P, float v, int row, i
   if (P.epi == EPI_BIAS) return __float2half_rn(v + __half2float(P.bias[col]));
   if (P.epi == EPI_RESIDUAL) return __hadd(P.res[static_cast<size_t>(row) * P.ldr + col], __float2half_rn(v));
   return __float2half_rn(v);
+}
+__device__ __forceinline__ __half swiglu_value(float gate, float up) {
+  return __float2half_rn(silu_mul(__half2float(__float2half_rn(gate)), __half2float(__float2half_rn(up))));
 }
 
 __global__ void __launch_bounds__(kThreads) w4a16_gemm_kernel(const __grid_constant__ Params P) {
@@ -455,7 +461,25 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_kernel(const __grid_const
     // Barrier 2: every partial row has arrived; each CTA sums and writes its rows.
     asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
     const int tok = min(P.xrows, P.m - m0), tok4 = (tok + 3) / 4;
-    for (int i = tid; i < rows_per * tok4; i += kThreads) {
+    if (P.epi == EPI_SWIGLU) {  // a thread per (gate, up) row pair and 4 tokens
+      const int pairs = rows_per / 2;
+      for (int i = tid; i < pairs * tok4; i += kThreads) {
+        const int lp = i % pairs, j = 4 * (i / pairs);
+        float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = g;
+        for (int c = 0; c < nsplit; ++c) {
+          const float4 vg = *reinterpret_cast<const float4*>(red + (c * rows_per + 2 * lp) * rs + j);
+          const float4 vu = *reinterpret_cast<const float4*>(red + (c * rows_per + 2 * lp + 1) * rs + j);
+          g.x += vg.x; g.y += vg.y; g.z += vg.z; g.w += vg.w;
+          u.x += vu.x; u.y += vu.y; u.z += vu.z; u.w += vu.w;
+        }
+        const float ga[4] = {g.x, g.y, g.z, g.w}, ua[4] = {u.x, u.y, u.z, u.w};
+        const int col = (n0 + static_cast<int>(rank) * rows_per) / 2 + lp;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (j + e < tok) P.y[static_cast<size_t>(m0 + j + e) * P.ldy + col] = swiglu_value(ga[e], ua[e]);
+      }
+    }
+    for (int i = tid; P.epi != EPI_SWIGLU && i < rows_per * tok4; i += kThreads) {
       const int lr = i % rows_per, j = 4 * (i / rows_per);
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int c = 0; c < nsplit; ++c) {
@@ -482,7 +506,13 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_kernel(const __grid_const
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         const int rw = m0 + c0 + j;
-        if (rw < P.m) P.y[static_cast<size_t>(rw) * P.ldy + col] = epi_value(P, __uint_as_float(r[j]), rw, col);
+        if (P.epi == EPI_SWIGLU) {  // gate row in the even lane, its up row in the next
+          const float up = __shfl_down_sync(0xffffffffu, __uint_as_float(r[j]), 1);
+          if ((lane & 1) == 0 && rw < P.m)
+            P.y[static_cast<size_t>(rw) * P.ldy + col / 2] = swiglu_value(__uint_as_float(r[j]), up);
+        } else if (rw < P.m) {
+          P.y[static_cast<size_t>(rw) * P.ldy + col] = epi_value(P, __uint_as_float(r[j]), rw, col);
+        }
       }
     }
   } else if (ok) {
@@ -492,7 +522,21 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_kernel(const __grid_const
     for (int c0 = 0; c0 < kRows; c0 += 32) {
       uint32_t r[32];
       tmem_ld32(tl + c0, r);
-      if (rw < P.m) {
+      if (rw < P.m && P.epi == EPI_SWIGLU) {  // 16 (gate, up) pairs -> 16 outputs
+        __half* yrow = P.y + static_cast<size_t>(rw) * P.ldy + (n0 + c0) / 2;
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i = 16 * g + 4 * e;  // pairs (i, i + 1), (i + 2, i + 3)
+            const __half2 hh = __halves2half2(swiglu_value(__uint_as_float(r[i]), __uint_as_float(r[i + 1])),
+                                              swiglu_value(__uint_as_float(r[i + 2]), __uint_as_float(r[i + 3])));
+            o[e] = *reinterpret_cast<const uint32_t*>(&hh);
+          }
+          *reinterpret_cast<uint4*>(yrow + 8 * g) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      } else if (rw < P.m) {
         __half* yrow = P.y + static_cast<size_t>(rw) * P.ldy + n0 + c0;
 #pragma unroll
         for (int g = 0; g < 4; ++g) {  // 8 columns per 16-byte store
@@ -638,7 +682,21 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
       for (int c0 = 0; c0 < kRows; c0 += 32) {
         uint32_t r[32];
         tmem_ld32(tl + c0, r);
-        if (rw < P.m) {
+        if (rw < P.m && P.epi == EPI_SWIGLU) {  // 16 (gate, up) pairs -> 16 outputs
+          __half* yrow = P.y + static_cast<size_t>(rw) * P.ldy + (n0 + c0) / 2;
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i = 16 * g + 4 * e;  // pairs (i, i + 1), (i + 2, i + 3)
+              const __half2 hh = __halves2half2(swiglu_value(__uint_as_float(r[i]), __uint_as_float(r[i + 1])),
+                                                swiglu_value(__uint_as_float(r[i + 2]), __uint_as_float(r[i + 3])));
+              o[e] = *reinterpret_cast<const uint32_t*>(&hh);
+            }
+            *reinterpret_cast<uint4*>(yrow + 8 * g) = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+        } else if (rw < P.m) {
           __half* yrow = P.y + static_cast<size_t>(rw) * P.ldy + n0 + c0;
 #pragma unroll
           for (int g = 0; g < 4; ++g) {  // 8 columns per 16-byte store
@@ -733,10 +791,11 @@ extern "C" int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed
   LMPS_CHECK_ARG(x && packed && scales && y && error);
   LMPS_CHECK_ARG(m >= 1 && n >= 1 && k >= 1);
   if (n % w4::kRows != 0 || k % w4::kBK != 0) return LMPS_ERR_UNSUPPORTED;
-  LMPS_CHECK_ARG(epilogue >= w4::EPI_NONE && epilogue <= w4::EPI_RESIDUAL);
+  LMPS_CHECK_ARG(epilogue >= w4::EPI_NONE && epilogue <= w4::EPI_SWIGLU);
   LMPS_CHECK_ARG(epilogue != w4::EPI_BIAS || bias);
   LMPS_CHECK_ARG(epilogue != w4::EPI_RESIDUAL || (residual && ldr >= n));
-  LMPS_CHECK_ARG(ldx >= k && ldx % 8 == 0 && ldy >= n && ldy % 8 == 0);
+  const int ncols = epilogue == w4::EPI_SWIGLU ? n / 2 : n;  // Y columns
+  LMPS_CHECK_ARG(ldx >= k && ldx % 8 == 0 && ldy >= ncols && ldy % 8 == 0);
   LMPS_CHECK_ARG(lmps_aligned(x, 16) && lmps_aligned(y, 16) && lmps_aligned(packed, 16) && lmps_aligned(scales, 4));
   w4::Params P{};
   const int xr = w4_xrows(m);

@@ -205,12 +205,12 @@ class QwenEngine:
 
     def _gate_up(self, lw, xn, gu, out, ws=None) -> None:
         """a = SwiGLU(W_gate xn, W_up xn) on the GEMM path: one GEMM over the
-        fused gate|up rows when the layer stores them together, else two."""
+        interleaved gate/up rows with the SwiGLU epilogue when the layer has
+        them, else two GEMMs and the SwiGLU kernel."""
         c = self.cfg
         if lw.gu_packed is not None:
-            K.w4a16_gemm(xn, lw.gu_packed, lw.gu_scales, 2 * c.intermediate, c.hidden, out=gu,
+            K.w4a16_gemm(xn, lw.gu_packed, lw.gu_scales, 2 * c.intermediate, c.hidden, swiglu=True, out=out,
                          error=self.gemm_err, workspace=self._ws(ws))
-            K.swiglu_rows(gu, c.intermediate, out)
         else:
             up = gu.reshape(-1)[:out.numel()].view(out.shape)  # contiguous [B, intermediate] scratch
             K.w4a16_gemm(xn, lw.gate_packed, lw.gate_scales, c.intermediate, c.hidden, out=out,

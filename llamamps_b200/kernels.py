@@ -218,24 +218,28 @@ def decode_advance(next_ids, tokens, pos, seq_lens, history=None, step=None):
          _dev(step, "step", torch.int32) if step is not None else None, max_steps, B, _stream())
 
 
-EPI_NONE, EPI_BIAS, EPI_RESIDUAL = 0, 1, 2
+EPI_NONE, EPI_BIAS, EPI_RESIDUAL, EPI_SWIGLU = 0, 1, 2, 3
 
 
 def w4a16_gemm_workspace_size(m: int, n: int) -> int:
     return int(lib().lmps_w4a16_gemm_workspace_size(m, n))
 
 
-def w4a16_gemm(x, packed, scales, n: int, k: int, *, bias=None, residual=None, out=None,
+def w4a16_gemm(x, packed, scales, n: int, k: int, *, bias=None, residual=None, swiglu: bool = False, out=None,
                error: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None):
     """tcgen05 W4A16 GEMM: out[m] = x[m] . W^T (+ bias | residual + fp16(.)).
 
     x is fp16 [m, k] (token-major); W the Q4 [n, k] layout.  Used where the
     projections of many tokens at once are dense contractions (prefill, large
-    batches).  Calls with m < 128 split K inside a thread-block cluster;
-    ``workspace`` is accepted for API stability and unused."""
+    batches).  ``swiglu``: W's rows interleave gate and up rows and out[m, t] =
+    SwiGLU(gate row t, up row t), n / 2 columns (interleave_rows builds W).
+    Calls with m < 128 split K inside a thread-block cluster; ``workspace`` is
+    accepted for API stability and unused."""
     x2, m = _x2d(x)
-    y = out if out is not None else torch.empty(m, n, dtype=FP16, device=x.device)
-    epi, b_ptr, r_ptr, ldr = EPI_NONE, None, None, 0
+    y = out if out is not None else torch.empty(m, n // 2 if swiglu else n, dtype=FP16, device=x.device)
+    epi, b_ptr, r_ptr, ldr = (EPI_SWIGLU if swiglu else EPI_NONE), None, None, 0
+    if swiglu and (bias is not None or residual is not None):
+        raise ValueError("the SwiGLU epilogue takes no bias or residual")
     if bias is not None:
         epi, b_ptr = EPI_BIAS, _dev(bias, "bias", FP16)
     if residual is not None:

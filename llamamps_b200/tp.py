@@ -36,7 +36,7 @@ import torch.distributed as dist
 from . import kernels as K
 from .config import ModelConfig
 from .engine import QwenEngine
-from .weights import LayerWeights, ModelWeights
+from .weights import LayerWeights, ModelWeights, interleave_rows
 
 
 def local_config(cfg: ModelConfig, world: int) -> ModelConfig:
@@ -80,9 +80,11 @@ def shard_layer(lw: LayerWeights, cfg: ModelConfig, rank: int, world: int) -> La
     u_p, u_s = _rows(lw.up_packed, lw.up_scales, D, [(i0, i1)])
     d_p, d_s = _cols(lw.down_packed, lw.down_scales, cfg.intermediate, i0, i1)
     del hd
+    n = loc.intermediate
     return LayerWeights(in_norm=lw.in_norm, post_norm=lw.post_norm, qkv_packed=qkv_p, qkv_scales=qkv_s,
                         qkv_bias=bias, o_packed=o_p, o_scales=o_s, gate_packed=g_p, gate_scales=g_s,
-                        up_packed=u_p, up_scales=u_s, down_packed=d_p, down_scales=d_s)
+                        up_packed=u_p, up_scales=u_s, down_packed=d_p, down_scales=d_s,
+                        gu_packed=interleave_rows(g_p, u_p, n), gu_scales=interleave_rows(g_s, u_s, n))
 
 
 def shard_model(mw: ModelWeights, rank: int, world: int) -> ModelWeights:

@@ -49,9 +49,9 @@ class LayerWeights:
     up_scales: torch.Tensor
     down_packed: torch.Tensor
     down_scales: torch.Tensor
-    # gate rows then up rows in one allocation (gate_* / up_* are views of
-    # it): the batched path runs both projections as one GEMM.  None when the
-    # two matrices are separate allocations.
+    # gate and up rows interleaved (row 2t = gate row t, 2t + 1 = up row t),
+    # a copy for the batched path: one GEMM with the SwiGLU epilogue.  None
+    # when absent (two GEMMs and a SwiGLU kernel instead).
     gu_packed: Optional[torch.Tensor] = None
     gu_scales: Optional[torch.Tensor] = None
 
@@ -81,6 +81,13 @@ def _mat_shape(cfg: ModelConfig, name: str):
             "gate": (i, d), "up": (i, d), "down": (d, i)}[name]
 
 
+def interleave_rows(a: torch.Tensor, b: torch.Tensor, rows: int) -> torch.Tensor:
+    """Row-interleave two [rows, w] matrices given flat: row 2t of the result
+    is a's row t, row 2t + 1 is b's (the gate/up layout of the GEMM's SwiGLU
+    epilogue)."""
+    return torch.stack([a.reshape(rows, -1), b.reshape(rows, -1)], dim=1).reshape(-1).contiguous()
+
+
 def layer_from_parts(cfg: ModelConfig, parts: Dict[str, torch.Tensor], device) -> LayerWeights:
     """Assemble the device layout from per-matrix packed/scales (+ optional bias)."""
     dev = torch.device(device)
@@ -93,10 +100,7 @@ def layer_from_parts(cfg: ModelConfig, parts: Dict[str, torch.Tensor], device) -
         b = parts.get(f"{n}_bias")
         bias.append(t(b, torch.float16) if b is not None else torch.zeros(rows, dtype=torch.float16, device=dev))
     gp, gs = t(parts["gate_packed"], torch.uint8), t(parts["gate_scales"], torch.float16)
-    gu_packed = torch.cat([gp, t(parts["up_packed"], torch.uint8)])
-    gu_scales = torch.cat([gs, t(parts["up_scales"], torch.float16)])
-    ng, ngs = gp.numel(), gs.numel()
-    del gp, gs
+    up, us = t(parts["up_packed"], torch.uint8), t(parts["up_scales"], torch.float16)
     return LayerWeights(
         in_norm=t(parts["in_norm"], torch.float16),
         post_norm=t(parts["post_norm"], torch.float16),
@@ -104,10 +108,9 @@ def layer_from_parts(cfg: ModelConfig, parts: Dict[str, torch.Tensor], device) -
         qkv_scales=torch.cat([t(parts[f"{n}_scales"], torch.float16) for n in "qkv"]),
         qkv_bias=torch.cat(bias),
         o_packed=t(parts["o_packed"], torch.uint8), o_scales=t(parts["o_scales"], torch.float16),
-        gate_packed=gu_packed[:ng], gate_scales=gu_scales[:ngs],
-        up_packed=gu_packed[ng:], up_scales=gu_scales[ngs:],
+        gate_packed=gp, gate_scales=gs, up_packed=up, up_scales=us,
         down_packed=t(parts["down_packed"], torch.uint8), down_scales=t(parts["down_scales"], torch.float16),
-        gu_packed=gu_packed, gu_scales=gu_scales,
+        gu_packed=interleave_rows(gp, up, cfg.intermediate), gu_scales=interleave_rows(gs, us, cfg.intermediate),
     )
 
 

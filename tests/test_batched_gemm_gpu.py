@@ -112,6 +112,31 @@ def test_swiglu_rows_matches_two_input_swiglu(cuda):
     assert torch.equal(out, ref)
 
 
+@pytest.mark.parametrize("m", [1, 5, 64, 127, 128, 300])
+def test_gemm_swiglu_epilogue_equals_gemm_then_swiglu(cuda, m):
+    """The GEMM's SwiGLU epilogue over row-interleaved gate/up weights, bit for
+    bit the GEMM over [gate; up] followed by swiglu_rows, on both tile shapes
+    (decode tiles with split K below 128 tokens, prefill tiles above)."""
+    from llamamps_b200 import kernels as K
+    from llamamps_b200.quant import pack_q4
+    from llamamps_b200.weights import interleave_rows
+    n, k = 640, 1536
+    g = torch.Generator(device="cuda").manual_seed(m)
+    gate = torch.randn(n, k, generator=g, device="cuda") * 0.02
+    up = torch.randn(n, k, generator=g, device="cuda") * 0.02
+    gp, gs = pack_q4(gate)
+    upk, us = pack_q4(up)
+    x = torch.randn(m, k, generator=g, device="cuda").half()
+    cat = K.w4a16_gemm(x, torch.cat([gp, upk]), torch.cat([gs, us]), 2 * n, k)
+    ref = torch.empty(m, n, dtype=torch.float16, device="cuda")
+    K.swiglu_rows(cat, n, ref)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    got = K.w4a16_gemm(x, interleave_rows(gp, upk, n), interleave_rows(gs, us, n), 2 * n, k, swiglu=True,
+                       error=err)
+    assert got.shape == (m, n) and int(err.item()) == 0
+    assert torch.equal(got, ref)
+
+
 @pytest.mark.parametrize("decoder", ["kernels", "persistent"])
 def test_dense_prefill_matches_oracle(cuda, small_model, decoder):
     """Prompts prefilled all at once on the GEMM path (3 x 100 tokens), then
