@@ -520,19 +520,21 @@ def time_prefill_attention(B: int, P: int, iters: int = 5) -> dict:
     bt = torch.randperm(B * pages, generator=g, device="cuda").to(torch.int32).reshape(B, pages)
     q = torch.randn(B * P, hq * hd, generator=g, device="cuda").half()
     out = torch.empty_like(q)
-    for _ in range(2):
-        K.prefill_attention(q, kp, vp, bt, out, B, P, ps, hq, hkv, hd)
-    torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(iters):
-        K.prefill_attention(q, kp, vp, bt, out, B, P, ps, hq, hkv, hd)
-    b.record()
-    torch.cuda.synchronize()
-    t = a.elapsed_time(b) / iters / 1e3
     flops = 4.0 * hd * P * (P + 1) / 2 * B * hq
-    return {"kernel": "prefill_attn_kernel", "batch": B, "seq_len": P, "us": round(t * 1e6, 1),
-            "tflops": round(flops / t / 1e12, 1)}
+    res = {"batch": B, "seq_len": P}
+    for name, tc in (("prefill_attn_tc_kernel", True), ("prefill_attn_kernel", False)):
+        for _ in range(2):
+            K.prefill_attention(q, kp, vp, bt, out, B, P, ps, hq, hkv, hd, tcgen05=tc)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(iters):
+            K.prefill_attention(q, kp, vp, bt, out, B, P, ps, hq, hkv, hd, tcgen05=tc)
+        b.record()
+        torch.cuda.synchronize()
+        t = a.elapsed_time(b) / iters / 1e3
+        res[name] = {"us": round(t * 1e6, 1), "tflops": round(flops / t / 1e12, 1)}
+    return res
 
 
 def time_gemv(rows: int, k: int, batch: int, iters: int = 20) -> dict:

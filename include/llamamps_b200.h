@@ -229,6 +229,18 @@ int lmps_prefill_attention(const uint16_t* q, int ldq, const uint16_t* k_pool, c
                            const int32_t* block_table, int max_pages, int page_size, uint16_t* out, int ldo,
                            int batch, int seq_len, int n_q_heads, int n_kv_heads, int head_dim, void* stream);
 
+/* The same causal prefill attention on the tcgen05 tensor cores with S and O
+ * accumulators in tensor memory and K/V tiles loaded by TMA from the pools
+ * (n_pages pages of [n_kv_heads, page_size, head_dim] each).  Takes head_dim
+ * 128, page_size a multiple of 64 and an even n_q_heads / n_kv_heads (else
+ * UNSUPPORTED: use lmps_prefill_attention).  q, the pools and out 16-byte
+ * aligned, ldq and ldo multiples of 8.  error[0] is set to 1 if a bounded
+ * wait for the tensor core gives up. */
+int lmps_prefill_attention_tcgen05(const uint16_t* q, int ldq, const uint16_t* k_pool, const uint16_t* v_pool,
+                                   int n_pages, const int32_t* block_table, int max_pages, int page_size,
+                                   uint16_t* out, int ldo, int batch, int seq_len, int n_q_heads,
+                                   int n_kv_heads, int head_dim, int32_t* error, void* stream);
+
 /* First-index argmax of each row of fp16 logits [rows, ld] over n columns
  * (runners/engine.py:180-181), the large-batch companion of the LM-head GEMM. */
 int lmps_argmax_rows(const uint16_t* logits, int ld, int rows, int n, int32_t* ids, void* stream);

@@ -48,6 +48,8 @@ _SIGS = {
     "lmps_decode_advance": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_vp]),
     "lmps_prefill_attention": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_vp, c_int, c_int, c_int,
                                        c_int, c_int, c_int, c_vp]),
+    "lmps_prefill_attention_tcgen05": (c_int, [c_vp, c_int, c_vp, c_vp, c_int, c_vp, c_int, c_int, c_vp, c_int,
+                                               c_int, c_int, c_int, c_int, c_int, c_vp, c_vp]),
     "lmps_swiglu_rows": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_int, c_vp]),
     "lmps_gqa_decode_attention_rope": (c_int, [c_vp, c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                                                c_size, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,

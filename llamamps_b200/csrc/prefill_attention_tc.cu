@@ -1,0 +1,367 @@
+// Causal prefill attention on the 5th-generation tensor cores (tcgen05.mma,
+// accumulators in tensor memory): the attention.metal / softmax.metal /
+// attn_sum.metal stages of runners/engine.py:202-212 for every prompt
+// position at once -- query p of a sequence attends to positions 0..p.
+//
+// One CTA per (128-query tile, pair of query heads of one KV head, KV head,
+// sequence); the longest query tiles are scheduled first.  Per 64-key tile
+// of the paged cache:
+//   * warp 0 (one lane) loads the tile's K and V rows with plain (non-
+//     multicast) TMA from this GPU's own pool into a two-stage ring (128-byte
+//     swizzle; the queries of both heads once at the start);
+//   * warp 1 (one lane) issues S_h = Q_h K^T (M = 128 queries, N = 64 keys,
+//     K = 128 dims) into TMEM, then, once the softmax has written P_h,
+//     O_h += P_h V (M = 128, N = 128 dims, K = 64 keys; V read MN-major
+//     straight from the cache rows);
+//   * warps 2-5 (thread = query row, its TMEM lane) read S_h, apply the
+//     scale 0.088388 and the causal mask, keep the running max and sum in
+//     fp32 (exp2), write P_h as fp16 into a 128-byte-swizzled K-major tile,
+//     and rescale O_h in TMEM only when the row max grows by more than 2^8
+//     (between rescales P stays below 2^8, so fp16 P and fp32 O are exact
+//     enough); at the end they read O_h, divide by the sum and store fp16.
+// The two heads alternate, so one head's softmax overlaps the other head's
+// MMAs.  Every mbarrier wait is bounded (error flag, no hang).
+#include <cmath>
+
+#include "common.cuh"
+#include "tcgen05.cuh"
+
+namespace lmps {
+namespace fa {
+
+using namespace tc;
+
+constexpr int kD = 128;        // head dim
+constexpr int kQ = 128;        // queries per tile (TMEM lanes)
+constexpr int kKV = 64;        // keys per tile
+constexpr int kH = 2;          // query heads per CTA
+constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 softmax + epilogue
+constexpr int kQSub = kQ * 128;    // 64 dims of a Q tile: 128 rows x 128 bytes
+constexpr int kKVSub = kKV * 128;  // 64 dims of a K or V tile: 64 rows x 128 bytes
+constexpr int kPTile = kQ * 128;   // P tile: 128 rows x 64 keys fp16
+constexpr int kOffK = kH * 2 * kQSub;          // 64 KB of Q
+constexpr int kOffV = kOffK + 2 * 2 * kKVSub;  // two stages of K
+constexpr int kOffP = kOffV + 2 * 2 * kKVSub;  // two stages of V
+constexpr int kOffBar = kOffP + kH * kPTile;
+constexpr int kSmemBytes = kOffBar + 16 * 8 + 1024;  // barriers, TMEM slot, abort flag; 1024-byte alignment slack
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0;    // S_h at columns 64 h
+constexpr uint32_t kColO = 128;  // O_h at columns 128 + 128 h
+constexpr float kScaleLog2 = 0.088388f * 1.4426950408889634f;  // attention.metal:40 scale, base 2
+constexpr float kRescaleLog2 = 8.0f;
+
+struct Params {
+  CUtensorMap tq;  // q [batch * seq_len, ldq] fp16, box {64, 128}
+  CUtensorMap tk;  // K pool [n_pages * n_kv * page_size, 128] fp16, box {64, 64}
+  CUtensorMap tv;
+  const int32_t* bt;  // [batch, max_pages]
+  __half* out;        // [batch * seq_len, ldo]
+  int ldo, seq_len, n_q, n_kv, max_pages, page_size, n_qtiles, head_pairs;
+  int* error;
+};
+
+__global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __grid_constant__ Params P) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  unsigned char* sq = base;
+  unsigned char* sk = base + kOffK;
+  unsigned char* sv = base + kOffV;
+  unsigned char* sp = base + kOffP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + kOffBar);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [kH]
+  uint64_t* p_full = bars + 7;    // [kH]
+  uint64_t* o_done = bars + 9;    // [kH]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  volatile int* abort_v = abort_flag;
+
+  lmps_pdl_trigger();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // work item: the query tile varies slowest, longest first
+  const int per_tile = static_cast<int>(gridDim.x) / P.n_qtiles;  // items per query tile
+  const int qt = P.n_qtiles - 1 - static_cast<int>(blockIdx.x) / per_tile;
+  int rest = static_cast<int>(blockIdx.x) % per_tile;
+  const int hp = rest % P.head_pairs;
+  rest /= P.head_pairs;
+  const int kvh = rest % P.n_kv, b = rest / P.n_kv;
+  const int G = P.n_q / P.n_kv;
+  const int h0 = kvh * G + 2 * hp;  // first query head of the pair
+  const int q0 = qt * kQ;
+  const int qend = min(P.seq_len, q0 + kQ);
+  const int nt = (qend + kKV - 1) / kKV;  // key tiles 0 .. nt-1 reach the tile's last query
+
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int h = 0; h < kH; ++h) {
+      mbar_init(&s_full[h], 1);
+      mbar_init(&p_full[h], kQ);
+      mbar_init(&o_done[h], 1);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (tid == 32) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&P.tq)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&P.tk)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&P.tv)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  lmps_pdl_wait();  // the queries and the cache rows come from the previous kernels
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer
+      mbar_expect_tx(q_full, kH * 2 * kQSub);
+      for (int h = 0; h < kH; ++h)
+        for (int dh = 0; dh < 2; ++dh)
+          tma_load_2d(sq + (2 * h + dh) * kQSub, &P.tq, (h0 + h) * kD + 64 * dh, b * P.seq_len + q0, q_full);
+      const int32_t* bt = P.bt + static_cast<size_t>(b) * P.max_pages;
+      int issued = 0;
+      for (int i = 0; i < nt; ++i) {
+        const int s = i & 1;
+        if (i >= 2 && !mbar_wait(&kv_empty[s], ((i >> 1) - 1) & 1, P.error, abort_v)) break;
+        const int k0 = i * kKV;
+        const int row = (__ldg(bt + k0 / P.page_size) * P.n_kv + kvh) * P.page_size + k0 % P.page_size;
+        mbar_expect_tx(&kv_full[s], 4 * kKVSub);
+        for (int dh = 0; dh < 2; ++dh) {
+          tma_load_2d(sk + (2 * s + dh) * kKVSub, &P.tk, 64 * dh, row, &kv_full[s]);
+          tma_load_2d(sv + (2 * s + dh) * kKVSub, &P.tv, 64 * dh, row, &kv_full[s]);
+        }
+        issued = i + 1;
+      }
+      // every issued copy lands before the CTA may exit
+      {
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try(q_full, 0))
+          if (globaltimer() - t0 > kTimeoutNs) break;
+      }
+      for (int i = max(0, issued - 2); i < issued; ++i) {
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try(&kv_full[i & 1], (i >> 1) & 1))
+          if (globaltimer() - t0 > kTimeoutNs) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---- MMA issuer
+      const uint32_t id_s = idesc_f16(kQ, kKV), id_o = idesc_f16(kQ, kD) | kBMajorMN;
+      auto issue_s = [&](int h, int s) {  // S_h = Q_h K^T over 8 k-steps of 16 dims
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint64_t a = sw128_desc(smem_u32(sq + (2 * h + (j >> 2)) * kQSub)) + 2 * (j & 3);
+          const uint64_t bk = sw128_desc(smem_u32(sk + (2 * s + (j >> 2)) * kKVSub)) + 2 * (j & 3);
+          mma_f16(tmem + kColS + kKV * h, a, bk, id_s, j > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_o = [&](int h, int s, bool acc) {  // O_h += P_h V over 4 k-steps of 16 keys
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint64_t a = sw128_desc(smem_u32(sp + h * kPTile)) + 2 * j;
+          const uint64_t bv = sw128_mn_desc(smem_u32(sv + (2 * s) * kKVSub + 2048 * j), kKVSub);
+          mma_f16(tmem + kColO + kD * h, a, bv, id_o, (acc || j > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(q_full, 0, P.error, abort_v) && mbar_wait(&kv_full[0], 0, P.error, abort_v);
+      if (ok) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        for (int h = 0; h < kH; ++h) {
+          issue_s(h, 0);
+          mma_commit(&s_full[h]);
+        }
+      }
+      for (int i = 0; ok && i < nt; ++i) {
+        const int s = i & 1;
+        for (int h = 0; h < kH; ++h) {
+          if (!mbar_wait(&p_full[h], i & 1, P.error, abort_v)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          issue_o(h, s, i > 0);
+          mma_commit(&o_done[h]);
+          if (i + 1 < nt) {  // S_h of the next tile: the softmax has read S_h of this one
+            if (h == 0 && !mbar_wait(&kv_full[s ^ 1], ((i + 1) >> 1) & 1, P.error, abort_v)) {
+              ok = false;
+              break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            issue_s(h, s ^ 1);
+            mma_commit(&s_full[h]);
+          }
+        }
+        if (ok) mma_commit(&kv_empty[s]);  // this tile's K and V are free once the MMAs above are done
+      }
+    }
+  } else {
+    // ---- softmax (thread = query row r of the tile, TMEM lane r)
+    const int quad = warp & 3, r = 32 * quad + lane, qi = q0 + r;
+    const uint32_t tl = tmem + (static_cast<uint32_t>(32 * quad) << 16);
+    float m_used[kH], l[kH];
+#pragma unroll
+    for (int h = 0; h < kH; ++h) {
+      m_used[h] = -INFINITY;
+      l[h] = 0.0f;
+    }
+    bool ok = true;
+    for (int i = 0; ok && i < nt; ++i) {
+      const int k0 = i * kKV;
+#pragma unroll
+      for (int h = 0; h < kH; ++h) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&s_full[h], i & 1, P.error, abort_v));
+        if (!ok) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        uint32_t sv0[32], sv1[32];
+        tmem_ld32(tl + kColS + kKV * h, sv0);
+        tmem_ld32(tl + kColS + kKV * h + 32, sv1);
+        float mt = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float x0 = k0 + c > qi ? -INFINITY : __uint_as_float(sv0[c]) * kScaleLog2;
+          const float x1 = k0 + 32 + c > qi ? -INFINITY : __uint_as_float(sv1[c]) * kScaleLog2;
+          sv0[c] = __float_as_uint(x0);
+          sv1[c] = __float_as_uint(x1);
+          mt = fmaxf(mt, fmaxf(x0, x1));
+        }
+        if (i > 0) {  // O_h of the previous tile is done: O_h may be rescaled and P_h rewritten
+          ok = __all_sync(0xffffffffu, mbar_wait(&o_done[h], (i - 1) & 1, P.error, abort_v));
+          if (!ok) break;
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        }
+        const float mnew = fmaxf(m_used[h], mt);
+        const bool grow = mnew > m_used[h] + kRescaleLog2;  // (always on the first tile)
+        const float alpha = grow ? exp2f(m_used[h] - mnew) : 1.0f;
+        if (i > 0 && __any_sync(0xffffffffu, grow)) {  // warp-wide read-modify-write of O_h
+#pragma unroll 1
+          for (int cc = 0; cc < kD; cc += 32) {
+            uint32_t o[32];
+            tmem_ld32(tl + kColO + kD * h + cc, o);
+#pragma unroll
+            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+            tmem_st32(tl + kColO + kD * h + cc, o);
+          }
+        }
+        if (grow) {
+          l[h] *= alpha;
+          m_used[h] = mnew;
+        }
+        // P = 2^(s - m) as fp16 into row r of the swizzled K-major P tile
+        uint32_t pk[32];
+        float sum = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const float a0 = exp2f(__uint_as_float(sv0[2 * c]) - m_used[h]);
+          const float a1 = exp2f(__uint_as_float(sv0[2 * c + 1]) - m_used[h]);
+          const float b0 = exp2f(__uint_as_float(sv1[2 * c]) - m_used[h]);
+          const float b1 = exp2f(__uint_as_float(sv1[2 * c + 1]) - m_used[h]);
+          sum += (a0 + a1) + (b0 + b1);
+          const __half2 ha = __floats2half2_rn(a0, a1), hb = __floats2half2_rn(b0, b1);
+          pk[c] = *reinterpret_cast<const uint32_t*>(&ha);
+          pk[16 + c] = *reinterpret_cast<const uint32_t*>(&hb);
+        }
+        l[h] += sum;
+        unsigned char* prow = sp + h * kPTile + r * 128;
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch)
+          *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> the tensor core
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        mbar_arrive(&p_full[h]);
+      }
+    }
+    // ---- epilogue: O_h / l, fp16, this row of the output
+    for (int h = 0; ok && h < kH; ++h) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&o_done[h], (nt - 1) & 1, P.error, abort_v));
+      if (!ok) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const float inv = l[h] > 0.0f ? 1.0f / l[h] : 0.0f;
+      __half* orow = P.out + static_cast<size_t>(b * P.seq_len + qi) * P.ldo + (h0 + h) * kD;
+#pragma unroll 1
+      for (int cc = 0; cc < kD; cc += 32) {
+        uint32_t o[32];
+        tmem_ld32(tl + kColO + kD * h + cc, o);
+        if (qi < qend) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const __half2 hh = __floats2half2_rn(__uint_as_float(o[8 * g + 2 * e]) * inv,
+                                                   __uint_as_float(o[8 * g + 2 * e + 1]) * inv);
+              w[e] = *reinterpret_cast<const uint32_t*>(&hh);
+            }
+            *reinterpret_cast<uint4*>(orow + cc + 8 * g) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+}
+
+}  // namespace fa
+}  // namespace lmps
+
+using namespace lmps;
+
+extern "C" int lmps_prefill_attention_tcgen05(const uint16_t* q, int ldq, const uint16_t* k_pool,
+                                              const uint16_t* v_pool, int n_pages, const int32_t* block_table,
+                                              int max_pages, int page_size, uint16_t* out, int ldo, int batch,
+                                              int seq_len, int n_q_heads, int n_kv_heads, int head_dim,
+                                              int32_t* error, void* stream) {
+  LMPS_CHECK_ARG(q && k_pool && v_pool && block_table && out && error);
+  LMPS_CHECK_ARG(batch >= 1 && seq_len >= 1 && n_pages >= 1 && max_pages >= 1 && page_size >= 1);
+  LMPS_CHECK_ARG(n_kv_heads >= 1 && n_q_heads % n_kv_heads == 0);
+  LMPS_CHECK_ARG(static_cast<long long>(seq_len) <= static_cast<long long>(max_pages) * page_size);
+  const int G = n_q_heads / n_kv_heads;
+  // 64-key tiles inside one page, head pairs, 128-dim heads
+  if (head_dim != fa::kD || page_size % fa::kKV != 0 || G % fa::kH != 0) return LMPS_ERR_UNSUPPORTED;
+  LMPS_CHECK_ARG(ldq >= n_q_heads * head_dim && ldq % 8 == 0 && ldo >= n_q_heads * head_dim && ldo % 8 == 0);
+  LMPS_CHECK_ARG(lmps_aligned(q, 16) && lmps_aligned(k_pool, 16) && lmps_aligned(v_pool, 16) &&
+                 lmps_aligned(out, 16));
+  fa::Params P{};
+  const uint64_t pool_rows = static_cast<uint64_t>(n_pages) * n_kv_heads * page_size;
+  if (!tc::encode_2d(&P.tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, q, static_cast<uint64_t>(n_q_heads) * head_dim,
+                     static_cast<uint64_t>(batch) * seq_len, static_cast<uint64_t>(ldq) * 2, 64, fa::kQ,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !tc::encode_2d(&P.tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, k_pool, head_dim, pool_rows, head_dim * 2, 64,
+                     fa::kKV, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !tc::encode_2d(&P.tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, v_pool, head_dim, pool_rows, head_dim * 2, 64,
+                     fa::kKV, CU_TENSOR_MAP_SWIZZLE_128B))
+    return LMPS_ERR_INVALID_ARGUMENT;
+  P.bt = block_table;
+  P.out = reinterpret_cast<__half*>(out);
+  P.ldo = ldo;
+  P.seq_len = seq_len;
+  P.n_q = n_q_heads;
+  P.n_kv = n_kv_heads;
+  P.max_pages = max_pages;
+  P.page_size = page_size;
+  P.n_qtiles = (seq_len + fa::kQ - 1) / fa::kQ;
+  P.head_pairs = G / fa::kH;
+  P.error = error;
+  const int st_attr = lmps_max_dyn_smem<fa::prefill_attn_tc_kernel>(fa::kSmemBytes);
+  if (st_attr != LMPS_OK) return st_attr;
+  const long long ctas = static_cast<long long>(P.n_qtiles) * P.head_pairs * n_kv_heads * batch;
+  if (ctas > 0x7FFFFFFFLL) return LMPS_ERR_UNSUPPORTED;
+  return lmps_launch_pdl(fa::prefill_attn_tc_kernel, dim3(static_cast<unsigned>(ctas)), dim3(fa::kThreads),
+                         static_cast<size_t>(fa::kSmemBytes), lmps_stream(stream), P);
+}

@@ -30,13 +30,13 @@
 //     cluster to fill the GPU; the fp32 partial tiles are summed through
 //     distributed shared memory, each CTA finishing a slice of the rows.
 // Every mbarrier wait is bounded (error flag, no hang).
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace lmps {
 namespace w4 {
+
+using namespace tc;
 
 constexpr int kBK = 64;        // K per stage
 constexpr int kRows = 128;     // weight rows per tile
@@ -46,7 +46,6 @@ constexpr int kMaxSplits = 8;  // K splits of a tile = CTAs of one (portable) cl
 constexpr int kScaleAhead = 6; // K steps a dequantising thread's scale loads run ahead
 constexpr int kStepBytes = kRows * kBK / 2;   // packed W bytes of one K step (4 KB)
 constexpr int kWTileBytes = kRows * kBK * 2;  // 16 KB fp16
-constexpr unsigned long long kTimeoutNs = 2000000000ull;
 
 // EPI_SWIGLU: W holds gate and up rows interleaved (row 2t = gate row t, row
 // 2t + 1 = up row t) and Y[m][t] = fp16(silu(fp16(gate)) * fp16(up)), the
@@ -72,85 +71,6 @@ struct __align__(64) Params {
   int* error;
   int ksteps_per_split;  // split K (gridDim.z > 1, swap tiles): K steps per cluster CTA
 };
-
-__device__ __forceinline__ uint64_t globaltimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Shared-memory matrix descriptor of a K-major, 128-byte-swizzled tile whose
-// rows are 128 bytes and whose 8-row groups are 1024 bytes apart (the tile
-// base is 1024-byte aligned): start address >> 4, leading byte offset 1
-// (unused by swizzled K-major layouts), stride byte offset 1024 >> 4,
-// descriptor version 1, layout SWIZZLE_128B (2).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
-         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
-         (static_cast<uint64_t>(2) << 61);
-}
-
-// Instruction descriptor of kind::f16: fp16 A and B, fp32 D, both K-major,
-// N >> 3 at bit 17, M >> 4 at bit 24.
-__device__ __forceinline__ uint32_t idesc_f16(int m, int n) {
-  return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_f16(uint32_t tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                        uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
-      : "memory");
-}
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait for a phase of `bar`: false when the CTA is aborting or the
-// wait timed out (which raises the error flag and the CTA's abort flag).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
-  if (mbar_try(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  while (!mbar_try(bar, parity)) {
-    if (*abort_flag) return false;
-    if (globaltimer() - t0 > kTimeoutNs) {
-      atomicExch(err, 1);
-      *abort_flag = 1;
-      return false;
-    }
-  }
-  return true;
-}
-// 2-D tiled TMA load (no multicast) into this CTA's shared memory.
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-          "r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
 
 // Position in a ring of n stages: the slot of the current use and the
 // parity of its fill (the fill count of the slot, mod 2).  Stepped once per
@@ -191,18 +111,6 @@ __device__ __forceinline__ uint4 dequant8(uint32_t w, __half2 s2) {
                     __byte_perm(t[0], t[1], 0x7632), __byte_perm(t[2], t[3], 0x7632));
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr)
-      : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
 
 // Y[row][col] from an fp32 accumulator value and the epilogue operands.
 __device__ __forceinline__ __half epi_value(const Params& P, float v, int row, int col) {
@@ -737,6 +645,7 @@ static size_t smem_bytes(int xrows, int xstages, int dstages, int wslots, int sp
 }  // namespace lmps
 
 using namespace lmps;
+using tc::encode_2d;
 
 // Token-tile geometry: fewer than 128 tokens run one token tile with the
 // weight rows as the MMA's M (rounded up to 16 tokens); otherwise 128-token
@@ -756,32 +665,6 @@ static int choose_splits(int tiles, int ksteps, int sms) {
   int s = 1;
   while (2 * s <= want && 2 * s <= w4::kMaxSplits && 2 * (2 * s) <= ksteps) s *= 2;
   return s;
-}
-
-// The driver's tensor-map encoder, looked up through the runtime (the
-// library has no link-time dependency on the driver library).
-static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
-static bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t inner, uint64_t outer,
-                      uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
-  const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
-  if (!enc) return false;
-  const cuuint64_t dims[2] = {inner, outer};
-  const cuuint64_t strides[1] = {row_bytes};
-  const cuuint32_t box[2] = {box_inner, box_outer};
-  const cuuint32_t estr[2] = {1, 1};
-  return enc(map, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 extern "C" int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed, const uint16_t* scales,

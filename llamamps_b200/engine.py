@@ -458,7 +458,7 @@ class QwenEngine:
             K.rope_kv_append(qkv, rows_pos, self.inv_freq, q, kp, vp, rows_bt, self.cache.page_size,
                              c.n_q_heads, c.n_kv_heads, c.head_dim, c.rope_style_code)
             K.prefill_attention(q, kp, vp, self.cache.block_table[:B], att, B, P, self.cache.page_size,
-                                c.n_q_heads, c.n_kv_heads, c.head_dim)
+                                c.n_q_heads, c.n_kv_heads, c.head_dim, error=err)
             self._o_proj(lw, att, x, True, ws=False)
             K.rms_norm(x, lw.post_norm, c.eps, out=xn)
             self._gate_up(lw, xn, gu, gate, ws=False)

@@ -275,8 +275,25 @@ def sample_rows(logits, n: int, top_k: int, temperature: float, seed: int, offse
 
 
 def prefill_attention(q, k_pool, v_pool, block_table, out, batch: int, seq_len: int, page_size: int,
-                      n_q_heads: int, n_kv_heads: int, head_dim: int):
-    """Causal attention of every prompt position (q rows b*seq_len + p) over the paged cache."""
+                      n_q_heads: int, n_kv_heads: int, head_dim: int, *, error: Optional[torch.Tensor] = None,
+                      tcgen05: Optional[bool] = None):
+    """Causal attention of every prompt position (q rows b*seq_len + p) over the paged cache.
+
+    On the tcgen05 kernel (S and O in tensor memory, TMA-loaded K/V) where it
+    takes the shape -- head_dim 128, page_size a multiple of 64, an even
+    query-head group -- else on the mma.sync kernel; ``tcgen05`` forces one.
+    ``error`` (int32 [1]) receives the tcgen05 kernel's wait-timeout flag."""
+    fits = head_dim == 128 and page_size % 64 == 0 and (n_q_heads // n_kv_heads) % 2 == 0
+    if tcgen05 is None:
+        tcgen05 = fits
+    if tcgen05:
+        n_pages = k_pool.numel() // (n_kv_heads * page_size * head_dim)
+        err = error if error is not None else torch.zeros(1, dtype=torch.int32, device=q.device)
+        call("lmps_prefill_attention_tcgen05", _dev(q, "q", FP16), q.shape[-1], _dev(k_pool, "k_pool", FP16),
+             _dev(v_pool, "v_pool", FP16), n_pages, _dev(block_table, "block_table", torch.int32),
+             block_table.shape[1], page_size, _dev(out, "out", FP16), out.shape[-1], batch, seq_len, n_q_heads,
+             n_kv_heads, head_dim, _dev(err, "error", torch.int32), _stream())
+        return out
     call("lmps_prefill_attention", _dev(q, "q", FP16), q.shape[-1], _dev(k_pool, "k_pool", FP16),
          _dev(v_pool, "v_pool", FP16), _dev(block_table, "block_table", torch.int32), block_table.shape[1],
          page_size, _dev(out, "out", FP16), out.shape[-1], batch, seq_len, n_q_heads, n_kv_heads, head_dim,

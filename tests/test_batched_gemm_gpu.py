@@ -112,6 +112,28 @@ def test_swiglu_rows_matches_two_input_swiglu(cuda):
     assert torch.equal(out, ref)
 
 
+@pytest.mark.parametrize("B,P,ps", [(1, 2048, 64), (3, 700, 128), (2, 129, 64)])
+def test_prefill_attention_tcgen05_matches_mma_sync_kernel(cuda, B, P, ps):
+    """The tcgen05 prefill attention against the mma.sync kernel on longer
+    prompts (many key tiles, the O rescale, several query tiles, pages of
+    128 positions, permuted page order)."""
+    from llamamps_b200 import kernels as K
+    Hq, Hkv, hd = 12, 2, 128
+    g = torch.Generator(device="cuda").manual_seed(B * P + ps)
+    pages = (P + ps - 1) // ps
+    kp = torch.randn(B * pages + 3, Hkv, ps, hd, generator=g, device="cuda").half()
+    vp = torch.randn(B * pages + 3, Hkv, ps, hd, generator=g, device="cuda").half()
+    bt = (torch.randperm(B * pages, generator=g, device="cuda") + 3).to(torch.int32).reshape(B, pages)
+    q = (torch.randn(B * P, Hq * hd, generator=g, device="cuda") * 2).half()
+    a, b = torch.empty_like(q), torch.empty_like(q)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    K.prefill_attention(q, kp, vp, bt, a, B, P, ps, Hq, Hkv, hd, error=err, tcgen05=True)
+    K.prefill_attention(q, kp, vp, bt, b, B, P, ps, Hq, Hkv, hd, tcgen05=False)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0 and bool(torch.isfinite(a.float()).all())
+    assert torch.allclose(a.float(), b.float(), atol=4e-3, rtol=1e-2), float((a.float() - b.float()).abs().max())
+
+
 @pytest.mark.parametrize("m", [1, 5, 64, 127, 128, 300])
 def test_gemm_swiglu_epilogue_equals_gemm_then_swiglu(cuda, m):
     """The GEMM's SwiGLU epilogue over row-interleaved gate/up weights, bit for
@@ -175,10 +197,12 @@ def test_dense_and_stepwise_prefill_fill_the_same_cache(cuda, small_model):
     assert torch.equal(a.pos[:2], b.pos[:2])
 
 
-@pytest.mark.parametrize("P", [1, 37, 130])
-def test_prefill_attention_matches_per_row_decode_attention(cuda, P):
-    """The causal prefill kernel against the decode attention kernel run with
-    one query row per position (seq_len = p + 1) on the same paged cache."""
+@pytest.mark.parametrize("tcgen05", [True, False])
+@pytest.mark.parametrize("P", [1, 37, 130, 300])
+def test_prefill_attention_matches_per_row_decode_attention(cuda, P, tcgen05):
+    """The causal prefill kernels (tcgen05 / TMEM and mma.sync) against the
+    decode attention kernel run with one query row per position (seq_len =
+    p + 1) on the same paged cache."""
     from llamamps_b200 import kernels as K
     B, Hq, Hkv, hd, ps = 2, 12, 2, 128, 64
     g = torch.Generator(device="cuda").manual_seed(P)
@@ -188,7 +212,9 @@ def test_prefill_attention_matches_per_row_decode_attention(cuda, P):
     bt = torch.randperm(B * pages, generator=g, device="cuda").to(torch.int32).reshape(B, pages)
     q = torch.randn(B * P, Hq * hd, generator=g, device="cuda").half()
     out = torch.empty_like(q)
-    K.prefill_attention(q, kp, vp, bt, out, B, P, ps, Hq, Hkv, hd)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    K.prefill_attention(q, kp, vp, bt, out, B, P, ps, Hq, Hkv, hd, error=err, tcgen05=tcgen05)
+    assert int(err.item()) == 0
     rows_bt = bt.repeat_interleave(P, dim=0).contiguous()
     lens = (torch.arange(P, device="cuda", dtype=torch.int32) + 1).repeat(B)
     ref = torch.empty_like(q)
