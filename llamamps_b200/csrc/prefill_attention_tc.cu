@@ -7,20 +7,23 @@
 // sequence); the longest query tiles are scheduled first.  Per 64-key tile
 // of the paged cache:
 //   * warp 0 (one lane) loads the tile's K and V rows with plain (non-
-//     multicast) TMA from this GPU's own pool into a two-stage ring (128-byte
+//     multicast) TMA from this GPU's own pool into a four-stage ring (128-byte
 //     swizzle; the queries of both heads once at the start);
 //   * warp 1 (one lane) issues S_h = Q_h K^T (M = 128 queries, N = 64 keys,
 //     K = 128 dims) into TMEM, then, once the softmax has written P_h,
 //     O_h += P_h V (M = 128, N = 128 dims, K = 64 keys; V read MN-major
 //     straight from the cache rows);
-//   * warps 2-5 (thread = query row, its TMEM lane) read S_h, apply the
-//     scale 0.088388 and the causal mask, keep the running max and sum in
-//     fp32 (exp2), write P_h as fp16 into a 128-byte-swizzled K-major tile,
-//     and rescale O_h in TMEM only when the row max grows by more than 2^8
-//     (between rescales P stays below 2^8, so fp16 P and fp32 O are exact
-//     enough); at the end they read O_h, divide by the sum and store fp16.
-// The two heads alternate, so one head's softmax overlaps the other head's
-// MMAs.  Every mbarrier wait is bounded (error flag, no hang).
+//   * warps 2-5 for head 0 and 6-9 for head 1 (thread = query row, its TMEM
+//     lane) read S_h twice (row max, then the exponentials), apply the scale
+//     0.088388 and the causal mask (diagonal tiles only), keep the running
+//     max and sum in fp32 (exp2), write P_h as fp16 into a 128-byte-swizzled
+//     K-major tile, and rescale O_h in TMEM only when the row max grows by
+//     more than 2^8 (between rescales P stays below 2^8, so fp16 P and fp32
+//     O are exact enough); at the end they read O_h, divide by the sum and
+//     store fp16.
+// The two heads' softmax warpgroups run side by side while the tensor core
+// works on the other head.  Every mbarrier wait is bounded (error flag, no
+// hang).
 #include <cmath>
 
 #include "common.cuh"
@@ -35,15 +38,16 @@ constexpr int kD = 128;        // head dim
 constexpr int kQ = 128;        // queries per tile (TMEM lanes)
 constexpr int kKV = 64;        // keys per tile
 constexpr int kH = 2;          // query heads per CTA
-constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 softmax + epilogue
+constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-5 / 6-9 softmax + epilogue of head 0 / 1
+constexpr int kStages = 4;     // K/V tiles in shared memory: loads run three tiles ahead
 constexpr int kQSub = kQ * 128;    // 64 dims of a Q tile: 128 rows x 128 bytes
 constexpr int kKVSub = kKV * 128;  // 64 dims of a K or V tile: 64 rows x 128 bytes
 constexpr int kPTile = kQ * 128;   // P tile: 128 rows x 64 keys fp16
 constexpr int kOffK = kH * 2 * kQSub;          // 64 KB of Q
-constexpr int kOffV = kOffK + 2 * 2 * kKVSub;  // two stages of K
-constexpr int kOffP = kOffV + 2 * 2 * kKVSub;  // two stages of V
+constexpr int kOffV = kOffK + kStages * 2 * kKVSub;  // the stages of K
+constexpr int kOffP = kOffV + kStages * 2 * kKVSub;  // the stages of V
 constexpr int kOffBar = kOffP + kH * kPTile;
-constexpr int kSmemBytes = kOffBar + 16 * 8 + 1024;  // barriers, TMEM slot, abort flag; 1024-byte alignment slack
+constexpr int kSmemBytes = kOffBar + 24 * 8 + 1024;  // barriers, TMEM slot, abort flag; 1024-byte alignment slack
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0;    // S_h at columns 64 h
 constexpr uint32_t kColO = 128;  // O_h at columns 128 + 128 h
@@ -70,12 +74,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
   unsigned char* sp = base + kOffP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + kOffBar);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [kH]
-  uint64_t* p_full = bars + 7;    // [kH]
-  uint64_t* o_done = bars + 9;    // [kH]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* kv_full = bars + 1;              // [kStages]
+  uint64_t* kv_empty = kv_full + kStages;    // [kStages]
+  uint64_t* s_full = kv_empty + kStages;     // [kH]
+  uint64_t* p_full = s_full + kH;            // [kH]
+  uint64_t* o_done = p_full + kH;            // [kH]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + kH);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   volatile int* abort_v = abort_flag;
 
@@ -96,7 +100,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
 
   if (tid == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
@@ -134,8 +138,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
       const int32_t* bt = P.bt + static_cast<size_t>(b) * P.max_pages;
       int issued = 0;
       for (int i = 0; i < nt; ++i) {
-        const int s = i & 1;
-        if (i >= 2 && !mbar_wait(&kv_empty[s], ((i >> 1) - 1) & 1, P.error, abort_v)) break;
+        const int s = i % kStages;
+        if (i >= kStages && !mbar_wait(&kv_empty[s], (i / kStages - 1) & 1, P.error, abort_v)) break;
         const int k0 = i * kKV;
         const int row = (__ldg(bt + k0 / P.page_size) * P.n_kv + kvh) * P.page_size + k0 % P.page_size;
         mbar_expect_tx(&kv_full[s], 4 * kKVSub);
@@ -151,9 +155,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
         while (!mbar_try(q_full, 0))
           if (globaltimer() - t0 > kTimeoutNs) break;
       }
-      for (int i = max(0, issued - 2); i < issued; ++i) {
+      for (int i = max(0, issued - kStages); i < issued; ++i) {
         const uint64_t t0 = globaltimer();
-        while (!mbar_try(&kv_full[i & 1], (i >> 1) & 1))
+        while (!mbar_try(&kv_full[i % kStages], (i / kStages) & 1))
           if (globaltimer() - t0 > kTimeoutNs) break;
       }
     }
@@ -185,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
         }
       }
       for (int i = 0; ok && i < nt; ++i) {
-        const int s = i & 1;
+        const int s = i % kStages, sn = (i + 1) % kStages;
         for (int h = 0; h < kH; ++h) {
           if (!mbar_wait(&p_full[h], i & 1, P.error, abort_v)) {
             ok = false;
@@ -195,12 +199,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
           issue_o(h, s, i > 0);
           mma_commit(&o_done[h]);
           if (i + 1 < nt) {  // S_h of the next tile: the softmax has read S_h of this one
-            if (h == 0 && !mbar_wait(&kv_full[s ^ 1], ((i + 1) >> 1) & 1, P.error, abort_v)) {
+            if (h == 0 && !mbar_wait(&kv_full[sn], ((i + 1) / kStages) & 1, P.error, abort_v)) {
               ok = false;
               break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            issue_s(h, s ^ 1);
+            issue_s(h, sn);
             mma_commit(&s_full[h]);
           }
         }
@@ -208,93 +212,99 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
       }
     }
   } else {
-    // ---- softmax (thread = query row r of the tile, TMEM lane r)
-    const int quad = warp & 3, r = 32 * quad + lane, qi = q0 + r;
+    // ---- softmax of head h = (warp - 2) / 4 (thread = query row r, TMEM lane r)
+    const int h = (warp - 2) >> 2, quad = warp & 3, r = 32 * quad + lane, qi = q0 + r;
     const uint32_t tl = tmem + (static_cast<uint32_t>(32 * quad) << 16);
-    float m_used[kH], l[kH];
-#pragma unroll
-    for (int h = 0; h < kH; ++h) {
-      m_used[h] = -INFINITY;
-      l[h] = 0.0f;
-    }
+    const uint32_t ts = tl + kColS + kKV * h, to = tl + kColO + kD * h;
+    float m_used = -INFINITY, l = 0.0f;  // running max (scaled, base 2) and sum
     bool ok = true;
     for (int i = 0; ok && i < nt; ++i) {
       const int k0 = i * kKV;
-#pragma unroll
-      for (int h = 0; h < kH; ++h) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&s_full[h], i & 1, P.error, abort_v));
-        if (!ok) break;
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        uint32_t sv0[32], sv1[32];
-        tmem_ld32(tl + kColS + kKV * h, sv0);
-        tmem_ld32(tl + kColS + kKV * h + 32, sv1);
-        float mt = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float x0 = k0 + c > qi ? -INFINITY : __uint_as_float(sv0[c]) * kScaleLog2;
-          const float x1 = k0 + 32 + c > qi ? -INFINITY : __uint_as_float(sv1[c]) * kScaleLog2;
-          sv0[c] = __float_as_uint(x0);
-          sv1[c] = __float_as_uint(x1);
-          mt = fmaxf(mt, fmaxf(x0, x1));
-        }
-        if (i > 0) {  // O_h of the previous tile is done: O_h may be rescaled and P_h rewritten
-          ok = __all_sync(0xffffffffu, mbar_wait(&o_done[h], (i - 1) & 1, P.error, abort_v));
-          if (!ok) break;
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        }
-        const float mnew = fmaxf(m_used[h], mt);
-        const bool grow = mnew > m_used[h] + kRescaleLog2;  // (always on the first tile)
-        const float alpha = grow ? exp2f(m_used[h] - mnew) : 1.0f;
-        if (i > 0 && __any_sync(0xffffffffu, grow)) {  // warp-wide read-modify-write of O_h
-#pragma unroll 1
-          for (int cc = 0; cc < kD; cc += 32) {
-            uint32_t o[32];
-            tmem_ld32(tl + kColO + kD * h + cc, o);
-#pragma unroll
-            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-            tmem_st32(tl + kColO + kD * h + cc, o);
-          }
-        }
-        if (grow) {
-          l[h] *= alpha;
-          m_used[h] = mnew;
-        }
-        // P = 2^(s - m) as fp16 into row r of the swizzled K-major P tile
-        uint32_t pk[32];
-        float sum = 0.0f;
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const float a0 = exp2f(__uint_as_float(sv0[2 * c]) - m_used[h]);
-          const float a1 = exp2f(__uint_as_float(sv0[2 * c + 1]) - m_used[h]);
-          const float b0 = exp2f(__uint_as_float(sv1[2 * c]) - m_used[h]);
-          const float b1 = exp2f(__uint_as_float(sv1[2 * c + 1]) - m_used[h]);
-          sum += (a0 + a1) + (b0 + b1);
-          const __half2 ha = __floats2half2_rn(a0, a1), hb = __floats2half2_rn(b0, b1);
-          pk[c] = *reinterpret_cast<const uint32_t*>(&ha);
-          pk[16 + c] = *reinterpret_cast<const uint32_t*>(&hb);
-        }
-        l[h] += sum;
-        unsigned char* prow = sp + h * kPTile + r * 128;
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch)
-          *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) =
-              make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> the tensor core
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        mbar_arrive(&p_full[h]);
-      }
-    }
-    // ---- epilogue: O_h / l, fp16, this row of the output
-    for (int h = 0; ok && h < kH; ++h) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&o_done[h], (nt - 1) & 1, P.error, abort_v));
+      const bool diag = k0 + kKV - 1 > q0;  // (warp-uniform) the tile reaches past some query of the tile
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[h], i & 1, P.error, abort_v));
       if (!ok) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const float inv = l[h] > 0.0f ? 1.0f / l[h] : 0.0f;
+      // pass 1: the row max of the raw scores (the scale is positive)
+      float mt = -INFINITY;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kKV; c0 += 32) {
+        uint32_t sc[32];
+        tmem_ld32(ts + c0, sc);
+        if (diag) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (k0 + c0 + c <= qi) mt = fmaxf(mt, __uint_as_float(sc[c]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) mt = fmaxf(mt, __uint_as_float(sc[c]));
+        }
+      }
+      mt *= kScaleLog2;
+      if (i > 0) {  // O_h of the previous tile is done: O_h may be rescaled and P_h rewritten
+        ok = __all_sync(0xffffffffu, mbar_wait(&o_done[h], (i - 1) & 1, P.error, abort_v));
+        if (!ok) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      }
+      const float mnew = fmaxf(m_used, mt);
+      const bool grow = mnew > m_used + kRescaleLog2;  // (always on the first tile)
+      const float alpha = grow ? exp2f(m_used - mnew) : 1.0f;
+      if (i > 0 && __any_sync(0xffffffffu, grow)) {  // warp-wide read-modify-write of O_h
+#pragma unroll 1
+        for (int cc = 0; cc < kD; cc += 32) {
+          uint32_t o[32];
+          tmem_ld32(to + cc, o);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+          tmem_st32(to + cc, o);
+        }
+      }
+      if (grow) {
+        l *= alpha;
+        m_used = mnew;
+      }
+      // pass 2: P = 2^(s * scale - m) as fp16 into row r of the swizzled K-major P tile
+      const float nm = -m_used;
+      float sum = 0.0f;
+      unsigned char* prow = sp + h * kPTile + r * 128;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kKV; c0 += 32) {
+        uint32_t sc[32];
+        tmem_ld32(ts + c0, sc);
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          float a0 = exp2f(fmaf(__uint_as_float(sc[2 * c]), kScaleLog2, nm));
+          float a1 = exp2f(fmaf(__uint_as_float(sc[2 * c + 1]), kScaleLog2, nm));
+          if (diag) {
+            a0 = k0 + c0 + 2 * c <= qi ? a0 : 0.0f;
+            a1 = k0 + c0 + 2 * c + 1 <= qi ? a1 : 0.0f;
+          }
+          sum += a0 + a1;
+          const __half2 hh = __floats2half2_rn(a0, a1);
+          pk[c] = *reinterpret_cast<const uint32_t*>(&hh);
+        }
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          const int chunk = (c0 >> 3) + ch;  // 16-byte chunk of the 128-byte row
+          *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+        }
+      }
+      l += sum;
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> the tensor core
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      mbar_arrive(&p_full[h]);
+    }
+    // ---- epilogue: O_h / l, fp16, this row of the output
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&o_done[h], (nt - 1) & 1, P.error, abort_v));
+    if (ok) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
       __half* orow = P.out + static_cast<size_t>(b * P.seq_len + qi) * P.ldo + (h0 + h) * kD;
 #pragma unroll 1
       for (int cc = 0; cc < kD; cc += 32) {
         uint32_t o[32];
-        tmem_ld32(tl + kColO + kD * h + cc, o);
+        tmem_ld32(to + cc, o);
         if (qi < qend) {
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
