@@ -14,7 +14,7 @@
 //     O_h += P_h V (M = 128, N = 128 dims, K = 64 keys; V read MN-major
 //     straight from the cache rows);
 //   * warps 2-5 for head 0 and 6-9 for head 1 (thread = query row, its TMEM
-//     lane) read S_h twice (row max, then the exponentials), apply the scale
+//     lane) read a row of S_h in one TMEM load, apply the scale
 //     0.088388 and the causal mask (diagonal tiles only), keep the running
 //     max and sum in fp32 (exp2), write P_h as fp16 into a 128-byte-swizzled
 //     K-major tile, and rescale O_h in TMEM only when the row max grows by
@@ -224,20 +224,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[h], i & 1, P.error, abort_v));
       if (!ok) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      // pass 1: the row max of the raw scores (the scale is positive)
+      // the row's 64 raw scores in one TMEM load; their max (the scale is positive)
+      uint32_t sc[64];
+      tmem_ld64(ts, sc);
       float mt = -INFINITY;
-#pragma unroll 1
-      for (int c0 = 0; c0 < kKV; c0 += 32) {
-        uint32_t sc[32];
-        tmem_ld32(ts + c0, sc);
-        if (diag) {
+      if (diag) {
 #pragma unroll
-          for (int c = 0; c < 32; ++c)
-            if (k0 + c0 + c <= qi) mt = fmaxf(mt, __uint_as_float(sc[c]));
-        } else {
+        for (int c = 0; c < kKV; ++c)
+          if (k0 + c <= qi) mt = fmaxf(mt, __uint_as_float(sc[c]));
+      } else {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) mt = fmaxf(mt, __uint_as_float(sc[c]));
-        }
+        for (int c = 0; c < kKV; ++c) mt = fmaxf(mt, __uint_as_float(sc[c]));
       }
       mt *= kScaleLog2;
       if (i > 0) {  // O_h of the previous tile is done: O_h may be rescaled and P_h rewritten
@@ -262,33 +259,27 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
         l *= alpha;
         m_used = mnew;
       }
-      // pass 2: P = 2^(s * scale - m) as fp16 into row r of the swizzled K-major P tile
+      // P = 2^(s * scale - m) as fp16 into row r of the swizzled K-major P tile
       const float nm = -m_used;
       float sum = 0.0f;
       unsigned char* prow = sp + h * kPTile + r * 128;
-#pragma unroll 1
-      for (int c0 = 0; c0 < kKV; c0 += 32) {
-        uint32_t sc[32];
-        tmem_ld32(ts + c0, sc);
-        uint32_t pk[16];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          float a0 = exp2f(fmaf(__uint_as_float(sc[2 * c]), kScaleLog2, nm));
-          float a1 = exp2f(fmaf(__uint_as_float(sc[2 * c + 1]), kScaleLog2, nm));
+      for (int ch = 0; ch < 8; ++ch) {  // 16-byte chunk ch: keys 8 ch .. 8 ch + 7
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = 8 * ch + 2 * e;
+          float a0 = exp2f(fmaf(__uint_as_float(sc[c]), kScaleLog2, nm));
+          float a1 = exp2f(fmaf(__uint_as_float(sc[c + 1]), kScaleLog2, nm));
           if (diag) {
-            a0 = k0 + c0 + 2 * c <= qi ? a0 : 0.0f;
-            a1 = k0 + c0 + 2 * c + 1 <= qi ? a1 : 0.0f;
+            a0 = k0 + c <= qi ? a0 : 0.0f;
+            a1 = k0 + c + 1 <= qi ? a1 : 0.0f;
           }
           sum += a0 + a1;
           const __half2 hh = __floats2half2_rn(a0, a1);
-          pk[c] = *reinterpret_cast<const uint32_t*>(&hh);
+          pk[e] = *reinterpret_cast<const uint32_t*>(&hh);
         }
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-          const int chunk = (c0 >> 3) + ch;  // 16-byte chunk of the 128-byte row
-          *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) =
-              make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-        }
+        *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
       l += sum;
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> the tensor core
