@@ -7,12 +7,14 @@
 // sequence); the longest query tiles are scheduled first.  Per 64-key tile
 // of the paged cache:
 //   * warp 0 (one lane) loads the tile's K and V rows with plain (non-
-//     multicast) TMA from this GPU's own pool into a four-stage ring (128-byte
+//     multicast) TMA from this GPU's own pool into a three-stage ring (128-byte
 //     swizzle; the queries of both heads once at the start);
 //   * warp 1 (one lane) issues S_h = Q_h K^T (M = 128 queries, N = 64 keys,
 //     K = 128 dims) into TMEM, then, once the softmax has written P_h,
 //     O_h += P_h V (M = 128, N = 128 dims, K = 64 keys; V read MN-major
-//     straight from the cache rows);
+//     straight from the cache rows); S and P have two buffers per head, so
+//     S of tile i + 1 is ready while the softmax works on tile i and the
+//     softmax never waits for the O MMA of the tile before;
 //   * warps 2-5 for head 0 and 6-9 for head 1 (thread = query row, its TMEM
 //     lane) read a row of S_h in one TMEM load, apply the scale
 //     0.088388 and the causal mask (diagonal tiles only), keep the running
@@ -39,18 +41,18 @@ constexpr int kQ = 128;        // queries per tile (TMEM lanes)
 constexpr int kKV = 64;        // keys per tile
 constexpr int kH = 2;          // query heads per CTA
 constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-5 / 6-9 softmax + epilogue of head 0 / 1
-constexpr int kStages = 4;     // K/V tiles in shared memory: loads run three tiles ahead
+constexpr int kStages = 3;     // K/V tiles in shared memory: loads run two tiles ahead
 constexpr int kQSub = kQ * 128;    // 64 dims of a Q tile: 128 rows x 128 bytes
 constexpr int kKVSub = kKV * 128;  // 64 dims of a K or V tile: 64 rows x 128 bytes
 constexpr int kPTile = kQ * 128;   // P tile: 128 rows x 64 keys fp16
 constexpr int kOffK = kH * 2 * kQSub;          // 64 KB of Q
 constexpr int kOffV = kOffK + kStages * 2 * kKVSub;  // the stages of K
 constexpr int kOffP = kOffV + kStages * 2 * kKVSub;  // the stages of V
-constexpr int kOffBar = kOffP + kH * kPTile;
-constexpr int kSmemBytes = kOffBar + 24 * 8 + 1024;  // barriers, TMEM slot, abort flag; 1024-byte alignment slack
+constexpr int kOffBar = kOffP + kH * 2 * kPTile;  // two P buffers per head
+constexpr int kSmemBytes = kOffBar + 24 * 8 + 1024;  // (kOffBar + 192 + 1024 <= 227 KB)  // barriers, TMEM slot, abort flag; 1024-byte alignment slack
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0;    // S_h at columns 64 h
-constexpr uint32_t kColO = 128;  // O_h at columns 128 + 128 h
+constexpr uint32_t kColS = 0;    // S of head h, buffer u at columns 64 (2 h + u)
+constexpr uint32_t kColO = 256;  // O_h at columns 256 + 128 h
 constexpr float kScaleLog2 = 0.088388f * 1.4426950408889634f;  // attention.metal:40 scale, base 2
 constexpr float kRescaleLog2 = 8.0f;
 
@@ -76,10 +78,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;              // [kStages]
   uint64_t* kv_empty = kv_full + kStages;    // [kStages]
-  uint64_t* s_full = kv_empty + kStages;     // [kH]
-  uint64_t* p_full = s_full + kH;            // [kH]
-  uint64_t* o_done = p_full + kH;            // [kH]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + kH);
+  // per head and buffer u (tile i uses buffer i & 1): S_h ready, P_h written
+  // (and S_h read), O_h += P_h V of the tile done
+  uint64_t* s_full = kv_empty + kStages;     // [kH][2]
+  uint64_t* p_full = s_full + 2 * kH;        // [kH][2]
+  uint64_t* o_done = p_full + 2 * kH;        // [kH][2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2 * kH);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   volatile int* abort_v = abort_flag;
 
@@ -104,10 +108,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int h = 0; h < kH; ++h) {
-      mbar_init(&s_full[h], 1);
-      mbar_init(&p_full[h], kQ);
-      mbar_init(&o_done[h], 1);
+    for (int u = 0; u < 2 * kH; ++u) {
+      mbar_init(&s_full[u], 1);
+      mbar_init(&p_full[u], kQ);
+      mbar_init(&o_done[u], 1);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -164,48 +168,53 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
   } else if (warp == 1) {
     if (lane == 0) {  // ---- MMA issuer
       const uint32_t id_s = idesc_f16(kQ, kKV), id_o = idesc_f16(kQ, kD) | kBMajorMN;
-      auto issue_s = [&](int h, int s) {  // S_h = Q_h K^T over 8 k-steps of 16 dims
+      auto issue_s = [&](int h, int s, int u) {  // S_h (buffer u) = Q_h K^T over 8 k-steps of 16 dims
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const uint64_t a = sw128_desc(smem_u32(sq + (2 * h + (j >> 2)) * kQSub)) + 2 * (j & 3);
           const uint64_t bk = sw128_desc(smem_u32(sk + (2 * s + (j >> 2)) * kKVSub)) + 2 * (j & 3);
-          mma_f16(tmem + kColS + kKV * h, a, bk, id_s, j > 0 ? 1u : 0u);
+          mma_f16(tmem + kColS + kKV * (2 * h + u), a, bk, id_s, j > 0 ? 1u : 0u);
         }
       };
-      auto issue_o = [&](int h, int s, bool acc) {  // O_h += P_h V over 4 k-steps of 16 keys
+      auto issue_o = [&](int h, int s, int u, bool acc) {  // O_h += P_h (buffer u) V over 4 k-steps of 16 keys
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const uint64_t a = sw128_desc(smem_u32(sp + h * kPTile)) + 2 * j;
+          const uint64_t a = sw128_desc(smem_u32(sp + (2 * h + u) * kPTile)) + 2 * j;
           const uint64_t bv = sw128_mn_desc(smem_u32(sv + (2 * s) * kKVSub + 2048 * j), kKVSub);
           mma_f16(tmem + kColO + kD * h, a, bv, id_o, (acc || j > 0) ? 1u : 0u);
         }
       };
-      bool ok = mbar_wait(q_full, 0, P.error, abort_v) && mbar_wait(&kv_full[0], 0, P.error, abort_v);
-      if (ok) {
+      // S of tiles 0 and 1 up front (both S buffers are free), then per tile
+      // and head: O += P V once the softmax wrote P, and S of the tile two
+      // ahead into the buffer the softmax just finished reading.
+      bool ok = mbar_wait(q_full, 0, P.error, abort_v);
+      for (int i = 0; ok && i < 2 && i < nt; ++i) {
+        ok = mbar_wait(&kv_full[i], 0, P.error, abort_v);
+        if (!ok) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         for (int h = 0; h < kH; ++h) {
-          issue_s(h, 0);
-          mma_commit(&s_full[h]);
+          issue_s(h, i, i);
+          mma_commit(&s_full[2 * h + i]);
         }
       }
       for (int i = 0; ok && i < nt; ++i) {
-        const int s = i % kStages, sn = (i + 1) % kStages;
+        const int s = i % kStages, u = i & 1, s2 = (i + 2) % kStages;
         for (int h = 0; h < kH; ++h) {
-          if (!mbar_wait(&p_full[h], i & 1, P.error, abort_v)) {
+          if (!mbar_wait(&p_full[2 * h + u], (i >> 1) & 1, P.error, abort_v)) {
             ok = false;
             break;
           }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          issue_o(h, s, i > 0);
-          mma_commit(&o_done[h]);
-          if (i + 1 < nt) {  // S_h of the next tile: the softmax has read S_h of this one
-            if (h == 0 && !mbar_wait(&kv_full[sn], ((i + 1) / kStages) & 1, P.error, abort_v)) {
+          issue_o(h, s, u, i > 0);
+          mma_commit(&o_done[2 * h + u]);
+          if (i + 2 < nt) {
+            if (h == 0 && !mbar_wait(&kv_full[s2], ((i + 2) / kStages) & 1, P.error, abort_v)) {
               ok = false;
               break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            issue_s(h, sn);
-            mma_commit(&s_full[h]);
+            issue_s(h, s2, u);
+            mma_commit(&s_full[2 * h + u]);
           }
         }
         if (ok) mma_commit(&kv_empty[s]);  // this tile's K and V are free once the MMAs above are done
@@ -215,18 +224,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
     // ---- softmax of head h = (warp - 2) / 4 (thread = query row r, TMEM lane r)
     const int h = (warp - 2) >> 2, quad = warp & 3, r = 32 * quad + lane, qi = q0 + r;
     const uint32_t tl = tmem + (static_cast<uint32_t>(32 * quad) << 16);
-    const uint32_t ts = tl + kColS + kKV * h, to = tl + kColO + kD * h;
+    const uint32_t to = tl + kColO + kD * h;
     float m_used = -INFINITY, l = 0.0f;  // running max (scaled, base 2) and sum
     bool ok = true;
     for (int i = 0; ok && i < nt; ++i) {
       const int k0 = i * kKV;
       const bool diag = k0 + kKV - 1 > q0;  // (warp-uniform) the tile reaches past some query of the tile
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[h], i & 1, P.error, abort_v));
+      const int u = i & 1;                  // S / P buffer of this tile
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[2 * h + u], (i >> 1) & 1, P.error, abort_v));
       if (!ok) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       // the row's 64 raw scores in one TMEM load; their max (the scale is positive)
       uint32_t sc[64];
-      tmem_ld64(ts, sc);
+      tmem_ld64(tl + kColS + kKV * (2 * h + u), sc);
       float mt = -INFINITY;
       if (diag) {
 #pragma unroll
@@ -237,15 +247,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
         for (int c = 0; c < kKV; ++c) mt = fmaxf(mt, __uint_as_float(sc[c]));
       }
       mt *= kScaleLog2;
-      if (i > 0) {  // O_h of the previous tile is done: O_h may be rescaled and P_h rewritten
-        ok = __all_sync(0xffffffffu, mbar_wait(&o_done[h], (i - 1) & 1, P.error, abort_v));
+      if (i >= 2) {  // O_h of tile i - 2 is done: its P buffer may be rewritten
+        ok = __all_sync(0xffffffffu, mbar_wait(&o_done[2 * h + u], ((i - 2) >> 1) & 1, P.error, abort_v));
         if (!ok) break;
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       }
       const float mnew = fmaxf(m_used, mt);
       const bool grow = mnew > m_used + kRescaleLog2;  // (always on the first tile)
       const float alpha = grow ? exp2f(m_used - mnew) : 1.0f;
       if (i > 0 && __any_sync(0xffffffffu, grow)) {  // warp-wide read-modify-write of O_h
+        // once O_h += P V of the previous tile (and so every earlier one) is done
+        ok = __all_sync(0xffffffffu, mbar_wait(&o_done[2 * h + (u ^ 1)], ((i - 1) >> 1) & 1, P.error, abort_v));
+        if (!ok) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll 1
         for (int cc = 0; cc < kD; cc += 32) {
           uint32_t o[32];
@@ -262,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
       // P = 2^(s * scale - m) as fp16 into row r of the swizzled K-major P tile
       const float nm = -m_used;
       float sum = 0.0f;
-      unsigned char* prow = sp + h * kPTile + r * 128;
+      unsigned char* prow = sp + (2 * h + u) * kPTile + r * 128;
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {  // 16-byte chunk ch: keys 8 ch .. 8 ch + 7
         uint32_t pk[4];
@@ -284,10 +297,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
       l += sum;
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> the tensor core
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      mbar_arrive(&p_full[h]);
+      mbar_arrive(&p_full[2 * h + u]);
     }
     // ---- epilogue: O_h / l, fp16, this row of the output
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&o_done[h], (nt - 1) & 1, P.error, abort_v));
+    if (ok)  // the last O_h += P V (and so every earlier one) done
+      ok = __all_sync(0xffffffffu, mbar_wait(&o_done[2 * h + ((nt - 1) & 1)], ((nt - 1) >> 1) & 1, P.error, abort_v));
     if (ok) {
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const float inv = l > 0.0f ? 1.0f / l : 0.0f;
