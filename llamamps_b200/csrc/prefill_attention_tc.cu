@@ -56,6 +56,14 @@ constexpr uint32_t kColO = 256;  // O_h at columns 256 + 128 h
 constexpr float kScaleLog2 = 0.088388f * 1.4426950408889634f;  // attention.metal:40 scale, base 2
 constexpr float kRescaleLog2 = 8.0f;
 
+// 2^x with the hardware approximation (ex2.approx.ftz: relative error ~2^-22,
+// far below the fp16 rounding P gets next).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 struct Params {
   CUtensorMap tq;  // q [batch * seq_len, ldq] fp16, box {64, 128}
   CUtensorMap tk;  // K pool [n_pages * n_kv * page_size, 128] fp16, box {64, 64}
@@ -237,15 +245,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
       // the row's 64 raw scores in one TMEM load; their max (the scale is positive)
       uint32_t sc[64];
       tmem_ld64(tl + kColS + kKV * (2 * h + u), sc);
-      float mt = -INFINITY;
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four chains
       if (diag) {
 #pragma unroll
         for (int c = 0; c < kKV; ++c)
-          if (k0 + c <= qi) mt = fmaxf(mt, __uint_as_float(sc[c]));
+          if (k0 + c <= qi) mx[c & 3] = fmaxf(mx[c & 3], __uint_as_float(sc[c]));
       } else {
 #pragma unroll
-        for (int c = 0; c < kKV; ++c) mt = fmaxf(mt, __uint_as_float(sc[c]));
+        for (int c = 0; c < kKV; ++c) mx[c & 3] = fmaxf(mx[c & 3], __uint_as_float(sc[c]));
       }
+      float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
       mt *= kScaleLog2;
       if (i >= 2) {  // O_h of tile i - 2 is done: its P buffer may be rewritten
         ok = __all_sync(0xffffffffu, mbar_wait(&o_done[2 * h + u], ((i - 2) >> 1) & 1, P.error, abort_v));
@@ -274,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
       }
       // P = 2^(s * scale - m) as fp16 into row r of the swizzled K-major P tile
       const float nm = -m_used;
-      float sum = 0.0f;
+      float sm[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // four chains
       unsigned char* prow = sp + (2 * h + u) * kPTile + r * 128;
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {  // 16-byte chunk ch: keys 8 ch .. 8 ch + 7
@@ -282,19 +291,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_tc_kernel(const __gr
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int c = 8 * ch + 2 * e;
-          float a0 = exp2f(fmaf(__uint_as_float(sc[c]), kScaleLog2, nm));
-          float a1 = exp2f(fmaf(__uint_as_float(sc[c + 1]), kScaleLog2, nm));
+          float a0 = fast_exp2(fmaf(__uint_as_float(sc[c]), kScaleLog2, nm));
+          float a1 = fast_exp2(fmaf(__uint_as_float(sc[c + 1]), kScaleLog2, nm));
           if (diag) {
             a0 = k0 + c <= qi ? a0 : 0.0f;
             a1 = k0 + c + 1 <= qi ? a1 : 0.0f;
           }
-          sum += a0 + a1;
+          sm[e] += a0 + a1;
           const __half2 hh = __floats2half2_rn(a0, a1);
           pk[e] = *reinterpret_cast<const uint32_t*>(&hh);
         }
         *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
-      l += sum;
+      l += (sm[0] + sm[1]) + (sm[2] + sm[3]);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> the tensor core
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       mbar_arrive(&p_full[2 * h + u]);
