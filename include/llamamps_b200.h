@@ -198,7 +198,7 @@ int lmps_gqa_decode_attention_noalloc(const uint16_t* q, const uint16_t* k_pool,
  * dense contractions: y[m, :n] = x[m, :k] . W^T with W the Q4 [n, k] layout of
  * lmps_gemv_q4_0 (dequantised to fp16 tile by tile), fp32 accumulate, fp16 out.
  * epilogue: 0 none, 1 + bias[n], 2 residual[m, n] + fp16(acc) (residual may
- * alias y), 3 SwiGLU (swiglu.metal:13-23): W's rows interleave gate and up
+ * alias y; 16-byte aligned, ldr a multiple of 8), 3 SwiGLU (swiglu.metal:13-23): W's rows interleave gate and up
  * (row 2t = gate row t, 2t + 1 = up row t) and y[m, t] =
  * fp16(silu(fp16(gate)) * fp16(up)) for t < n/2 (ldy >= n/2).
  * n must be a multiple of 128 and k of 64 (else UNSUPPORTED); any

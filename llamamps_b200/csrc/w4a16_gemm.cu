@@ -604,6 +604,22 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
             }
             *reinterpret_cast<uint4*>(yrow + 8 * g) = make_uint4(o[0], o[1], o[2], o[3]);
           }
+        } else if (rw < P.m && P.epi == EPI_RESIDUAL) {  // residual rows read 16 bytes at a time
+          __half* yrow = P.y + static_cast<size_t>(rw) * P.ldy + n0 + c0;
+          const __half* rrow = P.res + static_cast<size_t>(rw) * P.ldr + n0 + c0;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const uint4 rv = *reinterpret_cast<const uint4*>(rrow + 8 * g);
+            const __half2* r2 = reinterpret_cast<const __half2*>(&rv);
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const __half2 hh = __hadd2(r2[e], __floats2half2_rn(__uint_as_float(r[8 * g + 2 * e]),
+                                                                  __uint_as_float(r[8 * g + 2 * e + 1])));
+              o[e] = *reinterpret_cast<const uint32_t*>(&hh);
+            }
+            *reinterpret_cast<uint4*>(yrow + 8 * g) = make_uint4(o[0], o[1], o[2], o[3]);
+          }
         } else if (rw < P.m) {
           __half* yrow = P.y + static_cast<size_t>(rw) * P.ldy + n0 + c0;
 #pragma unroll
@@ -676,7 +692,7 @@ extern "C" int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed
   if (n % w4::kRows != 0 || k % w4::kBK != 0) return LMPS_ERR_UNSUPPORTED;
   LMPS_CHECK_ARG(epilogue >= w4::EPI_NONE && epilogue <= w4::EPI_SWIGLU);
   LMPS_CHECK_ARG(epilogue != w4::EPI_BIAS || bias);
-  LMPS_CHECK_ARG(epilogue != w4::EPI_RESIDUAL || (residual && ldr >= n));
+  LMPS_CHECK_ARG(epilogue != w4::EPI_RESIDUAL || (residual && ldr >= n && ldr % 8 == 0 && lmps_aligned(residual, 16)));
   const int ncols = epilogue == w4::EPI_SWIGLU ? n / 2 : n;  // Y columns
   LMPS_CHECK_ARG(ldx >= k && ldx % 8 == 0 && ldy >= ncols && ldy % 8 == 0);
   LMPS_CHECK_ARG(lmps_aligned(x, 16) && lmps_aligned(y, 16) && lmps_aligned(packed, 16) && lmps_aligned(scales, 4));
