@@ -467,14 +467,18 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_kernel(const __grid_const
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols) : "memory");
 }
 
-// Prefill tiles (128 tokens x 128 weight rows): one ring of S stages, each
-// holding the X tile, the step's packed W (128 rows x 32 bytes, one TMA
-// box) and the dequantised W tile.  Warp 0 lane 0 loads, warps 2-5
-// dequantise and then run the epilogue, warp 1 lane 0 issues the MMAs.
+// Prefill tiles (MT x 128 tokens x 128 weight rows): one ring of S stages,
+// each holding the MT X tiles, the step's packed W (128 rows x 32 bytes, one
+// TMA box) and the dequantised W tile, which serves the MT token halves (one
+// M = 128 MMA each, accumulators side by side in TMEM).  Warp 0 lane 0
+// loads, warps 2-5 dequantise and then run the epilogue, warp 1 lane 0
+// issues the MMAs.
+template <int MT>
 __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid_constant__ Params P) {
   extern __shared__ unsigned char smem_raw[];
   const int S = P.xstages;
-  constexpr int kX = 128 * 128;  // X tile bytes
+  constexpr int kX = MT * 128 * 128;  // X tile bytes of a stage (MT halves of 128 tokens)
+  constexpr uint32_t kCols = 128 * MT;  // TMEM columns
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   unsigned char* xs = base;
@@ -490,7 +494,7 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
 
   lmps_pdl_trigger();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = blockIdx.x * kRows, m0 = blockIdx.y * 128;
+  const int n0 = blockIdx.x * kRows, m0 = blockIdx.y * 128 * MT;
   const int ksteps = P.k / kBK;
   if (tid == 0) {
     for (int i = 0; i < S; ++i) {
@@ -504,7 +508,7 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(128)
+                 "r"(kCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -522,7 +526,9 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
         const int s = ps.slot;
         if (kt >= S && !mbar_wait(&empty[s], ps.phase ^ 1u, P.error, abort_v)) break;
         mbar_expect_tx(&full[s], static_cast<uint32_t>(kX + kStepBytes));
-        tma_load_2d(xs + static_cast<size_t>(s) * kX, &P.tx, kt * kBK, m0, &full[s]);
+#pragma unroll
+        for (int mh = 0; mh < MT; ++mh)
+          tma_load_2d(xs + static_cast<size_t>(s) * kX + mh * 128 * 128, &P.tx, kt * kBK, m0 + 128 * mh, &full[s]);
         tma_load_2d(wr + static_cast<size_t>(s) * kStepBytes, &P.tw, kt * (kBK / 2), n0, &full[s]);
         issued = kt + 1;
       }
@@ -540,11 +546,14 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
         const int s = ps.slot;
         if (!mbar_wait(&deq[s], ps.phase, P.error, abort_v)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint64_t ad = sw128_desc(smem_u32(xs + static_cast<size_t>(s) * kX));
         const uint64_t bd = sw128_desc(smem_u32(wd + static_cast<size_t>(s) * kWTileBytes));
 #pragma unroll
-        for (int j = 0; j < kBK / 16; ++j)
-          mma_f16(tmem, ad + 2 * j, bd + 2 * j, idesc, (kt > 0 || j > 0) ? 1u : 0u);
+        for (int mh = 0; mh < MT; ++mh) {
+          const uint64_t ad = sw128_desc(smem_u32(xs + static_cast<size_t>(s) * kX + mh * 128 * 128));
+#pragma unroll
+          for (int j = 0; j < kBK / 16; ++j)
+            mma_f16(tmem + 128 * mh, ad + 2 * j, bd + 2 * j, idesc, (kt > 0 || j > 0) ? 1u : 0u);
+        }
         mma_commit(&empty[s]);
       }
       mma_commit(done);
@@ -583,9 +592,11 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
     const bool ok = ksteps > 0 && mbar_wait(done, 0, P.error, abort_v);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const int q = warp & 3;
-    const uint32_t tl = tmem + (static_cast<uint32_t>(32 * q) << 16);
-    const int rw = m0 + 32 * q + lane;
-    if (ok) {
+#pragma unroll 1
+    for (int mh = 0; ok && mh < MT; ++mh) {
+    const uint32_t tl = tmem + (static_cast<uint32_t>(32 * q) << 16) + 128 * mh;
+    const int rw = m0 + 128 * mh + 32 * q + lane;
+    {
 #pragma unroll 1
       for (int c0 = 0; c0 < kRows; c0 += 32) {
         uint32_t r[32];
@@ -637,14 +648,15 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
         }
       }
     }
+    }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(128) : "memory");
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
 }
 
-static size_t tiles_smem_bytes(int stages) {
-  return static_cast<size_t>(stages) * (128 * 128 + kWTileBytes + kStepBytes) + 1024 +
+static size_t tiles_smem_bytes(int stages, int mt) {
+  return static_cast<size_t>(stages) * (mt * 128 * 128 + kWTileBytes + kStepBytes) + 1024 +
          (3 * kMaxStages + 1) * sizeof(uint64_t) + 16;
 }
 
@@ -726,14 +738,21 @@ extern "C" int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   (void)workspace;
   (void)workspace_bytes;
-  if (!P.swap) {  // prefill tiles: the single-ring kernel, three stages, two CTAs per SM
-    P.xstages = 3;
-    const size_t smem = w4::tiles_smem_bytes(P.xstages);
-    cudaError_t e = cudaFuncSetAttribute(w4::w4a16_gemm_tiles_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return static_cast<int>(e);
-    return lmps_launch_pdl(w4::w4a16_gemm_tiles_kernel, dim3(nt, mt), dim3(w4::kThreads), smem, lmps_stream(stream),
-                           P);
+  if (!P.swap) {  // prefill tiles: the single-ring kernel
+    if (m >= 256) {  // 256 tokens per CTA (each dequantised W tile serves two MMAs), four stages, one CTA per SM
+      P.xstages = 4;
+      const size_t smem = w4::tiles_smem_bytes(P.xstages, 2);
+      const int st_attr = lmps_max_dyn_smem<w4::w4a16_gemm_tiles_kernel<2>>(static_cast<int>(smem));
+      if (st_attr != LMPS_OK) return st_attr;
+      return lmps_launch_pdl(w4::w4a16_gemm_tiles_kernel<2>, dim3(nt, (m + 255) / 256), dim3(w4::kThreads), smem,
+                             lmps_stream(stream), P);
+    }
+    P.xstages = 3;  // three stages, two CTAs per SM
+    const size_t smem = w4::tiles_smem_bytes(P.xstages, 1);
+    const int st_attr = lmps_max_dyn_smem<w4::w4a16_gemm_tiles_kernel<1>>(static_cast<int>(smem));
+    if (st_attr != LMPS_OK) return st_attr;
+    return lmps_launch_pdl(w4::w4a16_gemm_tiles_kernel<1>, dim3(nt, mt), dim3(w4::kThreads), smem,
+                           lmps_stream(stream), P);
   }
   const int splits = choose_splits(nt, ksteps, sms);
   P.ksteps_per_split = (ksteps + splits - 1) / splits;  // trailing splits may get none: they add zeros
