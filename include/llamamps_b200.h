@@ -425,6 +425,65 @@ size_t lmps_decode_persistent_workspace_size(const lmps_model_desc* model, int b
 int lmps_decode_persistent(const lmps_model_desc* model, const lmps_decode_state* state,
                            int n_steps, void* stream);
 
+/* ---- Batched decode: all layers of a decode step for 1..64 sequences in one
+ * cooperative launch, the Q4 projections on the tcgen05 tensor cores
+ * (replaces the per-layer loop of runners/engine.py:183-245 run once per
+ * sequence; the LM head and argmax of :163-181 stay separate calls).
+ * Weights are read from tile-major copies of the Q4 matrices: */
+
+/* Bytes of the tile-major copy of an [n, k] Q4 matrix (n % 128 == 0,
+ * k % 64 == 0; 0 otherwise). */
+size_t lmps_q4_tile_blocks_size(int n, int k);
+/* Write the tile-major copy: for every 128 rows and 64-wide K step one
+ * 4608-byte block, the rows' 32 packed bytes (two 16-byte halves, swapped
+ * when (row >> 2) & 1) followed by their two group scales (fp16 pairs).
+ * packed/out 16-byte aligned. */
+int lmps_q4_tile_blocks(const uint8_t* packed, const uint16_t* scales, int n, int k, void* out,
+                        void* stream);
+
+typedef struct lmps_batched_layer {
+  const void* qkv_blocks;       /* tile-major W_q|k|v [(n_q+2*n_kv)*head_dim, hidden] */
+  const void* o_blocks;         /* tile-major W_o [hidden, n_q*head_dim] */
+  const void* gu_blocks;        /* tile-major W_gate|up, rows interleaved (2t gate t, 2t+1 up t)
+                                   [2*intermediate, hidden] */
+  const void* down_blocks;      /* tile-major W_down [hidden, intermediate] */
+  const uint16_t* qkv_bias;     /* fp16 [(n_q+2*n_kv)*head_dim] */
+  const uint16_t* in_norm;      /* fp16 [hidden] */
+  const uint16_t* post_norm;    /* fp16 [hidden] */
+  uint16_t* k_pool;             /* fp16 [n_pages, n_kv, page_size, head_dim] */
+  uint16_t* v_pool;
+} lmps_batched_layer;
+
+typedef struct lmps_batched_desc {
+  const lmps_batched_layer* layers;  /* DEVICE array of n_layers descriptors */
+  int n_layers, hidden, intermediate, n_q_heads, n_kv_heads, head_dim;
+  float eps;
+  int rope_style;                    /* LMPS_ROPE_* */
+  const float* inv_freq;             /* fp32 [head_dim/2] */
+} lmps_batched_desc;
+
+/* Workspace bytes for `batch` sequences (0 if the model is unsupported:
+ * head_dim 128, hidden a multiple of 512 and <= 4096, every projection's rows
+ * a multiple of 128 and at most one 128-row tile per SM, K a multiple of 64). */
+size_t lmps_decode_batched_workspace_size(const lmps_batched_desc* model, int batch, int max_seq_len);
+
+/* One decode step of every layer: x (fp16 [batch, hidden], the embedded
+ * tokens) becomes the residual after the last layer (the final norm is the
+ * caller's); the K/V rows of position pos[b] are appended to each layer's
+ * pools and attention covers seq_lens[b] = pos[b] + 1 positions.  workspace:
+ * 256-byte aligned, zeroed once (it carries a grid-barrier counter from
+ * launch to launch) and again after a reported error.  error: 1 = a bounded
+ * device wait gave up, 2 = a position outside the cache (nothing ran).
+ * trace (or NULL): %globaltimer stamps [grid][barriers][2] -- when each CTA's
+ * workers arrived at each grid barrier and when they saw it complete (0 where
+ * they did not wait); barriers = 1 + n_layers * (7, or 8 when the attention
+ * is split over CTAs). */
+int lmps_decode_batched(const lmps_batched_desc* model, uint16_t* x, const int32_t* pos,
+                        const int32_t* seq_lens, const int32_t* block_table, int max_pages,
+                        int page_size, int batch, int max_seq_len, void* workspace,
+                        size_t workspace_bytes, int32_t* error, unsigned long long* trace,
+                        void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -2,250 +2,30 @@
 //
 // One kernel does what kernels/attention.metal (scores), softmax.metal and
 // attn_sum.metal do in three dispatches (runners/engine.py:202-212), for a
-// real cache of seq_lens[b] positions:
-//   s[h, i] = (q_h . K[i, h/G]) * 0.088388,  p = softmax_i(s),  o_h = sum_i p V[i, h/G].
-// Grid = (splits, kv heads, sequences).  A CTA owns one KV head of one
-// sequence and a contiguous range of positions; the G query heads that share
-// the KV head (GQA, attention.metal:23) are processed together so each K/V
-// row is read from HBM once.  Tiles of 64 positions (K and V rows in the
-// cache's layout, 32 KB) are staged in shared memory with cp.async, double
-// buffered; each of the 4 warps folds one 16-position block of a tile into
-// its own online softmax on the tensor cores (flash_decode.cuh), and the
-// warps' states meet in shared memory at the end.  Each split writes an
-// unnormalised partial (acc, max, sum) that a combine kernel merges with a
-// log-sum-exp rescale; with one split the CTA writes the normalised output.
-// The _rope entry point also does rope_kv_append's work (kernels/rope.metal
-// on q and k, then the cache append): each CTA rotates the query heads of its
-// KV head from the q|k|v row, and the split that attends the new position
-// rotates and writes that K row (and the V row) into the paged cache and
-// into its staged tile.
-#include <cmath>
-
-#include "common.cuh"
-#include "flash_decode.cuh"
+// real cache of seq_lens[b] positions.  Grid = (splits, kv heads,
+// sequences): each CTA runs one split-KV item (decode_attention.cuh: the
+// G query heads of a KV head over a contiguous range of positions, K/V
+// tiles staged with cp.async, the folds on the tensor cores); with more than
+// one split a combine kernel merges the partials.  The _rope entry point
+// also does rope_kv_append's work (RoPE on q and k, the cache append).
+#include "decode_attention.cuh"
 
 namespace lmps {
-
-constexpr int kAttnWarps = 4;
-constexpr int kAttnThreads = kAttnWarps * kWarp;
-constexpr int kAttnTile = kAttnWarps * fd::kBlk;  // positions per staged tile
-constexpr int kAttnStages = 2;                     // tiles in shared memory: one in flight while one computes
-constexpr int kHeadDim = 128;
-constexpr int kMaxGroup = 8;
-
-struct AttnParams {
-  const __half* q;        // [B, Hq*128] (rotated)
-  const __half* k_pool;   // [pages, Hkv, page_size, 128]
-  const __half* v_pool;
-  const int32_t* block_table;  // [B, max_pages]
-  const int32_t* seq_lens;     // [B]
-  __half* out;                 // [B, Hq*128]
-  float* part_o;               // [B, Hq, splits, 128]
-  float2* part_ml;             // [B, Hq, splits]
-  int max_pages, page_size, n_q_heads, n_kv_heads, n_splits, chunk;
-  int page_shift;  // log2(page_size) when it is a power of two, else -1
-  // fused RoPE + append (qkv != nullptr): q|k|v rows [B, (Hq + 2 Hkv) * 128]
-  // (bias applied), position of the new token per sequence (seq_lens = pos + 1)
-  const __half* qkv;
-  const int32_t* pos;
-  const float* inv_freq;
-  int rope_style;
-  __half* k_new;  // the pools, writable
-  __half* v_new;
-};
-
-struct __align__(16) AttnSmem {
-  union {
-    uint4 kv[kAttnStages][2][kAttnTile][fd::kRowUnits];  // [stage][K, V][row][16-byte unit], the cache's layout
-    float wo[kAttnWarps][32][32];                         // after the tiles: per-warp O^T fragments
-  };
-  __half q[kMaxGroup][kHeadDim];             // rotated q, natural dim order
-  __half knew[kHeadDim], vnew[kHeadDim];     // the appended row (rope entry point)
-  float wm[kAttnWarps][kMaxGroup];           // per-warp running max and sum
-  float wl[kAttnWarps][kMaxGroup];
-};
 
 __global__ void __launch_bounds__(kAttnThreads) gqa_decode_attn_kernel(const AttnParams P) {
   lmps_pdl_trigger();
   lmps_pdl_wait();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   AttnSmem& S = *reinterpret_cast<AttnSmem*>(smem_raw);
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-  const int G = P.n_q_heads / P.n_kv_heads;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, t4 = lane & 3;
-  const int T = P.seq_lens[b];
-  const int start = split * P.chunk;
-  const int end = min(T, start + P.chunk);
-  const int q_dim = P.n_q_heads * kHeadDim;
-  int pnew = -1;  // position whose row comes from S.knew / S.vnew instead of the cache
-
-  if (P.qkv != nullptr) {
-    // RoPE of the G query heads (rounded to fp16 as rope_kv_append's output)
-    const int kv_dim = P.n_kv_heads * kHeadDim;
-    const __half* row = P.qkv + static_cast<size_t>(b) * (q_dim + 2 * kv_dim);
-    const int p = P.pos[b];
-    const float m = static_cast<float>(p);
-    for (int t = tid; t < G * (kHeadDim / 2); t += kAttnThreads) {
-      const int hl = t / (kHeadDim / 2);
-      int i1, i2, fi;
-      rope_pair_index(t - hl * (kHeadDim / 2), kHeadDim, P.rope_style, i1, i2, fi);
-      const __half* src = row + (kvh * G + hl) * kHeadDim;
-      __half a = src[i1], c = src[i2];
-      rope_rotate(a, c, m * P.inv_freq[fi]);
-      S.q[hl][i1] = a;
-      S.q[hl][i2] = c;
-    }
-    if (p >= start && p < end) {  // this split attends the new position: append its K/V rows
-      pnew = p;
-      const int page = P.block_table[static_cast<size_t>(b) * P.max_pages + p / P.page_size];
-      const size_t dst = ((static_cast<size_t>(page) * P.n_kv_heads + kvh) * P.page_size + p % P.page_size) * kHeadDim;
-      const __half* ksrc = row + q_dim + kvh * kHeadDim;
-      for (int t = tid; t < kHeadDim / 2; t += kAttnThreads) {
-        int i1, i2, fi;
-        rope_pair_index(t, kHeadDim, P.rope_style, i1, i2, fi);
-        __half a = ksrc[i1], c = ksrc[i2];
-        rope_rotate(a, c, m * P.inv_freq[fi]);
-        P.k_new[dst + i1] = a;
-        P.k_new[dst + i2] = c;
-        S.knew[i1] = a;
-        S.knew[i2] = c;
-      }
-      for (int t = tid; t < kHeadDim; t += kAttnThreads) {
-        const __half v = row[q_dim + kv_dim + kvh * kHeadDim + t];
-        P.v_new[dst + t] = v;
-        S.vnew[t] = v;
-      }
-    }
-  } else {
-    for (int i = tid; i < G * kHeadDim; i += kAttnThreads) {
-      const int h = i / kHeadDim, d = i - h * kHeadDim;
-      S.q[h][d] = P.q[static_cast<size_t>(b) * q_dim + (kvh * G + h) * kHeadDim + d];
-    }
-  }
-  __syncthreads();  // S.q, S.knew / S.vnew
-
-  // Stage tile ti (positions start + 64 ti ..) into buffer ti % stages: thread tid
-  // copies 16-byte unit (tid & 15) of rows (tid >> 4) + 8 j of K and of V,
-  // so a warp instruction reads two whole 256-byte rows.
-  const int32_t* bt = P.block_table + static_cast<size_t>(b) * P.max_pages;
-  auto stage = [&](int ti) {
-    const int t0 = start + ti * kAttnTile, u = tid & (fd::kRowUnits - 1);
-#pragma unroll 4
-    for (int j = 0; j < kAttnTile * fd::kRowUnits / kAttnThreads; ++j) {
-      const int r = (tid >> 4) + j * (kAttnThreads / fd::kRowUnits), p = t0 + r;
-      uint4* dk = &S.kv[ti % kAttnStages][0][r][u];
-      uint4* dv = &S.kv[ti % kAttnStages][1][r][u];
-      if (p == pnew) {
-        *dk = reinterpret_cast<const uint4*>(S.knew)[u];
-        *dv = reinterpret_cast<const uint4*>(S.vnew)[u];
-      } else if (p < end) {
-        const int pi = P.page_shift >= 0 ? p >> P.page_shift : p / P.page_size;
-        const int in_page = P.page_shift >= 0 ? p & (P.page_size - 1) : p - pi * P.page_size;
-        const size_t off =
-            ((static_cast<size_t>(__ldg(bt + pi)) * P.n_kv_heads + kvh) * P.page_size + in_page) * kHeadDim + 8 * u;
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dk)), "l"(P.k_pool + off)
-                     : "memory");
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dv)), "l"(P.v_pool + off)
-                     : "memory");
-      }
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  };
-  const int n_tiles = end > start ? (end - start + kAttnTile - 1) / kAttnTile : 0;
-  for (int ti = 0; ti < n_tiles && ti < kAttnStages - 1; ++ti) stage(ti);
-
-  uint32_t qf[16];
-  fd::load_qf(&S.q[0][0], G, qf);
-  float o[8][4];
-#pragma unroll
-  for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.0f;
-  float mrun0 = -INFINITY, mrun1 = -INFINITY, lrun0 = 0.0f, lrun1 = 0.0f;  // heads 2*t4, 2*t4+1
-  for (int ti = 0; ti < n_tiles; ++ti) {
-    if (ti + kAttnStages - 1 < n_tiles) stage(ti + kAttnStages - 1);  // into the buffer tile ti - 1 used
-    // tile ti's group complete: the groups of later tiles may stay in flight
-    const int later = min(n_tiles - 1, ti + kAttnStages - 1) - ti;
-    if (later >= 2)
-      asm volatile("cp.async.wait_group 2;" ::: "memory");
-    else if (later == 1)
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-    else
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();  // tile ti landed for every thread's copies
-    const int p0 = start + ti * kAttnTile + warp * fd::kBlk;
-    const int sb = ti % kAttnStages;
-    if (p0 < end) {
-      uint4 kr[2][4], vr[2][4];
-      fd::load_rows(&S.kv[sb][0][warp * fd::kBlk][0], &S.kv[sb][1][warp * fd::kBlk][0], p0, end, kr, vr);
-      fd::block_update(kr, vr, p0, end, qf, o, mrun0, mrun1, lrun0, lrun1);
-    }
-    __syncthreads();  // buffer sb is free for tile ti + stages
-  }
-
-  // -- the warps meet in shared memory; the reducing thread rescales each
-  // warp's state to the merged max
-  const int nw = min(kAttnWarps, (max(end - start, 0) + fd::kBlk - 1) / fd::kBlk);  // warps that saw positions
-  if (warp < nw) {
-    if ((lane >> 2) == 0) {
-      S.wm[warp][2 * t4] = mrun0;
-      S.wm[warp][2 * t4 + 1] = mrun1;
-      S.wl[warp][2 * t4] = lrun0;
-      S.wl[warp][2 * t4 + 1] = lrun1;
-    }
-    fd::store_frags(S.wo[warp], o);
-  }
-  __syncthreads();
-  for (int w = tid; w < G * (kHeadDim / 2); w += kAttnThreads) {
-    const int h = w / (kHeadDim / 2), d = 2 * (w - h * (kHeadDim / 2));
-    int la, k;
-    fd::frag_slot(h, d, la, k);
-    float M = -INFINITY;
-    for (int ww = 0; ww < nw; ++ww) M = fmaxf(M, S.wm[ww][h]);
-    float n0 = 0.0f, n1 = 0.0f, den = 0.0f;
-    for (int ww = 0; ww < nw; ++ww) {
-      const float f = expf(S.wm[ww][h] - M);
-      const float2 v = fd::load_frag_pair(S.wo[ww], la, k);
-      n0 = fmaf(v.x, f, n0);
-      n1 = fmaf(v.y, f, n1);
-      den = fmaf(S.wl[ww][h], f, den);
-    }
-    if (P.n_splits == 1) {
-      const float inv = den > 0.0f ? 1.0f / den : 0.0f;
-      *reinterpret_cast<__half2*>(&P.out[static_cast<size_t>(b) * q_dim + (kvh * G + h) * kHeadDim + d]) =
-          __floats2half2_rn(n0 * inv, n1 * inv);
-    } else {
-      const size_t prow = (static_cast<size_t>(b) * P.n_q_heads + kvh * G + h) * P.n_splits + split;
-      *reinterpret_cast<float2*>(&P.part_o[prow * kHeadDim + d]) = make_float2(n0, n1);
-      if (d == 0) P.part_ml[prow] = make_float2(M, den);
-    }
-  }
+  const QkvRowLoader qkv{P.qkv, (P.n_q_heads + 2 * P.n_kv_heads) * kHeadDim};
+  attn_item(P, S, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, P.qkv != nullptr, qkv, CtaSync{});
 }
 
 // Merge the per-split partials of one (sequence, query head): log-sum-exp.
 __global__ void __launch_bounds__(kHeadDim) gqa_combine_kernel(const AttnParams P) {
   lmps_pdl_trigger();
   lmps_pdl_wait();
-  const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
-  const size_t row0 = (static_cast<size_t>(b) * P.n_q_heads + h) * P.n_splits;
-  float M = -INFINITY;
-  for (int s = 0; s < P.n_splits; ++s) M = fmaxf(M, P.part_ml[row0 + s].x);
-  float num = 0.0f, den = 0.0f;
-  if (M != -INFINITY) {
-    for (int s = 0; s < P.n_splits; ++s) {
-      const float2 ml = P.part_ml[row0 + s];
-      if (ml.y > 0.0f) {
-        const float w = expf(ml.x - M);
-        num = fmaf(w, P.part_o[(row0 + s) * kHeadDim + d], num);
-        den = fmaf(w, ml.y, den);
-      }
-    }
-  }
-  P.out[static_cast<size_t>(b) * P.n_q_heads * kHeadDim + h * kHeadDim + d] =
-      __float2half_rn(den > 0.0f ? num / den : 0.0f);
-}
-
-static int attn_chunk(int max_seq_len, int n_splits) {
-  int chunk = (max_seq_len + n_splits - 1) / n_splits;
-  return (chunk + kAttnTile - 1) / kAttnTile * kAttnTile;
+  attn_combine(P, blockIdx.x, blockIdx.y, threadIdx.x);
 }
 
 }  // namespace lmps

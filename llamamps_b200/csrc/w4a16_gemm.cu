@@ -31,12 +31,14 @@
 //     distributed shared memory, each CTA finishing a slice of the rows.
 // Every mbarrier wait is bounded (error flag, no hang).
 #include "common.cuh"
+#include "q4_tile.cuh"
 #include "tcgen05.cuh"
 
 namespace lmps {
 namespace w4 {
 
 using namespace tc;
+using q4t::dequant8;
 
 constexpr int kBK = 64;        // K per stage
 constexpr int kRows = 128;     // weight rows per tile
@@ -95,22 +97,6 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
-
-// fp16 (nibble - 8) * scale of the 8 elements of one packed word, in element
-// order.  Halves of t_i hold the nibbles (i, i + 4) as 1024 + n.
-__device__ __forceinline__ uint4 dequant8(uint32_t w, __half2 s2) {
-  const __half2 k1032 = __halves2half2(__ushort_as_half(0x6408u), __ushort_as_half(0x6408u));
-  uint32_t t[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t v = ((w >> (4 * i)) & 0x000F000Fu) | 0x64006400u;
-    const __half2 h = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&v), k1032), s2);
-    t[i] = *reinterpret_cast<const uint32_t*>(&h);
-  }
-  return make_uint4(__byte_perm(t[0], t[1], 0x5410), __byte_perm(t[2], t[3], 0x5410),
-                    __byte_perm(t[0], t[1], 0x7632), __byte_perm(t[2], t[3], 0x7632));
-}
-
 
 // Y[row][col] from an fp32 accumulator value and the epilogue operands.
 __device__ __forceinline__ __half epi_value(const Params& P, float v, int row, int col) {

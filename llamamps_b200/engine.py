@@ -106,18 +106,24 @@ class QwenEngine:
         self._create_buffer_pool()
         self._graphs = {}
         # "persistent": one cooperative kernel per launch runs whole decode
-        # steps (csrc/decode_persistent.cu, batch <= 4); "kernels": one kernel
-        # per stage, replayed as a CUDA graph (any batch).
+        # steps (csrc/decode_persistent.cu, batch <= 4); "batched": one
+        # cooperative kernel runs every layer of a step (csrc/decode_batched.cu,
+        # batch <= 64), with the head kernels after it; "kernels": one kernel
+        # per stage (any batch).  The last two are replayed as CUDA graphs.
         from .persistent import MAX_BATCH as PERSISTENT_MAX_BATCH
         if decoder is None:
             decoder = "persistent" if max_batch <= PERSISTENT_MAX_BATCH else "kernels"
-        if decoder not in ("persistent", "kernels"):
+        if decoder not in ("persistent", "kernels", "batched"):
             raise ValueError(f"unknown decoder {decoder!r}")
         self.decoder = decoder
         self.pdec = None
+        self.bdec = None
         if decoder == "persistent":
             from .persistent import PersistentDecoder
             self.pdec = PersistentDecoder(self.weights, self.cache, self.inv_freq, max_batch)
+        elif decoder == "batched":
+            from .batched import BatchedDecoder
+            self.bdec = BatchedDecoder(self.weights, self.cache, self.inv_freq, max_batch)
         self.batch = 1
         self.reset(1)
 
@@ -178,6 +184,9 @@ class QwenEngine:
         c, w = self.cfg, self.weights
         x = self.buf_residual[:B]
         xn = self.buf_normed[:B]
+        if self.bdec is not None:  # every layer in one launch
+            self.bdec.run(B, x, self.pos[:B], self.seq_lens[:B])
+            return
         gemm = B > self.gemv_max_batch   # dense contraction: tcgen05 W4A16 GEMM
         for li, lw in enumerate(w.layers):
             kp, vp = self.cache.layer(li)
@@ -339,6 +348,8 @@ class QwenEngine:
         persistent decoder runs any number of steps in one launch."""
         if self.pdec is not None:
             return 1
+        if self.bdec is not None:  # embed, the layers, final norm, LM head + argmax, advance
+            return 1 + 1 + 1 + 2 + 1
         # norm, q|k|v, RoPE + append + attention (+ split combine), o, norm,
         # gate/up (+ SwiGLU on the GEMM path), down; then embed, final norm, the
         # LM head with its argmax (two launches on either path), advance
@@ -360,6 +371,8 @@ class QwenEngine:
         torch.cuda.current_stream(self.device).synchronize()
         if self.pdec is not None:
             self.pdec.check_error()
+        if self.bdec is not None:
+            self.bdec.check_error()
         return self._pin_next.numpy()[:B].copy()
 
     def decode_step(self, record: bool = True) -> None:
@@ -528,6 +541,8 @@ class QwenEngine:
         torch.cuda.synchronize(self.device)
         if self.pdec is not None:
             self.pdec.check_error()
+        if self.bdec is not None:
+            self.bdec.check_error()
         if int(self.bad_ids.item()) != 0:
             self.bad_ids.zero_()
             raise ValueError("token id outside the vocabulary")

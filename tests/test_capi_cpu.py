@@ -22,8 +22,29 @@ def test_library_exports_every_header_symbol():
 
 
 def test_every_header_symbol_has_a_python_signature():
-    from llamamps_b200 import persistent
-    assert set(_lib.header_symbols()) == set(_lib._SIGS) | set(persistent._SIGS)
+    from llamamps_b200 import batched, persistent
+    assert set(_lib.header_symbols()) == set(_lib._SIGS) | set(persistent._SIGS) | set(batched._SIGS)
+
+
+def test_batched_descriptor_layouts_match_the_header():
+    """ctypes mirrors of lmps_batched_layer / lmps_batched_desc; argument
+    validation of the batched decode and the tile-major repack."""
+    import ctypes
+    from llamamps_b200 import batched as Bd
+    assert ctypes.sizeof(Bd.BatchedLayer) == 9 * 8
+    assert Bd.BatchedDesc.n_layers.offset == 8 and Bd.BatchedDesc.inv_freq.offset == 40
+    assert ctypes.sizeof(Bd.BatchedDesc) == 48
+    L = Bd._declare()
+    assert L.lmps_q4_tile_blocks_size(2048, 1536) == 16 * 24 * 4608
+    assert L.lmps_q4_tile_blocks_size(100, 1536) == 0 and L.lmps_q4_tile_blocks_size(128, 100) == 0
+    assert L.lmps_q4_tile_blocks(None, None, 128, 64, None, None) == -1
+    assert L.lmps_q4_tile_blocks(16, 16, 100, 64, 16, None) == -1
+    m = Bd.BatchedDesc(None, 28, 1536, 8960, 12, 2, 128, 1e-6, 0, None)
+    assert L.lmps_decode_batched(ctypes.byref(m), 16, 16, 16, 16, 1, 64, 8, 64, 256, 1 << 20, 16, None, None) == -1
+    m = Bd.BatchedDesc(16, 28, 1536, 8960, 12, 2, 64, 1e-6, 0, 16)  # head_dim 64
+    assert L.lmps_decode_batched(ctypes.byref(m), 16, 16, 16, 16, 1, 64, 8, 64, 256, 1 << 20, 16, None, None) == -2
+    m = Bd.BatchedDesc(16, 28, 1536, 8960, 12, 2, 128, 1e-6, 0, 16)
+    assert L.lmps_decode_batched(ctypes.byref(m), 16, 16, 16, 16, 1, 64, 65, 64, 256, 1 << 20, 16, None, None) == -2
 
 
 def test_persistent_descriptor_layouts_match_the_header():
