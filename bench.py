@@ -619,8 +619,82 @@ def time_decode(B: int, T: int, n_layers: int, steps: int, launches: int = 3, ti
     return out
 
 
+def time_batched(B: int, steps: int, timeline: bool) -> dict:
+    """Decode steps of ``B`` sequences after 128-id prompts (the batched
+    configuration's prompt length), full model: the per-stage kernel path
+    against the one-launch batched decode kernel (csrc/decode_batched.cu),
+    CUDA events over ``steps`` graph replays.  With ``timeline``, the
+    batched kernel's grid-barrier timeline of one launch: per stage, the
+    median over layers of (last arrival - previous stage's last arrival),
+    and for the projection stages when the CTAs' weight tiles were
+    dequantised and their accumulators ready (medians over CTAs, us after
+    the gate barrier)."""
+    import numpy as np
+    import torch
+    from llamamps_b200 import kernels as K
+    from llamamps_b200.config import QWEN2_5_1_5B as cfg
+    from llamamps_b200.engine import QwenEngine
+    from llamamps_b200.weights import synth_model
+    mw = synth_model(cfg, seed=0, device="cuda")
+    out = {"kernel": "decode_batched_kernel vs per-stage kernels", "batch": B, "prompt": 128, "layers": cfg.n_layers}
+    for dec in ("kernels", "batched"):
+        eng = QwenEngine(weights=mw, max_batch=B, max_seq_len=128 + steps + 16, decoder=dec)
+        prompt = np.random.default_rng(2).integers(0, cfg.vocab, (B, 128))
+        eng.reset(B)
+        eng.prefill(torch.from_numpy(prompt))
+        eng.decode_steps(3, record=False)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        eng.decode_steps(steps, record=False)
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / steps
+        out[f"{dec}_ms_per_step"] = round(ms, 3)
+        out[f"{dec}_tok_s"] = round(B / ms * 1e3, 1)
+        if dec == "batched":
+            eng.bdec.check_error()
+        if dec == "batched" and timeline:
+            G = torch.cuda.get_device_properties(0).multi_processor_count
+            L = cfg.n_layers
+            nb = eng.bdec.barriers(B)
+            per = (nb - 1) // L
+            names = ["qkv", "attention"] + (["merge"] if per == 8 else []) + ["o", "reduce_o", "gate_up", "down",
+                                                                                  "reduce_down"]
+            tr = torch.zeros(G, nb, 4, dtype=torch.int64, device="cuda")
+            K.embed_gather(eng.weights.embed, eng.tokens[:B], eng.buf_residual[:B], eng.bad_ids)
+            eng.bdec.run(B, eng.buf_residual[:B], eng.pos[:B], eng.seq_lens[:B], trace=tr)
+            torch.cuda.synchronize()
+            t = tr.cpu().numpy().astype(np.float64)
+            last = t[:, :, 0].max(axis=0)
+            stage = {}
+            for j, nm in enumerate(names):
+                ks = [1 + l * per + j for l in range(L)]
+                d = {"us": round(float(np.median([(last[k] - last[k - 1]) / 1e3 for k in ks])), 2)}
+                if nm in ("qkv", "o", "gate_up", "down"):
+                    dq, ac = [], []
+                    for k in ks:
+                        m = t[:, k, 2] > 0
+                        dq.append((np.median(t[m, k, 2]) - last[k - 1]) / 1e3)
+                        ac.append((np.median(t[m, k, 3]) - last[k - 1]) / 1e3)
+                    d["dequantised_us"] = round(float(np.median(dq)), 2)
+                    d["accumulated_us"] = round(float(np.median(ac)), 2)
+                stage[nm] = d
+            obs = t[:, :, 1]
+            lat = [float(np.min(obs[obs[:, k] > 0, k]) - last[k]) / 1e3 for k in range(1, nb) if np.any(obs[:, k] > 0)]
+            out["timeline"] = {"per_layer_us": round(float((last[-1] - last[0]) / 1e3 / L), 2), "stages": stage,
+                               "barrier_latency_us": round(float(np.median(lat)), 2)}
+        del eng
+        torch.cuda.empty_cache()
+    return out
+
+
 def run_kernel_timing(args) -> int:
     """--time gemm|attention|prefill_attention|gemv|decode: one JSON line per shape (not a benchmark line)."""
+    if args.time == "batched":
+        for b in ([int(s) for s in args.shape] if args.shape else [8, 64]):
+            print(json.dumps(time_batched(b, args.iters, bool(args.timeline))))
+        return 0
     if args.time == "decode":
         shapes = [tuple(int(v) for v in s.split(",")) for s in args.shape] if args.shape else [(4, 32768)]
         for b, t in shapes:
@@ -805,11 +879,14 @@ def main():
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling only: build a model with fewer decoder layers (the JSON line "
                          "then names the reduced workload and is not a measurement of it)")
-    ap.add_argument("--time", choices=["gemm", "attention", "prefill_attention", "gemv", "decode"], default=None,
+    ap.add_argument("--time", choices=["gemm", "attention", "prefill_attention", "gemv", "decode", "batched"],
+                    default=None,
                     help="kernel timing tables instead of the benchmark: the tcgen05 W4A16 GEMM, the "
                          "split-KV decode attention, the causal prefill attention, the gate/up SwiGLU Q4 "
-                         "GEMV or the persistent decoder (--layers, --iters steps per launch), per --shape "
-                         "(m,n,k / batch,attended,cache / batch,seq_len / rows,k,batch / batch,cached)")
+                         "GEMV, the persistent decoder (--layers, --iters steps per launch) or the batched "
+                         "decode kernel against the per-stage path (--iters steps; --timeline any value: "
+                         "its barrier timeline), per --shape (m,n,k / batch,attended,cache / "
+                         "batch,seq_len / rows,k,batch / batch,cached / batch)")
     ap.add_argument("--shape", action="append", default=None, help="shape for --time (repeatable)")
     ap.add_argument("--iters", type=int, default=20,
                     help="calls per timing for --time gemm / gemv; steps per launch for --time decode")

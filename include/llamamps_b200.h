@@ -463,9 +463,12 @@ typedef struct lmps_batched_desc {
 } lmps_batched_desc;
 
 /* Workspace bytes for `batch` sequences (0 if the model is unsupported:
- * head_dim 128, hidden a multiple of 512 and <= 4096, every projection's rows
+ * head_dim 128, hidden a multiple of 512 and <= 2048, every projection's rows
  * a multiple of 128 and at most one 128-row tile per SM, K a multiple of 64). */
 size_t lmps_decode_batched_workspace_size(const lmps_batched_desc* model, int batch, int max_seq_len);
+
+/* Grid barriers of one launch (rows of its trace per CTA; 0 if unsupported). */
+int lmps_decode_batched_barriers(const lmps_batched_desc* model, int batch, int max_seq_len);
 
 /* One decode step of every layer: x (fp16 [batch, hidden], the embedded
  * tokens) becomes the residual after the last layer (the final norm is the
@@ -474,10 +477,11 @@ size_t lmps_decode_batched_workspace_size(const lmps_batched_desc* model, int ba
  * 256-byte aligned, zeroed once (it carries a grid-barrier counter from
  * launch to launch) and again after a reported error.  error: 1 = a bounded
  * device wait gave up, 2 = a position outside the cache (nothing ran).
- * trace (or NULL): %globaltimer stamps [grid][barriers][2] -- when each CTA's
- * workers arrived at each grid barrier and when they saw it complete (0 where
- * they did not wait); barriers = 1 + n_layers * (7, or 8 when the attention
- * is split over CTAs). */
+ * trace (or NULL): %globaltimer stamps [grid][barriers][4] -- when each CTA's
+ * workers arrived at each grid barrier, when they saw it complete (0 where
+ * they did not wait), and for a barrier that ends a projection stage, when
+ * the CTA's weight tiles were all dequantised and when its accumulator was
+ * ready; barriers: lmps_decode_batched_barriers(). */
 int lmps_decode_batched(const lmps_batched_desc* model, uint16_t* x, const int32_t* pos,
                         const int32_t* seq_lens, const int32_t* block_table, int max_pages,
                         int page_size, int batch, int max_seq_len, void* workspace,

@@ -38,6 +38,7 @@ _SIGS = {
     "lmps_q4_tile_blocks_size": (c_size, [c_int, c_int]),
     "lmps_q4_tile_blocks": (c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp]),
     "lmps_decode_batched_workspace_size": (c_size, [ctypes.POINTER(BatchedDesc), c_int, c_int]),
+    "lmps_decode_batched_barriers": (c_int, [ctypes.POINTER(BatchedDesc), c_int, c_int]),
     "lmps_decode_batched": (c_int, [ctypes.POINTER(BatchedDesc), c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int,
                                     c_int, c_vp, c_size, c_vp, c_vp, c_vp]),
 }
@@ -76,7 +77,7 @@ def tile_blocks(packed: torch.Tensor, scales: torch.Tensor, n: int, k: int) -> t
 def supported(cfg) -> bool:
     """The batched kernel's shape limits (the C side checks them again)."""
     qkv = (cfg.n_q_heads + 2 * cfg.n_kv_heads) * cfg.head_dim
-    return (cfg.head_dim == 128 and cfg.hidden % 512 == 0 and cfg.hidden <= 4096 and qkv % 128 == 0
+    return (cfg.head_dim == 128 and cfg.hidden % 512 == 0 and cfg.hidden <= 2048 and qkv % 128 == 0
             and (2 * cfg.intermediate) % 128 == 0 and cfg.intermediate % 64 == 0
             and cfg.n_q_heads // cfg.n_kv_heads <= 8)
 
@@ -127,6 +128,10 @@ class BatchedDecoder:
         self.workspace.zero_()
         self.error.zero_()
 
+    def barriers(self, batch: int) -> int:
+        """Grid barriers of one launch for ``batch`` sequences (trace rows per CTA)."""
+        return self.L.lmps_decode_batched_barriers(ctypes.byref(self.desc), batch, self.cache.max_seq_len)
+
     def check_error(self) -> None:
         e = int(self.error.item())
         if e:
@@ -139,9 +144,14 @@ class BatchedDecoder:
             trace: Optional[torch.Tensor] = None) -> None:
         """All layers for sequences 0..batch-1: x [batch, hidden] (embedded
         tokens) becomes the residual after the last layer; the new K/V rows
-        go into the cache at pos.  trace: optional int64 [grid, barriers, 2]
-        barrier timeline (%globaltimer ns)."""
+        go into the cache at pos.  trace: optional int64 [grid, barriers, 4]
+        timeline (%globaltimer ns; see include/llamamps_b200.h)."""
         cache = self.cache
+        if trace is not None:
+            want = (torch.cuda.get_device_properties(x.device).multi_processor_count,
+                    self.barriers(batch), 4)
+            if tuple(trace.shape) != want or trace.dtype != torch.int64:
+                raise ValueError(f"trace must be int64 {want}")
         check(self.L.lmps_decode_batched(ctypes.byref(self.desc), _p(x), _p(pos), _p(seq_lens),
                                          _p(cache.block_table), cache.block_table.shape[1], cache.page_size, batch,
                                          cache.max_seq_len, self.ws_view.data_ptr(), self.ws_view.numel(),

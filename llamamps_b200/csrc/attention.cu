@@ -12,6 +12,8 @@
 
 namespace lmps {
 
+using AttnSmem = AttnSmemT<2>;  // two K/V tiles: 67 KB, three CTAs per SM
+
 __global__ void __launch_bounds__(kAttnThreads) gqa_decode_attn_kernel(const AttnParams P) {
   lmps_pdl_trigger();
   lmps_pdl_wait();

@@ -32,7 +32,6 @@ namespace lmps {
 constexpr int kAttnWarps = 4;
 constexpr int kAttnThreads = kAttnWarps * kWarp;
 constexpr int kAttnTile = kAttnWarps * fd::kBlk;  // positions per staged tile
-constexpr int kAttnStages = 2;                     // tiles in shared memory: one in flight while one computes
 constexpr int kHeadDim = 128;
 constexpr int kMaxGroup = 8;
 
@@ -57,9 +56,12 @@ struct AttnParams {
   __half* v_new;
 };
 
-struct __align__(16) AttnSmem {
+// Shared memory of an item with `Stages` K/V tiles in flight (Stages - 1
+// loading while one is folded).
+template <int Stages>
+struct __align__(16) AttnSmemT {
   union {
-    uint4 kv[kAttnStages][2][kAttnTile][fd::kRowUnits];  // [stage][K, V][row][16-byte unit], the cache's layout
+    uint4 kv[Stages][2][kAttnTile][fd::kRowUnits];  // [stage][K, V][row][16-byte unit], the cache's layout
     float wo[kAttnWarps][32][32];                         // after the tiles: per-warp O^T fragments
   };
   __half q[kMaxGroup][kHeadDim];             // rotated q, natural dim order
@@ -84,9 +86,10 @@ struct CtaSync {
 
 // One item on kAttnThreads threads (tid = 0 .. 127 among them; `sync` is a
 // barrier over exactly those threads).
-template <class Loader, class Sync>
-__device__ __forceinline__ void attn_item(const AttnParams& P, AttnSmem& S, int split, int kvh, int b, int tid,
-                                          bool fused, const Loader& qkv, Sync sync) {
+template <int kAttnStages, class Loader, class Sync>
+__device__ __forceinline__ void attn_item(const AttnParams& P, AttnSmemT<kAttnStages>& S, int split, int kvh, int b,
+                                          int tid, bool fused, const Loader& qkv, Sync sync) {
+  static_assert(kAttnStages >= 2 && kAttnStages <= 4, "K/V tile stages");
   const int G = P.n_q_heads / P.n_kv_heads;
   const int warp = tid >> 5, lane = tid & 31, t4 = lane & 3;
   const int T = P.seq_lens[b];
@@ -179,7 +182,9 @@ __device__ __forceinline__ void attn_item(const AttnParams& P, AttnSmem& S, int 
     if (ti + kAttnStages - 1 < n_tiles) stage(ti + kAttnStages - 1);  // into the buffer tile ti - 1 used
     // tile ti's group complete: the groups of later tiles may stay in flight
     const int later = min(n_tiles - 1, ti + kAttnStages - 1) - ti;
-    if (later >= 2)
+    if (later >= 3)
+      asm volatile("cp.async.wait_group 3;" ::: "memory");
+    else if (later == 2)
       asm volatile("cp.async.wait_group 2;" ::: "memory");
     else if (later == 1)
       asm volatile("cp.async.wait_group 1;" ::: "memory");

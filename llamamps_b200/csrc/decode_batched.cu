@@ -28,13 +28,16 @@
 // 64-wide K step one 4608-byte block (packed nibbles, then the group scales),
 // fetched with one bulk copy.
 //
-// Roles of the 192 threads of a CTA (as in the W4A16 GEMM): warp 0 lane 0
+// Roles of the 352 threads of a CTA (as in the W4A16 GEMM): warp 0 lane 0
 // issues the weight and activation loads, warp 1 lane 0 the MMAs
 // (A = 128 dequantised weight rows, B = the tokens, N = batch rounded up to
-// 16, two TMEM accumulators used alternately), warps 2-5 dequantise, run the
-// epilogues and the attention / reduction phases.  Every wait is bounded: a
-// timeout sets the error word and a workspace abort flag that every CTA
-// polls, and the launch ends without a hang.
+// 16, two TMEM accumulators used alternately), warps 2-9 dequantise (half a
+// weight row of a K step per thread), warps 2-5 also run the epilogues and
+// the attention / reduction phases, warp 10 lane 0 watches the grid barrier
+// counter (the only thread of the CTA that polls global memory in a wait;
+// everything else waits on shared memory).  Every wait is bounded: a timeout
+// sets the error word and a workspace abort flag that the watchers see, and
+// the launch ends without a hang.
 #include <cmath>
 
 #include "common.cuh"
@@ -47,19 +50,25 @@ namespace bd {
 
 using namespace tc;
 
-constexpr int kThreads = 192;
-constexpr int kWorkers = 128;                 // warps 2-5
+constexpr int kThreads = 352;                 // 11 warps
+constexpr int kWorkers = 128;                 // warps 2-5: dequantise, epilogues, attention, reductions
+constexpr int kDequant = 256;                 // warps 2-9 dequantise (half a weight row per thread)
+constexpr int kWatcherTid = 320;              // warp 10 lane 0
+constexpr int kAttnStagesB = 3;               // K/V tiles in flight in the attention phase
+constexpr int kTPitch = 36;                   // epilogue transpose: floats per token row (16-byte rows)
 constexpr int kBK = 64;
 constexpr int kRows = 128;
 constexpr int kBlockBytes = q4t::kBlockBytes; // 4096 packed + 512 scale bytes
 constexpr int kMaxNt = 64;                    // tokens per MMA (batch rounded up to 16)
-constexpr int kXStages = 4;
-constexpr int kDStages = 3;
-constexpr int kXSlot = kMaxNt * 128;          // 8 KB: nt rows x 128 bytes, 1024-byte aligned
+constexpr int kXBytes = 48 * 1024;            // activation ring: nt x 128-byte slots (1024-byte multiples)
+constexpr int kMaxXStages = 16;
+constexpr int kDStages = 5;
 constexpr int kDSlot = kRows * 128;           // 16 KB dequantised fp16 tile
 constexpr int kMaxWSlots = 32;
 constexpr int kTmemCols = 2 * kMaxNt;         // two accumulators
 constexpr int kMaxLayers = 64;
+constexpr int kAttnMinChunk = 512;
+constexpr unsigned kIdleNs = 64;  // pause of a polling thread that found nothing to do
 
 enum Stage { ST_QKV = 0, ST_O = 1, ST_GU = 2, ST_DN = 3, ST_N = 4 };
 
@@ -71,7 +80,7 @@ struct __align__(64) Params {
   __half* xn;    // normalised activations [B, hidden]
   __half* attn;  // attention output [B, q_dim]
   __half* a;     // SwiGLU output [B, intermediate]
-  float* part[ST_N];  // fp32 split partials of QKV, O, DN: [split][B][rows]
+  float* part[ST_N];  // fp32 split-K accumulators of QKV, O, DN: [B][rows], zero between uses
   float* att_o;       // attention split partials
   float2* att_ml;
   unsigned long long* bar;  // grid barrier counter
@@ -88,7 +97,8 @@ struct __align__(64) Params {
   int tiles[ST_N], splits[ST_N], ksteps[ST_N];
   int att_splits, att_chunk;
   int wslots;
-  unsigned long long* trace;  // optional [grid][barriers][2]: arrival, completion seen (%globaltimer)
+  int xstages, xslot;         // activation ring: slots of nt * 128 bytes
+  unsigned long long* trace;  // optional [grid][barriers][4] %globaltimer stamps (see lmps_decode_batched)
   int n_bars;
 };
 
@@ -101,40 +111,27 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
 __device__ __forceinline__ void red_release_add(unsigned long long* p, unsigned long long v) {
   asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ bool aborted(const Params& P) {
-  return *reinterpret_cast<volatile int*>(P.abort_flag) != 0;
+__device__ __forceinline__ int ld_acquire_cta(const int* p) {
+  int v;
+  asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+  return v;
 }
-__device__ __noinline__ void raise_abort(const Params& P) {
-  atomicExch(P.error, 1);
-  atomicExch(P.abort_flag, 1);
-}
-// Bounded wait until the counter reaches `target` (false: aborted / timed out).
-__device__ bool counter_wait(const Params& P, unsigned long long target) {
-  if (ld_acquire_u64(P.bar) >= target) return true;
-  const uint64_t t0 = globaltimer();
-  while (ld_acquire_u64(P.bar) < target) {
-    if (aborted(P)) return false;
-    if (globaltimer() - t0 > kTimeoutNs) {
-      raise_abort(P);
-      return false;
-    }
-  }
-  return true;
+__device__ __forceinline__ void st_release_cta(int* p, int v) {
+  asm volatile("st.release.cta.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
 }
 __device__ __forceinline__ void workers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kWorkers) : "memory"); }
 
-// Bounded mbarrier wait that also gives up when another CTA aborted.
-__device__ __forceinline__ bool mwait(const Params& P, uint64_t* bar, uint32_t parity) {
-  if (mbar_try(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  while (!mbar_try(bar, parity)) {
-    if (aborted(P)) return false;
-    if (globaltimer() - t0 > kTimeoutNs) {
-      raise_abort(P);
-      return false;
-    }
-  }
-  return true;
+// Non-blocking probe of a phase (try_wait may suspend the thread for a while,
+// which the producer, polling two rings, cannot afford).
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
 }
 
 // 1-D bulk copy global -> this CTA's shared memory (no multicast).
@@ -193,52 +190,98 @@ struct Bars {
   }
 };
 
+using AttnSmemB = AttnSmemT<kAttnStagesB>;
+
 struct Smem {
-  unsigned char* xs;  // [kXStages][kXSlot] activation tiles (128-byte swizzle)
+  unsigned char* xs;  // [xstages][xslot] activation tiles (128-byte swizzle)
   unsigned char* wd;  // [kDStages][kDSlot] dequantised weight tiles (128-byte swizzle)
   unsigned char* wr;  // [wslots][kBlockBytes] tile-major weight blocks
-  uint64_t *fullw, *emptyw, *fullx, *emptyx, *deq, *emptyd, *accf, *acce, *done;
+  uint64_t *fullw, *emptyw, *fullx, *emptyx, *deq, *emptyd, *accf, *acce, *done, *attn_done;
   uint32_t* tmem_slot;
   int* stop;                 // workers' shared stop decision
+  int* sabort;               // this CTA is giving up (mirror of the launch's abort flag)
+  int* sseen;                // highest grid barrier seen complete (kept by the watcher)
   unsigned long long* base;  // grid-barrier count at launch start
   float* red;                // [4] per-warp sums
 };
-constexpr int kFixedSmem = 1024 + kXStages * kXSlot + kDStages * kDSlot + 2048;
-static_assert(sizeof(AttnSmem) + (kMaxGroup + 2) * kHeadDim * 2 <= kXStages * kXSlot + kDStages * kDSlot,
+constexpr int kFixedSmem = 1024 + kXBytes + kDStages * kDSlot + 2048;
+
+// Every wait polls shared memory only: a timeout (or a give-up seen by the
+// watcher) sets the CTA's abort word, and the launch's error and abort words.
+__device__ __forceinline__ bool cta_aborting(const Smem& S) { return *reinterpret_cast<volatile int*>(S.sabort) != 0; }
+__device__ __noinline__ void raise_abort(const Params& P, const Smem& S) {
+  atomicExch(P.error, 1);
+  atomicExch(P.abort_flag, 1);
+  *reinterpret_cast<volatile int*>(S.sabort) = 1;
+}
+__device__ __forceinline__ bool mwait(const Params& P, const Smem& S, uint64_t* bar, uint32_t parity) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try(bar, parity)) {
+    if (cta_aborting(S)) return false;
+    if (globaltimer() - t0 > kTimeoutNs) {
+      raise_abort(P, S);
+      return false;
+    }
+  }
+  return true;
+}
+// Bounded wait until grid barrier k is complete (as the watcher saw it).
+__device__ __forceinline__ bool bar_wait(const Params& P, const Smem& S, int k) {
+  if (ld_acquire_cta(S.sseen) >= k) return true;
+  const uint64_t t0 = globaltimer();
+  while (ld_acquire_cta(S.sseen) < k) {
+    __nanosleep(kIdleNs);
+    if (cta_aborting(S)) return false;
+    if (globaltimer() - t0 > kTimeoutNs) {
+      raise_abort(P, S);
+      return false;
+    }
+  }
+  return true;
+}
+
+// ---- warp 6 lane 0: the only poller of the launch's barrier counter; it
+// publishes each completed barrier to the CTA (release / acquire through
+// shared memory), and a give-up by another CTA.
+__device__ void watcher(const Params& P, const Smem& S, unsigned long long bbase) {
+  const unsigned long long G = gridDim.x;
+  const int last = P.n_bars - 1;
+  int seen = -1;
+  uint64_t t0 = globaltimer();
+  for (unsigned it = 0; seen < last; ++it) {
+    const int now = static_cast<int>((ld_acquire_u64(P.bar) - bbase) / G) - 1;
+    if (now > seen) {
+      seen = now;
+      st_release_cta(S.sseen, seen);
+      t0 = globaltimer();
+      continue;
+    }
+    if (cta_aborting(S)) return;
+    if ((it & 15u) == 15u && *reinterpret_cast<volatile int*>(P.abort_flag) != 0) {
+      *reinterpret_cast<volatile int*>(S.sabort) = 1;
+      return;
+    }
+    if (globaltimer() - t0 > kTimeoutNs) {
+      raise_abort(P, S);
+      return;
+    }
+  }
+}
+static_assert(sizeof(AttnSmemB) + (kMaxGroup + 2) * kHeadDim * 2 <= kXBytes + kDStages * kDSlot,
               "attention aliases the tile rings");
 
-// Sum over the K splits of a partial value, in split order, with every
-// split's load issued before the first add (one L2 round trip, not nsplit).
-constexpr int kMaxSplits = 16;
-__device__ __forceinline__ float split_sum(const float* p, size_t stride, int nsplit) {
-  float v[kMaxSplits];
-#pragma unroll
-  for (int k = 0; k < kMaxSplits; ++k) v[k] = k < nsplit ? __ldcg(p + k * stride) : 0.0f;
-  float s = v[0];
-#pragma unroll
-  for (int k = 1; k < kMaxSplits; ++k)
-    if (k < nsplit) s += v[k];
-  return s;
-}
-__device__ __forceinline__ float4 split_sum4(const float4* p, size_t stride, int nsplit) {
-  float4 v[kMaxSplits];
-#pragma unroll
-  for (int k = 0; k < kMaxSplits; ++k) v[k] = k < nsplit ? __ldcg(p + k * stride) : make_float4(0.f, 0.f, 0.f, 0.f);
-  float4 s = v[0];
-#pragma unroll
-  for (int k = 1; k < kMaxSplits; ++k)
-    if (k < nsplit) {
-      s.x += v[k].x;
-      s.y += v[k].y;
-      s.z += v[k].z;
-      s.w += v[k].w;
-    }
-  return s;
+// fp32 add into the L2-resident accumulator of a split-K stage (the splits
+// of a tile meet there; the reduction phase reads the sums and zeroes them).
+__device__ __forceinline__ void red_add_v4(float* p, float4 v) {  // p 16-byte aligned
+  asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
 }
 
 // q|k|v rows of one attention item, staged in shared memory before the item
-// runs: value = fp16(sum over the QKV splits (in order) + bias), the W4A16
-// GEMM's bias epilogue.  The item's loader reads them back by row index.
+// runs: value = fp16(sum of the QKV splits + bias), the W4A16 GEMM's bias
+// epilogue.  The item's loader reads them back by row index.
 struct StagedQkv {
   const __half* vals;  // [(G + 2) * 128]: the G query heads of the KV head, then its k and v rows
   int q0, k0, v0, G;   // row indices where the three runs start; heads per KV head
@@ -279,9 +322,8 @@ struct Cursor {
 
 // ---- warp 0 lane 0: weight blocks run up to wslots steps ahead; the
 // activation tiles of a stage wait for the barrier that publishes them.
-__device__ void producer(const Params& P, const Smem& S, const Unit (&U)[ST_N], const Bars& bars,
-                         unsigned long long bbase) {
-  const int R = P.wslots, L = P.n_layers, G = gridDim.x;
+__device__ void producer(const Params& P, const Smem& S, const Unit (&U)[ST_N], const Bars& bars) {
+  const int R = P.wslots, L = P.n_layers;
   const uint32_t xbytes = static_cast<uint32_t>(P.nt) * 128u;
   Cursor wc, xc;
   wc.skip(U, L);
@@ -293,7 +335,7 @@ __device__ void producer(const Params& P, const Smem& S, const Unit (&U)[ST_N], 
   while (wc.l < L || xc.l < L) {
     bool progress = false;
     if (wc.l < L) {
-      if (mbar_try(&S.emptyw[wp.slot], wp.phase ^ 1u)) {
+      if (mbar_test(&S.emptyw[wp.slot], wp.phase ^ 1u)) {
         const unsigned char* src =
             stage_blocks(P.layers[wc.l], wc.s) +
             (static_cast<size_t>(U[wc.s].tile) * P.ksteps[wc.s] + wc.k) * kBlockBytes;
@@ -308,18 +350,17 @@ __device__ void producer(const Params& P, const Smem& S, const Unit (&U)[ST_N], 
     if (xc.l < L) {
       const int g = bars.gate(xc.l, xc.s);
       if (g > seen) {
-        const unsigned long long cnt = ld_acquire_u64(P.bar);
-        const int done_bars = static_cast<int>((cnt - bbase) / static_cast<unsigned long long>(G));
-        if (done_bars - 1 > seen) {
-          seen = done_bars - 1;
+        const int now = ld_acquire_cta(S.sseen);
+        if (now > seen) {
+          seen = now;
           // the generic-proxy writes published by the barrier -> the TMA reads below
           asm volatile("fence.proxy.async.global;" ::: "memory");
         }
       }
-      if (g <= seen && mbar_try(&S.emptyx[xp.slot], xp.phase ^ 1u)) {
+      if (g <= seen && mbar_test(&S.emptyx[xp.slot], xp.phase ^ 1u)) {
         mbar_expect_tx(&S.fullx[xp.slot], xbytes);
-        tma_load_2d(S.xs + static_cast<size_t>(xp.slot) * kXSlot, &P.tx[xc.s], xc.k * kBK, 0, &S.fullx[xp.slot]);
-        xp.next(kXStages);
+        tma_load_2d(S.xs + static_cast<size_t>(xp.slot) * P.xslot, &P.tx[xc.s], xc.k * kBK, 0, &S.fullx[xp.slot]);
+        xp.next(P.xstages);
         ++nx;
         xc.next(U, L);
         progress = true;
@@ -328,9 +369,10 @@ __device__ void producer(const Params& P, const Smem& S, const Unit (&U)[ST_N], 
     if (progress) {
       t0 = globaltimer();
     } else {
-      if (aborted(P)) break;
+      __nanosleep(kIdleNs);  // leave the issue slots to the dequantising warps of this sub-partition
+      if (cta_aborting(S)) break;
       if (globaltimer() - t0 > kTimeoutNs) {
-        raise_abort(P);
+        raise_abort(P, S);
         break;
       }
     }
@@ -341,9 +383,9 @@ __device__ void producer(const Params& P, const Smem& S, const Unit (&U)[ST_N], 
     while (!mbar_try(&S.fullw[n % R], static_cast<uint32_t>(n / R) & 1u))
       if (globaltimer() - t1 > kTimeoutNs) break;
   }
-  for (int n = max(0, nx - kXStages); n < nx; ++n) {
+  for (int n = max(0, nx - P.xstages); n < nx; ++n) {
     const uint64_t t1 = globaltimer();
-    while (!mbar_try(&S.fullx[n % kXStages], static_cast<uint32_t>(n / kXStages) & 1u))
+    while (!mbar_try(&S.fullx[n % P.xstages], static_cast<uint32_t>(n / P.xstages) & 1u))
       if (globaltimer() - t1 > kTimeoutNs) break;
   }
 }
@@ -360,26 +402,26 @@ __device__ void mma_issuer(const Params& P, const Smem& S, const Unit (&U)[ST_N]
       const Unit& u = U[s];
       if (!u.valid) continue;
       // the epilogue has drained this accumulator's previous unit
-      if (!mwait(P, &S.acce[buf], (uses[buf] & 1u) ^ 1u)) {
+      if (!mwait(P, S, &S.acce[buf], (uses[buf] & 1u) ^ 1u)) {
         ok = false;
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint32_t acc = tmem + static_cast<uint32_t>(buf * kMaxNt);
       for (int k = u.k0; k < u.k1; ++k) {
-        if (!mwait(P, &S.fullx[xp.slot], xp.phase) || !mwait(P, &S.deq[dp.slot], dp.phase)) {
+        if (!mwait(P, S, &S.fullx[xp.slot], xp.phase) || !mwait(P, S, &S.deq[dp.slot], dp.phase)) {
           ok = false;
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint64_t xd = sw128_desc(smem_u32(S.xs + static_cast<size_t>(xp.slot) * kXSlot));
+        const uint64_t xd = sw128_desc(smem_u32(S.xs + static_cast<size_t>(xp.slot) * P.xslot));
         const uint64_t wdd = sw128_desc(smem_u32(S.wd + static_cast<size_t>(dp.slot) * kDSlot));
 #pragma unroll
         for (int j = 0; j < kBK / 16; ++j)  // K = 16 per MMA: 32 bytes further into the swizzle atom
           mma_f16(acc, wdd + 2 * j, xd + 2 * j, idesc, (k > u.k0 || j > 0) ? 1u : 0u);
         mma_commit(&S.emptyx[xp.slot]);
         mma_commit(&S.emptyd[dp.slot]);
-        xp.next(kXStages);
+        xp.next(P.xstages);
         dp.next(kDStages);
       }
       if (!ok) break;
@@ -395,33 +437,79 @@ __device__ void mma_issuer(const Params& P, const Smem& S, const Unit (&U)[ST_N]
     if (globaltimer() - t1 > kTimeoutNs) break;
 }
 
+// ---- dequantisation (warps 2-9): thread d takes half d >> 7 (32 elements) of
+// weight row d & 127 of every K step of the CTA's units, in unit order.
+struct Dequant {
+  const Params& P;
+  const Smem& S;
+  int r, h;  // weight row in the tile, half of the K step
+  RingPos wp, dp;
+  bool dead = false;  // warp-uniform: a wait of this warp gave up (the launch is aborting)
+
+  __device__ Dequant(const Params& P_, const Smem& S_, int d) : P(P_), S(S_), r(d & (kRows - 1)), h(d >> 7) {}
+
+  __device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t parity) {
+    const bool ok = !dead && mwait(P, S, bar, parity);
+    dead = !__all_sync(0xffffffffu, ok);
+    return !dead;
+  }
+  __device__ void unit(const Unit& u) {
+    if (!u.valid || dead) return;
+    const int sw = r & 7, hs = q4t::half_swap(r), c0 = 4 * h;
+    for (int k = u.k0; k < u.k1; ++k) {
+      if (!wait_all(&S.fullw[wp.slot], wp.phase)) return;
+      const unsigned char* blk = S.wr + static_cast<size_t>(wp.slot) * kBlockBytes;
+      const uint4 g = *reinterpret_cast<const uint4*>(blk + 32 * r + 16 * (h ^ hs));
+      const uint32_t sc = *reinterpret_cast<const uint32_t*>(blk + q4t::kPackedBytes + 4 * r);
+      mbar_arrive(&S.emptyw[wp.slot]);
+      wp.next(P.wslots);
+      if (!wait_all(&S.emptyd[dp.slot], dp.phase ^ 1u)) return;  // the MMAs are done with this tile
+      const __half2 sc2 = *reinterpret_cast<const __half2*>(&sc);
+      const __half2 s2 = h ? __high2half2(sc2) : __low2half2(sc2);
+      unsigned char* row = S.wd + static_cast<size_t>(dp.slot) * kDSlot + r * 128;
+      *reinterpret_cast<uint4*>(row + (((c0 + 0) ^ sw) << 4)) = q4t::dequant8(g.x, s2);
+      *reinterpret_cast<uint4*>(row + (((c0 + 1) ^ sw) << 4)) = q4t::dequant8(g.y, s2);
+      *reinterpret_cast<uint4*>(row + (((c0 + 2) ^ sw) << 4)) = q4t::dequant8(g.z, s2);
+      *reinterpret_cast<uint4*>(row + (((c0 + 3) ^ sw) << 4)) = q4t::dequant8(g.w, s2);
+      // generic-proxy shared-memory writes -> visible to the tensor core
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive(&S.deq[dp.slot]);
+      dp.next(kDStages);
+    }
+  }
+};
+
+// Warps 6-9: the second halves of every K step.  The attention phase of the
+// workers uses the dequantisation ring's shared memory, so these warps start
+// on a layer's o projection only after that layer's attention.
+__device__ void dequant_helper(const Params& P, const Smem& S, const Unit (&U)[ST_N]) {
+  Dequant dq(P, S, threadIdx.x - 64);
+  for (int l = 0; l < P.n_layers && !dq.dead; ++l) {
+    for (int s = 0; s < ST_N && !dq.dead; ++s) {
+      if (s == ST_O) dq.wait_all(S.attn_done, static_cast<uint32_t>(l) & 1u);
+      dq.unit(U[s]);
+    }
+  }
+}
+
 // ---- warps 2-5 --------------------------------------------------------------
 struct Workers {
   const Params& P;
   const Smem& S;
   const Unit (&U)[ST_N];
   uint32_t tmem;
-  unsigned long long bbase;
   int t, warp, lane, c, G;
-  RingPos wp, dp;
+  Dequant dq;
   uint32_t uses[2] = {0u, 0u};
   int buf = 0;
-  bool dead = false;  // warp-uniform: a wait of this warp gave up (the launch is aborting)
 
-  __device__ Workers(const Params& P_, const Smem& S_, const Unit (&U_)[ST_N], uint32_t tmem_,
-                     unsigned long long bbase_)
-      : P(P_), S(S_), U(U_), tmem(tmem_), bbase(bbase_) {
+  __device__ Workers(const Params& P_, const Smem& S_, const Unit (&U_)[ST_N], uint32_t tmem_)
+      : P(P_), S(S_), U(U_), tmem(tmem_), dq(P_, S_, threadIdx.x - 64) {
     t = threadIdx.x - 64;
     warp = threadIdx.x >> 5;
     lane = threadIdx.x & 31;
     c = blockIdx.x;
     G = gridDim.x;
-  }
-
-  __device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t parity) {
-    const bool ok = !dead && mwait(P, bar, parity);
-    dead = !__all_sync(0xffffffffu, ok);
-    return !dead;
   }
 
   // This CTA's outputs of the stage ending at barrier k are written: count
@@ -430,19 +518,18 @@ struct Workers {
   __device__ void arrive(int k) {
     asm volatile("fence.proxy.async.global;" ::: "memory");
     workers_sync();
-    if (t == 0 && P.trace) P.trace[(static_cast<size_t>(c) * P.n_bars + k) * 2] = globaltimer();
+    if (t == 0 && P.trace) P.trace[(static_cast<size_t>(c) * P.n_bars + k) * 4] = globaltimer();
     if (t == 0) {
-      if (k > 0) counter_wait(P, bbase + static_cast<unsigned long long>(k) * G);
-      __threadfence();
-      red_release_add(P.bar, 1ull);
+      if (k > 0) bar_wait(P, S, k - 1);
+      red_release_add(P.bar, 1ull);  // release: the workers' writes, ordered before it by the named barrier
     }
   }
   // Wait for barrier k; true when the launch is aborting (same answer in every worker).
   __device__ bool wait(int k) {
     if (t == 0) {
-      const bool ok = counter_wait(P, bbase + static_cast<unsigned long long>(k + 1) * G);
-      *S.stop = (!ok || aborted(P)) ? 1 : 0;
-      if (P.trace) P.trace[(static_cast<size_t>(c) * P.n_bars + k) * 2 + 1] = globaltimer();
+      const bool ok = bar_wait(P, S, k);
+      *S.stop = (!ok || cta_aborting(S)) ? 1 : 0;
+      if (P.trace) P.trace[(static_cast<size_t>(c) * P.n_bars + k) * 4 + 1] = globaltimer();
     }
     workers_sync();
     const bool stop = *reinterpret_cast<volatile int*>(S.stop) != 0;
@@ -450,60 +537,61 @@ struct Workers {
     return stop;
   }
 
-  // Dequantise the unit's weight blocks and write its epilogue.
-  __device__ void gemm_unit(int s) {
+  // Dequantise the first halves of the unit's weight blocks and write its
+  // epilogue: the accumulator tile goes through shared memory (the idle
+  // activation ring) so that each lane then adds four consecutive rows of a
+  // token at once into the split-K accumulator (vector atomics: a quarter of
+  // the L2 atomic operations), or writes eight SwiGLU outputs at once.
+  __device__ void gemm_unit(int s, int k_end) {
     const Unit& u = U[s];
-    if (!u.valid || dead) return;
-    const int R = P.wslots, sw = t & 7, hs = q4t::half_swap(t);
-    for (int k = u.k0; k < u.k1; ++k) {
-      if (!wait_all(&S.fullw[wp.slot], wp.phase)) return;
-      const unsigned char* blk = S.wr + static_cast<size_t>(wp.slot) * kBlockBytes;
-      const uint4 g0 = *reinterpret_cast<const uint4*>(blk + 32 * t + 16 * hs);
-      const uint4 g1 = *reinterpret_cast<const uint4*>(blk + 32 * t + 16 * (hs ^ 1));
-      const uint32_t sc = *reinterpret_cast<const uint32_t*>(blk + q4t::kPackedBytes + 4 * t);
-      mbar_arrive(&S.emptyw[wp.slot]);
-      wp.next(R);
-      if (!wait_all(&S.emptyd[dp.slot], dp.phase ^ 1u)) return;  // the MMAs are done with this tile
-      const __half2 sc2 = *reinterpret_cast<const __half2*>(&sc);
-      const __half2 s0 = __low2half2(sc2), s1 = __high2half2(sc2);
-      unsigned char* row = S.wd + static_cast<size_t>(dp.slot) * kDSlot + t * 128;
-      *reinterpret_cast<uint4*>(row + ((0 ^ sw) << 4)) = q4t::dequant8(g0.x, s0);
-      *reinterpret_cast<uint4*>(row + ((1 ^ sw) << 4)) = q4t::dequant8(g0.y, s0);
-      *reinterpret_cast<uint4*>(row + ((2 ^ sw) << 4)) = q4t::dequant8(g0.z, s0);
-      *reinterpret_cast<uint4*>(row + ((3 ^ sw) << 4)) = q4t::dequant8(g0.w, s0);
-      *reinterpret_cast<uint4*>(row + ((4 ^ sw) << 4)) = q4t::dequant8(g1.x, s1);
-      *reinterpret_cast<uint4*>(row + ((5 ^ sw) << 4)) = q4t::dequant8(g1.y, s1);
-      *reinterpret_cast<uint4*>(row + ((6 ^ sw) << 4)) = q4t::dequant8(g1.z, s1);
-      *reinterpret_cast<uint4*>(row + ((7 ^ sw) << 4)) = q4t::dequant8(g1.w, s1);
-      // generic-proxy shared-memory writes -> visible to the tensor core
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_arrive(&S.deq[dp.slot]);
-      dp.next(kDStages);
-    }
+    if (!u.valid || dq.dead) return;
+    dq.unit(u);
+    if (dq.dead) return;
+    if (t == 0 && P.trace) P.trace[(static_cast<size_t>(c) * P.n_bars + k_end) * 4 + 2] = globaltimer();
     // epilogue: warp w reads TMEM lanes 32 (w % 4) .. = weight rows of the tile
-    if (!wait_all(&S.accf[buf], uses[buf] & 1u)) return;
+    if (!dq.wait_all(&S.accf[buf], uses[buf] & 1u)) return;
+    if (t == 0 && P.trace) P.trace[(static_cast<size_t>(c) * P.n_bars + k_end) * 4 + 3] = globaltimer();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const int q = warp & 3, row = 32 * q + lane;
-    const int n0 = u.tile * kRows;
+    const int q = warp & 3;
+    const int n0 = u.tile * kRows + 32 * q;  // this warp's first weight row
     const uint32_t tl = tmem + static_cast<uint32_t>(buf * kMaxNt) + (static_cast<uint32_t>(32 * q) << 16);
     const int rows = P.tiles[s] * kRows;
+    float* T = reinterpret_cast<float*>(S.xs) + q * (kMaxNt * kTPitch);  // [token][row of the warp]
     for (int c0 = 0; c0 < P.nt; c0 += 32) {
       uint32_t r[32];
       tmem_ld32(tl + c0, r);
-      if (s == ST_GU) {  // gate row in the even lane, its up row in the next
-        __half* dst = P.a + (n0 + row) / 2;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float up = __shfl_down_sync(0xffffffffu, __uint_as_float(r[j]), 1);
-          if ((lane & 1) == 0 && c0 + j < P.B)
-            dst[static_cast<size_t>(c0 + j) * P.inter] = swiglu_value(__uint_as_float(r[j]), up);
+      for (int j = 0; j < 32; ++j) T[j * kTPitch + lane] = __uint_as_float(r[j]);
+      __syncwarp();
+      if (s == ST_GU) {
+        // lane: token (lane >> 1) + 16 it, pairs 8 (lane & 1) .. + 7 (gate row 2p, up row 2p + 1)
+#pragma unroll
+        for (int it = 0; it < 2; ++it) {
+          const int jj = (lane >> 1) + 16 * it, hh = lane & 1, tok = c0 + jj;
+          const float4* src = reinterpret_cast<const float4*>(T + jj * kTPitch + 16 * hh);
+          uint32_t o[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float4 v = src[i];
+            const __half2 hv = __halves2half2(swiglu_value(v.x, v.y), swiglu_value(v.z, v.w));
+            o[i] = *reinterpret_cast<const uint32_t*>(&hv);
+          }
+          if (tok < P.B)
+            *reinterpret_cast<uint4*>(P.a + static_cast<size_t>(tok) * P.inter + n0 / 2 + 8 * hh) =
+                make_uint4(o[0], o[1], o[2], o[3]);
         }
       } else {
-        float* dst = P.part[s] + static_cast<size_t>(u.split) * P.B * rows + n0 + row;
+        // lane: rows 4 (lane & 7) .. + 3 of token (lane >> 3) + 4 it
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (c0 + j < P.B) dst[static_cast<size_t>(c0 + j) * rows] = __uint_as_float(r[j]);
+        for (int it = 0; it < 8; ++it) {
+          const int jj = (lane >> 3) + 4 * it, tok = c0 + jj;
+          if (tok < P.B) {
+            const float4 v = *reinterpret_cast<const float4*>(T + jj * kTPitch + 4 * (lane & 7));
+            red_add_v4(P.part[s] + static_cast<size_t>(tok) * rows + n0 + 4 * (lane & 7), v);
+          }
+        }
       }
+      __syncwarp();  // T is read before the next chunk overwrites it
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     mbar_arrive(&S.acce[buf]);
@@ -511,32 +599,48 @@ struct Workers {
     buf ^= 1;
   }
 
-  // Sequence c (a CTA per sequence): x += fp16(sum of the stage's partials)
-  // (the residual epilogue, runners/engine.py:215-221, 237-243), then
-  // xn = RMSNorm(x) * gamma (rms_norm.metal:14-40) when gamma is given.
-  // s < 0: no partials (the norm of the embedded input).
-  __device__ void reduce_rows(int s, const __half* gamma) {
+  // Sequence c (a CTA per sequence): x += fp16(the stage's accumulated sum)
+  // (the residual epilogue, runners/engine.py:215-221, 237-243), the
+  // accumulator row zeroed for its next use, then xn = RMSNorm(x) * gamma
+  // (rms_norm.metal:14-40) when gamma is given.  s < 0: no sum (the norm of
+  // the embedded input).  zero_qkv: also zero the q|k|v accumulator row
+  // (its readers, the attention items, are done).
+  __device__ void reduce_rows(int s, const __half* gamma, bool zero_qkv) {
     if (c >= P.B) return;
+    constexpr int kMaxPer = 4;              // hidden <= 2048
     const int H = P.hidden, per = H / 512;  // 4-element groups per thread
-    const int ns = s >= 0 ? P.splits[s] : 0;
     __half* xr = P.x + static_cast<size_t>(c) * H;
-    uint2 xv[8];
-    float ss = 0.0f;
-    for (int i = 0; i < per; ++i) {
+    float4* pr = s >= 0 ? reinterpret_cast<float4*>(P.part[s] + static_cast<size_t>(c) * H) : nullptr;
+    // every load first (one L2 round trip), then the stores
+    uint2 xv[kMaxPer], gv[kMaxPer];
+    float4 acc[kMaxPer];
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      if (i >= per) break;
       const int g = t + kWorkers * i;
-      uint2 xo = __ldcg(reinterpret_cast<const uint2*>(xr) + g);
-      if (ns > 0) {
-        const float4* pp = reinterpret_cast<const float4*>(P.part[s] + static_cast<size_t>(c) * H) + g;
-        const float4 acc = split_sum4(pp, static_cast<size_t>(P.B) * H / 4, ns);
-        __half2* h = reinterpret_cast<__half2*>(&xo);
-        h[0] = __halves2half2(__hadd(__low2half(h[0]), __float2half_rn(acc.x)),
-                              __hadd(__high2half(h[0]), __float2half_rn(acc.y)));
-        h[1] = __halves2half2(__hadd(__low2half(h[1]), __float2half_rn(acc.z)),
-                              __hadd(__high2half(h[1]), __float2half_rn(acc.w)));
-        reinterpret_cast<uint2*>(xr)[g] = xo;
+      xv[i] = __ldcg(reinterpret_cast<const uint2*>(xr) + g);
+      acc[i] = pr ? __ldcg(pr + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+      gv[i] = gamma ? __ldg(reinterpret_cast<const uint2*>(gamma) + g) : make_uint2(0u, 0u);
+    }
+    if (zero_qkv) {
+      float4* q = reinterpret_cast<float4*>(P.part[ST_QKV] + static_cast<size_t>(c) * P.qkv_rows);
+      for (int i = t; i < P.qkv_rows / 4; i += kWorkers) q[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      if (i >= per) break;
+      const int g = t + kWorkers * i;
+      if (pr) {
+        pr[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+        __half2* h = reinterpret_cast<__half2*>(&xv[i]);
+        h[0] = __halves2half2(__hadd(__low2half(h[0]), __float2half_rn(acc[i].x)),
+                              __hadd(__high2half(h[0]), __float2half_rn(acc[i].y)));
+        h[1] = __halves2half2(__hadd(__low2half(h[1]), __float2half_rn(acc[i].z)),
+                              __hadd(__high2half(h[1]), __float2half_rn(acc[i].w)));
+        reinterpret_cast<uint2*>(xr)[g] = xv[i];
       }
-      xv[i] = xo;
-      const __half* h = reinterpret_cast<const __half*>(&xo);
+      const __half* h = reinterpret_cast<const __half*>(&xv[i]);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float v = __half2float(h[e]);
@@ -551,11 +655,12 @@ struct Workers {
     workers_sync();  // S.red is read before its next use
     const float scale = 1.0f / sqrtf(ss / static_cast<float>(H) + P.eps);
     __half* xnr = P.xn + static_cast<size_t>(c) * H;
-    for (int i = 0; i < per; ++i) {
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      if (i >= per) break;
       const int g = t + kWorkers * i;
-      const uint2 gv = __ldg(reinterpret_cast<const uint2*>(gamma) + g);
       const __half* h = reinterpret_cast<const __half*>(&xv[i]);
-      const __half* gh = reinterpret_cast<const __half*>(&gv);
+      const __half* gh = reinterpret_cast<const __half*>(&gv[i]);
       __half o[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -596,30 +701,42 @@ struct Workers {
     const AttnParams A = attn_params(l);
     const __half* bias = reinterpret_cast<const __half*>(P.layers[l].qkv_bias);
     const int Gq = P.n_q / P.n_kv, q_dim = P.n_q * kHeadDim, kv_dim = P.n_kv * kHeadDim;
-    const size_t stride = static_cast<size_t>(P.B) * P.qkv_rows;
-    const int nsplit = P.splits[ST_QKV];
-    AttnSmem& AS = *reinterpret_cast<AttnSmem*>(S.xs);
-    __half* staged = reinterpret_cast<__half*>(S.xs + sizeof(AttnSmem));
+    AttnSmemB& AS = *reinterpret_cast<AttnSmemB*>(S.xs);
+    __half* staged = reinterpret_cast<__half*>(S.xs + sizeof(AttnSmemB));
     const int items = P.B * P.n_kv * P.att_splits;
     for (int it = c; it < items; it += G) {
       const int split = it % P.att_splits, kvh = (it / P.att_splits) % P.n_kv;
       const int b = it / (P.att_splits * P.n_kv);
-      // the item's q heads, k and v rows: (Gq + 2) * 128 values, two per thread per round
+      // the item's q heads, k and v rows: (Gq + 2) * 128 <= 1280 values, two
+      // per thread per round, every round's loads issued before the stores
+      constexpr int kRounds = (kMaxGroup + 2) * kHeadDim / (2 * kWorkers);
       const int n = (Gq + 2) * kHeadDim;
       const float* row = P.part[ST_QKV] + static_cast<size_t>(b) * P.qkv_rows;
-      for (int j0 = 2 * t; j0 < n; j0 += 2 * kWorkers) {
-        const int r = j0 / kHeadDim, d = j0 - r * kHeadDim;
-        const int src = r < Gq ? (kvh * Gq + r) * kHeadDim + d
-                               : (r == Gq ? q_dim + kvh * kHeadDim + d : q_dim + kv_dim + kvh * kHeadDim + d);
-        const float s0 = split_sum(row + src, stride, nsplit), s1 = split_sum(row + src + 1, stride, nsplit);
-        staged[j0] = __float2half_rn(s0 + __half2float(__ldg(bias + src)));
-        staged[j0 + 1] = __float2half_rn(s1 + __half2float(__ldg(bias + src + 1)));
+      float2 v[kRounds];
+      __half2 bv[kRounds];
+#pragma unroll
+      for (int r = 0; r < kRounds; ++r) {
+        const int j0 = 2 * t + 2 * kWorkers * r;
+        if (j0 >= n) break;
+        const int hr = j0 / kHeadDim, d = j0 - hr * kHeadDim;
+        const int src = hr < Gq ? (kvh * Gq + hr) * kHeadDim + d
+                                : (hr == Gq ? q_dim + kvh * kHeadDim + d : q_dim + kv_dim + kvh * kHeadDim + d);
+        v[r] = __ldcg(reinterpret_cast<const float2*>(row + src));
+        bv[r] = __ldg(reinterpret_cast<const __half2*>(bias + src));
+      }
+#pragma unroll
+      for (int r = 0; r < kRounds; ++r) {
+        const int j0 = 2 * t + 2 * kWorkers * r;
+        if (j0 >= n) break;
+        staged[j0] = __float2half_rn(v[r].x + __half2float(__low2half(bv[r])));
+        staged[j0 + 1] = __float2half_rn(v[r].y + __half2float(__high2half(bv[r])));
       }
       workers_sync();
       const StagedQkv ld{staged, (kvh * Gq) * kHeadDim, q_dim + kvh * kHeadDim, q_dim + kv_dim + kvh * kHeadDim, Gq};
-      attn_item(A, AS, split, kvh, b, t, true, ld, WorkerSync{});
+      attn_item<kAttnStagesB>(A, AS, split, kvh, b, t, true, ld, WorkerSync{});
       workers_sync();  // the item's shared memory is read before the next item stages into it
     }
+    mbar_arrive(S.attn_done);  // the dequantisation ring's memory is free again
   }
   __device__ void merge(int l) {
     const AttnParams A = attn_params(l);
@@ -629,12 +746,12 @@ struct Workers {
   __device__ void run() {
     const int L = P.n_layers;
     const Bars bars{7 + (P.att_splits > 1 ? 1 : 0), P.att_splits > 1 ? 1 : 0};
-    reduce_rows(-1, reinterpret_cast<const __half*>(P.layers[0].in_norm));
+    reduce_rows(-1, reinterpret_cast<const __half*>(P.layers[0].in_norm), false);
     arrive(0);
     for (int l = 0; l < L; ++l) {
       const lmps_batched_layer& Ly = P.layers[l];
       const int b0 = bars.first(l);
-      gemm_unit(ST_QKV);
+      gemm_unit(ST_QKV, b0);
       arrive(b0);
       if (wait(b0)) return;
       attention(l);
@@ -645,17 +762,17 @@ struct Workers {
         arrive(b0 + 2);
       }
       const int bo = bars.after(l, ST_O);
-      gemm_unit(ST_O);
+      gemm_unit(ST_O, bo);
       arrive(bo);
       if (wait(bo)) return;
-      reduce_rows(ST_O, reinterpret_cast<const __half*>(Ly.post_norm));
+      reduce_rows(ST_O, reinterpret_cast<const __half*>(Ly.post_norm), true);
       arrive(bo + 1);
-      gemm_unit(ST_GU);
+      gemm_unit(ST_GU, bo + 2);
       arrive(bo + 2);
-      gemm_unit(ST_DN);
+      gemm_unit(ST_DN, bo + 3);
       arrive(bo + 3);
       if (wait(bo + 3)) return;
-      reduce_rows(ST_DN, l + 1 < L ? reinterpret_cast<const __half*>(P.layers[l + 1].in_norm) : nullptr);
+      reduce_rows(ST_DN, l + 1 < L ? reinterpret_cast<const __half*>(P.layers[l + 1].in_norm) : nullptr, false);
       arrive(bo + 4);
     }
   }
@@ -668,21 +785,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_batched_kernel(const __gri
   const int R = P.wslots;
   Smem S;
   S.xs = base;
-  S.wd = S.xs + kXStages * kXSlot;
+  S.wd = S.xs + kXBytes;
   S.wr = S.wd + kDStages * kDSlot;
   S.fullw = reinterpret_cast<uint64_t*>(S.wr + static_cast<size_t>(R) * kBlockBytes);
   S.emptyw = S.fullw + R;
   S.fullx = S.emptyw + R;
-  S.emptyx = S.fullx + kXStages;
-  S.deq = S.emptyx + kXStages;
+  S.emptyx = S.fullx + kMaxXStages;
+  S.deq = S.emptyx + kMaxXStages;
   S.emptyd = S.deq + kDStages;
   S.accf = S.emptyd + kDStages;
   S.acce = S.accf + 2;
   S.done = S.acce + 2;
-  S.base = reinterpret_cast<unsigned long long*>(S.done + 1);
+  S.attn_done = S.done + 1;
+  S.base = reinterpret_cast<unsigned long long*>(S.attn_done + 1);
   S.tmem_slot = reinterpret_cast<uint32_t*>(S.base + 1);
   S.stop = reinterpret_cast<int*>(S.tmem_slot + 1);
-  S.red = reinterpret_cast<float*>(S.stop + 1);
+  S.sabort = S.stop + 1;
+  S.sseen = S.sabort + 1;
+  S.red = reinterpret_cast<float*>(S.sseen + 1);
   const int tid = threadIdx.x, warp = tid >> 5;
 
   // Every position must lie inside the cache: all CTAs read the same values
@@ -697,14 +817,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_batched_kernel(const __gri
   if (tid == 0) {
     for (int i = 0; i < R; ++i) {
       mbar_init(&S.fullw[i], 1);
-      mbar_init(&S.emptyw[i], kWorkers);
+      mbar_init(&S.emptyw[i], kDequant);
     }
-    for (int i = 0; i < kXStages; ++i) {
+    for (int i = 0; i < P.xstages; ++i) {
       mbar_init(&S.fullx[i], 1);
       mbar_init(&S.emptyx[i], 1);
     }
     for (int i = 0; i < kDStages; ++i) {
-      mbar_init(&S.deq[i], kWorkers);
+      mbar_init(&S.deq[i], kDequant);
       mbar_init(&S.emptyd[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -712,12 +832,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_batched_kernel(const __gri
       mbar_init(&S.acce[i], kWorkers);
     }
     mbar_init(S.done, 1);
+    mbar_init(S.attn_done, kWorkers);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     // This CTA has not arrived at the launch's first barrier, so the count is
     // below the next multiple of the grid size.
     const unsigned long long cnt = ld_acquire_u64(P.bar);
     *S.base = cnt - cnt % gridDim.x;
     *S.stop = 0;
+    *S.sabort = 0;
+    *S.sseen = -1;
   }
   if (tid == 32) {
 #pragma unroll
@@ -742,11 +865,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_batched_kernel(const __gri
   const Bars bars{7 + merge, merge};
 
   if (warp == 0) {
-    if (tid == 0) producer(P, S, U, bars, bbase);
+    if (tid == 0) producer(P, S, U, bars);
   } else if (warp == 1) {
     if (tid == 32) mma_issuer(P, S, U, tmem);
+  } else if (warp == 10) {
+    if (tid == kWatcherTid) watcher(P, S, bbase);
+  } else if (warp >= 6) {
+    dequant_helper(P, S, U);
   } else {
-    Workers w(P, S, U, tmem, bbase);
+    Workers w(P, S, U, tmem);
     w.run();
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -815,14 +942,15 @@ static bool geometry(const lmps_batched_desc& m, int B, int max_seq_len, int G, 
     if (g.tiles[s] > G) return false;
     int sp = G / g.tiles[s];
     if (sp > g.ksteps[s]) sp = g.ksteps[s];
-    if (sp > kMaxSplits) sp = kMaxSplits;
     if (s == ST_GU || sp < 1) sp = 1;
     g.splits[s] = sp;
   }
-  const int ptiles = (max_seq_len + kAttnTile - 1) / kAttnTile;
+  // attention: split a (sequence, KV head) over CTAs only in chunks of at
+  // least 512 positions (below that the merge phase costs more than it saves)
   int S = G / (B * m.n_kv_heads);
+  const int by_len = (max_seq_len + kAttnMinChunk - 1) / kAttnMinChunk;
+  if (S > by_len) S = by_len;
   if (S < 1) S = 1;
-  if (S > ptiles) S = ptiles;
   g.att_chunk = attn_chunk(max_seq_len, S);
   g.att_splits = (max_seq_len + g.att_chunk - 1) / g.att_chunk;
   return true;
@@ -835,16 +963,19 @@ static size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255);
 static WsLayout ws_layout(const lmps_batched_desc& m, int B, const Geometry& g) {
   const size_t qkv_rows = static_cast<size_t>(m.n_q_heads + 2 * m.n_kv_heads) * m.head_dim;
   const size_t q_dim = static_cast<size_t>(m.n_q_heads) * m.head_dim;
+  const size_t T = kMaxNt;  // token rows of the fixed part: the same offsets for every batch size
   WsLayout w{};
   size_t off = 256;  // [0, 8): grid-barrier counter, [8, 12): abort flag
-  w.xn = off; off = align256(off + 2 * static_cast<size_t>(B) * m.hidden);
-  w.attn = off; off = align256(off + 2 * static_cast<size_t>(B) * q_dim);
-  w.a = off; off = align256(off + 2 * static_cast<size_t>(B) * m.intermediate);
+  // split-K accumulators first: they must be zero when a launch starts, and
+  // every launch leaves the rows it used zeroed, whatever its batch size
   const size_t prow[ST_N] = {qkv_rows, static_cast<size_t>(m.hidden), 0, static_cast<size_t>(m.hidden)};
   for (int s = 0; s < ST_N; ++s) {
     w.part[s] = off;
-    off = align256(off + 4 * static_cast<size_t>(g.splits[s]) * B * prow[s]);
+    off = align256(off + 4 * T * prow[s]);
   }
+  w.xn = off; off = align256(off + 2 * T * m.hidden);
+  w.attn = off; off = align256(off + 2 * T * q_dim);
+  w.a = off; off = align256(off + 2 * T * m.intermediate);
   const size_t arows = static_cast<size_t>(B) * m.n_q_heads * (g.att_splits > 1 ? g.att_splits : 0);
   w.att_o = off; off = align256(off + 4 * arows * m.head_dim);
   w.att_ml = off; off = align256(off + 8 * arows);
@@ -880,7 +1011,7 @@ static int batched_check(const lmps_batched_desc* model, int batch, int max_seq_
   const lmps_batched_desc& m = *model;
   if (!m.layers || m.n_layers < 1 || m.n_kv_heads < 1 || m.n_q_heads % m.n_kv_heads) return LMPS_ERR_INVALID_ARGUMENT;
   if (batch > bd::kMaxNt || m.head_dim != kHeadDim || m.n_q_heads / m.n_kv_heads > kMaxGroup ||
-      m.hidden % 512 || m.hidden > 4096 || m.n_layers > bd::kMaxLayers)
+      m.hidden % 512 || m.hidden > 2048 || m.n_layers > bd::kMaxLayers)
     return LMPS_ERR_UNSUPPORTED;
   return LMPS_OK;
 }
@@ -891,6 +1022,14 @@ extern "C" size_t lmps_decode_batched_workspace_size(const lmps_batched_desc* mo
   const int G = bd::sm_count();
   if (G < 1 || !bd::geometry(*model, batch, max_seq_len, G, g)) return 0;
   return bd::ws_layout(*model, batch, g).total;
+}
+
+extern "C" int lmps_decode_batched_barriers(const lmps_batched_desc* model, int batch, int max_seq_len) {
+  if (batched_check(model, batch, max_seq_len) != LMPS_OK) return 0;
+  bd::Geometry g{};
+  const int G = bd::sm_count();
+  if (G < 1 || !bd::geometry(*model, batch, max_seq_len, G, g)) return 0;
+  return 1 + model->n_layers * (7 + (g.att_splits > 1 ? 1 : 0));
 }
 
 extern "C" int lmps_decode_batched(const lmps_batched_desc* model, uint16_t* x, const int32_t* pos,
@@ -966,6 +1105,9 @@ extern "C" int lmps_decode_batched(const lmps_batched_desc* model, uint16_t* x, 
   if (R > bd::kMaxWSlots) R = bd::kMaxWSlots;
   if (R < 4) return LMPS_ERR_UNSUPPORTED;
   P.wslots = R;
+  P.xslot = g.nt * 128;
+  P.xstages = bd::kXBytes / P.xslot;
+  if (P.xstages > bd::kMaxXStages) P.xstages = bd::kMaxXStages;
   const size_t smem = static_cast<size_t>(bd::kFixedSmem) + static_cast<size_t>(R) * bd::kBlockBytes;
   const int st_attr = lmps_max_dyn_smem<bd::decode_batched_kernel>(static_cast<int>(smem));
   if (st_attr != LMPS_OK) return st_attr;

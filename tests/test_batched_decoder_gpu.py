@@ -52,17 +52,12 @@ def test_tile_blocks_layout(cuda):
     assert np.array_equal(got, want.reshape(-1))
 
 
-@pytest.mark.parametrize("B", [5, 16, 64])
-def test_batched_decoder_matches_kernel_path(cuda, small_model, B):
-    """Same prompts fed token by token through both decoders, then four
-    logits steps with the same fed tokens: fp16 logits within the decode
-    tolerance of the per-stage path's (split-K partial sums are added in a
-    different order)."""
-    cfg, mw, host = small_model
-    P, N = 5, 4
-    prompts = torch.as_tensor(np.random.default_rng(B).integers(0, cfg.vocab, (B, P)), dtype=torch.int32)
-    ref = _engine(mw, max_batch=B, max_seq_len=64, decoder="kernels")
-    eng = _engine(mw, max_batch=B, max_seq_len=64, decoder="batched")
+def _compare_logits_steps(ref, eng, B, P, N, seed):
+    """Prefill the same prompts token by token on both engines, then N
+    logits steps with the same fed tokens; the batched engine's fp16 logits
+    within the decode tolerance of the reference engine's."""
+    cfg = ref.cfg
+    prompts = torch.as_tensor(np.random.default_rng(seed).integers(0, cfg.vocab, (B, P)), dtype=torch.int32)
     for e in (ref, eng):
         e.reset(B)
         e.prefill(prompts, dense=False)
@@ -80,6 +75,26 @@ def test_batched_decoder_matches_kernel_path(cuda, small_model, B):
             assert_close(b[i], a[i], what=f"B={B} step {s} sequence {i}")
         eng.tokens[:B].copy_(ref.tokens[:B])
     assert eng.pos[:B].cpu().tolist() == [P + N] * B
+
+
+@pytest.mark.parametrize("B", [5, 16, 64])
+def test_batched_decoder_matches_kernel_path(cuda, small_model, B):
+    """Same prompts and fed tokens through both decoders (the split-K sums
+    are added in a different order)."""
+    cfg, mw, host = small_model
+    ref = _engine(mw, max_batch=B, max_seq_len=64, decoder="kernels")
+    eng = _engine(mw, max_batch=B, max_seq_len=64, decoder="batched")
+    _compare_logits_steps(ref, eng, B, 5, 4, B)
+
+
+def test_batched_decoder_batch_size_changes(cuda, small_model):
+    """One engine (and workspace) driven at 16 sequences, then 5, then 16
+    again: the split-K accumulators are zero at every launch."""
+    cfg, mw, host = small_model
+    ref = _engine(mw, max_batch=16, max_seq_len=64, decoder="kernels")
+    eng = _engine(mw, max_batch=16, max_seq_len=64, decoder="batched")
+    for i, B in enumerate((16, 5, 16)):
+        _compare_logits_steps(ref, eng, B, 3, 2, 100 + i)
 
 
 def test_batched_decoder_c2_shape_matches_oracle(cuda, small_model):
@@ -107,7 +122,7 @@ def test_batched_decoder_c2_shape_matches_oracle(cuda, small_model):
 def test_batched_decoder_long_context_matches_oracle(cuda, small_model):
     """Five sequences over 700..2000 cached positions (fp16 N(0,1) rows
     written into the paged cache): the attention phase splits each
-    (sequence, KV head) over 11 CTAs and merges the splits.  Three logits
+    (sequence, KV head) over 5 CTAs and merges the splits.  Three logits
     steps against the oracle holding the same cache prefix
     (kernels/attention.metal:22-40, softmax.metal:23-36, attn_sum.metal:22-33)."""
     cfg, mw, host = small_model
