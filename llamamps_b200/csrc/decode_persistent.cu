@@ -39,6 +39,8 @@
 // (engine.py:163-181), and every CTA derives the next token from the argmax.
 #include <cmath>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "flash_decode.cuh"
 
@@ -2156,14 +2158,42 @@ static int act_bytes_for(const lmps_model_desc& m, int nb) {
   return static_cast<int>((a + 127) & ~static_cast<size_t>(127));
 }
 
+// Launch configuration of one (device, batch instantiation, model shape):
+// found once with the CUDA attribute and occupancy queries, then reused (the
+// per-token path launches once per token, and those queries cost more host
+// time than the launch).
+struct LaunchCfg {
+  int key_layers = -1, key_hidden = 0, key_inter = 0, key_qkv = 0, key_vocab = 0;
+  int sms = 0, slots = 0;
+  size_t smem = 0;
+};
+constexpr int kCfgDevices = 64;
+
 template <int NB>
 static int launch(const Params& P0, const lmps_model_desc& m, cudaStream_t st) {
+  static LaunchCfg cache[kCfgDevices];
+  static std::mutex cache_mutex;
   Params P = P0;
-  int dev = 0, sms = 0, max_smem = 0;
-  cudaGetDevice(&dev);
+  int dev = 0;
+  cudaError_t e0 = cudaGetDevice(&dev);
+  if (e0 != cudaSuccess) return static_cast<int>(e0);
+  P.act_bytes = act_bytes_for(m, NB);
+  const int qkv_rows_k = (m.n_q_heads + 2 * m.n_kv_heads) * m.head_dim;
+  if (dev >= 0 && dev < kCfgDevices) {
+    std::lock_guard<std::mutex> lock(cache_mutex);
+    const LaunchCfg& c = cache[dev];
+    if (c.key_layers == m.n_layers && c.key_hidden == m.hidden && c.key_inter == m.intermediate &&
+        c.key_qkv == qkv_rows_k && c.key_vocab == m.vocab) {
+      P.slots = c.slots;
+      void* args[] = {&P};
+      const cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<void*>(decode_persistent_kernel<NB>),
+                                                        dim3(c.sms), dim3(kThreads), args, c.smem, st);
+      return e == cudaSuccess ? LMPS_OK : static_cast<int>(e);
+    }
+  }
+  int sms = 0, max_smem = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  P.act_bytes = act_bytes_for(m, NB);
   // rows of the hidden and q|k|v outputs one CTA owns (residual / bias kept in shared memory)
   const int qkv_rows = (m.n_q_heads + 2 * m.n_kv_heads) * m.head_dim;
   // (pair-aligned partitions: at most 2 * ceil(rows / 2 / ctas) rows per CTA,
@@ -2196,6 +2226,18 @@ static int launch(const Params& P0, const lmps_model_desc& m, cudaStream_t st) {
   }
   if (slots < 3) return LMPS_ERR_UNSUPPORTED;
   P.slots = slots;
+  if (dev >= 0 && dev < kCfgDevices) {
+    std::lock_guard<std::mutex> lock(cache_mutex);
+    LaunchCfg& c = cache[dev];
+    c.key_layers = m.n_layers;
+    c.key_hidden = m.hidden;
+    c.key_inter = m.intermediate;
+    c.key_qkv = qkv_rows_k;
+    c.key_vocab = m.vocab;
+    c.sms = sms;
+    c.slots = slots;
+    c.smem = smem;
+  }
   void* args[] = {&P};
   e = cudaLaunchCooperativeKernel(reinterpret_cast<void*>(kern), dim3(sms), dim3(kThreads), args, smem, st);
   return e == cudaSuccess ? LMPS_OK : static_cast<int>(e);

@@ -48,16 +48,23 @@ def argmax_first(logits) -> int:
     """runners/engine.py:180-181, ``np.argmax(logits.astype(np.float32))``:
     the first index of the largest value.
 
-    For a contiguous 1-D fp16 array the fp32 copy is skipped: fp16 -> fp32 is
-    exact and keeps the order, and the fp16 bit patterns map to int16 keys
-    in the same order (negative values: magnitude bits flipped), so the
-    int16 argmax is the same index -- except where fp32 comparison and the
-    bit patterns disagree: a NaN (np.argmax returns the first NaN) or a
-    maximum of zero (-0 and +0 compare equal).  Those arrays take the fp32
-    path.  ~6x faster on the 151936 LM-head logits."""
+    For a contiguous 1-D fp16 array the fp32 copy is skipped.  Read as int16,
+    the fp16 bit patterns of positive values keep their order and lie above
+    every negative value and zero, so when the largest int16 is a positive
+    number (finite or +inf) its first index is the answer -- unless the
+    array holds a NaN, which np.argmax would return: a positive NaN would be
+    that largest int16 (above +inf's 31744), a negative NaN is a uint16
+    pattern above -inf's 0xFC00.  Otherwise (no positive value, or a NaN) the
+    order-preserving keys (negative values: magnitude bits flipped) decide,
+    and a NaN or a maximum of zero (-0 and +0 compare equal) takes the fp32
+    path.  ~10x faster than the fp32 copy on the 151936 LM-head logits."""
     x = np.asarray(logits)
     if x.dtype == np.float16 and x.ndim == 1 and x.flags.c_contiguous and x.size:
         b = x.view(np.int16)
+        i = int(np.argmax(b))
+        v = int(b[i])
+        if 0 < v <= 31744 and int(x.view(np.uint16).max()) <= 0xFC00:
+            return i
         key = b ^ ((b >> 15) & np.int16(0x7FFF))
         i = int(np.argmax(key))
         k = int(key[i])
@@ -66,6 +73,8 @@ def argmax_first(logits) -> int:
         if k <= 31744 and k != 0 and k != -1 and int(key.min()) >= -31745:
             return i
     return int(np.argmax(x.astype(np.float32)))
+
+
 DENSE_PREFILL_TOKENS = 256  # prompts with at least this many tokens in total prefill on the GEMM path
 
 
@@ -164,6 +173,11 @@ class QwenEngine:
         self._pin_ids = torch.zeros(B, dtype=i32).pin_memory()
         self._pin_next = torch.zeros(B, dtype=i32).pin_memory()
         self._pin_err = torch.zeros(1, dtype=i32).pin_memory()
+        # run_inference's views, made once (it runs once per token)
+        self._pin_vec_np, self._pin_logits_np, self._pin_err_np = (
+            self._pin_vec.numpy(), self._pin_logits.numpy(), self._pin_err.numpy())
+        self._x_row0, self._x_rows1 = self.buf_residual[0], self.buf_residual[:1]
+        self._lg_row0, self._lg_rows1 = self.buf_logits[0], self.buf_logits[:1]
 
     def reset(self, batch: Optional[int] = None, start_pos: int = 0) -> None:
         """Start ``batch`` fresh sequences (slots 0..batch-1) at ``start_pos``."""
@@ -290,23 +304,22 @@ class QwenEngine:
         vec = np.ascontiguousarray(input_vector, dtype=np.float16).reshape(-1)
         if vec.size != self.cfg.hidden:
             raise ValueError(f"input vector has {vec.size} elements, expected {self.cfg.hidden}")
-        self._pin_vec.numpy()[:] = vec
-        self.buf_residual[0].copy_(self._pin_vec, non_blocking=True)
+        self._pin_vec_np[:] = vec
+        self._x_row0.copy_(self._pin_vec, non_blocking=True)
         if self.pdec is not None:
-            self.pdec.run(1, self.tokens, self.pos, 1, x_in=self.buf_residual[:1],
-                          logits=self.buf_logits[:1])
+            self.pdec.run(1, self.tokens, self.pos, 1, x_in=self._x_rows1, logits=self._lg_rows1)
         elif self.use_graphs:
             self._graph_for(1, record=False, vector=True).replay()
         else:
             self._vector_step()
-        self._pin_logits.copy_(self.buf_logits[0], non_blocking=True)
+        self._pin_logits.copy_(self._lg_row0, non_blocking=True)
         if self.pdec is not None:  # the device error word rides along with the logits
             self._pin_err.copy_(self.pdec.error, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
-        if self.pdec is not None and int(self._pin_err[0]) != 0:
+        if self.pdec is not None and self._pin_err_np[0] != 0:
             self.pdec.check_error()
         self.host_pos += 1
-        return self._pin_logits.numpy().copy()
+        return self._pin_logits_np.copy()
 
     def predict_next_token(self, logits: np.ndarray) -> int:
         """engine.py:180-181: argmax over fp32(logits), first index on ties."""
