@@ -453,6 +453,57 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_kernel(const __grid_const
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols) : "memory");
 }
 
+// Epilogue of 32 accumulator columns of a prefill tile: lane = token row rw,
+// r[j] = column n0 + c0 + j (a weight row; gate/up pairs for SwiGLU).
+__device__ __forceinline__ void tiles_epilogue_chunk(const Params& P, const uint32_t (&r)[32], int rw, int n0,
+                                                     int c0) {
+  if (rw < P.m && P.epi == EPI_SWIGLU) {  // 16 (gate, up) pairs -> 16 outputs
+    __half* yrow = P.y + static_cast<size_t>(rw) * P.ldy + (n0 + c0) / 2;
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = 16 * g + 4 * e;  // pairs (i, i + 1), (i + 2, i + 3)
+        const __half2 hh = __halves2half2(swiglu_value(__uint_as_float(r[i]), __uint_as_float(r[i + 1])),
+                                          swiglu_value(__uint_as_float(r[i + 2]), __uint_as_float(r[i + 3])));
+        o[e] = *reinterpret_cast<const uint32_t*>(&hh);
+      }
+      *reinterpret_cast<uint4*>(yrow + 8 * g) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  } else if (rw < P.m && P.epi == EPI_RESIDUAL) {  // residual rows read 16 bytes at a time
+    __half* yrow = P.y + static_cast<size_t>(rw) * P.ldy + n0 + c0;
+    const __half* rrow = P.res + static_cast<size_t>(rw) * P.ldr + n0 + c0;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const uint4 rv = *reinterpret_cast<const uint4*>(rrow + 8 * g);
+      const __half2* r2 = reinterpret_cast<const __half2*>(&rv);
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const __half2 hh = __hadd2(r2[e], __floats2half2_rn(__uint_as_float(r[8 * g + 2 * e]),
+                                                            __uint_as_float(r[8 * g + 2 * e + 1])));
+        o[e] = *reinterpret_cast<const uint32_t*>(&hh);
+      }
+      *reinterpret_cast<uint4*>(yrow + 8 * g) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  } else if (rw < P.m) {
+    __half* yrow = P.y + static_cast<size_t>(rw) * P.ldy + n0 + c0;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {  // 8 columns per 16-byte store
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int cc = n0 + c0 + 8 * g + 2 * e;
+        const __half2 hh = __halves2half2(epi_value(P, __uint_as_float(r[8 * g + 2 * e]), rw, cc),
+                                          epi_value(P, __uint_as_float(r[8 * g + 2 * e + 1]), rw, cc + 1));
+        o[e] = *reinterpret_cast<const uint32_t*>(&hh);
+      }
+      *reinterpret_cast<uint4*>(yrow + 8 * g) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
 // Prefill tiles (MT x 128 tokens x 128 weight rows): one ring of S stages,
 // each holding the MT X tiles, the step's packed W (128 rows x 32 bytes, one
 // TMA box) and the dequantised W tile, which serves the MT token halves (one
@@ -587,51 +638,7 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
       for (int c0 = 0; c0 < kRows; c0 += 32) {
         uint32_t r[32];
         tmem_ld32(tl + c0, r);
-        if (rw < P.m && P.epi == EPI_SWIGLU) {  // 16 (gate, up) pairs -> 16 outputs
-          __half* yrow = P.y + static_cast<size_t>(rw) * P.ldy + (n0 + c0) / 2;
-#pragma unroll
-          for (int g = 0; g < 2; ++g) {
-            uint32_t o[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int i = 16 * g + 4 * e;  // pairs (i, i + 1), (i + 2, i + 3)
-              const __half2 hh = __halves2half2(swiglu_value(__uint_as_float(r[i]), __uint_as_float(r[i + 1])),
-                                                swiglu_value(__uint_as_float(r[i + 2]), __uint_as_float(r[i + 3])));
-              o[e] = *reinterpret_cast<const uint32_t*>(&hh);
-            }
-            *reinterpret_cast<uint4*>(yrow + 8 * g) = make_uint4(o[0], o[1], o[2], o[3]);
-          }
-        } else if (rw < P.m && P.epi == EPI_RESIDUAL) {  // residual rows read 16 bytes at a time
-          __half* yrow = P.y + static_cast<size_t>(rw) * P.ldy + n0 + c0;
-          const __half* rrow = P.res + static_cast<size_t>(rw) * P.ldr + n0 + c0;
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const uint4 rv = *reinterpret_cast<const uint4*>(rrow + 8 * g);
-            const __half2* r2 = reinterpret_cast<const __half2*>(&rv);
-            uint32_t o[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const __half2 hh = __hadd2(r2[e], __floats2half2_rn(__uint_as_float(r[8 * g + 2 * e]),
-                                                                  __uint_as_float(r[8 * g + 2 * e + 1])));
-              o[e] = *reinterpret_cast<const uint32_t*>(&hh);
-            }
-            *reinterpret_cast<uint4*>(yrow + 8 * g) = make_uint4(o[0], o[1], o[2], o[3]);
-          }
-        } else if (rw < P.m) {
-          __half* yrow = P.y + static_cast<size_t>(rw) * P.ldy + n0 + c0;
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {  // 8 columns per 16-byte store
-            uint32_t o[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int cc = n0 + c0 + 8 * g + 2 * e;
-              const __half2 hh = __halves2half2(epi_value(P, __uint_as_float(r[8 * g + 2 * e]), rw, cc),
-                                                epi_value(P, __uint_as_float(r[8 * g + 2 * e + 1]), rw, cc + 1));
-              o[e] = *reinterpret_cast<const uint32_t*>(&hh);
-            }
-            *reinterpret_cast<uint4*>(yrow + 8 * g) = make_uint4(o[0], o[1], o[2], o[3]);
-          }
-        }
+        tiles_epilogue_chunk(P, r, rw, n0, c0);
       }
     }
     }
@@ -639,6 +646,204 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+}
+
+// Persistent prefill GEMM (256 tokens x 128 weight rows per tile): one CTA
+// per SM walks the tiles blockIdx.x, + gridDim.x, .. (weight-row tiles
+// fastest, so the CTAs at work share the same X rows in L2).  The load ring
+// and the dequantisation run on across tile boundaries; the accumulators
+// alternate between two 256-column halves of TMEM, so the epilogue of a tile
+// (warps 6-9) overlaps the main loop of the next; no per-tile prologue.
+//   warp 0 lane 0: TMA loads (two X boxes + the packed W of a K step per stage)
+//   warp 1 lane 0: tcgen05.mma (two M = 128 halves per K step), commits
+//   warps 2-5:     dequantisation (thread t = weight row t of the tile)
+//   warps 6-9:     epilogue (warp w reads TMEM lanes 32 (w % 4) ..)
+constexpr int kPThreads = 320;
+constexpr int kPMT = 2;
+__global__ void __launch_bounds__(kPThreads, 1) w4a16_gemm_persist_kernel(const __grid_constant__ Params P) {
+  extern __shared__ unsigned char smem_raw[];
+  const int S = P.xstages;
+  constexpr int kX = kPMT * 128 * 128;
+  constexpr uint32_t kAcc = 128 * kPMT;  // TMEM columns of one accumulator set
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  unsigned char* xs = base;
+  unsigned char* wd = xs + static_cast<size_t>(S) * kX;
+  unsigned char* wr = wd + static_cast<size_t>(S) * kWTileBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(wr + static_cast<size_t>(S) * kStepBytes);
+  uint64_t* deq = full + kMaxStages;
+  uint64_t* empty = deq + kMaxStages;
+  uint64_t* tfull = empty + kMaxStages;  // [2] accumulator set complete
+  uint64_t* tempty = tfull + 2;          // [2] accumulator set drained by the epilogue
+  uint64_t* done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  volatile int* abort_v = abort_flag;
+
+  lmps_pdl_trigger();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ksteps = P.k / kBK;
+  const int n_tiles = P.n / kRows, m_tiles = (P.m + 128 * kPMT - 1) / (128 * kPMT);
+  const int tiles = n_tiles * m_tiles;
+  if (tid == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&deq[i], 128);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 128);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(2 * kAcc)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer
+      lmps_pdl_wait();  // X is the previous kernel's output
+      RingPos ps;
+      int issued = 0;  // K steps issued over all tiles
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+        const int n0 = (tile % n_tiles) * kRows, m0 = (tile / n_tiles) * 128 * kPMT;
+        for (int kt = 0; kt < ksteps; ++kt, ps.next(S)) {
+          const int s = ps.slot;
+          if (issued >= S && !mbar_wait(&empty[s], ps.phase ^ 1u, P.error, abort_v)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[s], static_cast<uint32_t>(kX + kStepBytes));
+#pragma unroll
+          for (int mh = 0; mh < kPMT; ++mh)
+            tma_load_2d(xs + static_cast<size_t>(s) * kX + mh * 128 * 128, &P.tx, kt * kBK, m0 + 128 * mh, &full[s]);
+          tma_load_2d(wr + static_cast<size_t>(s) * kStepBytes, &P.tw, kt * (kBK / 2), n0, &full[s]);
+          ++issued;
+        }
+      }
+      for (int g = max(0, issued - S); g < issued; ++g) {  // every issued copy lands before exit
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try(&full[g % S], (g / S) & 1))
+          if (globaltimer() - t0 > kTimeoutNs) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---- MMA issuer
+      const uint32_t idesc = idesc_f16(128, 128);
+      RingPos ps;
+      uint32_t uses[2] = {0u, 0u};
+      int buf = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, buf ^= 1) {
+        // the epilogue has drained this accumulator set's previous tile
+        if (!mbar_wait(&tempty[buf], (uses[buf] & 1u) ^ 1u, P.error, abort_v)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t acc = tmem + static_cast<uint32_t>(buf) * kAcc;
+        for (int kt = 0; kt < ksteps; ++kt, ps.next(S)) {
+          const int s = ps.slot;
+          if (!mbar_wait(&deq[s], ps.phase, P.error, abort_v)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint64_t bd = sw128_desc(smem_u32(wd + static_cast<size_t>(s) * kWTileBytes));
+#pragma unroll
+          for (int mh = 0; mh < kPMT; ++mh) {
+            const uint64_t ad = sw128_desc(smem_u32(xs + static_cast<size_t>(s) * kX + mh * 128 * 128));
+#pragma unroll
+            for (int j = 0; j < kBK / 16; ++j)
+              mma_f16(acc + 128 * mh, ad + 2 * j, bd + 2 * j, idesc, (kt > 0 || j > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&tfull[buf]);
+        ++uses[buf];
+      }
+      // every MMA issued above finishes before the tensor memory is freed
+      mma_commit(done);
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try(done, 0u))
+        if (globaltimer() - t0 > kTimeoutNs) break;
+    }
+  } else if (warp < 6) {
+    // ---- dequantisation (thread t = weight row n0 + t of the current tile);
+    // a stage's full barrier completes only after the MMAs that last read it
+    // (the producer waited for them before refilling), so wd[s] is free then
+    const int t = tid - 64, sw = t & 7;
+    RingPos ps;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+      const int n0 = (tile % n_tiles) * kRows;
+      const uint32_t* srow = reinterpret_cast<const uint32_t*>(P.s + static_cast<size_t>(n0 + t) * (P.k / 32));
+      uint32_t sc_next = ksteps > 0 ? __ldg(srow) : 0u;
+      bool ok = true;
+      for (int kt = 0; kt < ksteps; ++kt, ps.next(S)) {
+        const int s = ps.slot;
+        const uint32_t sc = sc_next;
+        if (kt + 1 < ksteps) sc_next = __ldg(srow + kt + 1);
+        if (!mbar_wait(&full[s], ps.phase, P.error, abort_v)) {
+          ok = false;
+          break;
+        }
+        const uint4* raw = reinterpret_cast<const uint4*>(wr + static_cast<size_t>(s) * kStepBytes + t * 32);
+        const uint4 g0 = raw[0], g1 = raw[1];
+        const __half2 sc2 = *reinterpret_cast<const __half2*>(&sc);
+        const __half2 s0 = __low2half2(sc2), s1 = __high2half2(sc2);
+        unsigned char* row = wd + static_cast<size_t>(s) * kWTileBytes + t * 128;
+        *reinterpret_cast<uint4*>(row + ((0 ^ sw) << 4)) = dequant8(g0.x, s0);
+        *reinterpret_cast<uint4*>(row + ((1 ^ sw) << 4)) = dequant8(g0.y, s0);
+        *reinterpret_cast<uint4*>(row + ((2 ^ sw) << 4)) = dequant8(g0.z, s0);
+        *reinterpret_cast<uint4*>(row + ((3 ^ sw) << 4)) = dequant8(g0.w, s0);
+        *reinterpret_cast<uint4*>(row + ((4 ^ sw) << 4)) = dequant8(g1.x, s1);
+        *reinterpret_cast<uint4*>(row + ((5 ^ sw) << 4)) = dequant8(g1.y, s1);
+        *reinterpret_cast<uint4*>(row + ((6 ^ sw) << 4)) = dequant8(g1.z, s1);
+        *reinterpret_cast<uint4*>(row + ((7 ^ sw) << 4)) = dequant8(g1.w, s1);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(&deq[s]);
+      }
+      if (!ok) break;
+    }
+  } else {
+    // ---- epilogue (warps 6-9): lane = token m0 + 128 mh + 32 q + lane
+    lmps_pdl_wait();  // before any read of the residual or write of Y
+    const int q = warp & 3;
+    uint32_t uses[2] = {0u, 0u};
+    int buf = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, buf ^= 1) {
+      const int n0 = (tile % n_tiles) * kRows, m0 = (tile / n_tiles) * 128 * kPMT;
+      if (!mbar_wait(&tfull[buf], uses[buf] & 1u, P.error, abort_v)) break;
+      ++uses[buf];
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll 1
+      for (int mh = 0; mh < kPMT; ++mh) {
+        const uint32_t tl = tmem + static_cast<uint32_t>(buf) * kAcc + (static_cast<uint32_t>(32 * q) << 16) + 128 * mh;
+        const int rw = m0 + 128 * mh + 32 * q + lane;
+#pragma unroll 1
+        for (int c0 = 0; c0 < kRows; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(tl + c0, r);
+          tiles_epilogue_chunk(P, r, rw, n0, c0);
+        }
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      mbar_arrive(&tempty[buf]);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kAcc) : "memory");
 }
 
 static size_t tiles_smem_bytes(int stages, int mt) {
@@ -725,13 +930,14 @@ extern "C" int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed
   (void)workspace;
   (void)workspace_bytes;
   if (!P.swap) {  // prefill tiles: the single-ring kernel
-    if (m >= 256) {  // 256 tokens per CTA (each dequantised W tile serves two MMAs), four stages, one CTA per SM
+    if (m >= 256) {  // persistent: 256 tokens x 128 rows per tile, four stages, one CTA per SM
       P.xstages = 4;
-      const size_t smem = w4::tiles_smem_bytes(P.xstages, 2);
-      const int st_attr = lmps_max_dyn_smem<w4::w4a16_gemm_tiles_kernel<2>>(static_cast<int>(smem));
+      const size_t smem = w4::tiles_smem_bytes(P.xstages, 2) + 64;  // + the accumulator-set barriers
+      const int st_attr = lmps_max_dyn_smem<w4::w4a16_gemm_persist_kernel>(static_cast<int>(smem));
       if (st_attr != LMPS_OK) return st_attr;
-      return lmps_launch_pdl(w4::w4a16_gemm_tiles_kernel<2>, dim3(nt, (m + 255) / 256), dim3(w4::kThreads), smem,
-                             lmps_stream(stream), P);
+      const int tiles = nt * ((m + 255) / 256);
+      return lmps_launch_pdl(w4::w4a16_gemm_persist_kernel, dim3(tiles < sms ? tiles : sms), dim3(w4::kPThreads),
+                             smem, lmps_stream(stream), P);
     }
     P.xstages = 3;  // three stages, two CTAs per SM
     const size_t smem = w4::tiles_smem_bytes(P.xstages, 1);

@@ -40,6 +40,45 @@ def test_w4a16_gemm_matches_dequantised_product(cuda, n, k, m):
     assert_close(y.cpu().numpy(), ref, abs_tol=2e-2, rel_tol=1e-2, what=f"gemm {m}x{n}x{k}")
 
 
+@pytest.mark.parametrize("epi", ["none", "bias", "residual", "swiglu"])
+def test_w4a16_gemm_persistent_equals_single_tiles(cuda, epi):
+    """From 256 tokens the prefill GEMM is one persistent CTA per SM walking
+    256 x 128 tiles (several per CTA here: 2085 tokens x 8960 rows = 630
+    tiles), the accumulators alternating in TMEM.  Each output row sums the
+    same K steps in the same order as the one-tile-per-CTA kernel (128 tokens
+    per call), so the two agree bit for bit, for every epilogue and a ragged
+    last tile."""
+    from llamamps_b200 import kernels as K
+    n, k, m = 8960, 1536, 2085
+    packed, scales, x, wd = _case(n, k, m, seed=31)
+    pk, sc, xd = _dev(packed, scales, x)
+    rng = np.random.default_rng(32)
+    kw = {}
+    if epi == "bias":
+        kw["bias"] = torch.from_numpy(rng.normal(0, 0.02, n).astype(np.float16)).cuda()
+    if epi == "swiglu":
+        kw["swiglu"] = True
+    res = torch.from_numpy(rng.normal(0, 1, (m, n)).astype(np.float16)).cuda() if epi == "residual" else None
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    full = K.w4a16_gemm(xd, pk, sc, n, k, error=err, **kw, **({"residual": res} if res is not None else {}))
+    mp = (m + 127) // 128 * 128
+    xp = torch.zeros(mp, k, dtype=torch.float16, device="cuda")
+    xp[:m] = xd
+    rp = None
+    if res is not None:
+        rp = torch.zeros(mp, n, dtype=torch.float16, device="cuda")
+        rp[:m] = res
+    parts = []
+    for r0 in range(0, mp, 128):
+        extra = {"residual": rp[r0:r0 + 128].contiguous()} if rp is not None else {}
+        parts.append(K.w4a16_gemm(xp[r0:r0 + 128].contiguous(), pk, sc, n, k, error=err, **kw, **extra))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = torch.cat(parts)[:m]
+    assert full.shape == ref.shape
+    assert torch.equal(full, ref), f"persistent vs single tiles differ ({epi})"
+
+
 def test_w4a16_gemm_epilogues_and_gemv_agreement(cuda):
     from llamamps_b200 import kernels as K
     n, k, m = 256, 1536, 8
