@@ -599,7 +599,7 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
     // ---- dequantisation (thread t = weight row n0 + t); the full barrier of
     // a stage completes only after the MMAs that last read it (the producer
     // waited for them before refilling), so wd[s] is free once it is full
-    const int t = tid - 64, sw = t & 7;
+    const int t = tid - 64, sw = t & 7, hs = q4t::half_swap(t);
     const uint32_t* srow = reinterpret_cast<const uint32_t*>(P.s + static_cast<size_t>(n0 + t) * (P.k / 32));
     uint32_t sc_next = ksteps > 0 ? __ldg(srow) : 0u;
     RingPos ps;
@@ -608,8 +608,9 @@ __global__ void __launch_bounds__(kThreads) w4a16_gemm_tiles_kernel(const __grid
       const uint32_t sc = sc_next;
       if (kt + 1 < ksteps) sc_next = __ldg(srow + kt + 1);
       if (!mbar_wait(&full[s], ps.phase, P.error, abort_v)) break;
+      // row t's two 16-byte halves, swapped by the 32-byte TMA swizzle when (t >> 2) & 1
       const uint4* raw = reinterpret_cast<const uint4*>(wr + static_cast<size_t>(s) * kStepBytes + t * 32);
-      const uint4 g0 = raw[0], g1 = raw[1];
+      const uint4 g0 = raw[hs], g1 = raw[hs ^ 1];
       const __half2 sc2 = *reinterpret_cast<const __half2*>(&sc);
       const __half2 s0 = __low2half2(sc2), s1 = __high2half2(sc2);
       unsigned char* row = wd + static_cast<size_t>(s) * kWTileBytes + t * 128;
@@ -781,7 +782,7 @@ __global__ void __launch_bounds__(kPThreads, 1) w4a16_gemm_persist_kernel(const 
     // ---- dequantisation (thread t = weight row n0 + t of the current tile);
     // a stage's full barrier completes only after the MMAs that last read it
     // (the producer waited for them before refilling), so wd[s] is free then
-    const int t = tid - 64, sw = t & 7;
+    const int t = tid - 64, sw = t & 7, hs = q4t::half_swap(t);
     RingPos ps;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
       const int n0 = (tile % n_tiles) * kRows;
@@ -796,8 +797,9 @@ __global__ void __launch_bounds__(kPThreads, 1) w4a16_gemm_persist_kernel(const 
           ok = false;
           break;
         }
+        // row t's two 16-byte halves, swapped by the 32-byte TMA swizzle when (t >> 2) & 1
         const uint4* raw = reinterpret_cast<const uint4*>(wr + static_cast<size_t>(s) * kStepBytes + t * 32);
-        const uint4 g0 = raw[0], g1 = raw[1];
+        const uint4 g0 = raw[hs], g1 = raw[hs ^ 1];
         const __half2 sc2 = *reinterpret_cast<const __half2*>(&sc);
         const __half2 s0 = __low2half2(sc2), s1 = __high2half2(sc2);
         unsigned char* row = wd + static_cast<size_t>(s) * kWTileBytes + t * 128;
@@ -910,7 +912,7 @@ extern "C" int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed
                  static_cast<uint64_t>(ldx) * 2, w4::kBK, static_cast<uint32_t>(xr), CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_2d(&P.tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, static_cast<uint64_t>(k / 2), static_cast<uint64_t>(n),
                  static_cast<uint64_t>(k / 2), static_cast<uint32_t>(w4::kBK / 2 * P.wspb), w4::kRows,
-                 P.wspb == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE))
+                 P.wspb == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_32B))
     return LMPS_ERR_INVALID_ARGUMENT;
   P.s = reinterpret_cast<const __half*>(scales);
   P.bias = reinterpret_cast<const __half*>(bias);
