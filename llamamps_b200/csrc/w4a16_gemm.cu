@@ -23,7 +23,8 @@
 //   * warps 2-5 then read the accumulator (tcgen05.ld; warp w reads TMEM
 //     lanes 32 (w % 4) ..) and apply bias / residual.
 // Two tile shapes share the pipeline:
-//   * tokens >= 128 (prefill): A = X (M = 128 tokens), B = W (N = 128 rows);
+//   * tokens >= 128 (prefill; also 33-127 tokens of a very wide output, the
+//     LM head of a decode batch): A = X (M = 128 tokens), B = W (N = 128 rows);
 //   * fewer tokens (decode batches): A = W (M = 128 rows), B = X (N = the
 //     token count rounded up to 16), so no tensor-core row is padding and W
 //     is read once.  K is then split across the CTAs of a thread-block
@@ -871,7 +872,13 @@ using tc::encode_2d;
 // Token-tile geometry: fewer than 128 tokens run one token tile with the
 // weight rows as the MMA's M (rounded up to 16 tokens); otherwise 128-token
 // tiles.
-static int w4_xrows(int m) { return m < 128 ? ((m + 15) / 16) * 16 : 128; }
+// The swapped decode tile (weights as M, tokens as N, split K) below 128
+// tokens -- except for very wide outputs (the LM head) from 33 tokens on,
+// where the 128-token prefill tile (rows past m read as zero) is faster:
+// 64 x 151936 x 1536 116 -> 89 us, 100 tokens 142 -> 92 us (16 tokens
+// 95 -> 151 us, so not there).
+static bool w4_swap(int m, int n) { return m < 128 && (m <= 32 || n < 65536); }
+static int w4_xrows(int m, int n) { return w4_swap(m, n) ? ((m + 15) / 16) * 16 : 128; }
 
 extern "C" size_t lmps_w4a16_gemm_workspace_size(int m, int n) {
   (void)m;
@@ -902,8 +909,8 @@ extern "C" int lmps_w4a16_gemm(const uint16_t* x, int ldx, const uint8_t* packed
   LMPS_CHECK_ARG(ldx >= k && ldx % 8 == 0 && ldy >= ncols && ldy % 8 == 0);
   LMPS_CHECK_ARG(lmps_aligned(x, 16) && lmps_aligned(y, 16) && lmps_aligned(packed, 16) && lmps_aligned(scales, 4));
   w4::Params P{};
-  const int xr = w4_xrows(m);
-  P.swap = m < 128 ? 1 : 0;
+  const int xr = w4_xrows(m, n);
+  P.swap = w4_swap(m, n) ? 1 : 0;
   P.xrows = xr;
   // decode tiles stream packed W in 128-byte row pieces (4 K steps per load);
   // prefill tiles in 32-byte pieces, one per K step

@@ -26,7 +26,7 @@ def _dev(packed, scales, x):
 
 
 @pytest.mark.parametrize("n,k,m", [(128, 64, 1), (256, 1536, 200), (2048, 1536, 128), (1536, 8960, 64),
-                                   (384, 1536, 300)])
+                                   (384, 1536, 300), (65536, 512, 64), (65536, 512, 100), (65536, 512, 32)])
 def test_w4a16_gemm_matches_dequantised_product(cuda, n, k, m):
     from llamamps_b200 import kernels as K
     packed, scales, x, wd = _case(n, k, m, seed=n + k + m)
