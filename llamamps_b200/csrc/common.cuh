@@ -169,12 +169,16 @@ __device__ __forceinline__ void rope_pair_index(int pair, int head_dim, int styl
   fi = j;
 }
 
-__device__ __forceinline__ void rope_rotate(__half& a, __half& b, float ang) {
-  float s, c;
-  sincosf(ang, &s, &c);
+// The rotation with cos / sin already computed (rope_rotate's arithmetic).
+__device__ __forceinline__ void rope_rotate_cs(__half& a, __half& b, float c, float s) {
   const float x1 = __half2float(a), x2 = __half2float(b);
   a = __float2half_rn(x1 * c - x2 * s);
   b = __float2half_rn(x1 * s + x2 * c);
+}
+__device__ __forceinline__ void rope_rotate(__half& a, __half& b, float ang) {
+  float s, c;
+  sincosf(ang, &s, &c);
+  rope_rotate_cs(a, b, c, s);
 }
 
 }  // namespace lmps

@@ -47,6 +47,60 @@ rms_norm_kernel(const __half* __restrict__ x, const __half* __restrict__ gamma,
   }
 }
 
+// The same RMSNorm with one warp per row (8 rows per CTA) and 16-byte loads
+// and stores: no block barrier, every load of a row in flight at once.  For
+// at least 256 rows (the prefill's 16384 rows: 48 us per call with a CTA per
+// row), dim % 8 == 0, dim <= 2048, 16-byte aligned rows.
+constexpr int kNormRowsPerCta = 8;
+constexpr int kNormMaxVec = 8;  // 16-byte groups per lane: dim <= 8 * 8 * 32
+constexpr int kNormWarpMinRows = 256;
+__global__ void __launch_bounds__(kNormRowsPerCta * kWarp)
+rms_norm_warp_kernel(const __half* __restrict__ x, const __half* __restrict__ gamma, __half* __restrict__ out,
+                     int dim, float eps, int rows) {
+  lmps_pdl_trigger();
+  lmps_pdl_wait();
+  const int row = blockIdx.x * kNormRowsPerCta + static_cast<int>(threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int nv = dim / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * dim);
+  uint4 v[kNormMaxVec];
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int j = lane + kWarp * i;
+    if (j < nv) {
+      v[i] = xr[j];
+      const __half* h = reinterpret_cast<const __half*>(&v[i]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float f = __half2float(h[e]);
+        ss = fmaf(f, f, ss);
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  const float scale = 1.0f / sqrtf(ss / static_cast<float>(dim) + eps);
+  const uint4* gr = reinterpret_cast<const uint4*>(gamma);
+  uint4* orow = reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * dim);
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int j = lane + kWarp * i;
+    if (j < nv) {
+      const uint4 gv = __ldg(gr + j);
+      const __half* h = reinterpret_cast<const __half*>(&v[i]);
+      const __half* g = reinterpret_cast<const __half*>(&gv);
+      uint4 o;
+      __half* oh = reinterpret_cast<__half*>(&o);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const __half nrm = __float2half_rn(__half2float(h[e]) * scale);
+        oh[e] = __float2half_rn(__half2float(nrm) * __half2float(g[e]));
+      }
+      orow[j] = o;
+    }
+  }
+}
+
 // RoPE -- kernels/rope.metal:19-40 (rope_pair_index / rope_rotate in common.cuh).
 __global__ void rope_kernel(__half* vec, const int32_t* pos, const float* inv_freq, int n_heads,
                             int head_dim, int style) {
@@ -65,7 +119,7 @@ __global__ void rope_kernel(__half* vec, const int32_t* pos, const float* inv_fr
 }
 
 // RoPE on q and k of the fused q|k|v row, then the paged KV-cache append.
-__global__ void rope_kv_append_kernel(const __half* __restrict__ qkv, const int32_t* __restrict__ pos,
+__global__ void rope_kv_append_scalar_kernel(const __half* __restrict__ qkv, const int32_t* __restrict__ pos,
                                       const float* __restrict__ inv_freq, __half* __restrict__ q_out,
                                       __half* __restrict__ k_pool, __half* __restrict__ v_pool,
                                       const int32_t* __restrict__ block_table, int max_pages,
@@ -102,6 +156,77 @@ __global__ void rope_kv_append_kernel(const __half* __restrict__ qkv, const int3
   for (int i = threadIdx.x; i < kv_dim; i += blockDim.x) {
     const int h = i / head_dim;
     v_pool[((static_cast<size_t>(page) * n_kv_heads + h) * page_size + off) * head_dim + (i - h * head_dim)] = vsrc[i];
+  }
+}
+
+// The same with each row's head_dim / 2 (cos, sin) pairs computed once (not
+// once per head) and 16 bytes moved per thread: 4 adjacent pairs
+// (interleaved) or 8 pairs of a head's two halves (NeoX) per step.  For
+// head_dim % 16 == 0, head_dim <= 512, 16-byte aligned buffers.
+constexpr int kRopeMaxHalf = 256;
+__global__ void __launch_bounds__(256)
+rope_kv_append_kernel(const __half* __restrict__ qkv, const int32_t* __restrict__ pos,
+                      const float* __restrict__ inv_freq, __half* __restrict__ q_out, __half* __restrict__ k_pool,
+                      __half* __restrict__ v_pool, const int32_t* __restrict__ block_table, int max_pages,
+                      int page_size, int n_q_heads, int n_kv_heads, int head_dim, int style) {
+  lmps_pdl_trigger();
+  lmps_pdl_wait();
+  __shared__ float2 cs[kRopeMaxHalf];
+  const int b = blockIdx.x, tid = threadIdx.x, half_d = head_dim / 2;
+  const int q_dim = n_q_heads * head_dim, kv_dim = n_kv_heads * head_dim;
+  const __half* row = qkv + static_cast<size_t>(b) * (q_dim + 2 * kv_dim);
+  const int p = pos[b];
+  const float m = static_cast<float>(p);
+  const int page = block_table[static_cast<size_t>(b) * max_pages + p / page_size];
+  const int off = p % page_size;
+  for (int j = tid; j < half_d; j += blockDim.x) {
+    float sn, c;
+    sincosf(m * inv_freq[j], &sn, &c);
+    cs[j] = make_float2(c, sn);
+  }
+  __syncthreads();
+  auto kv_row = [&](__half* pool, int h) {
+    return pool + ((static_cast<size_t>(page) * n_kv_heads + h) * page_size + off) * head_dim;
+  };
+  if (style == LMPS_ROPE_INTERLEAVED) {  // element 2j pairs with 2j + 1, frequency j
+    for (int u = tid; u < (q_dim + kv_dim) / 8; u += blockDim.x) {
+      const int e0 = 8 * u;
+      const bool is_q = e0 < q_dim;
+      const int e = is_q ? e0 : e0 - q_dim, h = e / head_dim, d0 = e - h * head_dim;
+      uint4 v = *reinterpret_cast<const uint4*>(row + e0);
+      __half* hv = reinterpret_cast<__half*>(&v);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 t = cs[d0 / 2 + i];
+        rope_rotate_cs(hv[2 * i], hv[2 * i + 1], t.x, t.y);
+      }
+      __half* dst = is_q ? q_out + static_cast<size_t>(b) * q_dim + e : kv_row(k_pool, h) + d0;
+      *reinterpret_cast<uint4*>(dst) = v;
+    }
+  } else {  // NeoX: element j pairs with j + head_dim / 2, frequency j
+    const int upd = half_d / 8;  // 8-pair units per head
+    for (int u = tid; u < (n_q_heads + n_kv_heads) * upd; u += blockDim.x) {
+      const int hh = u / upd, j0 = 8 * (u - hh * upd);
+      const bool is_q = hh < n_q_heads;
+      const int h = is_q ? hh : hh - n_q_heads;
+      const __half* src = row + (is_q ? 0 : q_dim) + h * head_dim;
+      uint4 v1 = *reinterpret_cast<const uint4*>(src + j0), v2 = *reinterpret_cast<const uint4*>(src + j0 + half_d);
+      __half* h1 = reinterpret_cast<__half*>(&v1);
+      __half* h2 = reinterpret_cast<__half*>(&v2);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float2 t = cs[j0 + i];
+        rope_rotate_cs(h1[i], h2[i], t.x, t.y);
+      }
+      __half* dst = is_q ? q_out + static_cast<size_t>(b) * q_dim + h * head_dim : kv_row(k_pool, h);
+      *reinterpret_cast<uint4*>(dst + j0) = v1;
+      *reinterpret_cast<uint4*>(dst + j0 + half_d) = v2;
+    }
+  }
+  const __half* vsrc = row + q_dim + kv_dim;
+  for (int u = tid; u < kv_dim / 8; u += blockDim.x) {
+    const int e = 8 * u, h = e / head_dim;
+    *reinterpret_cast<uint4*>(kv_row(v_pool, h) + (e - h * head_dim)) = *reinterpret_cast<const uint4*>(vsrc + e);
   }
 }
 
@@ -340,6 +465,13 @@ extern "C" const char* lmps_status_string(int status) {
 extern "C" int lmps_rms_norm(const uint16_t* x, const uint16_t* gamma, uint16_t* out, int dim,
                              int batch, float eps, void* stream) {
   LMPS_CHECK_ARG(x && gamma && out && dim > 0 && batch > 0 && eps >= 0.0f);
+  // the warp-per-row kernel for the prefill's thousands of rows; decode
+  // batches keep a CTA per row (measured faster at 64 rows: c2 2.10 vs 2.17 ms)
+  if (batch >= kNormWarpMinRows && dim % 8 == 0 && dim <= kNormMaxVec * 8 * kWarp && lmps_aligned(x, 16) &&
+      lmps_aligned(gamma, 16) && lmps_aligned(out, 16))
+    return lmps_launch_pdl(rms_norm_warp_kernel, dim3((batch + kNormRowsPerCta - 1) / kNormRowsPerCta),
+                           dim3(kNormRowsPerCta * kWarp), 0, lmps_stream(stream), CH(x), CH(gamma), H(out), dim, eps,
+                           batch);
   return lmps_launch_pdl(rms_norm_kernel, dim3(batch), dim3(kNormThreads), 0, lmps_stream(stream), CH(x), CH(gamma),
                          H(out), dim, eps);
 }
@@ -364,7 +496,12 @@ extern "C" int lmps_rope_kv_append(const uint16_t* qkv, const int32_t* pos, cons
   LMPS_CHECK_ARG(max_pages > 0 && page_size > 0 && batch > 0 && head_dim > 0 && head_dim % 2 == 0);
   LMPS_CHECK_ARG(n_kv_heads > 0 && n_q_heads > 0 && n_q_heads % n_kv_heads == 0);
   LMPS_CHECK_ARG(style == LMPS_ROPE_INTERLEAVED || style == LMPS_ROPE_NEOX);
-  return lmps_launch_pdl(rope_kv_append_kernel, dim3(batch), dim3(256), 0, lmps_stream(stream), CH(qkv), pos,
+  if (head_dim % 16 == 0 && head_dim / 2 <= kRopeMaxHalf && lmps_aligned(qkv, 16) && lmps_aligned(q_out, 16) &&
+      lmps_aligned(k_pool, 16) && lmps_aligned(v_pool, 16))
+    return lmps_launch_pdl(rope_kv_append_kernel, dim3(batch), dim3(256), 0, lmps_stream(stream), CH(qkv), pos,
+                           inv_freq, H(q_out), H(k_pool), H(v_pool), block_table, max_pages, page_size, n_q_heads,
+                           n_kv_heads, head_dim, style);
+  return lmps_launch_pdl(rope_kv_append_scalar_kernel, dim3(batch), dim3(256), 0, lmps_stream(stream), CH(qkv), pos,
                          inv_freq, H(q_out), H(k_pool), H(v_pool), block_table, max_pages, page_size, n_q_heads,
                          n_kv_heads, head_dim, style);
 }

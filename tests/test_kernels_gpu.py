@@ -121,7 +121,7 @@ def test_lm_head_argmax_first_index_ties(cuda, batch):
     assert np.all(ids.cpu().numpy() == 17)
 
 
-@pytest.mark.parametrize("dim,batch", [(1536, 1), (1536, 4), (8960, 2), (96, 3)])
+@pytest.mark.parametrize("dim,batch", [(1536, 1), (1536, 4), (1536, 300), (2048, 263), (8960, 2), (96, 257), (100, 2)])
 def test_rms_norm(cuda, dim, batch):
     from llamamps_b200 import kernels as K
     rng = np.random.default_rng(dim + batch)
@@ -240,25 +240,40 @@ def test_gqa_decode_attention(cuda, T_list, page_size, max_seq):
             assert_close(o[b], ref, abs_tol=5e-3, what=f"attn T={T_list[b]} splits={n_splits}")
 
 
-def test_rope_kv_append_matches_oracle(cuda):
+@pytest.mark.parametrize("style", [0, 1])
+def test_rope_kv_append_matches_oracle(cuda, style):
+    """RoPE on q and k of the fused q|k|v rows and the paged-cache append
+    (both pair layouts) against the oracle; the 16-byte kernel (one cos/sin
+    table per row) bit-equal to the element-wise one, which a misaligned
+    output selects."""
     from llamamps_b200 import kernels as K
     from llamamps_b200.engine import rope_inv_freq
-    rng = np.random.default_rng(71)
+    rng = np.random.default_rng(71 + style)
     B, page_size, max_seq = 3, 16, 64
     kv, _ = _paged_setup(rng, B, [5, 16, 40], page_size, max_seq)
+    kv2, _ = _paged_setup(np.random.default_rng(71 + style), B, [5, 16, 40], page_size, max_seq)
     pos = np.array([5, 16, 40], np.int32)
     qkv = rng.normal(0, 1, (B, 2048)).astype(np.float16)
     q_out = torch.zeros(B, 1536, dtype=torch.float16, device="cuda")
     kp, vp = kv.layer(0)
-    K.rope_kv_append(_t(qkv), _t(pos), _t(rope_inv_freq(128, 1e6)), q_out, kp, vp, kv.block_table,
-                     page_size, 12, 2, 128, 0)
+    inv = _t(rope_inv_freq(128, 1e6))
+    K.rope_kv_append(_t(qkv), _t(pos), inv, q_out, kp, vp, kv.block_table, page_size, 12, 2, 128, style)
+    name = "neox" if style else "interleaved"
     for b in range(B):
-        qr = M.rope(qkv[b, :1536], int(pos[b]), 128, 1e6)
-        kr = M.rope(qkv[b, 1536:1792], int(pos[b]), 128, 1e6)
+        qr = M.rope(qkv[b, :1536], int(pos[b]), 128, 1e6, name)
+        kr = M.rope(qkv[b, 1536:1792], int(pos[b]), 128, 1e6, name)
         assert_close(q_out[b].cpu().numpy(), qr, abs_tol=2e-3, what="q rope")
         kk, vv = kv.read_positions(b, 0, int(pos[b]) + 1)
         assert_close(kk[-1].cpu().numpy(), kr, abs_tol=2e-3, what="k append")
         assert f16_bits_equal(vv[-1].cpu().numpy(), qkv[b, 1792:])
+    buf = torch.zeros(B * 1536 + 8, dtype=torch.float16, device="cuda")
+    q_mis = buf[1:1 + B * 1536].view(B, 1536)  # 2-byte aligned: the element-wise kernel
+    kp2, vp2 = kv2.layer(0)
+    K.rope_kv_append(_t(qkv), _t(pos), inv, q_mis, kp2, vp2, kv2.block_table, page_size, 12, 2, 128, style)
+    torch.cuda.synchronize()
+    assert torch.equal(q_mis.view(torch.int16), q_out.view(torch.int16))
+    assert torch.equal(kp2.view(torch.int16), kp.view(torch.int16))
+    assert torch.equal(vp2.view(torch.int16), vp.view(torch.int16))
 
 
 def test_q4_pack_device_bit_exact(cuda):
