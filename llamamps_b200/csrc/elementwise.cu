@@ -179,21 +179,31 @@ rope_kv_append_kernel(const __half* __restrict__ qkv, const int32_t* __restrict_
   const float m = static_cast<float>(p);
   const int page = block_table[static_cast<size_t>(b) * max_pages + p / page_size];
   const int off = p % page_size;
+  auto kv_row = [&](__half* pool, int h) {
+    return pool + ((static_cast<size_t>(page) * n_kv_heads + h) * page_size + off) * head_dim;
+  };
+  // the V rows and this thread's first q|k unit are read before the table is
+  // built (nothing of theirs depends on it)
+  const __half* vsrc = row + q_dim + kv_dim;
+  for (int u = tid; u < kv_dim / 8; u += blockDim.x) {
+    const int e = 8 * u, h = e / head_dim;
+    *reinterpret_cast<uint4*>(kv_row(v_pool, h) + (e - h * head_dim)) = *reinterpret_cast<const uint4*>(vsrc + e);
+  }
+  const bool il = style == LMPS_ROPE_INTERLEAVED;
+  uint4 first = make_uint4(0u, 0u, 0u, 0u);
+  if (il && tid < (q_dim + kv_dim) / 8) first = *reinterpret_cast<const uint4*>(row + 8 * tid);
   for (int j = tid; j < half_d; j += blockDim.x) {
     float sn, c;
     sincosf(m * inv_freq[j], &sn, &c);
     cs[j] = make_float2(c, sn);
   }
   __syncthreads();
-  auto kv_row = [&](__half* pool, int h) {
-    return pool + ((static_cast<size_t>(page) * n_kv_heads + h) * page_size + off) * head_dim;
-  };
-  if (style == LMPS_ROPE_INTERLEAVED) {  // element 2j pairs with 2j + 1, frequency j
+  if (il) {  // element 2j pairs with 2j + 1, frequency j
     for (int u = tid; u < (q_dim + kv_dim) / 8; u += blockDim.x) {
       const int e0 = 8 * u;
       const bool is_q = e0 < q_dim;
       const int e = is_q ? e0 : e0 - q_dim, h = e / head_dim, d0 = e - h * head_dim;
-      uint4 v = *reinterpret_cast<const uint4*>(row + e0);
+      uint4 v = u == tid ? first : *reinterpret_cast<const uint4*>(row + e0);
       __half* hv = reinterpret_cast<__half*>(&v);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -222,11 +232,6 @@ rope_kv_append_kernel(const __half* __restrict__ qkv, const int32_t* __restrict_
       *reinterpret_cast<uint4*>(dst + j0) = v1;
       *reinterpret_cast<uint4*>(dst + j0 + half_d) = v2;
     }
-  }
-  const __half* vsrc = row + q_dim + kv_dim;
-  for (int u = tid; u < kv_dim / 8; u += blockDim.x) {
-    const int e = 8 * u, h = e / head_dim;
-    *reinterpret_cast<uint4*>(kv_row(v_pool, h) + (e - h * head_dim)) = *reinterpret_cast<const uint4*>(vsrc + e);
   }
 }
 
