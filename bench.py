@@ -248,6 +248,17 @@ def gemv_roofline(eng, peak_gbs, peak_kind, reps: int = 3):
             "bytes_per_launch": bytes_per_launch, "us_per_launch": round(per_launch_s * 1e6, 3)}
 
 
+def _busy_stream(ms: float = 3.0):
+    """Keep the current stream busy for about ``ms`` with a device-side spin
+    (clock64 cycles at the 1965 MHz SM clock), so that the start event and
+    the launches after it are already queued when the GPU reaches them: the
+    host's time to enqueue them (and anything that delays the host thread,
+    such as the clock sampler's NVML queries) stays out of the device time.
+    The end-to-end measurement keeps every host cost."""
+    import torch
+    torch.cuda._sleep(int(ms * 1e-3 * 1.965e9))
+
+
 def _timed(fn, world, dist):
     """Device time of fn() bracketed by a barrier and synchronizes, max over ranks."""
     import torch
@@ -256,6 +267,7 @@ def _timed(fn, world, dist):
     torch.cuda.synchronize()
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _busy_stream()
     e0.record(st)
     fn()
     e1.record(st)
@@ -758,6 +770,7 @@ def run_ours(args):
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
+        _busy_stream()
         clk.mark(True)
         e0.record(st)
         eng.decode_steps(args.steps, record=False)   # persistent: one launch for all K steps
