@@ -178,6 +178,7 @@ class QwenEngine:
             self._pin_vec.numpy(), self._pin_logits.numpy(), self._pin_err.numpy())
         self._x_row0, self._x_rows1 = self.buf_residual[0], self.buf_residual[:1]
         self._lg_row0, self._lg_rows1 = self.buf_logits[0], self.buf_logits[:1]
+        self._ri_warm = False  # run_inference has launched once eagerly (then it replays a graph)
 
     def reset(self, batch: Optional[int] = None, start_pos: int = 0) -> None:
         """Start ``batch`` fresh sequences (slots 0..batch-1) at ``start_pos``."""
@@ -305,6 +306,23 @@ class QwenEngine:
         if vec.size != self.cfg.hidden:
             raise ValueError(f"input vector has {vec.size} elements, expected {self.cfg.hidden}")
         self._pin_vec_np[:] = vec
+        if self.pdec is not None and self.use_graphs and self._ri_warm:
+            # the whole per-token sequence -- input copy, persistent launch,
+            # logits and error word back -- as one graph replay
+            self._persistent_token_graph().replay()
+        else:
+            self._persistent_token_ops()
+            self._ri_warm = self.pdec is not None
+        torch.cuda.current_stream(self.device).synchronize()
+        if self.pdec is not None and self._pin_err_np[0] != 0:
+            self.pdec.check_error()
+        self.host_pos += 1
+        return self._pin_logits_np.copy()
+
+    def _persistent_token_ops(self) -> None:
+        """run_inference's device work: pinned input row in, one decode step
+        (persistent launch, graph replay or per-stage kernels), logits (and
+        the persistent kernel's error word) out to pinned memory."""
         self._x_row0.copy_(self._pin_vec, non_blocking=True)
         if self.pdec is not None:
             self.pdec.run(1, self.tokens, self.pos, 1, x_in=self._x_rows1, logits=self._lg_rows1)
@@ -315,11 +333,23 @@ class QwenEngine:
         self._pin_logits.copy_(self._lg_row0, non_blocking=True)
         if self.pdec is not None:  # the device error word rides along with the logits
             self._pin_err.copy_(self.pdec.error, non_blocking=True)
-        torch.cuda.current_stream(self.device).synchronize()
-        if self.pdec is not None and self._pin_err_np[0] != 0:
-            self.pdec.check_error()
-        self.host_pos += 1
-        return self._pin_logits_np.copy()
+
+    def _persistent_token_graph(self):
+        """The persistent per-token sequence captured once (after one eager
+        call has set the kernel's launch configuration); the launch reads
+        tokens, positions and its tag epoch from device memory, so every
+        replay decodes the next position."""
+        g = self._graphs.get("token")
+        if g is None:
+            g = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream(self.device)
+            s.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(g, stream=s):
+                    self._persistent_token_ops()
+            torch.cuda.current_stream(self.device).wait_stream(s)
+            self._graphs["token"] = g
+        return g
 
     def predict_next_token(self, logits: np.ndarray) -> int:
         """engine.py:180-181: argmax over fp32(logits), first index on ties."""
