@@ -1626,15 +1626,36 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
     float* wsm = &A.wo[0][0][0];      // [G][n_splits] weights
     float* inv_den = wsm + G * n_splits;  // [G]
     if (warp < G) {
+      // each lane loads its first kMergeLane splits' (max, sum) pairs once,
+      // all in flight together, and keeps them in registers for both passes
+      constexpr int kMergeLane = 4;
       const size_t prow0 = (static_cast<size_t>(b) * Hq + kvh * G + warp) * ms;
+      float2 mls[kMergeLane];
+#pragma unroll
+      for (int i = 0; i < kMergeLane; ++i) {
+        const int sp = lane + kWarp * i;
+        mls[i] = sp < n_splits ? __ldcg(&P.part_ml[prow0 + sp]) : make_float2(-INFINITY, 0.0f);
+      }
       float M = -INFINITY;
-      for (int sp = lane; sp < n_splits; sp += kWarp) {
+#pragma unroll
+      for (int i = 0; i < kMergeLane; ++i)
+        if (mls[i].y > 0.0f) M = fmaxf(M, mls[i].x);
+      for (int sp = lane + kWarp * kMergeLane; sp < n_splits; sp += kWarp) {
         const float2 ml = __ldcg(&P.part_ml[prow0 + sp]);
         if (ml.y > 0.0f) M = fmaxf(M, ml.x);
       }
       M = warp_max(M);
       float den = 0.0f;
-      for (int sp = lane; sp < n_splits; sp += kWarp) {
+#pragma unroll
+      for (int i = 0; i < kMergeLane; ++i) {
+        const int sp = lane + kWarp * i;
+        if (sp < n_splits) {
+          const float wgt = mls[i].y > 0.0f ? expf(mls[i].x - M) : 0.0f;
+          wsm[warp * n_splits + sp] = wgt;
+          den = fmaf(wgt, mls[i].y, den);
+        }
+      }
+      for (int sp = lane + kWarp * kMergeLane; sp < n_splits; sp += kWarp) {
         const float2 ml = __ldcg(&P.part_ml[prow0 + sp]);
         const float wgt = ml.y > 0.0f ? expf(ml.x - M) : 0.0f;
         wsm[warp * n_splits + sp] = wgt;
@@ -1649,7 +1670,7 @@ __device__ void attn_item(const Params& P, Smem& S, const LayerPtrs& L, int b, i
       const size_t prow0 = (static_cast<size_t>(b) * Hq + kvh * G + h) * ms;
       const float* wh = wsm + h * n_splits;
       float n0 = 0.0f, n1 = 0.0f;
-#pragma unroll 4
+#pragma unroll 16  // the partial outputs' loads issue together
       for (int sp = 0; sp < n_splits; ++sp) {
         const float wgt = wh[sp];
         const float2 po = __ldcg(reinterpret_cast<const float2*>(&P.part_o[(prow0 + sp) * kHD + 2 * dp]));
