@@ -2234,7 +2234,11 @@ static int launch(const Params& P0, const lmps_model_desc& m, cudaStream_t st) {
   // As many ring slots as fit next to one resident CTA per SM.
   const int tail = tail_bytes(m.n_layers);
   int slots = (max_smem - P.act_bytes - tail) / kSlotBytes;
-  if (slots > 16) slots = 16;
+  // At most one slot per consumer warp: chunk i of a stage goes to warp
+  // i mod min(warps, slots), so each slot's consecutive fills go to the same
+  // warp and no parity wait can match a phase two fills old.  (227 KB of
+  // shared memory holds at most 11 slots anyway.)
+  if (slots > kConsumerWarps) slots = kConsumerWarps;
   size_t smem = 0;
   for (; slots >= 3; --slots) {
     smem = static_cast<size_t>(slots) * kSlotBytes + P.act_bytes + tail;
