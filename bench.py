@@ -208,6 +208,9 @@ def run_reference(args):
         "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
                          "sample": "oracle (numpy fp32 restatement) decoder layer + LM-head slice per step"},
         "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": ("one host process (rank 0) at every n_gpus: the value is one CPU sequence's rate and does "
+                 "not grow with n_gpus, so at n_gpus > 1 a GPU/CPU ratio divides N GPUs' tokens by one "
+                 "process's"),
     }
     print(json.dumps(line))
     return 0

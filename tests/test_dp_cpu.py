@@ -181,3 +181,33 @@ def test_argument_checks_and_spans():
     with pytest.raises(ValueError):
         DPScheduler(s, 0, 1, 1, batch_timeout=0)
     assert DPScheduler(s, 0, 1, 0, **FAST).run(_ids).results == {}
+
+
+class _FakeEngine:
+    """Stands in for QwenEngine.generate_batch: ids from the prompts and the seed."""
+    max_batch = 3
+
+    def __init__(self):
+        self.calls = []
+
+    def generate_batch(self, prompts, n, temperature, top_k, seed):
+        self.calls.append((len(prompts), seed))
+        p = np.asarray(prompts)
+        return (p[:, :1] * 1000 + np.arange(n)[None] + seed * 100).astype(np.int32)
+
+
+def test_generate_dp_batches_seeds_and_order():
+    """Prompts split into engine.max_batch rows per batch, batch b sampled
+    with seed + b, the rows put back in prompt order."""
+    import torch.distributed as dist
+    from llamamps_b200.dp import generate_dp
+    eng = _FakeEngine()
+    prompts = np.arange(8)[:, None] * np.ones((1, 5), dtype=np.int64)
+    got, rep = generate_dp(eng, prompts, 4, dist.HashStore(), 0, 1, seed=7, **FAST)
+    assert eng.calls == [(3, 7), (3, 8), (2, 9)]
+    want = np.concatenate([_FakeEngine().generate_batch(prompts[lo:hi], 4, 0.0, 0, 7 + b)
+                           for b, (lo, hi) in enumerate([(0, 3), (3, 6), (6, 8)])])
+    assert np.array_equal(got, want) and got.shape == (8, 4)
+    assert rep.ran == [0, 1, 2]
+    with pytest.raises(ValueError):
+        generate_dp(eng, np.zeros((0, 4)), 4, dist.HashStore(), 0, 1, **FAST)
