@@ -43,6 +43,16 @@ from typing import Any, Callable, Dict, List, Optional, Sequence
 
 import numpy as np
 
+_jobs = 0  # schedulers made with the default prefix in this process
+_jobs_lock = threading.Lock()
+
+
+def _next_job_prefix() -> str:
+    global _jobs
+    with _jobs_lock:
+        _jobs += 1
+        return f"dp{_jobs}"
+
 
 def make_store(host: str, port: int, rank: int, world_size: int, timeout: float = 60.0):
     """A TCPStore shared by ``world_size`` ranks (rank 0 hosts it).  The host
@@ -76,10 +86,14 @@ class DPScheduler:
     ``store``: a key-value store shared by all ranks (``add``, ``set``,
     ``get``, ``check``, ``compare_set``: a torch.distributed Store).
     ``n_batches``: batches 0 .. n_batches-1, the same count on every rank.
-    ``prefix`` keeps the keys of separate jobs on one store apart.
+    ``prefix`` keeps the keys of separate jobs on one store apart; by
+    default each scheduler this process makes gets the next job number
+    (dp1, dp2, ..), which names the same job on every rank as long as the
+    ranks make their schedulers in the same order (one SPMD program).  A
+    job's keys stay in the store; a prefix must not be reused on one store.
     """
 
-    def __init__(self, store, rank: int, world_size: int, n_batches: int, *, prefix: str = "dp",
+    def __init__(self, store, rank: int, world_size: int, n_batches: int, *, prefix: Optional[str] = None,
                  heartbeat: float = 0.25, dead_after: float = 5.0, batch_timeout: Optional[float] = None,
                  poll: float = 0.02, timeout: float = 600.0):
         if world_size < 1 or not 0 <= rank < world_size:
@@ -91,7 +105,8 @@ class DPScheduler:
         if batch_timeout is not None and batch_timeout <= 0:
             raise ValueError("batch_timeout must be positive")
         self.store, self.rank, self.world, self.n = store, rank, world_size, n_batches
-        self.prefix, self.heartbeat, self.dead_after = prefix, heartbeat, dead_after
+        self.prefix = prefix if prefix is not None else _next_job_prefix()
+        self.heartbeat, self.dead_after = heartbeat, dead_after
         self.batch_timeout, self.poll, self.timeout = batch_timeout, poll, timeout
         self._lock = threading.Lock()  # one request at a time on the shared client
         self._stop = threading.Event()

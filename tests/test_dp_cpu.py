@@ -211,3 +211,17 @@ def test_generate_dp_batches_seeds_and_order():
     assert rep.ran == [0, 1, 2]
     with pytest.raises(ValueError):
         generate_dp(eng, np.zeros((0, 4)), 4, dist.HashStore(), 0, 1, **FAST)
+
+
+def test_consecutive_jobs_on_one_store_do_not_mix():
+    """Two jobs on the same store (as under one torchrun process group): the
+    second gets its own keys, so it runs its own batches instead of finding
+    the first job's counter and results."""
+    import torch.distributed as dist
+    from llamamps_b200.dp import DPScheduler
+    store = dist.HashStore()
+    a = DPScheduler(store, 0, 1, 3, **FAST).run(_ids)
+    b = DPScheduler(store, 0, 1, 4, **FAST).run(lambda i: _ids(i + 10))
+    assert a.ran == [0, 1, 2] and b.ran == [0, 1, 2, 3]
+    for i in range(4):
+        assert np.array_equal(b.results[i], _ids(i + 10))
